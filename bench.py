@@ -1,0 +1,373 @@
+"""Benchmark of the per-layer paged decode-attention path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload C2: batch 64, 32 query / 8 KV heads, head_dim 128, page 16, per-sequence KV
+lengths uniform in [512, 8192] (seed 0), page ids a random draw from a 600k-page pool
+(one layer, 39.3 GB of K+V), q/K/V ~ N(0, 1).  A step is one decode-attention pass over
+the batch (64 query tokens); the metric is decode tokens/s of that pass.
+
+* ``value``     -- kernel path, inputs resident in HBM: ops.paged_decode (the C ABI
+                   nslg_paged_decode: split-KV kernel + merge), CUDA events on the
+                   launching stream.  The 1.13 GB of KV read per step is 9x the 126 MB L2,
+                   so no L2 flush is needed between steps.
+* ``e2e``       -- the same decode step through the reference-facing API:
+                   manager.begin_forward -> CacheContext.attend -> end_forward, with q/k/v
+                   copied from pinned host memory and the output read back every step.
+* ``roofline``  -- algorithmic bytes per step / mean step time vs the measured HBM copy
+                   bandwidth (MEASURED_PEAKS.json).
+* ``cpu_baseline`` / ``--impl reference`` -- the reference's contiguous-SDPA attend
+                   (restated in oracle/attention.py) on the host cores.
+
+N > 1 (torchrun): every rank runs its own independent C2 batch (weak scaling, no
+collective on the data path); ``value`` is the sum over ranks of tokens / the slowest
+rank's time.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, HQ, HKV, D, PS = 64, 32, 8, 128, 16
+POOL_PAGES = 600_000
+LEN_LO, LEN_HI = 512, 8192
+FALLBACK_HBM_GBS = 6650.0
+
+
+def c2_lens(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(LEN_LO, LEN_HI + 1, (B,), generator=g).tolist()
+
+
+def alg_bytes(lens):
+    """Bytes a decode step must move: K and V of every cached token, q in, out, the page
+    ids and the small CSR arrays."""
+    pages = sum(math.ceil(n / PS) for n in lens)
+    kv = sum(lens) * HKV * D * 2 * 2
+    return kv + 2 * B * HQ * D * 2 + 4 * pages + 4 * (2 * B + 1)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        self.out.flush()
+        try:
+            rows = [r.split(",") for r in open(self.out.name).read().strip().splitlines()]
+        except Exception:
+            rows = []
+        os.unlink(self.out.name)
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------- ours
+def build_c2_device(device, seed):
+    """Pool [600k, 16, 8, 128] x2 bf16 ~ N(0,1), page table drawn from randperm(600k)."""
+    lens = c2_lens(seed)
+    npg = [math.ceil(n / PS) for n in lens]
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(POOL_PAGES, generator=g)
+    perm = perm[perm != 0][:sum(npg)].to(torch.int32)
+    indptr = torch.zeros(B + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(torch.tensor(npg), 0).to(torch.int32)
+    lpl = torch.tensor([n - (p - 1) * PS for n, p in zip(lens, npg)], dtype=torch.int32)
+    gd = torch.Generator(device=device).manual_seed(seed)
+    shape = (POOL_PAGES, PS, HKV, D)
+    pool_k = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    pool_v = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    for t in (pool_k, pool_v):
+        for i in range(0, POOL_PAGES, 50_000):      # bounded fp32 temporaries
+            t[i:i + 50_000] = torch.randn(t[i:i + 50_000].shape, device=device, generator=gd)
+    q = torch.randn(B, HQ, D, device=device, generator=gd).to(torch.bfloat16)
+    return dict(lens=lens, pool_k=pool_k, pool_v=pool_v, indptr=indptr.to(device),
+                indices=perm.to(device), lpl=lpl.to(device), q=q)
+
+
+def run_kernel(device, steps, warmup, seed):
+    from nanoslg_b200 import ops
+    c = build_c2_device(device, seed)
+    out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=device)
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        ops.paged_decode(c["q"], c["pool_k"], c["pool_v"], c["indptr"], c["indices"], c["lpl"],
+                         scale, out=out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    ops.check_device_status(device)
+    stream = torch.cuda.current_stream(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(device.index) as clk:
+        ev[0].record(stream)
+        for i in range(steps):
+            step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(device)
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    ops.check_device_status(device)
+    res = dict(total_ms=total_ms, per_ms=per, lens=c["lens"], clocks=clk.summary())
+    del c
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_e2e(device, steps, warmup, seed):
+    """Decode steps through B200PagedKVCache / CacheContext.attend with host buffers."""
+    from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
+    lens = c2_lens(seed)
+    cfg = KVCacheConfig(num_layers=1, num_kv_heads=HKV, num_qo_heads=HQ, head_dim=D,
+                        page_size=PS, max_pages=POOL_PAGES, dtype=torch.bfloat16, device=device,
+                        enable_prefix_caching=True)
+    mgr = B200PagedKVCache(cfg)
+    sids = [f"s{b}" for b in range(B)]
+    for s, n in zip(sids, lens):
+        mgr.allocate_sequence(s, None, num_tokens=n)
+        mgr.seqs[s].num_tokens = n            # history already cached
+    mgr.pool.flush_zero()
+    gd = torch.Generator(device=device).manual_seed(seed)
+    for t in (mgr.pool.k, mgr.pool.v):       # history values ~ N(0, 1)
+        for i in range(0, POOL_PAGES, 50_000):
+            t[0, i:i + 50_000] = torch.randn(t[0, i:i + 50_000].shape, device=device, generator=gd)
+    g = torch.Generator().manual_seed(seed + 1)
+    nbuf = 4
+    hq = [torch.randn(B, 1, HQ, D, generator=g).to(torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    hk = [torch.randn(B, 1, HKV, D, generator=g).to(torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    hv = [torch.randn(B, 1, HKV, D, generator=g).to(torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    hout = torch.empty(B, 1, HQ * D, dtype=torch.bfloat16).pin_memory()
+    stats = {"h2d": 0, "d2h": 0}
+
+    def step(i):
+        ctx = mgr.begin_forward(sids, [1] * B)
+        q = hq[i % nbuf].to(device, non_blocking=True)
+        k = hk[i % nbuf].to(device, non_blocking=True)
+        v = hv[i % nbuf].to(device, non_blocking=True)
+        out = ctx.attend(0, q, k, v, HQ, HKV)
+        hout.copy_(out, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()   # the result is on the host
+        mgr.end_forward(ctx)
+        plan = (ctx.kv_indices.numel() + ctx.kv_indptr.numel() + ctx.kv_last_page_len.numel()
+                + ctx.qo_indptr.numel() + ctx.q_row_start.numel() + ctx._write_loc.numel()
+                + ctx._pos_i32.numel()) * 4
+        stats["h2d"] = q.numel() * 2 + k.numel() * 2 + v.numel() * 2 + plan
+        stats["d2h"] = hout.numel() * 2
+
+    for i in range(warmup):
+        step(i)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(warmup + i)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1)
+    del mgr
+    torch.cuda.empty_cache()
+    return dict(total_ms=ms, h2d=stats["h2d"], d2h=stats["d2h"])
+
+
+# ------------------------------------------------------------------------ CPU side
+def cpu_reference(max_seconds, n_calls=None, seed=0):
+    """The reference's contiguous attend (oracle/attention.py restating
+    kv_cache.py:247-325) on the C2 workload, all host threads."""
+    from oracle.attention import ContiguousOracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    lens = c2_lens(seed)
+    smax = max(lens) + 1
+    orc = ContiguousOracle(1, B, smax, HKV, D, torch.bfloat16)
+    g = torch.Generator().manual_seed(seed)
+    blk = torch.randn(1024, HKV, D, generator=g).to(torch.bfloat16)
+    for b, n in enumerate(lens):                        # history: tiled random rows
+        reps = -(-n // 1024)
+        orc.k[0, b, :n] = blk.repeat(reps, 1, 1)[:n]
+        orc.v[0, b, :n] = blk.flip(0).repeat(reps, 1, 1)[:n]
+    q = torch.randn(B, 1, HQ, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, 1, HKV, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, 1, HKV, D, generator=g).to(torch.bfloat16)
+    starts = list(lens)
+    orc.attend(0, q, k, v, starts, [1] * B, [0] * B)       # warm-up
+    times = []
+    t_end = time.perf_counter() + max_seconds
+    while (n_calls is None and time.perf_counter() < t_end) or (n_calls and len(times) < n_calls):
+        t0 = time.perf_counter()
+        orc.attend(0, q, k, v, starts, [1] * B, [0] * B)
+        times.append(time.perf_counter() - t0)
+    mean = sum(times) / len(times)
+    return dict(value=B / mean, calls=len(times), s_per_call=mean, cores=torch.get_num_threads(),
+                sample=f"{len(times)} full C2 decode-attention calls (64 seqs, sum(len)="
+                       f"{sum(lens)}, one layer) through the contiguous cache + SDPA, bf16")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "decode tok/s (paged decode attention, C2: B=64, 32/8 heads, D=128, len U[512,8192])"
+    config = {"workload": "C2 decode-attention microbenchmark (BASELINE configs[1])",
+              "batch": B, "num_qo_heads": HQ, "num_kv_heads": HKV, "head_dim": D,
+              "page_size": PS, "pool_pages": POOL_PAGES, "kv_len": f"U[{LEN_LO},{LEN_HI}] seed 0",
+              "l2": "inputs larger than L2 (1.13 GB KV per step vs 126 MB L2), no flush",
+              "parallelism": f"{world} independent replicas" if world > 1 else "single GPU"}
+
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        per_call = cpu_reference(0, n_calls=1)["s_per_call"]
+        budget = 150.0
+        n = max(1, min(a.steps, int(budget / max(per_call, 1e-3))))
+        r = cpu_reference(0, n_calls=n)
+        line = {"metric": metric, "value": r["value"], "unit": "tok/s", "n_gpus": a.gpus,
+                "steps": r["calls"], "warmup": 1, "ms_per_step": r["s_per_call"] * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V, random page table)",
+                "config": config, "impl": "reference",
+                "cpu_baseline": {"value": r["value"], "unit": "tok/s", "cores": r["cores"],
+                                 "kind": "port", "sample": r["sample"]},
+                "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}))
+        return 1
+    torch.cuda.set_device(local)
+    device = torch.device(f"cuda:{local}")
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=device)
+    from nanoslg_b200 import build as nbuild
+    if not os.path.exists(nbuild.LIB):
+        nbuild.build()
+
+    kr = run_kernel(device, a.steps, a.warmup, seed=rank)
+    e2e_steps = a.e2e_steps or max(10, a.steps // 2)
+    er = run_e2e(device, e2e_steps, a.warmup, seed=rank)
+
+    total_ms, e2e_ms = kr["total_ms"], er["total_ms"]
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+    value = world * B * a.steps / (total_ms / 1e3)
+    e2e_value = world * B * e2e_steps / (e2e_ms / 1e3)
+    mean_ms = statistics.mean(kr["per_ms"])
+    ab = alg_bytes(kr["lens"])
+    hbm, src = peaks()
+    achieved = ab / (mean_ms / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "decode_tc_c2_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    line = {"metric": metric, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": total_ms / a.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) K/V, random page table over a 600k-page pool)",
+            "config": config,
+            "e2e": {"value": e2e_value, "unit": "tok/s", "ms_per_step": e2e_ms / e2e_steps,
+                    "steps": e2e_steps, "h2d_bytes_per_step": er["h2d"],
+                    "d2h_bytes_per_step": er["d2h"],
+                    "path": "B200PagedKVCache.begin_forward -> CacheContext.attend -> "
+                            "end_forward, pinned host q/k/v in, output to host"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": traffic,
+                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src ==
+                         "measured" else "fallback 6650 GB/s",
+                         "algorithmic_bytes_per_step": ab,
+                         "kernel_ms_mean": mean_ms,
+                         "kernel_ms_median": statistics.median(kr["per_ms"])},
+            "gpu_launches": 2 * a.steps,
+            "clocks": kr["clocks"]}
+    if rank == 0 and world == 1 and not a.no_cpu:
+        r = cpu_reference(a.cpu_seconds)
+        line["cpu_baseline"] = {"value": r["value"], "unit": "tok/s", "cores": r["cores"],
+                                "kind": "port", "sample": r["sample"]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,147 @@
+/*
+ * nslg_b200.h -- C ABI of the B200 (sm_100a) kernels behind NanoSLG's per-layer
+ * attention path.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes, plus the
+ * cudaStream_t to launch on (passed as void*), and returns an int status
+ * (NSLG_OK == 0).  On a non-zero status nslg_last_error() returns a message for the
+ * calling thread.  No entry point allocates device memory: scratch space is passed in
+ * by the caller (see nslg_decode_workspace_bytes).
+ *
+ * Errors that can only be seen on the device (a page id outside the pool, a write
+ * slot outside the pool, a position outside the RoPE table) never trap: the kernel
+ * skips the access and ORs an NSLG_DEV_* bit into *dev_status (when dev_status is not
+ * NULL).  The caller reads it whenever it chooses to synchronise.
+ *
+ * Layouts follow the reference (nanoslg/kv_cache.py):
+ *   KV pool, one layer:  [num_pages, page_size, num_kv_heads, head_dim]  ("NHD",
+ *                        kv_cache.py:384-392, PagePool.k[layer] / PagePool.v[layer])
+ *   CSR page list:       kv_indptr[B+1], kv_indices[kv_indptr[B]],
+ *                        kv_last_page_len[B]  (kv_cache.py:598-615, the arrays the
+ *                        reference hands to FlashInfer's plan())
+ */
+#ifndef NSLG_B200_H
+#define NSLG_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define NSLG_DTYPE_F32 0
+#define NSLG_DTYPE_BF16 1
+
+/* host-side status codes */
+#define NSLG_OK 0
+#define NSLG_ERR_ARG 1         /* invalid argument: null pointer, bad size or stride    */
+#define NSLG_ERR_UNSUPPORTED 2 /* shape / dtype combination this build does not cover  */
+#define NSLG_ERR_CUDA 3        /* a CUDA runtime call failed (message has the details)  */
+#define NSLG_ERR_WORKSPACE 4   /* workspace smaller than nslg_decode_workspace_bytes()  */
+
+/* device-side status bits (ORed into *dev_status) */
+#define NSLG_DEV_BAD_PAGE 1u     /* kv_indices entry outside [0, num_pages)            */
+#define NSLG_DEV_BAD_SLOT 2u     /* write location outside the pool                    */
+#define NSLG_DEV_BAD_POSITION 4u /* RoPE position outside the cos/sin table            */
+#define NSLG_DEV_WAIT_TIMEOUT 8u /* a bounded pipeline wait gave up (kernel returned)  */
+
+/* Library version string. */
+const char* nslg_version(void);
+
+/* Message for the last non-OK status returned on this thread ("" if none). */
+const char* nslg_last_error(void);
+
+/* Fused rotary embedding + paged KV append.
+ *
+ * Replaces the reference's RoPE on q and k (models.py:99-103, apply_rotary_emb at
+ * models.py:69-83: rotate-half, cos/sin cast to the activation type) followed by the
+ * KV write of attend() (kv_cache.py:661-674 paged, kv_cache.py:302-310 contiguous).
+ *
+ *   q[t, h, :]  at q + t*q_stride + h*head_dim   (t < num_tokens, h < num_qo_heads)
+ *   k, v        likewise with k_stride / v_stride and num_kv_heads
+ *   q_out       contiguous [num_tokens, num_qo_heads, head_dim]: rotated q
+ *   positions   [num_tokens] int32 row of cos/sin for each token; NULL = no rotation
+ *   cos_table, sin_table  fp32 [table_rows, head_dim] (models.py:37-66 layout)
+ *   write_loc   [num_tokens] int32 page*page_size + slot; < 0 = token not written
+ *   pool_k, pool_v        one layer of the pool, pool_slots = num_pages*page_size rows
+ *                         of [num_kv_heads, head_dim]; receive rotated k and plain v.
+ * head_dim must be even and a multiple of 16 (bf16) / 8 (fp32); rows 16-byte aligned.
+ */
+int nslg_rope_kv_append(int dtype, int num_tokens, int num_qo_heads, int num_kv_heads,
+                        int head_dim, const void* q, int64_t q_stride, const void* k,
+                        int64_t k_stride, const void* v, int64_t v_stride, void* q_out,
+                        const int32_t* positions, const float* cos_table,
+                        const float* sin_table, int64_t table_rows,
+                        const int32_t* write_loc, void* pool_k, void* pool_v,
+                        int64_t pool_slots, uint32_t* dev_status, void* stream);
+
+/* Bytes of scratch nslg_paged_decode needs for this batch / head count / head_dim on
+ * the current device. */
+int64_t nslg_decode_workspace_bytes(int batch, int num_qo_heads, int head_dim);
+
+/* Batched paged decode attention: one query token per sequence.
+ *
+ * Replaces FlashInferCacheContext.attend's decode branch (kv_cache.py:648-651,
+ * BatchDecodeWithPagedKVCacheWrapper.run over the CSR built at kv_cache.py:598-621)
+ * and ContiguousCacheContext.attend's SDPA for S == 1 (kv_cache.py:312-322).
+ *
+ *   q[b, h, :]   at q + b*q_stride + h*head_dim    [batch, num_qo_heads, head_dim]
+ *   out[b, h, :] at out + b*out_stride + h*head_dim
+ *   out = softmax(sm_scale * q . K^T) V over the kv_len(b) tokens of sequence b,
+ *   kv_len(b) = (kv_indptr[b+1]-kv_indptr[b]-1)*page_size + kv_last_page_len[b].
+ * GQA: query head h reads kv head h / (num_qo_heads / num_kv_heads).
+ * Sequences with no pages produce zeros.
+ */
+int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
+                      int head_dim, int page_size, const void* q, int64_t q_stride,
+                      void* out, int64_t out_stride, const void* pool_k,
+                      const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
+                      const int32_t* kv_indices, const int32_t* kv_last_page_len,
+                      float sm_scale, void* workspace, int64_t workspace_bytes,
+                      uint32_t* dev_status, void* stream);
+
+/* Batched paged prefill / extend attention with a causal mask.
+ *
+ * Replaces FlashInferCacheContext.attend's prefill branch (kv_cache.py:652-655,
+ * BatchPrefillWithPagedKVCacheWrapper.run with causal=True, planned at
+ * kv_cache.py:622-632) together with _pack_q/_unpack (kv_cache.py:676-691), and the
+ * masked SDPA of ContiguousCacheContext.attend (kv_cache.py:312-322 with the mask of
+ * _build_causal_mask, kv_cache.py:192-224).
+ *
+ * Sequence b has qo_len(b) = qo_indptr[b+1]-qo_indptr[b] new query rows; its rows live
+ * at q + (q_row_start[b] + i)*q_stride (i < qo_len(b)), or at qo_indptr[b] + i when
+ * q_row_start is NULL; outputs at the same rows of out.  Row i sits at absolute
+ * position kv_len(b) - qo_len(b) + i and, when causal != 0, attends to kv positions
+ * <= that position (the reference's kpos <= start + i  and  kpos < seq_len).
+ * max_qo_len bounds qo_len(b).
+ */
+int nslg_paged_prefill(int dtype, int batch, int num_qo_heads, int num_kv_heads,
+                       int head_dim, int page_size, const void* q, int64_t q_stride,
+                       void* out, int64_t out_stride, const int32_t* qo_indptr,
+                       const int32_t* q_row_start, int max_qo_len, const void* pool_k,
+                       const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
+                       const int32_t* kv_indices, const int32_t* kv_last_page_len,
+                       float sm_scale, int causal, uint32_t* dev_status, void* stream);
+
+/* Fused residual add + RMSNorm.
+ *
+ * Replaces RMSNorm.forward (models.py:31-34: fp32 statistics, normalised value rounded
+ * to the activation type, then multiplied by the weight) and the residual adds around
+ * it (models.py:169-172).
+ *   residual == NULL:  out = rmsnorm(x) * weight
+ *   residual != NULL:  residual = x + residual (rounded to dtype, in place);
+ *                      out = rmsnorm(residual) * weight
+ * x, residual, out: [rows, hidden] with row strides x_stride / residual_stride /
+ * out_stride (elements); weight: [hidden].
+ */
+int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x,
+                          int64_t x_stride, void* residual, int64_t residual_stride,
+                          const void* weight, void* out, int64_t out_stride, float eps,
+                          void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSLG_B200_H */

@@ -1,0 +1,187 @@
+// extern "C" entry points declared in include/nslg_b200.h: argument validation,
+// per-thread error messages, and the choice between the tensor-core kernels and the
+// CUDA-core kernel for shapes the former do not cover.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <string>
+
+#include "launch.h"
+
+namespace nslg {
+
+namespace {
+thread_local std::string g_last_error;
+std::atomic<int> g_sm_count[64];
+}  // namespace
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return set_error(NSLG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+  return NSLG_OK;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int esize(int dtype) { return dtype == NSLG_DTYPE_BF16 ? 2 : 4; }
+
+bool valid_dtype(int dtype) { return dtype == NSLG_DTYPE_BF16 || dtype == NSLG_DTYPE_F32; }
+
+int check_heads(const char* what, int hq, int hkv, int d) {
+  if (hq <= 0 || hkv <= 0 || d <= 0 || hq % hkv != 0)
+    return set_error(NSLG_ERR_ARG, std::string(what) + ": need num_qo_heads % num_kv_heads == 0");
+  return NSLG_OK;
+}
+
+}  // namespace
+}  // namespace nslg
+
+using namespace nslg;
+
+extern "C" {
+
+const char* nslg_version(void) { return "nanoslg-b200 0.1 (sm_100a)"; }
+
+const char* nslg_last_error(void) { return g_last_error.c_str(); }
+
+int nslg_rope_kv_append(int dtype, int num_tokens, int num_qo_heads, int num_kv_heads,
+                        int head_dim, const void* q, int64_t q_stride, const void* k,
+                        int64_t k_stride, const void* v, int64_t v_stride, void* q_out,
+                        const int32_t* positions, const float* cos_table,
+                        const float* sin_table, int64_t table_rows, const int32_t* write_loc,
+                        void* pool_k, void* pool_v, int64_t pool_slots, uint32_t* dev_status,
+                        void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return set_error(NSLG_ERR_ARG, "rope_kv_append: bad dtype");
+  if (num_tokens < 0) return set_error(NSLG_ERR_ARG, "rope_kv_append: num_tokens < 0");
+  if (num_tokens == 0) return NSLG_OK;
+  int rc = check_heads("rope_kv_append", num_qo_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  const int vec = 16 / esize(dtype);
+  if (head_dim % (2 * vec) != 0)
+    return set_error(NSLG_ERR_UNSUPPORTED, "rope_kv_append: head_dim must be a multiple of " +
+                                                std::to_string(2 * vec));
+  if (k == nullptr || v == nullptr)
+    return set_error(NSLG_ERR_ARG, "rope_kv_append: k and v are required");
+  if (q_out != nullptr && q == nullptr)
+    return set_error(NSLG_ERR_ARG, "rope_kv_append: q_out given without q");
+  if (positions != nullptr && (cos_table == nullptr || sin_table == nullptr || table_rows <= 0))
+    return set_error(NSLG_ERR_ARG, "rope_kv_append: positions need cos/sin tables");
+  if (write_loc != nullptr && (pool_k == nullptr || pool_v == nullptr || pool_slots <= 0))
+    return set_error(NSLG_ERR_ARG, "rope_kv_append: write_loc needs pool_k/pool_v");
+  const int64_t es = esize(dtype);
+  if ((q_out && (!aligned16(q) || !aligned16(q_out) || (q_stride * es) % 16)) || !aligned16(k) ||
+      !aligned16(v) || (k_stride * es) % 16 || (v_stride * es) % 16 ||
+      (pool_k && !aligned16(pool_k)) || (pool_v && !aligned16(pool_v)) ||
+      (cos_table && !aligned16(cos_table)) || (sin_table && !aligned16(sin_table)))
+    return set_error(NSLG_ERR_ARG, "rope_kv_append: pointers and row strides must be 16-byte aligned");
+  return launch_rope_kv_append(dtype, num_tokens, num_qo_heads, num_kv_heads, head_dim, q,
+                               q_stride, k, k_stride, v, v_stride, q_out, positions, cos_table,
+                               sin_table, table_rows, write_loc, pool_k, pool_v, pool_slots,
+                               dev_status, static_cast<cudaStream_t>(stream));
+}
+
+int64_t nslg_decode_workspace_bytes(int batch, int num_qo_heads, int head_dim) {
+  if (batch < 0 || num_qo_heads <= 0 || head_dim <= 0) return 0;
+  return decode_tc_workspace_bytes(batch, num_qo_heads, head_dim);
+}
+
+int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads, int head_dim,
+                      int page_size, const void* q, int64_t q_stride, void* out,
+                      int64_t out_stride, const void* pool_k, const void* pool_v,
+                      int64_t num_pages, const int32_t* kv_indptr, const int32_t* kv_indices,
+                      const int32_t* kv_last_page_len, float sm_scale, void* workspace,
+                      int64_t workspace_bytes, uint32_t* dev_status, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return set_error(NSLG_ERR_ARG, "paged_decode: bad dtype");
+  if (batch < 0) return set_error(NSLG_ERR_ARG, "paged_decode: batch < 0");
+  if (batch == 0) return NSLG_OK;
+  int rc = check_heads("paged_decode", num_qo_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (page_size <= 0 || num_pages <= 0)
+    return set_error(NSLG_ERR_ARG, "paged_decode: page_size and num_pages must be positive");
+  if (!q || !out || !pool_k || !pool_v || !kv_indptr || !kv_indices || !kv_last_page_len)
+    return set_error(NSLG_ERR_ARG, "paged_decode: null pointer");
+  if (!(sm_scale > 0.f)) return set_error(NSLG_ERR_ARG, "paged_decode: sm_scale must be > 0");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (decode_tc_supported(dtype, num_qo_heads, num_kv_heads, head_dim, page_size) &&
+      aligned16(pool_k) && aligned16(pool_v) && (reinterpret_cast<uintptr_t>(q) & 3u) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 3u) == 0 && q_stride % 2 == 0 && out_stride % 2 == 0)
+    return launch_paged_decode_tc(batch, num_qo_heads, num_kv_heads, head_dim, q, q_stride, out,
+                                  out_stride, pool_k, pool_v, num_pages, kv_indptr, kv_indices,
+                                  kv_last_page_len, sm_scale, workspace, workspace_bytes,
+                                  dev_status, st);
+  // decode is the one-row case of the general kernel (qo_indptr == NULL: row b of q is
+  // the single query of sequence b)
+  return launch_paged_attention_simt(dtype, batch, num_qo_heads, num_kv_heads, head_dim,
+                                     page_size, q, q_stride, out, out_stride, nullptr, nullptr, 1,
+                                     pool_k, pool_v, num_pages, kv_indptr, kv_indices,
+                                     kv_last_page_len, sm_scale, 0, dev_status, st);
+}
+
+int nslg_paged_prefill(int dtype, int batch, int num_qo_heads, int num_kv_heads, int head_dim,
+                       int page_size, const void* q, int64_t q_stride, void* out,
+                       int64_t out_stride, const int32_t* qo_indptr, const int32_t* q_row_start,
+                       int max_qo_len, const void* pool_k, const void* pool_v, int64_t num_pages,
+                       const int32_t* kv_indptr, const int32_t* kv_indices,
+                       const int32_t* kv_last_page_len, float sm_scale, int causal,
+                       uint32_t* dev_status, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return set_error(NSLG_ERR_ARG, "paged_prefill: bad dtype");
+  if (batch < 0 || max_qo_len < 0)
+    return set_error(NSLG_ERR_ARG, "paged_prefill: negative batch or max_qo_len");
+  if (batch == 0 || max_qo_len == 0) return NSLG_OK;
+  int rc = check_heads("paged_prefill", num_qo_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (page_size <= 0 || num_pages <= 0)
+    return set_error(NSLG_ERR_ARG, "paged_prefill: page_size and num_pages must be positive");
+  if (!q || !out || !qo_indptr || !pool_k || !pool_v || !kv_indptr || !kv_indices ||
+      !kv_last_page_len)
+    return set_error(NSLG_ERR_ARG, "paged_prefill: null pointer");
+  if (!(sm_scale > 0.f)) return set_error(NSLG_ERR_ARG, "paged_prefill: sm_scale must be > 0");
+  if (max_qo_len > 65535) return set_error(NSLG_ERR_UNSUPPORTED, "paged_prefill: max_qo_len > 65535");
+  return launch_paged_attention_simt(dtype, batch, num_qo_heads, num_kv_heads, head_dim,
+                                     page_size, q, q_stride, out, out_stride, qo_indptr,
+                                     q_row_start, max_qo_len, pool_k, pool_v, num_pages,
+                                     kv_indptr, kv_indices, kv_last_page_len, sm_scale, causal,
+                                     dev_status, static_cast<cudaStream_t>(stream));
+}
+
+int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int64_t x_stride,
+                          void* residual, int64_t residual_stride, const void* weight, void* out,
+                          int64_t out_stride, float eps, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return set_error(NSLG_ERR_ARG, "rmsnorm_residual: bad dtype");
+  if (rows < 0 || hidden <= 0) return set_error(NSLG_ERR_ARG, "rmsnorm_residual: bad shape");
+  if (rows == 0) return NSLG_OK;
+  if (!x || !weight || !out) return set_error(NSLG_ERR_ARG, "rmsnorm_residual: null pointer");
+  const int64_t es = esize(dtype);
+  if ((hidden * es) % 16 || !aligned16(x) || !aligned16(weight) || !aligned16(out) ||
+      (residual && !aligned16(residual)) || (x_stride * es) % 16 || (out_stride * es) % 16 ||
+      (residual && (residual_stride * es) % 16))
+    return set_error(NSLG_ERR_ARG, "rmsnorm_residual: rows must be 16-byte aligned");
+  return launch_rmsnorm_residual(dtype, rows, hidden, x, x_stride, residual, residual_stride,
+                                 weight, out, out_stride, eps, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,591 @@
+// Split-KV GQA decode attention for bf16, page_size 16, head_dim 128 (or 64).
+//
+// Work split. The pages of all sequences form one flat list (the CSR kv_indices,
+// kv_cache.py:598-615). CTA c of n takes the contiguous slice
+// [floor(T*c/n), floor(T*(c+1)/n)) of it, T = kv_indptr[B], so every CTA streams the
+// same number of pages whatever the sequence lengths are. n = min(#SMs, ceil(T/2)) and
+// is computed on the device from kv_indptr, so the launch needs no host-side plan and
+// can be replayed inside a CUDA graph. A CTA's slice is cut into segments at sequence
+// boundaries; segment (b, c) writes its softmax partial (o, lse) to slot b + c of the
+// workspace (unique: along the flat list either b or c grows by one at each new
+// segment). A sequence lying inside one CTA's slice is finished in place and written
+// straight to `out`; the others are combined by decode_merge_kernel with a
+// log-sum-exp merge.
+//
+// Data movement. One producer warp issues TMA tile loads (no multicast) of each page:
+// per kv head and per 64-dim half, a [16 tokens x 64 dims] box with 128-byte swizzle,
+// into a ring of `stages` stage buffers guarded by full/empty mbarriers. A stage holds
+// 8/HKV pages of all HKV heads, K and V: 64 KiB for head_dim 128.
+//
+// Math. Eight consumer warps; warp w owns kv head w % HKV and page w / HKV of every
+// stage. Its G = Hq/Hkv query heads are the rows of a 16-row mma tile (rows >= G are
+// zero), so one K/V page serves all heads of the GQA group:
+//   S[16 x 16 tokens] = Q[16 x D] . K^T   (mma.m16n8k16, K via ldmatrix from the
+//                                          swizzled tile, conflict free)
+//   online softmax in fp32 (exp2, row max/sum over the 4-lane quad)
+//   O[16 x D] += P[16 x 16] . V          (P reused from the S accumulators as the A
+//                                          fragment, V via ldmatrix.trans)
+// Warps that share a kv head (HKV < 8) merge their states through shared memory at
+// the end of each segment.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace nslg {
+namespace {
+
+constexpr int kPS = 16;             // tokens per page
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMinPagesPerCta = 2;
+constexpr int kBoxBytes = kPS * 64 * 2;  // one [16 x 64] bf16 box: 2 KiB
+constexpr int kMaxSmem = 232448;         // 227 KiB opt-in per CTA on sm_100
+
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* out;
+  const int32_t* indptr;
+  const int32_t* indices;
+  const int32_t* lpl;
+  float* part_o;    // [slots, hq, D]
+  float* part_lse;  // [slots, hq]
+  int64_t q_stride, out_stride, num_pages;
+  int batch, hq, group, stages, grid;
+  float scale_log2;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ int num_ctas(int64_t total_pages, int grid) {
+  const int64_t want = (total_pages + kMinPagesPerCta - 1) / kMinPagesPerCta;
+  return static_cast<int>(want < grid ? want : grid);
+}
+
+// CTA whose slice holds flat page p: the largest c with floor(T*c/n) <= p.
+__device__ __forceinline__ int cta_of(int64_t p, int64_t total, int n) {
+  return static_cast<int>((static_cast<int64_t>(n) * (p + 1) - 1) / total);
+}
+
+// Sequence holding flat page p (kv_indptr non-decreasing, kv_indptr[B] > p).
+__device__ __forceinline__ int seq_of(const int32_t* indptr, int batch, int64_t p) {
+  int lo = 1, hi = batch;  // first j in [1, B] with indptr[j] > p
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (indptr[mid] > p) hi = mid; else lo = mid + 1;
+  }
+  return lo - 1;
+}
+
+template <int HKV, int D>
+struct Cfg {
+  static constexpr int kPPS = kConsumerWarps / HKV;  // pages per stage
+  static constexpr int kHalves = D / 64;
+  static constexpr int kStageBytes = kPPS * 2 * kHalves * HKV * kBoxBytes;
+  // byte offset of the box (page j, K=0/V=1, half, head) inside a stage
+  __device__ static constexpr int box(int j, int kv, int half, int h) {
+    return (((j * 2 + kv) * kHalves + half) * HKV + h) * kBoxBytes;
+  }
+};
+
+template <int HKV, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                     const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
+  using C = Cfg<HKV, D>;
+  constexpr int NT = D / 8;   // 8-wide n tiles of the output
+  constexpr int KS = D / 16;  // 16-deep k steps of Q.K^T
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int stages = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * C::kStageBytes);
+  uint64_t* empty = full + stages;
+  float* comb = reinterpret_cast<float*>(empty + stages);  // [8 warps][G][D] o, then m, l
+
+  const int64_t total = p.indptr[p.batch];
+  const int n = num_ctas(total, p.grid);
+  const int c = blockIdx.x;
+  if (c >= n) return;
+  const int64_t p0 = total * c / n;
+  const int64_t p1 = total * (c + 1) / n;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_v);
+    const uint64_t policy = l2_policy_evict_first();
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed[4] = {0u, 0u, 0u, 0u};  // arms of each stage's full barrier
+    int b = seq_of(p.indptr, p.batch, p0);
+    for (int64_t pp = p0; pp < p1;) {
+      const int64_t seg_end = min(p1, static_cast<int64_t>(p.indptr[b + 1]));
+      for (int64_t q0 = pp; q0 < seg_end; q0 += C::kPPS) {
+        const int np = static_cast<int>(min(static_cast<int64_t>(C::kPPS), seg_end - q0));
+        if (!mbar_wait(&empty[stage], phase ^ 1)) {
+          report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+          // The consumers stopped releasing stages. Issue nothing more, wait (bounded)
+          // for the loads already in flight, and leave.
+          for (int s = 0; s < stages; ++s)
+            if (armed[s] > 0) (void)mbar_wait(&full[s], (armed[s] - 1) & 1);
+          return;
+        }
+        mbar_arrive_expect_tx(&full[stage], np * 2 * C::kHalves * HKV * kBoxBytes);
+        ++armed[stage];
+        uint8_t* sb = smem + stage * C::kStageBytes;
+        for (int j = 0; j < np; ++j) {
+          int pid = p.indices[q0 + j];
+          if (pid < 0 || pid >= p.num_pages) {
+            report(p.status, NSLG_DEV_BAD_PAGE);
+            pid = 0;  // keep the transaction count; page 0 is the pool's null page
+          }
+#pragma unroll
+          for (int half = 0; half < C::kHalves; ++half)
+#pragma unroll
+            for (int h = 0; h < HKV; ++h) {
+              tma_load_3d(sb + C::box(j, 0, half, h), &tmap_k, &full[stage], half * 64, h,
+                          pid * kPS, policy);
+              tma_load_3d(sb + C::box(j, 1, half, h), &tmap_v, &full[stage], half * 64, h,
+                          pid * kPS, policy);
+            }
+        }
+        if (++stage == stages) { stage = 0; phase ^= 1; }
+      }
+      pp = seg_end;
+      ++b;
+      while (b < p.batch && p.indptr[b + 1] <= pp) ++b;
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int h = warp % HKV;
+  const int j = warp / HKV;
+  const int g = lane >> 2;        // mma row group: query head g (and g + 8)
+  const int tq = lane & 3;        // thread in quad
+  const int G = p.group;
+  const float sl = p.scale_log2;
+  int stage = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  int b = seq_of(p.indptr, p.batch, p0);
+  for (int64_t pp = p0; pp < p1;) {
+    const int64_t seq_beg = p.indptr[b];
+    const int64_t seq_end = p.indptr[b + 1];
+    const int64_t seg_beg = pp;
+    const int64_t seg_end = min(p1, seq_end);
+    const int last_len = p.lpl[b];
+
+    // Q fragments (A operand, 16 rows = query heads h*G + r, r < G).
+    uint32_t qa[KS][4];
+    {
+      const __nv_bfloat16* qb = p.q + static_cast<int64_t>(b) * p.q_stride +
+                                static_cast<int64_t>(h) * G * D;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const int col = ks * 16 + tq * 2;
+        qa[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * D + col) : 0u;
+        qa[ks][1] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + col) : 0u;
+        qa[ks][2] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * D + col + 8) : 0u;
+        qa[ks][3] =
+            g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + col + 8) : 0u;
+      }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    for (int64_t q0 = seg_beg; q0 < seg_end; q0 += C::kPPS) {
+      const int np = static_cast<int>(min(static_cast<int64_t>(C::kPPS), seg_end - q0));
+      if (ok) {
+        // warp-uniform: a warp that gives up stops consuming and stops releasing
+        // stages, but keeps the control flow (and the named barriers) of the others
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase));
+        if (!ok && lane == 0) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+      }
+      if (ok && j < np) {
+        const int nvalid = (q0 + j == seq_end - 1) ? last_len : kPS;
+        const uint32_t sb = smem_u32(smem + stage * C::kStageBytes);
+        // ---- S = Q . K^T over the page's 16 tokens
+        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        {
+          const int mi = lane >> 3, r = lane & 7;
+          const int tok = (mi >> 1) * 8 + r;
+#pragma unroll
+          for (int ks = 0; ks < KS; ++ks) {
+            const int half = ks >> 2;
+            const int chunk = ((ks & 3) << 1) + (mi & 1);
+            const uint32_t addr = sb + C::box(j, 0, half, h) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+            uint32_t b00, b01, b10, b11;
+            ldmatrix_x4(addr, b00, b01, b10, b11);
+            mma_bf16_16816(s[0], qa[ks], b00, b01);
+            mma_bf16_16816(s[1], qa[ks], b10, b11);
+          }
+        }
+        // ---- mask the tail of the last page, online softmax
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (nt * 8 + tq * 2 + (e & 1) >= nvalid) s[nt][e] = -INFINITY;
+        float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+        float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float base0 = mn0 == -INFINITY ? 0.f : mn0 * sl;
+        const float base1 = mn1 == -INFINITY ? 0.f : mn1 * sl;
+        const float a0 = fast_exp2(fmaf(m0, sl, -base0));
+        const float a1 = fast_exp2(fmaf(m1, sl, -base1));
+        m0 = mn0;
+        m1 = mn1;
+        float ps[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          ps[nt][0] = fast_exp2(fmaf(s[nt][0], sl, -base0));
+          ps[nt][1] = fast_exp2(fmaf(s[nt][1], sl, -base0));
+          ps[nt][2] = fast_exp2(fmaf(s[nt][2], sl, -base1));
+          ps[nt][3] = fast_exp2(fmaf(s[nt][3], sl, -base1));
+        }
+        l0 = fmaf(l0, a0, ps[0][0] + ps[0][1] + ps[1][0] + ps[1][1]);
+        l1 = fmaf(l1, a1, ps[0][2] + ps[0][3] + ps[1][2] + ps[1][3]);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          o[t][0] *= a0; o[t][1] *= a0;
+          o[t][2] *= a1; o[t][3] *= a1;
+        }
+        uint32_t pa[4];
+        pa[0] = pack_bf16x2(ps[0][0], ps[0][1]);
+        pa[1] = pack_bf16x2(ps[0][2], ps[0][3]);
+        pa[2] = pack_bf16x2(ps[1][0], ps[1][1]);
+        pa[3] = pack_bf16x2(ps[1][2], ps[1][3]);
+        // ---- O += P . V
+        {
+          const int mi = lane >> 3, r = lane & 7;
+          const int tok = (mi & 1) * 8 + r;
+#pragma unroll
+          for (int qd = 0; qd < D / 16; ++qd) {
+            const int cg = qd * 2 + (mi >> 1);  // 8-dim chunk of the head row
+            const int half = cg >> 3, ch = cg & 7;
+            const uint32_t addr = sb + C::box(j, 1, half, h) + tok * 128 + ((ch ^ (tok & 7)) << 4);
+            uint32_t v0, v1, v2, v3;
+            ldmatrix_x4_trans(addr, v0, v1, v2, v3);
+            mma_bf16_16816(o[2 * qd], pa, v0, v1);
+            mma_bf16_16816(o[2 * qd + 1], pa, v2, v3);
+          }
+        }
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == stages) { stage = 0; phase ^= 1; }
+    }
+    pp = seg_end;
+
+    // ---- finish the segment: row sums over the quad
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+    if constexpr (C::kPPS > 1) {
+      // warps sharing kv head h (j = 1..kPPS-1) hand their state to warp j == 0
+      float* cw = comb + static_cast<size_t>(warp) * G * (D + 2);
+      if (j > 0) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const int col = t * 8 + tq * 2;
+          if (g < G) { cw[g * D + col] = o[t][0]; cw[g * D + col + 1] = o[t][1]; }
+          if (g + 8 < G) { cw[(g + 8) * D + col] = o[t][2]; cw[(g + 8) * D + col + 1] = o[t][3]; }
+        }
+        if (tq == 0) {
+          if (g < G) { cw[G * D + g] = m0; cw[G * D + G + g] = l0; }
+          if (g + 8 < G) { cw[G * D + g + 8] = m1; cw[G * D + G + g + 8] = l1; }
+        }
+      }
+      named_barrier_sync(1, kConsumerWarps * 32);
+      if (j == 0) {
+        for (int jj = 1; jj < C::kPPS; ++jj) {
+          const float* cx = comb + static_cast<size_t>(jj * HKV + h) * G * (D + 2);
+          const float mx0 = g < G ? cx[G * D + g] : -INFINITY;
+          const float lx0 = g < G ? cx[G * D + G + g] : 0.f;
+          const float mx1 = g + 8 < G ? cx[G * D + g + 8] : -INFINITY;
+          const float lx1 = g + 8 < G ? cx[G * D + G + g + 8] : 0.f;
+          const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+          const float b0 = mn0 == -INFINITY ? 0.f : mn0 * sl;
+          const float b1 = mn1 == -INFINITY ? 0.f : mn1 * sl;
+          const float wa0 = fast_exp2(fmaf(m0, sl, -b0)), wb0 = fast_exp2(fmaf(mx0, sl, -b0));
+          const float wa1 = fast_exp2(fmaf(m1, sl, -b1)), wb1 = fast_exp2(fmaf(mx1, sl, -b1));
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const int col = t * 8 + tq * 2;
+            const float x0 = g < G ? cx[g * D + col] : 0.f;
+            const float x1 = g < G ? cx[g * D + col + 1] : 0.f;
+            const float x2 = g + 8 < G ? cx[(g + 8) * D + col] : 0.f;
+            const float x3 = g + 8 < G ? cx[(g + 8) * D + col + 1] : 0.f;
+            o[t][0] = o[t][0] * wa0 + x0 * wb0;
+            o[t][1] = o[t][1] * wa0 + x1 * wb0;
+            o[t][2] = o[t][2] * wa1 + x2 * wb1;
+            o[t][3] = o[t][3] * wa1 + x3 * wb1;
+          }
+          l0 = l0 * wa0 + lx0 * wb0;
+          l1 = l1 * wa1 + lx1 * wb1;
+          m0 = mn0;
+          m1 = mn1;
+        }
+      }
+    }
+
+    if (j == 0 && ok) {
+      const bool whole = cta_of(seq_beg, total, n) == cta_of(seq_end - 1, total, n);
+      const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+      const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int r = g + rr * 8;
+        if (r >= G) continue;
+        const int hq = h * G + r;
+        const float inv = rr ? inv1 : inv0;
+        if (whole) {
+          __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride +
+                              static_cast<int64_t>(hq) * D;
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+            *reinterpret_cast<uint32_t*>(ob + t * 8 + tq * 2) =
+                pack_bf16x2(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
+        } else {
+          const int64_t slot = static_cast<int64_t>(b) + c;
+          float* po = p.part_o + (slot * p.hq + hq) * D;
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+            *reinterpret_cast<float2*>(po + t * 8 + tq * 2) =
+                make_float2(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
+          if (tq == 0) {
+            const float m = rr ? m1 : m0, l = rr ? l1 : l0;
+            p.part_lse[slot * p.hq + hq] = l > 0.f ? m * sl + __log2f(l) : -INFINITY;
+          }
+        }
+      }
+    }
+    if constexpr (C::kPPS > 1) named_barrier_sync(1, kConsumerWarps * 32);
+    ++b;
+    while (b < p.batch && p.indptr[b + 1] <= pp) ++b;
+  }
+}
+
+// Combines the partials of sequences that span several CTAs; one warp per
+// (sequence, query head). Sequences finished in place by the decode kernel, and
+// sequences without pages (written as zeros here), need no merge.
+template <int D>
+__global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int hq = blockIdx.x * 4 + warp;
+  const int b = blockIdx.y;
+  if (hq >= p.hq) return;
+  constexpr int DV = D / 32;
+  __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
+  const int64_t total = p.indptr[p.batch];
+  const int64_t beg = p.indptr[b], end = p.indptr[b + 1];
+  if (beg == end) {
+#pragma unroll
+    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const int n = num_ctas(total, p.grid);
+  const int cf = cta_of(beg, total, n), cl = cta_of(end - 1, total, n);
+  if (cf == cl) return;
+  float mx = -INFINITY;
+  for (int c = cf; c <= cl; ++c) mx = fmaxf(mx, p.part_lse[(static_cast<int64_t>(b) + c) * p.hq + hq]);
+  float acc[DV];
+#pragma unroll
+  for (int e = 0; e < DV; ++e) acc[e] = 0.f;
+  float wsum = 0.f;
+  for (int c = cf; c <= cl; ++c) {
+    const int64_t slot = static_cast<int64_t>(b) + c;
+    const float lse = p.part_lse[slot * p.hq + hq];
+    const float w = lse == -INFINITY ? 0.f : fast_exp2(lse - mx);
+    wsum += w;
+    const float* po = p.part_o + (slot * p.hq + hq) * D + lane * DV;
+#pragma unroll
+    for (int e = 0; e < DV; ++e) acc[e] = fmaf(w, po[e], acc[e]);
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+  for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(acc[e] * inv);
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// Tensor maps are cached per (pool layer pointer, pages, heads, head_dim): the pool is
+// allocated once and each layer's K and V maps are reused on every step.
+struct MapEntry {
+  const void* ptr = nullptr;
+  int64_t pages = 0;
+  int hkv = 0, d = 0;
+  CUtensorMap map;
+};
+constexpr int kMapCache = 512;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+std::mutex g_map_mu;
+
+int pool_tensor_map(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  for (int i = 0; i < kMapCache; ++i) {
+    const MapEntry& e = g_maps[i];
+    if (e.ptr == pool && e.pages == pages && e.hkv == hkv && e.d == d) {
+      *out = e.map;
+      return NSLG_OK;
+    }
+  }
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return set_error(NSLG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  // dims (innermost first): head_dim, kv head, token row (= page * 16 + slot)
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(hkv),
+                              static_cast<cuuint64_t>(pages) * kPS};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2,
+                                 static_cast<cuuint64_t>(hkv) * d * 2};
+  const cuuint32_t box[3] = {64, 1, kPS};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  MapEntry& e = g_maps[g_map_next];
+  const CUresult r = enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(pool),
+                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    e.ptr = nullptr;
+    return set_error(NSLG_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  }
+  e.ptr = pool;
+  e.pages = pages;
+  e.hkv = hkv;
+  e.d = d;
+  *out = e.map;
+  g_map_next = (g_map_next + 1) % kMapCache;
+  return NSLG_OK;
+}
+
+template <int HKV, int D>
+int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
+                 cudaStream_t stream) {
+  using C = Cfg<HKV, D>;
+  const size_t comb = C::kPPS > 1 ? static_cast<size_t>(kConsumerWarps) * p.group * (D + 2) * 4 : 0;
+  const size_t fixed = 1024 + comb + 2 * 8 * 8;
+  int stages = static_cast<int>((kMaxSmem - fixed) / C::kStageBytes);
+  if (stages > 4) stages = 4;
+  if (stages < 2) return set_error(NSLG_ERR_UNSUPPORTED, "decode: group too large for smem");
+  p.stages = stages;
+  const size_t smem = 1024 + static_cast<size_t>(stages) * C::kStageBytes + 2 * stages * 8 + comb;
+  auto kern = decode_tc_kernel<HKV, D>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
+  kern<<<p.grid, kThreads, smem, stream>>>(tk, tv, p);
+  int rc = check_launch("decode_tc");
+  if (rc != NSLG_OK) return rc;
+  dim3 mgrid((p.hq + 3) / 4, p.batch);
+  decode_merge_kernel<D><<<mgrid, 128, 0, stream>>>(p);
+  return check_launch("decode_merge");
+}
+
+}  // namespace
+
+bool decode_tc_supported(int dtype, int hq, int hkv, int d, int page_size) {
+  return dtype == NSLG_DTYPE_BF16 && page_size == kPS && (d == 128 || d == 64) &&
+         (hkv == 1 || hkv == 2 || hkv == 4 || hkv == 8) && hq % hkv == 0 && hq / hkv <= 16;
+}
+
+int64_t decode_tc_workspace_bytes(int batch, int hq, int d) {
+  const int64_t slots = static_cast<int64_t>(batch) + sm_count();
+  return slots * hq * (static_cast<int64_t>(d) + 1) * 4 + 256;
+}
+
+int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int64_t q_stride,
+                           void* out, int64_t out_stride, const void* pool_k,
+                           const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
+                           const int32_t* kv_indices, const int32_t* kv_last_page_len,
+                           float sm_scale, void* workspace, int64_t workspace_bytes,
+                           uint32_t* status, cudaStream_t stream) {
+  if (batch == 0) return NSLG_OK;
+  const int64_t need = decode_tc_workspace_bytes(batch, hq, d);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(NSLG_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need) + " bytes");
+  if (num_pages * kPS > (int64_t{1} << 31))
+    return set_error(NSLG_ERR_UNSUPPORTED, "decode: pool larger than 2^31 token rows");
+  CUtensorMap tk, tv;
+  int rc = pool_tensor_map(pool_k, num_pages, hkv, d, &tk);
+  if (rc != NSLG_OK) return rc;
+  rc = pool_tensor_map(pool_v, num_pages, hkv, d, &tv);
+  if (rc != NSLG_OK) return rc;
+  const int grid = sm_count();
+  const int64_t slots = static_cast<int64_t>(batch) + grid;
+  uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
+  DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.indptr = kv_indptr;
+  p.indices = kv_indices;
+  p.lpl = kv_last_page_len;
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_lse = p.part_o + slots * hq * d;
+  p.q_stride = q_stride;
+  p.out_stride = out_stride;
+  p.num_pages = num_pages;
+  p.batch = batch;
+  p.hq = hq;
+  p.group = hq / hkv;
+  p.grid = grid;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.status = status;
+  if (d == 128) {
+    switch (hkv) {
+      case 1: return launch_typed<1, 128>(tk, tv, p, stream);
+      case 2: return launch_typed<2, 128>(tk, tv, p, stream);
+      case 4: return launch_typed<4, 128>(tk, tv, p, stream);
+      case 8: return launch_typed<8, 128>(tk, tv, p, stream);
+    }
+  } else if (d == 64) {
+    switch (hkv) {
+      case 1: return launch_typed<1, 64>(tk, tv, p, stream);
+      case 2: return launch_typed<2, 64>(tk, tv, p, stream);
+      case 4: return launch_typed<4, 64>(tk, tv, p, stream);
+      case 8: return launch_typed<8, 64>(tk, tv, p, stream);
+    }
+  }
+  return set_error(NSLG_ERR_UNSUPPORTED, "decode: unsupported head count / head_dim");
+}
+
+}  // namespace nslg

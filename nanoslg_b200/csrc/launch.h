@@ -1,0 +1,54 @@
+// Host-side declarations shared by the kernel files and the C ABI in capi.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/nslg_b200.h"
+
+namespace nslg {
+
+// Records `msg` as this thread's last error and returns `code`.
+int set_error(int code, const std::string& msg);
+
+// Turns a pending launch error into NSLG_ERR_CUDA with the kernel's name.
+int check_launch(const char* what);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, const void* q,
+                          int64_t q_stride, const void* k, int64_t k_stride, const void* v,
+                          int64_t v_stride, void* q_out, const int32_t* positions,
+                          const float* cos_t, const float* sin_t, int64_t table_rows,
+                          const int32_t* write_loc, void* pool_k, void* pool_v,
+                          int64_t pool_slots, uint32_t* status, cudaStream_t stream);
+
+int launch_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int64_t x_stride,
+                            void* residual, int64_t residual_stride, const void* weight,
+                            void* out, int64_t out_stride, float eps, cudaStream_t stream);
+
+// CUDA-core paged attention (any page size, head_dim <= 256, fp32 or bf16): decode is
+// the qo_len == 1 case.
+int launch_paged_attention_simt(int dtype, int batch, int hq, int hkv, int d, int page_size,
+                                const void* q, int64_t q_stride, void* out,
+                                int64_t out_stride, const int32_t* qo_indptr,
+                                const int32_t* q_row_start, int max_qo_len,
+                                const void* pool_k, const void* pool_v, int64_t num_pages,
+                                const int32_t* kv_indptr, const int32_t* kv_indices,
+                                const int32_t* kv_last_page_len, float sm_scale, int causal,
+                                uint32_t* status, cudaStream_t stream);
+
+// TMA-fed split-KV decode for bf16, page_size 16, head_dim 128.
+bool decode_tc_supported(int dtype, int hq, int hkv, int d, int page_size);
+int64_t decode_tc_workspace_bytes(int batch, int hq, int d);
+int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int64_t q_stride,
+                           void* out, int64_t out_stride, const void* pool_k,
+                           const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
+                           const int32_t* kv_indices, const int32_t* kv_last_page_len,
+                           float sm_scale, void* workspace, int64_t workspace_bytes,
+                           uint32_t* status, cudaStream_t stream);
+
+}  // namespace nslg

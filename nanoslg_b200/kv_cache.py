@@ -1,0 +1,635 @@
+"""B200 paged KV cache behind NanoSLG's ``CacheContext`` boundary.
+
+Drop-in for ``nanoslg/kv_cache.py``: the same ``KVCacheConfig``, ``CacheContext`` and
+``KVCacheManager`` ABCs, the same page pool (page 0 = null page, refcounts, a free *set*
+whose ``pop()`` order decides page ids, zero-on-alloc, copy-on-write) and the same
+per-token radix prefix tree, so page tables, write slots and CSR arrays are bit-exact
+with the reference's (kv_cache.py:382-531, 694-777).  What changes is behind
+``attend()``: instead of FlashInfer's wrappers (kv_cache.py:703-705, 618-632, 650, 654)
+or contiguous SDPA (kv_cache.py:312-322), each layer launches the sm_100a kernels of
+``nanoslg_b200/csrc`` through the C ABI -- the KV append (optionally fused with RoPE,
+see ``attend_rope``) and split-KV decode or causal prefill attention reading the pages
+in place.  The per-forward plan (positions, write slots, CSR) is built once per
+``begin_forward`` and shipped to the device in one host-to-device copy.
+
+``create_cache_manager`` always returns the B200 backend: there is no second backend
+and no CPU fallback; the bookkeeping itself runs on any device (tests drive it with
+CPU tensors), the kernels need CUDA.
+"""
+import itertools
+import math
+import threading
+from abc import ABC, abstractmethod
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Set, Tuple
+
+import numpy as np
+import torch
+
+from . import ops
+
+
+@dataclass
+class KVCacheConfig:
+    """Cache sizing (kv_cache.py:59-145). ``backend`` is kept for config compatibility;
+    every value selects the B200 paged backend."""
+    num_layers: int
+    num_kv_heads: int          # per TP rank
+    num_qo_heads: int          # per TP rank
+    head_dim: int
+    page_size: int = 16
+    max_pages: int = 0         # 0 = auto
+    max_batch_size: int = 8
+    max_seq_len: int = 4096
+    memory_fraction: float = 0.30
+    dtype: torch.dtype = torch.bfloat16
+    device: torch.device = None
+    enable_prefix_caching: bool = True
+    backend: str = "b200"
+
+    def __post_init__(self):
+        if self.backend not in ("auto", "b200", "flashinfer", "contiguous"):
+            raise ValueError(f"unknown kv backend {self.backend!r}")
+        self.backend = "b200"
+        if self.max_pages <= 0:
+            self.max_pages = self._auto_pages()
+
+    def _elem_bytes(self) -> int:
+        return {torch.float16: 2, torch.bfloat16: 2, torch.float32: 4}.get(self.dtype, 2)
+
+    def _auto_pages(self) -> int:
+        """Same budget rule as the reference (kv_cache.py:88-102): free memory minus a
+        max(2 GiB, 15%) headroom, times memory_fraction, capped at 65536 pages."""
+        if self.device is None or torch.device(self.device).type != "cuda":
+            return 256
+        try:
+            free, total = torch.cuda.mem_get_info(self.device)
+        except Exception:
+            return 256
+        headroom = max(2 << 30, int(total * 0.15))
+        budget = int(max(0, free - headroom) * self.memory_fraction)
+        per_page = (2 * self.num_layers * self.page_size * self.num_kv_heads
+                    * self.head_dim * self._elem_bytes())
+        return max(64, min(budget // max(per_page, 1), 65536))
+
+    @classmethod
+    def from_hf_config(cls, hf_config, parallel_config=None, device=None, **kw):
+        """Per-rank shape from an HF config (kv_cache.py:119-145)."""
+        nl = getattr(hf_config, "num_hidden_layers", getattr(hf_config, "num_layers", 32))
+        nkv = getattr(hf_config, "num_key_value_heads",
+                      getattr(hf_config, "multi_query_group_num",
+                              getattr(hf_config, "num_attention_heads", 32)))
+        nq = getattr(hf_config, "num_attention_heads", 32)
+        hd = getattr(hf_config, "head_dim",
+                     getattr(hf_config, "kv_channels", hf_config.hidden_size // nq))
+        if parallel_config is not None:
+            tp = parallel_config.tp_size
+            if tp > 1:
+                nkv //= tp
+                nq //= tp
+            if parallel_config.pp_size > 1 and parallel_config.pp_layer_splits:
+                try:
+                    from .parallel import ParallelContext
+                    ctx = ParallelContext.get()
+                    if ctx and ctx.pp_rank in parallel_config.pp_layer_splits:
+                        nl = len(parallel_config.pp_layer_splits[ctx.pp_rank])
+                except Exception:
+                    pass
+        return cls(num_layers=nl, num_kv_heads=nkv, num_qo_heads=nq, head_dim=hd,
+                   device=device, **kw)
+
+
+class CacheContext(ABC):
+    """Per-forward context handed to every layer (kv_cache.py:149-163)."""
+    seq_ids: List[str]
+    new_token_counts: List[int]
+    input_offsets: List[int]
+    batch_size: int
+    seq_lens: List[int]
+
+    @abstractmethod
+    def get_position_ids(self, max_input_len: int) -> torch.Tensor: ...
+
+    @abstractmethod
+    def attend(self, layer_idx: int, q: torch.Tensor, k_new: torch.Tensor,
+               v_new: torch.Tensor, n_heads: int, n_kv_heads: int) -> torch.Tensor: ...
+
+    @abstractmethod
+    def get_start_pos(self, batch_idx: int = 0) -> int: ...
+
+
+class KVCacheManager(ABC):
+    """Cache manager interface (kv_cache.py:166-189)."""
+    cfg: KVCacheConfig
+
+    @abstractmethod
+    def allocate_sequence(self, seq_id: str, token_ids: Optional[List[int]] = None,
+                          num_tokens: int = 0) -> int: ...
+
+    @abstractmethod
+    def extend_sequence(self, seq_id: str, num_new: int = 1): ...
+
+    @abstractmethod
+    def begin_forward(self, seq_ids: List[str], new_token_counts: List[int],
+                      input_offsets: Optional[List[int]] = None) -> CacheContext: ...
+
+    @abstractmethod
+    def end_forward(self, ctx: CacheContext): ...
+
+    @abstractmethod
+    def release_sequence(self, seq_id: str): ...
+
+    @abstractmethod
+    def append_token_ids(self, seq_id: str, new_ids: List[int]): ...
+
+    @abstractmethod
+    def reset(self): ...
+
+    @property
+    @abstractmethod
+    def stats(self) -> Dict: ...
+
+
+class PagePool:
+    """K/V pages ``[num_layers, max_pages, page_size, num_kv_heads, head_dim]``; page 0 is
+    the permanent null page (kv_cache.py:382-442).
+
+    Page ids come from ``set.pop()`` on a free set built and updated exactly as the
+    reference does, so the same call sequence hands out the same ids.  The reference
+    zeroes a page on every allocation with two small copies per page; here the ids are
+    queued and zeroed together by ``flush_zero()`` before the device next touches the
+    pool (the context calls it when it is built, ``cow`` before its copy), which leaves
+    the same pool contents."""
+
+    def __init__(self, cfg: KVCacheConfig):
+        self.cfg = cfg
+        shape = (cfg.num_layers, cfg.max_pages, cfg.page_size, cfg.num_kv_heads, cfg.head_dim)
+        self.k = torch.zeros(shape, dtype=cfg.dtype, device=cfg.device)
+        self.v = torch.zeros(shape, dtype=cfg.dtype, device=cfg.device)
+        self.ref_count = [0] * cfg.max_pages
+        self.tokens_used = [0] * cfg.max_pages
+        self.ref_count[0] = 1
+        self.free_set: Set[int] = set(range(1, cfg.max_pages))
+        self._lock = threading.Lock()
+        self._pending_zero: List[int] = []
+
+    def alloc(self, n=1) -> Optional[List[int]]:
+        with self._lock:
+            if len(self.free_set) < n:
+                return None
+            out = []
+            for _ in range(n):
+                pid = self.free_set.pop()
+                self.ref_count[pid] = 1
+                self.tokens_used[pid] = 0
+                out.append(pid)
+            self._pending_zero.extend(out)
+            return out
+
+    def flush_zero(self):
+        """Zeroes every page allocated since the last flush (all layers, K and V)."""
+        with self._lock:
+            if not self._pending_zero:
+                return
+            ids = sorted(set(self._pending_zero))
+            self._pending_zero.clear()
+        idx = torch.tensor(ids, dtype=torch.long).to(self.k.device, non_blocking=True)
+        self.k.index_fill_(1, idx, 0)
+        self.v.index_fill_(1, idx, 0)
+
+    def release(self, pid):
+        if pid <= 0:
+            return
+        with self._lock:
+            self.ref_count[pid] -= 1
+            if self.ref_count[pid] <= 0:
+                self.ref_count[pid] = 0
+                self.tokens_used[pid] = 0
+                self.free_set.add(pid)
+
+    def add_ref(self, pid):
+        with self._lock:
+            self.ref_count[pid] += 1
+
+    def is_shared(self, pid):
+        return self.ref_count[pid] > 1
+
+    def cow(self, pid):
+        new = self.alloc(1)
+        if new is None:
+            return None
+        d = new[0]
+        self.flush_zero()
+        self.k[:, d].copy_(self.k[:, pid])
+        self.v[:, d].copy_(self.v[:, pid])
+        self.tokens_used[d] = self.tokens_used[pid]
+        return d
+
+    @property
+    def num_free(self):
+        return len(self.free_set)
+
+    @property
+    def utilization(self):
+        return 1.0 - self.num_free / max(self.cfg.max_pages - 1, 1)
+
+
+class _RNode:
+    __slots__ = ("children", "page_id", "ref", "last_access", "depth")
+
+    def __init__(self, d=0):
+        self.children: Dict[int, "_RNode"] = {}
+        self.page_id = -1
+        self.ref = 0
+        self.last_access = 0
+        self.depth = d
+
+
+class RadixTree:
+    """Per-token prefix trie with a page id at every page-aligned depth
+    (kv_cache.py:453-531).  ``last_access`` is a logical clock ticked once per
+    match/insert call: the eviction order equals the reference's wall-clock order."""
+
+    def __init__(self, ps, pool):
+        self.root = _RNode()
+        self.ps = ps
+        self.pool = pool
+        self._lock = threading.Lock()
+        self._clock = 0
+
+    def _tick(self):
+        self._clock += 1
+        return self._clock
+
+    def match(self, tokens):
+        with self._lock:
+            node, pages, now = self.root, [], self._tick()
+            for i, tok in enumerate(tokens):
+                ch = node.children.get(tok)
+                if ch is None:
+                    break
+                node = ch
+                node.last_access = now
+                if (i + 1) % self.ps == 0 and node.page_id >= 0:
+                    if self.pool.ref_count[node.page_id] > 0:
+                        pages.append(node.page_id)
+                    else:
+                        node.page_id = -1
+                        break
+            return len(pages) * self.ps, pages
+
+    def insert(self, tokens, page_ids):
+        with self._lock:
+            node, pi, now = self.root, 0, self._tick()
+            for i, tok in enumerate(tokens):
+                if tok not in node.children:
+                    node.children[tok] = _RNode(i + 1)
+                node = node.children[tok]
+                node.last_access = now
+                if (i + 1) % self.ps == 0 and pi < len(page_ids):
+                    incoming = page_ids[pi]
+                    pi += 1
+                    if node.page_id < 0:
+                        node.page_id = incoming
+                        self.pool.add_ref(incoming)
+
+    def add_refs(self, tokens, n=1):
+        with self._lock:
+            node = self.root
+            for tok in tokens:
+                ch = node.children.get(tok)
+                if ch is None:
+                    break
+                node = ch
+                node.ref += n
+
+    def dec_refs(self, tokens, n=1):
+        with self._lock:
+            node = self.root
+            for tok in tokens:
+                ch = node.children.get(tok)
+                if ch is None:
+                    break
+                node = ch
+                node.ref = max(0, node.ref - n)
+
+    def evict_lru(self, need):
+        with self._lock:
+            cands = []
+            self._collect(self.root, cands)
+            cands.sort(key=lambda x: x[0])
+            freed = 0
+            for _, nd, par, edge in cands:
+                if freed >= need:
+                    break
+                if nd.ref > 0:
+                    continue
+                if nd.page_id >= 0:
+                    self.pool.release(nd.page_id)
+                    nd.page_id = -1
+                    freed += 1
+                if not nd.children and par is not None:
+                    par.children.pop(edge, None)
+            return freed
+
+    def _collect(self, node, out, par=None, edge=-1):
+        # iterative pre-order walk in the reference's visiting order (deep tries of
+        # long prompts would overflow Python's recursion limit)
+        stack = [(node, par, edge)]
+        while stack:
+            nd, pa, ed = stack.pop()
+            if nd.page_id >= 0 and nd.ref == 0:
+                out.append((nd.last_access, nd, pa, ed))
+            for t, ch in reversed(list(nd.children.items())):
+                stack.append((ch, nd, t))
+
+    @property
+    def cached_pages(self):
+        c, stack = 0, [self.root]
+        while stack:
+            n = stack.pop()
+            if n.page_id >= 0:
+                c += 1
+            stack.extend(n.children.values())
+        return c
+
+
+class _PagedSeqState:
+    __slots__ = ("seq_id", "block_table", "num_tokens", "prefix_len", "token_ids")
+
+    def __init__(self, sid, prefix_pages=None, plen=0, tids=None):
+        self.seq_id = sid
+        self.block_table = list(prefix_pages or [])
+        self.num_tokens = plen
+        self.prefix_len = plen
+        self.token_ids = list(tids or [])
+
+
+class B200CacheContext(CacheContext):
+    """Per-forward context of the B200 backend.
+
+    Host side (once per forward) it computes what ``FlashInferCacheContext.__init__``
+    computes (kv_cache.py:547-632): start positions and sequence lengths, the per-token
+    (page, slot) write targets with copy-on-write of shared pages, and the CSR page list
+    ``kv_indptr / kv_indices / kv_last_page_len`` (+ ``qo_indptr`` for prefill).  They
+    travel to the device in one copy as int32 arrays:
+
+      positions [B*iw]  absolute position of every input cell (0 for left padding)
+      write_loc [B*iw]  page*page_size + slot of every input cell, -1 = not written
+      kv_indptr [B+1], kv_indices [T], kv_last_page_len [B], qo_indptr [B+1],
+      q_row_start [B] = b*iw + input_offsets[b]  (first real row of sequence b)
+
+    Per layer, ``attend`` / ``attend_rope`` launch the append kernel and the decode
+    (all counts == 1) or prefill kernel; no Python loop runs per layer.
+    """
+
+    def __init__(self, cache: "B200PagedKVCache", seq_ids, new_token_counts, input_offsets):
+        self.cache = cache
+        self.seq_ids = seq_ids
+        self.new_token_counts = new_token_counts
+        self.input_offsets = input_offsets or [0] * len(seq_ids)
+        self.batch_size = B = len(seq_ids)
+        cfg = cache.cfg
+        pool = cache.pool
+        ps = cfg.page_size
+        dev = cfg.device
+
+        self.start_positions = [cache.seqs[s].num_tokens for s in seq_ids]
+        self.seq_lens = [self.start_positions[i] + new_token_counts[i] for i in range(B)]
+        self.max_kv_len = max(self.seq_lens) if self.seq_lens else 0
+        self._is_decode = all(n == 1 for n in new_token_counts)
+        self._iw = (max(o + n for o, n in zip(self.input_offsets, new_token_counts))
+                    if B else 1)
+        iw = self._iw
+
+        # write targets with copy-on-write, page by page in the reference's order
+        # (kv_cache.py:575-594: the first token written into a shared page copies it)
+        positions = np.zeros((B, iw), dtype=np.int32)
+        write_loc = np.full((B, iw), -1, dtype=np.int32)
+        self._write_info: List[List[Tuple[int, int]]] = []
+        for b in range(B):
+            st = cache.seqs[seq_ids[b]]
+            n = new_token_counts[b]
+            o = self.input_offsets[b]
+            start = st.num_tokens
+            info: List[Tuple[int, int]] = []
+            if n > 0:
+                positions[b, o:o + n] = np.arange(start, start + n, dtype=np.int32)
+                ap = start
+                end = start + n
+                while ap < end:
+                    pi = ap // ps
+                    stop = min(end, (pi + 1) * ps)
+                    if pi >= len(st.block_table):
+                        info.extend([(0, 0)] * (stop - ap))
+                    else:
+                        pid = st.block_table[pi]
+                        if pool.is_shared(pid):
+                            np_ = pool.cow(pid)
+                            if np_ is None:
+                                raise RuntimeError("KV OOM during CoW")
+                            st.block_table[pi] = np_
+                            pool.release(pid)
+                            pid = np_
+                        info.extend((pid, sl) for sl in range(ap % ps, stop - pi * ps))
+                        pool.tokens_used[pid] = max(pool.tokens_used[pid], stop - pi * ps)
+                    ap = stop
+                write_loc[b, o:o + n] = [p_ * ps + s_ for p_, s_ in info]
+            self._write_info.append(info)
+
+        # CSR page list (kv_cache.py:598-615)
+        indptr = np.zeros(B + 1, dtype=np.int32)
+        lpl = np.zeros(max(B, 1), dtype=np.int32)
+        tables = []
+        for b in range(B):
+            st = cache.seqs[seq_ids[b]]
+            kv = self.seq_lens[b]
+            npg = -(-kv // ps) if kv > 0 else 0
+            bt = st.block_table
+            tables.append(bt[:npg] if npg <= len(bt) else bt + [0] * (npg - len(bt)))
+            indptr[b + 1] = indptr[b] + npg
+            lpl[b] = (kv - (npg - 1) * ps) if npg > 0 else 0
+        total = int(indptr[B])
+        indices = np.fromiter(itertools.chain.from_iterable(tables), dtype=np.int32,
+                              count=total) if total else np.zeros(1, dtype=np.int32)
+        qo = np.zeros(B + 1, dtype=np.int32)
+        qo[1:] = np.cumsum(new_token_counts, dtype=np.int64) if B else []
+        row_start = (np.arange(B, dtype=np.int32) * iw
+                     + np.asarray(self.input_offsets, dtype=np.int32)) if B else \
+            np.zeros(0, dtype=np.int32)
+
+        parts = [positions.ravel(), write_loc.ravel(), indptr, indices, lpl, qo, row_start]
+        offs = np.cumsum([0] + [p.size for p in parts])
+        flat = np.concatenate(parts)
+        host = torch.from_numpy(flat)
+        dev_t = torch.device(dev) if dev is not None else torch.device("cpu")
+        if dev_t.type == "cuda":
+            host = host.pin_memory()
+        pool.flush_zero()
+        d = host.to(dev_t, non_blocking=True)
+        views = [d[offs[i]:offs[i + 1]] for i in range(len(parts))]
+        (self._pos_i32, self._write_loc, self.kv_indptr, self.kv_indices,
+         self.kv_last_page_len, self.qo_indptr, self.q_row_start) = views
+        self.kv_indices = self.kv_indices[:max(total, 1)]
+        self._indptr_host = indptr
+        self._indices_host = indices[:total]
+        self._lpl_host = lpl[:B]
+        self._qo_host = qo
+        self._pos64 = None
+        self._sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    # -- CacheContext ------------------------------------------------------------
+    def get_position_ids(self, S):
+        if self._pos64 is None:
+            self._pos64 = self._pos_i32.view(self.batch_size, self._iw).long()
+        pos = self._pos64
+        if S <= self._iw:
+            return pos[:, :S]
+        return torch.cat([pos, pos.new_zeros(self.batch_size, S - self._iw)], 1)
+
+    def get_start_pos(self, idx=0):
+        return self.start_positions[idx]
+
+    def attend(self, layer_idx, q, k_new, v_new, n_heads, n_kv_heads):
+        """q, k_new already rotated (the ABC contract, models.py:99-105)."""
+        self._check_width(q)
+        pool = self.cache.pool
+        ops.rope_kv_append(None, k_new, v_new, None, None, None, self._write_loc,
+                           pool.k[layer_idx], pool.v[layer_idx], rotate=False)
+        return self._attention(layer_idx, q)
+
+    def attend_rope(self, layer_idx, q, k_new, v_new, cos, sin):
+        """Fused path: RoPE on q and k (positions from this context, rows of the fp32
+        cos/sin tables of models.py:37-66), KV append, attention."""
+        self._check_width(q)
+        pool = self.cache.pool
+        B, S, hq, d = q.shape
+        q_rot = ops.rope_kv_append(q, k_new, v_new, self._pos_i32, cos, sin, self._write_loc,
+                                   pool.k[layer_idx], pool.v[layer_idx])
+        return self._attention(layer_idx, q_rot.view(B, S, hq, d))
+
+    def _check_width(self, q):
+        if q.shape[0] != self.batch_size or q.shape[1] != self._iw:
+            raise ValueError(f"attend: q is {tuple(q.shape[:2])}, the context was planned for "
+                             f"{(self.batch_size, self._iw)} (batch, input width)")
+
+    def _attention(self, layer_idx, q):
+        B, S, hq, d = q.shape
+        pool = self.cache.pool
+        pk, pv = pool.k[layer_idx], pool.v[layer_idx]
+        if self._is_decode:
+            out = ops.paged_decode(q[:, 0], pk, pv, self.kv_indptr, self.kv_indices,
+                                   self.kv_last_page_len, self._sm_scale)
+            return out.view(B, 1, hq * d)
+        out = torch.zeros((B, S, hq, d), dtype=q.dtype, device=q.device)
+        ops.paged_prefill(q, self.qo_indptr, S, pk, pv, self.kv_indptr, self.kv_indices,
+                          self.kv_last_page_len, self._sm_scale, causal=True,
+                          q_row_start=self.q_row_start, out=out)
+        return out.view(B, S, hq * d)
+
+
+class B200PagedKVCache(KVCacheManager):
+    """Paged manager (kv_cache.py:694-777) with the FlashInfer wrappers removed."""
+
+    def __init__(self, cfg: KVCacheConfig):
+        self.cfg = cfg
+        self.pool = PagePool(cfg)
+        self.tree = RadixTree(cfg.page_size, self.pool) if cfg.enable_prefix_caching else None
+        self.seqs: Dict[str, _PagedSeqState] = {}
+
+    def allocate_sequence(self, seq_id, token_ids=None, num_tokens=0):
+        tids = token_ids or []
+        total = len(tids) if tids else num_tokens
+        plen, ppages = 0, []
+        if self.tree and len(tids) >= self.cfg.page_size:
+            plen, ppages = self.tree.match(tids)
+            for p in ppages:
+                self.pool.add_ref(p)
+            if ppages:
+                self.tree.add_refs(tids[:plen])
+        st = _PagedSeqState(seq_id, ppages, plen, tids)
+        st.num_tokens = plen
+        new = total - plen
+        if new > 0:
+            st.block_table.extend(self._alloc(math.ceil(new / self.cfg.page_size)))
+        self.seqs[seq_id] = st
+        return plen
+
+    def extend_sequence(self, seq_id, num_new=1):
+        st = self.seqs[seq_id]
+        need = math.ceil((st.num_tokens + num_new) / self.cfg.page_size)
+        if need > len(st.block_table):
+            st.block_table.extend(self._alloc(need - len(st.block_table)))
+
+    def begin_forward(self, seq_ids, ntoks, offsets=None):
+        for s, n in zip(seq_ids, ntoks):
+            self.extend_sequence(s, n)
+        return B200CacheContext(self, seq_ids, ntoks, offsets)
+
+    def end_forward(self, ctx):
+        for b in range(ctx.batch_size):
+            self.seqs[ctx.seq_ids[b]].num_tokens += ctx.new_token_counts[b]
+
+    def release_sequence(self, seq_id):
+        if seq_id not in self.seqs:
+            return
+        st = self.seqs[seq_id]
+        if self.tree and st.token_ids:
+            nf = st.num_tokens // self.cfg.page_size
+            if nf:
+                self.tree.insert(st.token_ids[:nf * self.cfg.page_size], st.block_table[:nf])
+            if st.prefix_len:
+                self.tree.dec_refs(st.token_ids[:st.prefix_len])
+        for p in st.block_table:
+            self.pool.release(p)
+        del self.seqs[seq_id]
+
+    def append_token_ids(self, seq_id, ids):
+        if seq_id in self.seqs:
+            self.seqs[seq_id].token_ids.extend(ids)
+
+    def reset(self):
+        for s in list(self.seqs):
+            self.release_sequence(s)
+
+    def _alloc(self, n):
+        pages = self.pool.alloc(n)
+        if pages:
+            return pages
+        if self.tree:
+            if self.tree.evict_lru(n) > 0:
+                pages = self.pool.alloc(n)
+                if pages:
+                    return pages
+        raise RuntimeError(f"KV OOM: need {n}, free {self.pool.num_free}")
+
+    @property
+    def stats(self):
+        return {"backend": "b200",
+                "active_seqs": len(self.seqs),
+                "pages_used": self.cfg.max_pages - 1 - self.pool.num_free,
+                "pages_free": self.pool.num_free,
+                "util": f"{self.pool.utilization:.1%}",
+                "radix": self.tree.cached_pages if self.tree else 0}
+
+
+def create_cache_manager(hf_config, parallel_config, device, dtype, model_config,
+                         max_batch_size=4) -> KVCacheManager:
+    """Factory with the reference's signature (kv_cache.py:780-804); always the B200
+    paged backend."""
+    dev = torch.device(device) if device is not None else None
+    if dev is not None and dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
+    kv_cfg = KVCacheConfig.from_hf_config(
+        hf_config, parallel_config=parallel_config, device=device,
+        page_size=getattr(model_config, "page_size", 16),
+        max_pages=getattr(model_config, "max_kv_pages", 0),
+        max_batch_size=max_batch_size,
+        max_seq_len=getattr(model_config, "max_seq_len", 4096),
+        memory_fraction=getattr(model_config, "kv_memory_fraction", 0.30),
+        dtype=dtype,
+        enable_prefix_caching=getattr(model_config, "enable_prefix_caching", True),
+        backend=getattr(model_config, "kv_backend", "auto"),
+    )
+    return B200PagedKVCache(kv_cfg)

@@ -1,0 +1,253 @@
+"""Llama-architecture models driving the per-layer path (nanoslg/models.py:25-383).
+
+Same module tree and parameter names as the reference's LlamaTP / LlamaPP / LlamaHybrid
+(so its weight loaders and init rules apply unchanged), with three changes on the hot
+path:
+
+* ``RMSNorm`` runs the fused residual-add + RMSNorm kernel.  The blocks carry the
+  residual stream explicitly: block i returns (mlp_out, residual) and block i+1 adds
+  them inside its input norm.  The sums are the reference's ``h = x + attn`` and
+  ``x + mlp`` (models.py:169-172) with the same bf16 rounding, one kernel instead of
+  an add and ~7 norm kernels.
+* ``_attention_forward`` (models.py:86-105) hands q, k, v and the RoPE tables to
+  ``cache_ctx.attend_rope`` when the context has it (the B200 context does): RoPE, the
+  KV append and attention become kernels behind the context.  Any other CacheContext
+  gets the reference's torch RoPE followed by ``attend``.
+* The GEMMs stay cuBLAS through ``F.linear`` (tp_layers), the collectives NCCL.
+"""
+import math
+from typing import List
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .parallel import ParallelMode, get_parallel_context
+from .tp_layers import ColumnParallelLinear, ParallelLMHead, RowParallelLinear
+
+
+class RMSNorm(nn.Module):
+    """weight * bf16(x * rsqrt(mean(x^2) + eps)) with fp32 statistics (models.py:25-34)."""
+
+    def __init__(self, dim, eps=1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        return ops.rmsnorm_residual(x, self.weight, self.eps)
+
+    def add_forward(self, x, residual):
+        """residual <- x + residual (in place); returns (rmsnorm(residual), residual)."""
+        out = ops.rmsnorm_residual(x, self.weight, self.eps, residual=residual)
+        return out, residual
+
+
+def precompute_rope_frequencies(dim, max_seq_len, theta, config):
+    """fp32 (cos, sin) tables [max_seq_len, dim] of cat(f, f) (models.py:37-66)."""
+    freqs = 1.0 / (theta ** (torch.arange(0, dim, 2)[: dim // 2].float() / dim))
+    sc = getattr(config, "rope_scaling", None)
+    if sc and sc.get("rope_type") == "llama3":
+        factor = sc.get("factor", 8.0)
+        lo, hi = sc.get("low_freq_factor", 1.0), sc.get("high_freq_factor", 4.0)
+        old_ctx = sc.get("original_max_position_embeddings", 8192)
+        wl = 2 * math.pi / freqs
+        smooth = (old_ctx / wl - lo) / (hi - lo)
+        mid = (1 - smooth) * freqs / factor + smooth * freqs
+        freqs = torch.where(wl < old_ctx / hi, freqs,
+                            torch.where(wl > old_ctx / lo, freqs / factor, mid))
+    t = torch.arange(max_seq_len, dtype=torch.float32)
+    f = torch.outer(t, freqs)
+    f = torch.cat((f, f), dim=-1)
+    return f.cos(), f.sin()
+
+
+def apply_rotary_emb(x, cos, sin):
+    """Rotate-half RoPE with cos/sin cast to x's dtype (models.py:69-83)."""
+    if cos.dim() == 2:
+        cos, sin = cos[None, :, None, :], sin[None, :, None, :]
+    elif cos.dim() == 3:
+        cos, sin = cos[:, :, None, :], sin[:, :, None, :]
+    cos = cos.to(x.device, dtype=x.dtype)
+    sin = sin.to(x.device, dtype=x.dtype)
+    half = x.shape[-1] // 2
+    x1, x2 = x[..., :half], x[..., half:]
+    return x * cos + torch.cat((-x2, x1), dim=-1) * sin
+
+
+def _attention_forward(q, k_new, v_new, layer_idx, n_heads, n_kv_heads, cos, sin, cache_ctx):
+    attend_rope = getattr(cache_ctx, "attend_rope", None)
+    if attend_rope is not None:
+        return attend_rope(layer_idx, q, k_new, v_new, cos, sin)
+    S = q.shape[1]
+    pos_ids = cache_ctx.get_position_ids(S)
+    q = apply_rotary_emb(q, cos[pos_ids], sin[pos_ids])
+    k_new = apply_rotary_emb(k_new, cos[pos_ids], sin[pos_ids])
+    return cache_ctx.attend(layer_idx, q, k_new, v_new, n_heads, n_kv_heads)
+
+
+class TPAttention(nn.Module):
+    def __init__(self, config, layer_idx):
+        super().__init__()
+        tp = get_parallel_context().config.tp_size
+        self.hidden_size = config.hidden_size
+        self.n_heads = config.num_attention_heads
+        self.n_kv_heads = getattr(config, "num_key_value_heads",
+                                  getattr(config, "multi_query_group_num", self.n_heads))
+        self.head_dim = config.hidden_size // self.n_heads   # models.py:117
+        self.layer_idx = layer_idx
+        if self.n_heads % tp or self.n_kv_heads % tp:
+            raise ValueError("head counts must be divisible by tp_size")
+        self.n_heads_tp = self.n_heads // tp
+        self.n_kv_heads_tp = self.n_kv_heads // tp
+        h, d = self.hidden_size, self.head_dim
+        self.q_proj = ColumnParallelLinear(h, self.n_heads * d, gather_output=False)
+        self.k_proj = ColumnParallelLinear(h, self.n_kv_heads * d, gather_output=False)
+        self.v_proj = ColumnParallelLinear(h, self.n_kv_heads * d, gather_output=False)
+        self.o_proj = RowParallelLinear(self.n_heads * d, h, input_is_parallel=True)
+
+    def forward(self, x, cos, sin, cache_ctx, mask=None):
+        B, S, _ = x.shape
+        q = self.q_proj(x).view(B, S, self.n_heads_tp, self.head_dim)
+        k = self.k_proj(x).view(B, S, self.n_kv_heads_tp, self.head_dim)
+        v = self.v_proj(x).view(B, S, self.n_kv_heads_tp, self.head_dim)
+        a = _attention_forward(q, k, v, self.layer_idx, self.n_heads_tp, self.n_kv_heads_tp,
+                               cos, sin, cache_ctx)
+        return self.o_proj(a)
+
+
+class TPMLP(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        h, i = config.hidden_size, config.intermediate_size
+        self.gate_proj = ColumnParallelLinear(h, i, gather_output=False)
+        self.up_proj = ColumnParallelLinear(h, i, gather_output=False)
+        self.down_proj = RowParallelLinear(i, h, input_is_parallel=True)
+
+    def forward(self, x):
+        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+class TPTransformerBlock(nn.Module):
+    """models.py:160-172 with the residual carried between blocks (see module doc)."""
+
+    def __init__(self, config, layer_idx):
+        super().__init__()
+        self.self_attn = TPAttention(config, layer_idx)
+        self.mlp = TPMLP(config)
+        eps = getattr(config, "rms_norm_eps", 1e-5)
+        self.input_layernorm = RMSNorm(config.hidden_size, eps=eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=eps)
+
+    def forward(self, x, cos, sin, cache_ctx, residual=None):
+        if residual is None:
+            residual = x.clone()
+            h = self.input_layernorm(x)
+        else:
+            h, residual = self.input_layernorm.add_forward(x, residual)
+        a = self.self_attn(h, cos, sin, cache_ctx)
+        h, residual = self.post_attention_layernorm.add_forward(a, residual)
+        return self.mlp(h), residual
+
+
+# The reference's PP blocks (models.py:175-239) are the TP blocks with plain nn.Linear;
+# at tp_size 1 the TP layers are exactly that, with the same parameter names.
+PPTransformerBlock = TPTransformerBlock
+
+
+class _LlamaStage(nn.Module):
+    """Layers [layer_indices] of a Llama model, with the embedding on the first stage and
+    the final norm + LM head on the last."""
+
+    def __init__(self, hf_config, layer_indices: List[int], is_first, is_last, lm_head_tp):
+        super().__init__()
+        self.device = get_parallel_context().device
+        self.layer_indices = layer_indices
+        self.is_first, self.is_last = is_first, is_last
+        self.n_layers = len(layer_indices)
+        if is_first:
+            self.embed_tokens = nn.Embedding(hf_config.vocab_size, hf_config.hidden_size)
+        self.layers = nn.ModuleList(
+            [TPTransformerBlock(hf_config, i) for i in range(len(layer_indices))])
+        if is_last:
+            self.norm = RMSNorm(hf_config.hidden_size, eps=getattr(hf_config, "rms_norm_eps", 1e-5))
+            if lm_head_tp:
+                self.lm_head = ParallelLMHead(hf_config.hidden_size, hf_config.vocab_size,
+                                              gather_output=True)
+            else:
+                self.lm_head = nn.Linear(hf_config.hidden_size, hf_config.vocab_size, bias=False)
+        theta = getattr(hf_config, "rope_theta", 500000.0)
+        mx = getattr(hf_config, "max_position_embeddings", 8192)
+        hd = hf_config.hidden_size // hf_config.num_attention_heads
+        # plain fp32 attributes on the rank's device, untouched by model.to(dtype), as in
+        # the reference (models.py:265-270)
+        cos, sin = precompute_rope_frequencies(hd, mx, theta, hf_config)
+        self.cos = cos.to(self.device)
+        self.sin = sin.to(self.device)
+
+    def forward(self, x, cache_ctx, mask=None):
+        h = self.embed_tokens(x) if self.is_first and x.dtype == torch.long else x
+        residual = None
+        for layer in self.layers:
+            h, residual = layer(h, self.cos, self.sin, cache_ctx, residual)
+        if residual is not None:
+            # the stage's output is the residual stream after its last block
+            if self.is_last:
+                h, _ = self.norm.add_forward(h, residual)
+                return self.lm_head(h)
+            return _add(h, residual)
+        return self.lm_head(self.norm(h)) if self.is_last else h
+
+
+def _add(a, b):
+    return b.add_(a)
+
+
+class LlamaTP(_LlamaStage):
+    """All layers on every rank, weights split by TP (models.py:246-276)."""
+
+    def __init__(self, hf_config):
+        super().__init__(hf_config, list(range(hf_config.num_hidden_layers)), True, True,
+                         lm_head_tp=True)
+
+
+class LlamaPP(_LlamaStage):
+    """A pipeline stage without TP (models.py:279-318)."""
+
+    def __init__(self, hf_config, layer_indices, is_first, is_last):
+        super().__init__(hf_config, layer_indices, is_first, is_last, lm_head_tp=False)
+
+
+class LlamaHybrid(_LlamaStage):
+    """A pipeline stage whose layers are TP-split (models.py:321-360)."""
+
+    def __init__(self, hf_config, layer_indices, is_first, is_last):
+        super().__init__(hf_config, layer_indices, is_first, is_last, lm_head_tp=True)
+
+
+def create_model(hf_config, parallel_config):
+    """models.py:362-383."""
+    ctx = get_parallel_context()
+    if parallel_config.mode == ParallelMode.TENSOR:
+        return LlamaTP(hf_config)
+    li = parallel_config.pp_layer_splits[ctx.pp_rank]
+    first, last = ctx.pp_rank == 0, ctx.pp_rank == parallel_config.pp_size - 1
+    if parallel_config.mode == ParallelMode.PIPELINE:
+        return LlamaPP(hf_config, li, first, last)
+    if parallel_config.mode == ParallelMode.HYBRID:
+        return LlamaHybrid(hf_config, li, first, last)
+    raise ValueError(f"Unknown mode: {parallel_config.mode}")
+
+
+def init_random_(model, seed=0, std=0.02):
+    """Random init of the BASELINE configs: manual_seed(seed), normal_(0, std) over
+    named_parameters() in order, norm weights kept at 1 (the golden fixture's rule)."""
+    torch.manual_seed(seed)
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            if "norm" in n:
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, std)
+    return model

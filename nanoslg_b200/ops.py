@@ -1,0 +1,218 @@
+"""Torch-tensor wrappers over the C ABI (``include/nslg_b200.h``).
+
+Each op checks devices, dtypes and layouts, passes raw pointers and the current CUDA
+stream to the native library, and raises on any non-zero status.  Nothing here
+computes on the CPU: the ops need CUDA tensors and the built library.
+"""
+import threading
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.bfloat16: N.DTYPE_BF16, torch.float32: N.DTYPE_F32}
+
+
+def _dtype_code(t):
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"nanoslg_b200 kernels support bfloat16 and float32, got {t.dtype}")
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("nanoslg_b200 kernels need CUDA tensors (no CPU path)")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _rows(x, name):
+    """Views ``x`` ([..., H, D] with contiguous heads) as rows: returns (rows, stride)."""
+    if x.dim() < 2 or x.stride(-1) != 1 or x.stride(-2) != x.shape[-1]:
+        raise ValueError(f"{name}: heads and head_dim must be contiguous, got strides {x.stride()}")
+    lead = x.shape[:-2]
+    n = 1
+    for s in lead:
+        n *= s
+    if x.dim() == 2:
+        return 1, x.shape[-1] * x.shape[-2]
+    # all leading dims must collapse into one row index with a single stride
+    stride = x.stride(-3)
+    expect = stride
+    for dim in range(x.dim() - 3, -1, -1):
+        if x.shape[dim] != 1 and x.stride(dim) != expect:
+            raise ValueError(f"{name}: leading dims do not form one row stride {x.stride()}")
+        expect *= x.shape[dim]
+    return n, stride
+
+
+class _DeviceState:
+    """Per-device scratch: the decode workspace and the device status word."""
+
+    def __init__(self):
+        self.lock = threading.Lock()
+        self.ws = {}
+        self.status = {}
+
+    def workspace(self, device, nbytes):
+        with self.lock:
+            buf = self.ws.get(device)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                self.ws[device] = buf
+            return buf
+
+    def status_word(self, device):
+        with self.lock:
+            st = self.status.get(device)
+            if st is None:
+                st = torch.zeros(1, dtype=torch.int32, device=device)
+                self.status[device] = st
+            return st
+
+
+_STATE = _DeviceState()
+
+
+def status_word(device):
+    """The int32 device word the kernels OR their NSLG_DEV_* error bits into."""
+    return _STATE.status_word(torch.device(device))
+
+
+def check_device_status(device, reset=True):
+    """Synchronises and raises RuntimeError if a kernel on ``device`` flagged an error."""
+    st = status_word(device)
+    v = int(st.item())
+    if reset and v:
+        st.zero_()
+    if v:
+        names = [n for bit, n in ((N.DEV_BAD_PAGE, "page id outside the pool"),
+                                  (N.DEV_BAD_SLOT, "write slot outside the pool"),
+                                  (N.DEV_BAD_POSITION, "position outside the RoPE table"),
+                                  (N.DEV_WAIT_TIMEOUT, "pipeline wait timed out")) if v & bit]
+        raise RuntimeError("nanoslg_b200 device error: " + ", ".join(names))
+
+
+def rope_kv_append(q, k, v, positions, cos, sin, write_loc, pool_k, pool_v, q_out=None,
+                   rotate=True):
+    """Rotates q and k (rotate-half RoPE) and appends rotated k and plain v to the pool.
+
+    q: [..., Hq, D]; k, v: [..., Hkv, D] with the same leading token dims;
+    positions: int32 [T] (row of the cos/sin tables per token);
+    write_loc: int32 [T] flat slot page*page_size+slot, -1 = do not write;
+    pool_k / pool_v: one layer of the pool, [num_pages, page_size, Hkv, D].
+    Returns q_out ([T, Hq, D], rotated q), or None when q is None.
+    With ``rotate=False`` q and k are taken as already rotated (positions ignored).
+    """
+    _need_cuda(q, k, v, positions, cos, sin, write_loc, pool_k, pool_v)
+    dt = _dtype_code(k)
+    nk, ks = _rows(k, "k")
+    nv, vs = _rows(v, "v")
+    hkv, d = k.shape[-2], k.shape[-1]
+    if nk != nv:
+        raise ValueError("k and v token counts differ")
+    qs, hq = 0, hkv
+    if q is not None:
+        nq, qs = _rows(q, "q")
+        hq = q.shape[-2]
+        if nq != nk or q.dtype != k.dtype:
+            raise ValueError("q must match k in token count and dtype")
+        if q_out is None:
+            q_out = torch.empty((nq, hq, d), dtype=q.dtype, device=q.device)
+    if pool_k.dtype != k.dtype or pool_v.dtype != k.dtype:
+        raise TypeError("pool dtype must match k/v")
+    if not (pool_k.is_contiguous() and pool_v.is_contiguous()):
+        raise ValueError("pool layers must be contiguous")
+    slots = pool_k.shape[0] * pool_k.shape[1]
+    if write_loc is not None and (write_loc.dtype != torch.int32 or write_loc.numel() != nk):
+        raise ValueError("write_loc must be int32 with one entry per token")
+    if rotate:
+        if positions is None or positions.dtype != torch.int32 or positions.numel() != nk:
+            raise ValueError("positions must be int32 with one entry per token")
+        if cos.dtype != torch.float32 or not cos.is_contiguous() or not sin.is_contiguous():
+            raise ValueError("cos/sin tables must be contiguous float32 [rows, D]")
+        rows = cos.shape[0]
+    else:
+        positions = cos = sin = None
+        rows = 0
+    N.call("nslg_rope_kv_append", dt, nk, hq, hkv, d, _ptr(q), qs, _ptr(k), ks, _ptr(v), vs,
+           _ptr(q_out), _ptr(positions), _ptr(cos), _ptr(sin), rows, _ptr(write_loc),
+           _ptr(pool_k), _ptr(pool_v), slots, _ptr(status_word(k.device)), _stream(k))
+    return q_out
+
+
+def paged_decode(q, pool_k, pool_v, kv_indptr, kv_indices, kv_last_page_len, sm_scale,
+                 out=None):
+    """Decode attention, one query per sequence. q: [B, Hq, D] -> out [B, Hq, D]."""
+    _need_cuda(q, pool_k, pool_v, kv_indptr, kv_indices, kv_last_page_len)
+    dt = _dtype_code(q)
+    nb, qs = _rows(q, "q")
+    hq, d = q.shape[-2], q.shape[-1]
+    num_pages, ps, hkv = pool_k.shape[0], pool_k.shape[1], pool_k.shape[2]
+    if out is None:
+        out = torch.empty((nb, hq, d), dtype=q.dtype, device=q.device)
+    _, os_ = _rows(out, "out")
+    for t in (kv_indptr, kv_indices, kv_last_page_len):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("CSR arrays must be contiguous int32")
+    wsb = N.lib().nslg_decode_workspace_bytes(nb, hq, d)
+    ws = _STATE.workspace(q.device, wsb)
+    N.call("nslg_paged_decode", dt, nb, hq, hkv, d, ps, _ptr(q), qs, _ptr(out), os_,
+           _ptr(pool_k), _ptr(pool_v), num_pages, _ptr(kv_indptr), _ptr(kv_indices),
+           _ptr(kv_last_page_len), float(sm_scale), _ptr(ws), ws.numel(),
+           _ptr(status_word(q.device)), _stream(q))
+    return out
+
+
+def paged_prefill(q, qo_indptr, max_qo_len, pool_k, pool_v, kv_indptr, kv_indices,
+                  kv_last_page_len, sm_scale, causal=True, q_row_start=None, out=None):
+    """Causal prefill/extend attention over the paged KV.
+
+    q: [rows, Hq, D] (or [B, S, Hq, D], viewed as rows); sequence b's qo_len rows start at
+    row q_row_start[b] (default qo_indptr[b]).  out has q's row layout; rows that belong
+    to no sequence are left as they are (zero them first if they must read as zero).
+    """
+    _need_cuda(q, qo_indptr, pool_k, pool_v, kv_indptr, kv_indices, kv_last_page_len,
+               q_row_start)
+    dt = _dtype_code(q)
+    nrows, qs = _rows(q, "q")
+    hq, d = q.shape[-2], q.shape[-1]
+    num_pages, ps, hkv = pool_k.shape[0], pool_k.shape[1], pool_k.shape[2]
+    if out is None:
+        out = torch.zeros(q.shape, dtype=q.dtype, device=q.device)
+    _, os_ = _rows(out, "out")
+    batch = qo_indptr.numel() - 1
+    N.call("nslg_paged_prefill", dt, batch, hq, hkv, d, ps, _ptr(q), qs, _ptr(out), os_,
+           _ptr(qo_indptr), _ptr(q_row_start), int(max_qo_len), _ptr(pool_k), _ptr(pool_v),
+           num_pages, _ptr(kv_indptr), _ptr(kv_indices), _ptr(kv_last_page_len),
+           float(sm_scale), 1 if causal else 0, _ptr(status_word(q.device)), _stream(q))
+    return out
+
+
+def rmsnorm_residual(x, weight, eps, residual=None, out=None):
+    """out = rmsnorm(x [+ residual]) * weight; with a residual, residual <- x + residual."""
+    _need_cuda(x, weight, residual, out)
+    dt = _dtype_code(x)
+    hidden = x.shape[-1]
+    if x.stride(-1) != 1 or weight.dtype != x.dtype or weight.numel() != hidden:
+        raise ValueError("rmsnorm_residual: bad layout or weight")
+    rows = x.numel() // hidden
+    x2 = x.reshape(rows, hidden)
+    if out is None:
+        out = torch.empty_like(x2)
+    out2 = out.view(rows, hidden)
+    r2 = None
+    if residual is not None:
+        r2 = residual.view(rows, hidden)
+    N.call("nslg_rmsnorm_residual", dt, rows, hidden, _ptr(x2), x2.stride(0), _ptr(r2),
+           r2.stride(0) if r2 is not None else 0, _ptr(weight), _ptr(out2), out2.stride(0),
+           float(eps), _stream(x))
+    return out.view(x.shape)

@@ -1,0 +1,161 @@
+"""The B200 CacheContext / model path on the GPU against the reference's recorded
+outputs (tests/golden): contiguous-SDPA attention cases and the tiny fp32 Llama's greedy
+tokens."""
+import json
+import math
+import os
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle.attention import attend_sequences
+from oracle.rope_norm import apply_rotary, rope_table
+from nanoslg_b200 import ops
+from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig, create_cache_manager
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+ATT = torch.load(os.path.join(GOLDEN, "attention_cases.pt"))
+
+
+@pytest.fixture(autouse=True)
+def _clean_status():
+    ops.status_word(DEV).zero_()
+    yield
+    ops.check_device_status(DEV)
+
+
+@pytest.mark.parametrize("case", ATT, ids=[c["name"] for c in ATT])
+def test_context_attend_matches_reference(case):
+    dt = torch.float32 if case["dtype"] == "torch.float32" else torch.bfloat16
+    tol = dict(rtol=1e-2, atol=2e-2) if dt == torch.bfloat16 else dict(rtol=1e-4, atol=1e-5)
+    B = len(case["lens"])
+    cfg = KVCacheConfig(num_layers=2, num_kv_heads=case["hkv"], num_qo_heads=case["hq"],
+                        head_dim=case["d"], page_size=16, max_pages=64, dtype=dt, device=DEV)
+    mgr = B200PagedKVCache(cfg)
+    sids = [f"s{i}" for i in range(B)]
+    for s in sids:
+        mgr.allocate_sequence(s)
+    for step in case["steps"]:
+        ctx = mgr.begin_forward(sids, step["counts"], step["offsets"])
+        assert ctx.start_positions == step["start_positions"]
+        for li, lay in enumerate(step["layers"]):
+            out = ctx.attend(li, lay["q"].to(DEV), lay["k"].to(DEV), lay["v"].to(DEV),
+                             case["hq"], case["hkv"]).cpu()
+            for b, (o, n) in enumerate(zip(step["offsets"], step["counts"])):
+                torch.testing.assert_close(out[b, o:o + n], lay["out"][b, o:o + n], **tol)
+        mgr.end_forward(ctx)
+
+
+def test_attend_rope_equals_unfused_path():
+    """attend_rope (fused kernel) == torch RoPE (the reference's ops) + attend."""
+    hq, hkv, d = 32, 8, 128
+    cos, sin = rope_table(d, 8192, 500000.0)
+    cos_d, sin_d = cos.to(DEV), sin.to(DEV)
+    outs = []
+    for fused in (True, False):
+        cfg = KVCacheConfig(num_layers=1, num_kv_heads=hkv, num_qo_heads=hq, head_dim=d,
+                            page_size=16, max_pages=256, dtype=torch.bfloat16, device=DEV)
+        mgr = B200PagedKVCache(cfg)
+        g = torch.Generator().manual_seed(21)
+        sids = ["a", "b", "c"]
+        for s, n in zip(sids, (300, 17, 64)):
+            mgr.allocate_sequence(s, list(range(n)))
+        res = []
+        plan = [([300, 17, 64], [0, 283, 236])] + [([1, 1, 1], None)] * 3
+        for counts, offs in plan:
+            ctx = mgr.begin_forward(sids, counts, offs)
+            S = max(counts)
+            q = torch.randn(3, S, hq, d, generator=g).to(torch.bfloat16).to(DEV)
+            k = torch.randn(3, S, hkv, d, generator=g).to(torch.bfloat16).to(DEV)
+            v = torch.randn(3, S, hkv, d, generator=g).to(torch.bfloat16).to(DEV)
+            if fused:
+                o = ctx.attend_rope(0, q, k, v, cos_d, sin_d)
+            else:
+                pos = ctx.get_position_ids(S)
+                o = ctx.attend(0, apply_rotary(q, cos_d[pos], sin_d[pos]),
+                               apply_rotary(k, cos_d[pos], sin_d[pos]), v, hq, hkv)
+            res.append(o.cpu())
+            mgr.end_forward(ctx)
+        outs.append(res)
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+def test_llama8b_layer_shapes_prefill_then_decode():
+    """One 8B-shaped layer (32/8 heads, D 128): prompt prefill of 512 then decode, against
+    the oracle over the rotated q/k the kernel produced."""
+    hq, hkv, d, B = 32, 8, 128, 4
+    cos, sin = rope_table(d, 8192, 500000.0)
+    cfg = KVCacheConfig(num_layers=1, num_kv_heads=hkv, num_qo_heads=hq, head_dim=d,
+                        page_size=16, max_pages=512, dtype=torch.bfloat16, device=DEV)
+    mgr = B200PagedKVCache(cfg)
+    sids = [f"s{i}" for i in range(B)]
+    lens = [512, 300, 511, 17]
+    for s, n in zip(sids, lens):
+        mgr.allocate_sequence(s, list(range(n)))
+    g = torch.Generator().manual_seed(8)
+    hist_k = [torch.zeros(0, hkv, d, dtype=torch.bfloat16) for _ in range(B)]
+    hist_v = [torch.zeros(0, hkv, d, dtype=torch.bfloat16) for _ in range(B)]
+    plan = [(lens, [512 - n for n in lens])] + [([1] * B, None)] * 4
+    for counts, offs in plan:
+        ctx = mgr.begin_forward(sids, counts, offs)
+        S = max(counts)
+        offs = offs or [0] * B
+        q = torch.randn(B, S, hq, d, generator=g).to(torch.bfloat16)
+        k = torch.randn(B, S, hkv, d, generator=g).to(torch.bfloat16)
+        v = torch.randn(B, S, hkv, d, generator=g).to(torch.bfloat16)
+        out = ctx.attend_rope(0, q.to(DEV), k.to(DEV), v.to(DEV), cos.to(DEV), sin.to(DEV)).cpu()
+        pos = ctx.get_position_ids(S).cpu()
+        qr, kr = apply_rotary(q, cos[pos], sin[pos]), apply_rotary(k, cos[pos], sin[pos])
+        qs = []
+        for b in range(B):
+            o, n = offs[b], counts[b]
+            hist_k[b] = torch.cat([hist_k[b], kr[b, o:o + n]])
+            hist_v[b] = torch.cat([hist_v[b], v[b, o:o + n]])
+            qs.append(qr[b, o:o + n])
+        ref = attend_sequences(qs, hist_k, hist_v)
+        for b in range(B):
+            o, n = offs[b], counts[b]
+            torch.testing.assert_close(out[b, o:o + n].view(n, hq, d), ref[b],
+                                       rtol=1e-2, atol=2e-2)
+        mgr.end_forward(ctx)
+
+
+def test_tiny_llama_greedy_tokens_match_reference():
+    """Config C1 (fp32, 2 layers, hidden 256) through nanoslg_b200.models + the B200 cache,
+    driven like worker.py drives a TP=1 request: identical greedy tokens."""
+    from nanoslg_b200 import models
+    from nanoslg_b200.parallel import ParallelConfig, ParallelContext, ParallelMode
+    with open(os.path.join(GOLDEN, "tiny_llama.json")) as f:
+        g = json.load(f)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    pcfg = ParallelConfig(ParallelMode.TENSOR, 1)
+    ParallelContext.initialize(pcfg, 0, device=DEV)
+    hf = SimpleNamespace(**g["config"])
+    model = models.create_model(hf, pcfg).float()
+    assert [n for n, _ in model.named_parameters()] == g["param_order"]
+    models.init_random_(model, seed=0)
+    model = model.to(DEV)
+    mc = SimpleNamespace(page_size=16, max_kv_pages=64, enable_prefix_caching=True)
+    mgr = create_cache_manager(hf, pcfg, DEV, torch.float32, mc, max_batch_size=1)
+    prompt = torch.tensor([g["prompt"]], device=DEV)
+    toks = []
+    with torch.inference_mode():
+        mgr.allocate_sequence("s0", g["prompt"])
+        ctx = mgr.begin_forward(["s0"], [len(g["prompt"])], [0])
+        logits = model(prompt, ctx)
+        mgr.end_forward(ctx)
+        for step in range(len(g["tokens"])):
+            t = int(logits[0, -1].argmax())
+            toks.append(t)
+            mgr.append_token_ids("s0", [t])
+            if step + 1 == len(g["tokens"]):
+                break
+            ctx = mgr.begin_forward(["s0"], [1])
+            logits = model(torch.tensor([[t]], device=DEV), ctx)
+            mgr.end_forward(ctx)
+    assert toks == g["tokens"]

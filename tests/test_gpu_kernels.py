@@ -1,0 +1,170 @@
+"""GPU parity of each kernel against the CPU oracle, through the C ABI.
+
+Tolerances (north star): RoPE/KV append bit-exact; attention in bf16 within 2e-2 abs /
+1e-2 rel of the fp32 oracle over the same bf16 inputs; fp32 attention within 1e-5."""
+import math
+
+import pytest
+import torch
+
+from oracle.attention import attend_sequences
+from oracle.rope_norm import apply_rotary, rmsnorm, rope_table
+from nanoslg_b200 import ops
+from paged_util import make_paged, sequence_kv
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+BF16_TOL = dict(rtol=1e-2, atol=2e-2)
+F32_TOL = dict(rtol=1e-5, atol=1e-5)
+
+
+def _tol(dt):
+    return BF16_TOL if dt == torch.bfloat16 else F32_TOL
+
+
+@pytest.fixture(autouse=True)
+def _clean_status():
+    ops.status_word(DEV).zero_()
+    yield
+    ops.check_device_status(DEV)
+
+
+@pytest.mark.parametrize("dt,hq,hkv,d", [(torch.bfloat16, 32, 8, 128), (torch.float32, 4, 2, 64),
+                                         (torch.bfloat16, 8, 1, 64)])
+def test_rope_kv_append_bit_exact(dt, hq, hkv, d):
+    g = torch.Generator().manual_seed(3)
+    T, ps, P = 37, 16, 20
+    cos, sin = rope_table(d, 4096, 500000.0)
+    q = torch.randn(T, hq, d, generator=g).to(dt)
+    k = torch.randn(T, hkv, d, generator=g).to(dt)
+    v = torch.randn(T, hkv, d, generator=g).to(dt)
+    pos = torch.randint(0, 4096, (T,), generator=g, dtype=torch.int32)
+    loc = torch.randperm(P * ps, generator=g)[:T].to(torch.int32)
+    loc[::5] = -1                                        # padded cells are not written
+    pk = torch.full((P, ps, hkv, d), 7.0, dtype=dt, device=DEV)
+    pv = torch.full((P, ps, hkv, d), 7.0, dtype=dt, device=DEV)
+    q_out = ops.rope_kv_append(q.to(DEV), k.to(DEV), v.to(DEV), pos.to(DEV), cos.to(DEV),
+                               sin.to(DEV), loc.to(DEV), pk, pv)
+    p64 = pos.long()[None]
+    q_ref = apply_rotary(q[None], cos[p64], sin[p64])[0]
+    k_ref = apply_rotary(k[None], cos[p64], sin[p64])[0]
+    assert torch.equal(q_out.cpu(), q_ref)
+    fk, fv = pk.view(-1, hkv, d).cpu(), pv.view(-1, hkv, d).cpu()
+    w = loc >= 0
+    assert torch.equal(fk[loc[w].long()], k_ref[w])
+    assert torch.equal(fv[loc[w].long()], v[w])
+    untouched = torch.ones(P * ps, dtype=torch.bool)
+    untouched[loc[w].long()] = False
+    assert bool((fk[untouched] == 7.0).all()) and bool((fv[untouched] == 7.0).all())
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("hidden", [256, 4096, 8192])
+def test_rmsnorm_residual(dt, hidden):
+    g = torch.Generator().manual_seed(4)
+    x = (torch.randn(9, hidden, generator=g) * 2).to(dt)
+    r = torch.randn(9, hidden, generator=g).to(dt)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(dt)
+    y = ops.rmsnorm_residual(x.to(DEV), w.to(DEV), 1e-5)
+    tol = dict(rtol=1e-2, atol=1e-2) if dt == torch.bfloat16 else dict(rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(y.cpu(), rmsnorm(x, w, 1e-5), **tol)
+    rd = r.to(DEV)
+    y2 = ops.rmsnorm_residual(x.to(DEV), w.to(DEV), 1e-5, residual=rd)
+    h = x + r
+    assert torch.equal(rd.cpu(), h)                      # the residual add is bit-exact
+    torch.testing.assert_close(y2.cpu(), rmsnorm(h, w, 1e-5), **tol)
+
+
+DECODE_CASES = [
+    # hq, hkv, d, lens
+    (32, 8, 128, [1, 15, 16, 17, 100, 1000, 2049]),
+    (16, 4, 128, [3, 33, 700, 1500]),
+    (16, 2, 128, [5, 16, 900]),
+    (4, 1, 128, [1, 2, 31, 32, 33, 600]),
+    (8, 1, 128, [77, 1200]),
+    (64, 8, 128, [40, 513]),
+    (8, 8, 128, [19, 260]),
+    (8, 2, 64, [9, 300, 1024]),
+    (32, 8, 128, [0, 50, 0, 3]),                         # sequences without pages
+]
+
+
+@pytest.mark.parametrize("hq,hkv,d,lens", DECODE_CASES)
+def test_paged_decode_bf16(hq, hkv, d, lens):
+    pk = make_paged(lens, hkv, d, 4096, torch.bfloat16, DEV, seed=len(lens) + hq)
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(len(lens), hq, d, generator=g).to(torch.bfloat16)
+    out = ops.paged_decode(q.to(DEV), pk["pool_k"], pk["pool_v"], pk["indptr"], pk["indices"],
+                           pk["lpl"], 1 / math.sqrt(d)).cpu()
+    ks = [sequence_kv(pk, b, "k") for b in range(len(lens))]
+    vs = [sequence_kv(pk, b, "v") for b in range(len(lens))]
+    ref = attend_sequences([q[b:b + 1] for b in range(len(lens))], ks, vs)
+    for b, n in enumerate(lens):
+        exp = ref[b][0] if n > 0 else torch.zeros(hq, d, dtype=torch.bfloat16)
+        torch.testing.assert_close(out[b], exp, **BF16_TOL)
+
+
+def test_paged_decode_many_sequences_split_across_ctas():
+    g = torch.Generator().manual_seed(6)
+    lens = torch.randint(1, 3000, (97,), generator=g).tolist()
+    pk = make_paged(lens, 8, 128, 30000, torch.bfloat16, DEV, seed=9)
+    q = torch.randn(len(lens), 32, 128, generator=g).to(torch.bfloat16)
+    out = ops.paged_decode(q.to(DEV), pk["pool_k"], pk["pool_v"], pk["indptr"], pk["indices"],
+                           pk["lpl"], 1 / math.sqrt(128)).cpu()
+    for b in range(len(lens)):
+        ref = attend_sequences([q[b:b + 1]], [sequence_kv(pk, b, "k")], [sequence_kv(pk, b, "v")])
+        torch.testing.assert_close(out[b], ref[0][0], **BF16_TOL)
+
+
+def test_paged_decode_fp32_and_other_page_sizes():
+    for dt, ps, d in [(torch.float32, 16, 64), (torch.float32, 4, 128), (torch.bfloat16, 8, 128)]:
+        lens = [1, 7, 64, 301]
+        pk = make_paged(lens, 2, d, 1024, dt, DEV, seed=11, page_size=ps)
+        q = torch.randn(len(lens), 8, d, generator=torch.Generator().manual_seed(2)).to(dt)
+        out = ops.paged_decode(q.to(DEV), pk["pool_k"], pk["pool_v"], pk["indptr"],
+                               pk["indices"], pk["lpl"], 1 / math.sqrt(d)).cpu()
+        for b in range(len(lens)):
+            ref = attend_sequences([q[b:b + 1]], [sequence_kv(pk, b, "k")],
+                                   [sequence_kv(pk, b, "v")])
+            torch.testing.assert_close(out[b], ref[0][0], **_tol(dt))
+
+
+@pytest.mark.parametrize("dt,hq,hkv,d", [(torch.bfloat16, 32, 8, 128), (torch.float32, 4, 2, 64),
+                                         (torch.bfloat16, 16, 2, 128)])
+def test_paged_prefill_causal_ragged(dt, hq, hkv, d):
+    # (history already in the cache, new rows): covers plain prefill, extend after a
+    # prefix hit, single-token rows and empty sequences
+    spec = [(0, 37), (16, 20), (5, 1), (0, 130), (64, 0), (200, 77)]
+    lens = [h + n for h, n in spec]
+    pk = make_paged(lens, hkv, d, 2048, dt, DEV, seed=13)
+    g = torch.Generator().manual_seed(7)
+    S = max(n for _, n in spec)
+    B = len(spec)
+    q = torch.randn(B, S, hq, d, generator=g).to(dt)
+    offsets = [S - n for _, n in spec]                    # left padded like the worker
+    counts = [n for _, n in spec]
+    qo = torch.tensor([0] + list(torch.cumsum(torch.tensor(counts), 0)), dtype=torch.int32)
+    row_start = torch.tensor([b * S + o for b, o in enumerate(offsets)], dtype=torch.int32)
+    out = ops.paged_prefill(q.to(DEV), qo.to(DEV), S, pk["pool_k"], pk["pool_v"], pk["indptr"],
+                            pk["indices"], pk["lpl"], 1 / math.sqrt(d), causal=True,
+                            q_row_start=row_start.to(DEV)).cpu()
+    ks = [sequence_kv(pk, b, "k") for b in range(B)]
+    vs = [sequence_kv(pk, b, "v") for b in range(B)]
+    ref = attend_sequences([q[b, offsets[b]:] for b in range(B)], ks, vs)
+    for b in range(B):
+        torch.testing.assert_close(out[b, offsets[b]:], ref[b], **_tol(dt))
+        assert bool((out[b, :offsets[b]] == 0).all())     # padded rows stay zero
+
+
+def test_bad_page_id_sets_status_without_fault():
+    pk = make_paged([40, 40], 8, 128, 64, torch.bfloat16, DEV, seed=1)
+    bad = pk["indices"].clone()
+    bad[1] = 10 ** 6                                      # outside the 64-page pool
+    q = torch.randn(2, 32, 128, device=DEV).to(torch.bfloat16)
+    ops.paged_decode(q, pk["pool_k"], pk["pool_v"], pk["indptr"], bad, pk["lpl"], 0.1)
+    with pytest.raises(RuntimeError, match="page id outside the pool"):
+        ops.check_device_status(DEV)
+    ops.paged_prefill(q[:, None], torch.tensor([0, 1, 2], dtype=torch.int32, device=DEV), 1,
+                      pk["pool_k"], pk["pool_v"], pk["indptr"], bad, pk["lpl"], 0.1)
+    with pytest.raises(RuntimeError, match="page id outside the pool"):
+        ops.check_device_status(DEV)
