@@ -101,6 +101,31 @@ int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
                       float sm_scale, void* workspace, int64_t workspace_bytes,
                       uint32_t* dev_status, void* stream);
 
+/* Scratch size of nslg_paged_decode_noalloc: a fixed device array inside the library. */
+#define NSLG_NOALLOC_SCRATCH_BYTES (8ll << 20)
+
+/* nslg_paged_decode for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference (NanoSLG always lets FlashInfer use a workspace it
+ * allocated). For callers with no device allocator of their own -- a serving process
+ * that gave nearly all HBM to its KV page pool and runs on a fixed budget, a host
+ * program in another language binding this ABI, a decode loop that cannot take the
+ * synchronisation of cudaMalloc/cudaFree. Same arguments and result as
+ * nslg_paged_decode minus the workspace: the split-KV partials go to a fixed
+ * NSLG_NOALLOC_SCRATCH_BYTES array compiled into the library, which every GPU that loads
+ * the library holds until the process exits. Batches whose scratch
+ * ((batch + #SMs) * num_qo_heads * (head_dim + 1) * 4 bytes) exceeds it are rejected with
+ * NSLG_ERR_WORKSPACE. The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress) with that device current; make it before any stream capture.
+ * All calls on a device share the array, so calls that overlap on the GPU race: order
+ * them. Allocates and frees nothing. */
+int nslg_paged_decode_noalloc(int dtype, int batch, int num_qo_heads, int num_kv_heads,
+                              int head_dim, int page_size, const void* q, int64_t q_stride,
+                              void* out, int64_t out_stride, const void* pool_k,
+                              const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
+                              const int32_t* kv_indices, const int32_t* kv_last_page_len,
+                              float sm_scale, uint32_t* dev_status, void* stream);
+
 /* Batched paged prefill / extend attention with a causal mask.
  *
  * Replaces FlashInferCacheContext.attend's prefill branch (kv_cache.py:652-655,

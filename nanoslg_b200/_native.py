@@ -35,6 +35,8 @@ SIGNATURES = {
     "nslg_decode_workspace_bytes": (_i64, [_i32, _i32, _i32]),
     "nslg_paged_decode": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp,
                                  _vp, _i64, _vp, _vp, _vp, _f32, _vp, _i64, _vp, _vp]),
+    "nslg_paged_decode_noalloc": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp,
+                                         _i64, _vp, _vp, _i64, _vp, _vp, _vp, _f32, _vp, _vp]),
     "nslg_paged_prefill": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp,
                                   _vp, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _f32, _i32, _vp,
                                   _vp]),
