@@ -117,31 +117,31 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------- ours
-def build_c2_device(device, seed):
+def build_c2_device(device, seed, pool_pages=POOL_PAGES):
     """Pool [600k, 16, 8, 128] x2 bf16 ~ N(0,1), page table drawn from randperm(600k)."""
     lens = c2_lens(seed)
     npg = [math.ceil(n / PS) for n in lens]
     g = torch.Generator().manual_seed(seed)
-    perm = torch.randperm(POOL_PAGES, generator=g)
+    perm = torch.randperm(pool_pages, generator=g)
     perm = perm[perm != 0][:sum(npg)].to(torch.int32)
     indptr = torch.zeros(B + 1, dtype=torch.int32)
     indptr[1:] = torch.cumsum(torch.tensor(npg), 0).to(torch.int32)
     lpl = torch.tensor([n - (p - 1) * PS for n, p in zip(lens, npg)], dtype=torch.int32)
     gd = torch.Generator(device=device).manual_seed(seed)
-    shape = (POOL_PAGES, PS, HKV, D)
+    shape = (pool_pages, PS, HKV, D)
     pool_k = torch.empty(shape, dtype=torch.bfloat16, device=device)
     pool_v = torch.empty(shape, dtype=torch.bfloat16, device=device)
     for t in (pool_k, pool_v):
-        for i in range(0, POOL_PAGES, 50_000):      # bounded fp32 temporaries
+        for i in range(0, pool_pages, 50_000):      # bounded fp32 temporaries
             t[i:i + 50_000] = torch.randn(t[i:i + 50_000].shape, device=device, generator=gd)
     q = torch.randn(B, HQ, D, device=device, generator=gd).to(torch.bfloat16)
     return dict(lens=lens, pool_k=pool_k, pool_v=pool_v, indptr=indptr.to(device),
                 indices=perm.to(device), lpl=lpl.to(device), q=q)
 
 
-def run_kernel(device, steps, warmup, seed):
+def run_kernel(device, steps, warmup, seed, pool_pages=POOL_PAGES):
     from nanoslg_b200 import ops
-    c = build_c2_device(device, seed)
+    c = build_c2_device(device, seed, pool_pages)
     out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=device)
     scale = 1.0 / math.sqrt(D)
 
@@ -272,6 +272,11 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--pool-pages", type=int, default=POOL_PAGES,
+                    help="page pool size; the profiling case uses a smaller pool with the same "
+                         "batch (still 1.13 GB of KV per step)")
+    ap.add_argument("--only", choices=["all", "kernel"], default="all",
+                    help="kernel: run only the resident-input kernel timing (profiling case)")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -318,7 +323,16 @@ def main():
     if not os.path.exists(nbuild.LIB):
         nbuild.build()
 
-    kr = run_kernel(device, a.steps, a.warmup, seed=rank)
+    kr = run_kernel(device, a.steps, a.warmup, seed=rank, pool_pages=a.pool_pages)
+    if a.only == "kernel":
+        if rank == 0:
+            mean_ms = statistics.mean(kr["per_ms"])
+            print(json.dumps({"case": "kernel only", "pool_pages": a.pool_pages,
+                              "kernel_ms_mean": mean_ms,
+                              "achieved_gbs": alg_bytes(kr["lens"]) / mean_ms / 1e6}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
     e2e_steps = a.e2e_steps or max(10, a.steps // 2)
     er = run_e2e(device, e2e_steps, a.warmup, seed=rank)
 
