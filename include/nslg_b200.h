@@ -139,11 +139,14 @@ int nslg_paged_decode_noalloc(int dtype, int batch, int num_qo_heads, int num_kv
  * q_row_start is NULL; outputs at the same rows of out.  Row i sits at absolute
  * position kv_len(b) - qo_len(b) + i and, when causal != 0, attends to kv positions
  * <= that position (the reference's kpos <= start + i  and  kpos < seq_len).
- * max_qo_len bounds qo_len(b).
+ * q and out hold q_rows rows (the extent of the TMA view of q; rows past it read as
+ * zero). max_qo_len bounds qo_len(b). bf16 with head_dim 128, page_size 16 and a GQA
+ * group (num_qo_heads / num_kv_heads) that divides 128 runs on tcgen05 tensor cores;
+ * other shapes and fp32 run on CUDA cores.
  */
 int nslg_paged_prefill(int dtype, int batch, int num_qo_heads, int num_kv_heads,
                        int head_dim, int page_size, const void* q, int64_t q_stride,
-                       void* out, int64_t out_stride, const int32_t* qo_indptr,
+                       int64_t q_rows, void* out, int64_t out_stride, const int32_t* qo_indptr,
                        const int32_t* q_row_start, int max_qo_len, const void* pool_k,
                        const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
                        const int32_t* kv_indices, const int32_t* kv_last_page_len,

@@ -37,8 +37,8 @@ SIGNATURES = {
                                  _vp, _i64, _vp, _vp, _vp, _f32, _vp, _i64, _vp, _vp]),
     "nslg_paged_decode_noalloc": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp,
                                          _i64, _vp, _vp, _i64, _vp, _vp, _vp, _f32, _vp, _vp]),
-    "nslg_paged_prefill": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp,
-                                  _vp, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _f32, _i32, _vp,
+    "nslg_paged_prefill": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64,
+                                  _vp, _vp, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _f32, _i32, _vp,
                                   _vp]),
     "nslg_rmsnorm_residual": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i64,
                                      _f32, _vp]),

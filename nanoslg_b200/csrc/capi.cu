@@ -140,7 +140,7 @@ int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads, 
 }
 
 int nslg_paged_prefill(int dtype, int batch, int num_qo_heads, int num_kv_heads, int head_dim,
-                       int page_size, const void* q, int64_t q_stride, void* out,
+                       int page_size, const void* q, int64_t q_stride, int64_t q_rows, void* out,
                        int64_t out_stride, const int32_t* qo_indptr, const int32_t* q_row_start,
                        int max_qo_len, const void* pool_k, const void* pool_v, int64_t num_pages,
                        const int32_t* kv_indptr, const int32_t* kv_indices,
@@ -160,11 +160,20 @@ int nslg_paged_prefill(int dtype, int batch, int num_qo_heads, int num_kv_heads,
     return set_error(NSLG_ERR_ARG, "paged_prefill: null pointer");
   if (!(sm_scale > 0.f)) return set_error(NSLG_ERR_ARG, "paged_prefill: sm_scale must be > 0");
   if (max_qo_len > 65535) return set_error(NSLG_ERR_UNSUPPORTED, "paged_prefill: max_qo_len > 65535");
+  if (q_rows <= 0) return set_error(NSLG_ERR_ARG, "paged_prefill: q_rows must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (prefill_tc_supported(dtype, num_qo_heads, num_kv_heads, head_dim, page_size) &&
+      aligned16(q) && aligned16(out) && aligned16(pool_k) && aligned16(pool_v) &&
+      (q_stride * 2) % 16 == 0 && (out_stride * 2) % 16 == 0)
+    return launch_paged_prefill_tc(batch, num_qo_heads, num_kv_heads, q, q_stride, q_rows, out,
+                                   out_stride, qo_indptr, q_row_start, max_qo_len, pool_k,
+                                   pool_v, num_pages, kv_indptr, kv_indices, kv_last_page_len,
+                                   sm_scale, causal, dev_status, st);
   return launch_paged_attention_simt(dtype, batch, num_qo_heads, num_kv_heads, head_dim,
                                      page_size, q, q_stride, out, out_stride, qo_indptr,
                                      q_row_start, max_qo_len, pool_k, pool_v, num_pages,
                                      kv_indptr, kv_indices, kv_last_page_len, sm_scale, causal,
-                                     dev_status, static_cast<cudaStream_t>(stream));
+                                     dev_status, st);
 }
 
 int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int64_t x_stride,

@@ -29,8 +29,6 @@
 // the end of each segment.
 #include <cuda.h>
 
-#include <mutex>
-
 #include "common.cuh"
 #include "launch.h"
 
@@ -430,74 +428,6 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
 }
 
 // ------------------------------------------------------------------ host side
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
-// Tensor maps are cached per (pool layer pointer, pages, heads, head_dim): the pool is
-// allocated once and each layer's K and V maps are reused on every step.
-struct MapEntry {
-  const void* ptr = nullptr;
-  int64_t pages = 0;
-  int hkv = 0, d = 0;
-  CUtensorMap map;
-};
-constexpr int kMapCache = 512;
-MapEntry g_maps[kMapCache];
-int g_map_next = 0;
-std::mutex g_map_mu;
-
-int pool_tensor_map(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out) {
-  std::lock_guard<std::mutex> lock(g_map_mu);
-  for (int i = 0; i < kMapCache; ++i) {
-    const MapEntry& e = g_maps[i];
-    if (e.ptr == pool && e.pages == pages && e.hkv == hkv && e.d == d) {
-      *out = e.map;
-      return NSLG_OK;
-    }
-  }
-  EncodeTiledFn enc = encode_fn();
-  if (enc == nullptr) return set_error(NSLG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  // dims (innermost first): head_dim, kv head, token row (= page * 16 + slot)
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(hkv),
-                              static_cast<cuuint64_t>(pages) * kPS};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2,
-                                 static_cast<cuuint64_t>(hkv) * d * 2};
-  const cuuint32_t box[3] = {64, 1, kPS};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  MapEntry& e = g_maps[g_map_next];
-  const CUresult r = enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(pool),
-                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    e.ptr = nullptr;
-    return set_error(NSLG_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
-  }
-  e.ptr = pool;
-  e.pages = pages;
-  e.hkv = hkv;
-  e.d = d;
-  *out = e.map;
-  g_map_next = (g_map_next + 1) % kMapCache;
-  return NSLG_OK;
-}
-
 template <int HKV, int D>
 int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
                  cudaStream_t stream) {

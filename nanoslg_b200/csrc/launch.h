@@ -1,6 +1,7 @@
 // Host-side declarations shared by the kernel files and the C ABI in capi.cu.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,6 +19,14 @@ int check_launch(const char* what);
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// 3-D tiled bf16 tensor map with 128-byte swizzle (strides in bytes, dims innermost first).
+int encode_tiled_3d_bf16(CUtensorMap* out, const void* base, uint64_t d0, uint64_t d1,
+                         uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                         uint32_t box0, uint32_t box1, uint32_t box2);
+
+// Cached map of one pool layer [pages, 16, hkv, d] with a [16 tok x 1 head x 64 dim] box.
+int pool_tensor_map(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out);
 
 int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, const void* q,
                           int64_t q_stride, const void* k, int64_t k_stride, const void* v,
@@ -50,5 +59,15 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
                            const int32_t* kv_indices, const int32_t* kv_last_page_len,
                            float sm_scale, void* workspace, int64_t workspace_bytes,
                            uint32_t* status, cudaStream_t stream);
+
+// tcgen05 causal prefill for bf16, page_size 16, head_dim 128, group <= 16 dividing 128.
+bool prefill_tc_supported(int dtype, int hq, int hkv, int d, int page_size);
+int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q_stride,
+                            int64_t q_rows, void* out, int64_t out_stride,
+                            const int32_t* qo_indptr, const int32_t* q_row_start, int max_qo_len,
+                            const void* pool_k, const void* pool_v, int64_t num_pages,
+                            const int32_t* kv_indptr, const int32_t* kv_indices,
+                            const int32_t* kv_last_page_len, float sm_scale, int causal,
+                            uint32_t* status, cudaStream_t stream);
 
 }  // namespace nslg

@@ -190,7 +190,7 @@ def paged_prefill(q, qo_indptr, max_qo_len, pool_k, pool_v, kv_indptr, kv_indice
         out = torch.zeros(q.shape, dtype=q.dtype, device=q.device)
     _, os_ = _rows(out, "out")
     batch = qo_indptr.numel() - 1
-    N.call("nslg_paged_prefill", dt, batch, hq, hkv, d, ps, _ptr(q), qs, _ptr(out), os_,
+    N.call("nslg_paged_prefill", dt, batch, hq, hkv, d, ps, _ptr(q), qs, nrows, _ptr(out), os_,
            _ptr(qo_indptr), _ptr(q_row_start), int(max_qo_len), _ptr(pool_k), _ptr(pool_v),
            num_pages, _ptr(kv_indptr), _ptr(kv_indices), _ptr(kv_last_page_len),
            float(sm_scale), 1 if causal else 0, _ptr(status_word(q.device)), _stream(q))

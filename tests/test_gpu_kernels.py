@@ -130,7 +130,8 @@ def test_paged_decode_fp32_and_other_page_sizes():
 
 
 @pytest.mark.parametrize("dt,hq,hkv,d", [(torch.bfloat16, 32, 8, 128), (torch.float32, 4, 2, 64),
-                                         (torch.bfloat16, 16, 2, 128)])
+                                         (torch.bfloat16, 16, 2, 128), (torch.bfloat16, 8, 8, 128),
+                                         (torch.bfloat16, 16, 1, 128), (torch.bfloat16, 8, 2, 64)])
 def test_paged_prefill_causal_ragged(dt, hq, hkv, d):
     # (history already in the cache, new rows): covers plain prefill, extend after a
     # prefix hit, single-token rows and empty sequences

@@ -45,8 +45,8 @@ def test_version_and_argument_errors_without_gpu(lib):
                                None, None, None, 1.0, None, 0, None, None)
     assert rc == N.ERR_ARG and b"num_kv_heads" in lib.nslg_last_error()
     with pytest.raises(N.NativeError):
-        N.call("nslg_paged_prefill", N.DTYPE_F32, 1, 4, 2, 64, 16, None, 0, None, 0, None, None,
-               4, None, None, 1, None, None, None, 0.125, 1, None, None)
+        N.call("nslg_paged_prefill", N.DTYPE_F32, 1, 4, 2, 64, 16, None, 0, 1, None, 0, None,
+               None, 4, None, None, 1, None, None, None, 0.125, 1, None, None)
     # batch 0 is a no-op
     assert lib.nslg_paged_decode(N.DTYPE_BF16, 0, 32, 8, 128, 16, None, 0, None, 0, None, None,
                                  1, None, None, None, 1.0, None, 0, None, None) == N.OK
