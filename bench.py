@@ -231,6 +231,93 @@ def run_e2e(device, steps, warmup, seed):
     return dict(total_ms=ms, h2d=stats["h2d"], d2h=stats["d2h"])
 
 
+# ------------------------------------------------------------------ prefill kernel
+def run_prefill_kernel(device, reps=10, batch=64, prompt=512):
+    """Causal prefill attention of the C3 batch-64 prompts (32/8 heads, D=128) on the
+    tcgen05 kernel: algorithmic FLOPs = sum_b sum_i 4*Hq*D*(i+1) over the causal rows."""
+    from nanoslg_b200 import ops
+    npg = -(-prompt // PS)
+    pages = batch * npg + 1
+    g = torch.Generator(device=device).manual_seed(7)
+    pool_k = torch.randn(pages, PS, HKV, D, device=device, generator=g).to(torch.bfloat16)
+    pool_v = torch.randn(pages, PS, HKV, D, device=device, generator=g).to(torch.bfloat16)
+    indices = (torch.randperm(pages - 1, device=device, generator=g)[:batch * npg] + 1).int()
+    indptr = torch.arange(0, batch * npg + 1, npg, device=device, dtype=torch.int32)
+    lpl = torch.full((batch,), prompt - (npg - 1) * PS, device=device, dtype=torch.int32)
+    qo = torch.arange(0, batch * prompt + 1, prompt, device=device, dtype=torch.int32)
+    q = torch.randn(batch * prompt, HQ, D, device=device, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(D)
+
+    def run():
+        ops.paged_prefill(q, qo, prompt, pool_k, pool_v, indptr, indices, lpl, scale,
+                          causal=True, out=out)
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    ev[0].record()
+    for i in range(reps):
+        run()
+        ev[i + 1].record()
+    torch.cuda.synchronize(device)
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(reps)]
+    flops = batch * 4 * HQ * D * (prompt * (prompt + 1) // 2)
+    ms = statistics.median(per)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+        src = "measured burst bf16_tflops"
+    except Exception:
+        peak, src = 1590.0, "fallback 1590 TFLOP/s"
+    tf = flops / (ms / 1e3) / 1e12
+    del pool_k, pool_v, q, out
+    torch.cuda.empty_cache()
+    return {"workload": f"causal prefill attention, batch {batch} x {prompt} tokens, 32/8 heads, "
+                        "D=128, page 16 (C3 prompts)", "kernel": "prefill_tc_kernel (tcgen05)",
+            "ms_median": ms, "tflops": tf, "peak_tflops": peak, "frac": tf / peak,
+            "peak_source": src, "algorithmic_flops": flops}
+
+
+# ------------------------------------------------------------------ model decode
+def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=None):
+    """Llama-3.1-8B-architecture decode (BASELINE config C3 at TP=1, TP=world under
+    torchrun): prefill of ``prompt`` random token ids per sequence, then ``steps`` timed
+    greedy decode steps of the whole batch through the B200 path."""
+    from nanoslg_b200.runner import LlamaRunner, llama_config
+    hf = llama_config("llama-3.1-8b")
+    if runner is None:
+        pages = 2 * 64 * (-(-(prompt + 8 + 64 + 2) // PS)) + 64
+        runner = LlamaRunner(hf, device, tp_size=world, rank=rank, max_kv_pages=pages)
+    g = torch.Generator().manual_seed(123 + batch)
+    prompts = torch.randint(0, hf.vocab_size, (batch, prompt), generator=g).tolist()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    tok = runner.prefill(prompts)
+    torch.cuda.synchronize(device)
+    prefill_ms = (time.perf_counter() - t0) * 1e3
+    for _ in range(warmup):
+        tok = runner.decode_step(tok)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        tok = runner.decode_step(tok)
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1)
+    if torch.distributed.is_initialized():
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    runner.release()
+    return runner, {"batch": batch, "prompt": prompt, "steps": steps, "ms_per_step": ms / steps,
+                    "tok_s": batch * steps / (ms / 1e3), "prefill_ms": prefill_ms}
+
+
 # ------------------------------------------------------------------------ CPU side
 def cpu_reference(max_seconds, n_calls=None, seed=0):
     """The reference's contiguous attend (oracle/attention.py restating
@@ -275,6 +362,8 @@ def main():
     ap.add_argument("--pool-pages", type=int, default=POOL_PAGES,
                     help="page pool size; the profiling case uses a smaller pool with the same "
                          "batch (still 1.13 GB of KV per step)")
+    ap.add_argument("--no-model", action="store_true", help="skip the Llama-3.1-8B decode leg")
+    ap.add_argument("--model-steps", type=int, default=32)
     ap.add_argument("--only", choices=["all", "kernel"], default="all",
                     help="kernel: run only the resident-input kernel timing (profiling case)")
     a = ap.parse_args()
@@ -371,6 +460,17 @@ def main():
                          "kernel_ms_median": statistics.median(kr["per_ms"])},
             "gpu_launches": 2 * a.steps,
             "clocks": kr["clocks"]}
+    line["prefill_attention"] = run_prefill_kernel(device) if rank == 0 else None
+    if not a.no_model:
+        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4)
+        _, r1 = run_llama_decode(device, world, rank, 1, 512, a.model_steps, 4, runner=runner)
+        line["llama8b_decode"] = {
+            "model": "Llama-3.1-8B architecture, random init N(0, 0.02), bf16 (BASELINE C3)",
+            "parallelism": f"TP={world}", "batch64": r64, "batch1": r1,
+            "note": "greedy decode steps through models.LlamaTP + B200PagedKVCache; GEMMs "
+                    "cuBLAS, attention/RoPE/append/RMSNorm the nslg kernels"}
+        del runner
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not a.no_cpu:
         r = cpu_reference(a.cpu_seconds)
         line["cpu_baseline"] = {"value": r["value"], "unit": "tok/s", "cores": r["cores"],

@@ -186,7 +186,11 @@ class _LlamaStage(nn.Module):
         self.cos = cos.to(self.device)
         self.sin = sin.to(self.device)
 
-    def forward(self, x, cache_ctx, mask=None):
+    def forward(self, x, cache_ctx, mask=None, last_only=False):
+        """Reference semantics (models.py:272-276): logits for every input position.
+        ``last_only`` computes the final norm and LM head for the last position only
+        (the only one the decode loop reads), which saves the [B, S, vocab] logits of a
+        long prefill."""
         h = self.embed_tokens(x) if self.is_first and x.dtype == torch.long else x
         residual = None
         for layer in self.layers:
@@ -194,9 +198,13 @@ class _LlamaStage(nn.Module):
         if residual is not None:
             # the stage's output is the residual stream after its last block
             if self.is_last:
+                if last_only:
+                    h, residual = h[:, -1:].contiguous(), residual[:, -1:].contiguous()
                 h, _ = self.norm.add_forward(h, residual)
                 return self.lm_head(h)
             return _add(h, residual)
+        if self.is_last and last_only:
+            h = h[:, -1:].contiguous()
         return self.lm_head(self.norm(h)) if self.is_last else h
 
 

@@ -1,0 +1,103 @@
+"""Batch runner driving the per-layer path the way NanoSLG's worker drives it.
+
+``LlamaRunner`` is the core of ``run_tp_worker``'s batch loop (nanoslg/worker.py:365-426):
+prefix-aware allocation with the prompt clamp of ``allocate_batch_with_prefix``
+(worker.py:169-213), one left-padded prefill forward, then greedy decode steps of
+``begin_forward -> model -> end_forward -> argmax``, and release (which inserts the
+sequences into the radix tree for later batches).  The scheduler, queues, HTTP server
+and broadcasts of the worker are not part of the path and are left out; under
+torch.distributed every TP rank runs the same runner on the same token ids, as the
+worker's ranks do after their metadata broadcasts.
+"""
+from types import SimpleNamespace
+
+import torch
+
+from . import models
+from .kv_cache import create_cache_manager
+from .parallel import ParallelConfig, ParallelContext, ParallelMode
+
+
+def llama_config(name):
+    """Architectures of the BASELINE configs (random init; no checkpoint is read)."""
+    cfgs = {
+        "tiny": dict(num_hidden_layers=2, hidden_size=256, num_attention_heads=4,
+                     num_key_value_heads=2, intermediate_size=512, vocab_size=1024,
+                     rms_norm_eps=1e-5, rope_theta=10000.0, max_position_embeddings=128),
+        "llama-3.1-8b": dict(num_hidden_layers=32, hidden_size=4096, num_attention_heads=32,
+                             num_key_value_heads=8, intermediate_size=14336, vocab_size=128256,
+                             rms_norm_eps=1e-5, rope_theta=500000.0,
+                             max_position_embeddings=8192),
+        "llama-3-70b": dict(num_hidden_layers=80, hidden_size=8192, num_attention_heads=64,
+                            num_key_value_heads=8, intermediate_size=28672, vocab_size=128256,
+                            rms_norm_eps=1e-5, rope_theta=500000.0,
+                            max_position_embeddings=8192),
+    }
+    return SimpleNamespace(**cfgs[name])
+
+
+class LlamaRunner:
+    def __init__(self, hf_config, device, dtype=torch.bfloat16, tp_size=1, rank=0,
+                 max_kv_pages=0, page_size=16, prefix_caching=True, seed=0):
+        self.device = torch.device(device)
+        self.dtype = dtype
+        mode = ParallelMode.TENSOR
+        self.pcfg = ParallelConfig(mode, tp_size)
+        ctx = ParallelContext.initialize(self.pcfg, rank, device=self.device)
+        if tp_size > 1:
+            ctx.setup_groups()
+        self.hf = hf_config
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(dtype)
+        try:
+            with torch.device(self.device):
+                self.model = models.create_model(hf_config, self.pcfg)
+        finally:
+            torch.set_default_dtype(prev)
+        models.init_random_(self.model, seed=seed + ctx.tp_rank)
+        self.model.eval()
+        mc = SimpleNamespace(page_size=page_size, max_kv_pages=max_kv_pages,
+                             enable_prefix_caching=prefix_caching)
+        self.cache = create_cache_manager(hf_config, self.pcfg, self.device, dtype, mc,
+                                          max_batch_size=0)
+        self.seq_ids = []
+
+    @torch.inference_mode()
+    def prefill(self, prompts):
+        """Allocates the batch (radix hits clamped to len-1, worker.py:190-195), runs the
+        left-padded prefill and returns the first greedy token of every sequence."""
+        mgr = self.cache
+        self.seq_ids = [f"s{i}" for i in range(len(prompts))]
+        prefix = []
+        for sid, toks in zip(self.seq_ids, prompts):
+            plen = mgr.allocate_sequence(sid, list(toks))
+            pl = len(toks)
+            prefix.append(min(plen, pl - 1) if pl > 1 else 0)
+        counts = [len(t) - p for t, p in zip(prompts, prefix)]
+        width = max(counts)
+        offsets = [width - n for n in counts]
+        ids = torch.zeros(len(prompts), width, dtype=torch.long)
+        for i, (t, p, n) in enumerate(zip(prompts, prefix, counts)):
+            ids[i, width - n:] = torch.tensor(t[p:p + n])
+        self.prefix_lens = prefix
+        ctx = mgr.begin_forward(self.seq_ids, counts, offsets)
+        logits = self.model(ids.to(self.device, non_blocking=True), ctx, last_only=True)
+        mgr.end_forward(ctx)
+        return logits[:, -1].argmax(-1)
+
+    @torch.inference_mode()
+    def decode_step(self, tokens):
+        mgr = self.cache
+        ctx = mgr.begin_forward(self.seq_ids, [1] * len(self.seq_ids))
+        logits = self.model(tokens[:, None], ctx, last_only=True)
+        mgr.end_forward(ctx)
+        return logits[:, -1].argmax(-1)
+
+    def release(self, generated=None):
+        """Records generated ids (for radix insertion) and releases the batch."""
+        if generated is not None:
+            for sid, ids in zip(self.seq_ids, generated):
+                self.cache.append_token_ids(sid, list(ids))
+        for sid in self.seq_ids:
+            self.cache.release_sequence(sid)
+        self.seq_ids = []

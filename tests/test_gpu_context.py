@@ -159,3 +159,27 @@ def test_tiny_llama_greedy_tokens_match_reference():
             logits = model(torch.tensor([[t]], device=DEV), ctx)
             mgr.end_forward(ctx)
     assert toks == g["tokens"]
+
+
+def test_runner_tiny_llama_matches_reference_tokens():
+    """The batch runner (worker.py's loop) on config C1 gives the reference's tokens, also
+    for a second batch that hits the radix tree with the same prompt."""
+    from nanoslg_b200.runner import LlamaRunner
+    with open(os.path.join(GOLDEN, "tiny_llama.json")) as f:
+        g = json.load(f)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    r = LlamaRunner(SimpleNamespace(**g["config"]), DEV, dtype=torch.float32, max_kv_pages=64)
+    # the runner builds on the device; re-draw the weights with the fixture's CPU rule
+    from nanoslg_b200 import models
+    cpu = models.init_random_(models.create_model(SimpleNamespace(**g["config"]), r.pcfg).float())
+    r.model.load_state_dict(cpu.state_dict())
+    for attempt in range(2):
+        tok = r.prefill([g["prompt"]])
+        toks = [int(tok[0])]
+        for _ in range(len(g["tokens"]) - 1):
+            tok = r.decode_step(tok)
+            toks.append(int(tok[0]))
+        assert toks == g["tokens"], f"batch {attempt}"
+        if attempt == 1:
+            assert r.prefix_lens == [16]          # 32-token prompt: 2 cached pages, clamped
+        r.release([toks])
