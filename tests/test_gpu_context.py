@@ -162,24 +162,32 @@ def test_tiny_llama_greedy_tokens_match_reference():
 
 
 def test_runner_tiny_llama_matches_reference_tokens():
-    """The batch runner (worker.py's loop) on config C1 gives the reference's tokens, also
-    for a second batch that hits the radix tree with the same prompt."""
+    """The batch runner (worker.py's loop) on config C1 gives the reference's tokens; a
+    second batch whose prompt is the first prompt plus 8 generated tokens reuses the two
+    cached prompt pages through the radix tree and continues the same greedy sequence."""
+    from nanoslg_b200 import models
     from nanoslg_b200.runner import LlamaRunner
     with open(os.path.join(GOLDEN, "tiny_llama.json")) as f:
         g = json.load(f)
     torch.backends.cuda.matmul.allow_tf32 = False
-    r = LlamaRunner(SimpleNamespace(**g["config"]), DEV, dtype=torch.float32, max_kv_pages=64)
-    # the runner builds on the device; re-draw the weights with the fixture's CPU rule
-    from nanoslg_b200 import models
-    cpu = models.init_random_(models.create_model(SimpleNamespace(**g["config"]), r.pcfg).float())
+    hf = SimpleNamespace(**g["config"])
+    r = LlamaRunner(hf, DEV, dtype=torch.float32, max_kv_pages=64)
+    # the runner draws its weights on the device; load the fixture's CPU draw instead
+    cpu = models.init_random_(models.create_model(hf, r.pcfg).float())
     r.model.load_state_dict(cpu.state_dict())
-    for attempt in range(2):
-        tok = r.prefill([g["prompt"]])
-        toks = [int(tok[0])]
-        for _ in range(len(g["tokens"]) - 1):
-            tok = r.decode_step(tok)
-            toks.append(int(tok[0]))
-        assert toks == g["tokens"], f"batch {attempt}"
-        if attempt == 1:
-            assert r.prefix_lens == [16]          # 32-token prompt: 2 cached pages, clamped
-        r.release([toks])
+    want = g["tokens"]
+    tok = r.prefill([g["prompt"]])
+    toks = [int(tok[0])]
+    for _ in range(len(want) - 1):
+        tok = r.decode_step(tok)
+        toks.append(int(tok[0]))
+    assert toks == want
+    r.release([toks])
+    tok = r.prefill([g["prompt"] + want[:8]])
+    assert r.prefix_lens == [32]                 # two 16-token pages from the radix tree
+    toks2 = [int(tok[0])]
+    for _ in range(7):
+        tok = r.decode_step(tok)
+        toks2.append(int(tok[0]))
+    assert toks2 == want[8:16]
+    r.release([toks2])
