@@ -207,10 +207,7 @@ def run_e2e(device, steps, warmup, seed):
         hout.copy_(out, non_blocking=True)
         torch.cuda.current_stream(device).synchronize()   # the result is on the host
         mgr.end_forward(ctx)
-        plan = (ctx.kv_indices.numel() + ctx.kv_indptr.numel() + ctx.kv_last_page_len.numel()
-                + ctx.qo_indptr.numel() + ctx.q_row_start.numel() + ctx._write_loc.numel()
-                + ctx._pos_i32.numel()) * 4
-        stats["h2d"] = q.numel() * 2 + k.numel() * 2 + v.numel() * 2 + plan
+        stats["h2d"] = q.numel() * 2 + k.numel() * 2 + v.numel() * 2 + ctx._plan_bytes
         stats["d2h"] = hout.numel() * 2
 
     for i in range(warmup):
@@ -290,6 +287,7 @@ def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=N
     if runner is None:
         pages = 2 * 64 * (-(-(prompt + 8 + 64 + 2) // PS)) + 64
         runner = LlamaRunner(hf, device, tp_size=world, rank=rank, max_kv_pages=pages)
+        runner.enable_cuda_graphs([64, 1])
     g = torch.Generator().manual_seed(123 + batch)
     prompts = torch.randint(0, hf.vocab_size, (batch, prompt), generator=g).tolist()
     torch.cuda.synchronize(device)

@@ -16,7 +16,6 @@ in place.  The per-forward plan (positions, write slots, CSR) is built once per
 and no CPU fallback; the bookkeeping itself runs on any device (tests drive it with
 CPU tensors), the kernels need CUDA.
 """
-import itertools
 import math
 import threading
 from abc import ABC, abstractmethod
@@ -354,12 +353,57 @@ class RadixTree:
         return c
 
 
+class _BlockTable(list):
+    """A sequence's page list -- the reference's ``block_table`` list, same contents and
+    list behaviour -- with an int32 numpy mirror kept in step on every append, extend and
+    item assignment, so a forward's CSR page list is a concatenation of array prefixes
+    instead of a Python loop over every page of every sequence."""
+    __slots__ = ("arr",)
+
+    def __init__(self, pages=()):
+        super().__init__(pages)
+        self.arr = np.empty(max(16, 2 * len(self)), dtype=np.int32)
+        if len(self):
+            self.arr[:len(self)] = np.asarray(self, dtype=np.int32)
+
+    def _reserve(self, n, keep):
+        """Capacity for n entries, preserving the first ``keep``."""
+        if n > self.arr.size:
+            grown = np.empty(max(n, 2 * self.arr.size), dtype=np.int32)
+            grown[:keep] = self.arr[:keep]
+            self.arr = grown
+
+    def extend(self, pages):
+        pages = list(pages)
+        old = len(self)
+        self._reserve(old + len(pages), old)
+        super().extend(pages)
+        self.arr[old:len(self)] = pages
+
+    def append(self, page):
+        self.extend([page])
+
+    def __setitem__(self, i, v):
+        super().__setitem__(i, v)
+        if isinstance(i, slice):
+            self._reserve(len(self), 0)
+            self.arr[:len(self)] = np.asarray(self, dtype=np.int32)
+        else:
+            self.arr[i if i >= 0 else i + len(self)] = v
+
+    def prefix(self, n):
+        """int32 array of the first n page ids, 0 (the null page) past the end."""
+        if n <= len(self):
+            return self.arr[:n]
+        return np.concatenate([self.arr[:len(self)], np.zeros(n - len(self), np.int32)])
+
+
 class _PagedSeqState:
     __slots__ = ("seq_id", "block_table", "num_tokens", "prefix_len", "token_ids")
 
     def __init__(self, sid, prefix_pages=None, plen=0, tids=None):
         self.seq_id = sid
-        self.block_table = list(prefix_pages or [])
+        self.block_table = _BlockTable(prefix_pages or [])
         self.num_tokens = plen
         self.prefix_len = plen
         self.token_ids = list(tids or [])
@@ -438,27 +482,25 @@ class B200CacheContext(CacheContext):
             self._write_info.append(info)
 
         # CSR page list (kv_cache.py:598-615)
+        kv_lens = np.asarray(self.seq_lens, dtype=np.int64)
+        npgs = (kv_lens + ps - 1) // ps
         indptr = np.zeros(B + 1, dtype=np.int32)
-        lpl = np.zeros(max(B, 1), dtype=np.int32)
-        tables = []
-        for b in range(B):
-            st = cache.seqs[seq_ids[b]]
-            kv = self.seq_lens[b]
-            npg = -(-kv // ps) if kv > 0 else 0
-            bt = st.block_table
-            tables.append(bt[:npg] if npg <= len(bt) else bt + [0] * (npg - len(bt)))
-            indptr[b + 1] = indptr[b] + npg
-            lpl[b] = (kv - (npg - 1) * ps) if npg > 0 else 0
+        indptr[1:] = np.cumsum(npgs)
+        lpl = np.where(npgs > 0, kv_lens - (npgs - 1) * ps, 0).astype(np.int32)
         total = int(indptr[B])
-        indices = np.fromiter(itertools.chain.from_iterable(tables), dtype=np.int32,
-                              count=total) if total else np.zeros(1, dtype=np.int32)
+        indices = (np.concatenate([cache.seqs[s].block_table.prefix(int(n))
+                                   for s, n in zip(seq_ids, npgs)])
+                   if total else np.zeros(1, dtype=np.int32))
         qo = np.zeros(B + 1, dtype=np.int32)
         qo[1:] = np.cumsum(new_token_counts, dtype=np.int64) if B else []
         row_start = (np.arange(B, dtype=np.int32) * iw
                      + np.asarray(self.input_offsets, dtype=np.int32)) if B else \
             np.zeros(0, dtype=np.int32)
 
-        parts = [positions.ravel(), write_loc.ravel(), indptr, indices, lpl, qo, row_start]
+        # one int32 buffer, page ids last so that every other view sits at an offset that
+        # depends only on (B, input width): a fixed plan buffer keeps them in place
+        parts = [positions.ravel(), write_loc.ravel(), indptr, lpl[:max(B, 1)], qo, row_start,
+                 indices]
         offs = np.cumsum([0] + [p.size for p in parts])
         flat = np.concatenate(parts)
         host = torch.from_numpy(flat)
@@ -466,15 +508,17 @@ class B200CacheContext(CacheContext):
         if dev_t.type == "cuda":
             host = host.pin_memory()
         pool.flush_zero()
-        d = host.to(dev_t, non_blocking=True)
+        static = cache.static_plan_for(B, iw, flat.size)
+        if static is not None:
+            static[:flat.size].copy_(host, non_blocking=True)
+            d = static
+        else:
+            d = host.to(dev_t, non_blocking=True)
         views = [d[offs[i]:offs[i + 1]] for i in range(len(parts))]
-        (self._pos_i32, self._write_loc, self.kv_indptr, self.kv_indices,
-         self.kv_last_page_len, self.qo_indptr, self.q_row_start) = views
-        self.kv_indices = self.kv_indices[:max(total, 1)]
-        self._indptr_host = indptr
-        self._indices_host = indices[:total]
-        self._lpl_host = lpl[:B]
-        self._qo_host = qo
+        (self._pos_i32, self._write_loc, self.kv_indptr, self.kv_last_page_len,
+         self.qo_indptr, self.q_row_start, self.kv_indices) = views
+        self.kv_last_page_len = self.kv_last_page_len[:max(B, 1)]
+        self._plan_bytes = flat.size * 4
         self._pos64 = None
         self._sm_scale = 1.0 / math.sqrt(cfg.head_dim)
 
@@ -536,6 +580,22 @@ class B200PagedKVCache(KVCacheManager):
         self.pool = PagePool(cfg)
         self.tree = RadixTree(cfg.page_size, self.pool) if cfg.enable_prefix_caching else None
         self.seqs: Dict[str, _PagedSeqState] = {}
+        self._static_plans: Dict[Tuple[int, int], torch.Tensor] = {}
+
+    def use_static_plan(self, batch, input_width=1, max_pages=None):
+        """From now on, forwards of exactly (batch, input_width) put their plan into one
+        fixed device buffer (page-id capacity ``max_pages``, default the whole pool), so a
+        CUDA graph captured over one such forward can be replayed for the later ones."""
+        cap = max_pages if max_pages is not None else self.cfg.max_pages
+        n = 2 * batch * input_width + (batch + 1) + max(batch, 1) + (batch + 1) + batch + cap
+        self._static_plans[(batch, input_width)] = torch.zeros(
+            n, dtype=torch.int32, device=self.cfg.device)
+
+    def static_plan_for(self, batch, input_width, size):
+        buf = self._static_plans.get((batch, input_width))
+        if buf is not None and size > buf.numel():
+            raise RuntimeError("plan larger than the static plan buffer")
+        return buf
 
     def allocate_sequence(self, seq_id, token_ids=None, num_tokens=0):
         tids = token_ids or []

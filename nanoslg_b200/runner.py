@@ -61,6 +61,17 @@ class LlamaRunner:
         self.cache = create_cache_manager(hf_config, self.pcfg, self.device, dtype, mc,
                                           max_batch_size=0)
         self.seq_ids = []
+        self.use_graphs = False
+        self._graphs = {}        # batch -> (graph, static tokens in, static tokens out)
+
+    def enable_cuda_graphs(self, batches):
+        """Decode steps of these batch sizes run as one captured CUDA graph each: the plan
+        goes into a fixed device buffer (copied from pinned memory before every replay), the
+        token ids into a fixed input tensor, and the whole model forward plus argmax replays
+        without per-kernel launches from Python."""
+        for b in batches:
+            self.cache.use_static_plan(b, 1)
+        self.use_graphs = True
 
     @torch.inference_mode()
     def prefill(self, prompts):
@@ -88,10 +99,34 @@ class LlamaRunner:
     @torch.inference_mode()
     def decode_step(self, tokens):
         mgr = self.cache
-        ctx = mgr.begin_forward(self.seq_ids, [1] * len(self.seq_ids))
-        logits = self.model(tokens[:, None], ctx, last_only=True)
+        B = len(self.seq_ids)
+        ctx = mgr.begin_forward(self.seq_ids, [1] * B)
+        if not (self.use_graphs and mgr.static_plan_for(B, 1, 0) is not None):
+            logits = self.model(tokens[:, None], ctx, last_only=True)
+            mgr.end_forward(ctx)
+            return logits[:, -1].argmax(-1)
+        entry = self._graphs.get(B)
+        if entry is None:
+            tok_in = tokens.clone()
+            # warm-up forwards on a side stream, then capture; each re-writes this step's
+            # K/V slots with the same values
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self.model(tok_in[:, None], ctx, last_only=True)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                logits = self.model(tok_in[:, None], ctx, last_only=True)
+                tok_out = logits[:, -1].argmax(-1)
+            entry = (graph, tok_in, tok_out)
+            self._graphs[B] = entry
+        else:
+            entry[1].copy_(tokens)
+        entry[0].replay()
         mgr.end_forward(ctx)
-        return logits[:, -1].argmax(-1)
+        return entry[2].clone()
 
     def release(self, generated=None):
         """Records generated ids (for radix insertion) and releases the batch."""

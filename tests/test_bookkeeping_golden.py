@@ -113,3 +113,26 @@ def test_factory_returns_b200_backend():
     mgr = create_cache_manager(hf, None, torch.device("cpu"), torch.float32, mc)
     assert isinstance(mgr, B200PagedKVCache) and mgr.cfg.backend == "b200"
     assert tuple(mgr.pool.k.shape) == (2, 32, 16, 2, 64)
+
+
+def test_csr_matches_plain_loop_restatement_at_c2_size():
+    """At the full C2 batch (64 sequences, lengths U[512, 8192]) the vectorised CSR of a
+    decode step equals the reference's per-page loop restated in oracle/paged_plan.py."""
+    from oracle import paged_plan
+    g = torch.Generator().manual_seed(0)
+    lens = torch.randint(512, 8193, (64,), generator=g).tolist()
+    mgr = _manager(16, 40000)
+    sids = [f"s{i}" for i in range(64)]
+    for s, n in zip(sids, lens):
+        mgr.allocate_sequence(s, None, num_tokens=n)
+        mgr.seqs[s].num_tokens = n
+    for step in range(3):
+        ctx = mgr.begin_forward(sids, [1] * 64)
+        bts = [list(mgr.seqs[s].block_table) for s in sids]
+        ind, idx, lpl = paged_plan.csr(bts, ctx.seq_lens, 16)
+        assert ctx.kv_indptr.tolist() == ind
+        assert ctx.kv_indices.tolist() == idx
+        assert ctx.kv_last_page_len.tolist() == lpl
+        wi = paged_plan.write_targets(bts, ctx.start_positions, [1] * 64, 16)
+        assert [[list(x) for x in w] for w in ctx._write_info] == [[list(x) for x in w] for w in wi]
+        mgr.end_forward(ctx)
