@@ -362,8 +362,9 @@ def main():
                          "batch (still 1.13 GB of KV per step)")
     ap.add_argument("--no-model", action="store_true", help="skip the Llama-3.1-8B decode leg")
     ap.add_argument("--model-steps", type=int, default=32)
-    ap.add_argument("--only", choices=["all", "kernel"], default="all",
-                    help="kernel: run only the resident-input kernel timing (profiling case)")
+    ap.add_argument("--only", choices=["all", "kernel", "model"], default="all",
+                    help="kernel: only the resident-input kernel timing (profiling case); "
+                         "model: only the Llama-3.1-8B decode leg")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -410,6 +411,13 @@ def main():
     if not os.path.exists(nbuild.LIB):
         nbuild.build()
 
+    if a.only == "model":
+        _, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4)
+        if rank == 0:
+            print(json.dumps({"case": "model only", "llama8b_decode_batch64": r64}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
     kr = run_kernel(device, a.steps, a.warmup, seed=rank, pool_pages=a.pool_pages)
     if a.only == "kernel":
         if rank == 0:

@@ -195,7 +195,8 @@ def test_runner_tiny_llama_matches_reference_tokens():
 
 def test_runner_cuda_graph_decode_matches_reference_tokens():
     """Decode steps replayed from a captured CUDA graph (fixed plan buffer, fixed token
-    input) produce the same greedy tokens as the reference, across two batches."""
+    input) give the reference's greedy tokens; a second batch (radix hit on the first
+    prompt's pages) replays the same graph and continues the sequence."""
     from nanoslg_b200 import models
     from nanoslg_b200.runner import LlamaRunner
     with open(os.path.join(GOLDEN, "tiny_llama.json")) as f:
@@ -206,12 +207,20 @@ def test_runner_cuda_graph_decode_matches_reference_tokens():
     cpu = models.init_random_(models.create_model(hf, r.pcfg).float())
     r.model.load_state_dict(cpu.state_dict())
     r.enable_cuda_graphs([1])
-    for _ in range(2):
-        tok = r.prefill([g["prompt"]])
-        toks = [int(tok[0])]
-        for _ in range(len(g["tokens"]) - 1):
-            tok = r.decode_step(tok)
-            toks.append(int(tok[0]))
-        assert toks == g["tokens"]
-        r.release()                               # no token ids recorded: no radix hit
+    want = g["tokens"]
+    tok = r.prefill([g["prompt"]])
+    toks = [int(tok[0])]
+    for _ in range(len(want) - 1):
+        tok = r.decode_step(tok)
+        toks.append(int(tok[0]))
+    assert toks == want
     assert 1 in r._graphs
+    r.release([toks])
+    tok = r.prefill([g["prompt"] + want[:8]])
+    assert r.prefix_lens == [32]
+    toks2 = [int(tok[0])]
+    for _ in range(7):
+        tok = r.decode_step(tok)
+        toks2.append(int(tok[0]))
+    assert toks2 == want[8:16]
+    r.release([toks2])
