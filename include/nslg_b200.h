@@ -168,6 +168,17 @@ int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x,
                           const void* weight, void* out, int64_t out_stride, float eps,
                           void* stream);
 
+/* SwiGLU activation on a fused gate|up projection output.
+ *
+ * Replaces F.silu(gate_proj(x)) * up_proj(x) (models.py:156-157) when the gate and up
+ * weights are stacked into one GEMM: gate_up is [rows, 2*inter] (gate in columns
+ * [0, inter), up in [inter, 2*inter)) with row stride gate_up_stride; out [rows, inter]
+ * with row stride out_stride receives silu(gate) * up, each op rounded to dtype as in
+ * the reference.
+ */
+int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gate_up_stride,
+                  void* out, int64_t out_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

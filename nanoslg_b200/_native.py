@@ -40,6 +40,7 @@ SIGNATURES = {
     "nslg_paged_prefill": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64,
                                   _vp, _vp, _i32, _vp, _vp, _i64, _vp, _vp, _vp, _f32, _i32, _vp,
                                   _vp]),
+    "nslg_silu_mul": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp]),
     "nslg_rmsnorm_residual": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i64,
                                      _f32, _vp]),
 }

@@ -193,4 +193,19 @@ int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int64_
                                  weight, out, out_stride, eps, static_cast<cudaStream_t>(stream));
 }
 
+int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gate_up_stride,
+                  void* out, int64_t out_stride, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return set_error(NSLG_ERR_ARG, "silu_mul: bad dtype");
+  if (rows < 0 || inter <= 0) return set_error(NSLG_ERR_ARG, "silu_mul: bad shape");
+  if (rows == 0) return NSLG_OK;
+  if (!gate_up || !out) return set_error(NSLG_ERR_ARG, "silu_mul: null pointer");
+  const int64_t es = esize(dtype);
+  if ((inter * es) % 16 || !aligned16(gate_up) || !aligned16(out) || (gate_up_stride * es) % 16 ||
+      (out_stride * es) % 16)
+    return set_error(NSLG_ERR_ARG, "silu_mul: rows must be 16-byte aligned");
+  return launch_silu_mul(dtype, rows, inter, gate_up, gate_up_stride, out, out_stride,
+                         static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -39,6 +39,9 @@ int launch_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int6
                             void* residual, int64_t residual_stride, const void* weight,
                             void* out, int64_t out_stride, float eps, cudaStream_t stream);
 
+int launch_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gu_stride,
+                    void* out, int64_t out_stride, cudaStream_t stream);
+
 // CUDA-core paged attention (any page size, head_dim <= 256, fp32 or bf16): decode is
 // the qo_len == 1 case.
 int launch_paged_attention_simt(int dtype, int batch, int hq, int hkv, int d, int page_size,

@@ -106,12 +106,27 @@ class TPAttention(nn.Module):
         self.k_proj = ColumnParallelLinear(h, self.n_kv_heads * d, gather_output=False)
         self.v_proj = ColumnParallelLinear(h, self.n_kv_heads * d, gather_output=False)
         self.o_proj = RowParallelLinear(self.n_heads * d, h, input_is_parallel=True)
+        self._qkv = None
+
+    def fuse_projections(self):
+        """Stacks the q, k and v weights into one buffer and makes the three Parameters
+        views of it (same names, shapes and state-dict entries), so one GEMM produces
+        q, k and v and reads the layer's input once."""
+        self._qkv = _stack_as_views([self.q_proj, self.k_proj, self.v_proj])
 
     def forward(self, x, cos, sin, cache_ctx, mask=None):
         B, S, _ = x.shape
-        q = self.q_proj(x).view(B, S, self.n_heads_tp, self.head_dim)
-        k = self.k_proj(x).view(B, S, self.n_kv_heads_tp, self.head_dim)
-        v = self.v_proj(x).view(B, S, self.n_kv_heads_tp, self.head_dim)
+        hd = self.head_dim
+        if _views_intact(self._qkv, [self.q_proj, self.k_proj, self.v_proj]):
+            qkv = F.linear(x, self._qkv)
+            nq, nk = self.n_heads_tp * hd, self.n_kv_heads_tp * hd
+            q = qkv[..., :nq].view(B, S, self.n_heads_tp, hd)
+            k = qkv[..., nq:nq + nk].view(B, S, self.n_kv_heads_tp, hd)
+            v = qkv[..., nq + nk:].view(B, S, self.n_kv_heads_tp, hd)
+        else:
+            q = self.q_proj(x).view(B, S, self.n_heads_tp, hd)
+            k = self.k_proj(x).view(B, S, self.n_kv_heads_tp, hd)
+            v = self.v_proj(x).view(B, S, self.n_kv_heads_tp, hd)
         a = _attention_forward(q, k, v, self.layer_idx, self.n_heads_tp, self.n_kv_heads_tp,
                                cos, sin, cache_ctx)
         return self.o_proj(a)
@@ -124,9 +139,44 @@ class TPMLP(nn.Module):
         self.gate_proj = ColumnParallelLinear(h, i, gather_output=False)
         self.up_proj = ColumnParallelLinear(h, i, gather_output=False)
         self.down_proj = RowParallelLinear(i, h, input_is_parallel=True)
+        self._gu = None
+
+    def fuse_projections(self):
+        """Stacks gate and up weights (views, as in TPAttention.fuse_projections): one GEMM
+        and one silu*mul kernel instead of two GEMMs and two elementwise kernels."""
+        self._gu = _stack_as_views([self.gate_proj, self.up_proj])
 
     def forward(self, x):
+        if _views_intact(self._gu, [self.gate_proj, self.up_proj]):
+            return self.down_proj(ops.silu_mul(F.linear(x, self._gu)))
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+def _stack_as_views(linears):
+    """Concatenates the layers' weights along the output dim into one tensor and turns each
+    layer's weight Parameter into a view of its rows (in-place loads keep them views)."""
+    stacked = torch.cat([m.weight.data for m in linears], 0)
+    row = 0
+    for m in linears:
+        n = m.weight.shape[0]
+        m.weight = nn.Parameter(stacked[row:row + n], requires_grad=m.weight.requires_grad)
+        row += n
+    return stacked
+
+
+def _views_intact(stacked, linears):
+    """True while every weight is still the view of ``stacked`` made by _stack_as_views
+    (a later model.to(...) replaces Parameters with fresh tensors and ends the fusion)."""
+    if stacked is None:
+        return False
+    ptr, es = stacked.data_ptr(), stacked.element_size()
+    row = 0
+    for m in linears:
+        w = m.weight
+        if w.dtype != stacked.dtype or w.data_ptr() != ptr + row * stacked.shape[1] * es:
+            return False
+        row += w.shape[0]
+    return True
 
 
 class TPTransformerBlock(nn.Module):
@@ -210,6 +260,15 @@ class _LlamaStage(nn.Module):
 
 def _add(a, b):
     return b.add_(a)
+
+
+def fuse_projections(model):
+    """Fuses the q/k/v and gate/up GEMMs of every block of ``model`` (call once the model
+    is on its final device and dtype)."""
+    for layer in model.layers:
+        layer.self_attn.fuse_projections()
+        layer.mlp.fuse_projections()
+    return model
 
 
 class LlamaTP(_LlamaStage):

@@ -216,3 +216,22 @@ def rmsnorm_residual(x, weight, eps, residual=None, out=None):
            r2.stride(0) if r2 is not None else 0, _ptr(weight), _ptr(out2), out2.stride(0),
            float(eps), _stream(x))
     return out.view(x.shape)
+
+
+def silu_mul(gate_up, out=None):
+    """silu(gate) * up of a fused [..., 2*I] gate|up tensor -> [..., I]."""
+    _need_cuda(gate_up, out)
+    dt = _dtype_code(gate_up)
+    two_i = gate_up.shape[-1]
+    inter = two_i // 2
+    if gate_up.stride(-1) != 1 or two_i % 2:
+        raise ValueError("silu_mul: last dim must be contiguous and even")
+    rows = gate_up.numel() // two_i
+    g2 = gate_up.reshape(rows, two_i)
+    if out is None:
+        out = torch.empty(gate_up.shape[:-1] + (inter,), dtype=gate_up.dtype,
+                          device=gate_up.device)
+    o2 = out.view(rows, inter)
+    N.call("nslg_silu_mul", dt, rows, inter, _ptr(g2), g2.stride(0), _ptr(o2), o2.stride(0),
+           _stream(gate_up))
+    return out

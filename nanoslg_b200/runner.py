@@ -55,6 +55,7 @@ class LlamaRunner:
         finally:
             torch.set_default_dtype(prev)
         models.init_random_(self.model, seed=seed + ctx.tp_rank)
+        models.fuse_projections(self.model)
         self.model.eval()
         mc = SimpleNamespace(page_size=page_size, max_kv_pages=max_kv_pages,
                              enable_prefix_caching=prefix_caching)

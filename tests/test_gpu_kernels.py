@@ -169,3 +169,42 @@ def test_bad_page_id_sets_status_without_fault():
                       pk["pool_k"], pk["pool_v"], pk["indptr"], bad, pk["lpl"], 0.1)
     with pytest.raises(RuntimeError, match="page id outside the pool"):
         ops.check_device_status(DEV)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_silu_mul_matches_reference_ops(dt):
+    g = torch.Generator().manual_seed(12)
+    gu = (torch.randn(37, 2 * 1024, generator=g) * 3).to(dt).to(DEV)
+    out = ops.silu_mul(gu)
+    ref = torch.nn.functional.silu(gu[:, :1024]) * gu[:, 1024:]     # models.py:156-157
+    tol = dict(rtol=1e-2, atol=1e-2) if dt == torch.bfloat16 else dict(rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(out, ref, **tol)
+
+
+def test_fused_projections_match_separate_layers():
+    """One stacked q/k/v GEMM and one gate/up GEMM + silu*mul give the same block output
+    as the reference's separate projections (bf16, GEMM rounding tolerance)."""
+    from nanoslg_b200 import models
+    from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
+    from nanoslg_b200.parallel import ParallelConfig, ParallelContext, ParallelMode
+    from nanoslg_b200.runner import llama_config
+    hf = llama_config("tiny")
+    pc = ParallelConfig(ParallelMode.TENSOR, 1)
+    ParallelContext.initialize(pc, 0, device=DEV)
+    m = models.init_random_(models.create_model(hf, pc)).to(DEV).to(torch.bfloat16)
+    ids = torch.randint(0, 1024, (3, 20), device=DEV)
+    outs = []
+    for fused in (False, True):
+        if fused:
+            models.fuse_projections(m)
+        cfg = KVCacheConfig(num_layers=2, num_kv_heads=2, num_qo_heads=4, head_dim=64,
+                            page_size=16, max_pages=32, dtype=torch.bfloat16, device=DEV)
+        mgr = B200PagedKVCache(cfg)
+        for i in range(3):
+            mgr.allocate_sequence(f"s{i}")
+        ctx = mgr.begin_forward(["s0", "s1", "s2"], [20, 20, 20], [0, 0, 0])
+        with torch.inference_mode():
+            outs.append(m(ids, ctx).float())
+    assert models._views_intact(m.layers[0].mlp._gu, [m.layers[0].mlp.gate_proj,
+                                                      m.layers[0].mlp.up_proj])
+    torch.testing.assert_close(outs[1], outs[0], rtol=2e-2, atol=2e-2)
