@@ -38,19 +38,20 @@ def _rows(x, name):
     """Views ``x`` ([..., H, D] with contiguous heads) as rows: returns (rows, stride)."""
     if x.dim() < 2 or x.stride(-1) != 1 or x.stride(-2) != x.shape[-1]:
         raise ValueError(f"{name}: heads and head_dim must be contiguous, got strides {x.stride()}")
-    lead = x.shape[:-2]
     n = 1
-    for s in lead:
+    for s in x.shape[:-2]:
         n *= s
-    if x.dim() == 2:
-        return 1, x.shape[-1] * x.shape[-2]
-    # all leading dims must collapse into one row index with a single stride
-    stride = x.stride(-3)
+    # the leading dims must collapse into one row index with a single stride; size-1 dims
+    # carry no stride information (views give them arbitrary strides) and are skipped
+    dims = [(x.shape[i], x.stride(i)) for i in range(x.dim() - 2) if x.shape[i] != 1]
+    if not dims:
+        return n, x.shape[-1] * x.shape[-2]
+    stride = dims[-1][1]
     expect = stride
-    for dim in range(x.dim() - 3, -1, -1):
-        if x.shape[dim] != 1 and x.stride(dim) != expect:
+    for size, st in reversed(dims):
+        if st != expect:
             raise ValueError(f"{name}: leading dims do not form one row stride {x.stride()}")
-        expect *= x.shape[dim]
+        expect *= size
     return n, stride
 
 
