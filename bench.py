@@ -405,14 +405,15 @@ def main():
     device = torch.device(f"cuda:{local}")
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                              device_id=device)
     from nanoslg_b200 import build as nbuild
     if not os.path.exists(nbuild.LIB):
         nbuild.build()
 
     if a.only == "model":
-        _, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4)
+        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4)
+        runner.close()
         if rank == 0:
             print(json.dumps({"case": "model only", "llama8b_decode_batch64": r64}), flush=True)
         if world > 1:
@@ -475,8 +476,8 @@ def main():
             "parallelism": f"TP={world}", "batch64": r64, "batch1": r1,
             "note": "greedy decode steps through models.LlamaTP + B200PagedKVCache; GEMMs "
                     "cuBLAS, attention/RoPE/append/RMSNorm the nslg kernels"}
+        runner.close()
         del runner
-        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not a.no_cpu:
         r = cpu_reference(a.cpu_seconds)
         line["cpu_baseline"] = {"value": r["value"], "unit": "tok/s", "cores": r["cores"],

@@ -129,6 +129,15 @@ class LlamaRunner:
         mgr.end_forward(ctx)
         return entry[2].clone()
 
+    def close(self):
+        """Drops the captured graphs (they may hold NCCL calls, which must be gone before
+        the process group is destroyed), the model and the cache."""
+        self._graphs.clear()
+        self.model = None
+        self.cache = None
+        torch.cuda.synchronize(self.device)
+        torch.cuda.empty_cache()
+
     def release(self, generated=None):
         """Records generated ids (for radix insertion) and releases the batch."""
         if generated is not None:

@@ -1,0 +1,73 @@
+"""N > 1 host logic on CPU with two gloo ranks: the TP linear layers and collectives of
+nanoslg_b200.tp_layers / parallel (Megatron column/row split, SUM all-reduce, LM-head
+all-gather) against one unsplit layer, and identical page tables on every TP rank (each
+rank runs the same bookkeeping on the same token ids, so attention needs no exchange)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nanoslg_b200 import parallel, tp_layers
+        from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
+        cfg = parallel.ParallelConfig(parallel.ParallelMode.TENSOR, world)
+        ctx = parallel.ParallelContext.initialize(cfg, rank, device="cpu")
+        ctx.setup_groups()
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(3, 5, 16, generator=g)
+        w_col = torch.randn(8, 16, generator=g)
+        w_row = torch.randn(16, 8, generator=g)
+        col = tp_layers.ColumnParallelLinear(16, 8, gather_output=True)
+        row = tp_layers.RowParallelLinear(8, 16)
+        with torch.no_grad():
+            col.weight.copy_(w_col.chunk(world, 0)[rank])          # models.py:409-421 split
+            row.weight.copy_(w_row.chunk(world, 1)[rank])          # models.py:424-427 split
+            y_col = col(x)
+            y_row = row(torch.nn.functional.linear(x, w_col).chunk(world, -1)[rank].contiguous())
+        ok_col = torch.allclose(y_col, torch.nn.functional.linear(x, w_col), atol=1e-5)
+        ok_row = torch.allclose(y_row, torch.nn.functional.linear(
+            torch.nn.functional.linear(x, w_col), w_row), atol=1e-4)
+        # bookkeeping: same ops on every rank -> same CSR
+        kc = KVCacheConfig(num_layers=1, num_kv_heads=8 // world, num_qo_heads=32 // world,
+                           head_dim=16, page_size=16, max_pages=256, dtype=torch.float32,
+                           device=torch.device("cpu"))
+        mgr = B200PagedKVCache(kc)
+        for i, n in enumerate([40, 17, 300]):
+            mgr.allocate_sequence(f"s{i}", list(range(i, i + n)))
+        c = mgr.begin_forward(["s0", "s1", "s2"], [40, 17, 300], [260, 283, 0])
+        sig = torch.tensor([hash((tuple(c.kv_indices.tolist()), tuple(c._write_loc.tolist())))
+                            % (1 << 31)], dtype=torch.int64)
+        sigs = [torch.zeros_like(sig) for _ in range(world)]
+        dist.all_gather(sigs, sig)
+        same = all(int(s) == int(sigs[0]) for s in sigs)
+        out[rank] = (ok_col, ok_row, same, tuple(col.weight.shape), tuple(row.weight.shape))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_tp_layers_and_bookkeeping():
+    world = 2
+    port = _free_port()
+    with mp.Manager() as m:
+        out = m.dict()
+        mp.start_processes(_worker, args=(world, port, out), nprocs=world, start_method="spawn",
+                           join=True)
+        res = dict(out)
+    assert set(res) == {0, 1}
+    for rank, (ok_col, ok_row, same, wc, wr) in res.items():
+        assert ok_col and ok_row and same, (rank, res[rank])
+        assert wc == (4, 16) and wr == (16, 4)
