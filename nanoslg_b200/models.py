@@ -307,6 +307,34 @@ def create_model(hf_config, parallel_config):
     raise ValueError(f"Unknown mode: {parallel_config.mode}")
 
 
+_COLUMN = ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj", "lm_head")
+_ROW = ("o_proj", "down_proj")
+
+
+def load_full_state_dict(model, full, tp_size=1, tp_rank=0):
+    """Copies this rank's shard of an unsharded LlamaTP state dict ``full`` into ``model``
+    (in place, so stacked q/k/v and gate/up buffers stay fused), with the reference's
+    split rule (models.py:386-573): column layers (q, k, v, gate, up, LM head) take chunk
+    ``tp_rank`` of dim 0, row layers (o, down) of dim 1, the rest is copied whole; a
+    pipeline stage's local layer i is global layer ``model.layer_indices[i]``."""
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            src = name
+            if name.startswith("layers."):
+                parts = name.split(".")
+                parts[1] = str(model.layer_indices[int(parts[1])])
+                src = ".".join(parts)
+            elif name == "lm_head.weight":                  # LlamaPP's plain nn.Linear
+                src = "lm_head.lm_head.weight"
+            t = full[src]
+            if tp_size > 1 and any(k in name for k in _COLUMN):
+                t = t.chunk(tp_size, 0)[tp_rank]
+            elif tp_size > 1 and any(k in name for k in _ROW):
+                t = t.chunk(tp_size, 1)[tp_rank]
+            p.data.copy_(t.to(p.device, p.dtype))
+    return model
+
+
 def init_random_(model, seed=0, std=0.02):
     """Random init of the BASELINE configs: manual_seed(seed), normal_(0, std) over
     named_parameters() in order, norm weights kept at 1 (the golden fixture's rule)."""

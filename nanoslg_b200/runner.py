@@ -13,9 +13,11 @@ from types import SimpleNamespace
 
 import torch
 
+import torch.distributed as dist
+
 from . import models
 from .kv_cache import create_cache_manager
-from .parallel import ParallelConfig, ParallelContext, ParallelMode
+from .parallel import ParallelConfig, ParallelContext, ParallelMode, get_layers_for_pp_rank
 
 
 def llama_config(name):
@@ -37,15 +39,31 @@ def llama_config(name):
 
 
 class LlamaRunner:
+    """One rank of a TP, PP or hybrid TP x PP deployment (parallel.py:15-68 layout: rank =
+    pp_rank * tp_size + tp_rank).  With pp_size > 1 each rank holds its stage's layers
+    (get_layers_for_pp_rank) and its stage-local KV cache; a forward runs the stages in
+    turn, each TP rank sending the hidden state to the same TP rank of the next stage
+    (NCCL send/recv, the reference's handoff of worker.py:561-593 / 654-685 without the
+    TP-master funnel: every TP rank already holds the all-reduced hidden), and the last
+    stage broadcasts the greedy tokens to every rank."""
+
     def __init__(self, hf_config, device, dtype=torch.bfloat16, tp_size=1, rank=0,
-                 max_kv_pages=0, page_size=16, prefix_caching=True, seed=0):
+                 max_kv_pages=0, page_size=16, prefix_caching=True, seed=0, pp_size=1):
         self.device = torch.device(device)
         self.dtype = dtype
-        mode = ParallelMode.TENSOR
-        self.pcfg = ParallelConfig(mode, tp_size)
+        world = tp_size * pp_size
+        if pp_size == 1:
+            self.pcfg = ParallelConfig(ParallelMode.TENSOR, world)
+        else:
+            mode = ParallelMode.PIPELINE if tp_size == 1 else ParallelMode.HYBRID
+            self.pcfg = ParallelConfig(mode, world, tp_size=tp_size, pp_size=pp_size)
+            L = hf_config.num_hidden_layers
+            self.pcfg.pp_layer_splits = {r: get_layers_for_pp_rank(L, pp_size, r)
+                                         for r in range(pp_size)}
         ctx = ParallelContext.initialize(self.pcfg, rank, device=self.device)
-        if tp_size > 1:
+        if world > 1:
             ctx.setup_groups()
+        self.pctx = ctx
         self.hf = hf_config
         prev = torch.get_default_dtype()
         torch.set_default_dtype(dtype)
@@ -64,6 +82,30 @@ class LlamaRunner:
         self.seq_ids = []
         self.use_graphs = False
         self._graphs = {}        # batch -> (graph, static tokens in, static tokens out)
+
+    def load_full_state_dict(self, full):
+        """Loads this rank's shard of an unsharded state dict (reference split rule)."""
+        models.load_full_state_dict(self.model, full, self.pcfg.tp_size, self.pctx.tp_rank)
+
+    def _forward_tokens(self, x, ctx, width):
+        """One forward of the whole deployment for this step's cache context; returns the
+        greedy token of every sequence on every rank."""
+        if self.pcfg.pp_size == 1:
+            logits = self.model(x, ctx, last_only=True)
+            return logits[:, -1].argmax(-1)
+        pc = self.pctx
+        B = len(self.seq_ids)
+        if not pc.is_first_pp_stage:
+            x = torch.empty(B, width, self.hf.hidden_size, dtype=self.dtype, device=self.device)
+            dist.recv(x, src=pc.get_pp_prev_rank())
+        out = self.model(x, ctx, last_only=pc.is_last_pp_stage)
+        if pc.is_last_pp_stage:
+            tok = out[:, -1].argmax(-1)
+        else:
+            dist.send(out.contiguous(), dst=pc.get_pp_next_rank())
+            tok = torch.empty(B, dtype=torch.long, device=self.device)
+        dist.broadcast(tok, src=(self.pcfg.pp_size - 1) * self.pcfg.tp_size)
+        return tok
 
     def enable_cuda_graphs(self, batches):
         """Decode steps of these batch sizes run as one captured CUDA graph each: the plan
@@ -93,19 +135,20 @@ class LlamaRunner:
             ids[i, width - n:] = torch.tensor(t[p:p + n])
         self.prefix_lens = prefix
         ctx = mgr.begin_forward(self.seq_ids, counts, offsets)
-        logits = self.model(ids.to(self.device, non_blocking=True), ctx, last_only=True)
+        tok = self._forward_tokens(ids.to(self.device, non_blocking=True), ctx, width)
         mgr.end_forward(ctx)
-        return logits[:, -1].argmax(-1)
+        return tok
 
     @torch.inference_mode()
     def decode_step(self, tokens):
         mgr = self.cache
         B = len(self.seq_ids)
         ctx = mgr.begin_forward(self.seq_ids, [1] * B)
-        if not (self.use_graphs and mgr.static_plan_for(B, 1, 0) is not None):
-            logits = self.model(tokens[:, None], ctx, last_only=True)
+        if not (self.use_graphs and self.pcfg.pp_size == 1
+                and mgr.static_plan_for(B, 1, 0) is not None):
+            tok = self._forward_tokens(tokens[:, None], ctx, 1)
             mgr.end_forward(ctx)
-            return logits[:, -1].argmax(-1)
+            return tok
         entry = self._graphs.get(B)
         if entry is None:
             tok_in = tokens.clone()
