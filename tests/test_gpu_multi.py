@@ -61,7 +61,7 @@ def test_sharded_tiny_llama_matches_reference(tp, pp):
         pytest.skip(f"needs {world} GPUs")
     with open(os.path.join(GOLDEN, "tiny_llama.json")) as f:
         want = json.load(f)["tokens"]
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.start_processes(_rank_main, args=(world, tp, pp, _free_port(), out), nprocs=world,
                            start_method="spawn", join=True)

@@ -62,7 +62,7 @@ def _worker(rank, world, port, out):
 def test_two_rank_tp_layers_and_bookkeeping():
     world = 2
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.start_processes(_worker, args=(world, port, out), nprocs=world, start_method="spawn",
                            join=True)
