@@ -8,7 +8,7 @@ lengths uniform in [512, 8192] (seed 0), page ids a random draw from a 600k-page
 the batch (64 query tokens); the metric is decode tokens/s of that pass.
 
 * ``value``     -- kernel path, inputs resident in HBM: ops.paged_decode (the C ABI
-                   nslg_paged_decode: one split-KV launch), CUDA events on the
+                   nslg_paged_decode: split-KV kernel + merge), CUDA events on the
                    launching stream.  The 1.13 GB of KV read per step is 9x the 126 MB L2,
                    so no L2 flush is needed between steps.
 * ``e2e``       -- the same decode step through the reference-facing API:
@@ -465,7 +465,7 @@ def main():
                          "algorithmic_bytes_per_step": ab,
                          "kernel_ms_mean": mean_ms,
                          "kernel_ms_median": statistics.median(kr["per_ms"])},
-            "gpu_launches": a.steps,
+            "gpu_launches": 2 * a.steps,
             "clocks": kr["clocks"]}
     line["prefill_attention"] = run_prefill_kernel(device) if rank == 0 else None
     if not a.no_model:

@@ -20,17 +20,13 @@
 // loaded yet.
 //
 // Sharing. Every call on a device uses the same array and it keeps whatever the last
-// call left there. The partial results are always written before they are read in the
-// same call; the only state that must start at zero is the block of per-sequence
-// arrival counters at the front of the array, which is zero when the library is loaded
-// (a __device__ array without an initialiser starts zeroed) and which every call puts
-// back to zero before it finishes. Two calls whose kernels overlap on the GPU (for
-// example on two streams without an ordering between them) race on the array and
-// corrupt each other's results; order them.
+// call left there. Nothing in it has to start at zero: the merge step reads only
+// partial results that the decode step of the same call has just written. Two calls
+// whose kernels overlap on the GPU (for example on two streams without an ordering
+// between them) race on the array and corrupt each other's results; order them.
 //
-// Limit. The scratch a call needs is 64 KiB of counters plus
-// (batch + #SMs) * num_qo_heads * (head_dim + 1) * 4 bytes (plus 256 for alignment);
-// calls needing more than 8 MiB are rejected with
+// Limit. The scratch a call needs is (batch + #SMs) * num_qo_heads * (head_dim + 1) * 4
+// bytes (plus 256 for alignment); calls needing more than 8 MiB are rejected with
 // NSLG_ERR_WORKSPACE and a message. Shapes the tensor-core kernel does not cover run the
 // CUDA-core kernel, which needs no scratch. No call allocates or frees device memory.
 #include <cuda_runtime.h>

@@ -9,12 +9,8 @@
 // boundaries; segment (b, c) writes its softmax partial (o, lse) to slot b + c of the
 // workspace (unique: along the flat list either b or c grows by one at each new
 // segment). A sequence lying inside one CTA's slice is finished in place and written
-// straight to `out`. For a sequence split over CTAs cf..cl, each CTA writes its partial,
-// then takes a ticket from the sequence's arrival counter; the CTA drawing the last
-// ticket merges the partials (log-sum-exp) into `out` and puts the counter back to
-// zero. The counters live at offset 0 of the workspace, must be zero before the first
-// call, and every call (timeouts included) leaves them at zero. Sequences without pages
-// are zero-filled by a strided scan at kernel start. One launch per decode.
+// straight to `out`; the others are combined by decode_merge_kernel with a
+// log-sum-exp merge.
 //
 // Data movement. One producer warp issues TMA tile loads (no multicast) of each page:
 // per kv head and per 64-dim half, a [16 tokens x 64 dims] box with 128-byte swizzle,
@@ -44,9 +40,7 @@ constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMinPagesPerCta = 2;
 constexpr int kBoxBytes = kPS * 64 * 2;  // one [16 x 64] bf16 box: 2 KiB
-constexpr int kMaxSmem = 232448 - 64;    // 227 KiB opt-in per CTA on sm_100, less static
-constexpr int kMaxBatch = 16384;         // counters region: kMaxBatch ints at offset 0
-constexpr int64_t kCounterBytes = int64_t{kMaxBatch} * 4;
+constexpr int kMaxSmem = 232448;         // 227 KiB opt-in per CTA on sm_100
 
 struct DecodeParams {
   const __nv_bfloat16* q;
@@ -56,7 +50,6 @@ struct DecodeParams {
   const int32_t* lpl;
   float* part_o;    // [slots, hq, D]
   float* part_lse;  // [slots, hq]
-  int* counters;    // [batch] arrival tickets of split sequences (kept at zero)
   int64_t q_stride, out_stride, num_pages;
   int batch, hq, group, stages, grid;
   float scale_log2;
@@ -109,14 +102,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + stages;
   float* comb = reinterpret_cast<float*>(empty + stages);  // [8 warps][G][D] o, then m, l
 
-  __shared__ int s_last;
-  // sequences without pages produce zeros (strided over all CTAs, before any early exit)
-  for (int bb = blockIdx.x; bb < p.batch; bb += gridDim.x) {
-    if (p.indptr[bb] == p.indptr[bb + 1]) {
-      uint32_t* ob = reinterpret_cast<uint32_t*>(p.out + static_cast<int64_t>(bb) * p.out_stride);
-      for (int i = threadIdx.x; i < p.hq * D / 2; i += blockDim.x) ob[i] = 0u;
-    }
-  }
   const int64_t total = p.indptr[p.batch];
   const int n = num_ctas(total, p.grid);
   const int c = blockIdx.x;
@@ -364,9 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
-    const int cf = cta_of(seq_beg, total, n), cl = cta_of(seq_end - 1, total, n);
-    const bool whole = cf == cl;
     if (j == 0 && ok) {
+      const bool whole = cta_of(seq_beg, total, n) == cta_of(seq_end - 1, total, n);
       const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
       const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
@@ -396,50 +380,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (!whole) {
-      // this CTA's partial of sequence b is written; take an arrival ticket
-      named_barrier_sync(1, kConsumerWarps * 32);
-      if (threadIdx.x == 0) {
-        __threadfence();
-        const int old = atomicAdd(&p.counters[b], 1);
-        s_last = old == cl - cf;
-      }
-      named_barrier_sync(1, kConsumerWarps * 32);
-      if (s_last) {
-        // last arrival: all partials of b are visible; merge them into out
-        __threadfence();
-        constexpr int DV = D / 32;
-        for (int hq = warp; hq < p.hq; hq += kConsumerWarps) {
-          float mx = -INFINITY;
-          for (int cc = cf; cc <= cl; ++cc)
-            mx = fmaxf(mx, __ldcg(p.part_lse + (static_cast<int64_t>(b) + cc) * p.hq + hq));
-          float acc[DV];
-#pragma unroll
-          for (int e = 0; e < DV; ++e) acc[e] = 0.f;
-          float wsum = 0.f;
-          for (int cc = cf; cc <= cl; ++cc) {
-            const int64_t slot = static_cast<int64_t>(b) + cc;
-            const float lse = __ldcg(p.part_lse + slot * p.hq + hq);
-            const float w = lse == -INFINITY ? 0.f : fast_exp2(lse - mx);
-            wsum += w;
-            const float* po = p.part_o + (slot * p.hq + hq) * D + lane * DV;
-#pragma unroll
-            for (int e = 0; e < DV; ++e) acc[e] = fmaf(w, __ldcg(po + e), acc[e]);
-          }
-          const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-          __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride +
-                              static_cast<int64_t>(hq) * D + lane * DV;
-#pragma unroll
-          for (int e = 0; e < DV; e += 2)
-            *reinterpret_cast<uint32_t*>(ob + e) = pack_bf16x2(acc[e] * inv, acc[e + 1] * inv);
-        }
-        if (threadIdx.x == 0) p.counters[b] = 0;   // ready for the next call
-      }
-    }
     if constexpr (C::kPPS > 1) named_barrier_sync(1, kConsumerWarps * 32);
     ++b;
     while (b < p.batch && p.indptr[b + 1] <= pp) ++b;
   }
+}
+
+// Combines the partials of sequences that span several CTAs; one warp per
+// (sequence, query head). Sequences finished in place by the decode kernel, and
+// sequences without pages (written as zeros here), need no merge.
+template <int D>
+__global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int hq = blockIdx.x * 4 + warp;
+  const int b = blockIdx.y;
+  if (hq >= p.hq) return;
+  constexpr int DV = D / 32;
+  __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
+  const int64_t total = p.indptr[p.batch];
+  const int64_t beg = p.indptr[b], end = p.indptr[b + 1];
+  if (beg == end) {
+#pragma unroll
+    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const int n = num_ctas(total, p.grid);
+  const int cf = cta_of(beg, total, n), cl = cta_of(end - 1, total, n);
+  if (cf == cl) return;
+  float mx = -INFINITY;
+  for (int c = cf; c <= cl; ++c) mx = fmaxf(mx, p.part_lse[(static_cast<int64_t>(b) + c) * p.hq + hq]);
+  float acc[DV];
+#pragma unroll
+  for (int e = 0; e < DV; ++e) acc[e] = 0.f;
+  float wsum = 0.f;
+  for (int c = cf; c <= cl; ++c) {
+    const int64_t slot = static_cast<int64_t>(b) + c;
+    const float lse = p.part_lse[slot * p.hq + hq];
+    const float w = lse == -INFINITY ? 0.f : fast_exp2(lse - mx);
+    wsum += w;
+    const float* po = p.part_o + (slot * p.hq + hq) * D + lane * DV;
+#pragma unroll
+    for (int e = 0; e < DV; ++e) acc[e] = fmaf(w, po[e], acc[e]);
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+  for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(acc[e] * inv);
 }
 
 // ------------------------------------------------------------------ host side
@@ -459,7 +444,11 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
   kern<<<p.grid, kThreads, smem, stream>>>(tk, tv, p);
-  return check_launch("decode_tc");
+  int rc = check_launch("decode_tc");
+  if (rc != NSLG_OK) return rc;
+  dim3 mgrid((p.hq + 3) / 4, p.batch);
+  decode_merge_kernel<D><<<mgrid, 128, 0, stream>>>(p);
+  return check_launch("decode_merge");
 }
 
 }  // namespace
@@ -471,7 +460,7 @@ bool decode_tc_supported(int dtype, int hq, int hkv, int d, int page_size) {
 
 int64_t decode_tc_workspace_bytes(int batch, int hq, int d) {
   const int64_t slots = static_cast<int64_t>(batch) + sm_count();
-  return kCounterBytes + slots * hq * (static_cast<int64_t>(d) + 1) * 4 + 256;
+  return slots * hq * (static_cast<int64_t>(d) + 1) * 4 + 256;
 }
 
 int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int64_t q_stride,
@@ -486,10 +475,6 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
     return set_error(NSLG_ERR_WORKSPACE, "decode workspace needs " + std::to_string(need) + " bytes");
   if (num_pages * kPS > (int64_t{1} << 31))
     return set_error(NSLG_ERR_UNSUPPORTED, "decode: pool larger than 2^31 token rows");
-  if (batch > kMaxBatch)
-    return set_error(NSLG_ERR_UNSUPPORTED, "decode: more than 16384 sequences per call");
-  if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
-    return set_error(NSLG_ERR_ARG, "decode: workspace must be 16-byte aligned");
   CUtensorMap tk, tv;
   int rc = pool_tensor_map(pool_k, num_pages, hkv, d, &tk);
   if (rc != NSLG_OK) return rc;
@@ -497,8 +482,7 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
   if (rc != NSLG_OK) return rc;
   const int grid = sm_count();
   const int64_t slots = static_cast<int64_t>(batch) + grid;
-  uintptr_t ws = reinterpret_cast<uintptr_t>(workspace) + kCounterBytes;
-  ws = (ws + 255) & ~static_cast<uintptr_t>(255);
+  uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
   DecodeParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.out = static_cast<__nv_bfloat16*>(out);
@@ -507,7 +491,6 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
   p.lpl = kv_last_page_len;
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_lse = p.part_o + slots * hq * d;
-  p.counters = static_cast<int*>(workspace);
   p.q_stride = q_stride;
   p.out_stride = out_stride;
   p.num_pages = num_pages;

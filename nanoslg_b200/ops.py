@@ -67,8 +67,7 @@ class _DeviceState:
         with self.lock:
             buf = self.ws.get(device)
             if buf is None or buf.numel() < nbytes:
-                # zero-filled: the decode kernel's arrival counters must start at zero
-                buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
                 self.ws[device] = buf
             return buf
 
