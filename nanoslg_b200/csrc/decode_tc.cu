@@ -29,6 +29,8 @@
 // the end of each segment.
 #include <cuda.h>
 
+#include <string>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -110,6 +112,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t p1 = total * (c + 1) / n;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // let the merge kernel (launched with programmatic stream serialisation) be scheduled
+  // as SMs free up; it waits for this grid's completion before reading any partial
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -394,11 +399,13 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int hq = blockIdx.x * 4 + warp;
   const int b = blockIdx.y;
-  if (hq >= p.hq) return;
   constexpr int DV = D / 32;
-  __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
+  // the CSR is an input of both kernels: read it before waiting for the decode grid
   const int64_t total = p.indptr[p.batch];
   const int64_t beg = p.indptr[b], end = p.indptr[b + 1];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (hq >= p.hq) return;
+  __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
   if (beg == end) {
 #pragma unroll
     for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(0.f);
@@ -446,8 +453,21 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
   kern<<<p.grid, kThreads, smem, stream>>>(tk, tv, p);
   int rc = check_launch("decode_tc");
   if (rc != NSLG_OK) return rc;
-  dim3 mgrid((p.hq + 3) / 4, p.batch);
-  decode_merge_kernel<D><<<mgrid, 128, 0, stream>>>(p);
+  // programmatic dependent launch: the merge grid is launched while the decode grid
+  // drains and starts its work once the decode grid has completed
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.hq + 3) / 4, p.batch);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, decode_merge_kernel<D>, p);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("decode_merge: ") +
+                                                              cudaGetErrorString(err));
   return check_launch("decode_merge");
 }
 
