@@ -29,6 +29,7 @@
 // the end of each segment.
 #include <cuda.h>
 
+#include <atomic>
 #include <string>
 
 #include "common.cuh"
@@ -54,6 +55,7 @@ struct DecodeParams {
   float* part_lse;  // [slots, hq]
   int64_t q_stride, out_stride, num_pages;
   int batch, hq, group, stages, grid;
+  int box_all_heads;  // tensor maps with a [64 dim x 16 tok x HKV head] box (token-major)
   float scale_log2;
   uint32_t* status;
 };
@@ -133,43 +135,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     uint32_t armed[4] = {0u, 0u, 0u, 0u};  // arms of each stage's full barrier
+    // Stages in order: (first flat page, page count) over the segments of this CTA's
+    // slice. The page ids of the next stage are loaded one stage ahead so their latency
+    // overlaps the wait for a free stage.
     int b = seq_of(p.indptr, p.batch, p0);
-    for (int64_t pp = p0; pp < p1;) {
-      const int64_t seg_end = min(p1, static_cast<int64_t>(p.indptr[b + 1]));
-      for (int64_t q0 = pp; q0 < seg_end; q0 += C::kPPS) {
-        const int np = static_cast<int>(min(static_cast<int64_t>(C::kPPS), seg_end - q0));
-        if (!mbar_wait(&empty[stage], phase ^ 1)) {
-          report(p.status, NSLG_DEV_WAIT_TIMEOUT);
-          // The consumers stopped releasing stages. Issue nothing more, wait (bounded)
-          // for the loads already in flight, and leave.
-          for (int s = 0; s < stages; ++s)
-            if (armed[s] > 0) (void)mbar_wait(&full[s], (armed[s] - 1) & 1);
-          return;
-        }
-        mbar_arrive_expect_tx(&full[stage], np * 2 * C::kHalves * HKV * kBoxBytes);
-        ++armed[stage];
-        uint8_t* sb = smem + stage * C::kStageBytes;
-        for (int j = 0; j < np; ++j) {
-          int pid = p.indices[q0 + j];
-          if (pid < 0 || pid >= p.num_pages) {
-            report(p.status, NSLG_DEV_BAD_PAGE);
-            pid = 0;  // keep the transaction count; page 0 is the pool's null page
-          }
+    int64_t seg_end = min(p1, static_cast<int64_t>(p.indptr[b + 1]));
+    int64_t cursor = p0;
+    auto next_stage = [&](int64_t& q0, int& np) -> bool {
+      if (cursor >= p1) return false;
+      if (cursor >= seg_end) {
+        ++b;
+        while (b < p.batch && p.indptr[b + 1] <= cursor) ++b;
+        seg_end = min(p1, static_cast<int64_t>(p.indptr[b + 1]));
+      }
+      q0 = cursor;
+      np = static_cast<int>(min(static_cast<int64_t>(C::kPPS), seg_end - cursor));
+      cursor += np;
+      return true;
+    };
+    int ids[C::kPPS];
+    int64_t q0 = 0;
+    int np = 0;
+    bool have = next_stage(q0, np);
 #pragma unroll
-          for (int half = 0; half < C::kHalves; ++half)
+    for (int jj = 0; jj < C::kPPS; ++jj) ids[jj] = (have && jj < np) ? p.indices[q0 + jj] : 0;
+    while (have) {
+      int64_t nq0 = 0;
+      int nnp = 0;
+      const bool nhave = next_stage(nq0, nnp);
+      int nids[C::kPPS];
+#pragma unroll
+      for (int jj = 0; jj < C::kPPS; ++jj) nids[jj] = (nhave && jj < nnp) ? p.indices[nq0 + jj] : 0;
+      if (!mbar_wait(&empty[stage], phase ^ 1)) {
+        report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+        // The consumers stopped releasing stages. Issue nothing more, wait (bounded)
+        // for the loads already in flight, and leave.
+        for (int s = 0; s < stages; ++s)
+          if (armed[s] > 0) (void)mbar_wait(&full[s], (armed[s] - 1) & 1);
+        return;
+      }
+      mbar_arrive_expect_tx(&full[stage], np * 2 * C::kHalves * HKV * kBoxBytes);
+      ++armed[stage];
+      uint8_t* sb = smem + stage * C::kStageBytes;
+#pragma unroll
+      for (int jj = 0; jj < C::kPPS; ++jj) {
+        if (jj >= np) break;
+        int pid = ids[jj];
+        if (pid < 0 || pid >= p.num_pages) {
+          report(p.status, NSLG_DEV_BAD_PAGE);
+          pid = 0;  // keep the transaction count; page 0 is the pool's null page
+        }
+#pragma unroll
+        for (int half = 0; half < C::kHalves; ++half) {
+          if (p.box_all_heads) {
+            // one box covers every kv head of the page half (token-major map)
+            tma_load_3d(sb + C::box(jj, 0, half, 0), &tmap_k, &full[stage], half * 64,
+                        pid * kPS, 0, policy);
+            tma_load_3d(sb + C::box(jj, 1, half, 0), &tmap_v, &full[stage], half * 64,
+                        pid * kPS, 0, policy);
+          } else {
 #pragma unroll
             for (int h = 0; h < HKV; ++h) {
-              tma_load_3d(sb + C::box(j, 0, half, h), &tmap_k, &full[stage], half * 64, h,
+              tma_load_3d(sb + C::box(jj, 0, half, h), &tmap_k, &full[stage], half * 64, h,
                           pid * kPS, policy);
-              tma_load_3d(sb + C::box(j, 1, half, h), &tmap_v, &full[stage], half * 64, h,
+              tma_load_3d(sb + C::box(jj, 1, half, h), &tmap_v, &full[stage], half * 64, h,
                           pid * kPS, policy);
             }
+          }
         }
-        if (++stage == stages) { stage = 0; phase ^= 1; }
       }
-      pp = seg_end;
-      ++b;
-      while (b < p.batch && p.indptr[b + 1] <= pp) ++b;
+      if (++stage == stages) { stage = 0; phase ^= 1; }
+      have = nhave;
+      q0 = nq0;
+      np = nnp;
+#pragma unroll
+      for (int jj = 0; jj < C::kPPS; ++jj) ids[jj] = nids[jj];
     }
     return;
   }
@@ -496,10 +536,24 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
   if (num_pages * kPS > (int64_t{1} << 31))
     return set_error(NSLG_ERR_UNSUPPORTED, "decode: pool larger than 2^31 token rows");
   CUtensorMap tk, tv;
-  int rc = pool_tensor_map(pool_k, num_pages, hkv, d, &tk);
-  if (rc != NSLG_OK) return rc;
-  rc = pool_tensor_map(pool_v, num_pages, hkv, d, &tv);
-  if (rc != NSLG_OK) return rc;
+  // -1 unknown, 1 the driver takes the token-major all-heads map, 0 it does not
+  static std::atomic<int> all_heads_ok{-1};
+  int box_all = all_heads_ok.load(std::memory_order_relaxed) != 0 ? 1 : 0;
+  int rc = NSLG_ERR_UNSUPPORTED;
+  if (box_all) {
+    rc = pool_tensor_map_all_heads(pool_k, num_pages, hkv, d, &tk);
+    if (rc == NSLG_OK) rc = pool_tensor_map_all_heads(pool_v, num_pages, hkv, d, &tv);
+    if (all_heads_ok.load(std::memory_order_relaxed) < 0)
+      all_heads_ok.store(rc == NSLG_OK ? 1 : 0, std::memory_order_relaxed);
+  }
+  if (rc != NSLG_OK) {
+    // the driver did not take the token-major strides: one box per kv head instead
+    box_all = 0;
+    rc = pool_tensor_map(pool_k, num_pages, hkv, d, &tk);
+    if (rc != NSLG_OK) return rc;
+    rc = pool_tensor_map(pool_v, num_pages, hkv, d, &tv);
+    if (rc != NSLG_OK) return rc;
+  }
   const int grid = sm_count();
   const int64_t slots = static_cast<int64_t>(batch) + grid;
   uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
@@ -520,6 +574,7 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
   p.grid = grid;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.status = status;
+  p.box_all_heads = box_all;
   if (d == 128) {
     switch (hkv) {
       case 1: return launch_typed<1, 128>(tk, tv, p, stream);

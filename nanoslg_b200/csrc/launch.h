@@ -27,6 +27,9 @@ int encode_tiled_3d_bf16(CUtensorMap* out, const void* base, uint64_t d0, uint64
 
 // Cached map of one pool layer [pages, 16, hkv, d] with a [16 tok x 1 head x 64 dim] box.
 int pool_tensor_map(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out);
+// Same pool with a [16 tok x hkv heads x 64 dim] box landing as [head][token][64] in smem
+// (dims listed token-major); fails if the driver rejects the stride order.
+int pool_tensor_map_all_heads(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out);
 
 int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, const void* q,
                           int64_t q_stride, const void* k, int64_t k_stride, const void* v,

@@ -37,6 +37,7 @@ struct MapEntry {
   const void* ptr = nullptr;
   int64_t pages = 0;
   int hkv = 0, d = 0;
+  int all_heads = 0;
   CUtensorMap map;
 };
 constexpr int kMapCache = 512;
@@ -64,31 +65,45 @@ int encode_tiled_3d_bf16(CUtensorMap* out, const void* base, uint64_t d0, uint64
   return NSLG_OK;
 }
 
-int pool_tensor_map(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out) {
+int cached_pool_map(const void* pool, int64_t pages, int hkv, int d, int all_heads,
+                    CUtensorMap* out) {
   std::lock_guard<std::mutex> lock(g_map_mu);
   for (int i = 0; i < kMapCache; ++i) {
     const MapEntry& e = g_maps[i];
-    if (e.ptr == pool && e.pages == pages && e.hkv == hkv && e.d == d) {
+    if (e.ptr == pool && e.pages == pages && e.hkv == hkv && e.d == d &&
+        e.all_heads == all_heads) {
       *out = e.map;
       return NSLG_OK;
     }
   }
-  // dims (innermost first): head_dim, kv head, token row (= page * 16 + slot);
-  // box: 64 dims x 1 head x 16 tokens (one page of one head, half the head row)
   MapEntry& e = g_maps[g_map_next];
   e.ptr = nullptr;
-  const int rc = encode_tiled_3d_bf16(&e.map, pool, static_cast<uint64_t>(d),
-                                      static_cast<uint64_t>(hkv), static_cast<uint64_t>(pages) * 16,
-                                      static_cast<uint64_t>(d) * 2,
-                                      static_cast<uint64_t>(hkv) * d * 2, 64, 1, 16);
+  const uint64_t tok = static_cast<uint64_t>(pages) * 16;
+  const uint64_t tok_stride = static_cast<uint64_t>(hkv) * d * 2, head_stride = static_cast<uint64_t>(d) * 2;
+  const int rc =
+      all_heads
+          // dims: head_dim, token row, kv head (token stride listed before the smaller head
+          // stride); box 64 dims x 16 tokens x all heads -> smem [head][token][64 dims]
+          ? encode_tiled_3d_bf16(&e.map, pool, d, tok, hkv, tok_stride, head_stride, 64, 16, hkv)
+          // dims: head_dim, kv head, token row; box 64 dims x 1 head x 16 tokens
+          : encode_tiled_3d_bf16(&e.map, pool, d, hkv, tok, head_stride, tok_stride, 64, 1, 16);
   if (rc != NSLG_OK) return rc;
   e.ptr = pool;
   e.pages = pages;
   e.hkv = hkv;
   e.d = d;
+  e.all_heads = all_heads;
   *out = e.map;
   g_map_next = (g_map_next + 1) % kMapCache;
   return NSLG_OK;
+}
+
+int pool_tensor_map(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out) {
+  return cached_pool_map(pool, pages, hkv, d, 0, out);
+}
+
+int pool_tensor_map_all_heads(const void* pool, int64_t pages, int hkv, int d, CUtensorMap* out) {
+  return cached_pool_map(pool, pages, hkv, d, 1, out);
 }
 
 }  // namespace nslg
