@@ -362,7 +362,7 @@ def main():
                          "batch (still 1.13 GB of KV per step)")
     ap.add_argument("--no-model", action="store_true", help="skip the Llama-3.1-8B decode leg")
     ap.add_argument("--model-steps", type=int, default=32)
-    ap.add_argument("--only", choices=["all", "kernel", "model"], default="all",
+    ap.add_argument("--only", choices=["all", "kernel", "model", "prefill"], default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg")
     a = ap.parse_args()
@@ -411,6 +411,13 @@ def main():
     if not os.path.exists(nbuild.LIB):
         nbuild.build()
 
+    if a.only == "prefill":
+        if rank == 0:
+            print(json.dumps({"case": "prefill only", "prefill_attention":
+                              run_prefill_kernel(device)}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
     if a.only == "model":
         runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4)
         runner.close()

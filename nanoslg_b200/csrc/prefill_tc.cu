@@ -223,8 +223,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_load_3d(sq, &tmap_q, q_full, 0, h * G, row0, keep);
       tma_load_3d(sq + kQHalf, &tmap_q, q_full, 64, h * G, row0, keep);
       int issued = 0;
+      // page ids of a tile are fetched together, one tile ahead of their TMA loads
+      auto fetch_ids = [&](int j, int (&ids)[kPagesPerTile]) {
+#pragma unroll
+        for (int pg = 0; pg < kPagesPerTile; ++pg) {
+          const int pi = j * kPagesPerTile + pg;
+          ids[pg] = (j < ntiles && pi < npages) ? p.indices[kv_beg + pi] : -1;
+        }
+      };
+      int ids[kPagesPerTile];
+      fetch_ids(0, ids);
       for (int j = 0; j < ntiles; ++j) {
         const int s = j & 1;
+        int next_ids[kPagesPerTile];
+        fetch_ids(j + 1, next_ids);
         if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1)) {
           report(p.status, NSLG_DEV_WAIT_TIMEOUT);
           *abort_flag = 1;
@@ -234,11 +246,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
         uint8_t* kt = skv + s * kStageBytes;
         uint8_t* vt = kt + kKVTile;
+#pragma unroll
         for (int pg = 0; pg < kPagesPerTile; ++pg) {
           const int pi = j * kPagesPerTile + pg;
           int tok_row = static_cast<int>(p.num_pages) * kPS;  // outside the pool: zero fill
           if (pi < npages) {
-            const int pid = p.indices[kv_beg + pi];
+            const int pid = ids[pg];
             if (pid >= 0 && pid < p.num_pages) tok_row = pid * kPS;
             else report(p.status, NSLG_DEV_BAD_PAGE);
           }
@@ -250,6 +263,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                         tok_row, keep);
           }
         }
+#pragma unroll
+        for (int pg = 0; pg < kPagesPerTile; ++pg) ids[pg] = next_ids[pg];
       }
       if (*abort_flag) {
         // no load may still be writing shared memory when the CTA leaves (bounded waits)
