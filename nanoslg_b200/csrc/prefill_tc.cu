@@ -22,6 +22,9 @@
 // TMEM: S 64 columns, P 32, O 128 -> 256 allocated, two CTAs per SM.
 // The MMA warp issues S(j+1) before PV(j), so the softmax of tile j+1 overlaps PV(j).
 //
+// Persistent grid of 2 CTAs per SM walking the (query tile, sequence, kv head) items,
+// longest causal spans first; TMEM, barriers and the TMA pipeline carry across items.
+//
 // Every mbarrier wait is bounded (2 s); on a timeout the kernel records
 // NSLG_DEV_WAIT_TIMEOUT, stops issuing work, drains what it issued (bounded), frees its
 // TMEM and returns.
@@ -60,7 +63,7 @@ struct PrefillParams {
   const int32_t* indices;
   const int32_t* lpl;
   int64_t out_stride, num_pages;
-  int batch, hq, hkv, group, tokens_per_tile, causal;
+  int batch, hq, hkv, group, tokens_per_tile, causal, n_items;
   float scale_log2;
   uint32_t* status;
 };
@@ -146,30 +149,48 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ----------------------------------------------------------------- work items
+// Item = (query tile, sequence, kv head), ordered with the query tiles that sit latest in
+// their sequences -- the longest causal spans -- first; CTA c takes items c, c + grid, ...
+struct Item {
+  int b, h, i0, qo_len, kv_beg, npages, kv_len, ntiles, row0;
+};
+
+__device__ __forceinline__ bool load_item(const PrefillParams& p, int item, Item& it) {
+  const int per = p.batch * p.hkv;
+  const int tq_rev = item / per;
+  const int rem = item - tq_rev * per;
+  it.b = rem / p.hkv;
+  it.h = rem - it.b * p.hkv;
+  it.qo_len = p.qo_indptr[it.b + 1] - p.qo_indptr[it.b];
+  const int ntile_q = (it.qo_len + p.tokens_per_tile - 1) / p.tokens_per_tile;
+  const int tq = ntile_q - 1 - tq_rev;
+  if (tq < 0) return false;
+  it.i0 = tq * p.tokens_per_tile;
+  it.kv_beg = p.indptr[it.b];
+  it.npages = p.indptr[it.b + 1] - it.kv_beg;
+  it.kv_len = it.npages > 0 ? (it.npages - 1) * kPS + p.lpl[it.b] : 0;
+  const int last_tok = min(it.i0 + p.tokens_per_tile, it.qo_len) - 1;
+  const int last_qpos = it.kv_len - it.qo_len + last_tok;
+  const int kv_span = p.causal ? min(it.kv_len, last_qpos + 1) : it.kv_len;
+  it.ntiles = (kv_span + kBN - 1) / kBN;
+  if (it.ntiles <= 0) return false;
+  it.row0 = (p.q_row_start ? p.q_row_start[it.b] : p.qo_indptr[it.b]) + it.i0;
+  return true;
+}
+
 // ----------------------------------------------------------------- the kernel
+// Persistent: each CTA walks its items with one TMEM allocation and one set of barriers.
+// A global tile counter t (over all items of the CTA) drives the barrier phases, so the
+// producer streams Q and K/V of the next item while the current one is still computing.
+// q_empty (MMA commit after an item's last S MMA) frees the single Q buffer, o_free (the
+// softmax warpgroup after reading O in an item's epilogue) frees the O accumulator for
+// the next item's first P.V MMA.
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v, const PrefillParams p) {
-  // longest tiles first: blockIdx.x counts query tiles from the end of the sequence
-  const int b = blockIdx.y;
-  const int h = blockIdx.z;
-  const int qo_len = p.qo_indptr[b + 1] - p.qo_indptr[b];
-  const int ntile_q = (qo_len + p.tokens_per_tile - 1) / p.tokens_per_tile;
-  const int tq = ntile_q - 1 - static_cast<int>(blockIdx.x);
-  if (tq < 0) return;
-  const int i0 = tq * p.tokens_per_tile;
-  const int kv_beg = p.indptr[b];
-  const int npages = p.indptr[b + 1] - kv_beg;
-  const int kv_len = npages > 0 ? (npages - 1) * kPS + p.lpl[b] : 0;
-  const int last_tok = min(i0 + p.tokens_per_tile, qo_len) - 1;
-  const int last_qpos = kv_len - qo_len + last_tok;
-  const int kv_span = p.causal ? min(kv_len, last_qpos + 1) : kv_len;
-  const int ntiles = (kv_span + kBN - 1) / kBN;
-  if (ntiles <= 0) return;
-  const int row0 = (p.q_row_start ? p.q_row_start[b] : p.qo_indptr[b]) + i0;
   const int G = p.group;
-
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -183,12 +204,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* p_full = bars + 6;
   uint64_t* pv_done = bars + 7;
   uint64_t* mma_drain = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 10);
+  uint64_t* q_empty = bars + 9;
+  uint64_t* o_free = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 12);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -196,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(s_full, 1);
     mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
+    mbar_init(o_free, 128);
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -219,58 +244,62 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tmap_k);
       prefetch_tmap(&tmap_v);
       const uint64_t keep = l2_policy_evict_last();
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      tma_load_3d(sq, &tmap_q, q_full, 0, h * G, row0, keep);
-      tma_load_3d(sq + kQHalf, &tmap_q, q_full, 64, h * G, row0, keep);
-      int issued = 0;
-      // page ids of a tile are fetched together, one tile ahead of their TMA loads
-      auto fetch_ids = [&](int j, int (&ids)[kPagesPerTile]) {
+      int t = 0, n_it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        Item it;
+        if (!load_item(p, item, it)) continue;
+        if (n_it > 0 && (*abort_flag || !mbar_wait(q_empty, (n_it - 1) & 1))) { ok = false; break; }
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        tma_load_3d(sq, &tmap_q, q_full, 0, it.h * G, it.row0, keep);
+        tma_load_3d(sq + kQHalf, &tmap_q, q_full, 64, it.h * G, it.row0, keep);
+        ++n_it;
+        // page ids of a tile are fetched together, one tile ahead of their TMA loads
+        auto fetch_ids = [&](int j, int (&ids)[kPagesPerTile]) {
 #pragma unroll
-        for (int pg = 0; pg < kPagesPerTile; ++pg) {
-          const int pi = j * kPagesPerTile + pg;
-          ids[pg] = (j < ntiles && pi < npages) ? p.indices[kv_beg + pi] : -1;
-        }
-      };
-      int ids[kPagesPerTile];
-      fetch_ids(0, ids);
-      for (int j = 0; j < ntiles; ++j) {
-        const int s = j & 1;
-        int next_ids[kPagesPerTile];
-        fetch_ids(j + 1, next_ids);
-        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1)) {
-          report(p.status, NSLG_DEV_WAIT_TIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
-        issued = j + 1;
-        mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
-        uint8_t* kt = skv + s * kStageBytes;
-        uint8_t* vt = kt + kKVTile;
+          for (int pg = 0; pg < kPagesPerTile; ++pg) {
+            const int pi = j * kPagesPerTile + pg;
+            ids[pg] = (j < it.ntiles && pi < it.npages) ? p.indices[it.kv_beg + pi] : -1;
+          }
+        };
+        int ids[kPagesPerTile];
+        fetch_ids(0, ids);
+        for (int j = 0; j < it.ntiles; ++j, ++t) {
+          const int s = t & 1;
+          int next_ids[kPagesPerTile];
+          fetch_ids(j + 1, next_ids);
+          if (*abort_flag || !mbar_wait(&kv_empty[s], ((t >> 1) & 1) ^ 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
+          uint8_t* kt = skv + s * kStageBytes;
+          uint8_t* vt = kt + kKVTile;
 #pragma unroll
-        for (int pg = 0; pg < kPagesPerTile; ++pg) {
-          const int pi = j * kPagesPerTile + pg;
-          int tok_row = static_cast<int>(p.num_pages) * kPS;  // outside the pool: zero fill
-          if (pi < npages) {
-            const int pid = ids[pg];
-            if (pid >= 0 && pid < p.num_pages) tok_row = pid * kPS;
-            else report(p.status, NSLG_DEV_BAD_PAGE);
+          for (int pg = 0; pg < kPagesPerTile; ++pg) {
+            const int pi = j * kPagesPerTile + pg;
+            int tok_row = static_cast<int>(p.num_pages) * kPS;  // outside the pool: zeros
+            if (pi < it.npages) {
+              const int pid = ids[pg];
+              if (pid >= 0 && pid < p.num_pages) tok_row = pid * kPS;
+              else report(p.status, NSLG_DEV_BAD_PAGE);
+            }
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              tma_load_3d(kt + half * kKVHalf + pg * kPS * 128, &tmap_k, &kv_full[s], half * 64,
+                          it.h, tok_row, keep);
+              tma_load_3d(vt + half * kKVHalf + pg * kPS * 128, &tmap_v, &kv_full[s], half * 64,
+                          it.h, tok_row, keep);
+            }
           }
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tma_load_3d(kt + half * kKVHalf + pg * kPS * 128, &tmap_k, &kv_full[s], half * 64, h,
-                        tok_row, keep);
-            tma_load_3d(vt + half * kKVHalf + pg * kPS * 128, &tmap_v, &kv_full[s], half * 64, h,
-                        tok_row, keep);
-          }
+          for (int pg = 0; pg < kPagesPerTile; ++pg) ids[pg] = next_ids[pg];
         }
-#pragma unroll
-        for (int pg = 0; pg < kPagesPerTile; ++pg) ids[pg] = next_ids[pg];
       }
-      if (*abort_flag) {
+      if (!ok) {
+        report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+        *abort_flag = 1;
         // no load may still be writing shared memory when the CTA leaves (bounded waits)
-        (void)mbar_wait(q_full, 0);
-        for (int t = issued - 2 < 0 ? 0 : issued - 2; t < issued; ++t)
-          (void)mbar_wait(&kv_full[t & 1], (t >> 1) & 1);
+        if (n_it > 0) (void)mbar_wait(q_full, (n_it - 1) & 1);
+        for (int u = t - 2 < 0 ? 0 : t - 2; u < t; ++u)
+          (void)mbar_wait(&kv_full[u & 1], (u >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -279,9 +308,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t kIdescS = idesc_bf16(kBN, false);
       constexpr uint32_t kIdescO = idesc_bf16(kD, true);
       const uint32_t q_base = smem_u32(sq);
-      bool ok = mbar_wait(q_full, 0);
-      auto issue_s = [&](int j) {
-        const uint32_t k_base = smem_u32(skv + (j & 1) * kStageBytes);
+      auto issue_s = [&](int t) {
+        const uint32_t k_base = smem_u32(skv + (t & 1) * kStageBytes);
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
           const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
@@ -291,21 +319,44 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         mma_commit(s_full);
       };
-      if (ok && (ok = mbar_wait(&kv_full[0], 0))) issue_s(0);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        if (!(ok = mbar_wait(p_full, j & 1))) break;
+      int t = 0, n_it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        Item it;
+        if (!load_item(p, item, it)) continue;
+        if (*abort_flag || !mbar_wait(q_full, n_it & 1)) { ok = false; break; }
         tc_fence_after();
-        if (j + 1 < ntiles) {
-          if (!(ok = mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
-          issue_s(j + 1);
-        }
-        const uint32_t v_base = smem_u32(skv + (j & 1) * kStageBytes + kKVTile);
+        for (int j = 0; j < it.ntiles; ++j, ++t) {
+          // q_empty is committed right after an item's last S MMA: Q is free once it is done
+          if (j == 0) {
+            if (!(ok = mbar_wait(&kv_full[t & 1], (t >> 1) & 1))) break;
+            tc_fence_after();
+            issue_s(t);
+            if (it.ntiles == 1) mma_commit(q_empty);
+          }
+          if (!(ok = mbar_wait(p_full, t & 1))) break;
+          tc_fence_after();
+          if (j + 1 < it.ntiles) {
+            if (!(ok = mbar_wait(&kv_full[(t + 1) & 1], ((t + 1) >> 1) & 1))) break;
+            tc_fence_after();
+            issue_s(t + 1);
+            if (j + 2 == it.ntiles) mma_commit(q_empty);
+          }
+          if (j == 0 && n_it > 0) {
+            if (!(ok = mbar_wait(o_free, (n_it - 1) & 1))) break;
+            tc_fence_after();
+          }
+          const uint32_t v_base = smem_u32(skv + (t & 1) * kStageBytes + kKVTile);
 #pragma unroll
-        for (int kt = 0; kt < kBN / 16; ++kt)
-          mma_ts(tmem + kColO, tmem + kColP + kt * 8, smem_desc(v_base + kt * 2048, kKVHalf, 1024),
-                 kIdescO, (j > 0 || kt > 0) ? 1u : 0u);
-        mma_commit(pv_done);
-        mma_commit(&kv_empty[j & 1]);
+          for (int kt = 0; kt < kBN / 16; ++kt)
+            mma_ts(tmem + kColO, tmem + kColP + kt * 8,
+                   smem_desc(v_base + kt * 2048, kKVHalf, 1024), kIdescO,
+                   (j > 0 || kt > 0) ? 1u : 0u);
+          mma_commit(pv_done);
+          mma_commit(&kv_empty[t & 1]);
+          if (*abort_flag) { ok = false; break; }
+        }
+        ++n_it;
       }
       if (!ok) {
         report(p.status, NSLG_DEV_WAIT_TIMEOUT);
@@ -320,89 +371,99 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int quarter = warp & 3;              // TMEM lanes 32*quarter .. +31
     const int r = quarter * 32 + lane;         // row = TMEM lane
     const int tok = r / G, g = r % G;
-    const bool row_valid = (i0 + tok) < qo_len && r < G * p.tokens_per_tile;
-    const int qpos = kv_len - qo_len + i0 + tok;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const float sl = p.scale_log2;
-    float m_ref = -INFINITY, l = 0.f;
+    int t = 0;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1))) { ok = false; break; }
-      tc_fence_after();
-      float s[2][32];
-      tmem_ld32(lane_base + kColS, s[0]);
-      tmem_ld32(lane_base + kColS + 32, s[1]);
-      tmem_wait_ld();
-      const int kbase = j * kBN;
-      float mt = -INFINITY;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int kpos = kbase + hh * 32 + c;
-          const bool vis = row_valid && kpos < kv_len && (!p.causal || kpos <= qpos);
-          s[hh][c] = vis ? s[hh][c] * sl : -INFINITY;
-          mt = fmaxf(mt, s[hh][c]);
-        }
-      const float m_new = fmaxf(m_ref, mt);
-      const bool rescale = m_new > m_ref + 8.0f;   // also true on the first finite max
-      const float alpha = (rescale && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
-      if (rescale) m_ref = m_new;
-      float rs = 0.f;
-      uint32_t pk[32];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float p0 = m_ref == -INFINITY ? 0.f : fast_exp2(s[hh][c] - m_ref);
-          const float p1 = m_ref == -INFINITY ? 0.f : fast_exp2(s[hh][c + 1] - m_ref);
-          rs += p0 + p1;
-          pk[hh * 16 + c / 2] = pack_bf16x2(p0, p1);
-        }
-      // PV(j-1) must be done before P is overwritten or O is rescaled
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1))) { ok = false; break; }
+    for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      Item it;
+      if (!load_item(p, item, it)) continue;
+      const bool row_valid = (it.i0 + tok) < it.qo_len;
+      const int qpos = it.kv_len - it.qo_len + it.i0 + tok;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.ntiles; ++j, ++t) {
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full, t & 1))) { ok = false; break; }
         tc_fence_after();
-        // tcgen05.ld/st are warp-collective: the whole warp takes the rescale branch when
-        // any of its rows needs it (rows that do not multiply by 1)
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          for (int cb = 0; cb < kD; cb += 32) {
-            float o[32];
-            tmem_ld32(lane_base + kColO + cb, o);
-            tmem_wait_ld();
-            uint32_t w[32];
+        float s[2][32];
+        tmem_ld32(lane_base + kColS, s[0]);
+        tmem_ld32(lane_base + kColS + 32, s[1]);
+        tmem_wait_ld();
+        const int kbase = j * kBN;
+        float mt = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < 32; ++c) w[c] = __float_as_uint(o[c] * alpha);
-            tmem_st32(lane_base + kColO + cb, w);
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int kpos = kbase + hh * 32 + c;
+            const bool vis = row_valid && kpos < it.kv_len && (!p.causal || kpos <= qpos);
+            s[hh][c] = vis ? s[hh][c] * sl : -INFINITY;
+            mt = fmaxf(mt, s[hh][c]);
+          }
+        const float m_new = fmaxf(m_ref, mt);
+        const bool rescale = m_new > m_ref + 8.0f;   // also true on the first finite max
+        const float alpha = (rescale && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
+        if (rescale) m_ref = m_new;
+        float rs = 0.f;
+        uint32_t pk[32];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float p0 = m_ref == -INFINITY ? 0.f : fast_exp2(s[hh][c] - m_ref);
+            const float p1 = m_ref == -INFINITY ? 0.f : fast_exp2(s[hh][c + 1] - m_ref);
+            rs += p0 + p1;
+            pk[hh * 16 + c / 2] = pack_bf16x2(p0, p1);
+          }
+        // PV of the previous tile must be done before P is overwritten or O is rescaled
+        // (for j == 0 the previous item's epilogue already waited for it)
+        if (j > 0) {
+          if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (t - 1) & 1))) { ok = false; break; }
+          tc_fence_after();
+          // tcgen05.ld/st are warp-collective: the whole warp takes the rescale branch
+          // when any of its rows needs it (rows that do not multiply by 1)
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+            for (int cb = 0; cb < kD; cb += 32) {
+              float o[32];
+              tmem_ld32(lane_base + kColO + cb, o);
+              tmem_wait_ld();
+              uint32_t w[32];
+#pragma unroll
+              for (int c = 0; c < 32; ++c) w[c] = __float_as_uint(o[c] * alpha);
+              tmem_st32(lane_base + kColO + cb, w);
+            }
           }
         }
+        l = l * alpha + rs;
+        tmem_st32(lane_base + kColP, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full);
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
       }
-      l = l * alpha + rs;
-      tmem_st32(lane_base + kColP, pk);
-      tmem_wait_st();
+      if (!ok) break;
+      // epilogue: O of this item -> bf16 rows, then hand O back to the MMA warp
+      if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (t - 1) & 1))) { ok = false; break; }
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.out + static_cast<int64_t>(it.row0 + tok) * p.out_stride +
+                            static_cast<int64_t>(it.h * G + g) * kD;
+      for (int cb = 0; cb < kD; cb += 32) {
+        float o[32];
+        tmem_ld32(lane_base + kColO + cb, o);
+        tmem_wait_ld();
+        if (row_valid) {
+          uint4 pkt[4];
+          uint32_t* u = reinterpret_cast<uint32_t*>(pkt);
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) u[c / 2] = pack_bf16x2(o[c] * inv, o[c + 1] * inv);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(orow + cb)[v] = pkt[v];
+        }
+      }
       tc_fence_before();
-      mbar_arrive(p_full);
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      mbar_arrive(o_free);
     }
-    const bool done = __all_sync(0xffffffffu, ok && mbar_wait(pv_done, (ntiles - 1) & 1));
-    if (!done) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
-    tc_fence_after();
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    __nv_bfloat16* orow = p.out + static_cast<int64_t>(row0 + tok) * p.out_stride +
-                          static_cast<int64_t>(h * G + g) * kD;
-    for (int cb = 0; cb < kD; cb += 32) {
-      float o[32];
-      tmem_ld32(lane_base + kColO + cb, o);
-      tmem_wait_ld();
-      if (done && row_valid) {
-        uint4 pkt[4];
-        uint32_t* u = reinterpret_cast<uint32_t*>(pkt);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) u[c / 2] = pack_bf16x2(o[c] * inv, o[c + 1] * inv);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(orow + cb)[v] = pkt[v];
-      }
-    }
+    if (!ok) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
   }
 
   tc_fence_before();
@@ -465,9 +526,11 @@ int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q
   cudaError_t err = cudaFuncSetAttribute(prefill_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
-  dim3 grid((max_qo_len + tpt - 1) / tpt, batch, hkv);
-  if (grid.y > 65535 || grid.z > 65535) return set_error(NSLG_ERR_UNSUPPORTED, "prefill: grid");
-  prefill_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
+  const int64_t items = static_cast<int64_t>((max_qo_len + tpt - 1) / tpt) * batch * hkv;
+  if (items >= (int64_t{1} << 31)) return set_error(NSLG_ERR_UNSUPPORTED, "prefill: too many tiles");
+  p.n_items = static_cast<int>(items);
+  const int64_t grid = items < 2 * static_cast<int64_t>(sm_count()) ? items : 2 * sm_count();
+  prefill_tc_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
   return check_launch("prefill_tc");
 }
 
