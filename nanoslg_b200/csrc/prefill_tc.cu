@@ -1,29 +1,32 @@
 // Causal paged prefill / extend attention on the 5th-generation tensor cores
 // (tcgen05.mma, accumulators in TMEM), bf16, page_size 16, head_dim 128.
 //
-// Work unit. One CTA computes 128 query rows of one kv head h: T = 128/G new tokens of
-// sequence b times the G query heads h*G .. h*G+G-1 that share h (GQA), row r = token
-// r/G, head r%G. Q arrives by TMA as two [T tok x G heads x 64 dims] boxes straight out
-// of the caller's [rows, Hq, D] tensor (no packing: sequence b's rows start at
-// q_row_start[b]), so each K/V tile is loaded once for all G heads.
+// Work item. 128 query rows of one kv head h: T = 128/G new tokens of sequence b times
+// the G query heads h*G .. h*G+G-1 that share h (GQA), row r = token r/G, head r%G. Q
+// arrives by TMA as two [T tok x G heads x 64 dims] boxes straight out of the caller's
+// [rows, Hq, D] tensor (no packing: sequence b's rows start at q_row_start[b]), so each
+// K/V tile is loaded once for all G heads. A persistent grid (2 CTAs per SM) walks the
+// items, longest causal spans first; TMEM, barriers and the TMA pipeline carry across
+// items.
 //
-// Pipeline (per kv tile of 64 tokens = 4 pages, 2 smem stages):
-//   producer warp   TMA: per page, per 64-dim half, a [16 tok x 64] box of K and of V
-//                   (128-byte swizzle; pages past the sequence are loaded from outside
-//                   the tensor, which TMA fills with zeros)
-//   MMA warp        S(j) = Q . K(j)^T     M=128 N=64  K=128  A,B K-major from smem
-//                   O   += P(j) . V(j)    M=128 N=128 K=64   A = P from TMEM,
-//                                                            B = V MN-major from smem
-//   softmax WG      thread r owns TMEM lane r = row r: loads S(j), masks kpos > qpos,
-//                   keeps a running max m (log2 domain) and sum l; O is rescaled in
-//                   TMEM only when the max grows by more than 8 (2^8 headroom for P in
-//                   bf16), P is written back to TMEM as bf16 for the PV MMA.
-//   epilogue        O / l -> bf16 -> out row (q_row_start[b] + token, head).
-// TMEM: S 64 columns, P 32, O 128 -> 256 allocated, two CTAs per SM.
-// The MMA warp issues S(j+1) before PV(j), so the softmax of tile j+1 overlaps PV(j).
-//
-// Persistent grid of 2 CTAs per SM walking the (query tile, sequence, kv head) items,
-// longest causal spans first; TMEM, barriers and the TMA pipeline carry across items.
+// Pipeline over kv tiles of 64 tokens (4 pages), t counting every tile of the CTA:
+//   producer warp   TMA, per page and 64-dim half, a [16 tok x 64] box of K (ring of 2)
+//                   and of V (ring of 2); K runs one tile ahead of V. Pages past the
+//                   sequence are loaded from outside the tensor, which TMA fills with
+//                   zeros.
+//   MMA warp        S(t) = Q . K(t)^T  M=128 N=64  K=128, A and B K-major (smem),
+//                   into TMEM buffer S[t%2];
+//                   O += P(t) . V(t)   M=128 N=128 K=64, A = P(t) in TMEM (written over
+//                   S[t%2]), B = V MN-major (smem).
+//                   S(t+2) goes into S[t%2] as soon as P(t) . V(t) is done, so the
+//                   softmax of tile t+1 overlaps P(t).V(t) and S(t+2).
+//   softmax WG      thread r owns TMEM lane r = row r: loads S(t), masks only on tiles
+//                   that cross the causal or length edge, keeps a running max (log2
+//                   domain) and sum, writes P as bf16 over S, rescales O in TMEM only when
+//                   the max grows by more than 8 (2^8 headroom for P in bf16).
+//   epilogue        O / l -> bf16 -> out row (q_row_start[b] + token, head); then O is
+//                   handed back to the MMA warp for the next item.
+// TMEM: S[0] 64 columns, S[1] 64, O 128 = 256, two CTAs per SM.
 //
 // Every mbarrier wait is bounded (2 s); on a timeout the kernel records
 // NSLG_DEV_WAIT_TIMEOUT, stops issuing work, drains what it issued (bounded), frees its
@@ -39,21 +42,21 @@ namespace nslg {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kBM = 128;           // rows per CTA
+constexpr int kBM = 128;           // rows per item
 constexpr int kBN = 64;            // kv tokens per tile
 constexpr int kPS = 16;
 constexpr int kPagesPerTile = kBN / kPS;
 constexpr int kThreads = 192;      // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
 constexpr int kTmemCols = 256;
-constexpr int kColS = 0, kColP = 64, kColO = 128;
+constexpr int kColS = 0;           // S[b] at kColS + 64*b, P(t) over S[t%2]
+constexpr int kColO = 128;
 
 constexpr int kQBytes = kBM * kD * 2;           // 32 KiB: [2 halves][128 rows][128 B]
 constexpr int kQHalf = kBM * 128;               // 16 KiB
 constexpr int kKVHalf = kBN * 128;              // 8 KiB: [64 tok][128 B]
-constexpr int kKVTile = 2 * kKVHalf;            // 16 KiB per K (or V) tile
-constexpr int kStageBytes = 2 * kKVTile;        // K + V: 32 KiB
-constexpr int kStages = 2;
-constexpr int kSmemBytes = 1024 + kQBytes + kStages * kStageBytes + 256;
+constexpr int kTile = 2 * kKVHalf;              // 16 KiB per K (or V) tile
+constexpr int kRing = 2;                        // K ring and V ring depth
+constexpr int kSmemBytes = 1024 + kQBytes + 2 * kRing * kTile + 256;
 
 struct PrefillParams {
   __nv_bfloat16* out;
@@ -180,12 +183,9 @@ __device__ __forceinline__ bool load_item(const PrefillParams& p, int item, Item
 }
 
 // ----------------------------------------------------------------- the kernel
-// Persistent: each CTA walks its items with one TMEM allocation and one set of barriers.
-// A global tile counter t (over all items of the CTA) drives the barrier phases, so the
-// producer streams Q and K/V of the next item while the current one is still computing.
-// q_empty (MMA commit after an item's last S MMA) frees the single Q buffer, o_free (the
-// softmax warpgroup after reading O in an item's epilogue) frees the O accumulator for
-// the next item's first P.V MMA.
+// Barrier phases. Every per-buffer barrier (k/v full/empty, s_full, p_full, pv_done)
+// completes once per tile that uses its buffer, so the tile t's phase parity there is
+// (t >> 1) & 1; q_full, q_empty and o_free complete once per item.
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k,
@@ -195,31 +195,36 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sq = smem;
-  uint8_t* skv = smem + kQBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(skv + kStages * kStageBytes);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;        // [2]
-  uint64_t* kv_empty = bars + 3;       // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* pv_done = bars + 7;
-  uint64_t* mma_drain = bars + 8;
-  uint64_t* q_empty = bars + 9;
-  uint64_t* o_free = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 12);
+  uint8_t* sk = smem + kQBytes;                 // [kRing][2 halves][64 tok][128 B]
+  uint8_t* sv = sk + kRing * kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + kRing * kTile);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;     // [2]
+  uint64_t* k_empty = bars + 4;    // [2]
+  uint64_t* v_full = bars + 6;     // [2]
+  uint64_t* v_empty = bars + 8;    // [2]
+  uint64_t* s_full = bars + 10;    // [2]
+  uint64_t* p_full = bars + 12;    // [2]
+  uint64_t* pv_done = bars + 14;   // [2]
+  uint64_t* o_free = bars + 16;
+  uint64_t* mma_drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 19);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
     mbar_init(o_free, 128);
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
@@ -244,8 +249,32 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tmap_k);
       prefetch_tmap(&tmap_v);
       const uint64_t keep = l2_policy_evict_last();
-      int t = 0, n_it = 0;
+      int tk = 0, tv = 0, n_it = 0;      // K tiles, V tiles, Q loads issued
       bool ok = true;
+      // loads one [64 tok x 128 dim] tile (K or V) of the item into ring slot `slot`
+      auto load_tile = [&](const Item& it, int j, const CUtensorMap* map, uint8_t* dst,
+                           uint64_t* bar) {
+        mbar_arrive_expect_tx(bar, kTile);
+        int ids[kPagesPerTile];
+#pragma unroll
+        for (int pg = 0; pg < kPagesPerTile; ++pg) {
+          const int pi = j * kPagesPerTile + pg;
+          ids[pg] = pi < it.npages ? p.indices[it.kv_beg + pi] : -1;
+        }
+#pragma unroll
+        for (int pg = 0; pg < kPagesPerTile; ++pg) {
+          const int pi = j * kPagesPerTile + pg;
+          int tok_row = static_cast<int>(p.num_pages) * kPS;  // outside the pool: zeros
+          if (pi < it.npages) {
+            if (ids[pg] >= 0 && ids[pg] < p.num_pages) tok_row = ids[pg] * kPS;
+            else report(p.status, NSLG_DEV_BAD_PAGE);
+          }
+#pragma unroll
+          for (int half = 0; half < 2; ++half)
+            tma_load_3d(dst + half * kKVHalf + pg * kPS * 128, map, bar, half * 64, it.h,
+                        tok_row, keep);
+        }
+      };
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         Item it;
         if (!load_item(p, item, it)) continue;
@@ -254,43 +283,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_3d(sq, &tmap_q, q_full, 0, it.h * G, it.row0, keep);
         tma_load_3d(sq + kQHalf, &tmap_q, q_full, 64, it.h * G, it.row0, keep);
         ++n_it;
-        // page ids of a tile are fetched together, one tile ahead of their TMA loads
-        auto fetch_ids = [&](int j, int (&ids)[kPagesPerTile]) {
-#pragma unroll
-          for (int pg = 0; pg < kPagesPerTile; ++pg) {
-            const int pi = j * kPagesPerTile + pg;
-            ids[pg] = (j < it.ntiles && pi < it.npages) ? p.indices[it.kv_beg + pi] : -1;
+        // K(j) before V(j-1): keys run one tile ahead of values
+        for (int j = 0; j <= it.ntiles; ++j) {
+          if (j < it.ntiles) {
+            const int s = tk & 1;
+            if (*abort_flag || !mbar_wait(&k_empty[s], ((tk >> 1) & 1) ^ 1)) { ok = false; break; }
+            load_tile(it, j, &tmap_k, sk + s * kTile, &k_full[s]);
+            ++tk;
           }
-        };
-        int ids[kPagesPerTile];
-        fetch_ids(0, ids);
-        for (int j = 0; j < it.ntiles; ++j, ++t) {
-          const int s = t & 1;
-          int next_ids[kPagesPerTile];
-          fetch_ids(j + 1, next_ids);
-          if (*abort_flag || !mbar_wait(&kv_empty[s], ((t >> 1) & 1) ^ 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
-          uint8_t* kt = skv + s * kStageBytes;
-          uint8_t* vt = kt + kKVTile;
-#pragma unroll
-          for (int pg = 0; pg < kPagesPerTile; ++pg) {
-            const int pi = j * kPagesPerTile + pg;
-            int tok_row = static_cast<int>(p.num_pages) * kPS;  // outside the pool: zeros
-            if (pi < it.npages) {
-              const int pid = ids[pg];
-              if (pid >= 0 && pid < p.num_pages) tok_row = pid * kPS;
-              else report(p.status, NSLG_DEV_BAD_PAGE);
-            }
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              tma_load_3d(kt + half * kKVHalf + pg * kPS * 128, &tmap_k, &kv_full[s], half * 64,
-                          it.h, tok_row, keep);
-              tma_load_3d(vt + half * kKVHalf + pg * kPS * 128, &tmap_v, &kv_full[s], half * 64,
-                          it.h, tok_row, keep);
-            }
+          if (j > 0) {
+            const int s = tv & 1;
+            if (*abort_flag || !mbar_wait(&v_empty[s], ((tv >> 1) & 1) ^ 1)) { ok = false; break; }
+            load_tile(it, j - 1, &tmap_v, sv + s * kTile, &v_full[s]);
+            ++tv;
           }
-#pragma unroll
-          for (int pg = 0; pg < kPagesPerTile; ++pg) ids[pg] = next_ids[pg];
         }
       }
       if (!ok) {
@@ -298,8 +304,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         *abort_flag = 1;
         // no load may still be writing shared memory when the CTA leaves (bounded waits)
         if (n_it > 0) (void)mbar_wait(q_full, (n_it - 1) & 1);
-        for (int u = t - 2 < 0 ? 0 : t - 2; u < t; ++u)
-          (void)mbar_wait(&kv_full[u & 1], (u >> 1) & 1);
+        for (int u = tk - 2 < 0 ? 0 : tk - 2; u < tk; ++u)
+          (void)mbar_wait(&k_full[u & 1], (u >> 1) & 1);
+        for (int u = tv - 2 < 0 ? 0 : tv - 2; u < tv; ++u)
+          (void)mbar_wait(&v_full[u & 1], (u >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -308,53 +316,56 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t kIdescS = idesc_bf16(kBN, false);
       constexpr uint32_t kIdescO = idesc_bf16(kD, true);
       const uint32_t q_base = smem_u32(sq);
-      auto issue_s = [&](int t) {
-        const uint32_t k_base = smem_u32(skv + (t & 1) * kStageBytes);
+      bool ok = true;
+      // S(u) into S[u%2]; the buffer is free once P(u-2).V(u-2) is done
+      auto issue_s = [&](int u) -> bool {
+        const int b = u & 1;
+        if (!mbar_wait(&k_full[b], (u >> 1) & 1)) return false;
+        if (u >= 2 && !mbar_wait(&pv_done[b], ((u - 2) >> 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(sk + b * kTile);
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
           const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
           const uint32_t koff = (ks >> 2) * kKVHalf + (ks & 3) * 32;
-          mma_ss(tmem + kColS, smem_desc(q_base + off, 16, 1024),
+          mma_ss(tmem + kColS + 64 * b, smem_desc(q_base + off, 16, 1024),
                  smem_desc(k_base + koff, 16, 1024), kIdescS, ks > 0 ? 1u : 0u);
         }
-        mma_commit(s_full);
+        mma_commit(&s_full[b]);
+        mma_commit(&k_empty[b]);
+        return true;
       };
       int t = 0, n_it = 0;
-      bool ok = true;
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         Item it;
         if (!load_item(p, item, it)) continue;
         if (*abort_flag || !mbar_wait(q_full, n_it & 1)) { ok = false; break; }
         tc_fence_after();
-        for (int j = 0; j < it.ntiles; ++j, ++t) {
-          // q_empty is committed right after an item's last S MMA: Q is free once it is done
-          if (j == 0) {
-            if (!(ok = mbar_wait(&kv_full[t & 1], (t >> 1) & 1))) break;
-            tc_fence_after();
-            issue_s(t);
-            if (it.ntiles == 1) mma_commit(q_empty);
-          }
-          if (!(ok = mbar_wait(p_full, t & 1))) break;
+        const int t0 = t;
+        const int last = t0 + it.ntiles - 1;
+        for (int u = t0; ok && u <= last && u < t0 + 2; ++u) {
+          ok = issue_s(u);
+          if (ok && u == last) mma_commit(q_empty);   // Q is free once the last S is done
+        }
+        for (int j = 0; ok && j < it.ntiles; ++j, ++t) {
+          const int b = t & 1;
+          if (!(ok = mbar_wait(&p_full[b], (t >> 1) & 1))) break;
+          if (j == 0 && n_it > 0 && !(ok = mbar_wait(o_free, (n_it - 1) & 1))) break;
+          if (!(ok = mbar_wait(&v_full[b], (t >> 1) & 1))) break;
           tc_fence_after();
-          if (j + 1 < it.ntiles) {
-            if (!(ok = mbar_wait(&kv_full[(t + 1) & 1], ((t + 1) >> 1) & 1))) break;
-            tc_fence_after();
-            issue_s(t + 1);
-            if (j + 2 == it.ntiles) mma_commit(q_empty);
-          }
-          if (j == 0 && n_it > 0) {
-            if (!(ok = mbar_wait(o_free, (n_it - 1) & 1))) break;
-            tc_fence_after();
-          }
-          const uint32_t v_base = smem_u32(skv + (t & 1) * kStageBytes + kKVTile);
+          const uint32_t v_base = smem_u32(sv + b * kTile);
 #pragma unroll
           for (int kt = 0; kt < kBN / 16; ++kt)
-            mma_ts(tmem + kColO, tmem + kColP + kt * 8,
+            mma_ts(tmem + kColO, tmem + kColS + 64 * b + kt * 8,
                    smem_desc(v_base + kt * 2048, kKVHalf, 1024), kIdescO,
                    (j > 0 || kt > 0) ? 1u : 0u);
-          mma_commit(pv_done);
-          mma_commit(&kv_empty[t & 1]);
-          if (*abort_flag) { ok = false; break; }
+          mma_commit(&pv_done[b]);
+          mma_commit(&v_empty[b]);
+          if (t + 2 <= last) {
+            ok = issue_s(t + 2);
+            if (ok && t + 2 == last) mma_commit(q_empty);
+          }
+          if (*abort_flag) ok = false;
         }
         ++n_it;
       }
@@ -379,70 +390,75 @@ __global__ void __launch_bounds__(kThreads, 2)
       Item it;
       if (!load_item(p, item, it)) continue;
       const bool row_valid = (it.i0 + tok) < it.qo_len;
-      const int qpos = it.kv_len - it.qo_len + it.i0 + tok;
-      float m_ref = -INFINITY, l = 0.f;
+      // last kv position the row sees (-1: none)
+      const int lim = row_valid ? (p.causal ? min(it.kv_len - it.qo_len + it.i0 + tok,
+                                                  it.kv_len - 1)
+                                            : it.kv_len - 1)
+                                : -1;
+      float m_ref = -INFINITY, l = 0.f;   // m_ref in log2 units (raw score * sl)
       for (int j = 0; j < it.ntiles; ++j, ++t) {
-        if (!__all_sync(0xffffffffu, mbar_wait(s_full, t & 1))) { ok = false; break; }
+        const int b = t & 1;
+        const uint32_t scol = kColS + 64 * b;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (t >> 1) & 1))) { ok = false; break; }
         tc_fence_after();
-        float s[2][32];
-        tmem_ld32(lane_base + kColS, s[0]);
-        tmem_ld32(lane_base + kColS + 32, s[1]);
+        float s[64];
+        tmem_ld32(lane_base + scol, *reinterpret_cast<float(*)[32]>(&s[0]));
+        tmem_ld32(lane_base + scol + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
         tmem_wait_ld();
         const int kbase = j * kBN;
-        float mt = -INFINITY;
+        // columns past `lim` are masked; interior tiles (every row of the warp sees the
+        // whole tile) skip the per-column test
+        if (!__all_sync(0xffffffffu, kbase + kBN - 1 <= lim)) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
+          for (int c = 0; c < 64; ++c)
+            if (kbase + c > lim) s[c] = -INFINITY;
+        }
+        float mt = s[0];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int kpos = kbase + hh * 32 + c;
-            const bool vis = row_valid && kpos < it.kv_len && (!p.causal || kpos <= qpos);
-            s[hh][c] = vis ? s[hh][c] * sl : -INFINITY;
-            mt = fmaxf(mt, s[hh][c]);
-          }
-        const float m_new = fmaxf(m_ref, mt);
+        for (int c = 1; c < 64; ++c) mt = fmaxf(mt, s[c]);
+        const float m_new = fmaxf(m_ref, mt * sl);
         const bool rescale = m_new > m_ref + 8.0f;   // also true on the first finite max
         const float alpha = (rescale && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
         if (rescale) m_ref = m_new;
+        const float neg = m_ref == -INFINITY ? 0.f : -m_ref;
         float rs = 0.f;
         uint32_t pk[32];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const float p0 = m_ref == -INFINITY ? 0.f : fast_exp2(s[hh][c] - m_ref);
-            const float p1 = m_ref == -INFINITY ? 0.f : fast_exp2(s[hh][c + 1] - m_ref);
-            rs += p0 + p1;
-            pk[hh * 16 + c / 2] = pack_bf16x2(p0, p1);
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = fast_exp2(fmaf(s[c], sl, neg));
+          const float p1 = fast_exp2(fmaf(s[c + 1], sl, neg));
+          rs += p0 + p1;
+          pk[c / 2] = pack_bf16x2(p0, p1);
+        }
+        // O may only be rescaled once P(t-1).V(t-1) is done (warp-uniform branch: the
+        // tcgen05.ld/st are warp-collective; rows with alpha == 1 multiply by 1)
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[b ^ 1], ((t - 1) >> 1) & 1))) {
+            ok = false;
+            break;
           }
-        // PV of the previous tile must be done before P is overwritten or O is rescaled
-        // (for j == 0 the previous item's epilogue already waited for it)
-        if (j > 0) {
-          if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (t - 1) & 1))) { ok = false; break; }
           tc_fence_after();
-          // tcgen05.ld/st are warp-collective: the whole warp takes the rescale branch
-          // when any of its rows needs it (rows that do not multiply by 1)
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
-            for (int cb = 0; cb < kD; cb += 32) {
-              float o[32];
-              tmem_ld32(lane_base + kColO + cb, o);
-              tmem_wait_ld();
-              uint32_t w[32];
+          for (int cb = 0; cb < kD; cb += 32) {
+            float o[32];
+            tmem_ld32(lane_base + kColO + cb, o);
+            tmem_wait_ld();
+            uint32_t w[32];
 #pragma unroll
-              for (int c = 0; c < 32; ++c) w[c] = __float_as_uint(o[c] * alpha);
-              tmem_st32(lane_base + kColO + cb, w);
-            }
+            for (int c = 0; c < 32; ++c) w[c] = __float_as_uint(o[c] * alpha);
+            tmem_st32(lane_base + kColO + cb, w);
           }
         }
         l = l * alpha + rs;
-        tmem_st32(lane_base + kColP, pk);
+        tmem_st32(lane_base + scol, pk);           // P(t) over S(t)
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[b]);
         if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
       }
       if (!ok) break;
       // epilogue: O of this item -> bf16 rows, then hand O back to the MMA warp
-      if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (t - 1) & 1))) { ok = false; break; }
+      const int tl = t - 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[tl & 1], (tl >> 1) & 1))) { ok = false; break; }
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.out + static_cast<int64_t>(it.row0 + tok) * p.out_stride +
