@@ -251,16 +251,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t keep = l2_policy_evict_last();
       int tk = 0, tv = 0, n_it = 0;      // K tiles, V tiles, Q loads issued
       bool ok = true;
-      // loads one [64 tok x 128 dim] tile (K or V) of the item into ring slot `slot`
-      auto load_tile = [&](const Item& it, int j, const CUtensorMap* map, uint8_t* dst,
-                           uint64_t* bar) {
-        mbar_arrive_expect_tx(bar, kTile);
-        int ids[kPagesPerTile];
+      // page ids of tile j of the item (-1 past the sequence)
+      auto fetch_ids = [&](const Item& it, int j, int (&ids)[kPagesPerTile]) {
 #pragma unroll
         for (int pg = 0; pg < kPagesPerTile; ++pg) {
           const int pi = j * kPagesPerTile + pg;
-          ids[pg] = pi < it.npages ? p.indices[it.kv_beg + pi] : -1;
+          ids[pg] = (j < it.ntiles && pi < it.npages) ? p.indices[it.kv_beg + pi] : -1;
         }
+      };
+      // loads one [64 tok x 128 dim] tile (K or V) of the item into ring slot `slot`
+      auto load_tile = [&](const Item& it, int j, const int (&ids)[kPagesPerTile],
+                           const CUtensorMap* map, uint8_t* dst, uint64_t* bar) {
+        mbar_arrive_expect_tx(bar, kTile);
 #pragma unroll
         for (int pg = 0; pg < kPagesPerTile; ++pg) {
           const int pi = j * kPagesPerTile + pg;
@@ -283,19 +285,29 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_3d(sq, &tmap_q, q_full, 0, it.h * G, it.row0, keep);
         tma_load_3d(sq + kQHalf, &tmap_q, q_full, 64, it.h * G, it.row0, keep);
         ++n_it;
-        // K(j) before V(j-1): keys run one tile ahead of values
+        // K(j) before V(j-1): keys run one tile ahead of values. The page ids of tile j+1
+        // are fetched before waiting for K(j)'s slot, so their latency is hidden, and are
+        // reused for V one tile later.
+        int ids_v[kPagesPerTile], ids_k[kPagesPerTile], ids_n[kPagesPerTile];
+        fetch_ids(it, 0, ids_k);
         for (int j = 0; j <= it.ntiles; ++j) {
+          fetch_ids(it, j + 1, ids_n);
           if (j < it.ntiles) {
             const int s = tk & 1;
             if (*abort_flag || !mbar_wait(&k_empty[s], ((tk >> 1) & 1) ^ 1)) { ok = false; break; }
-            load_tile(it, j, &tmap_k, sk + s * kTile, &k_full[s]);
+            load_tile(it, j, ids_k, &tmap_k, sk + s * kTile, &k_full[s]);
             ++tk;
           }
           if (j > 0) {
             const int s = tv & 1;
             if (*abort_flag || !mbar_wait(&v_empty[s], ((tv >> 1) & 1) ^ 1)) { ok = false; break; }
-            load_tile(it, j - 1, &tmap_v, sv + s * kTile, &v_full[s]);
+            load_tile(it, j - 1, ids_v, &tmap_v, sv + s * kTile, &v_full[s]);
             ++tv;
+          }
+#pragma unroll
+          for (int pg = 0; pg < kPagesPerTile; ++pg) {
+            ids_v[pg] = ids_k[pg];
+            ids_k[pg] = ids_n[pg];
           }
         }
       }
