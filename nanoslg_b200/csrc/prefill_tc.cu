@@ -1,32 +1,41 @@
 // Causal paged prefill / extend attention on the 5th-generation tensor cores
 // (tcgen05.mma, accumulators in TMEM), bf16, page_size 16, head_dim 128.
 //
-// Work item. 128 query rows of one kv head h: T = 128/G new tokens of sequence b times
-// the G query heads h*G .. h*G+G-1 that share h (GQA), row r = token r/G, head r%G. Q
-// arrives by TMA as two [T tok x G heads x 64 dims] boxes straight out of the caller's
-// [rows, Hq, D] tensor (no packing: sequence b's rows start at q_row_start[b]), so each
-// K/V tile is loaded once for all G heads. A persistent grid (2 CTAs per SM) walks the
-// items, longest causal spans first; TMEM, barriers and the TMA pipeline carry across
-// items.
+// Work item. Two adjacent query tiles ("halves" A and B) of one sequence b and one kv
+// head h, each 128 rows: T = 128/G new tokens times the G query heads h*G .. h*G+G-1
+// that share h (GQA), row r = token r/G, head r%G. Both halves read the same K/V tiles,
+// so every K/V byte brought on chip feeds two 128-row MMAs. Q arrives by TMA as
+// [T tok x G heads x 64 dims] boxes straight out of the caller's [rows, Hq, D] tensor (no
+// packing: sequence b's rows start at q_row_start[b]). A persistent grid (one CTA per
+// SM) walks the items, longest causal spans first; TMEM, barriers and the TMA pipeline
+// carry across items, and the next item's Q is loaded while the current one runs.
 //
 // Pipeline over kv tiles of 64 tokens (4 pages), t counting every tile of the CTA:
-//   producer warp   TMA, per page and 64-dim half, a [16 tok x 64] box of K (ring of 2)
-//                   and of V (ring of 2); K runs one tile ahead of V. Pages past the
-//                   sequence are loaded from outside the tensor, which TMA fills with
-//                   zeros.
-//   MMA warp        S(t) = Q . K(t)^T  M=128 N=64  K=128, A and B K-major (smem),
-//                   into TMEM buffer S[t%2];
-//                   O += P(t) . V(t)   M=128 N=128 K=64, A = P(t) in TMEM (written over
-//                   S[t%2]), B = V MN-major (smem).
-//                   S(t+2) goes into S[t%2] as soon as P(t) . V(t) is done, so the
+//   producer warp   TMA: Q of the next item (two Q slots), and per page and 64-dim half
+//                   a [16 tok x 64] box of K (ring of 3 tiles) and of V (ring of 3); K runs
+//                   one tile ahead of V. Pages past the sequence are loaded from outside
+//                   the tensor (TMA fills zeros).
+//   MMA warp        for X in {A, B}:
+//                   S_X(t) = Q_X . K(t)^T  M=128 N=64  K=128, A and B K-major (smem),
+//                   into TMEM buffer S_X[t%2];
+//                   O_X += P_X(t) . V(t)   M=128 N=128 K=64, A = P_X(t) in TMEM (written
+//                   over S_X[t%2]), B = V MN-major (smem).
+//                   S_X(t+2) goes into S_X[t%2] as soon as P_X(t) . V(t) is done, so the
 //                   softmax of tile t+1 overlaps P(t).V(t) and S(t+2).
-//   softmax WG      thread r owns TMEM lane r = row r: loads S(t), masks only on tiles
-//                   that cross the causal or length edge, keeps a running max (log2
-//                   domain) and sum, writes P as bf16 over S, rescales O in TMEM only when
-//                   the max grows by more than 8 (2^8 headroom for P in bf16).
-//   epilogue        O / l -> bf16 -> out row (q_row_start[b] + token, head); then O is
-//                   handed back to the MMA warp for the next item.
-// TMEM: S[0] 64 columns, S[1] 64, O 128 = 256, two CTAs per SM.
+//   softmax WG X    (two warpgroups, one per half) thread r owns TMEM lane r = row r:
+//                   loads S_X(t), masks only on tiles that cross the causal or length
+//                   edge, keeps a running max (log2 domain) and sum, writes P as bf16 over
+//                   S, rescales O_X in TMEM only when the max grows by more than 8 (2^8
+//                   headroom for P in bf16).
+//   epilogue        softmax WG X reads O_X out of TMEM (then hands O_X back to the MMA
+//                   warp), scales by 1/l and writes bf16 rows into its half of the item's
+//                   Q slot (dead once the item's last S is done), in the 128-byte swizzled
+//                   layout of the Q load;
+//   store warp      writes each staged half to `out` with two TMA stores (the Q box
+//                   shape), or, for a tile that ends inside the sequence's last rows, with
+//                   plain coalesced stores of the valid rows only; frees the Q slot.
+// Both halves run the item's tile count (the longer span); the other half's extra
+// columns are masked. TMEM: per half S[0] 64 + S[1] 64 + O 128 columns = 512.
 //
 // Every mbarrier wait is bounded (2 s); on a timeout the kernel records
 // NSLG_DEV_WAIT_TIMEOUT, stops issuing work, drains what it issued (bounded), frees its
@@ -42,21 +51,22 @@ namespace nslg {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kBM = 128;           // rows per item
+constexpr int kBM = 128;           // rows per half
 constexpr int kBN = 64;            // kv tokens per tile
 constexpr int kPS = 16;
 constexpr int kPagesPerTile = kBN / kPS;
-constexpr int kThreads = 192;      // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
-constexpr int kTmemCols = 256;
-constexpr int kColS = 0;           // S[b] at kColS + 64*b, P(t) over S[t%2]
+constexpr int kThreads = 352;      // warp 0 TMA, 1 MMA, 2-5 / 6-9 softmax A / B, 10 stores
+constexpr int kTmemCols = 512;
+constexpr int kHalfCols = 256;     // per half: S[0] at +0, S[1] at +64, O at +128
 constexpr int kColO = 128;
 
-constexpr int kQBytes = kBM * kD * 2;           // 32 KiB: [2 halves][128 rows][128 B]
+constexpr int kQBytes = kBM * kD * 2;           // 32 KiB per half: [2 dims halves][128 rows][128 B]
 constexpr int kQHalf = kBM * 128;               // 16 KiB
+constexpr int kQSlot = 2 * kQBytes;             // one item's Q (both halves); two slots
 constexpr int kKVHalf = kBN * 128;              // 8 KiB: [64 tok][128 B]
 constexpr int kTile = 2 * kKVHalf;              // 16 KiB per K (or V) tile
-constexpr int kRing = 2;                        // K ring and V ring depth
-constexpr int kSmemBytes = 1024 + kQBytes + 2 * kRing * kTile + 256;
+constexpr int kRing = 3;                        // K ring and V ring depth
+constexpr int kSmemBytes = 1024 + 2 * kQSlot + 2 * kRing * kTile + 512;
 
 struct PrefillParams {
   __nv_bfloat16* out;
@@ -66,7 +76,7 @@ struct PrefillParams {
   const int32_t* indices;
   const int32_t* lpl;
   int64_t out_stride, num_pages;
-  int batch, hq, hkv, group, tokens_per_tile, causal, n_items;
+  int batch, hq, hkv, group, tokens_per_tile, causal, n_items, max_pairs;
   float scale_log2;
   uint32_t* status;
 };
@@ -152,80 +162,127 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 3-D tiled bulk tensor store from this CTA's shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_src, int c0,
+                                             int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          tmap),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// the stores of every committed group have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// ... and have completed
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// generic-proxy shared-memory writes become visible to the TMA (async proxy)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ----------------------------------------------------------------- work items
-// Item = (query tile, sequence, kv head), ordered with the query tiles that sit latest in
-// their sequences -- the longest causal spans -- first; CTA c takes items c, c + grid, ...
+// Item = (pair of query tiles, sequence, kv head), pairs latest in their sequences (the
+// longest causal spans) first; CTA c takes items c, c + grid, ... Half X of pair k is
+// query tile 2k + X.
+struct Half {
+  int i0, row0, lim_base;  // first new token, first row, kv_len - qo_len (+ i for causal)
+  bool any;                // the half has rows of this sequence
+};
 struct Item {
-  int b, h, i0, qo_len, kv_beg, npages, kv_len, ntiles, row0;
+  int b, h, qo_len, kv_beg, npages, kv_len, ntiles;
+  Half x[2];
 };
 
 __device__ __forceinline__ bool load_item(const PrefillParams& p, int item, Item& it) {
   const int per = p.batch * p.hkv;
-  const int tq_rev = item / per;
-  const int rem = item - tq_rev * per;
+  const int pk_rev = item / per;
+  const int rem = item - pk_rev * per;
   it.b = rem / p.hkv;
   it.h = rem - it.b * p.hkv;
+  const int tpt = p.tokens_per_tile;
   it.qo_len = p.qo_indptr[it.b + 1] - p.qo_indptr[it.b];
-  const int ntile_q = (it.qo_len + p.tokens_per_tile - 1) / p.tokens_per_tile;
-  const int tq = ntile_q - 1 - tq_rev;
-  if (tq < 0) return false;
-  it.i0 = tq * p.tokens_per_tile;
+  const int ntile_q = (it.qo_len + tpt - 1) / tpt;
+  const int npairs = (ntile_q + 1) / 2;
+  const int pk = npairs - 1 - pk_rev;
+  if (pk < 0) return false;
   it.kv_beg = p.indptr[it.b];
   it.npages = p.indptr[it.b + 1] - it.kv_beg;
   it.kv_len = it.npages > 0 ? (it.npages - 1) * kPS + p.lpl[it.b] : 0;
-  const int last_tok = min(it.i0 + p.tokens_per_tile, it.qo_len) - 1;
-  const int last_qpos = it.kv_len - it.qo_len + last_tok;
-  const int kv_span = p.causal ? min(it.kv_len, last_qpos + 1) : it.kv_len;
+  const int rs = p.q_row_start ? p.q_row_start[it.b] : p.qo_indptr[it.b];
+  int last_tok = -1;
+  for (int x = 0; x < 2; ++x) {
+    Half& hx = it.x[x];
+    hx.i0 = (2 * pk + x) * tpt;
+    hx.row0 = rs + hx.i0;
+    hx.any = hx.i0 < it.qo_len;
+    hx.lim_base = it.kv_len - it.qo_len + hx.i0;
+    if (hx.any) last_tok = min(hx.i0 + tpt, it.qo_len) - 1;
+  }
+  const int kv_span = p.causal ? min(it.kv_len, it.kv_len - it.qo_len + last_tok + 1) : it.kv_len;
   it.ntiles = (kv_span + kBN - 1) / kBN;
-  if (it.ntiles <= 0) return false;
-  it.row0 = (p.q_row_start ? p.q_row_start[it.b] : p.qo_indptr[it.b]) + it.i0;
-  return true;
+  return it.ntiles > 0;
 }
 
 // ----------------------------------------------------------------- the kernel
-// Barrier phases. Every per-buffer barrier (k/v full/empty, s_full, p_full, pv_done)
-// completes once per tile that uses its buffer, so the tile t's phase parity there is
-// (t >> 1) & 1; q_full, q_empty and o_free complete once per item.
-__global__ void __launch_bounds__(kThreads, 2)
+// Barrier phases. K/V ring barriers complete once per use of their slot (tile t uses slot
+// t % 3, parity (t / 3) & 1); per-half S-buffer barriers (s_full, p_full, pv_done) once
+// per use of their buffer (parity (t >> 1) & 1); Q-slot barriers (q_full, q_empty,
+// o_staged) once per use of their slot (item n uses slot n & 1, parity (n >> 1) & 1);
+// o_free once per item.
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k,
-                      const __grid_constant__ CUtensorMap tmap_v, const PrefillParams p) {
+                      const __grid_constant__ CUtensorMap tmap_v,
+                      const __grid_constant__ CUtensorMap tmap_o, const PrefillParams p) {
   const int G = p.group;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sq = smem;
-  uint8_t* sk = smem + kQBytes;                 // [kRing][2 halves][64 tok][128 B]
+  uint8_t* sq = smem;                            // [2 slots][2 halves][32 KiB]
+  uint8_t* sk = smem + 2 * kQSlot;               // [kRing][2 dim halves][64 tok][128 B]
   uint8_t* sv = sk + kRing * kTile;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sv + kRing * kTile);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;     // [2]
-  uint64_t* k_empty = bars + 4;    // [2]
-  uint64_t* v_full = bars + 6;     // [2]
-  uint64_t* v_empty = bars + 8;    // [2]
-  uint64_t* s_full = bars + 10;    // [2]
-  uint64_t* p_full = bars + 12;    // [2]
-  uint64_t* pv_done = bars + 14;   // [2]
-  uint64_t* o_free = bars + 16;
-  uint64_t* mma_drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 19);
+  uint64_t* q_full = bars + 0;     // [slot]
+  uint64_t* q_empty = bars + 2;    // [slot]: last S done (MMA) + staged O stored (store warp)
+  uint64_t* k_full = bars + 4;     // [kRing]
+  uint64_t* k_empty = bars + 7;    // [kRing]
+  uint64_t* v_full = bars + 10;    // [kRing]
+  uint64_t* v_empty = bars + 13;   // [kRing]
+  uint64_t* s_full = bars + 16;    // [half][2]
+  uint64_t* p_full = bars + 20;    // [half][2]
+  uint64_t* pv_done = bars + 24;   // [half][2]
+  uint64_t* o_free = bars + 28;    // [half]
+  uint64_t* o_staged = bars + 30;  // [half][slot]
+  uint64_t* mma_drain = bars + 34;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 35);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 36);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 2);
+      mbar_init(&o_free[i], 128);
+    }
+    for (int i = 0; i < kRing; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&pv_done[i], 1);
+      mbar_init(&o_staged[i], 128);
     }
-    mbar_init(o_free, 128);
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -249,9 +306,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tmap_k);
       prefetch_tmap(&tmap_v);
       const uint64_t keep = l2_policy_evict_last();
-      int tk = 0, tv = 0, n_it = 0;      // K tiles, V tiles, Q loads issued
+      int tk = 0, tv = 0, nq = 0;      // K tiles, V tiles, Q loads issued
       bool ok = true;
-      // page ids of tile j of the item (-1 past the sequence)
+      auto q_slot_free = [&](bool block) {   // the slot of Q load nq has been released
+        const uint32_t par = ((nq >> 1) & 1) ^ 1;
+        return block ? mbar_wait(&q_empty[nq & 1], par) : mbar_try_wait(&q_empty[nq & 1], par);
+      };
+      auto load_q = [&](const Item& it) {
+        const int s = nq & 1;
+        mbar_arrive_expect_tx(&q_full[s], 2 * kQBytes);
+        for (int x = 0; x < 2; ++x) {
+          uint8_t* dst = sq + s * kQSlot + x * kQBytes;
+          tma_load_3d(dst, &tmap_q, &q_full[s], 0, it.h * G, it.x[x].row0, keep);
+          tma_load_3d(dst + kQHalf, &tmap_q, &q_full[s], 64, it.h * G, it.x[x].row0, keep);
+        }
+        ++nq;
+      };
       auto fetch_ids = [&](const Item& it, int j, int (&ids)[kPagesPerTile]) {
 #pragma unroll
         for (int pg = 0; pg < kPagesPerTile; ++pg) {
@@ -259,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           ids[pg] = (j < it.ntiles && pi < it.npages) ? p.indices[it.kv_beg + pi] : -1;
         }
       };
-      // loads one [64 tok x 128 dim] tile (K or V) of the item into ring slot `slot`
       auto load_tile = [&](const Item& it, int j, const int (&ids)[kPagesPerTile],
                            const CUtensorMap* map, uint8_t* dst, uint64_t* bar) {
         mbar_arrive_expect_tx(bar, kTile);
@@ -277,30 +346,37 @@ __global__ void __launch_bounds__(kThreads, 2)
                         tok_row, keep);
         }
       };
-      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
-        Item it;
-        if (!load_item(p, item, it)) continue;
-        if (n_it > 0 && (*abort_flag || !mbar_wait(q_empty, (n_it - 1) & 1))) { ok = false; break; }
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_3d(sq, &tmap_q, q_full, 0, it.h * G, it.row0, keep);
-        tma_load_3d(sq + kQHalf, &tmap_q, q_full, 64, it.h * G, it.row0, keep);
-        ++n_it;
-        // K(j) before V(j-1): keys run one tile ahead of values. The page ids of tile j+1
-        // are fetched before waiting for K(j)'s slot, so their latency is hidden, and are
-        // reused for V one tile later.
+      auto next_item = [&](int from, Item& it) {
+        int item = from;
+        while (item < p.n_items && !load_item(p, item, it)) item += gridDim.x;
+        return item;
+      };
+      Item it;
+      int item = next_item(blockIdx.x, it);
+      if (item < p.n_items) load_q(it);      // slot 0 starts free
+      while (ok && item < p.n_items) {
+        Item nx;
+        const int nitem = next_item(item + gridDim.x, nx);
+        bool nx_q = nitem >= p.n_items;       // next item's Q issued (or no next item)
+        // K(j) before V(j-1); page ids of tile j+1 fetched before waiting for K(j)'s slot;
+        // the next item's Q goes out as soon as its slot is released
         int ids_v[kPagesPerTile], ids_k[kPagesPerTile], ids_n[kPagesPerTile];
         fetch_ids(it, 0, ids_k);
         for (int j = 0; j <= it.ntiles; ++j) {
           fetch_ids(it, j + 1, ids_n);
+          if (!nx_q && q_slot_free(false)) {
+            load_q(nx);
+            nx_q = true;
+          }
           if (j < it.ntiles) {
-            const int s = tk & 1;
-            if (*abort_flag || !mbar_wait(&k_empty[s], ((tk >> 1) & 1) ^ 1)) { ok = false; break; }
+            const int s = tk % kRing;
+            if (*abort_flag || !mbar_wait(&k_empty[s], ((tk / kRing) & 1) ^ 1)) { ok = false; break; }
             load_tile(it, j, ids_k, &tmap_k, sk + s * kTile, &k_full[s]);
             ++tk;
           }
           if (j > 0) {
-            const int s = tv & 1;
-            if (*abort_flag || !mbar_wait(&v_empty[s], ((tv >> 1) & 1) ^ 1)) { ok = false; break; }
+            const int s = tv % kRing;
+            if (*abort_flag || !mbar_wait(&v_empty[s], ((tv / kRing) & 1) ^ 1)) { ok = false; break; }
             load_tile(it, j - 1, ids_v, &tmap_v, sv + s * kTile, &v_full[s]);
             ++tv;
           }
@@ -310,16 +386,24 @@ __global__ void __launch_bounds__(kThreads, 2)
             ids_k[pg] = ids_n[pg];
           }
         }
+        if (!ok) break;
+        if (!nx_q) {
+          if (*abort_flag || !q_slot_free(true)) { ok = false; break; }
+          load_q(nx);
+        }
+        it = nx;
+        item = nitem;
       }
       if (!ok) {
         report(p.status, NSLG_DEV_WAIT_TIMEOUT);
         *abort_flag = 1;
         // no load may still be writing shared memory when the CTA leaves (bounded waits)
-        if (n_it > 0) (void)mbar_wait(q_full, (n_it - 1) & 1);
-        for (int u = tk - 2 < 0 ? 0 : tk - 2; u < tk; ++u)
-          (void)mbar_wait(&k_full[u & 1], (u >> 1) & 1);
-        for (int u = tv - 2 < 0 ? 0 : tv - 2; u < tv; ++u)
-          (void)mbar_wait(&v_full[u & 1], (u >> 1) & 1);
+        for (int u = nq - 2 < 0 ? 0 : nq - 2; u < nq; ++u)
+          (void)mbar_wait(&q_full[u & 1], (u >> 1) & 1);
+        for (int u = tk - kRing < 0 ? 0 : tk - kRing; u < tk; ++u)
+          (void)mbar_wait(&k_full[u % kRing], (u / kRing) & 1);
+        for (int u = tv - kRing < 0 ? 0 : tv - kRing; u < tv; ++u)
+          (void)mbar_wait(&v_full[u % kRing], (u / kRing) & 1);
       }
     }
   } else if (warp == 1) {
@@ -327,55 +411,63 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       constexpr uint32_t kIdescS = idesc_bf16(kBN, false);
       constexpr uint32_t kIdescO = idesc_bf16(kD, true);
-      const uint32_t q_base = smem_u32(sq);
       bool ok = true;
-      // S(u) into S[u%2]; the buffer is free once P(u-2).V(u-2) is done
-      auto issue_s = [&](int u) -> bool {
-        const int b = u & 1;
-        if (!mbar_wait(&k_full[b], (u >> 1) & 1)) return false;
-        if (u >= 2 && !mbar_wait(&pv_done[b], ((u - 2) >> 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(sk + b * kTile);
+      // S_X(u) into S_X[u%2] for both halves; the buffer is free once P_X(u-2).V is done
+      auto issue_s = [&](int u, int qs) -> bool {
+        const int slot = u % kRing, b = u & 1;
+        if (!mbar_wait(&k_full[slot], (u / kRing) & 1)) return false;
+        const uint32_t k_base = smem_u32(sk + slot * kTile);
+        for (int x = 0; x < 2; ++x) {
+          if (u >= 2 && !mbar_wait(&pv_done[x * 2 + b], ((u - 2) >> 1) & 1)) return false;
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(sq + qs * kQSlot + x * kQBytes);
+          const uint32_t dcol = tmem + x * kHalfCols + 64 * b;
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
-          const uint32_t koff = (ks >> 2) * kKVHalf + (ks & 3) * 32;
-          mma_ss(tmem + kColS + 64 * b, smem_desc(q_base + off, 16, 1024),
-                 smem_desc(k_base + koff, 16, 1024), kIdescS, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < kD / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
+            const uint32_t koff = (ks >> 2) * kKVHalf + (ks & 3) * 32;
+            mma_ss(dcol, smem_desc(q_base + off, 16, 1024), smem_desc(k_base + koff, 16, 1024),
+                   kIdescS, ks > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[x * 2 + b]);
         }
-        mma_commit(&s_full[b]);
-        mma_commit(&k_empty[b]);
+        mma_commit(&k_empty[slot]);
         return true;
       };
       int t = 0, n_it = 0;
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         Item it;
         if (!load_item(p, item, it)) continue;
-        if (*abort_flag || !mbar_wait(q_full, n_it & 1)) { ok = false; break; }
+        const int qs = n_it & 1;
+        if (*abort_flag || !mbar_wait(&q_full[qs], (n_it >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
         const int t0 = t;
         const int last = t0 + it.ntiles - 1;
         for (int u = t0; ok && u <= last && u < t0 + 2; ++u) {
-          ok = issue_s(u);
-          if (ok && u == last) mma_commit(q_empty);   // Q is free once the last S is done
+          ok = issue_s(u, qs);
+          if (ok && u == last) mma_commit(&q_empty[qs]);   // Q is read for the last time
         }
         for (int j = 0; ok && j < it.ntiles; ++j, ++t) {
-          const int b = t & 1;
-          if (!(ok = mbar_wait(&p_full[b], (t >> 1) & 1))) break;
-          if (j == 0 && n_it > 0 && !(ok = mbar_wait(o_free, (n_it - 1) & 1))) break;
-          if (!(ok = mbar_wait(&v_full[b], (t >> 1) & 1))) break;
-          tc_fence_after();
-          const uint32_t v_base = smem_u32(sv + b * kTile);
+          const int slot = t % kRing, b = t & 1;
+          if (!(ok = mbar_wait(&v_full[slot], (t / kRing) & 1))) break;
+          const uint32_t v_base = smem_u32(sv + slot * kTile);
+          for (int x = 0; x < 2; ++x) {
+            if (!(ok = mbar_wait(&p_full[x * 2 + b], (t >> 1) & 1))) break;
+            if (j == 0 && n_it > 0 && !(ok = mbar_wait(&o_free[x], (n_it - 1) & 1))) break;
+            tc_fence_after();
+            const uint32_t hb = tmem + x * kHalfCols;
 #pragma unroll
-          for (int kt = 0; kt < kBN / 16; ++kt)
-            mma_ts(tmem + kColO, tmem + kColS + 64 * b + kt * 8,
-                   smem_desc(v_base + kt * 2048, kKVHalf, 1024), kIdescO,
-                   (j > 0 || kt > 0) ? 1u : 0u);
-          mma_commit(&pv_done[b]);
-          mma_commit(&v_empty[b]);
+            for (int kt = 0; kt < kBN / 16; ++kt)
+              mma_ts(hb + kColO, hb + 64 * b + kt * 8,
+                     smem_desc(v_base + kt * 2048, kKVHalf, 1024), kIdescO,
+                     (j > 0 || kt > 0) ? 1u : 0u);
+            mma_commit(&pv_done[x * 2 + b]);
+          }
+          if (!ok) break;
+          mma_commit(&v_empty[slot]);
           if (t + 2 <= last) {
-            ok = issue_s(t + 2);
-            if (ok && t + 2 == last) mma_commit(q_empty);
+            ok = issue_s(t + 2, qs);
+            if (ok && t + 2 == last) mma_commit(&q_empty[qs]);
           }
           if (*abort_flag) ok = false;
         }
@@ -389,29 +481,78 @@ __global__ void __launch_bounds__(kThreads, 2)
       mma_commit(mma_drain);
       (void)mbar_wait(mma_drain, 0);
     }
-  } else {
-    // -------------------------------------------------------------- softmax warpgroup
-    const int quarter = warp & 3;              // TMEM lanes 32*quarter .. +31
-    const int r = quarter * 32 + lane;         // row = TMEM lane
-    const int tok = r / G, g = r % G;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const float sl = p.scale_log2;
-    int t = 0;
+  } else if (warp == 10) {
+    // -------------------------------------------------------------- output stores
+    int n_it = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
       Item it;
       if (!load_item(p, item, it)) continue;
-      const bool row_valid = (it.i0 + tok) < it.qo_len;
+      const int qs = n_it & 1;
+      for (int x = 0; x < 2; ++x) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_staged[x * 2 + qs], (n_it >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        const Half& hx = it.x[x];
+        if (!hx.any) continue;
+        const uint8_t* stage = sq + qs * kQSlot + x * kQBytes;
+        const int ntok = min(p.tokens_per_tile, it.qo_len - hx.i0);
+        if (ntok == p.tokens_per_tile) {
+          if (lane == 0) {
+            tma_store_3d(&tmap_o, stage, 0, it.h * G, hx.row0);
+            tma_store_3d(&tmap_o, stage + kQHalf, 64, it.h * G, hx.row0);
+          }
+        } else {
+          // the tile ends inside the sequence: only its first ntok tokens are written
+          const int rows = ntok * G;
+          for (int idx = lane; idx < rows * 16; idx += 32) {
+            const int r = idx >> 4, c = idx & 15, cc = c & 7;
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + (c >> 3) * kQHalf + r * 128 +
+                                                            ((cc ^ (r & 7)) << 4));
+            __nv_bfloat16* dst = p.out + static_cast<int64_t>(hx.row0 + r / G) * p.out_stride +
+                                 static_cast<int64_t>(it.h * G + r % G) * kD + c * 8;
+            *reinterpret_cast<uint4*>(dst) = v;
+          }
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) {
+        bulk_commit_group();
+        bulk_wait_read_all();   // the slot may be refilled once the stores have read it
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_empty[qs]);
+      ++n_it;
+    }
+    if (lane == 0) bulk_wait_all();
+    if (!ok && lane == 0) {
+      report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+      *abort_flag = 1;
+    }
+  } else {
+    // -------------------------------------------------------------- softmax warpgroups
+    const int x = (warp - 2) / 4;                 // half A (warps 2-5) or B (warps 6-9)
+    const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
+    const int r = quarter * 32 + lane;            // row = TMEM lane
+    const int tok = r / G;
+    const uint32_t lane_base = tmem + x * kHalfCols + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float sl = p.scale_log2;
+    int t = 0, n_it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      Item it;
+      if (!load_item(p, item, it)) continue;
+      const Half& hx = it.x[x];
+      const bool row_valid = (hx.i0 + tok) < it.qo_len;
       // last kv position the row sees (-1: none)
-      const int lim = row_valid ? (p.causal ? min(it.kv_len - it.qo_len + it.i0 + tok,
-                                                  it.kv_len - 1)
-                                            : it.kv_len - 1)
+      const int lim = row_valid ? (p.causal ? min(hx.lim_base + tok, it.kv_len - 1) : it.kv_len - 1)
                                 : -1;
       float m_ref = -INFINITY, l = 0.f;   // m_ref in log2 units (raw score * sl)
       for (int j = 0; j < it.ntiles; ++j, ++t) {
         const int b = t & 1;
-        const uint32_t scol = kColS + 64 * b;
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (t >> 1) & 1))) { ok = false; break; }
+        const uint32_t scol = 64 * b;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x * 2 + b], (t >> 1) & 1))) { ok = false; break; }
         tc_fence_after();
         float s[64];
         tmem_ld32(lane_base + scol, *reinterpret_cast<float(*)[32]>(&s[0]));
@@ -445,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // O may only be rescaled once P(t-1).V(t-1) is done (warp-uniform branch: the
         // tcgen05.ld/st are warp-collective; rows with alpha == 1 multiply by 1)
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[b ^ 1], ((t - 1) >> 1) & 1))) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[x * 2 + (b ^ 1)], ((t - 1) >> 1) & 1))) {
             ok = false;
             break;
           }
@@ -464,32 +605,46 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_st32(lane_base + scol, pk);           // P(t) over S(t)
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[b]);
+        mbar_arrive(&p_full[x * 2 + b]);
         if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
       }
       if (!ok) break;
-      // epilogue: O of this item -> bf16 rows, then hand O back to the MMA warp
+      // epilogue: O of this half -> TMEM is handed back -> bf16 rows staged in this half of
+      // the item's Q slot (128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7)), for
+      // the store warp
       const int tl = t - 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[tl & 1], (tl >> 1) & 1))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[x * 2 + (tl & 1)], (tl >> 1) & 1))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.out + static_cast<int64_t>(it.row0 + tok) * p.out_stride +
-                            static_cast<int64_t>(it.h * G + g) * kD;
-      for (int cb = 0; cb < kD; cb += 32) {
-        float o[32];
-        tmem_ld32(lane_base + kColO + cb, o);
+      const int qs = n_it & 1;
+      uint8_t* stage = sq + qs * kQSlot + x * kQBytes + r * 128;
+      for (int cb = 0; cb < kD; cb += 64) {
+        float o0[32], o1[32];
+        tmem_ld32(lane_base + kColO + cb, o0);
+        tmem_ld32(lane_base + kColO + cb + 32, o1);
         tmem_wait_ld();
-        if (row_valid) {
-          uint4 pkt[4];
-          uint32_t* u = reinterpret_cast<uint32_t*>(pkt);
+        if (cb + 64 == kD) {
+          tc_fence_before();
+          mbar_arrive(&o_free[x]);                  // O_X may be overwritten now
+        }
+        uint8_t* row = stage + (cb >> 6) * kQHalf;
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) u[c / 2] = pack_bf16x2(o[c] * inv, o[c + 1] * inv);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(orow + cb)[v] = pkt[v];
+        for (int c = 0; c < 8; ++c) {
+          const float* src = c < 4 ? &o0[c * 8] : &o1[(c - 4) * 8];
+          uint4 pkt;
+          pkt.x = pack_bf16x2(src[0] * inv, src[1] * inv);
+          pkt.y = pack_bf16x2(src[2] * inv, src[3] * inv);
+          pkt.z = pack_bf16x2(src[4] * inv, src[5] * inv);
+          pkt.w = pack_bf16x2(src[6] * inv, src[7] * inv);
+          *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = pkt;
         }
       }
-      tc_fence_before();
-      mbar_arrive(o_free);
+      fence_proxy_async_smem();
+      mbar_arrive(&o_staged[x * 2 + qs]);
+      ++n_it;
     }
     if (!ok) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
   }
@@ -526,13 +681,17 @@ int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q
     return set_error(NSLG_ERR_UNSUPPORTED, "prefill: pool larger than 2^31 token rows");
   if (q_rows <= 0 || q_rows >= (int64_t{1} << 31))
     return set_error(NSLG_ERR_ARG, "prefill: q_rows out of range");
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   int rc = pool_tensor_map(pool_k, num_pages, hkv, kD, &tk);
   if (rc != NSLG_OK) return rc;
   rc = pool_tensor_map(pool_v, num_pages, hkv, kD, &tv);
   if (rc != NSLG_OK) return rc;
   rc = encode_tiled_3d_bf16(&tq, q, kD, hq, q_rows, static_cast<uint64_t>(kD) * 2,
                             static_cast<uint64_t>(q_stride) * 2, 64, G, tpt);
+  if (rc != NSLG_OK) return rc;
+  // out rows have the Q layout; the store box is the Q box
+  rc = encode_tiled_3d_bf16(&to, out, kD, hq, q_rows, static_cast<uint64_t>(kD) * 2,
+                            static_cast<uint64_t>(out_stride) * 2, 64, G, tpt);
   if (rc != NSLG_OK) return rc;
   PrefillParams p{};
   p.out = static_cast<__nv_bfloat16*>(out);
@@ -554,11 +713,13 @@ int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q
   cudaError_t err = cudaFuncSetAttribute(prefill_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
-  const int64_t items = static_cast<int64_t>((max_qo_len + tpt - 1) / tpt) * batch * hkv;
+  const int64_t pairs = ((max_qo_len + tpt - 1) / tpt + 1) / 2;
+  const int64_t items = pairs * batch * hkv;
   if (items >= (int64_t{1} << 31)) return set_error(NSLG_ERR_UNSUPPORTED, "prefill: too many tiles");
   p.n_items = static_cast<int>(items);
-  const int64_t grid = items < 2 * static_cast<int64_t>(sm_count()) ? items : 2 * sm_count();
-  prefill_tc_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
+  const int64_t grid = items < static_cast<int64_t>(sm_count()) ? items : sm_count();
+  prefill_tc_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tq, tk, tv, to,
+                                                                                   p);
   return check_launch("prefill_tc");
 }
 
