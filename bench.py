@@ -278,7 +278,8 @@ def run_prefill_kernel(device, reps=10, batch=64, prompt=512):
 
 
 # ------------------------------------------------------------------ model decode
-def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=None):
+def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=None,
+                     peer_allreduce=True):
     """Llama-3.1-8B-architecture decode (BASELINE config C3 at TP=1, TP=world under
     torchrun): prefill of ``prompt`` random token ids per sequence, then ``steps`` timed
     greedy decode steps of the whole batch through the B200 path."""
@@ -286,7 +287,8 @@ def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=N
     hf = llama_config("llama-3.1-8b")
     if runner is None:
         pages = 2 * 64 * (-(-(prompt + 8 + 64 + 2) // PS)) + 64
-        runner = LlamaRunner(hf, device, tp_size=world, rank=rank, max_kv_pages=pages)
+        runner = LlamaRunner(hf, device, tp_size=world, rank=rank, max_kv_pages=pages,
+                             peer_allreduce=peer_allreduce)
         runner.enable_cuda_graphs([64, 1])
     g = torch.Generator().manual_seed(123 + batch)
     prompts = torch.randint(0, hf.vocab_size, (batch, prompt), generator=g).tolist()
@@ -362,6 +364,9 @@ def main():
                          "batch (still 1.13 GB of KV per step)")
     ap.add_argument("--no-model", action="store_true", help="skip the Llama-3.1-8B decode leg")
     ap.add_argument("--model-steps", type=int, default=32)
+    ap.add_argument("--tp-reduce", choices=["peer", "nccl"], default="peer",
+                    help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
+                         "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
     ap.add_argument("--only", choices=["all", "kernel", "model", "prefill"], default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg")
@@ -419,7 +424,8 @@ def main():
             torch.distributed.destroy_process_group()
         return 0
     if a.only == "model":
-        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4)
+        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,
+                                       peer_allreduce=a.tp_reduce == "peer")
         runner.close()
         if rank == 0:
             print(json.dumps({"case": "model only", "llama8b_decode_batch64": r64}), flush=True)
@@ -476,7 +482,8 @@ def main():
             "clocks": kr["clocks"]}
     line["prefill_attention"] = run_prefill_kernel(device) if rank == 0 else None
     if not a.no_model:
-        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4)
+        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,
+                                       peer_allreduce=a.tp_reduce == "peer")
         _, r1 = run_llama_decode(device, world, rank, 1, 512, a.model_steps, 4, runner=runner)
         line["llama8b_decode"] = {
             "model": "Llama-3.1-8B architecture, random init N(0, 0.02), bf16 (BASELINE C3)",

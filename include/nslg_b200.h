@@ -179,6 +179,55 @@ int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x,
 int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gate_up_stride,
                   void* out, int64_t out_stride, void* stream);
 
+/* ---------------------------------------------------------------- tensor parallel */
+
+#define NSLG_IPC_HANDLE_BYTES 64   /* cudaIpcMemHandle_t                                 */
+#define NSLG_TP_MAX_WORLD 8
+#define NSLG_TP_COUNTER_BYTES 1024 /* per-rank call counters of nslg_tp_allreduce_rmsnorm */
+
+/* Device memory that peers in other processes can map (CUDA IPC, no multicast).
+ * nslg_ipc_alloc: cudaMalloc of `bytes` on the current device, zeroed, and its
+ *   NSLG_IPC_HANDLE_BYTES-byte handle in handle_out (to be sent to the peers);
+ * nslg_ipc_open: maps a peer's handle into this process (peer access over NVLink);
+ * nslg_ipc_close / nslg_ipc_free: undo open / alloc.
+ * Replaces nothing in the reference (whose only collective path is NCCL through
+ * parallel.py:167-184); it sets up the memory nslg_tp_allreduce_rmsnorm writes.
+ */
+int nslg_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle_out);
+int nslg_ipc_open(const void* handle, void** dev_ptr);
+int nslg_ipc_close(void* dev_ptr);
+int nslg_ipc_free(void* dev_ptr);
+
+/* Tensor-parallel all-reduce of a RowParallelLinear output fused with the residual add
+ * and the RMSNorm that follow it, over peer memory.
+ *
+ * Replaces RowParallelLinear.forward's all-reduce (tp_layers.py:148-158, through
+ * all_reduce_tp, parallel.py:167-172) together with the block's `h = x + attn` /
+ * `h + mlp` and the next RMSNorm (models.py:169-172, 25-34), for one TP group of
+ * `world` ranks (one process per GPU), this process being `rank`:
+ *   sum            = sum over ranks of partial[row]   (fp32, rank order, rounded once)
+ *   residual[row] <- round(residual[row] + sum)       (in place)
+ *   out[row]       = weight * round(residual[row] * rsqrt(mean(residual[row]^2) + eps))
+ *                    (skipped when weight == NULL: the caller wants the residual only)
+ * partial, residual, out: [rows, hidden] (row strides in elements, rows 16-byte aligned,
+ *   hidden * element size <= 16 KiB).
+ * stage_bufs: HOST array of `world` device pointers, entry i = rank i's stage buffer
+ *   (stage_bytes each, the same on every rank, >= 4 * world * rows * hidden * element
+ *   size), from nslg_ipc_alloc: entry `rank` is this process's own allocation, the
+ *   others its nslg_ipc_open mappings of the peers'. Peers write into it.
+ * counters: this rank's NSLG_TP_COUNTER_BYTES of zeroed device memory, kept between
+ *   calls (private to the rank).
+ * Every rank must make the same sequence of calls (the counters pair them; the launch
+ * may be captured in a CUDA graph). A wait on a peer gives up after timeout_ns, sets
+ * NSLG_DEV_WAIT_TIMEOUT in *dev_status and leaves that call's rows unwritten.
+ */
+int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int world, int rank,
+                              const void* partial, int64_t partial_stride,
+                              void* const* stage_bufs, int64_t stage_bytes, void* counters,
+                              void* residual, int64_t residual_stride, const void* weight,
+                              void* out, int64_t out_stride, float eps, int64_t timeout_ns,
+                              uint32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

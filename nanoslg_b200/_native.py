@@ -43,7 +43,17 @@ SIGNATURES = {
     "nslg_silu_mul": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp]),
     "nslg_rmsnorm_residual": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i64,
                                      _f32, _vp]),
+    "nslg_ipc_alloc": (_i32, [_i64, ctypes.POINTER(_vp), _vp]),
+    "nslg_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "nslg_ipc_close": (_i32, [_vp]),
+    "nslg_ipc_free": (_i32, [_vp]),
+    "nslg_tp_allreduce_rmsnorm": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp,
+                                         _vp, _i64, _vp, _vp, _i64, _f32, _i64, _vp, _vp]),
 }
+
+IPC_HANDLE_BYTES = 64
+TP_MAX_WORLD = 8
+TP_COUNTER_BYTES = 1024
 
 _lib = None
 _lock = threading.Lock()

@@ -1,0 +1,313 @@
+// Tensor-parallel all-reduce fused with the residual add and RMSNorm that follow it,
+// over peer memory (CUDA IPC mappings across NVLink / NVSwitch), and the IPC helpers
+// that set the peer memory up.
+//
+// Replaces, for the rows of one decode step, RowParallelLinear's NCCL all-reduce
+// (tp_layers.py:148-158 -> parallel.py:167-172) and the block's residual add + RMSNorm
+// (models.py:169-172, 25-34): one kernel per RowParallel output instead of an NCCL
+// all-reduce, an add and a norm.
+//
+// Protocol: one-shot push with flags inside the data ("low-latency" packing). Each
+// 16-byte store carries 8 bytes of activations and, in each of its 8-byte halves, the
+// 32-bit call number: {d0, call, d1, call}. An 8-byte store is single-copy atomic, so a
+// reader that sees the call number in both halves has both data words of this call; no
+// fence and no separate flag are needed, and the only cross-GPU latency on the critical
+// path is one NVLink write. Rank r writes its partial rows into slot (call & 1), source
+// region r, of every peer's stage buffer; each rank then polls its own buffer (local
+// memory) for the other ranks' words, sums all ranks' rows in fp32 in rank order (its
+// own partial read directly), rounds once to the activation type (one NCCL bf16 sum of
+// two ranks rounds the same way), adds the residual (rounded), stores the new residual,
+// and writes weight * round(h * rsqrt(mean(h^2) + eps)) as the rmsnorm kernel does.
+//
+// Calls are numbered per block: block b keeps its call count in this rank's counter
+// buffer (word b) and the grid is always kGrid blocks, so block b of every rank sees
+// the same sequence of call numbers (every rank makes the same calls). The count lives
+// in device memory, so the launch can be captured in a CUDA graph and replayed. Two
+// slots suffice: a peer can be at most one call ahead (its call e + 1 needs this rank's
+// words of call e + 1, written only after this rank finished call e), and words left
+// from call e - 1 carry another call number.
+//
+// Stage buffer of each rank: [2 slots][world sources][rows][2 x row bytes] (the packed
+// rows are twice the activations). Every wait is bounded by `timeout_ns` of
+// %globaltimer; a block that gives up records NSLG_DEV_WAIT_TIMEOUT and leaves its rows
+// unwritten, so the context stays usable.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace nslg {
+namespace {
+
+constexpr int kGrid = 128;          // blocks per call, the same on every rank and call
+constexpr int kThreads = 256;
+constexpr int kVecPerThread = 4;    // 16-byte vectors of a row per thread (hidden <= 8192 bf16)
+static_assert(kGrid * 4 <= NSLG_TP_COUNTER_BYTES, "counter buffer too small");
+
+struct ArParams {
+  const void* partial;
+  int64_t p_stride;
+  uint8_t* stage[NSLG_TP_MAX_WORLD];
+  int64_t slot_bytes, region_bytes;
+  uint32_t* counters;
+  void* residual;
+  int64_t r_stride;
+  const void* weight;
+  void* out;
+  int64_t o_stride;
+  int rows, hidden, world, rank;
+  float eps;
+  uint64_t timeout_ns;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void st_relaxed_v4(void* p, uint4 v) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_relaxed_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+template <typename T, int VEC>
+union NVec {
+  uint4 u;
+  T e[VEC];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const ArParams p) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int nv = p.hidden / VEC;                  // 16-byte vectors per row
+  const int64_t units_per_row = 2 * static_cast<int64_t>(nv);
+  uint32_t* counter = p.counters + blockIdx.x;
+  const uint32_t call = *reinterpret_cast<volatile uint32_t*>(counter) + 1;
+  const int64_t slot_off = (call & 1u) * p.slot_bytes;
+  __shared__ volatile int bad;      // a wait of this block gave up: the others stop too
+  __shared__ float red[kThreads / 32];
+  if (threadIdx.x == 0) bad = 0;
+
+  // 1. push this rank's partial rows, packed with the call number, to every peer
+  for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.partial) +
+                                                      row * p.p_stride);
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      const uint4 v = src[i];
+      const uint4 u0 = make_uint4(v.x, call, v.y, call), u1 = make_uint4(v.z, call, v.w, call);
+      for (int d = 0; d < p.world; ++d) {
+        if (d == p.rank) continue;
+        uint4* dst = reinterpret_cast<uint4*>(p.stage[d] + slot_off + p.rank * p.region_bytes) +
+                     row * units_per_row + 2 * i;
+        st_relaxed_v4(dst, u0);
+        st_relaxed_v4(dst + 1, u1);
+      }
+    }
+  }
+  __syncthreads();   // `bad` is initialised before anyone can set it
+
+  // 2. per row: wait for and sum every rank's words, then residual add and RMSNorm
+  const T* w = static_cast<const T*>(p.weight);
+  for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const uint4* mine = reinterpret_cast<const uint4*>(static_cast<const T*>(p.partial) +
+                                                       row * p.p_stride);
+    float acc[kVecPerThread][VEC];
+#pragma unroll
+    for (int k = 0; k < kVecPerThread; ++k) {
+      const int i = threadIdx.x + k * kThreads;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[k][j] = 0.f;
+      if (i >= nv) continue;
+      for (int s = 0; s < p.world; ++s) {
+        NVec<T, VEC> v;
+        if (s == p.rank) {
+          v.u = mine[i];
+        } else {
+          const uint4* q = reinterpret_cast<const uint4*>(p.stage[p.rank] + slot_off +
+                                                          s * p.region_bytes) +
+                           row * units_per_row + 2 * i;
+          uint4 a = ld_relaxed_v4(q), b = ld_relaxed_v4(q + 1);
+          if (!(a.y == call && a.w == call && b.y == call && b.w == call)) {
+            const uint64_t t0 = global_ns();
+            while (true) {
+              a = ld_relaxed_v4(q);
+              b = ld_relaxed_v4(q + 1);
+              if (a.y == call && a.w == call && b.y == call && b.w == call) break;
+              if (bad) break;
+              if (global_ns() - t0 > p.timeout_ns) {
+                bad = 1;
+                report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+                break;
+              }
+            }
+          }
+          v.u = make_uint4(a.x, a.z, b.x, b.z);
+        }
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[k][j] = __fadd_rn(acc[k][j], Elem<T>::to_f(v.e[j]));
+      }
+    }
+    __syncthreads();
+    if (bad) break;     // block-uniform: a peer never delivered; nothing is written
+    T* res = static_cast<T*>(p.residual) + row * p.r_stride;
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kVecPerThread; ++k) {
+      const int i = threadIdx.x + k * kThreads;
+      if (i >= nv) continue;
+      NVec<T, VEC> r;
+      r.u = reinterpret_cast<const uint4*>(res)[i];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float sum = Elem<T>::round(acc[k][j]);              // the all-reduced output
+        r.e[j] = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(r.e[j]), sum));
+        const float h = Elem<T>::to_f(r.e[j]);
+        ss = fmaf(h, h, ss);
+      }
+      reinterpret_cast<uint4*>(res)[i] = r.u;
+    }
+    if (w == nullptr) continue;
+    // the same reduction tree as the rmsnorm kernel, so both give the same statistics
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+      float v = lane < kThreads / 32 ? red[lane] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(red[0], static_cast<float>(p.hidden)), p.eps));
+    T* out = static_cast<T*>(p.out) + row * p.o_stride;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      NVec<T, VEC> a, ww, o;
+      a.u = reinterpret_cast<const uint4*>(res)[i];
+      ww.u = reinterpret_cast<const uint4*>(w)[i];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float y = Elem<T>::round(__fmul_rn(Elem<T>::to_f(a.e[j]), inv));
+        o.e[j] = Elem<T>::from_f(__fmul_rn(Elem<T>::to_f(ww.e[j]), y));
+      }
+      reinterpret_cast<uint4*>(out)[i] = o.u;
+    }
+    __syncthreads();   // red[] is rewritten by the next row
+  }
+  // 3. this block's call count (read by the next launch on this stream)
+  if (threadIdx.x == 0) *counter = call;
+}
+
+}  // namespace
+}  // namespace nslg
+
+using namespace nslg;
+
+extern "C" int nslg_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle_out) {
+  if (bytes <= 0 || dev_ptr == nullptr || handle_out == nullptr)
+    return set_error(NSLG_ERR_ARG, "ipc_alloc: bytes must be > 0 and pointers non-null");
+  void* p = nullptr;
+  cudaError_t err = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("ipc_alloc: ") + cudaGetErrorString(err));
+  err = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (err == cudaSuccess) err = cudaDeviceSynchronize();
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return set_error(NSLG_ERR_CUDA, std::string("ipc_alloc: ") + cudaGetErrorString(err));
+  }
+  *dev_ptr = p;
+  return NSLG_OK;
+}
+
+extern "C" int nslg_ipc_open(const void* handle, void** dev_ptr) {
+  if (handle == nullptr || dev_ptr == nullptr) return set_error(NSLG_ERR_ARG, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t err = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("ipc_open: ") + cudaGetErrorString(err));
+  return NSLG_OK;
+}
+
+extern "C" int nslg_ipc_close(void* dev_ptr) {
+  const cudaError_t err = cudaIpcCloseMemHandle(dev_ptr);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("ipc_close: ") + cudaGetErrorString(err));
+  return NSLG_OK;
+}
+
+extern "C" int nslg_ipc_free(void* dev_ptr) {
+  const cudaError_t err = cudaFree(dev_ptr);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("ipc_free: ") + cudaGetErrorString(err));
+  return NSLG_OK;
+}
+
+extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int world, int rank,
+                                         const void* partial, int64_t partial_stride,
+                                         void* const* stage_bufs, int64_t stage_bytes,
+                                         void* counters, void* residual, int64_t residual_stride,
+                                         const void* weight, void* out, int64_t out_stride,
+                                         float eps, int64_t timeout_ns, uint32_t* dev_status,
+                                         void* stream) {
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F32)
+    return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad dtype");
+  if (world < 2 || world > NSLG_TP_MAX_WORLD || rank < 0 || rank >= world)
+    return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: need 2 <= world <= 8 and 0 <= rank < world");
+  if (rows < 0 || hidden <= 0) return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad shape");
+  const int esz = dtype == NSLG_DTYPE_BF16 ? 2 : 4;
+  if ((static_cast<int64_t>(hidden) * esz) % 16)
+    return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: hidden * element size must be a multiple of 16 bytes");
+  if (static_cast<int64_t>(hidden) * esz > 16ll * kThreads * kVecPerThread)
+    return set_error(NSLG_ERR_UNSUPPORTED, "tp_allreduce_rmsnorm: rows longer than 16 KiB");
+  if (!partial || !stage_bufs || !counters || !residual || (weight && !out))
+    return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: null pointer");
+  // [2 slots][world][rows][2 * row bytes]
+  const int64_t row_bytes = static_cast<int64_t>(hidden) * esz;
+  const int64_t region = (stage_bytes / 2 / world) & ~static_cast<int64_t>(15);
+  if (2 * row_bytes * rows > region)
+    return set_error(NSLG_ERR_WORKSPACE, "tp_allreduce_rmsnorm: " + std::to_string(rows) +
+                                             " rows need " + std::to_string(4 * row_bytes * rows * world) +
+                                             " stage bytes per rank, have " + std::to_string(stage_bytes));
+  if (timeout_ns <= 0) return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: timeout_ns must be > 0");
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (!a16(partial) || !a16(residual) || !a16(counters) || (weight && (!a16(weight) || !a16(out))) ||
+      (partial_stride * esz) % 16 || (residual_stride * esz) % 16 || (weight && (out_stride * esz) % 16))
+    return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: rows must be 16-byte aligned");
+  ArParams p{};
+  for (int i = 0; i < world; ++i) {
+    if (!stage_bufs[i] || !a16(stage_bufs[i]))
+      return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad stage buffer");
+    p.stage[i] = static_cast<uint8_t*>(stage_bufs[i]);
+  }
+  p.partial = partial;
+  p.p_stride = partial_stride;
+  p.region_bytes = region;
+  p.slot_bytes = region * world;
+  p.counters = static_cast<uint32_t*>(counters);
+  p.residual = residual;
+  p.r_stride = residual_stride;
+  p.weight = weight;
+  p.out = out;
+  p.o_stride = out_stride;
+  p.rows = rows;
+  p.hidden = hidden;
+  p.world = world;
+  p.rank = rank;
+  p.eps = eps;
+  p.timeout_ns = static_cast<uint64_t>(timeout_ns);
+  p.status = dev_status;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == NSLG_DTYPE_BF16)
+    tp_allreduce_rmsnorm_kernel<__nv_bfloat16><<<kGrid, kThreads, 0, st>>>(p);
+  else
+    tp_allreduce_rmsnorm_kernel<float><<<kGrid, kThreads, 0, st>>>(p);
+  return check_launch("tp_allreduce_rmsnorm");
+}

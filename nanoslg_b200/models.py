@@ -38,8 +38,12 @@ class RMSNorm(nn.Module):
     def forward(self, x):
         return ops.rmsnorm_residual(x, self.weight, self.eps)
 
-    def add_forward(self, x, residual):
-        """residual <- x + residual (in place); returns (rmsnorm(residual), residual)."""
+    def add_forward(self, x, residual, peer=None):
+        """residual <- x + residual (in place); returns (rmsnorm(residual), residual).
+        With an active PeerAllReduce ``peer``, ``x`` is this rank's partial RowParallel
+        output and is summed over the TP group first (one fused kernel)."""
+        if peer is not None:
+            return peer.allreduce_add_norm(x, residual, self.weight, self.eps), residual
         out = ops.rmsnorm_residual(x, self.weight, self.eps, residual=residual)
         return out, residual
 
@@ -190,14 +194,17 @@ class TPTransformerBlock(nn.Module):
         self.input_layernorm = RMSNorm(config.hidden_size, eps=eps)
         self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=eps)
 
+    peer_reduce = None      # PeerAllReduce of the TP group (enable_peer_allreduce)
+
     def forward(self, x, cos, sin, cache_ctx, residual=None):
+        peer = self.peer_reduce if self.peer_reduce is not None and self.peer_reduce.active else None
         if residual is None:
             residual = x.clone()
             h = self.input_layernorm(x)
         else:
-            h, residual = self.input_layernorm.add_forward(x, residual)
+            h, residual = self.input_layernorm.add_forward(x, residual, peer)
         a = self.self_attn(h, cos, sin, cache_ctx)
-        h, residual = self.post_attention_layernorm.add_forward(a, residual)
+        h, residual = self.post_attention_layernorm.add_forward(a, residual, peer)
         return self.mlp(h), residual
 
 
@@ -236,22 +243,33 @@ class _LlamaStage(nn.Module):
         self.cos = cos.to(self.device)
         self.sin = sin.to(self.device)
 
+    peer_reduce = None      # PeerAllReduce of the TP group (enable_peer_allreduce)
+
     def forward(self, x, cache_ctx, mask=None, last_only=False):
         """Reference semantics (models.py:272-276): logits for every input position.
         ``last_only`` computes the final norm and LM head for the last position only
         (the only one the decode loop reads), which saves the [B, S, vocab] logits of a
         long prefill."""
         h = self.embed_tokens(x) if self.is_first and x.dtype == torch.long else x
+        peer = self.peer_reduce
+        if peer is not None:
+            # the same decision on every TP rank: they run the same shapes
+            peer.active = peer.fits(h.shape[0] * h.shape[1])
+            peer = peer if peer.active else None
         residual = None
         for layer in self.layers:
             h, residual = layer(h, self.cos, self.sin, cache_ctx, residual)
         if residual is not None:
-            # the stage's output is the residual stream after its last block
+            # the stage's output is the residual stream after its last block (with an
+            # active peer reduction, h is still this rank's partial down_proj output;
+            # slicing the last position commutes with the sum)
             if self.is_last:
                 if last_only:
                     h, residual = h[:, -1:].contiguous(), residual[:, -1:].contiguous()
-                h, _ = self.norm.add_forward(h, residual)
+                h, _ = self.norm.add_forward(h, residual, peer)
                 return self.lm_head(h)
+            if peer is not None:
+                return peer.allreduce_add_norm(h, residual, None, 0.0)
             return _add(h, residual)
         if self.is_last and last_only:
             h = h[:, -1:].contiguous()
@@ -260,6 +278,18 @@ class _LlamaStage(nn.Module):
 
 def _add(a, b):
     return b.add_(a)
+
+
+def enable_peer_allreduce(model, peer):
+    """Routes the RowParallel reductions of ``model`` (o_proj, down_proj) through
+    ``peer`` (a tp_comm.PeerAllReduce of this rank's TP group) for forwards whose rows
+    fit its buffers; ``None`` restores the NCCL all-reduce everywhere."""
+    model.peer_reduce = peer
+    for layer in model.layers:
+        layer.peer_reduce = peer
+        layer.self_attn.o_proj.peer_reduce = peer
+        layer.mlp.down_proj.peer_reduce = peer
+    return model
 
 
 def fuse_projections(model):

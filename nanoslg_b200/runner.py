@@ -48,7 +48,8 @@ class LlamaRunner:
     stage broadcasts the greedy tokens to every rank."""
 
     def __init__(self, hf_config, device, dtype=torch.bfloat16, tp_size=1, rank=0,
-                 max_kv_pages=0, page_size=16, prefix_caching=True, seed=0, pp_size=1):
+                 max_kv_pages=0, page_size=16, prefix_caching=True, seed=0, pp_size=1,
+                 peer_allreduce=True, peer_max_rows=256):
         self.device = torch.device(device)
         self.dtype = dtype
         world = tp_size * pp_size
@@ -75,6 +76,14 @@ class LlamaRunner:
         models.init_random_(self.model, seed=seed + ctx.tp_rank)
         models.fuse_projections(self.model)
         self.model.eval()
+        # decode-sized RowParallel reductions over NVLink peer memory, fused with the
+        # residual add and RMSNorm (tp_comm.PeerAllReduce); prefill keeps NCCL
+        self.peer = None
+        if tp_size > 1 and peer_allreduce:
+            from .tp_comm import PeerAllReduce
+            self.peer = PeerAllReduce(ctx.tp_group, ctx.tp_rank, tp_size, self.device,
+                                      peer_max_rows, hf_config.hidden_size, dtype)
+            models.enable_peer_allreduce(self.model, self.peer)
         mc = SimpleNamespace(page_size=page_size, max_kv_pages=max_kv_pages,
                              enable_prefix_caching=prefix_caching)
         self.cache = create_cache_manager(hf_config, self.pcfg, self.device, dtype, mc,
@@ -179,6 +188,9 @@ class LlamaRunner:
         self.model = None
         self.cache = None
         torch.cuda.synchronize(self.device)
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
         torch.cuda.empty_cache()
 
     def release(self, generated=None):

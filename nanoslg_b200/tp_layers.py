@@ -59,9 +59,16 @@ class RowParallelLinear(nn.Module):
         else:
             nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
 
+    # A PeerAllReduce set here (models.enable_peer_allreduce) takes over the reduction
+    # while it is active: forward returns this rank's partial product and the RMSNorm
+    # that consumes it sums the partials, adds the residual and normalises in one kernel.
+    peer_reduce = None
+
     def forward(self, x):
         out = F.linear(x, self.weight)
         if self.tp_size > 1:
+            if self.peer_reduce is not None and self.peer_reduce.active and self.bias is None:
+                return out
             out = all_reduce_tp(out)
         if self.bias is not None:
             out = out + self.bias
