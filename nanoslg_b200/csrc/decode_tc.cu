@@ -44,6 +44,7 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMinPagesPerCta = 2;
 constexpr int kBoxBytes = kPS * 64 * 2;  // one [16 x 64] bf16 box: 2 KiB
 constexpr int kMaxSmem = 232448;         // 227 KiB opt-in per CTA on sm_100
+constexpr int kSmemCsrBatch = 1024;      // batches up to this size keep the CSR in smem
 
 struct DecodeParams {
   const __nv_bfloat16* q;
@@ -55,6 +56,7 @@ struct DecodeParams {
   float* part_lse;  // [slots, hq]
   int64_t q_stride, out_stride, num_pages;
   int batch, hq, group, stages, grid;
+  int smem_csr;       // kv_indptr and kv_last_page_len are staged in shared memory
   int box_all_heads;  // tensor maps with a [64 dim x 16 tok x HKV head] box (token-major)
   float scale_log2;
   uint32_t* status;
@@ -106,7 +108,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + stages;
   float* comb = reinterpret_cast<float*>(empty + stages);  // [8 warps][G][D] o, then m, l
 
-  const int64_t total = p.indptr[p.batch];
+  // The CSR lookups (slice bounds, sequence of a page, segment ends, last-page lengths)
+  // are chains of dependent loads; with the arrays in shared memory (one coalesced load
+  // by the whole CTA) they no longer delay the first TMA issue or each new segment.
+  const int32_t* indptr = p.indptr;
+  const int32_t* lpl = p.lpl;
+  if (p.smem_csr) {
+    int32_t* s_ip = reinterpret_cast<int32_t*>(
+        reinterpret_cast<uint8_t*>(comb) +
+        (C::kPPS > 1 ? static_cast<size_t>(kConsumerWarps) * p.group * (D + 2) * 4 : 0));
+    int32_t* s_lpl = s_ip + p.batch + 1;
+    for (int i = threadIdx.x; i <= p.batch; i += blockDim.x) s_ip[i] = p.indptr[i];
+    for (int i = threadIdx.x; i < p.batch; i += blockDim.x) s_lpl[i] = p.lpl[i];
+    __syncthreads();
+    indptr = s_ip;
+    lpl = s_lpl;
+  }
+
+  const int64_t total = indptr[p.batch];
   const int n = num_ctas(total, p.grid);
   const int c = blockIdx.x;
   if (c >= n) return;
@@ -128,88 +147,91 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
-    if (lane != 0) return;
+    // The whole warp issues the TMA boxes of a stage (lane L takes boxes L, L + 32, ...),
+    // so stages of many small boxes (few kv heads) go out in a few instructions; lane jj
+    // holds the page id of the stage's page jj.
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
     const uint64_t policy = l2_policy_evict_first();
+    constexpr int kHB = 1;  // boxes per (page, K/V, half) with the all-heads map
     int stage = 0;
     uint32_t phase = 0;
-    uint32_t armed[4] = {0u, 0u, 0u, 0u};  // arms of each stage's full barrier
+    uint32_t armed[4] = {0u, 0u, 0u, 0u};  // arms of each stage's full barrier (lane 0)
     // Stages in order: (first flat page, page count) over the segments of this CTA's
     // slice. The page ids of the next stage are loaded one stage ahead so their latency
     // overlaps the wait for a free stage.
-    int b = seq_of(p.indptr, p.batch, p0);
-    int64_t seg_end = min(p1, static_cast<int64_t>(p.indptr[b + 1]));
+    int b = seq_of(indptr, p.batch, p0);
+    int64_t seg_end = min(p1, static_cast<int64_t>(indptr[b + 1]));
     int64_t cursor = p0;
     auto next_stage = [&](int64_t& q0, int& np) -> bool {
       if (cursor >= p1) return false;
       if (cursor >= seg_end) {
         ++b;
-        while (b < p.batch && p.indptr[b + 1] <= cursor) ++b;
-        seg_end = min(p1, static_cast<int64_t>(p.indptr[b + 1]));
+        while (b < p.batch && indptr[b + 1] <= cursor) ++b;
+        seg_end = min(p1, static_cast<int64_t>(indptr[b + 1]));
       }
       q0 = cursor;
       np = static_cast<int>(min(static_cast<int64_t>(C::kPPS), seg_end - cursor));
       cursor += np;
       return true;
     };
-    int ids[C::kPPS];
     int64_t q0 = 0;
     int np = 0;
     bool have = next_stage(q0, np);
-#pragma unroll
-    for (int jj = 0; jj < C::kPPS; ++jj) ids[jj] = (have && jj < np) ? p.indices[q0 + jj] : 0;
+    int my_id = (have && lane < np) ? p.indices[q0 + lane] : 0;
     while (have) {
       int64_t nq0 = 0;
       int nnp = 0;
       const bool nhave = next_stage(nq0, nnp);
-      int nids[C::kPPS];
-#pragma unroll
-      for (int jj = 0; jj < C::kPPS; ++jj) nids[jj] = (nhave && jj < nnp) ? p.indices[nq0 + jj] : 0;
-      if (!mbar_wait(&empty[stage], phase ^ 1)) {
-        report(p.status, NSLG_DEV_WAIT_TIMEOUT);
-        // The consumers stopped releasing stages. Issue nothing more, wait (bounded)
-        // for the loads already in flight, and leave.
-        for (int s = 0; s < stages; ++s)
-          if (armed[s] > 0) (void)mbar_wait(&full[s], (armed[s] - 1) & 1);
+      const int my_nid = (nhave && lane < nnp) ? p.indices[nq0 + lane] : 0;
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1))) {
+        if (lane == 0) {
+          report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+          // The consumers stopped releasing stages. Issue nothing more, wait (bounded)
+          // for the loads already in flight, and leave.
+          for (int s = 0; s < stages; ++s)
+            if (armed[s] > 0) (void)mbar_wait(&full[s], (armed[s] - 1) & 1);
+        }
         return;
       }
-      mbar_arrive_expect_tx(&full[stage], np * 2 * C::kHalves * HKV * kBoxBytes);
-      ++armed[stage];
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[stage], np * 2 * C::kHalves * HKV * kBoxBytes);
+        ++armed[stage];
+      }
+      __syncwarp();
+      if (lane < np && (my_id < 0 || my_id >= p.num_pages)) {
+        report(p.status, NSLG_DEV_BAD_PAGE);
+        my_id = 0;  // keep the transaction count; page 0 is the pool's null page
+      }
       uint8_t* sb = smem + stage * C::kStageBytes;
-#pragma unroll
-      for (int jj = 0; jj < C::kPPS; ++jj) {
-        if (jj >= np) break;
-        int pid = ids[jj];
-        if (pid < 0 || pid >= p.num_pages) {
-          report(p.status, NSLG_DEV_BAD_PAGE);
-          pid = 0;  // keep the transaction count; page 0 is the pool's null page
-        }
-#pragma unroll
-        for (int half = 0; half < C::kHalves; ++half) {
-          if (p.box_all_heads) {
-            // one box covers every kv head of the page half (token-major map)
-            tma_load_3d(sb + C::box(jj, 0, half, 0), &tmap_k, &full[stage], half * 64,
-                        pid * kPS, 0, policy);
-            tma_load_3d(sb + C::box(jj, 1, half, 0), &tmap_v, &full[stage], half * 64,
-                        pid * kPS, 0, policy);
-          } else {
-#pragma unroll
-            for (int h = 0; h < HKV; ++h) {
-              tma_load_3d(sb + C::box(jj, 0, half, h), &tmap_k, &full[stage], half * 64, h,
-                          pid * kPS, policy);
-              tma_load_3d(sb + C::box(jj, 1, half, h), &tmap_v, &full[stage], half * 64, h,
-                          pid * kPS, policy);
-            }
-          }
+      const int per_page = 2 * C::kHalves * (p.box_all_heads ? kHB : HKV);
+      const int nbox = np * per_page;
+      // every lane runs the same rounds (the shuffle needs the whole warp)
+      for (int k0 = 0; k0 < C::kPPS * per_page; k0 += 32) {
+        const int k = k0 + lane;
+        const int jj = min(k / per_page, C::kPPS - 1);
+        const int pid = __shfl_sync(0xffffffffu, my_id, jj);
+        if (k >= nbox) continue;
+        int r = k - jj * per_page;
+        const int kv = r & 1;
+        r >>= 1;
+        const CUtensorMap* map = kv ? &tmap_v : &tmap_k;
+        if (p.box_all_heads) {
+          // one box covers every kv head of the page half (token-major map)
+          const int half = r;
+          tma_load_3d(sb + C::box(jj, kv, half, 0), map, &full[stage], half * 64, pid * kPS, 0,
+                      policy);
+        } else {
+          const int half = r % C::kHalves, h = r / C::kHalves;
+          tma_load_3d(sb + C::box(jj, kv, half, h), map, &full[stage], half * 64, h, pid * kPS,
+                      policy);
         }
       }
       if (++stage == stages) { stage = 0; phase ^= 1; }
       have = nhave;
       q0 = nq0;
       np = nnp;
-#pragma unroll
-      for (int jj = 0; jj < C::kPPS; ++jj) ids[jj] = nids[jj];
+      my_id = my_nid;
     }
     return;
   }
@@ -224,13 +246,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   int stage = 0;
   uint32_t phase = 0;
   bool ok = true;
-  int b = seq_of(p.indptr, p.batch, p0);
+  int b = seq_of(indptr, p.batch, p0);
   for (int64_t pp = p0; pp < p1;) {
-    const int64_t seq_beg = p.indptr[b];
-    const int64_t seq_end = p.indptr[b + 1];
+    const int64_t seq_beg = indptr[b];
+    const int64_t seq_end = indptr[b + 1];
     const int64_t seg_beg = pp;
     const int64_t seg_end = min(p1, seq_end);
-    const int last_len = p.lpl[b];
+    const int last_len = lpl[b];
 
     // Q fragments (A operand, 16 rows = query heads h*G + r, r < G).
     uint32_t qa[KS][4];
@@ -427,19 +449,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if constexpr (C::kPPS > 1) named_barrier_sync(1, kConsumerWarps * 32);
     ++b;
-    while (b < p.batch && p.indptr[b + 1] <= pp) ++b;
+    while (b < p.batch && indptr[b + 1] <= pp) ++b;
   }
 }
 
 // Combines the partials of sequences that span several CTAs; one warp per
 // (sequence, query head). Sequences finished in place by the decode kernel, and
-// sequences without pages (written as zeros here), need no merge.
+// sequences without pages (written as zeros here), need no merge. The lanes read the
+// partials' log-sum-exps in parallel (lane i: partial i, i + 32, ...) and the weighted
+// partial outputs are loaded four partials at a time, so the merge costs a few load
+// latencies however many CTAs the sequence spans.
 template <int D>
 __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int hq = blockIdx.x * 4 + warp;
   const int b = blockIdx.y;
   constexpr int DV = D / 32;
+  static_assert(DV == 4 || DV == 2, "head_dim 128 or 64");
   // the CSR is an input of both kernels: read it before waiting for the decode grid
   const int64_t total = p.indptr[p.batch];
   const int64_t beg = p.indptr[b], end = p.indptr[b + 1];
@@ -454,21 +480,45 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
   const int n = num_ctas(total, p.grid);
   const int cf = cta_of(beg, total, n), cl = cta_of(end - 1, total, n);
   if (cf == cl) return;
+  const int cnt = cl - cf + 1;
+  auto lse_of = [&](int i) {   // partial i of this sequence (CTA cf + i)
+    return p.part_lse[(static_cast<int64_t>(b) + cf + i) * p.hq + hq];
+  };
   float mx = -INFINITY;
-  for (int c = cf; c <= cl; ++c) mx = fmaxf(mx, p.part_lse[(static_cast<int64_t>(b) + c) * p.hq + hq]);
+  for (int i = lane; i < cnt; i += 32) mx = fmaxf(mx, lse_of(i));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float acc[DV];
 #pragma unroll
   for (int e = 0; e < DV; ++e) acc[e] = 0.f;
   float wsum = 0.f;
-  for (int c = cf; c <= cl; ++c) {
-    const int64_t slot = static_cast<int64_t>(b) + c;
-    const float lse = p.part_lse[slot * p.hq + hq];
-    const float w = lse == -INFINITY ? 0.f : fast_exp2(lse - mx);
+  for (int base = 0; base < cnt; base += 32) {
+    const int i = base + lane;
+    const float l = i < cnt ? lse_of(i) : -INFINITY;
+    const float w = l == -INFINITY ? 0.f : fast_exp2(l - mx);
     wsum += w;
-    const float* po = p.part_o + (slot * p.hq + hq) * D + lane * DV;
-#pragma unroll
-    for (int e = 0; e < DV; ++e) acc[e] = fmaf(w, po[e], acc[e]);
+    const int m = min(32, cnt - base);
+    const float* po0 = p.part_o + ((static_cast<int64_t>(b) + cf + base) * p.hq + hq) * D + lane * DV;
+    const int64_t step = static_cast<int64_t>(p.hq) * D;   // from one partial to the next
+#pragma unroll 4
+    for (int k = 0; k < m; ++k) {
+      const float wk = __shfl_sync(0xffffffffu, w, k);
+      const float* po = po0 + k * step;
+      if constexpr (DV == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(po);
+        acc[0] = fmaf(wk, v.x, acc[0]);
+        acc[1] = fmaf(wk, v.y, acc[1]);
+        acc[2] = fmaf(wk, v.z, acc[2]);
+        acc[3] = fmaf(wk, v.w, acc[3]);
+      } else {
+        const float2 v = *reinterpret_cast<const float2*>(po);
+        acc[0] = fmaf(wk, v.x, acc[0]);
+        acc[1] = fmaf(wk, v.y, acc[1]);
+      }
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
   for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(acc[e] * inv);
@@ -480,12 +530,15 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
                  cudaStream_t stream) {
   using C = Cfg<HKV, D>;
   const size_t comb = C::kPPS > 1 ? static_cast<size_t>(kConsumerWarps) * p.group * (D + 2) * 4 : 0;
-  const size_t fixed = 1024 + comb + 2 * 8 * 8;
+  p.smem_csr = p.batch <= kSmemCsrBatch ? 1 : 0;
+  const size_t csr = p.smem_csr ? static_cast<size_t>(2 * p.batch + 1) * 4 : 0;
+  const size_t fixed = 1024 + comb + csr + 2 * 8 * 8;
   int stages = static_cast<int>((kMaxSmem - fixed) / C::kStageBytes);
   if (stages > 4) stages = 4;
   if (stages < 2) return set_error(NSLG_ERR_UNSUPPORTED, "decode: group too large for smem");
   p.stages = stages;
-  const size_t smem = 1024 + static_cast<size_t>(stages) * C::kStageBytes + 2 * stages * 8 + comb;
+  const size_t smem =
+      1024 + static_cast<size_t>(stages) * C::kStageBytes + 2 * stages * 8 + comb + csr;
   auto kern = decode_tc_kernel<HKV, D>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
