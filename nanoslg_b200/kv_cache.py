@@ -427,7 +427,8 @@ class B200CacheContext(CacheContext):
     (all counts == 1) or prefill kernel; no Python loop runs per layer.
     """
 
-    def __init__(self, cache: "B200PagedKVCache", seq_ids, new_token_counts, input_offsets):
+    def __init__(self, cache: "B200PagedKVCache", seq_ids, new_token_counts, input_offsets,
+                 states=None):
         self.cache = cache
         self.seq_ids = seq_ids
         self.new_token_counts = new_token_counts
@@ -438,7 +439,8 @@ class B200CacheContext(CacheContext):
         ps = cfg.page_size
         dev = cfg.device
 
-        self.start_positions = [cache.seqs[s].num_tokens for s in seq_ids]
+        sts = states if states is not None else [cache.seqs[s] for s in seq_ids]
+        self.start_positions = [st.num_tokens for st in sts]
         self.seq_lens = [self.start_positions[i] + new_token_counts[i] for i in range(B)]
         self.max_kv_len = max(self.seq_lens) if self.seq_lens else 0
         self._is_decode = all(n == 1 for n in new_token_counts)
@@ -446,13 +448,55 @@ class B200CacheContext(CacheContext):
                     if B else 1)
         iw = self._iw
 
+        # Decode fast path: one new token per sequence, every target page allocated and
+        # private (no copy-on-write): the write targets are whole-batch array arithmetic.
+        # Anything else takes the general loop below.
+        self._wi = None
+        self._wi_src = None
+        fast = self._is_decode and iw == 1 and B > 0
+        if fast:
+            rc = pool.ref_count
+            pids = []
+            for st, start in zip(sts, self.start_positions):
+                bt = st.block_table
+                pi = start // ps
+                if pi >= len(bt) or rc[bt[pi]] > 1:
+                    fast = False
+                    break
+                pids.append(bt[pi])
+        if fast:
+            start = np.asarray(self.start_positions, dtype=np.int64)
+            slots = start % ps
+            positions = start.astype(np.int32).reshape(B, 1)
+            write_loc = (np.asarray(pids, dtype=np.int64) * ps + slots).astype(np.int32).reshape(B, 1)
+            tu = pool.tokens_used
+            for pid, used in zip(pids, (slots + 1).tolist()):
+                if tu[pid] < used:
+                    tu[pid] = used
+            self._wi_src = (pids, slots.tolist())
+        else:
+            positions, write_loc = self._general_write_targets(sts, new_token_counts, iw, ps)
+
+        self._finish_plan(B, iw, ps, sts, positions, write_loc, new_token_counts, dev)
+
+    @property
+    def _write_info(self) -> List[List[Tuple[int, int]]]:
+        """(page, slot) of every new token of every sequence (kv_cache.py:575-594)."""
+        if self._wi is None:
+            pids, slots = self._wi_src
+            self._wi = [[(p_, s_)] for p_, s_ in zip(pids, slots)]
+        return self._wi
+
+    def _general_write_targets(self, sts, new_token_counts, iw, ps):
         # write targets with copy-on-write, page by page in the reference's order
         # (kv_cache.py:575-594: the first token written into a shared page copies it)
+        B = self.batch_size
+        pool = self.cache.pool
         positions = np.zeros((B, iw), dtype=np.int32)
         write_loc = np.full((B, iw), -1, dtype=np.int32)
-        self._write_info: List[List[Tuple[int, int]]] = []
+        self._wi = []
         for b in range(B):
-            st = cache.seqs[seq_ids[b]]
+            st = sts[b]
             n = new_token_counts[b]
             o = self.input_offsets[b]
             start = st.num_tokens
@@ -479,8 +523,13 @@ class B200CacheContext(CacheContext):
                         pool.tokens_used[pid] = max(pool.tokens_used[pid], stop - pi * ps)
                     ap = stop
                 write_loc[b, o:o + n] = [p_ * ps + s_ for p_, s_ in info]
-            self._write_info.append(info)
+            self._wi.append(info)
+        return positions, write_loc
 
+    def _finish_plan(self, B, iw, ps, sts, positions, write_loc, new_token_counts, dev):
+        cache = self.cache
+        cfg = cache.cfg
+        pool = cache.pool
         # CSR page list (kv_cache.py:598-615)
         kv_lens = np.asarray(self.seq_lens, dtype=np.int64)
         npgs = (kv_lens + ps - 1) // ps
@@ -488,8 +537,8 @@ class B200CacheContext(CacheContext):
         indptr[1:] = np.cumsum(npgs)
         lpl = np.where(npgs > 0, kv_lens - (npgs - 1) * ps, 0).astype(np.int32)
         total = int(indptr[B])
-        indices = (np.concatenate([cache.seqs[s].block_table.prefix(int(n))
-                                   for s, n in zip(seq_ids, npgs)])
+        indices = (np.concatenate([st.block_table.prefix(n)
+                                   for st, n in zip(sts, npgs.tolist())])
                    if total else np.zeros(1, dtype=np.int32))
         qo = np.zeros(B + 1, dtype=np.int32)
         qo[1:] = np.cumsum(new_token_counts, dtype=np.int64) if B else []
@@ -502,23 +551,29 @@ class B200CacheContext(CacheContext):
         parts = [positions.ravel(), write_loc.ravel(), indptr, lpl[:max(B, 1)], qo, row_start,
                  indices]
         offs = np.cumsum([0] + [p.size for p in parts])
-        flat = np.concatenate(parts)
-        host = torch.from_numpy(flat)
+        size = int(offs[-1])
         dev_t = torch.device(dev) if dev is not None else torch.device("cpu")
         if dev_t.type == "cuda":
-            host = host.pin_memory()
+            # assembled straight into a reused pinned buffer (one host->device copy)
+            host = cache._pinned_plan(size)
+            np.concatenate(parts, out=host.numpy())
+        else:
+            host = torch.from_numpy(np.concatenate(parts))
+        flat_size = size
         pool.flush_zero()
-        static = cache.static_plan_for(B, iw, flat.size)
+        static = cache.static_plan_for(B, iw, flat_size)
         if static is not None:
-            static[:flat.size].copy_(host, non_blocking=True)
+            static[:flat_size].copy_(host, non_blocking=True)
             d = static
         else:
             d = host.to(dev_t, non_blocking=True)
+        if dev_t.type == "cuda":
+            cache._plan_copied()
         views = [d[offs[i]:offs[i + 1]] for i in range(len(parts))]
         (self._pos_i32, self._write_loc, self.kv_indptr, self.kv_last_page_len,
          self.qo_indptr, self.q_row_start, self.kv_indices) = views
         self.kv_last_page_len = self.kv_last_page_len[:max(B, 1)]
-        self._plan_bytes = flat.size * 4
+        self._plan_bytes = flat_size * 4
         self._pos64 = None
         self._sm_scale = 1.0 / math.sqrt(cfg.head_dim)
 
@@ -581,6 +636,8 @@ class B200PagedKVCache(KVCacheManager):
         self.tree = RadixTree(cfg.page_size, self.pool) if cfg.enable_prefix_caching else None
         self.seqs: Dict[str, _PagedSeqState] = {}
         self._static_plans: Dict[Tuple[int, int], torch.Tensor] = {}
+        self._pin_buf = None          # pinned host staging of the plan, reused per forward
+        self._pin_event = None        # recorded after the copy out of it
 
     def use_static_plan(self, batch, input_width=1, max_pages=None):
         """From now on, forwards of exactly (batch, input_width) put their plan into one
@@ -596,6 +653,24 @@ class B200PagedKVCache(KVCacheManager):
         if buf is not None and size > buf.numel():
             raise RuntimeError("plan larger than the static plan buffer")
         return buf
+
+    def _pinned_plan(self, size):
+        """A pinned int32 host buffer of ``size`` entries for this forward's plan; the
+        previous forward's copy out of it has completed before it is handed out again."""
+        buf = self._pin_buf
+        if buf is None or buf.numel() < size:
+            cap = max(size, 4096, 2 * (buf.numel() if buf is not None else 0))
+            if self._pin_event is not None:
+                self._pin_event.synchronize()
+            self._pin_buf = buf = torch.empty(cap, dtype=torch.int32).pin_memory()
+        elif self._pin_event is not None:
+            self._pin_event.synchronize()
+        return buf[:size]
+
+    def _plan_copied(self):
+        if self._pin_event is None:
+            self._pin_event = torch.cuda.Event()
+        self._pin_event.record(torch.cuda.current_stream(self.cfg.device))
 
     def allocate_sequence(self, seq_id, token_ids=None, num_tokens=0):
         tids = token_ids or []
@@ -622,9 +697,16 @@ class B200PagedKVCache(KVCacheManager):
             st.block_table.extend(self._alloc(need - len(st.block_table)))
 
     def begin_forward(self, seq_ids, ntoks, offsets=None):
-        for s, n in zip(seq_ids, ntoks):
-            self.extend_sequence(s, n)
-        return B200CacheContext(self, seq_ids, ntoks, offsets)
+        # extend_sequence for every sequence, inlined (sequences in order, so the page
+        # allocation order is the reference's)
+        sts = [self.seqs[s] for s in seq_ids]
+        ps = self.cfg.page_size
+        for st, n in zip(sts, ntoks):
+            bt = st.block_table
+            if st.num_tokens + n > len(bt) * ps:
+                need = -(-(st.num_tokens + n) // ps)
+                bt.extend(self._alloc(need - len(bt)))
+        return B200CacheContext(self, seq_ids, ntoks, offsets, sts)
 
     def end_forward(self, ctx):
         for b in range(ctx.batch_size):
