@@ -45,6 +45,7 @@ extern "C" {
 #define NSLG_DEV_BAD_SLOT 2u     /* write location outside the pool                    */
 #define NSLG_DEV_BAD_POSITION 4u /* RoPE position outside the cos/sin table            */
 #define NSLG_DEV_WAIT_TIMEOUT 8u /* a bounded pipeline wait gave up (kernel returned)  */
+#define NSLG_DEV_BAD_PLAN 16u    /* plan input outside the block tables / plan buffer   */
 
 /* Library version string. */
 const char* nslg_version(void);
@@ -178,6 +179,30 @@ int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x,
  */
 int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gate_up_stride,
                   void* out, int64_t out_stride, void* stream);
+
+/* Device-side plan of a decode step (every sequence adds one token).
+ *
+ * Replaces the per-forward plan of FlashInferCacheContext.__init__ and
+ * _plan_flashinfer (kv_cache.py:547-632) for decode steps: the host keeps the page
+ * bookkeeping and the block tables, and mirrors the tables into device memory
+ * (block_tables: bt_rows rows of bt_stride int32 page ids, one row per sequence "slot").
+ *   slots[b]     row of sequence b;  starts[b]  its token count before the step
+ *   updates      num_updates triples (slot, index, page id) written into the tables first
+ *                (pages added or copied on write since the last step)
+ * Outputs, all int32 device arrays, with the host plan's values:
+ *   positions[b] = starts[b];  write_loc[b] = page * page_size + starts[b] % page_size of
+ *   the page holding position starts[b];  kv_indptr[B+1], kv_indices (<= max_indices
+ *   entries), kv_last_page_len[B] of the sequences' first ceil((starts[b]+1)/page_size)
+ *   pages;  qo_indptr[b] = b (B+1 entries);  q_row_start[b] = b.
+ * Entries outside the tables or a page list longer than max_indices set
+ * NSLG_DEV_BAD_PLAN in *dev_status. batch <= 4096.
+ */
+int nslg_plan_decode(int batch, int page_size, const int32_t* slots, const int32_t* starts,
+                     int num_updates, const int32_t* updates, int32_t* block_tables,
+                     int64_t bt_stride, int64_t bt_rows, int32_t* positions, int32_t* write_loc,
+                     int32_t* kv_indptr, int32_t* kv_last_page_len, int32_t* qo_indptr,
+                     int32_t* q_row_start, int32_t* kv_indices, int64_t max_indices,
+                     uint32_t* dev_status, void* stream);
 
 /* ---------------------------------------------------------------- tensor parallel */
 

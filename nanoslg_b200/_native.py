@@ -23,6 +23,7 @@ DEV_BAD_PAGE = 1
 DEV_BAD_SLOT = 2
 DEV_BAD_POSITION = 4
 DEV_WAIT_TIMEOUT = 8
+DEV_BAD_PLAN = 16
 
 _i32, _i64, _f32, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -43,6 +44,8 @@ SIGNATURES = {
     "nslg_silu_mul": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp]),
     "nslg_rmsnorm_residual": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i64,
                                      _f32, _vp]),
+    "nslg_plan_decode": (_i32, [_i32, _i32, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _vp, _vp, _vp,
+                                _vp, _vp, _vp, _vp, _i64, _vp, _vp]),
     "nslg_ipc_alloc": (_i32, [_i64, ctypes.POINTER(_vp), _vp]),
     "nslg_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
     "nslg_ipc_close": (_i32, [_vp]),

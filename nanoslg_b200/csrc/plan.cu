@@ -1,0 +1,151 @@
+// Device-side planning of a decode step: the per-forward plan of
+// FlashInferCacheContext.__init__ + _plan_flashinfer (kv_cache.py:547-632) for the case
+// where every sequence adds one token, built on the GPU from block tables that live in
+// device memory.
+//
+// The host keeps the page bookkeeping (pool, radix tree, block tables) and sends, per
+// step, only the batch's table rows ("slots"), the sequences' token counts before the
+// step and the block-table entries that changed since the last step (new pages, copies
+// on write). Kernel 1 (one CTA) applies the changes, then computes every sequence's
+// position, write location (page * page_size + slot), page count and last-page length,
+// and the page-list offsets kv_indptr with a block-wide exclusive scan; kernel 2 (one
+// CTA per sequence) gathers each sequence's page ids into kv_indices. Output layout and
+// values are those of the host plan, element for element.
+#include "common.cuh"
+#include "launch.h"
+
+namespace nslg {
+namespace {
+
+constexpr int kScanThreads = 1024;
+constexpr int kMaxItems = 4;                 // sequences per scan thread (batch <= 4096)
+
+struct PlanParams {
+  int batch, page_size, num_updates;
+  const int32_t* slots;
+  const int32_t* starts;
+  const int32_t* updates;   // [num_updates][3] = (slot, index, page id)
+  int32_t* bt;
+  int64_t bt_stride, bt_rows;
+  int32_t *positions, *write_loc, *indptr, *lpl, *qo, *row_start, *indices;
+  int64_t max_indices;
+  uint32_t* status;
+};
+
+__global__ void __launch_bounds__(kScanThreads) plan_decode_scan_kernel(const PlanParams p) {
+  __shared__ int32_t warp_sums[kScanThreads / 32];
+  const int t = threadIdx.x, lane = t % 32, warp = t / 32;
+  // 1. block-table changes
+  for (int i = t; i < p.num_updates; i += kScanThreads) {
+    const int s = p.updates[3 * i], j = p.updates[3 * i + 1], pg = p.updates[3 * i + 2];
+    if (s >= 0 && s < p.bt_rows && j >= 0 && j < p.bt_stride)
+      p.bt[s * p.bt_stride + j] = pg;
+    else
+      report(p.status, NSLG_DEV_BAD_PLAN);
+  }
+  __syncthreads();
+  // 2. per-sequence values; thread t owns sequences [t * k, t * k + k)
+  const int k = (p.batch + kScanThreads - 1) / kScanThreads;
+  int npg[kMaxItems];
+  int local = 0;
+#pragma unroll
+  for (int e = 0; e < kMaxItems; ++e) {
+    const int b = t * k + e;
+    npg[e] = 0;
+    if (e >= k || b >= p.batch) continue;
+    const int s = p.slots[b];
+    const int pos = p.starts[b];
+    const int len = pos + 1;
+    const int n = (len + p.page_size - 1) / p.page_size;
+    const int pi = pos / p.page_size;
+    int loc = -1;
+    if (s >= 0 && s < p.bt_rows && pi < p.bt_stride) {
+      loc = p.bt[s * p.bt_stride + pi] * p.page_size + pos % p.page_size;
+    } else {
+      report(p.status, NSLG_DEV_BAD_PLAN);
+    }
+    p.positions[b] = pos;
+    p.write_loc[b] = loc;
+    p.lpl[b] = len - (n - 1) * p.page_size;
+    p.qo[b] = b;
+    p.row_start[b] = b;
+    npg[e] = n;
+    local += n;
+  }
+  // 3. exclusive scan of the page counts
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += v;
+    }
+    warp_sums[lane] = w;   // inclusive over warps
+  }
+  __syncthreads();
+  int run = incl - local + (warp > 0 ? warp_sums[warp - 1] : 0);
+#pragma unroll
+  for (int e = 0; e < kMaxItems; ++e) {
+    const int b = t * k + e;
+    if (e >= k || b >= p.batch) continue;
+    p.indptr[b] = run;
+    run += npg[e];
+  }
+  if (t == kScanThreads - 1) {
+    p.indptr[p.batch] = run;
+    p.qo[p.batch] = p.batch;
+    if (run > p.max_indices) report(p.status, NSLG_DEV_BAD_PLAN);
+  }
+}
+
+__global__ void __launch_bounds__(128) plan_decode_gather_kernel(const PlanParams p) {
+  const int b = blockIdx.x;
+  const int beg = p.indptr[b], end = p.indptr[b + 1];
+  const int s = p.slots[b];
+  if (s < 0 || s >= p.bt_rows || end - beg > p.bt_stride || end > p.max_indices) {
+    if (threadIdx.x == 0) report(p.status, NSLG_DEV_BAD_PLAN);
+    return;
+  }
+  const int32_t* row = p.bt + s * p.bt_stride;
+  for (int j = threadIdx.x; j < end - beg; j += blockDim.x) p.indices[beg + j] = row[j];
+}
+
+}  // namespace
+}  // namespace nslg
+
+using namespace nslg;
+
+extern "C" int nslg_plan_decode(int batch, int page_size, const int32_t* slots,
+                                const int32_t* starts, int num_updates, const int32_t* updates,
+                                int32_t* block_tables, int64_t bt_stride, int64_t bt_rows,
+                                int32_t* positions, int32_t* write_loc, int32_t* kv_indptr,
+                                int32_t* kv_last_page_len, int32_t* qo_indptr,
+                                int32_t* q_row_start, int32_t* kv_indices, int64_t max_indices,
+                                uint32_t* dev_status, void* stream) {
+  if (batch < 1 || batch > kScanThreads * kMaxItems)
+    return set_error(NSLG_ERR_UNSUPPORTED, "plan_decode: batch must be in [1, 4096]");
+  if (page_size <= 0 || bt_stride <= 0 || bt_rows <= 0 || num_updates < 0 || max_indices < 1)
+    return set_error(NSLG_ERR_ARG, "plan_decode: bad sizes");
+  if (bt_rows * bt_stride >= (int64_t{1} << 31))
+    return set_error(NSLG_ERR_UNSUPPORTED, "plan_decode: block tables larger than 2^31 entries");
+  if (!slots || !starts || (num_updates && !updates) || !block_tables || !positions ||
+      !write_loc || !kv_indptr || !kv_last_page_len || !qo_indptr || !q_row_start || !kv_indices)
+    return set_error(NSLG_ERR_ARG, "plan_decode: null pointer");
+  PlanParams p{batch, page_size, num_updates, slots, starts, updates, block_tables, bt_stride,
+               bt_rows, positions, write_loc, kv_indptr, kv_last_page_len, qo_indptr,
+               q_row_start, kv_indices, max_indices, dev_status};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  plan_decode_scan_kernel<<<1, kScanThreads, 0, st>>>(p);
+  int rc = check_launch("plan_decode_scan");
+  if (rc != NSLG_OK) return rc;
+  plan_decode_gather_kernel<<<batch, 128, 0, st>>>(p);
+  return check_launch("plan_decode_gather");
+}

@@ -358,10 +358,11 @@ class _BlockTable(list):
     list behaviour -- with an int32 numpy mirror kept in step on every append, extend and
     item assignment, so a forward's CSR page list is a concatenation of array prefixes
     instead of a Python loop over every page of every sequence."""
-    __slots__ = ("arr",)
+    __slots__ = ("arr", "dirty_from")
 
     def __init__(self, pages=()):
         super().__init__(pages)
+        self.dirty_from = 0    # entries [dirty_from, len) differ from the device copy
         self.arr = np.empty(max(16, 2 * len(self)), dtype=np.int32)
         if len(self):
             self.arr[:len(self)] = np.asarray(self, dtype=np.int32)
@@ -379,6 +380,8 @@ class _BlockTable(list):
         self._reserve(old + len(pages), old)
         super().extend(pages)
         self.arr[old:len(self)] = pages
+        if old < self.dirty_from:
+            self.dirty_from = old
 
     def append(self, page):
         self.extend([page])
@@ -388,8 +391,12 @@ class _BlockTable(list):
         if isinstance(i, slice):
             self._reserve(len(self), 0)
             self.arr[:len(self)] = np.asarray(self, dtype=np.int32)
+            self.dirty_from = 0
         else:
-            self.arr[i if i >= 0 else i + len(self)] = v
+            j = i if i >= 0 else i + len(self)
+            self.arr[j] = v
+            if j < self.dirty_from:
+                self.dirty_from = j
 
     def prefix(self, n):
         """int32 array of the first n page ids, 0 (the null page) past the end."""
@@ -399,9 +406,10 @@ class _BlockTable(list):
 
 
 class _PagedSeqState:
-    __slots__ = ("seq_id", "block_table", "num_tokens", "prefix_len", "token_ids")
+    __slots__ = ("seq_id", "block_table", "num_tokens", "prefix_len", "token_ids", "slot")
 
     def __init__(self, sid, prefix_pages=None, plen=0, tids=None):
+        self.slot = -1          # row of the device block tables (device planning)
         self.seq_id = sid
         self.block_table = _BlockTable(prefix_pages or [])
         self.num_tokens = plen
@@ -467,17 +475,34 @@ class B200CacheContext(CacheContext):
         if fast:
             start = np.asarray(self.start_positions, dtype=np.int64)
             slots = start % ps
-            positions = start.astype(np.int32).reshape(B, 1)
-            write_loc = (np.asarray(pids, dtype=np.int64) * ps + slots).astype(np.int32).reshape(B, 1)
             tu = pool.tokens_used
             for pid, used in zip(pids, (slots + 1).tolist()):
                 if tu[pid] < used:
                     tu[pid] = used
             self._wi_src = (pids, slots.tolist())
+            if cache.device_plan and B <= 4096:
+                # the plan arrays are built on the GPU from the device block tables
+                self._sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+                self._pos64 = None
+                cache._plan_decode_on_device(self, sts, start)
+                return
+            positions = start.astype(np.int32).reshape(B, 1)
+            write_loc = (np.asarray(pids, dtype=np.int64) * ps + slots).astype(np.int32).reshape(B, 1)
         else:
             positions, write_loc = self._general_write_targets(sts, new_token_counts, iw, ps)
 
         self._finish_plan(B, iw, ps, sts, positions, write_loc, new_token_counts, dev)
+
+    def _set_plan_views(self, d, B, iw, total):
+        """Slices the plan arrays out of the flat int32 device buffer ``d`` (layout of the
+        class docstring, page ids last)."""
+        sizes = [B * iw, B * iw, B + 1, max(B, 1), B + 1, B, total]
+        offs = np.cumsum([0] + sizes)
+        views = [d[offs[i]:offs[i + 1]] for i in range(len(sizes))]
+        (self._pos_i32, self._write_loc, self.kv_indptr, self.kv_last_page_len,
+         self.qo_indptr, self.q_row_start, self.kv_indices) = views
+        self.kv_last_page_len = self.kv_last_page_len[:max(B, 1)]
+        return int(offs[-1])
 
     @property
     def _write_info(self) -> List[List[Tuple[int, int]]]:
@@ -638,6 +663,14 @@ class B200PagedKVCache(KVCacheManager):
         self._static_plans: Dict[Tuple[int, int], torch.Tensor] = {}
         self._pin_buf = None          # pinned host staging of the plan, reused per forward
         self._pin_event = None        # recorded after the copy out of it
+        # device planning of decode steps (CUDA pools): block tables mirrored on the GPU,
+        # one row ("slot") per live sequence, rows reused after release
+        dev = torch.device(cfg.device) if cfg.device is not None else torch.device("cpu")
+        self.device_plan = dev.type == "cuda"
+        self._dbt = None              # int32 [rows, stride] device block tables
+        self._slot_free: List[int] = []
+        self._slot_next = 0
+        self._up_dev = None           # device copy of (slots, starts, table updates)
 
     def use_static_plan(self, batch, input_width=1, max_pages=None):
         """From now on, forwards of exactly (batch, input_width) put their plan into one
@@ -671,6 +704,80 @@ class B200PagedKVCache(KVCacheManager):
         if self._pin_event is None:
             self._pin_event = torch.cuda.Event()
         self._pin_event.record(torch.cuda.current_stream(self.cfg.device))
+
+    def _ensure_tables(self, rows, stride):
+        cur = self._dbt
+        r0, s0 = (cur.shape if cur is not None else (0, 0))
+        if rows <= r0 and stride <= s0:
+            return
+        nr = max(rows, r0 if rows <= r0 else 2 * r0, 64)
+        ns = max(stride, s0 if stride <= s0 else 2 * s0, 256)
+        new = torch.zeros((nr, ns), dtype=torch.int32, device=self.cfg.device)
+        if cur is not None:
+            new[:r0, :s0].copy_(cur)
+        self._dbt = new
+
+    def _plan_decode_on_device(self, ctx, sts, start):
+        """Fills ``ctx``'s plan views for a decode step with nslg_plan_decode: uploads the
+        batch's table rows, start positions and the block-table entries changed since the
+        last upload (one small host->device copy); the kernels build the rest."""
+        B = len(sts)
+        ps = self.cfg.page_size
+        slots = np.empty(B, dtype=np.int32)
+        upd = []
+        longest = 0
+        for b, st in enumerate(sts):
+            if st.slot < 0:
+                st.slot = self._slot_free.pop() if self._slot_free else self._slot_next
+                if st.slot == self._slot_next:
+                    self._slot_next += 1
+                st.block_table.dirty_from = 0
+            slots[b] = st.slot
+            bt = st.block_table
+            n = len(bt)
+            if n > longest:
+                longest = n
+            if bt.dirty_from < n:
+                d = bt.dirty_from
+                u = np.empty((n - d, 3), dtype=np.int32)
+                u[:, 0] = st.slot
+                u[:, 1] = np.arange(d, n, dtype=np.int32)
+                u[:, 2] = bt.arr[d:n]
+                upd.append(u)
+                bt.dirty_from = n
+        self._ensure_tables(self._slot_next, longest)
+        nu = sum(u.shape[0] for u in upd)
+        npgs = (start + ps) // ps                      # ceil((start + 1) / ps)
+        total = int(npgs.sum())
+        size_up = 2 * B + 3 * nu
+        host = self._pinned_plan(size_up)
+        hn = host.numpy()
+        hn[:B] = slots
+        hn[B:2 * B] = start
+        if nu:
+            np.concatenate(upd, out=hn[2 * B:].reshape(nu, 3))
+        if self._up_dev is None or self._up_dev.numel() < size_up:
+            self._up_dev = torch.empty(max(size_up, 4096, 2 * (self._up_dev.numel() if self._up_dev is not None else 0)),
+                                       dtype=torch.int32, device=self.cfg.device)
+        up = self._up_dev
+        up[:size_up].copy_(host, non_blocking=True)
+        self._plan_copied()
+        self.pool.flush_zero()
+        plan_size = 5 * B + 2 + max(B, 1) + total
+        static = self.static_plan_for(B, 1, plan_size)
+        d = static if static is not None else torch.empty(plan_size, dtype=torch.int32,
+                                                          device=self.cfg.device)
+        ctx._set_plan_views(d, B, 1, total)
+        ctx._plan_bytes = size_up * 4
+        dbt = self._dbt
+        from . import _native as N
+        N.call("nslg_plan_decode", B, ps, up.data_ptr(), up.data_ptr() + 4 * B, nu,
+               up.data_ptr() + 8 * B if nu else None, dbt.data_ptr(), dbt.shape[1], dbt.shape[0],
+               ctx._pos_i32.data_ptr(), ctx._write_loc.data_ptr(), ctx.kv_indptr.data_ptr(),
+               ctx.kv_last_page_len.data_ptr(), ctx.qo_indptr.data_ptr(),
+               ctx.q_row_start.data_ptr(), ctx.kv_indices.data_ptr(), max(total, 1),
+               ops.status_word(self.cfg.device).data_ptr(),
+               torch.cuda.current_stream(self.cfg.device).cuda_stream)
 
     def allocate_sequence(self, seq_id, token_ids=None, num_tokens=0):
         tids = token_ids or []
@@ -724,6 +831,8 @@ class B200PagedKVCache(KVCacheManager):
                 self.tree.dec_refs(st.token_ids[:st.prefix_len])
         for p in st.block_table:
             self.pool.release(p)
+        if st.slot >= 0:
+            self._slot_free.append(st.slot)
         del self.seqs[seq_id]
 
     def append_token_ids(self, seq_id, ids):

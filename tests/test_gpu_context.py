@@ -224,3 +224,63 @@ def test_runner_cuda_graph_decode_matches_reference_tokens():
         toks2.append(int(tok[0]))
     assert toks2 == want[8:16]
     r.release([toks2])
+
+
+def test_device_plan_matches_host_plan():
+    """nslg_plan_decode (device block tables, csrc/plan.cu) builds the same decode plan as
+    the host path (kv_cache.py:547-632 restated) over a run with page-boundary crossings,
+    sequences joining and leaving (table rows reused, tables grown) and radix-shared
+    prefixes (copy on write takes the host path for that step, then the device tables are
+    refreshed)."""
+    import random
+    from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
+    dev = torch.device("cuda:0")
+    cfg = dict(num_layers=1, num_kv_heads=2, num_qo_heads=4, head_dim=64, page_size=16,
+               max_pages=4096, dtype=torch.bfloat16, device=dev, enable_prefix_caching=True)
+    mgrs = [B200PagedKVCache(KVCacheConfig(**cfg)) for _ in range(2)]
+    mgrs[1].device_plan = False
+    assert mgrs[0].device_plan
+    rng = random.Random(3)
+    shared = [rng.randrange(1000) for _ in range(48)]
+    live, nxt = [], 0
+
+    def add(n_new):
+        nonlocal nxt
+        for _ in range(n_new):
+            sid = f"q{nxt}"
+            nxt += 1
+            if rng.random() < 0.3:      # a prompt starting with a page-aligned shared prefix
+                toks = shared + [rng.randrange(1000) for _ in range(rng.randrange(1, 40))]
+            else:
+                toks = [rng.randrange(1000) for _ in range(rng.randrange(1, 300))]
+            for m in mgrs:
+                m.allocate_sequence(sid, toks)
+                st = m.seqs[sid]
+                st.num_tokens = len(toks)        # prompt already cached
+            live.append(sid)
+
+    def drop(k):
+        for _ in range(k):
+            sid = live.pop(rng.randrange(len(live)))
+            for m in mgrs:
+                m.append_token_ids(sid, [1, 2, 3])
+                m.release_sequence(sid)
+
+    add(24)
+    fields = ("_pos_i32", "_write_loc", "kv_indptr", "kv_indices", "kv_last_page_len",
+              "qo_indptr", "q_row_start")
+    for step in range(60):
+        if step in (15, 35):
+            drop(8)
+            add(12)
+        ctxs = [m.begin_forward(list(live), [1] * len(live)) for m in mgrs]
+        for f in fields:
+            a, b = getattr(ctxs[0], f), getattr(ctxs[1], f)
+            assert a.tolist() == b.tolist(), f"step {step}: {f} differs"
+        assert ctxs[0]._write_info == ctxs[1]._write_info
+        assert [list(m.seqs[s].block_table) for s in live for m in mgrs[:1]] == \
+               [list(m.seqs[s].block_table) for s in live for m in mgrs[1:]]
+        for m, c in zip(mgrs, ctxs):
+            m.end_forward(c)
+    from nanoslg_b200 import ops
+    ops.check_device_status(dev)
