@@ -204,6 +204,13 @@ int nslg_plan_decode(int batch, int page_size, const int32_t* slots, const int32
                      int32_t* q_row_start, int32_t* kv_indices, int64_t max_indices,
                      uint32_t* dev_status, void* stream);
 
+/* Zeroes whole pages of a KV pool tensor [layers, num_pages, page elements]
+ * (page_bytes bytes per page and layer): every layer of pages[0 .. n). Replaces the
+ * page zeroing of PagePool.alloc (kv_cache.py:411), done once per forward for the pages
+ * allocated since the last one. */
+int nslg_zero_pages(const int32_t* pages, int num_pages_to_zero, void* pool, int64_t layers,
+                    int64_t num_pages, int64_t page_bytes, uint32_t* dev_status, void* stream);
+
 /* ---------------------------------------------------------------- tensor parallel */
 
 #define NSLG_IPC_HANDLE_BYTES 64   /* cudaIpcMemHandle_t                                 */

@@ -118,10 +118,43 @@ __global__ void __launch_bounds__(128) plan_decode_gather_kernel(const PlanParam
   for (int j = threadIdx.x; j < end - beg; j += blockDim.x) p.indices[beg + j] = row[j];
 }
 
+// Zeroes `pages` of a pool tensor [layers, pages_total, page elements]: block (i, l)
+// clears page pages[i] of layer l with 16-byte stores.
+__global__ void __launch_bounds__(256) zero_pages_kernel(const int32_t* pages, int n,
+                                                         uint8_t* pool, int64_t num_pages,
+                                                         int64_t layer_stride,
+                                                         int64_t page_bytes, uint32_t* status) {
+  const int i = blockIdx.x, l = blockIdx.y;
+  const int pg = pages[i];
+  if (pg < 0 || pg >= num_pages) {
+    if (threadIdx.x == 0) report(status, NSLG_DEV_BAD_PLAN);
+    return;
+  }
+  uint4* dst = reinterpret_cast<uint4*>(pool + l * layer_stride + pg * page_bytes);
+  const int64_t nv = page_bytes / 16;
+  for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) dst[v] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 }  // namespace
 }  // namespace nslg
 
 using namespace nslg;
+
+extern "C" int nslg_zero_pages(const int32_t* pages, int num_pages_to_zero, void* pool,
+                               int64_t layers, int64_t num_pages, int64_t page_bytes,
+                               uint32_t* dev_status, void* stream) {
+  if (num_pages_to_zero == 0) return NSLG_OK;
+  if (num_pages_to_zero < 0 || layers <= 0 || num_pages <= 0 || page_bytes <= 0 ||
+      page_bytes % 16 || layers > 65535)
+    return set_error(NSLG_ERR_ARG, "zero_pages: bad sizes");
+  if (!pages || !pool || (reinterpret_cast<uintptr_t>(pool) & 15u))
+    return set_error(NSLG_ERR_ARG, "zero_pages: null or misaligned pointer");
+  zero_pages_kernel<<<dim3(num_pages_to_zero, static_cast<unsigned>(layers)), 256, 0,
+                      static_cast<cudaStream_t>(stream)>>>(
+      pages, num_pages_to_zero, static_cast<uint8_t*>(pool), num_pages, num_pages * page_bytes,
+      page_bytes, dev_status);
+  return check_launch("zero_pages");
+}
 
 extern "C" int nslg_plan_decode(int batch, int page_size, const int32_t* slots,
                                 const int32_t* starts, int num_updates, const int32_t* updates,

@@ -25,6 +25,7 @@ from typing import Dict, List, Optional, Set, Tuple
 import numpy as np
 import torch
 
+from . import _native as N
 from . import ops
 
 
@@ -185,13 +186,21 @@ class PagePool:
             self._pending_zero.extend(out)
             return out
 
-    def flush_zero(self):
-        """Zeroes every page allocated since the last flush (all layers, K and V)."""
+    def take_pending_zero(self) -> List[int]:
+        """The pages allocated since the last flush (sorted, unique); the caller zeroes
+        them (nslg_zero_pages)."""
         with self._lock:
             if not self._pending_zero:
-                return
+                return []
             ids = sorted(set(self._pending_zero))
             self._pending_zero.clear()
+            return ids
+
+    def flush_zero(self):
+        """Zeroes every page allocated since the last flush (all layers, K and V)."""
+        ids = self.take_pending_zero()
+        if not ids:
+            return
         idx = torch.tensor(ids, dtype=torch.long).to(self.k.device, non_blocking=True)
         self.k.index_fill_(1, idx, 0)
         self.v.index_fill_(1, idx, 0)
@@ -670,7 +679,8 @@ class B200PagedKVCache(KVCacheManager):
         self._dbt = None              # int32 [rows, stride] device block tables
         self._slot_free: List[int] = []
         self._slot_next = 0
-        self._up_dev = None           # device copy of (slots, starts, table updates)
+        self._up_dev = None           # device copy of (slots, starts, table updates, zeroes)
+        self._plan_dev = None         # device plan buffer of the forwards without a static one
 
     def use_static_plan(self, batch, input_width=1, max_pages=None):
         """From now on, forwards of exactly (batch, input_width) put their plan into one
@@ -700,10 +710,11 @@ class B200PagedKVCache(KVCacheManager):
             self._pin_event.synchronize()
         return buf[:size]
 
-    def _plan_copied(self):
+    def _plan_copied(self, stream=None):
         if self._pin_event is None:
             self._pin_event = torch.cuda.Event()
-        self._pin_event.record(torch.cuda.current_stream(self.cfg.device))
+        self._pin_event.record(stream if stream is not None
+                               else torch.cuda.current_stream(self.cfg.device))
 
     def _ensure_tables(self, rows, stride):
         cur = self._dbt
@@ -749,35 +760,52 @@ class B200PagedKVCache(KVCacheManager):
         nu = sum(u.shape[0] for u in upd)
         npgs = (start + ps) // ps                      # ceil((start + 1) / ps)
         total = int(npgs.sum())
-        size_up = 2 * B + 3 * nu
+        zero = self.pool.take_pending_zero()           # pages allocated since the last forward
+        nz = len(zero)
+        size_up = 2 * B + 3 * nu + nz
         host = self._pinned_plan(size_up)
         hn = host.numpy()
         hn[:B] = slots
         hn[B:2 * B] = start
         if nu:
-            np.concatenate(upd, out=hn[2 * B:].reshape(nu, 3))
+            np.concatenate(upd, out=hn[2 * B:2 * B + 3 * nu].reshape(nu, 3))
+        if nz:
+            hn[2 * B + 3 * nu:] = zero
         if self._up_dev is None or self._up_dev.numel() < size_up:
-            self._up_dev = torch.empty(max(size_up, 4096, 2 * (self._up_dev.numel() if self._up_dev is not None else 0)),
-                                       dtype=torch.int32, device=self.cfg.device)
+            grown = 2 * self._up_dev.numel() if self._up_dev is not None else 0
+            self._up_dev = torch.empty(max(size_up, 4096, grown), dtype=torch.int32,
+                                       device=self.cfg.device)
         up = self._up_dev
+        stream = torch.cuda.current_stream(self.cfg.device)
         up[:size_up].copy_(host, non_blocking=True)
-        self._plan_copied()
-        self.pool.flush_zero()
+        self._plan_copied(stream)
+        base = up.data_ptr()
+        status = ops.status_word(self.cfg.device).data_ptr()
+        if nz:
+            pool = self.pool
+            page_bytes = pool.k[0, 0].numel() * pool.k.element_size()
+            for t in (pool.k, pool.v):
+                N.call("nslg_zero_pages", base + 4 * (2 * B + 3 * nu), nz, t.data_ptr(),
+                       t.shape[0], t.shape[1], page_bytes, status, stream.cuda_stream)
         plan_size = 5 * B + 2 + max(B, 1) + total
-        static = self.static_plan_for(B, 1, plan_size)
-        d = static if static is not None else torch.empty(plan_size, dtype=torch.int32,
-                                                          device=self.cfg.device)
+        d = self.static_plan_for(B, 1, plan_size)
+        if d is None:
+            # one buffer reused by every forward: its readers are earlier launches on the
+            # same stream
+            if self._plan_dev is None or self._plan_dev.numel() < plan_size:
+                grown = 2 * self._plan_dev.numel() if self._plan_dev is not None else 0
+                self._plan_dev = torch.empty(max(plan_size, 65536, grown), dtype=torch.int32,
+                                             device=self.cfg.device)
+            d = self._plan_dev
         ctx._set_plan_views(d, B, 1, total)
         ctx._plan_bytes = size_up * 4
         dbt = self._dbt
-        from . import _native as N
-        N.call("nslg_plan_decode", B, ps, up.data_ptr(), up.data_ptr() + 4 * B, nu,
-               up.data_ptr() + 8 * B if nu else None, dbt.data_ptr(), dbt.shape[1], dbt.shape[0],
+        N.call("nslg_plan_decode", B, ps, base, base + 4 * B, nu, base + 8 * B if nu else None,
+               dbt.data_ptr(), dbt.shape[1], dbt.shape[0],
                ctx._pos_i32.data_ptr(), ctx._write_loc.data_ptr(), ctx.kv_indptr.data_ptr(),
                ctx.kv_last_page_len.data_ptr(), ctx.qo_indptr.data_ptr(),
                ctx.q_row_start.data_ptr(), ctx.kv_indices.data_ptr(), max(total, 1),
-               ops.status_word(self.cfg.device).data_ptr(),
-               torch.cuda.current_stream(self.cfg.device).cuda_stream)
+               status, stream.cuda_stream)
 
     def allocate_sequence(self, seq_id, token_ids=None, num_tokens=0):
         tids = token_ids or []

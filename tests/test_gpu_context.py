@@ -284,3 +284,29 @@ def test_device_plan_matches_host_plan():
             m.end_forward(c)
     from nanoslg_b200 import ops
     ops.check_device_status(dev)
+
+
+def test_device_plan_zeroes_new_pages():
+    """Pages allocated since the last forward are zeroed in every layer (PagePool.alloc,
+    kv_cache.py:411) by nslg_zero_pages on the device-planned decode path; the null page
+    and pages of other sequences are left alone."""
+    from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
+    dev = torch.device("cuda:0")
+    mgr = B200PagedKVCache(KVCacheConfig(num_layers=3, num_kv_heads=2, num_qo_heads=4,
+                                         head_dim=64, page_size=16, max_pages=64,
+                                         dtype=torch.bfloat16, device=dev,
+                                         enable_prefix_caching=False))
+    assert mgr.device_plan
+    mgr.pool.k.fill_(3.0)
+    mgr.pool.v.fill_(3.0)
+    for s, n in (("a", 40), ("b", 16)):
+        mgr.allocate_sequence(s, None, num_tokens=n)
+        mgr.seqs[s].num_tokens = n
+    ctx = mgr.begin_forward(["a", "b"], [1, 1])
+    torch.cuda.synchronize(dev)
+    pages = set(mgr.seqs["a"].block_table) | set(mgr.seqs["b"].block_table)
+    for pid in pages:
+        assert mgr.pool.k[:, pid].abs().sum() == 0 and mgr.pool.v[:, pid].abs().sum() == 0
+    untouched = [p for p in range(64) if p not in pages]
+    assert bool((mgr.pool.k[:, untouched] == 3.0).all())
+    mgr.end_forward(ctx)
