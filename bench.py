@@ -287,9 +287,12 @@ def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=N
     hf = llama_config("llama-3.1-8b")
     if runner is None:
         pages = 2 * 64 * (-(-(prompt + 8 + 64 + 2) // PS)) + 64
+        # room for one batch of 64 x 512-token prompts, or the C4 batches of
+        # 1024 + 128 + 136 tokens per request (shared prefix pages counted once)
+        pages = max(pages, 64 * (-(-(128 + 136) // PS)) * 2 + 2 * (1024 // PS) + 64)
         runner = LlamaRunner(hf, device, tp_size=world, rank=rank, max_kv_pages=pages,
                              peer_allreduce=peer_allreduce)
-        runner.enable_cuda_graphs([64, 1])
+        runner.enable_cuda_graphs([64, 16, 4, 1])
     g = torch.Generator().manual_seed(123 + batch)
     prompts = torch.randint(0, hf.vocab_size, (batch, prompt), generator=g).tolist()
     torch.cuda.synchronize(device)
@@ -316,6 +319,59 @@ def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=N
     runner.release()
     return runner, {"batch": batch, "prompt": prompt, "steps": steps, "ms_per_step": ms / steps,
                     "tok_s": batch * steps / (ms / 1e3), "prefill_ms": prefill_ms}
+
+
+def run_llama_c4(device, world, rank, runner, batches=(4, 16, 64), prefix_len=1024,
+                 suffix_len=128, steps=128):
+    """BASELINE config C4 on the TP=world runner: every request shares one random
+    1024-token prefix and has a unique random 128-token suffix. A priming batch (prefill
+    + 4 decode steps + release, which inserts its pages into the radix tree) precedes each
+    measured batch; the measured batch's prefill reuses the shared pages (prefix_skip
+    tokens per request) and then decodes ``steps`` greedy tokens, CUDA events around the
+    decode loop, max over ranks."""
+    from nanoslg_b200.runner import llama_config
+    hf = llama_config("llama-3.1-8b")
+    g = torch.Generator().manual_seed(77)
+    prefix = torch.randint(0, hf.vocab_size, (prefix_len,), generator=g).tolist()
+    out = {}
+    for bsz in batches:
+        def batch():
+            return [prefix + torch.randint(0, hf.vocab_size, (suffix_len,), generator=g).tolist()
+                    for _ in range(bsz)]
+        tok = runner.prefill(batch())                          # priming batch
+        gen = [[int(t)] for t in tok.tolist()]
+        for _ in range(4):
+            tok = runner.decode_step(tok)
+            for gl, t in zip(gen, tok.tolist()):
+                gl.append(int(t))
+        runner.release(gen)
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        tok = runner.prefill(batch())                          # measured batch
+        torch.cuda.synchronize(device)
+        prefill_ms = (time.perf_counter() - t0) * 1e3
+        skip = list(runner.prefix_lens)
+        for _ in range(3):
+            tok = runner.decode_step(tok)
+        if torch.distributed.is_initialized():
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            tok = runner.decode_step(tok)
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        if torch.distributed.is_initialized():
+            t = torch.tensor([ms, prefill_ms], device=device, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms, prefill_ms = t.tolist()
+        runner.release()
+        out[f"batch{bsz}"] = {"decode_tok_s": bsz * steps / (ms / 1e3),
+                              "ms_per_step": ms / steps, "prefill_ms": prefill_ms,
+                              "prefix_skip_tokens": min(skip), "steps": steps}
+    return out
 
 
 # ------------------------------------------------------------------------ CPU side
@@ -426,9 +482,11 @@ def main():
     if a.only == "model":
         runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,
                                        peer_allreduce=a.tp_reduce == "peer")
+        c4 = run_llama_c4(device, world, rank, runner) if world > 1 else None
         runner.close()
         if rank == 0:
-            print(json.dumps({"case": "model only", "llama8b_decode_batch64": r64}), flush=True)
+            print(json.dumps({"case": "model only", "llama8b_decode_batch64": r64,
+                              "llama8b_c4_radix": c4}), flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
         return 0
@@ -488,8 +546,14 @@ def main():
         line["llama8b_decode"] = {
             "model": "Llama-3.1-8B architecture, random init N(0, 0.02), bf16 (BASELINE C3)",
             "parallelism": f"TP={world}", "batch64": r64, "batch1": r1,
+            "tp_reduce": a.tp_reduce if world > 1 else None,
             "note": "greedy decode steps through models.LlamaTP + B200PagedKVCache; GEMMs "
                     "cuBLAS, attention/RoPE/append/RMSNorm the nslg kernels"}
+        if world > 1:
+            line["llama8b_c4_radix"] = {
+                "config": "BASELINE C4: TP=N, shared 1024-token prefix + unique 128-token "
+                          "suffix per request, 128 greedy decode tokens, radix prefix caching",
+                **run_llama_c4(device, world, rank, runner)}
         runner.close()
         del runner
     if rank == 0 and world == 1 and not a.no_cpu:

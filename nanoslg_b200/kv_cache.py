@@ -596,6 +596,7 @@ class B200CacheContext(CacheContext):
         flat_size = size
         pool.flush_zero()
         static = cache.static_plan_for(B, iw, flat_size)
+        self.plan_static = static is not None
         if static is not None:
             static[:flat_size].copy_(host, non_blocking=True)
             d = static
@@ -686,15 +687,22 @@ class B200PagedKVCache(KVCacheManager):
         """From now on, forwards of exactly (batch, input_width) put their plan into one
         fixed device buffer (page-id capacity ``max_pages``, default the whole pool), so a
         CUDA graph captured over one such forward can be replayed for the later ones."""
-        cap = max_pages if max_pages is not None else self.cfg.max_pages
+        # page-list capacity: every sequence lists its shared prefix pages again, so the
+        # list can be longer than the pool; size it for full-length sequences
+        ps = self.cfg.page_size
+        cap = max_pages if max_pages is not None else max(
+            self.cfg.max_pages, batch * -(-self.cfg.max_seq_len // ps))
         n = 2 * batch * input_width + (batch + 1) + max(batch, 1) + (batch + 1) + batch + cap
         self._static_plans[(batch, input_width)] = torch.zeros(
             n, dtype=torch.int32, device=self.cfg.device)
 
     def static_plan_for(self, batch, input_width, size):
+        """The fixed plan buffer of (batch, input_width), or None when there is none or
+        this plan does not fit it (the forward then gets a buffer of its own, and
+        ``plan_static`` of its context is False)."""
         buf = self._static_plans.get((batch, input_width))
         if buf is not None and size > buf.numel():
-            raise RuntimeError("plan larger than the static plan buffer")
+            return None
         return buf
 
     def _pinned_plan(self, size):
@@ -789,6 +797,7 @@ class B200PagedKVCache(KVCacheManager):
                        t.shape[0], t.shape[1], page_bytes, status, stream.cuda_stream)
         plan_size = 5 * B + 2 + max(B, 1) + total
         d = self.static_plan_for(B, 1, plan_size)
+        ctx.plan_static = d is not None
         if d is None:
             # one buffer reused by every forward: its readers are earlier launches on the
             # same stream

@@ -154,7 +154,7 @@ class LlamaRunner:
         B = len(self.seq_ids)
         ctx = mgr.begin_forward(self.seq_ids, [1] * B)
         if not (self.use_graphs and self.pcfg.pp_size == 1
-                and mgr.static_plan_for(B, 1, 0) is not None):
+                and getattr(ctx, "plan_static", False)):
             tok = self._forward_tokens(tokens[:, None], ctx, 1)
             mgr.end_forward(ctx)
             return tok
