@@ -172,6 +172,10 @@ class PagePool:
         self.free_set: Set[int] = set(range(1, cfg.max_pages))
         self._lock = threading.Lock()
         self._pending_zero: List[int] = []
+        # per-layer views, made once (indexing the pool tensor every call costs more
+        # than the views themselves)
+        self.k_layers = [self.k[i] for i in range(cfg.num_layers)]
+        self.v_layers = [self.v[i] for i in range(cfg.num_layers)]
 
     def alloc(self, n=1) -> Optional[List[int]]:
         with self._lock:
@@ -629,7 +633,7 @@ class B200CacheContext(CacheContext):
         self._check_width(q)
         pool = self.cache.pool
         ops.rope_kv_append(None, k_new, v_new, None, None, None, self._write_loc,
-                           pool.k[layer_idx], pool.v[layer_idx], rotate=False)
+                           pool.k_layers[layer_idx], pool.v_layers[layer_idx], rotate=False)
         return self._attention(layer_idx, q)
 
     def attend_rope(self, layer_idx, q, k_new, v_new, cos, sin):
@@ -639,7 +643,7 @@ class B200CacheContext(CacheContext):
         pool = self.cache.pool
         B, S, hq, d = q.shape
         q_rot = ops.rope_kv_append(q, k_new, v_new, self._pos_i32, cos, sin, self._write_loc,
-                                   pool.k[layer_idx], pool.v[layer_idx])
+                                   pool.k_layers[layer_idx], pool.v_layers[layer_idx])
         return self._attention(layer_idx, q_rot.view(B, S, hq, d))
 
     def _check_width(self, q):
@@ -650,7 +654,7 @@ class B200CacheContext(CacheContext):
     def _attention(self, layer_idx, q):
         B, S, hq, d = q.shape
         pool = self.cache.pool
-        pk, pv = pool.k[layer_idx], pool.v[layer_idx]
+        pk, pv = pool.k_layers[layer_idx], pool.v_layers[layer_idx]
         if self._is_decode:
             out = ops.paged_decode(q[:, 0], pk, pv, self.kv_indptr, self.kv_indices,
                                    self.kv_last_page_len, self._sm_scale)

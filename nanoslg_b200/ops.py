@@ -30,7 +30,15 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t):
+    """cudaStream_t of the current stream of t's device (the raw handle when torch
+    exposes it, which avoids building a Stream object per launch)."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index if t.device.index is not None
+                           else torch.cuda.current_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -64,6 +72,9 @@ class _DeviceState:
         self.status = {}
 
     def workspace(self, device, nbytes):
+        buf = self.ws.get(device)
+        if buf is not None and buf.numel() >= nbytes:
+            return buf
         with self.lock:
             buf = self.ws.get(device)
             if buf is None or buf.numel() < nbytes:
@@ -72,6 +83,9 @@ class _DeviceState:
             return buf
 
     def status_word(self, device):
+        st = self.status.get(device)
+        if st is not None:
+            return st
         with self.lock:
             st = self.status.get(device)
             if st is None:
@@ -85,7 +99,11 @@ _STATE = _DeviceState()
 
 def status_word(device):
     """The int32 device word the kernels OR their NSLG_DEV_* error bits into."""
-    return _STATE.status_word(torch.device(device))
+    if not isinstance(device, torch.device):
+        device = torch.device(device)
+    if device.index is None and device.type == "cuda":
+        device = torch.device("cuda", torch.cuda.current_device())
+    return _STATE.status_word(device)
 
 
 def check_device_status(device, reset=True):
