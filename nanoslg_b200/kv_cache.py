@@ -740,6 +740,79 @@ class B200PagedKVCache(KVCacheManager):
             new[:r0, :s0].copy_(cur)
         self._dbt = new
 
+    def _begin_decode_device(self, seq_ids, ntoks):
+        """begin_forward for a decode step (one new token per sequence) planned on the
+        device, in one pass over the batch: page extension (in batch order, as
+        extend_sequence), the write page, tokens_used, the device table row and the table
+        entries to upload. Returns None -- nothing but page extensions and tokens_used
+        updates done, both of which the general path repeats idempotently -- when a
+        target page is shared (copy on write) or missing."""
+        ps = self.cfg.page_size
+        rc = self.pool.ref_count
+        tu = self.pool.tokens_used
+        seqs = self.seqs
+        sts, starts, pids, slots, dirty = [], [], [], [], []
+        longest = 0
+        for sid in seq_ids:
+            st = seqs[sid]
+            n0 = st.num_tokens
+            bt = st.block_table
+            nb = len(bt)
+            if n0 >= nb * ps:
+                bt.extend(self._alloc(n0 // ps + 1 - nb))
+                nb = len(bt)
+            pid = bt[n0 // ps]
+            if rc[pid] > 1:
+                return None
+            used = n0 % ps + 1
+            if tu[pid] < used:
+                tu[pid] = used
+            if st.slot < 0:
+                if self._slot_free:
+                    st.slot = self._slot_free.pop()
+                else:
+                    st.slot = self._slot_next
+                    self._slot_next += 1
+                bt.dirty_from = 0
+            if bt.dirty_from < nb:
+                dirty.append(st)
+            if nb > longest:
+                longest = nb
+            sts.append(st)
+            starts.append(n0)
+            pids.append(pid)
+            slots.append(st.slot)
+        ctx = B200CacheContext.__new__(B200CacheContext)
+        B = len(sts)
+        ctx.cache = self
+        ctx.seq_ids = seq_ids
+        ctx.new_token_counts = ntoks
+        ctx.input_offsets = [0] * B
+        ctx.batch_size = B
+        ctx.start_positions = starts
+        ctx.seq_lens = [n + 1 for n in starts]
+        ctx.max_kv_len = max(ctx.seq_lens)
+        ctx._is_decode = True
+        ctx._iw = 1
+        ctx._wi = None
+        ctx._wi_src = (pids, [n % ps for n in starts])
+        ctx._sm_scale = 1.0 / math.sqrt(self.cfg.head_dim)
+        ctx._pos64 = None
+        upd = []
+        for st in dirty:
+            bt = st.block_table
+            d, nb = bt.dirty_from, len(bt)
+            u = np.empty((nb - d, 3), dtype=np.int32)
+            u[:, 0] = st.slot
+            u[:, 1] = np.arange(d, nb, dtype=np.int32)
+            u[:, 2] = bt.arr[d:nb]
+            upd.append(u)
+            bt.dirty_from = nb
+        self._ensure_tables(self._slot_next, longest)
+        self._launch_device_plan(ctx, np.asarray(slots, dtype=np.int32),
+                                 np.asarray(starts, dtype=np.int64), upd)
+        return ctx
+
     def _plan_decode_on_device(self, ctx, sts, start):
         """Fills ``ctx``'s plan views for a decode step with nslg_plan_decode: uploads the
         batch's table rows, start positions and the block-table entries changed since the
@@ -769,6 +842,13 @@ class B200PagedKVCache(KVCacheManager):
                 upd.append(u)
                 bt.dirty_from = n
         self._ensure_tables(self._slot_next, longest)
+        self._launch_device_plan(ctx, slots, start, upd)
+
+    def _launch_device_plan(self, ctx, slots, start, upd):
+        """Uploads (slots, start positions, table entries ``upd``, pages to zero) and
+        launches nslg_zero_pages / nslg_plan_decode into ``ctx``'s plan views."""
+        B = len(slots)
+        ps = self.cfg.page_size
         nu = sum(u.shape[0] for u in upd)
         npgs = (start + ps) // ps                      # ceil((start + 1) / ps)
         total = int(npgs.sum())
@@ -845,6 +925,11 @@ class B200PagedKVCache(KVCacheManager):
             st.block_table.extend(self._alloc(need - len(st.block_table)))
 
     def begin_forward(self, seq_ids, ntoks, offsets=None):
+        if (self.device_plan and 0 < len(seq_ids) <= 4096 and not any(offsets or ())
+                and all(n == 1 for n in ntoks)):
+            ctx = self._begin_decode_device(seq_ids, ntoks)
+            if ctx is not None:
+                return ctx
         # extend_sequence for every sequence, inlined (sequences in order, so the page
         # allocation order is the reference's)
         sts = [self.seqs[s] for s in seq_ids]
