@@ -374,6 +374,63 @@ def run_llama_c4(device, world, rank, runner, batches=(4, 16, 64), prefix_len=10
     return out
 
 
+def run_llama70b_c5(device, world, rank, steps=256, batch=32, prompt=2048):
+    """BASELINE C5: Llama-3-70B architecture (random init), bf16, TP=4 x PP=2 on 8 GPUs,
+    batch 32, 2048-token random prompts, 256 greedy decode tokens. The prefill runs the
+    reference's lock-step pipeline; decode is measured with the config's 4 pipeline
+    micro-batches (LlamaRunner.decode_microbatched), with 2, and lock step (the
+    reference's schedule), every stage forward a CUDA graph. CUDA events around the
+    decode loop, max over ranks."""
+    from nanoslg_b200.runner import LlamaRunner, llama_config
+    if world != 8:
+        raise ValueError("C5 runs on 8 GPUs (TP=4 x PP=2)")
+    hf = llama_config("llama-3-70b")
+    pages = batch * (-(-(prompt + steps + 16) // PS)) + 64
+    runner = LlamaRunner(hf, device, tp_size=4, pp_size=2, rank=rank, max_kv_pages=pages,
+                         prefix_caching=False)
+    runner.enable_cuda_graphs([batch, batch // 2, batch // 4])
+    g = torch.Generator().manual_seed(70)
+    prompts = torch.randint(0, hf.vocab_size, (batch, prompt), generator=g).tolist()
+    out = {"model": "Llama-3-70B architecture, random init N(0, 0.02), bf16",
+           "parallelism": "TP=4 x PP=2", "batch": batch, "prompt": prompt, "steps": steps}
+
+    def maxed(x):
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    for name, micro in (("microbatch4", 4), ("microbatch2", 2), ("lockstep", 1)):
+        torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        tok = runner.prefill(prompts)
+        torch.cuda.synchronize(device)
+        prefill_ms = maxed((time.perf_counter() - t0) * 1e3)
+
+        def decode(n, tok):
+            if micro > 1:
+                gen = runner.decode_microbatched(tok, micro, n)
+                return gen[:, -1].contiguous()
+            for _ in range(n):
+                tok = runner.decode_step(tok)
+            return tok
+
+        tok = decode(2, tok)                                   # graph capture, warm-up
+        torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        tok = decode(steps, tok)
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = maxed(e0.elapsed_time(e1))
+        runner.release()
+        out[name] = {"decode_tok_s": batch * steps / (ms / 1e3), "ms_per_step": ms / steps,
+                     "prefill_ms": prefill_ms}
+    runner.close()
+    return out
+
+
 # ------------------------------------------------------------------------ CPU side
 def cpu_reference(max_seconds, n_calls=None, seed=0):
     """The reference's contiguous attend (oracle/attention.py restating
@@ -420,6 +477,8 @@ def main():
                          "batch (still 1.13 GB of KV per step)")
     ap.add_argument("--no-model", action="store_true", help="skip the Llama-3.1-8B decode leg")
     ap.add_argument("--model-steps", type=int, default=32)
+    ap.add_argument("--c5", action="store_true",
+                    help="only BASELINE C5 (Llama-3-70B, TP=4 x PP=2, needs --gpus 8)")
     ap.add_argument("--tp-reduce", choices=["peer", "nccl"], default="peer",
                     help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
@@ -478,6 +537,13 @@ def main():
                               run_prefill_kernel(device)}), flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
+        return 0
+    if a.c5:
+        r = run_llama70b_c5(device, world, rank)
+        if rank == 0:
+            print(json.dumps({"case": "C5", "llama70b_c5": r}), flush=True)
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
         return 0
     if a.only == "model":
         runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,

@@ -107,6 +107,16 @@ class LlamaRunner:
         if not pc.is_first_pp_stage:
             x = torch.empty(B, width, self.hf.hidden_size, dtype=self.dtype, device=self.device)
             dist.recv(x, src=pc.get_pp_prev_rank())
+        if width == 1 and self.use_graphs:
+            # decode step: the stage forward replays its CUDA graph
+            res = self._stage_decode_forward(x, ctx, B)
+            if pc.is_last_pp_stage:
+                tok = res.clone()
+            else:
+                dist.send(res.contiguous(), dst=pc.get_pp_next_rank())
+                tok = torch.empty(B, dtype=torch.long, device=self.device)
+            dist.broadcast(tok, src=(self.pcfg.pp_size - 1) * self.pcfg.tp_size)
+            return tok
         out = self.model(x, ctx, last_only=pc.is_last_pp_stage)
         if pc.is_last_pp_stage:
             tok = out[:, -1].argmax(-1)
@@ -180,6 +190,102 @@ class LlamaRunner:
         entry[0].replay()
         mgr.end_forward(ctx)
         return entry[2].clone()
+
+    def _stage_decode_forward(self, x, ctx, B):
+        """Decode forward of this rank's pipeline stage for B sequences: the last stage
+        returns their greedy tokens [B], the others the hidden state [B, 1, hidden].
+        With graphs enabled and the plan in the static buffer, the stage forward replays
+        one CUDA graph per B (no collective inside: the stage's TP reductions are the
+        peer-memory kernel, or NCCL in the graph as in ``decode_step``). The result is the
+        graph's static output: use it before the next call with the same B."""
+        last = self.pctx.is_last_pp_stage
+        if not (self.use_graphs and getattr(ctx, "plan_static", False)):
+            out = self.model(x, ctx, last_only=last)
+            return out[:, -1].argmax(-1) if last else out
+        key = ("stage", B)
+        entry = self._graphs.get(key)
+        if entry is None:
+            x_in = x.clone()
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):       # rewrites this step's K/V slots with the same values
+                    self.model(x_in, ctx, last_only=last)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = self.model(x_in, ctx, last_only=last)
+                res = out[:, -1].argmax(-1) if last else out
+            entry = (graph, x_in, res)
+            self._graphs[key] = entry
+        else:
+            entry[1].copy_(x)
+        entry[0].replay()
+        return entry[2]
+
+    @torch.inference_mode()
+    def decode_microbatched(self, tokens, num_micro, steps):
+        """``steps`` greedy decode steps of the current batch split into ``num_micro``
+        micro-batches flowing through the pipeline stages (BASELINE C5; the reference runs
+        its PP stages in lock step, worker.py:580-607). Tick i: stage p runs micro-batch
+        (i - p) mod M; after every tick each rank exchanges, in one grouped NCCL
+        send/recv, the hidden state with the neighbouring stages (same TP rank) and the
+        last stage returns the micro-batch's tokens to the first, which needs them M - P
+        + 1 ticks later (M >= P). Returns the generated tokens [B, steps] on every rank
+        of the first and last stage (other stages: None)."""
+        pc = self.pctx
+        P = self.pcfg.pp_size
+        if P < 2:
+            raise ValueError("decode_microbatched needs pipeline stages")
+        p = pc.pp_rank
+        B = len(self.seq_ids)
+        M = num_micro
+        if B % M or M < P:
+            raise ValueError("batch must split into num_micro >= pp_size equal micro-batches")
+        mb = B // M
+        tp = self.pcfg.tp_size
+        groups = [self.seq_ids[j * mb:(j + 1) * mb] for j in range(M)]
+        first_rank = pc.tp_rank
+        last_rank = (P - 1) * tp + pc.tp_rank
+        H = self.hf.hidden_size
+        tok_mb = [tokens[j * mb:(j + 1) * mb].clone() for j in range(M)]
+        gen = [[] for _ in range(M)]
+        recv_h = None
+        n_work = steps * M
+        for i in range(n_work + P - 1):
+            k = i - p
+            active = 0 <= k < n_work
+            out = None
+            if active:
+                m = k % M
+                ctx = self.cache.begin_forward(groups[m], [1] * mb)
+                x = tok_mb[m][:, None] if p == 0 else recv_h
+                out = self._stage_decode_forward(x, ctx, mb)
+                self.cache.end_forward(ctx)
+                if p == P - 1:
+                    gen[m].append(out.clone())
+            ops = []
+            if active and p < P - 1:
+                ops.append(dist.P2POp(dist.isend, out.contiguous(), pc.get_pp_next_rank()))
+            if p > 0 and 0 <= i + 1 - p < n_work:
+                recv_h = torch.empty(mb, 1, H, dtype=self.dtype, device=self.device)
+                ops.append(dist.P2POp(dist.irecv, recv_h, pc.get_pp_prev_rank()))
+            if active and p == P - 1:
+                ops.append(dist.P2POp(dist.isend, out.contiguous(), first_rank))
+            pending = None
+            if p == 0 and 0 <= i - (P - 1) < n_work:
+                t = torch.empty(mb, dtype=torch.long, device=self.device)
+                ops.append(dist.P2POp(dist.irecv, t, last_rank))
+                pending = ((i - (P - 1)) % M, t)
+            if ops:
+                for r in dist.batch_isend_irecv(ops):
+                    r.wait()
+            if pending is not None:
+                tok_mb[pending[0]] = pending[1]
+                gen[pending[0]].append(pending[1])
+        if p != 0 and p != P - 1:
+            return None
+        return torch.cat([torch.stack(g, 1) for g in gen], 0)
 
     def close(self):
         """Drops the captured graphs (they may hold NCCL calls, which must be gone before

@@ -69,3 +69,73 @@ def test_sharded_tiny_llama_matches_reference(tp, pp):
     assert sorted(res) == list(range(world))
     for rank, toks in res.items():
         assert toks == want, f"rank {rank}"
+
+
+def _micro_main(rank, world, port, out):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    res = {}
+    try:
+        from oracle.llama import init_params
+        from nanoslg_b200.runner import LlamaRunner
+        with open(os.path.join(GOLDEN, "tiny_llama.json")) as f:
+            g = json.load(f)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        r = LlamaRunner(SimpleNamespace(**g["config"]), dev, dtype=torch.float32, tp_size=1,
+                        pp_size=2, rank=rank, max_kv_pages=256, prefix_caching=False)
+        r.load_full_state_dict(init_params(g["config"]))
+        gen = torch.Generator().manual_seed(5)
+        prompts = [torch.randint(0, 1024, (n,), generator=gen).tolist() for n in (9, 17, 30, 4)]
+        steps = 6
+        tok = r.prefill(prompts)
+        lock = [tok]
+        for _ in range(steps):
+            tok = r.decode_step(tok)
+            lock.append(tok)
+        want = torch.stack(lock[1:], 1).tolist()
+        r.release()
+        for graphs in (False, True):
+            if graphs:
+                r.enable_cuda_graphs([4, 2, 1])
+                # lock step again, every stage forward a CUDA graph
+                tok = r.prefill(prompts)
+                seq = []
+                for _ in range(steps):
+                    tok = r.decode_step(tok)
+                    seq.append(tok)
+                r.release()
+                res[(graphs, 1)] = torch.stack(seq, 1).tolist() == want
+            for m in (2, 4):
+                tok = r.prefill(prompts)
+                got = r.decode_microbatched(tok, m, steps)
+                r.release()
+                res[(graphs, m)] = got.tolist() == want
+        r.close()
+        res["done"] = True
+    finally:
+        out[rank] = res
+        dist.destroy_process_group()
+
+
+def test_pipeline_microbatched_decode_matches_lock_step():
+    """Micro-batched pipeline decode (LlamaRunner.decode_microbatched, the C5 schedule)
+    gives the lock-step pipeline's greedy tokens for every micro-batch split, eager and
+    with per-stage CUDA graphs."""
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with mp.get_context("spawn").Manager() as m:
+        out = m.dict()
+        mp.start_processes(_micro_main, args=(world, _free_port(), out), nprocs=world,
+                           start_method="spawn", join=True)
+        res = dict(out)
+    for rank in range(world):
+        assert res[rank].get("done"), res[rank]
+        assert all(v for k, v in res[rank].items() if k != "done"), res[rank]
