@@ -367,82 +367,83 @@ __global__ void __launch_bounds__(kThreads, 1)
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const bool whole = cta_of(seq_beg, total, n) == cta_of(seq_end - 1, total, n);
+    const int64_t slot = static_cast<int64_t>(b) + c;
 
-    if constexpr (C::kPPS > 1) {
-      // warps sharing kv head h (j = 1..kPPS-1) hand their state to warp j == 0
-      float* cw = comb + static_cast<size_t>(warp) * G * (D + 2);
-      if (j > 0) {
+    if constexpr (C::kPPS == 1) {
+      // one warp per kv head: its state is the segment's
+      if (ok) {
+        const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+        const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const int col = t * 8 + tq * 2;
-          if (g < G) { cw[g * D + col] = o[t][0]; cw[g * D + col + 1] = o[t][1]; }
-          if (g + 8 < G) { cw[(g + 8) * D + col] = o[t][2]; cw[(g + 8) * D + col + 1] = o[t][3]; }
+        for (int rr = 0; rr < 2; ++rr) {
+          const int r = g + rr * 8;
+          if (r >= G) continue;
+          const int hq = h * G + r;
+          const float inv = rr ? inv1 : inv0;
+          if (whole) {
+            __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride +
+                                static_cast<int64_t>(hq) * D;
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+              *reinterpret_cast<uint32_t*>(ob + t * 8 + tq * 2) =
+                  pack_bf16x2(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
+          } else {
+            float* po = p.part_o + (slot * p.hq + hq) * D;
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+              *reinterpret_cast<float2*>(po + t * 8 + tq * 2) =
+                  make_float2(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
+            if (tq == 0) {
+              const float m = rr ? m1 : m0, l = rr ? l1 : l0;
+              p.part_lse[slot * p.hq + hq] = l > 0.f ? m * sl + __log2f(l) : -INFINITY;
+            }
+          }
         }
-        if (tq == 0) {
-          if (g < G) { cw[G * D + g] = m0; cw[G * D + G + g] = l0; }
-          if (g + 8 < G) { cw[G * D + g + 8] = m1; cw[G * D + G + g + 8] = l1; }
-        }
+      }
+    } else {
+      // The kPPS warps of kv head h (pages j = 0..kPPS-1 of each stage) each hold a
+      // partial softmax state. All of them store it in shared memory; then warp j merges
+      // the kPPS states for D / kPPS of the head dims (every row of the group) and writes
+      // them, so the combine costs one pass instead of kPPS - 1 serial ones.
+      float* cw = comb + static_cast<size_t>(warp) * G * (D + 2);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const int col = t * 8 + tq * 2;
+        if (g < G) { cw[g * D + col] = o[t][0]; cw[g * D + col + 1] = o[t][1]; }
+        if (g + 8 < G) { cw[(g + 8) * D + col] = o[t][2]; cw[(g + 8) * D + col + 1] = o[t][3]; }
+      }
+      if (tq == 0) {
+        if (g < G) { cw[G * D + g] = m0; cw[G * D + G + g] = l0; }
+        if (g + 8 < G) { cw[G * D + g + 8] = m1; cw[G * D + G + g + 8] = l1; }
       }
       named_barrier_sync(1, kConsumerWarps * 32);
-      if (j == 0) {
-        for (int jj = 1; jj < C::kPPS; ++jj) {
-          const float* cx = comb + static_cast<size_t>(jj * HKV + h) * G * (D + 2);
-          const float mx0 = g < G ? cx[G * D + g] : -INFINITY;
-          const float lx0 = g < G ? cx[G * D + G + g] : 0.f;
-          const float mx1 = g + 8 < G ? cx[G * D + g + 8] : -INFINITY;
-          const float lx1 = g + 8 < G ? cx[G * D + G + g + 8] : 0.f;
-          const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-          const float b0 = mn0 == -INFINITY ? 0.f : mn0 * sl;
-          const float b1 = mn1 == -INFINITY ? 0.f : mn1 * sl;
-          const float wa0 = fast_exp2(fmaf(m0, sl, -b0)), wb0 = fast_exp2(fmaf(mx0, sl, -b0));
-          const float wa1 = fast_exp2(fmaf(m1, sl, -b1)), wb1 = fast_exp2(fmaf(mx1, sl, -b1));
+      if (ok) {
+        constexpr int DS = D / C::kPPS;          // head dims merged and written by this warp
+        for (int e = lane; e < G * DS; e += 32) {
+          const int r = e / DS, col = j * DS + e % DS;
+          float mx = -INFINITY;
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const int col = t * 8 + tq * 2;
-            const float x0 = g < G ? cx[g * D + col] : 0.f;
-            const float x1 = g < G ? cx[g * D + col + 1] : 0.f;
-            const float x2 = g + 8 < G ? cx[(g + 8) * D + col] : 0.f;
-            const float x3 = g + 8 < G ? cx[(g + 8) * D + col + 1] : 0.f;
-            o[t][0] = o[t][0] * wa0 + x0 * wb0;
-            o[t][1] = o[t][1] * wa0 + x1 * wb0;
-            o[t][2] = o[t][2] * wa1 + x2 * wb1;
-            o[t][3] = o[t][3] * wa1 + x3 * wb1;
+          for (int jj = 0; jj < C::kPPS; ++jj)
+            mx = fmaxf(mx, comb[static_cast<size_t>(jj * HKV + h) * G * (D + 2) + G * D + r]);
+          const float base = mx == -INFINITY ? 0.f : mx * sl;
+          float lsum = 0.f, acc = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < C::kPPS; ++jj) {
+            const float* cx = comb + static_cast<size_t>(jj * HKV + h) * G * (D + 2);
+            const float w = fast_exp2(fmaf(cx[G * D + r], sl, -base));
+            lsum = fmaf(cx[G * D + G + r], w, lsum);
+            acc = fmaf(cx[r * D + col], w, acc);
           }
-          l0 = l0 * wa0 + lx0 * wb0;
-          l1 = l1 * wa1 + lx1 * wb1;
-          m0 = mn0;
-          m1 = mn1;
-        }
-      }
-    }
-
-    if (j == 0 && ok) {
-      const bool whole = cta_of(seq_beg, total, n) == cta_of(seq_end - 1, total, n);
-      const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
-      const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int r = g + rr * 8;
-        if (r >= G) continue;
-        const int hq = h * G + r;
-        const float inv = rr ? inv1 : inv0;
-        if (whole) {
-          __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride +
-                              static_cast<int64_t>(hq) * D;
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-            *reinterpret_cast<uint32_t*>(ob + t * 8 + tq * 2) =
-                pack_bf16x2(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
-        } else {
-          const int64_t slot = static_cast<int64_t>(b) + c;
-          float* po = p.part_o + (slot * p.hq + hq) * D;
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-            *reinterpret_cast<float2*>(po + t * 8 + tq * 2) =
-                make_float2(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
-          if (tq == 0) {
-            const float m = rr ? m1 : m0, l = rr ? l1 : l0;
-            p.part_lse[slot * p.hq + hq] = l > 0.f ? m * sl + __log2f(l) : -INFINITY;
+          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+          const int hq = h * G + r;
+          if (whole) {
+            p.out[static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D + col] =
+                __float2bfloat16_rn(acc * inv);
+          } else {
+            p.part_o[(slot * p.hq + hq) * D + col] = acc * inv;
+            if (j == 0 && e % DS == 0)
+              p.part_lse[slot * p.hq + hq] = lsum > 0.f ? mx * sl + __log2f(lsum) : -INFINITY;
           }
         }
       }
@@ -484,6 +485,42 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
   auto lse_of = [&](int i) {   // partial i of this sequence (CTA cf + i)
     return p.part_lse[(static_cast<int64_t>(b) + cf + i) * p.hq + hq];
   };
+  const int64_t step = static_cast<int64_t>(p.hq) * D;   // from one partial to the next
+  if (cnt <= 8) {
+    // every load in flight at once: lane i's log-sum-exp and all partial outputs
+    const float* po0 = p.part_o + ((static_cast<int64_t>(b) + cf) * p.hq + hq) * D + lane * DV;
+    const float l = lane < cnt ? lse_of(lane) : -INFINITY;
+    float v[8][DV];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < cnt) {
+#pragma unroll
+        for (int e = 0; e < DV; ++e) v[k][e] = po0[k * step + e];
+      }
+    }
+    float mx = l;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float w = l == -INFINITY ? 0.f : fast_exp2(l - mx);
+    float wsum = w;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+    float acc[DV];
+#pragma unroll
+    for (int e = 0; e < DV; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float wk = __shfl_sync(0xffffffffu, w, k);
+      if (k < cnt) {
+#pragma unroll
+        for (int e = 0; e < DV; ++e) acc[e] = fmaf(wk, v[k][e], acc[e]);
+      }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(acc[e] * inv);
+    return;
+  }
   float mx = -INFINITY;
   for (int i = lane; i < cnt; i += 32) mx = fmaxf(mx, lse_of(i));
 #pragma unroll
@@ -499,7 +536,6 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
     wsum += w;
     const int m = min(32, cnt - base);
     const float* po0 = p.part_o + ((static_cast<int64_t>(b) + cf + base) * p.hq + hq) * D + lane * DV;
-    const int64_t step = static_cast<int64_t>(p.hq) * D;   // from one partial to the next
 #pragma unroll 4
     for (int k = 0; k < m; ++k) {
       const float wk = __shfl_sync(0xffffffffu, w, k);

@@ -19,6 +19,7 @@ import math
 from typing import List
 
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
@@ -245,11 +246,13 @@ class _LlamaStage(nn.Module):
 
     peer_reduce = None      # PeerAllReduce of the TP group (enable_peer_allreduce)
 
-    def forward(self, x, cache_ctx, mask=None, last_only=False):
+    def forward(self, x, cache_ctx, mask=None, last_only=False, greedy=False):
         """Reference semantics (models.py:272-276): logits for every input position.
         ``last_only`` computes the final norm and LM head for the last position only
         (the only one the decode loop reads), which saves the [B, S, vocab] logits of a
-        long prefill."""
+        long prefill. ``greedy`` (last stage, with ``last_only``) returns the greedy token
+        of the last position, [B] int64, instead of its logits: under TP each rank takes
+        the argmax of its vocabulary shard and only (max, index) pairs are gathered."""
         h = self.embed_tokens(x) if self.is_first and x.dtype == torch.long else x
         peer = self.peer_reduce
         if peer is not None:
@@ -267,13 +270,39 @@ class _LlamaStage(nn.Module):
                 if last_only:
                     h, residual = h[:, -1:].contiguous(), residual[:, -1:].contiguous()
                 h, _ = self.norm.add_forward(h, residual, peer)
+                if greedy and last_only:
+                    return self._greedy(h)
                 return self.lm_head(h)
             if peer is not None:
                 return peer.allreduce_add_norm(h, residual, None, 0.0)
             return _add(h, residual)
         if self.is_last and last_only:
             h = h[:, -1:].contiguous()
+        if self.is_last and greedy and last_only:
+            return self._greedy(self.norm(h))
         return self.lm_head(self.norm(h)) if self.is_last else h
+
+    def _greedy(self, h):
+        """argmax over the vocabulary of the LM head applied to h [B, 1, hidden]: the
+        first index of the maximum, as torch.argmax over the all-gathered logits
+        (tp_layers.py:89 gathers them in the reference). With a vocab-parallel head each
+        rank reduces its shard and one all-gather of [B, 2] fp32 (max, global index)
+        pairs replaces the gather of [B, vocab] logits; the lowest rank holding the
+        maximum wins, and its shard holds the lowest indices."""
+        head = getattr(self.lm_head, "lm_head", None)
+        tp = getattr(head, "tp_size", 1)
+        if (head is None or tp == 1 or not getattr(head, "gather_output", False)
+                or head.out_features >= (1 << 24)):
+            return self.lm_head(h)[:, -1].argmax(-1)
+        local = F.linear(h[:, -1], head.weight, head.bias)              # [B, V/tp]
+        val, idx = local.max(-1)
+        ctx = get_parallel_context()
+        offset = ctx.tp_rank * head.out_features_per_partition
+        pair = torch.stack([val.float(), (idx + offset).float()], -1)     # exact below 2^24
+        allp = torch.empty((tp,) + tuple(pair.shape), dtype=pair.dtype, device=pair.device)
+        dist.all_gather_into_tensor(allp, pair.contiguous(), group=ctx.tp_group)
+        best = allp[..., 0].argmax(0)                                      # first max rank
+        return allp[..., 1].gather(0, best[None]).squeeze(0).long()
 
 
 def _add(a, b):

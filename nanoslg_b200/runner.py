@@ -100,8 +100,7 @@ class LlamaRunner:
         """One forward of the whole deployment for this step's cache context; returns the
         greedy token of every sequence on every rank."""
         if self.pcfg.pp_size == 1:
-            logits = self.model(x, ctx, last_only=True)
-            return logits[:, -1].argmax(-1)
+            return self.model(x, ctx, last_only=True, greedy=True)
         pc = self.pctx
         B = len(self.seq_ids)
         if not pc.is_first_pp_stage:
@@ -117,9 +116,9 @@ class LlamaRunner:
                 tok = torch.empty(B, dtype=torch.long, device=self.device)
             dist.broadcast(tok, src=(self.pcfg.pp_size - 1) * self.pcfg.tp_size)
             return tok
-        out = self.model(x, ctx, last_only=pc.is_last_pp_stage)
+        out = self.model(x, ctx, last_only=pc.is_last_pp_stage, greedy=pc.is_last_pp_stage)
         if pc.is_last_pp_stage:
-            tok = out[:, -1].argmax(-1)
+            tok = out
         else:
             dist.send(out.contiguous(), dst=pc.get_pp_next_rank())
             tok = torch.empty(B, dtype=torch.long, device=self.device)
@@ -181,8 +180,7 @@ class LlamaRunner:
             torch.cuda.current_stream(self.device).wait_stream(side)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                logits = self.model(tok_in[:, None], ctx, last_only=True)
-                tok_out = logits[:, -1].argmax(-1)
+                tok_out = self.model(tok_in[:, None], ctx, last_only=True, greedy=True)
             entry = (graph, tok_in, tok_out)
             self._graphs[B] = entry
         else:
@@ -200,8 +198,7 @@ class LlamaRunner:
         graph's static output: use it before the next call with the same B."""
         last = self.pctx.is_last_pp_stage
         if not (self.use_graphs and getattr(ctx, "plan_static", False)):
-            out = self.model(x, ctx, last_only=last)
-            return out[:, -1].argmax(-1) if last else out
+            return self.model(x, ctx, last_only=last, greedy=last)
         key = ("stage", B)
         entry = self._graphs.get(key)
         if entry is None:
@@ -214,8 +211,7 @@ class LlamaRunner:
             torch.cuda.current_stream(self.device).wait_stream(side)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                out = self.model(x_in, ctx, last_only=last)
-                res = out[:, -1].argmax(-1) if last else out
+                res = self.model(x_in, ctx, last_only=last, greedy=last)
             entry = (graph, x_in, res)
             self._graphs[key] = entry
         else:
