@@ -200,27 +200,48 @@ struct Item {
   Half x[2];
 };
 
-__device__ __forceinline__ bool load_item(const PrefillParams& p, int item, Item& it) {
+// The per-sequence values of an item, read with independent loads. A warp issues them
+// one item ahead (issue_item) and turns them into the Item at the next item boundary
+// (finish_item), so the loads' latency overlaps the current item instead of delaying
+// the first MMA of the next one.
+struct ItemLoads {
+  int b, h, pk_rev;
+  int qo0, qo1, ip0, ip1, lpl, rs;
+};
+
+__device__ __forceinline__ void issue_item(const PrefillParams& p, int item, ItemLoads& L) {
+  if (item >= p.n_items) return;
   const int per = p.batch * p.hkv;
-  const int pk_rev = item / per;
-  const int rem = item - pk_rev * per;
-  it.b = rem / p.hkv;
-  it.h = rem - it.b * p.hkv;
+  L.pk_rev = item / per;
+  const int rem = item - L.pk_rev * per;
+  L.b = rem / p.hkv;
+  L.h = rem - L.b * p.hkv;
+  L.qo0 = p.qo_indptr[L.b];
+  L.qo1 = p.qo_indptr[L.b + 1];
+  L.ip0 = p.indptr[L.b];
+  L.ip1 = p.indptr[L.b + 1];
+  L.lpl = p.lpl[L.b];
+  L.rs = p.q_row_start ? p.q_row_start[L.b] : L.qo0;
+}
+
+__device__ __forceinline__ bool finish_item(const PrefillParams& p, const ItemLoads& L,
+                                            Item& it) {
+  it.b = L.b;
+  it.h = L.h;
   const int tpt = p.tokens_per_tile;
-  it.qo_len = p.qo_indptr[it.b + 1] - p.qo_indptr[it.b];
+  it.qo_len = L.qo1 - L.qo0;
   const int ntile_q = (it.qo_len + tpt - 1) / tpt;
   const int npairs = (ntile_q + 1) / 2;
-  const int pk = npairs - 1 - pk_rev;
+  const int pk = npairs - 1 - L.pk_rev;
   if (pk < 0) return false;
-  it.kv_beg = p.indptr[it.b];
-  it.npages = p.indptr[it.b + 1] - it.kv_beg;
-  it.kv_len = it.npages > 0 ? (it.npages - 1) * kPS + p.lpl[it.b] : 0;
-  const int rs = p.q_row_start ? p.q_row_start[it.b] : p.qo_indptr[it.b];
+  it.kv_beg = L.ip0;
+  it.npages = L.ip1 - L.ip0;
+  it.kv_len = it.npages > 0 ? (it.npages - 1) * kPS + L.lpl : 0;
   int last_tok = -1;
   for (int x = 0; x < 2; ++x) {
     Half& hx = it.x[x];
     hx.i0 = (2 * pk + x) * tpt;
-    hx.row0 = rs + hx.i0;
+    hx.row0 = L.rs + hx.i0;
     hx.any = hx.i0 < it.qo_len;
     hx.lim_base = it.kv_len - it.qo_len + hx.i0;
     if (hx.any) last_tok = min(hx.i0 + tpt, it.qo_len) - 1;
@@ -228,6 +249,12 @@ __device__ __forceinline__ bool load_item(const PrefillParams& p, int item, Item
   const int kv_span = p.causal ? min(it.kv_len, it.kv_len - it.qo_len + last_tok + 1) : it.kv_len;
   it.ntiles = (kv_span + kBN - 1) / kBN;
   return it.ntiles > 0;
+}
+
+__device__ __forceinline__ bool load_item(const PrefillParams& p, int item, Item& it) {
+  ItemLoads L;
+  issue_item(p, item, L);
+  return finish_item(p, L, it);
 }
 
 // ----------------------------------------------------------------- the kernel
@@ -435,9 +462,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       int t = 0, n_it = 0;
+      ItemLoads nxt;
+      issue_item(p, blockIdx.x, nxt);
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        const ItemLoads cur = nxt;
+        issue_item(p, item + gridDim.x, nxt);
         Item it;
-        if (!load_item(p, item, it)) continue;
+        if (!finish_item(p, cur, it)) continue;
         const int qs = n_it & 1;
         if (*abort_flag || !mbar_wait(&q_full[qs], (n_it >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
@@ -485,9 +516,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- output stores
     int n_it = 0;
     bool ok = true;
+    ItemLoads nxt;
+    issue_item(p, blockIdx.x, nxt);
     for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      const ItemLoads cur = nxt;
+      issue_item(p, item + gridDim.x, nxt);
       Item it;
-      if (!load_item(p, item, it)) continue;
+      if (!finish_item(p, cur, it)) continue;
       const int qs = n_it & 1;
       for (int x = 0; x < 2; ++x) {
         if (!__all_sync(0xffffffffu, mbar_wait(&o_staged[x * 2 + qs], (n_it >> 1) & 1))) {
@@ -540,9 +575,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl = p.scale_log2;
     int t = 0, n_it = 0;
     bool ok = true;
+    ItemLoads nxt;
+    issue_item(p, blockIdx.x, nxt);
     for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      const ItemLoads cur = nxt;
+      issue_item(p, item + gridDim.x, nxt);
       Item it;
-      if (!load_item(p, item, it)) continue;
+      if (!finish_item(p, cur, it)) continue;
       const Half& hx = it.x[x];
       const bool row_valid = (hx.i0 + tok) < it.qo_len;
       // last kv position the row sees (-1: none)
