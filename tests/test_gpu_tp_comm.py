@@ -119,8 +119,8 @@ def _peer_main(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_peer_allreduce_rmsnorm_two_ranks():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_allreduce_rmsnorm(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     with mp.get_context("spawn").Manager() as m:
