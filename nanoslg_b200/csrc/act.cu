@@ -20,6 +20,8 @@ union AVec {
 template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* gu, int64_t gu_stride, T* out,
                                                        int64_t out_stride, int rows, int inter) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   const int per_row = inter / VEC;
   const int64_t total = static_cast<int64_t>(rows) * per_row;
@@ -51,15 +53,14 @@ int launch_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t
   int64_t blocks = (total + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
+  const dim3 grid(static_cast<unsigned>(blocks));
   if (dtype == NSLG_DTYPE_BF16)
-    silu_mul_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(gate_up), gu_stride, static_cast<__nv_bfloat16*>(out),
-        out_stride, rows, inter);
-  else
-    silu_mul_kernel<float><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-        static_cast<const float*>(gate_up), gu_stride, static_cast<float*>(out), out_stride,
-        rows, inter);
-  return check_launch("silu_mul");
+    return launch_pdl("silu_mul", silu_mul_kernel<__nv_bfloat16>, grid, dim3(threads), 0, stream,
+                      static_cast<const __nv_bfloat16*>(gate_up), gu_stride,
+                      static_cast<__nv_bfloat16*>(out), out_stride, rows, inter);
+  return launch_pdl("silu_mul", silu_mul_kernel<float>, grid, dim3(threads), 0, stream,
+                    static_cast<const float*>(gate_up), gu_stride, static_cast<float*>(out),
+                    out_stride, rows, inter);
 }
 
 }  // namespace nslg

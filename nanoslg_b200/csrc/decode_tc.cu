@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + stages;
   float* comb = reinterpret_cast<float*>(empty + stages);  // [8 warps][G][D] o, then m, l
 
+  pdl_wait();   // q (rotated by the append kernel) and the plan come from earlier work
   // The CSR lookups (slice bounds, sequence of a page, segment ends, last-page lengths)
   // are chains of dependent loads; with the arrays in shared memory (one coalesced load
   // by the whole CTA) they no longer delay the first TMA issue or each new segment.
@@ -579,8 +580,7 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
-  kern<<<p.grid, kThreads, smem, stream>>>(tk, tv, p);
-  int rc = check_launch("decode_tc");
+  int rc = launch_pdl("decode_tc", kern, dim3(p.grid), dim3(kThreads), smem, stream, tk, tv, p);
   if (rc != NSLG_OK) return rc;
   // programmatic dependent launch: the merge grid is launched while the decode grid
   // drains and starts its work once the decode grid has completed

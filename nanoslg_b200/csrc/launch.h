@@ -20,6 +20,28 @@ int check_launch(const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Launches `kern` with programmatic dependent launch allowed: the grid may be scheduled
+// while the previous kernel on the stream drains, which hides the launch gap between
+// consecutive kernels (also inside CUDA graphs). The kernel must execute pdl_wait()
+// (common.cuh) before it reads anything the previous kernel wrote.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+  return check_launch(what);
+}
+
 // 3-D tiled bf16 tensor map with 128-byte swizzle (strides in bytes, dims innermost first).
 int encode_tiled_3d_bf16(CUtensorMap* out, const void* base, uint64_t d0, uint64_t d1,
                          uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,

@@ -28,6 +28,8 @@ union NVec {
 
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_residual_kernel(const NormParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   const int row = blockIdx.x;
   const int nv = p.hidden / VEC;
@@ -95,10 +97,10 @@ int launch_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int6
   int threads = 32;
   while (threads < nv && threads < 256) threads *= 2;
   if (dtype == NSLG_DTYPE_BF16)
-    rmsnorm_residual_kernel<__nv_bfloat16><<<rows, threads, 0, stream>>>(p);
-  else
-    rmsnorm_residual_kernel<float><<<rows, threads, 0, stream>>>(p);
-  return check_launch("rmsnorm_residual");
+    return launch_pdl("rmsnorm_residual", rmsnorm_residual_kernel<__nv_bfloat16>, dim3(rows),
+                      dim3(threads), 0, stream, p);
+  return launch_pdl("rmsnorm_residual", rmsnorm_residual_kernel<float>, dim3(rows),
+                    dim3(threads), 0, stream, p);
 }
 
 }  // namespace nslg

@@ -45,6 +45,8 @@ __device__ __forceinline__ float rot_term(float x, float c) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) rope_kv_append_kernel(const RopeParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   const int half = p.d / 2;
   const int vh = half / VEC;   // 16-byte vectors per half row
@@ -137,11 +139,12 @@ int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, con
   if (total == 0) return NSLG_OK;
   const int threads = 256;
   const int64_t blocks = (total + threads - 1) / threads;
+  const dim3 grid(static_cast<unsigned>(blocks));
   if (dtype == NSLG_DTYPE_BF16)
-    rope_kv_append_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
-  else
-    rope_kv_append_kernel<float><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
-  return check_launch("rope_kv_append");
+    return launch_pdl("rope_kv_append", rope_kv_append_kernel<__nv_bfloat16>, grid,
+                      dim3(threads), 0, stream, p);
+  return launch_pdl("rope_kv_append", rope_kv_append_kernel<float>, grid, dim3(threads), 0,
+                    stream, p);
 }
 
 }  // namespace nslg

@@ -86,6 +86,8 @@ union NVec {
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const ArParams p) {
+  pdl_wait();      // the partial is the previous kernel's output
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   const int nv = p.hidden / VEC;                  // 16-byte vectors per row
   const int64_t units_per_row = 2 * static_cast<int64_t>(nv);
@@ -306,8 +308,8 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
   p.status = dev_status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == NSLG_DTYPE_BF16)
-    tp_allreduce_rmsnorm_kernel<__nv_bfloat16><<<kGrid, kThreads, 0, st>>>(p);
-  else
-    tp_allreduce_rmsnorm_kernel<float><<<kGrid, kThreads, 0, st>>>(p);
-  return check_launch("tp_allreduce_rmsnorm");
+    return launch_pdl("tp_allreduce_rmsnorm", tp_allreduce_rmsnorm_kernel<__nv_bfloat16>,
+                      dim3(kGrid), dim3(kThreads), 0, st, p);
+  return launch_pdl("tp_allreduce_rmsnorm", tp_allreduce_rmsnorm_kernel<float>, dim3(kGrid),
+                    dim3(kThreads), 0, st, p);
 }
