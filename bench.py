@@ -432,6 +432,57 @@ def run_llama70b_c5(device, world, rank, steps=256, batch=32, prompt=2048):
     return out
 
 
+def run_allreduce(device, world, rank, hidden=4096, rows_list=(1, 64, 256), calls=50,
+                  replays=10):
+    """The fused TP reduction (nslg_tp_allreduce_rmsnorm: all-reduce of a RowParallel
+    partial + residual add + RMSNorm over NVLink peer memory) against what it replaces
+    (NCCL all-reduce + the rmsnorm kernel), bf16 [rows, hidden], each timed as ``calls``
+    back-to-back calls captured in one CUDA graph and replayed ``replays`` times; CUDA
+    events, max over ranks, microseconds per call."""
+    from nanoslg_b200 import ops
+    from nanoslg_b200.tp_comm import PeerAllReduce
+    bf = torch.bfloat16
+    peer = PeerAllReduce(torch.distributed.group.WORLD, rank, world, device, max(rows_list),
+                         hidden, bf)
+    w = torch.ones(hidden, dtype=bf, device=device)
+    out = {}
+    for rows in rows_list:
+        x = torch.randn(rows, hidden, device=device).to(bf)
+        r = torch.randn(rows, hidden, device=device).to(bf)
+
+        def nccl():
+            torch.distributed.all_reduce(x)
+            return ops.rmsnorm_residual(x, w, 1e-5, residual=r)
+
+        def fused():
+            return peer.allreduce_add_norm(x, r, w, 1e-5)
+
+        for name, fn in (("nccl_allreduce_plus_rmsnorm_us", nccl), ("fused_us", fused)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(calls):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize(device)
+            torch.distributed.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(replays):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (calls * replays)], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            out.setdefault(f"rows{rows}", {})[name] = round(float(t.item()), 2)
+            del g
+    ops.check_device_status(device)
+    peer.close()
+    return {"world": world, "hidden": hidden, "dtype": "bf16", **out}
+
+
 # ------------------------------------------------------------------------ CPU side
 def cpu_reference(max_seconds, n_calls=None, seed=0):
     """The reference's contiguous attend (oracle/attention.py restating
@@ -483,7 +534,8 @@ def main():
     ap.add_argument("--tp-reduce", choices=["peer", "nccl"], default="peer",
                     help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
-    ap.add_argument("--only", choices=["all", "kernel", "model", "prefill"], default="all",
+    ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce"],
+                    default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg")
     a = ap.parse_args()
@@ -538,6 +590,15 @@ def main():
                               run_prefill_kernel(device)}), flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
+        return 0
+    if a.only == "allreduce":
+        if world < 2:
+            raise SystemExit("--only allreduce needs torchrun with 2 or more GPUs")
+        r = run_allreduce(device, world, rank)
+        if rank == 0:
+            print(json.dumps({"case": "allreduce", "tp_allreduce_rmsnorm": r}), flush=True)
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
         return 0
     if a.c5:
         r = run_llama70b_c5(device, world, rank)

@@ -58,3 +58,42 @@ def test_ops_refuse_cpu_tensors(lib):
     x = torch.zeros(2, 16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.rmsnorm_residual(x, torch.ones(16), 1e-5)
+
+
+def test_tp_plan_and_ipc_argument_errors_without_gpu(lib):
+    """The tensor-parallel reduction, the decode planner, page zeroing and the IPC helpers
+    reject bad arguments on the host, before any CUDA call."""
+    vp = ctypes.c_void_p
+    stages = (vp * 2)(vp(16), vp(32))
+    # world 1 is not a tensor-parallel group
+    rc = lib.nslg_tp_allreduce_rmsnorm(N.DTYPE_BF16, 4, 4096, 1, 0, vp(16), 4096,
+                                       ctypes.cast(stages, vp), 1 << 20, vp(16), vp(16), 4096,
+                                       vp(16), vp(16), 4096, 1e-5, 10**9, None, None)
+    assert rc == N.ERR_ARG and b"world" in lib.nslg_last_error()
+    # stage buffers too small for the rows: 4 * world * rows * hidden * 2 bytes needed
+    rc = lib.nslg_tp_allreduce_rmsnorm(N.DTYPE_BF16, 64, 4096, 2, 0, vp(16), 4096,
+                                       ctypes.cast(stages, vp), 1 << 20, vp(16), vp(16), 4096,
+                                       vp(16), vp(16), 4096, 1e-5, 10**9, None, None)
+    assert rc == N.ERR_WORKSPACE and b"stage bytes" in lib.nslg_last_error()
+    # rows longer than 16 KiB are not supported
+    rc = lib.nslg_tp_allreduce_rmsnorm(N.DTYPE_BF16, 1, 16384, 2, 1, vp(16), 16384,
+                                       ctypes.cast(stages, vp), 1 << 30, vp(16), vp(16), 16384,
+                                       vp(16), vp(16), 16384, 1e-5, 10**9, None, None)
+    assert rc == N.ERR_UNSUPPORTED
+    # a non-positive wait limit would make every wait give up at once
+    rc = lib.nslg_tp_allreduce_rmsnorm(N.DTYPE_BF16, 1, 4096, 2, 1, vp(16), 4096,
+                                       ctypes.cast(stages, vp), 1 << 20, vp(16), vp(16), 4096,
+                                       vp(16), vp(16), 4096, 1e-5, 0, None, None)
+    assert rc == N.ERR_ARG and b"timeout" in lib.nslg_last_error()
+    # the planner takes 1..4096 sequences
+    args = [vp(16)] * 2 + [0, None, vp(16), 512, 64] + [vp(16)] * 7 + [1024, None, None]
+    assert lib.nslg_plan_decode(0, 16, *args) == N.ERR_UNSUPPORTED
+    assert lib.nslg_plan_decode(4097, 16, *args) == N.ERR_UNSUPPORTED
+    assert lib.nslg_plan_decode(4, 0, *args) == N.ERR_ARG
+    # page zeroing: nothing to do is fine, bad sizes are not
+    assert lib.nslg_zero_pages(None, 0, None, 1, 1, 16, None, None) == N.OK
+    assert lib.nslg_zero_pages(vp(16), 2, vp(16), 1, 64, 24, None, None) == N.ERR_ARG
+    # IPC helpers
+    ptr = vp()
+    assert lib.nslg_ipc_alloc(0, ctypes.byref(ptr), ctypes.create_string_buffer(64)) == N.ERR_ARG
+    assert lib.nslg_ipc_open(None, ctypes.byref(ptr)) == N.ERR_ARG
