@@ -176,6 +176,8 @@ class PagePool:
         # than the views themselves)
         self.k_layers = [self.k[i] for i in range(cfg.num_layers)]
         self.v_layers = [self.v[i] for i in range(cfg.num_layers)]
+        self.layer_ptrs = [(a.data_ptr(), b.data_ptr())
+                           for a, b in zip(self.k_layers, self.v_layers)]
 
     def alloc(self, n=1) -> Optional[List[int]]:
         with self._lock:
@@ -474,6 +476,7 @@ class B200CacheContext(CacheContext):
         # Anything else takes the general loop below.
         self._wi = None
         self._wi_src = None
+        self._direct_ptrs = None
         fast = self._is_decode and iw == 1 and B > 0
         if fast:
             rc = pool.ref_count
@@ -631,6 +634,10 @@ class B200CacheContext(CacheContext):
     def attend(self, layer_idx, q, k_new, v_new, n_heads, n_kv_heads):
         """q, k_new already rotated (the ABC contract, models.py:99-105)."""
         self._check_width(q)
+        if self._is_decode:
+            out = self._decode_direct(layer_idx, q, k_new, v_new)
+            if out is not None:
+                return out
         pool = self.cache.pool
         ops.rope_kv_append(None, k_new, v_new, None, None, None, self._write_loc,
                            pool.k_layers[layer_idx], pool.v_layers[layer_idx], rotate=False)
@@ -645,6 +652,45 @@ class B200CacheContext(CacheContext):
         q_rot = ops.rope_kv_append(q, k_new, v_new, self._pos_i32, cos, sin, self._write_loc,
                                    pool.k_layers[layer_idx], pool.v_layers[layer_idx])
         return self._attention(layer_idx, q_rot.view(B, S, hq, d))
+
+    def _decode_direct(self, layer_idx, q, k, v):
+        """Decode ``attend`` straight through the C entry points (KV append, then paged
+        decode), skipping the generic wrappers' per-call checks, for the common inputs:
+        dense CUDA q [B, 1, Hq, D] and k, v [B, 1, Hkv, D] of the pool's dtype and head
+        sizes. Returns None for anything else (the caller takes the generic path)."""
+        pool = self.cache.pool
+        pk = pool.k_layers[layer_idx]
+        dt = pk.dtype
+        if not (q.is_cuda and q.dtype == dt and k.dtype == dt and v.dtype == dt
+                and q.dim() == 4 and k.dim() == 4 and k.shape == v.shape
+                and k.shape[0] == q.shape[0] and k.shape[1] == 1
+                and k.shape[2] == pk.shape[2] and k.shape[3] == pk.shape[3]
+                and q.shape[3] == pk.shape[3] and q.shape[2] % k.shape[2] == 0
+                and q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+            return None
+        B, _, hq, d = q.shape
+        P, ps, hkv, _ = pk.shape
+        lib, dtc, status, ws_t = self.cache._direct_state(B, hq, d, q.device)
+        ws, wsb = ws_t.data_ptr(), ws_t.numel()
+        ptrs = self._direct_ptrs
+        if ptrs is None:
+            ptrs = self._direct_ptrs = (self._write_loc.data_ptr(), self.kv_indptr.data_ptr(),
+                                        self.kv_indices.data_ptr(),
+                                        self.kv_last_page_len.data_ptr())
+        stream = ops._stream(q)
+        pkp, pvp = pool.layer_ptrs[layer_idx]
+        rc = lib.nslg_rope_kv_append(dtc, B, hkv, hkv, d, None, 0, k.data_ptr(), hkv * d,
+                                     v.data_ptr(), hkv * d, None, None, None, None, 0, ptrs[0],
+                                     pkp, pvp, P * ps, status, stream)
+        if rc:
+            raise N.NativeError("nslg_rope_kv_append", rc, lib.nslg_last_error().decode())
+        out = torch.empty((B, 1, hq * d), dtype=dt, device=q.device)
+        rc = lib.nslg_paged_decode(dtc, B, hq, hkv, d, ps, q.data_ptr(), hq * d, out.data_ptr(),
+                                   hq * d, pkp, pvp, P, ptrs[1], ptrs[2], ptrs[3],
+                                   self._sm_scale, ws, wsb, status, stream)
+        if rc:
+            raise N.NativeError("nslg_paged_decode", rc, lib.nslg_last_error().decode())
+        return out
 
     def _check_width(self, q):
         if q.shape[0] != self.batch_size or q.shape[1] != self._iw:
@@ -675,6 +721,7 @@ class B200PagedKVCache(KVCacheManager):
         self.tree = RadixTree(cfg.page_size, self.pool) if cfg.enable_prefix_caching else None
         self.seqs: Dict[str, _PagedSeqState] = {}
         self._static_plans: Dict[Tuple[int, int], torch.Tensor] = {}
+        self._direct = {}             # (batch, heads, head_dim) -> direct decode state
         self._pin_buf = None          # pinned host staging of the plan, reused per forward
         self._pin_event = None        # recorded after the copy out of it
         # device planning of decode steps (CUDA pools): block tables mirrored on the GPU,
@@ -708,6 +755,21 @@ class B200PagedKVCache(KVCacheManager):
         if buf is not None and size > buf.numel():
             return None
         return buf
+
+    def _direct_state(self, batch, hq, d, device):
+        """(library, dtype code, status word pointer, decode workspace pointer and size)
+        for the direct decode path, looked up once per (batch, heads, head_dim)."""
+        key = (batch, hq, d)
+        st = self._direct.get(key)
+        if st is None:
+            lib = N.lib()
+            wsb = lib.nslg_decode_workspace_bytes(batch, hq, d)
+            ws = ops._STATE.workspace(device, wsb)
+            # the tuple holds the workspace tensor itself: it stays allocated even if the
+            # shared workspace is regrown for a larger call later
+            st = (lib, ops._dtype_code(self.pool.k), ops.status_word(device).data_ptr(), ws)
+            self._direct[key] = st
+        return st
 
     def _pinned_plan(self, size):
         """A pinned int32 host buffer of ``size`` entries for this forward's plan; the
@@ -798,6 +860,7 @@ class B200PagedKVCache(KVCacheManager):
         ctx._wi_src = (pids, [n % ps for n in starts])
         ctx._sm_scale = 1.0 / math.sqrt(self.cfg.head_dim)
         ctx._pos64 = None
+        ctx._direct_ptrs = None
         upd = []
         for st in dirty:
             bt = st.block_table
