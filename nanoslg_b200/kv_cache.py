@@ -438,8 +438,11 @@ class B200CacheContext(CacheContext):
     Host side (once per forward) it computes what ``FlashInferCacheContext.__init__``
     computes (kv_cache.py:547-632): start positions and sequence lengths, the per-token
     (page, slot) write targets with copy-on-write of shared pages, and the CSR page list
-    ``kv_indptr / kv_indices / kv_last_page_len`` (+ ``qo_indptr`` for prefill).  They
-    travel to the device in one copy as int32 arrays:
+    ``kv_indptr / kv_indices / kv_last_page_len`` (+ ``qo_indptr`` for prefill).  On a
+    CUDA pool a decode step (one new token per sequence, no copy-on-write) is planned on
+    the GPU instead (``B200PagedKVCache._begin_decode_device``, ``nslg_plan_decode``);
+    otherwise the arrays travel to the device in one copy. Either way they are int32
+    views of one buffer:
 
       positions [B*iw]  absolute position of every input cell (0 for left padding)
       write_loc [B*iw]  page*page_size + slot of every input cell, -1 = not written
@@ -496,12 +499,6 @@ class B200CacheContext(CacheContext):
                 if tu[pid] < used:
                     tu[pid] = used
             self._wi_src = (pids, slots.tolist())
-            if cache.device_plan and B <= 4096:
-                # the plan arrays are built on the GPU from the device block tables
-                self._sm_scale = 1.0 / math.sqrt(cfg.head_dim)
-                self._pos64 = None
-                cache._plan_decode_on_device(self, sts, start)
-                return
             positions = start.astype(np.int32).reshape(B, 1)
             write_loc = (np.asarray(pids, dtype=np.int64) * ps + slots).astype(np.int32).reshape(B, 1)
         else:
@@ -875,37 +872,6 @@ class B200PagedKVCache(KVCacheManager):
         self._launch_device_plan(ctx, np.asarray(slots, dtype=np.int32),
                                  np.asarray(starts, dtype=np.int64), upd)
         return ctx
-
-    def _plan_decode_on_device(self, ctx, sts, start):
-        """Fills ``ctx``'s plan views for a decode step with nslg_plan_decode: uploads the
-        batch's table rows, start positions and the block-table entries changed since the
-        last upload (one small host->device copy); the kernels build the rest."""
-        B = len(sts)
-        ps = self.cfg.page_size
-        slots = np.empty(B, dtype=np.int32)
-        upd = []
-        longest = 0
-        for b, st in enumerate(sts):
-            if st.slot < 0:
-                st.slot = self._slot_free.pop() if self._slot_free else self._slot_next
-                if st.slot == self._slot_next:
-                    self._slot_next += 1
-                st.block_table.dirty_from = 0
-            slots[b] = st.slot
-            bt = st.block_table
-            n = len(bt)
-            if n > longest:
-                longest = n
-            if bt.dirty_from < n:
-                d = bt.dirty_from
-                u = np.empty((n - d, 3), dtype=np.int32)
-                u[:, 0] = st.slot
-                u[:, 1] = np.arange(d, n, dtype=np.int32)
-                u[:, 2] = bt.arr[d:n]
-                upd.append(u)
-                bt.dirty_from = n
-        self._ensure_tables(self._slot_next, longest)
-        self._launch_device_plan(ctx, slots, start, upd)
 
     def _launch_device_plan(self, ctx, slots, start, upd):
         """Uploads (slots, start positions, table entries ``upd``, pages to zero) and
