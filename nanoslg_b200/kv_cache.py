@@ -421,15 +421,34 @@ class _BlockTable(list):
 
 
 class _PagedSeqState:
-    __slots__ = ("seq_id", "block_table", "num_tokens", "prefix_len", "token_ids", "slot")
+    __slots__ = ("seq_id", "block_table", "_n", "prefix_len", "token_ids", "slot")
+    # bumped by every assignment to num_tokens (a decode batch cached by the manager is
+    # only reused while nothing outside its own begin/end changed a token count)
+    version = 0
 
     def __init__(self, sid, prefix_pages=None, plen=0, tids=None):
         self.slot = -1          # row of the device block tables (device planning)
         self.seq_id = sid
         self.block_table = _BlockTable(prefix_pages or [])
-        self.num_tokens = plen
+        self._n = plen
         self.prefix_len = plen
         self.token_ids = list(tids or [])
+
+    @property
+    def num_tokens(self):
+        return self._n
+
+    @num_tokens.setter
+    def num_tokens(self, v):
+        self._n = v
+        _PagedSeqState.version += 1
+
+
+class _DecodeBatch:
+    """A decode batch planned on the device, kept for the next step of the same batch:
+    its sequence states, table rows, token counts before the step, the page holding each
+    sequence's next position, and the longest block table."""
+    __slots__ = ("ids", "mut", "ver", "sts", "slots", "n0", "cur_pid", "longest")
 
 
 class B200CacheContext(CacheContext):
@@ -522,7 +541,7 @@ class B200CacheContext(CacheContext):
         """(page, slot) of every new token of every sequence (kv_cache.py:575-594)."""
         if self._wi is None:
             pids, slots = self._wi_src
-            self._wi = [[(p_, s_)] for p_, s_ in zip(pids, slots)]
+            self._wi = [[(int(p_), int(s_))] for p_, s_ in zip(pids, slots)]
         return self._wi
 
     def _general_write_targets(self, sts, new_token_counts, iw, ps):
@@ -719,6 +738,8 @@ class B200PagedKVCache(KVCacheManager):
         self.seqs: Dict[str, _PagedSeqState] = {}
         self._static_plans: Dict[Tuple[int, int], torch.Tensor] = {}
         self._direct = {}             # (batch, heads, head_dim) -> direct decode state
+        self._mut = 0                 # bumped by every bookkeeping change outside the
+        self._dc = None               # cached decode batch's own steps (_DecodeBatch)
         self._pin_buf = None          # pinned host staging of the plan, reused per forward
         self._pin_event = None        # recorded after the copy out of it
         # device planning of decode steps (CUDA pools): block tables mirrored on the GPU,
@@ -869,8 +890,83 @@ class B200PagedKVCache(KVCacheManager):
             upd.append(u)
             bt.dirty_from = nb
         self._ensure_tables(self._slot_next, longest)
-        self._launch_device_plan(ctx, np.asarray(slots, dtype=np.int32),
-                                 np.asarray(starts, dtype=np.int64), upd)
+        c = _DecodeBatch()
+        c.ids = tuple(seq_ids)
+        c.mut = self._mut
+        c.ver = _PagedSeqState.version
+        c.sts = sts
+        c.slots = np.asarray(slots, dtype=np.int32)
+        c.n0 = np.asarray(starts, dtype=np.int64)
+        c.cur_pid = np.asarray(pids, dtype=np.int64)
+        c.longest = longest
+        self._dc = c
+        ctx._dc = c
+        self._launch_device_plan(ctx, c.slots, c.n0, upd)
+        return ctx
+
+    def _begin_decode_cached(self, c, seq_ids, ntoks):
+        """Next decode step of the cached batch ``c``: only the sequences whose next
+        position opens a page are visited (page extension in batch order, copy-on-write
+        check); everything else is array arithmetic. None (cache dropped) when a page to
+        write is shared: the general path takes the step."""
+        ps = self.cfg.page_size
+        n0 = c.n0
+        dirty = []
+        opening = np.flatnonzero(n0 % ps == 0)
+        if opening.size:
+            rc = self.pool.ref_count
+            for i in opening.tolist():
+                st = c.sts[i]
+                bt = st.block_table
+                pi = int(n0[i]) // ps
+                nb = len(bt)
+                if pi >= nb:
+                    bt.extend(self._alloc(pi + 1 - nb))
+                    nb = len(bt)
+                    if nb > c.longest:
+                        c.longest = nb
+                pid = bt[pi]
+                if rc[pid] > 1:
+                    self._dc = None
+                    return None
+                c.cur_pid[i] = pid
+                if bt.dirty_from < nb:
+                    dirty.append(st)
+        # tokens_used of each sequence's page: positions fill a private page in order
+        tu = self.pool.tokens_used
+        for pid, used in zip(c.cur_pid.tolist(), (n0 % ps + 1).tolist()):
+            if tu[pid] < used:
+                tu[pid] = used
+        upd = []
+        for st in dirty:
+            bt = st.block_table
+            d, nb = bt.dirty_from, len(bt)
+            u = np.empty((nb - d, 3), dtype=np.int32)
+            u[:, 0] = st.slot
+            u[:, 1] = np.arange(d, nb, dtype=np.int32)
+            u[:, 2] = bt.arr[d:nb]
+            upd.append(u)
+            bt.dirty_from = nb
+        self._ensure_tables(self._slot_next, c.longest)
+        B = len(c.sts)
+        ctx = B200CacheContext.__new__(B200CacheContext)
+        ctx.cache = self
+        ctx.seq_ids = seq_ids
+        ctx.new_token_counts = ntoks
+        ctx.input_offsets = [0] * B
+        ctx.batch_size = B
+        ctx.start_positions = n0.tolist()
+        ctx.seq_lens = (n0 + 1).tolist()
+        ctx.max_kv_len = int(n0.max()) + 1
+        ctx._is_decode = True
+        ctx._iw = 1
+        ctx._wi = None
+        ctx._wi_src = (c.cur_pid.copy(), n0 % ps)
+        ctx._sm_scale = 1.0 / math.sqrt(self.cfg.head_dim)
+        ctx._pos64 = None
+        ctx._direct_ptrs = None
+        ctx._dc = c
+        self._launch_device_plan(ctx, c.slots, n0, upd)
         return ctx
 
     def _launch_device_plan(self, ctx, slots, start, upd):
@@ -930,6 +1026,7 @@ class B200PagedKVCache(KVCacheManager):
                status, stream.cuda_stream)
 
     def allocate_sequence(self, seq_id, token_ids=None, num_tokens=0):
+        self._mut += 1
         tids = token_ids or []
         total = len(tids) if tids else num_tokens
         plen, ppages = 0, []
@@ -948,6 +1045,7 @@ class B200PagedKVCache(KVCacheManager):
         return plen
 
     def extend_sequence(self, seq_id, num_new=1):
+        self._mut += 1
         st = self.seqs[seq_id]
         need = math.ceil((st.num_tokens + num_new) / self.cfg.page_size)
         if need > len(st.block_table):
@@ -956,9 +1054,16 @@ class B200PagedKVCache(KVCacheManager):
     def begin_forward(self, seq_ids, ntoks, offsets=None):
         if (self.device_plan and 0 < len(seq_ids) <= 4096 and not any(offsets or ())
                 and all(n == 1 for n in ntoks)):
+            c = self._dc
+            if (c is not None and c.mut == self._mut and c.ver == _PagedSeqState.version
+                    and c.ids == tuple(seq_ids)):
+                ctx = self._begin_decode_cached(c, seq_ids, ntoks)
+                if ctx is not None:
+                    return ctx
             ctx = self._begin_decode_device(seq_ids, ntoks)
             if ctx is not None:
                 return ctx
+        self._mut += 1
         # extend_sequence for every sequence, inlined (sequences in order, so the page
         # allocation order is the reference's)
         sts = [self.seqs[s] for s in seq_ids]
@@ -971,12 +1076,22 @@ class B200PagedKVCache(KVCacheManager):
         return B200CacheContext(self, seq_ids, ntoks, offsets, sts)
 
     def end_forward(self, ctx):
+        c = getattr(ctx, "_dc", None)
+        if c is not None and c is self._dc:
+            # a step of the cached decode batch: one token each, cache kept in step
+            for st in c.sts:
+                st._n += 1
+            c.n0 += 1
+            return
+        self._mut += 1
         for b in range(ctx.batch_size):
-            self.seqs[ctx.seq_ids[b]].num_tokens += ctx.new_token_counts[b]
+            st = self.seqs[ctx.seq_ids[b]]
+            st._n += ctx.new_token_counts[b]
 
     def release_sequence(self, seq_id):
         if seq_id not in self.seqs:
             return
+        self._mut += 1
         st = self.seqs[seq_id]
         if self.tree and st.token_ids:
             nf = st.num_tokens // self.cfg.page_size

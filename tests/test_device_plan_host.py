@@ -1,0 +1,132 @@
+"""Host side of the device-planned decode step, on CPU.
+
+The manager of a CUDA pool plans decode steps on the GPU (csrc/plan.cu) from block
+tables mirrored in device memory: per step it sends the batch's table rows, the token
+counts before the step and the table entries changed since the last step. When the same
+batch steps again with nothing else changed, a cached copy of the batch's state is
+advanced instead of walking every sequence. Here the launch is replaced by a recorder
+that applies the uploads to a numpy mirror of the device tables, and three managers run
+the same random workload: device planning with the cache, device planning without it,
+and the host plan (kv_cache.py:547-632 restated). Page ids, block tables, refcounts,
+tokens_used, write targets and the mirrored tables must agree at every step."""
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
+
+
+class _Mirror:
+    """Stands in for nslg_plan_decode: applies the table updates, records the step."""
+
+    def __init__(self, mgr):
+        self.mgr = mgr
+        self.rows = {}
+        self.last = None
+
+    def __call__(self, ctx, slots, start, upd):
+        for u in upd:
+            for s, j, pg in u.tolist():
+                self.rows.setdefault(s, {})[j] = pg
+        self.mgr.pool.take_pending_zero()
+        self.last = (np.asarray(slots).tolist(), np.asarray(start).tolist())
+        ctx.plan_static = False
+
+
+def _managers(page_size, max_pages):
+    out = []
+    for mode in ("cached", "uncached", "host"):
+        cfg = KVCacheConfig(num_layers=1, num_kv_heads=1, num_qo_heads=1, head_dim=16,
+                            page_size=page_size, max_pages=max_pages, dtype=torch.float32,
+                            device=torch.device("cpu"), enable_prefix_caching=True)
+        m = B200PagedKVCache(cfg)
+        m.device_plan = mode != "host"
+        m._mode = mode
+        if m.device_plan:
+            m._mirror = _Mirror(m)
+            m._launch_device_plan = m._mirror
+        out.append(m)
+    return out
+
+
+@pytest.mark.parametrize("page_size", [1, 4, 16])
+def test_cached_decode_batches_match_host_plan(page_size):
+    mgrs = _managers(page_size, 6000)
+    rng = random.Random(11 + page_size)
+    shared = [rng.randrange(1000) for _ in range(3 * page_size)]
+    live, nxt = [], 0
+    hits = {"cached": 0}
+
+    def add(n_new):
+        nonlocal nxt
+        for _ in range(n_new):
+            sid = f"q{nxt}"
+            nxt += 1
+            r = rng.random()
+            if r < 0.15:
+                # the whole prompt matched in the tree and the last tokens recomputed: the
+                # pages to write are shared, copy on write on the host path
+                toks, back = list(shared), rng.randrange(1, 2 * page_size + 1)
+            elif r < 0.4:
+                toks, back = shared + [rng.randrange(1000) for _ in range(rng.randrange(1, 40))], 0
+            else:
+                toks, back = [rng.randrange(1000) for _ in range(rng.randrange(1, 120))], 0
+            for m in mgrs:
+                m.allocate_sequence(sid, toks)
+                m.seqs[sid].num_tokens = max(len(toks) - back, 0)
+            live.append(sid)
+
+    def drop(k):
+        for _ in range(k):
+            sid = live.pop(rng.randrange(len(live)))
+            for m in mgrs:
+                m.append_token_ids(sid, [1, 2, 3])
+                m.release_sequence(sid)
+
+    add(20)
+    for step in range(80):
+        if step in (20, 50):
+            drop(6)
+            add(8)
+        if step == 35:                      # another bookkeeping call drops the cache
+            for m in mgrs:
+                m.extend_sequence(live[0], 1)
+        if step == 65:                      # so does a direct token-count change
+            for m in mgrs:
+                m.seqs[live[1]].num_tokens += 0
+        ctxs = []
+        for m in mgrs:
+            if m._mode == "uncached":
+                m._dc = None
+            was = m._dc
+            c = m.begin_forward(list(live), [1] * len(live))
+            if m._mode == "cached" and was is not None and getattr(c, "_dc", None) is was:
+                hits["cached"] += 1
+            ctxs.append(c)
+        host = ctxs[2]
+        for m, c in zip(mgrs, ctxs):
+            assert c.start_positions == host.start_positions, (step, m._mode)
+            assert c._write_info == host._write_info, (step, m._mode)
+        for m in mgrs[1:]:
+            assert {s: list(st.block_table) for s, st in m.seqs.items()} == \
+                   {s: list(st.block_table) for s, st in mgrs[0].seqs.items()}, step
+            assert m.pool.ref_count == mgrs[0].pool.ref_count, step
+            assert m.pool.tokens_used == mgrs[0].pool.tokens_used, step
+        for m, c in zip(mgrs[:2], ctxs[:2]):
+            if getattr(c, "_dc", None) is None:
+                continue                    # the host path took this step
+            slots, starts = m._mirror.last
+            assert starts == host.start_positions
+            for sid, slot, n0 in zip(live, slots, starts):
+                row = m._mirror.rows.get(slot, {})
+                bt = list(m.seqs[sid].block_table)
+                npg = n0 // page_size + 1
+                assert [row.get(j) for j in range(npg)] == bt[:npg], (step, sid, m._mode)
+        for m, c in zip(mgrs, ctxs):
+            m.end_forward(c)
+        for m in mgrs[1:]:
+            assert {s: st.num_tokens for s, st in m.seqs.items()} == \
+                   {s: st.num_tokens for s, st in mgrs[0].seqs.items()}
+    assert hits["cached"] > 40
