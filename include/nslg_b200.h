@@ -211,6 +211,26 @@ int nslg_plan_decode(int batch, int page_size, const int32_t* slots, const int32
 int nslg_zero_pages(const int32_t* pages, int num_pages_to_zero, void* pool, int64_t layers,
                     int64_t num_pages, int64_t page_bytes, uint32_t* dev_status, void* stream);
 
+/* One decode step's planning from HOST arrays in a single call: nslg_zero_pages of
+ * zero_pages[0 .. num_zero) on both pools (pool_k, pool_v; skipped when num_zero == 0),
+ * then nslg_plan_decode. slots, starts, updates and zero_pages are host memory, copied
+ * into pinned, device-mapped staging owned by the library before the call returns (the
+ * caller may reuse them at once); the kernels read them from there. The plan goes to one
+ * device array `plan` laid out as
+ *   positions[B] | write_loc[B] | kv_indptr[B+1] | kv_last_page_len[B] | qo_indptr[B+1] |
+ *   q_row_start[B] | kv_indices[max_indices]
+ * (offsets 0, B, 2B, 3B+1, 4B+1, 5B+2, 6B+2 int32 entries). The staging is a ring of
+ * slots per device, a slot reused only after the kernels of its earlier call finished.
+ * Not capturable in a CUDA graph (NSLG_ERR_UNSUPPORTED during capture). Replaces the
+ * decode-step plan of FlashInferCacheContext.__init__ + _plan_flashinfer
+ * (kv_cache.py:547-632) and the page zeroing of PagePool.alloc (kv_cache.py:411). */
+int nslg_plan_decode_host(int batch, int page_size, const int32_t* slots, const int32_t* starts,
+                          int num_updates, const int32_t* updates, int num_zero,
+                          const int32_t* zero_pages, void* pool_k, void* pool_v, int64_t layers,
+                          int64_t num_pages, int64_t page_bytes, int32_t* block_tables,
+                          int64_t bt_stride, int64_t bt_rows, int32_t* plan,
+                          int64_t max_indices, uint32_t* dev_status, void* stream);
+
 /* ---------------------------------------------------------------- tensor parallel */
 
 #define NSLG_IPC_HANDLE_BYTES 64   /* cudaIpcMemHandle_t                                 */

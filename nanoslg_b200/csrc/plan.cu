@@ -11,6 +11,17 @@
 // and the page-list offsets kv_indptr with a block-wide exclusive scan; kernel 2 (one
 // CTA per sequence) gathers each sequence's page ids into kv_indices. Output layout and
 // values are those of the host plan, element for element.
+//
+// nslg_plan_decode_host does the same step from HOST arrays in one call: it copies them
+// into a pinned, device-mapped staging slot owned by the library (a ring of slots per
+// device, each reused only after the kernels that read it have finished, tracked with
+// one event per slot) and the kernels read the few hundred bytes straight from there;
+// the pages allocated since the last forward are zeroed (K and V pools) in the same
+// call. No device upload buffer, no separate copy: one host call per decode step.
+#include <cstring>
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -118,22 +129,71 @@ __global__ void __launch_bounds__(128) plan_decode_gather_kernel(const PlanParam
   for (int j = threadIdx.x; j < end - beg; j += blockDim.x) p.indices[beg + j] = row[j];
 }
 
-// Zeroes `pages` of a pool tensor [layers, pages_total, page elements]: block (i, l)
-// clears page pages[i] of layer l with 16-byte stores.
+// Zeroes `pages` of one or two pool tensors [layers, pages_total, page elements]: block
+// (i, l, z) clears page pages[i] of layer l of pool z with 16-byte stores.
 __global__ void __launch_bounds__(256) zero_pages_kernel(const int32_t* pages, int n,
-                                                         uint8_t* pool, int64_t num_pages,
+                                                         uint8_t* pool0, uint8_t* pool1,
+                                                         int64_t num_pages,
                                                          int64_t layer_stride,
                                                          int64_t page_bytes, uint32_t* status) {
   const int i = blockIdx.x, l = blockIdx.y;
   const int pg = pages[i];
   if (pg < 0 || pg >= num_pages) {
-    if (threadIdx.x == 0) report(status, NSLG_DEV_BAD_PLAN);
+    if (threadIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) report(status, NSLG_DEV_BAD_PLAN);
     return;
   }
+  uint8_t* pool = blockIdx.z ? pool1 : pool0;
   uint4* dst = reinterpret_cast<uint4*>(pool + l * layer_stride + pg * page_bytes);
   const int64_t nv = page_bytes / 16;
   for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) dst[v] = make_uint4(0u, 0u, 0u, 0u);
 }
+
+int check_plan_args(int batch, int page_size, int64_t bt_stride, int64_t bt_rows,
+                    int num_updates, int64_t max_indices) {
+  if (batch < 1 || batch > kScanThreads * kMaxItems)
+    return set_error(NSLG_ERR_UNSUPPORTED, "plan_decode: batch must be in [1, 4096]");
+  if (page_size <= 0 || bt_stride <= 0 || bt_rows <= 0 || num_updates < 0 || max_indices < 1)
+    return set_error(NSLG_ERR_ARG, "plan_decode: bad sizes");
+  if (bt_rows * bt_stride >= (int64_t{1} << 31))
+    return set_error(NSLG_ERR_UNSUPPORTED, "plan_decode: block tables larger than 2^31 entries");
+  return NSLG_OK;
+}
+
+int check_zero_args(int n, const void* pool, int64_t layers, int64_t num_pages,
+                    int64_t page_bytes) {
+  if (n < 0 || layers <= 0 || num_pages <= 0 || page_bytes <= 0 || page_bytes % 16 ||
+      layers > 65535)
+    return set_error(NSLG_ERR_ARG, "zero_pages: bad sizes");
+  if (!pool || (reinterpret_cast<uintptr_t>(pool) & 15u))
+    return set_error(NSLG_ERR_ARG, "zero_pages: null or misaligned pointer");
+  return NSLG_OK;
+}
+
+int launch_plan(const PlanParams& p, cudaStream_t st) {
+  plan_decode_scan_kernel<<<1, kScanThreads, 0, st>>>(p);
+  int rc = check_launch("plan_decode_scan");
+  if (rc != NSLG_OK) return rc;
+  plan_decode_gather_kernel<<<p.batch, 128, 0, st>>>(p);
+  return check_launch("plan_decode_gather");
+}
+
+// Pinned, device-mapped staging of nslg_plan_decode_host: kStageSlots slots per device,
+// used round robin; a slot's event is recorded after the kernels that read it, and the
+// slot is written again only once that event has completed.
+constexpr int kMaxDevices = 64;
+constexpr int kStageSlots = 8;
+struct StageSlot {
+  int32_t* host = nullptr;
+  size_t cap = 0;              // int32 entries
+  cudaEvent_t done = nullptr;
+  bool pending = false;
+};
+struct DeviceStage {
+  std::mutex mu;
+  StageSlot slot[kStageSlots];
+  int next = 0;
+};
+DeviceStage g_stage[kMaxDevices];
 
 }  // namespace
 }  // namespace nslg
@@ -144,15 +204,14 @@ extern "C" int nslg_zero_pages(const int32_t* pages, int num_pages_to_zero, void
                                int64_t layers, int64_t num_pages, int64_t page_bytes,
                                uint32_t* dev_status, void* stream) {
   if (num_pages_to_zero == 0) return NSLG_OK;
-  if (num_pages_to_zero < 0 || layers <= 0 || num_pages <= 0 || page_bytes <= 0 ||
-      page_bytes % 16 || layers > 65535)
-    return set_error(NSLG_ERR_ARG, "zero_pages: bad sizes");
-  if (!pages || !pool || (reinterpret_cast<uintptr_t>(pool) & 15u))
-    return set_error(NSLG_ERR_ARG, "zero_pages: null or misaligned pointer");
-  zero_pages_kernel<<<dim3(num_pages_to_zero, static_cast<unsigned>(layers)), 256, 0,
+  int rc = check_zero_args(num_pages_to_zero, pool, layers, num_pages, page_bytes);
+  if (rc != NSLG_OK) return rc;
+  if (!pages) return set_error(NSLG_ERR_ARG, "zero_pages: null or misaligned pointer");
+  uint8_t* p8 = static_cast<uint8_t*>(pool);
+  zero_pages_kernel<<<dim3(num_pages_to_zero, static_cast<unsigned>(layers), 1), 256, 0,
                       static_cast<cudaStream_t>(stream)>>>(
-      pages, num_pages_to_zero, static_cast<uint8_t*>(pool), num_pages, num_pages * page_bytes,
-      page_bytes, dev_status);
+      pages, num_pages_to_zero, p8, p8, num_pages, num_pages * page_bytes, page_bytes,
+      dev_status);
   return check_launch("zero_pages");
 }
 
@@ -163,22 +222,107 @@ extern "C" int nslg_plan_decode(int batch, int page_size, const int32_t* slots,
                                 int32_t* kv_last_page_len, int32_t* qo_indptr,
                                 int32_t* q_row_start, int32_t* kv_indices, int64_t max_indices,
                                 uint32_t* dev_status, void* stream) {
-  if (batch < 1 || batch > kScanThreads * kMaxItems)
-    return set_error(NSLG_ERR_UNSUPPORTED, "plan_decode: batch must be in [1, 4096]");
-  if (page_size <= 0 || bt_stride <= 0 || bt_rows <= 0 || num_updates < 0 || max_indices < 1)
-    return set_error(NSLG_ERR_ARG, "plan_decode: bad sizes");
-  if (bt_rows * bt_stride >= (int64_t{1} << 31))
-    return set_error(NSLG_ERR_UNSUPPORTED, "plan_decode: block tables larger than 2^31 entries");
+  int rc = check_plan_args(batch, page_size, bt_stride, bt_rows, num_updates, max_indices);
+  if (rc != NSLG_OK) return rc;
   if (!slots || !starts || (num_updates && !updates) || !block_tables || !positions ||
       !write_loc || !kv_indptr || !kv_last_page_len || !qo_indptr || !q_row_start || !kv_indices)
     return set_error(NSLG_ERR_ARG, "plan_decode: null pointer");
   PlanParams p{batch, page_size, num_updates, slots, starts, updates, block_tables, bt_stride,
                bt_rows, positions, write_loc, kv_indptr, kv_last_page_len, qo_indptr,
                q_row_start, kv_indices, max_indices, dev_status};
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  plan_decode_scan_kernel<<<1, kScanThreads, 0, st>>>(p);
-  int rc = check_launch("plan_decode_scan");
+  return launch_plan(p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nslg_plan_decode_host(int batch, int page_size, const int32_t* slots,
+                                     const int32_t* starts, int num_updates,
+                                     const int32_t* updates, int num_zero,
+                                     const int32_t* zero_pages, void* pool_k, void* pool_v,
+                                     int64_t layers, int64_t num_pages, int64_t page_bytes,
+                                     int32_t* block_tables, int64_t bt_stride, int64_t bt_rows,
+                                     int32_t* plan, int64_t max_indices, uint32_t* dev_status,
+                                     void* stream) {
+  int rc = check_plan_args(batch, page_size, bt_stride, bt_rows, num_updates, max_indices);
   if (rc != NSLG_OK) return rc;
-  plan_decode_gather_kernel<<<batch, 128, 0, st>>>(p);
-  return check_launch("plan_decode_gather");
+  if (!slots || !starts || (num_updates && !updates) || !block_tables || !plan)
+    return set_error(NSLG_ERR_ARG, "plan_decode_host: null pointer");
+  if (num_zero < 0) return set_error(NSLG_ERR_ARG, "zero_pages: bad sizes");
+  if (num_zero) {
+    if (!zero_pages) return set_error(NSLG_ERR_ARG, "plan_decode_host: null pointer");
+    rc = check_zero_args(num_zero, pool_k, layers, num_pages, page_bytes);
+    if (rc == NSLG_OK) rc = check_zero_args(num_zero, pool_v, layers, num_pages, page_bytes);
+    if (rc != NSLG_OK) return rc;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t err = cudaStreamIsCapturing(st, &cs);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
+  if (cs != cudaStreamCaptureStatusNone)
+    return set_error(NSLG_ERR_UNSUPPORTED,
+                     "plan_decode_host: reads host staging, cannot be captured in a graph");
+  int dev = 0;
+  err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(NSLG_ERR_UNSUPPORTED, "plan_decode_host: device index >= 64");
+
+  const size_t need = 2 * static_cast<size_t>(batch) + 3 * static_cast<size_t>(num_updates) +
+                      static_cast<size_t>(num_zero);
+  DeviceStage& ds = g_stage[dev];
+  std::lock_guard<std::mutex> lock(ds.mu);
+  StageSlot& sl = ds.slot[ds.next];
+  if (sl.pending) {
+    err = cudaEventSynchronize(sl.done);   // the kernels of kStageSlots calls ago
+    if (err != cudaSuccess)
+      return set_error(NSLG_ERR_CUDA, std::string("plan_decode_host: ") + cudaGetErrorString(err));
+    sl.pending = false;
+  }
+  if (sl.done == nullptr) {
+    err = cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming);
+    if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
+  }
+  if (sl.cap < need) {
+    if (sl.host) cudaFreeHost(sl.host);
+    sl.host = nullptr;
+    sl.cap = 0;
+    size_t cap = need > 16384 ? need : 16384;
+    err = cudaHostAlloc(reinterpret_cast<void**>(&sl.host), cap * sizeof(int32_t),
+                        cudaHostAllocMapped | cudaHostAllocPortable);
+    if (err != cudaSuccess)
+      return set_error(NSLG_ERR_CUDA, std::string("plan_decode_host: cudaHostAlloc: ") +
+                                          cudaGetErrorString(err));
+    sl.cap = cap;
+  }
+  int32_t* h = sl.host;
+  std::memcpy(h, slots, sizeof(int32_t) * batch);
+  std::memcpy(h + batch, starts, sizeof(int32_t) * batch);
+  if (num_updates) std::memcpy(h + 2 * batch, updates, sizeof(int32_t) * 3 * num_updates);
+  if (num_zero) std::memcpy(h + 2 * batch + 3 * num_updates, zero_pages, sizeof(int32_t) * num_zero);
+  int32_t* d = nullptr;   // the same memory as the device sees it (UVA: normally h)
+  err = cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
+
+  if (num_zero) {
+    zero_pages_kernel<<<dim3(num_zero, static_cast<unsigned>(layers), 2), 256, 0, st>>>(
+        d + 2 * batch + 3 * num_updates, num_zero, static_cast<uint8_t*>(pool_k),
+        static_cast<uint8_t*>(pool_v), num_pages, num_pages * page_bytes, page_bytes,
+        dev_status);
+    rc = check_launch("zero_pages");
+  }
+  if (rc == NSLG_OK) {
+    const int64_t B = batch;
+    PlanParams p{batch, page_size, num_updates, d, d + batch,
+                 num_updates ? d + 2 * batch : nullptr, block_tables, bt_stride, bt_rows, plan,
+                 plan + B, plan + 2 * B, plan + 3 * B + 1, plan + 4 * B + 1, plan + 5 * B + 2,
+                 plan + 6 * B + 2, max_indices, dev_status};
+    rc = launch_plan(p, st);
+  }
+  // whatever was launched may still read the slot: it is handed out again only after this
+  err = cudaEventRecord(sl.done, st);
+  if (err == cudaSuccess) {
+    sl.pending = true;
+    ds.next = (ds.next + 1) % kStageSlots;
+  } else if (rc == NSLG_OK) {
+    rc = set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
+  }
+  return rc;
 }

@@ -448,7 +448,7 @@ class _DecodeBatch:
     """A decode batch planned on the device, kept for the next step of the same batch:
     its sequence states, table rows, token counts before the step, the page holding each
     sequence's next position, and the longest block table."""
-    __slots__ = ("ids", "mut", "ver", "sts", "slots", "n0", "cur_pid", "longest")
+    __slots__ = ("ids", "mut", "ver", "sts", "slots", "n0", "ptrs", "cur_pid", "longest")
 
 
 class B200CacheContext(CacheContext):
@@ -459,7 +459,7 @@ class B200CacheContext(CacheContext):
     (page, slot) write targets with copy-on-write of shared pages, and the CSR page list
     ``kv_indptr / kv_indices / kv_last_page_len`` (+ ``qo_indptr`` for prefill).  On a
     CUDA pool a decode step (one new token per sequence, no copy-on-write) is planned on
-    the GPU instead (``B200PagedKVCache._begin_decode_device``, ``nslg_plan_decode``);
+    the GPU instead (``B200PagedKVCache._begin_decode_device``, ``nslg_plan_decode_host``);
     otherwise the arrays travel to the device in one copy. Either way they are int32
     views of one buffer:
 
@@ -524,6 +524,19 @@ class B200CacheContext(CacheContext):
             positions, write_loc = self._general_write_targets(sts, new_token_counts, iw, ps)
 
         self._finish_plan(B, iw, ps, sts, positions, write_loc, new_token_counts, dev)
+
+    _PLAN_VIEWS = frozenset(("_pos_i32", "_write_loc", "kv_indptr", "kv_last_page_len",
+                             "qo_indptr", "q_row_start", "kv_indices"))
+
+    def __getattr__(self, name):
+        # a device-planned decode step slices its plan views out of the buffer on first
+        # use (most steps only need the raw pointers)
+        if name in B200CacheContext._PLAN_VIEWS:
+            src = self.__dict__.get("_plan_src")
+            if src is not None:
+                self._set_plan_views(*src)
+                return self.__dict__[name]
+        raise AttributeError(name)
 
     def _set_plan_views(self, d, B, iw, total):
         """Slices the plan arrays out of the flat int32 device buffer ``d`` (layout of the
@@ -751,6 +764,9 @@ class B200PagedKVCache(KVCacheManager):
         self._slot_next = 0
         self._up_dev = None           # device copy of (slots, starts, table updates, zeroes)
         self._plan_dev = None         # device plan buffer of the forwards without a static one
+        self._hs = None               # host scratch of table updates and pages to zero
+        self._hs_ptr = 0
+        self._pc = None               # constant arguments of nslg_plan_decode_host
 
     def use_static_plan(self, batch, input_width=1, max_pages=None):
         """From now on, forwards of exactly (batch, input_width) put their plan into one
@@ -862,33 +878,8 @@ class B200PagedKVCache(KVCacheManager):
             starts.append(n0)
             pids.append(pid)
             slots.append(st.slot)
-        ctx = B200CacheContext.__new__(B200CacheContext)
         B = len(sts)
-        ctx.cache = self
-        ctx.seq_ids = seq_ids
-        ctx.new_token_counts = ntoks
-        ctx.input_offsets = [0] * B
-        ctx.batch_size = B
-        ctx.start_positions = starts
-        ctx.seq_lens = [n + 1 for n in starts]
-        ctx.max_kv_len = max(ctx.seq_lens)
-        ctx._is_decode = True
-        ctx._iw = 1
-        ctx._wi = None
-        ctx._wi_src = (pids, [n % ps for n in starts])
-        ctx._sm_scale = 1.0 / math.sqrt(self.cfg.head_dim)
-        ctx._pos64 = None
-        ctx._direct_ptrs = None
-        upd = []
-        for st in dirty:
-            bt = st.block_table
-            d, nb = bt.dirty_from, len(bt)
-            u = np.empty((nb - d, 3), dtype=np.int32)
-            u[:, 0] = st.slot
-            u[:, 1] = np.arange(d, nb, dtype=np.int32)
-            u[:, 2] = bt.arr[d:nb]
-            upd.append(u)
-            bt.dirty_from = nb
+        nu = self._stage_updates(dirty)
         self._ensure_tables(self._slot_next, longest)
         c = _DecodeBatch()
         c.ids = tuple(seq_ids)
@@ -896,12 +887,14 @@ class B200PagedKVCache(KVCacheManager):
         c.ver = _PagedSeqState.version
         c.sts = sts
         c.slots = np.asarray(slots, dtype=np.int32)
-        c.n0 = np.asarray(starts, dtype=np.int64)
+        c.n0 = np.asarray(starts, dtype=np.int32)
+        c.ptrs = (c.slots.ctypes.data, c.n0.ctypes.data)
         c.cur_pid = np.asarray(pids, dtype=np.int64)
         c.longest = longest
         self._dc = c
-        ctx._dc = c
-        self._launch_device_plan(ctx, c.slots, c.n0, upd)
+        ctx = self._decode_context(c, seq_ids, ntoks, starts, c.n0 % ps)
+        ctx._wi_src = (pids, ctx._wi_src[1])
+        self._launch_device_plan(ctx, c, nu)
         return ctx
 
     def _begin_decode_cached(self, c, seq_ids, ntoks):
@@ -911,8 +904,9 @@ class B200PagedKVCache(KVCacheManager):
         write is shared: the general path takes the step."""
         ps = self.cfg.page_size
         n0 = c.n0
+        rem = n0 % ps
         dirty = []
-        opening = np.flatnonzero(n0 % ps == 0)
+        opening = np.flatnonzero(rem == 0)
         if opening.size:
             rc = self.pool.ref_count
             for i in opening.tolist():
@@ -934,77 +928,101 @@ class B200PagedKVCache(KVCacheManager):
                     dirty.append(st)
         # tokens_used of each sequence's page: positions fill a private page in order
         tu = self.pool.tokens_used
-        for pid, used in zip(c.cur_pid.tolist(), (n0 % ps + 1).tolist()):
+        for pid, used in zip(c.cur_pid.tolist(), (rem + 1).tolist()):
             if tu[pid] < used:
                 tu[pid] = used
-        upd = []
-        for st in dirty:
-            bt = st.block_table
-            d, nb = bt.dirty_from, len(bt)
-            u = np.empty((nb - d, 3), dtype=np.int32)
-            u[:, 0] = st.slot
-            u[:, 1] = np.arange(d, nb, dtype=np.int32)
-            u[:, 2] = bt.arr[d:nb]
-            upd.append(u)
-            bt.dirty_from = nb
+        nu = self._stage_updates(dirty) if dirty else 0
         self._ensure_tables(self._slot_next, c.longest)
-        B = len(c.sts)
+        ctx = self._decode_context(c, seq_ids, ntoks, n0.tolist(), rem)
+        self._launch_device_plan(ctx, c, nu)
+        return ctx
+
+    def _decode_context(self, c, seq_ids, ntoks, starts, rem):
+        """The context of a device-planned decode step of batch ``c`` (start positions
+        ``starts``, in-page slots ``rem``); its plan arrays come from _launch_device_plan."""
+        B = len(starts)
         ctx = B200CacheContext.__new__(B200CacheContext)
         ctx.cache = self
         ctx.seq_ids = seq_ids
         ctx.new_token_counts = ntoks
         ctx.input_offsets = [0] * B
         ctx.batch_size = B
-        ctx.start_positions = n0.tolist()
-        ctx.seq_lens = (n0 + 1).tolist()
-        ctx.max_kv_len = int(n0.max()) + 1
+        ctx.start_positions = starts
+        ctx.seq_lens = [n + 1 for n in starts]
+        ctx.max_kv_len = max(starts) + 1
         ctx._is_decode = True
         ctx._iw = 1
         ctx._wi = None
-        ctx._wi_src = (c.cur_pid.copy(), n0 % ps)
+        ctx._wi_src = (c.cur_pid.copy(), rem)
         ctx._sm_scale = 1.0 / math.sqrt(self.cfg.head_dim)
         ctx._pos64 = None
-        ctx._direct_ptrs = None
         ctx._dc = c
-        self._launch_device_plan(ctx, c.slots, n0, upd)
         return ctx
 
-    def _launch_device_plan(self, ctx, slots, start, upd):
-        """Uploads (slots, start positions, table entries ``upd``, pages to zero) and
-        launches nslg_zero_pages / nslg_plan_decode into ``ctx``'s plan views."""
-        B = len(slots)
+    def _host_scratch(self, n):
+        """The int32 host array the table updates and pages to zero are written into
+        (at least ``n`` entries; reallocation moves it)."""
+        hs = self._hs
+        if hs is None or hs.size < n:
+            new = np.empty(max(n, 4096, 2 * (hs.size if hs is not None else 0)), dtype=np.int32)
+            if hs is not None:
+                new[:hs.size] = hs
+            self._hs = hs = new
+            self._hs_ptr = new.ctypes.data
+        return hs
+
+    def _stage_updates(self, dirty):
+        """Writes the block-table entries of every sequence in ``dirty`` changed since its
+        last upload, as (table row, index, page id) triples, to the start of the host
+        scratch; returns how many."""
+        k = 0
+        for st in dirty:
+            bt = st.block_table
+            d, nb = bt.dirty_from, len(bt)
+            n = nb - d
+            hs = self._host_scratch(3 * (k + n))
+            if n == 1:
+                j = 3 * k
+                hs[j] = st.slot
+                hs[j + 1] = d
+                hs[j + 2] = bt.arr[d]
+            else:
+                v = hs[3 * k:3 * (k + n)].reshape(n, 3)
+                v[:, 0] = st.slot
+                v[:, 1] = np.arange(d, nb, dtype=np.int32)
+                v[:, 2] = bt.arr[d:nb]
+            k += n
+            bt.dirty_from = nb
+        return k
+
+    def _plan_consts(self):
+        pc = self._pc
+        if pc is None:
+            pool = self.pool
+            dev = torch.device(self.cfg.device)
+            idx = dev.index if dev.index is not None else torch.cuda.current_device()
+            page_bytes = pool.k[0, 0].numel() * pool.k.element_size()
+            pc = self._pc = (N.lib(), pool.k.data_ptr(), pool.v.data_ptr(), pool.k.shape[0],
+                             pool.k.shape[1], page_bytes,
+                             ops.status_word(torch.device("cuda", idx)).data_ptr(), idx)
+        return pc
+
+    def _launch_device_plan(self, ctx, c, nu):
+        """One nslg_plan_decode_host call: the batch's table rows and start positions
+        (arrays of ``c``), the ``nu`` table updates at the start of the host scratch and
+        the pages to zero after them; the plan goes to the static buffer of this batch
+        size when there is one and it fits, else to the manager's own plan buffer."""
+        n0 = c.n0
+        B = n0.shape[0]
         ps = self.cfg.page_size
-        nu = sum(u.shape[0] for u in upd)
-        npgs = (start + ps) // ps                      # ceil((start + 1) / ps)
-        total = int(npgs.sum())
+        total = int(((n0 + ps) // ps).sum())           # sum of ceil((start + 1) / ps)
         zero = self.pool.take_pending_zero()           # pages allocated since the last forward
         nz = len(zero)
-        size_up = 2 * B + 3 * nu + nz
-        host = self._pinned_plan(size_up)
-        hn = host.numpy()
-        hn[:B] = slots
-        hn[B:2 * B] = start
-        if nu:
-            np.concatenate(upd, out=hn[2 * B:2 * B + 3 * nu].reshape(nu, 3))
         if nz:
-            hn[2 * B + 3 * nu:] = zero
-        if self._up_dev is None or self._up_dev.numel() < size_up:
-            grown = 2 * self._up_dev.numel() if self._up_dev is not None else 0
-            self._up_dev = torch.empty(max(size_up, 4096, grown), dtype=torch.int32,
-                                       device=self.cfg.device)
-        up = self._up_dev
-        stream = torch.cuda.current_stream(self.cfg.device)
-        up[:size_up].copy_(host, non_blocking=True)
-        self._plan_copied(stream)
-        base = up.data_ptr()
-        status = ops.status_word(self.cfg.device).data_ptr()
-        if nz:
-            pool = self.pool
-            page_bytes = pool.k[0, 0].numel() * pool.k.element_size()
-            for t in (pool.k, pool.v):
-                N.call("nslg_zero_pages", base + 4 * (2 * B + 3 * nu), nz, t.data_ptr(),
-                       t.shape[0], t.shape[1], page_bytes, status, stream.cuda_stream)
-        plan_size = 5 * B + 2 + max(B, 1) + total
+            self._host_scratch(3 * nu + nz)[3 * nu:3 * nu + nz] = zero
+        elif self._hs is None:
+            self._host_scratch(1)
+        plan_size = 6 * B + 2 + total
         d = self.static_plan_for(B, 1, plan_size)
         ctx.plan_static = d is not None
         if d is None:
@@ -1015,15 +1033,24 @@ class B200PagedKVCache(KVCacheManager):
                 self._plan_dev = torch.empty(max(plan_size, 65536, grown), dtype=torch.int32,
                                              device=self.cfg.device)
             d = self._plan_dev
-        ctx._set_plan_views(d, B, 1, total)
-        ctx._plan_bytes = size_up * 4
+        base = d.data_ptr()
+        # plan views are sliced from d on first use (B200CacheContext.__getattr__); the
+        # direct decode path takes these pointers
+        ctx._plan_src = (d, B, 1, total)
+        ctx._direct_ptrs = (base + 4 * B, base + 8 * B, base + 4 * (6 * B + 2),
+                            base + 4 * (3 * B + 1))
+        ctx._plan_bytes = 4 * (2 * B + 3 * nu + nz)
+        lib, pk, pv, layers, pages, page_bytes, status, idx = self._plan_consts()
+        stream = (ops._raw_stream(idx) if ops._raw_stream is not None
+                  else torch.cuda.current_stream(idx).cuda_stream)
         dbt = self._dbt
-        N.call("nslg_plan_decode", B, ps, base, base + 4 * B, nu, base + 8 * B if nu else None,
-               dbt.data_ptr(), dbt.shape[1], dbt.shape[0],
-               ctx._pos_i32.data_ptr(), ctx._write_loc.data_ptr(), ctx.kv_indptr.data_ptr(),
-               ctx.kv_last_page_len.data_ptr(), ctx.qo_indptr.data_ptr(),
-               ctx.q_row_start.data_ptr(), ctx.kv_indices.data_ptr(), max(total, 1),
-               status, stream.cuda_stream)
+        hp = self._hs_ptr
+        rc = lib.nslg_plan_decode_host(B, ps, c.ptrs[0], c.ptrs[1], nu, hp, nz, hp + 12 * nu,
+                                       pk, pv, layers, pages, page_bytes, dbt.data_ptr(),
+                                       dbt.shape[1], dbt.shape[0], base, max(total, 1), status,
+                                       stream)
+        if rc:
+            raise N.NativeError("nslg_plan_decode_host", rc, lib.nslg_last_error().decode())
 
     def allocate_sequence(self, seq_id, token_ids=None, num_tokens=0):
         self._mut += 1

@@ -1,11 +1,12 @@
 """Host side of the device-planned decode step, on CPU.
 
-The manager of a CUDA pool plans decode steps on the GPU (csrc/plan.cu) from block
-tables mirrored in device memory: per step it sends the batch's table rows, the token
-counts before the step and the table entries changed since the last step. When the same
-batch steps again with nothing else changed, a cached copy of the batch's state is
-advanced instead of walking every sequence. Here the launch is replaced by a recorder
-that applies the uploads to a numpy mirror of the device tables, and three managers run
+The manager of a CUDA pool plans decode steps on the GPU (csrc/plan.cu,
+nslg_plan_decode_host) from block tables mirrored in device memory: per step it sends the
+batch's table rows, the token counts before the step and the table entries changed since
+the last step. When the same batch steps again with nothing else changed, a cached copy
+of the batch's state is advanced instead of walking every sequence. Here the launch is
+replaced by a recorder that applies the uploads to a numpy mirror of the device tables,
+and three managers run
 the same random workload: device planning with the cache, device planning without it,
 and the host plan (kv_cache.py:547-632 restated). Page ids, block tables, refcounts,
 tokens_used, write targets and the mirrored tables must agree at every step."""
@@ -19,19 +20,20 @@ from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
 
 
 class _Mirror:
-    """Stands in for nslg_plan_decode: applies the table updates, records the step."""
+    """Stands in for the nslg_plan_decode_host launch: applies the table updates, records
+    the step."""
 
     def __init__(self, mgr):
         self.mgr = mgr
         self.rows = {}
         self.last = None
 
-    def __call__(self, ctx, slots, start, upd):
-        for u in upd:
-            for s, j, pg in u.tolist():
+    def __call__(self, ctx, c, nu):
+        if nu:
+            for s, j, pg in self.mgr._hs[:3 * nu].reshape(nu, 3).tolist():
                 self.rows.setdefault(s, {})[j] = pg
         self.mgr.pool.take_pending_zero()
-        self.last = (np.asarray(slots).tolist(), np.asarray(start).tolist())
+        self.last = (c.slots.tolist(), c.n0.tolist())
         ctx.plan_static = False
 
 

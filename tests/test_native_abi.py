@@ -93,6 +93,20 @@ def test_tp_plan_and_ipc_argument_errors_without_gpu(lib):
     # page zeroing: nothing to do is fine, bad sizes are not
     assert lib.nslg_zero_pages(None, 0, None, 1, 1, 16, None, None) == N.OK
     assert lib.nslg_zero_pages(vp(16), 2, vp(16), 1, 64, 24, None, None) == N.ERR_ARG
+    # the one-call planner from host arrays: same batch limits, its own argument checks
+    # (all of them before any CUDA call)
+    hbuf = (ctypes.c_int32 * 64)()
+    h = ctypes.cast(hbuf, vp)
+    hargs = lambda b, ps, nz, pk, pb, plan: (b, ps, h, h, 0, None, nz, h, pk, pk, 1, 64, pb,
+                                             vp(16), 512, 64, plan, 1024, None, None)
+    assert lib.nslg_plan_decode_host(*hargs(0, 16, 0, None, 16, vp(16))) == N.ERR_UNSUPPORTED
+    assert lib.nslg_plan_decode_host(*hargs(4097, 16, 0, None, 16, vp(16))) == N.ERR_UNSUPPORTED
+    assert lib.nslg_plan_decode_host(*hargs(4, 0, 0, None, 16, vp(16))) == N.ERR_ARG
+    assert lib.nslg_plan_decode_host(*hargs(4, 16, 0, None, 16, None)) == N.ERR_ARG
+    assert lib.nslg_plan_decode_host(*hargs(4, 16, -1, None, 16, vp(16))) == N.ERR_ARG
+    assert lib.nslg_plan_decode_host(*hargs(4, 16, 2, None, 16, vp(16))) == N.ERR_ARG
+    assert lib.nslg_plan_decode_host(*hargs(4, 16, 2, vp(16), 24, vp(16))) == N.ERR_ARG
+    assert lib.nslg_plan_decode_host(*hargs(4, 16, 2, vp(8), 16, vp(16))) == N.ERR_ARG
     # IPC helpers
     ptr = vp()
     assert lib.nslg_ipc_alloc(0, ctypes.byref(ptr), ctypes.create_string_buffer(64)) == N.ERR_ARG
