@@ -20,8 +20,11 @@
 //                   into TMEM buffer S_X[t%2];
 //                   O_X += P_X(t) . V(t)   M=128 N=128 K=64, A = P_X(t) in TMEM (written
 //                   over S_X[t%2]), B = V MN-major (smem).
-//                   S_X(t+2) goes into S_X[t%2] as soon as P_X(t) . V(t) is done, so the
-//                   softmax of tile t+1 overlaps P(t).V(t) and S(t+2).
+//                   Issue order per tile: P_A(t).V(t), S_A(t+1), P_B(t).V(t), S_B(t+1).
+//                   S_X(t+1) reuses the buffer of P_X(t-1), whose P.V was issued a tile
+//                   earlier, so the issuer never waits on an MMA still in the pipe, and
+//                   the softmax of S_A(t+1) runs while the pipe does half B's MMAs (and
+//                   the other way round).
 //   softmax WG X    (two warpgroups, one per half) thread r owns TMEM lane r = row r:
 //                   loads S_X(t), masks only on tiles that cross the causal or length
 //                   edge, keeps a running max (log2 domain) and sum, writes P as bf16 over
@@ -439,26 +442,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kIdescS = idesc_bf16(kBN, false);
       constexpr uint32_t kIdescO = idesc_bf16(kD, true);
       bool ok = true;
-      // S_X(u) into S_X[u%2] for both halves; the buffer is free once P_X(u-2).V is done
-      auto issue_s = [&](int u, int qs) -> bool {
+      // S_X(u) = Q_X . K(u)^T into S_X[u%2]; the buffer is free once P_X(u-2).V is done.
+      // Issued per half, right after that half's P_X(u-1).V: the wait is then on an MMA
+      // issued a whole tile earlier (long complete), so the tensor pipe never drains
+      // while the issuer waits, and the softmax of S_X(u) overlaps the other half's MMAs.
+      auto issue_s = [&](int u, int qs, int x) -> bool {
         const int slot = u % kRing, b = u & 1;
-        if (!mbar_wait(&k_full[slot], (u / kRing) & 1)) return false;
+        if (x == 0 && !mbar_wait(&k_full[slot], (u / kRing) & 1)) return false;
         const uint32_t k_base = smem_u32(sk + slot * kTile);
-        for (int x = 0; x < 2; ++x) {
-          if (u >= 2 && !mbar_wait(&pv_done[x * 2 + b], ((u - 2) >> 1) & 1)) return false;
-          tc_fence_after();
-          const uint32_t q_base = smem_u32(sq + qs * kQSlot + x * kQBytes);
-          const uint32_t dcol = tmem + x * kHalfCols + 64 * b;
+        if (u >= 2 && !mbar_wait(&pv_done[x * 2 + b], ((u - 2) >> 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t q_base = smem_u32(sq + qs * kQSlot + x * kQBytes);
+        const uint32_t dcol = tmem + x * kHalfCols + 64 * b;
 #pragma unroll
-          for (int ks = 0; ks < kD / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
-            const uint32_t koff = (ks >> 2) * kKVHalf + (ks & 3) * 32;
-            mma_ss(dcol, smem_desc(q_base + off, 16, 1024), smem_desc(k_base + koff, 16, 1024),
-                   kIdescS, ks > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full[x * 2 + b]);
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
+          const uint32_t koff = (ks >> 2) * kKVHalf + (ks & 3) * 32;
+          mma_ss(dcol, smem_desc(q_base + off, 16, 1024), smem_desc(k_base + koff, 16, 1024),
+                 kIdescS, ks > 0 ? 1u : 0u);
         }
-        mma_commit(&k_empty[slot]);
+        mma_commit(&s_full[x * 2 + b]);
+        if (x == 1) mma_commit(&k_empty[slot]);
         return true;
       };
       int t = 0, n_it = 0;
@@ -474,10 +478,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const int t0 = t;
         const int last = t0 + it.ntiles - 1;
-        for (int u = t0; ok && u <= last && u < t0 + 2; ++u) {
-          ok = issue_s(u, qs);
-          if (ok && u == last) mma_commit(&q_empty[qs]);   // Q is read for the last time
-        }
+        for (int x = 0; ok && x < 2; ++x) ok = issue_s(t0, qs, x);
+        if (ok && t0 == last) mma_commit(&q_empty[qs]);   // Q is read for the last time
         for (int j = 0; ok && j < it.ntiles; ++j, ++t) {
           const int slot = t % kRing, b = t & 1;
           if (!(ok = mbar_wait(&v_full[slot], (t / kRing) & 1))) break;
@@ -493,13 +495,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                      smem_desc(v_base + kt * 2048, kKVHalf, 1024), kIdescO,
                      (j > 0 || kt > 0) ? 1u : 0u);
             mma_commit(&pv_done[x * 2 + b]);
+            if (x == 1) mma_commit(&v_empty[slot]);
+            if (t + 1 <= last && !(ok = issue_s(t + 1, qs, x))) break;
           }
           if (!ok) break;
-          mma_commit(&v_empty[slot]);
-          if (t + 2 <= last) {
-            ok = issue_s(t + 2, qs);
-            if (ok && t + 2 == last) mma_commit(&q_empty[qs]);
-          }
+          if (t + 1 == last) mma_commit(&q_empty[qs]);
           if (*abort_flag) ok = false;
         }
         ++n_it;
