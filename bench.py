@@ -278,6 +278,79 @@ def run_prefill_kernel(device, reps=10, batch=64, prompt=512):
             "peak_source": src, "algorithmic_flops": flops}
 
 
+def _hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return 6650.0, "fallback 6650 GB/s"
+
+
+def run_elementwise_kernels(device, reps=10, batch=64, prompt=512, hidden=4096):
+    """The two bandwidth-bound kernels of the layer at the C3 prefill shape (64 prompts x
+    512 tokens = 32768 rows; inputs larger than L2, no flush):
+      rope_kv_append_bf16_kernel: q [T, 32, 128], k, v [T, 8, 128] bf16, positions 0..511 per
+        prompt, fp32 cos/sin table [8192, 128]; writes q_rot and K/V into a shuffled pool.
+        Algorithmic bytes: q, k, v read + q_rot written + K/V written + the touched table
+        rows (512 x 128 x 4 B x 2) + positions and write slots (4 B each per row);
+      rmsnorm_residual_kernel: x, residual [T, 4096] bf16 with weight; residual <- x +
+        residual, out = rmsnorm(residual) * weight. Algorithmic bytes: x, residual read,
+        residual and out written, weight once.
+    CUDA events, median of ``reps`` launches each."""
+    from nanoslg_b200 import ops
+    from nanoslg_b200.models import precompute_rope_frequencies
+    bf = torch.bfloat16
+    T = batch * prompt
+    g = torch.Generator(device=device).manual_seed(11)
+    npg = -(-prompt // PS)
+    pages = batch * npg + 1
+    q = torch.randn(T, HQ, D, device=device, generator=g).to(bf)
+    k = torch.randn(T, HKV, D, device=device, generator=g).to(bf)
+    v = torch.randn(T, HKV, D, device=device, generator=g).to(bf)
+    q_out = torch.empty_like(q)
+    pool_k = torch.zeros(pages, PS, HKV, D, device=device, dtype=bf)
+    pool_v = torch.zeros_like(pool_k)
+    perm = torch.randperm(pages - 1, device=device, generator=g)[:batch * npg] + 1
+    pos = torch.arange(prompt, device=device, dtype=torch.int32).repeat(batch)
+    page_of = perm.view(batch, npg)[:, (pos[:prompt] // PS).long()].reshape(-1)
+    write_loc = (page_of * PS + (pos % PS)).to(torch.int32)
+    cos, sin = precompute_rope_frequencies(D, 8192, 500000.0, None)
+    cos, sin = cos.to(device).float().contiguous(), sin.to(device).float().contiguous()
+    x = torch.randn(T, hidden, device=device, generator=g).to(bf)
+    res = torch.randn(T, hidden, device=device, generator=g).to(bf)
+    w = torch.ones(hidden, device=device, dtype=bf)
+    out = torch.empty_like(x)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+        ev[0].record()
+        for i in range(reps):
+            fn()
+            ev[i + 1].record()
+        torch.cuda.synchronize(device)
+        return statistics.median(ev[i].elapsed_time(ev[i + 1]) for i in range(reps))
+
+    peak, src = _hbm_peak()
+    rope_ms = timed(lambda: ops.rope_kv_append(q, k, v, pos, cos, sin, write_loc, pool_k,
+                                               pool_v, q_out=q_out))
+    rope_bytes = (T * HQ * D * 2) * 2 + (T * HKV * D * 2) * 4 + 2 * prompt * D * 4 + 8 * T
+    norm_ms = timed(lambda: ops.rmsnorm_residual(x, w, 1e-5, residual=res, out=out))
+    norm_bytes = 4 * T * hidden * 2 + hidden * 2
+    del q, k, v, q_out, pool_k, pool_v, x, res, out
+    torch.cuda.empty_cache()
+    leg = lambda name, ms, nbytes: {
+        "kernel": name, "ms_median": ms, "algorithmic_bytes": nbytes,
+        "gbs": nbytes / (ms / 1e3) / 1e9, "frac": nbytes / (ms / 1e3) / 1e9 / peak}
+    return {"workload": f"C3 prefill shape: {batch} prompts x {prompt} tokens "
+                        f"({T} rows), 32/8 heads, D=128, hidden {hidden}, bf16",
+            "peak_gbs": peak, "peak_source": src,
+            "rope_kv_append": leg("rope_kv_append_bf16_kernel", rope_ms, rope_bytes),
+            "rmsnorm_residual": leg("rmsnorm_residual_kernel", norm_ms, norm_bytes)}
+
+
 # ------------------------------------------------------------------ model decode
 def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=None,
                      peer_allreduce=True):
@@ -534,10 +607,12 @@ def main():
     ap.add_argument("--tp-reduce", choices=["peer", "nccl"], default="peer",
                     help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
-    ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce"],
+    ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce",
+                                       "elementwise"],
                     default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
-                         "model: only the Llama-3.1-8B decode leg")
+                         "model: only the Llama-3.1-8B decode leg; elementwise: the RoPE + "
+                         "KV-append and RMSNorm + residual kernels at the C3 prefill shape")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -588,6 +663,13 @@ def main():
         if rank == 0:
             print(json.dumps({"case": "prefill only", "prefill_attention":
                               run_prefill_kernel(device)}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
+    if a.only == "elementwise":
+        if rank == 0:
+            print(json.dumps({"case": "elementwise only", "elementwise":
+                              run_elementwise_kernels(device)}), flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
         return 0

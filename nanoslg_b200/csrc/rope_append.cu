@@ -1,14 +1,22 @@
 // Fused rotary embedding + paged KV append.
 //
-// One thread owns 16 bytes of a head row. For q and k it owns the matching 16 bytes
-// of both halves of the row (rotate-half pairs dimension d with d + D/2), rotates
-// them and stores them with 16-byte vector stores: q into q_out, k into the page
-// slot the context assigned to the token. v is copied unrotated. The arithmetic
-// repeats the reference's elementwise ops with their rounding points
-// (models.py:79-83): cos/sin are first cast to the activation type, then
+// A thread owns 16 bytes of a head row. For q and k it owns the matching 16 bytes of
+// both halves of the row (rotate-half pairs dimension d with d + D/2), rotates them and
+// stores them with 16-byte vector stores: q into q_out, k into the page slot the
+// context assigned to the token. v is copied unrotated. The arithmetic repeats the
+// reference's elementwise ops with their rounding points (models.py:79-83): cos/sin
+// are first cast to the activation type, then
 //   out = x*cos + cat(-x2, x1)*sin
-// with every product and the sum rounded to the activation type. fp32 uses the
-// explicitly rounded intrinsics so no fused multiply-add changes the result.
+// with every product and the sum rounded to the activation type.
+//
+// bf16 (rope_kv_append_bf16_kernel): one CTA per token. The token's cos/sin row is
+// rounded to bf16 once, into shared memory, and every q/k head of the token reads it
+// from there; the products and sums run as paired bf16 instructions (mul/add/sub.rn
+// .bf16x2: each rounds the exact result once, as torch does after computing the op in
+// fp32, and explicit .rn keeps them from being contracted into a fused multiply-add).
+// Per 16-byte output: 4 multiplies and 2 adds of bf16 pairs, no conversions.
+// fp32 (rope_kv_append_kernel): the explicitly rounded fp32 intrinsics, so no fused
+// multiply-add changes the result.
 #include "common.cuh"
 #include "launch.h"
 
@@ -121,6 +129,109 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(const RopeParams p)
   }
 }
 
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+constexpr int kBf16MaxThreads = 512;
+
+template <int D>
+__global__ void __launch_bounds__(kBf16MaxThreads) rope_kv_append_bf16_kernel(const RopeParams p) {
+  constexpr int HALF = D / 2;
+  constexpr int VH = HALF / 8;    // 16-byte chunks per half row
+  constexpr int VROW = D / 8;     // 16-byte chunks per row
+  // bf16 pairs of the token's cos / sin row, rounded: word i = dims 2i, 2i + 1
+  __shared__ __align__(16) uint32_t cs2[HALF];
+  __shared__ __align__(16) uint32_t sn2[HALF];
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  int64_t loc = p.write_loc != nullptr ? p.write_loc[t] : -1;
+  if (loc >= p.pool_slots) {
+    if (threadIdx.x == 0) report(p.status, NSLG_DEV_BAD_SLOT);
+    loc = -1;
+  }
+  bool rot = false;
+  if (p.positions != nullptr) {
+    const int64_t pos = p.positions[t];
+    if (pos < 0 || pos >= p.table_rows) {
+      if (threadIdx.x == 0) report(p.status, NSLG_DEV_BAD_POSITION);
+    } else {
+      rot = true;
+      const float2* c = reinterpret_cast<const float2*>(p.cos_t + pos * D);
+      const float2* sn = reinterpret_cast<const float2*>(p.sin_t + pos * D);
+      for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+        const __nv_bfloat162 cb = __float22bfloat162_rn(c[i]);
+        const __nv_bfloat162 sb = __float22bfloat162_rn(sn[i]);
+        cs2[i] = *reinterpret_cast<const uint32_t*>(&cb);
+        sn2[i] = *reinterpret_cast<const uint32_t*>(&sb);
+      }
+    }
+  }
+  __syncthreads();
+  const int q_items = p.q_out != nullptr ? p.hq * VH : 0;
+  const int k_items = p.hkv * VH;
+  const int per_tok = q_items + k_items + p.hkv * VROW;
+  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) + t * p.q_stride;
+  const __nv_bfloat16* kb = static_cast<const __nv_bfloat16*>(p.k) + t * p.k_stride;
+  for (int w = threadIdx.x; w < per_tok; w += blockDim.x) {
+    if (w < q_items + k_items) {
+      const bool is_q = w < q_items;
+      const int idx = is_q ? w : w - q_items;
+      const int h = idx / VH, c = idx % VH;
+      const __nv_bfloat16* src = (is_q ? qb : kb) + h * D;
+      __nv_bfloat16* dst;
+      if (is_q) {
+        dst = static_cast<__nv_bfloat16*>(p.q_out) + (static_cast<int64_t>(t) * p.hq + h) * D;
+      } else {
+        if (loc < 0) continue;
+        dst = static_cast<__nv_bfloat16*>(p.pool_k) + (loc * p.hkv + h) * D;
+      }
+      uint4 x1 = *reinterpret_cast<const uint4*>(src + c * 8);
+      uint4 x2 = *reinterpret_cast<const uint4*>(src + HALF + c * 8);
+      if (rot) {
+        const uint4 c1 = *reinterpret_cast<const uint4*>(&cs2[c * 4]);
+        const uint4 s1 = *reinterpret_cast<const uint4*>(&sn2[c * 4]);
+        const uint4 c2 = *reinterpret_cast<const uint4*>(&cs2[HALF / 2 + c * 4]);
+        const uint4 s2 = *reinterpret_cast<const uint4*>(&sn2[HALF / 2 + c * 4]);
+        // d <  D/2:  x[d]*cos[d] - x[d+D/2]*sin[d];  d >= D/2:  x[d]*cos[d] + x[d-D/2]*sin[d]
+        const uint4 o1{bf2_sub(bf2_mul(x1.x, c1.x), bf2_mul(x2.x, s1.x)),
+                       bf2_sub(bf2_mul(x1.y, c1.y), bf2_mul(x2.y, s1.y)),
+                       bf2_sub(bf2_mul(x1.z, c1.z), bf2_mul(x2.z, s1.z)),
+                       bf2_sub(bf2_mul(x1.w, c1.w), bf2_mul(x2.w, s1.w))};
+        const uint4 o2{bf2_add(bf2_mul(x2.x, c2.x), bf2_mul(x1.x, s2.x)),
+                       bf2_add(bf2_mul(x2.y, c2.y), bf2_mul(x1.y, s2.y)),
+                       bf2_add(bf2_mul(x2.z, c2.z), bf2_mul(x1.z, s2.z)),
+                       bf2_add(bf2_mul(x2.w, c2.w), bf2_mul(x1.w, s2.w))};
+        x1 = o1;
+        x2 = o2;
+      }
+      *reinterpret_cast<uint4*>(dst + c * 8) = x1;
+      *reinterpret_cast<uint4*>(dst + HALF + c * 8) = x2;
+    } else {
+      if (loc < 0) continue;
+      const int idx = w - q_items - k_items;
+      const int h = idx / VROW, c = idx % VROW;
+      const __nv_bfloat16* src =
+          static_cast<const __nv_bfloat16*>(p.v) + t * p.v_stride + h * D + c * 8;
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.pool_v) + (loc * p.hkv + h) * D + c * 8;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    }
+  }
+}
+
 }  // namespace
 
 int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, const void* q,
@@ -132,6 +243,18 @@ int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, con
   RopeParams p{q,        k,        v,          q_out,    positions, cos_t,      sin_t,
                write_loc, pool_k,  pool_v,     q_stride, k_stride,  v_stride,   table_rows,
                pool_slots, num_tokens, hq,     hkv,      d,         status};
+  if (dtype == NSLG_DTYPE_BF16 && (d == 128 || d == 64) && num_tokens > 0) {
+    const int per_tok = (q_out ? hq * (d / 16) : 0) + hkv * (d / 16) + hkv * (d / 8);
+    if (per_tok == 0) return NSLG_OK;
+    int threads = (per_tok + 31) / 32 * 32;
+    if (threads > kBf16MaxThreads) threads = kBf16MaxThreads;
+    const dim3 grid(static_cast<unsigned>(num_tokens));
+    if (d == 128)
+      return launch_pdl("rope_kv_append", rope_kv_append_bf16_kernel<128>, grid, dim3(threads),
+                        0, stream, p);
+    return launch_pdl("rope_kv_append", rope_kv_append_bf16_kernel<64>, grid, dim3(threads), 0,
+                      stream, p);
+  }
   const int esz = dtype == NSLG_DTYPE_BF16 ? 2 : 4;
   const int vec = 16 / esz;
   const int per_tok = (q_out ? hq * (d / 2 / vec) : 0) + hkv * (d / 2 / vec) + hkv * (d / vec);

@@ -116,7 +116,9 @@ def check_device_status(device, reset=True):
         names = [n for bit, n in ((N.DEV_BAD_PAGE, "page id outside the pool"),
                                   (N.DEV_BAD_SLOT, "write slot outside the pool"),
                                   (N.DEV_BAD_POSITION, "position outside the RoPE table"),
-                                  (N.DEV_WAIT_TIMEOUT, "pipeline wait timed out")) if v & bit]
+                                  (N.DEV_WAIT_TIMEOUT, "pipeline wait timed out"),
+                                  (N.DEV_BAD_PLAN, "plan entry outside the device block "
+                                                   "tables")) if v & bit]
         raise RuntimeError("nanoslg_b200 device error: " + ", ".join(names))
 
 

@@ -58,6 +58,37 @@ def test_rope_kv_append_bit_exact(dt, hq, hkv, d):
     assert bool((fk[untouched] == 7.0).all()) and bool((fv[untouched] == 7.0).all())
 
 
+@pytest.mark.parametrize("d", [128, 64])
+def test_rope_kv_append_bf16_wide_range(d):
+    """bf16 path (paired bf16 multiplies and adds) against the reference's torch ops over
+    many tokens whose values span 2^-40 .. 2^20 (products down to the bf16 subnormal
+    range), positions across the whole table, and the unrotated append (rotate=False)."""
+    g = torch.Generator().manual_seed(17)
+    T, hq, hkv, ps, P = 3000, 16, 4, 16, 200
+    bf = torch.bfloat16
+    cos, sin = rope_table(d, 8192, 500000.0)
+    scale = lambda *s: torch.exp2(torch.randint(-40, 21, s, generator=g).float())
+    q = (torch.randn(T, hq, d, generator=g) * scale(T, hq, 1)).to(bf)
+    k = (torch.randn(T, hkv, d, generator=g) * scale(T, hkv, 1)).to(bf)
+    v = torch.randn(T, hkv, d, generator=g).to(bf)
+    pos = torch.randint(0, 8192, (T,), generator=g, dtype=torch.int32)
+    loc = torch.randperm(P * ps, generator=g)[:T].to(torch.int32)
+    pk = torch.zeros((P, ps, hkv, d), dtype=bf, device=DEV)
+    pv = torch.zeros_like(pk)
+    q_out = ops.rope_kv_append(q.to(DEV), k.to(DEV), v.to(DEV), pos.to(DEV), cos.to(DEV),
+                               sin.to(DEV), loc.to(DEV), pk, pv)
+    p64 = pos.long()[None]
+    assert torch.equal(q_out.cpu(), apply_rotary(q[None], cos[p64], sin[p64])[0])
+    fk = pk.view(-1, hkv, d).cpu()
+    assert torch.equal(fk[loc.long()], apply_rotary(k[None], cos[p64], sin[p64])[0])
+    assert torch.equal(pv.view(-1, hkv, d).cpu()[loc.long()], v)
+    # already-rotated k (the attend() path): copied as is
+    pk.zero_()
+    ops.rope_kv_append(None, k.to(DEV), v.to(DEV), None, None, None, loc.to(DEV), pk, pv,
+                       rotate=False)
+    assert torch.equal(pk.view(-1, hkv, d).cpu()[loc.long()], k)
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("hidden", [256, 4096, 8192])
 def test_rmsnorm_residual(dt, hidden):
@@ -208,3 +239,35 @@ def test_fused_projections_match_separate_layers():
     assert models._views_intact(m.layers[0].mlp._gu, [m.layers[0].mlp.gate_proj,
                                                       m.layers[0].mlp.up_proj])
     torch.testing.assert_close(outs[1], outs[0], rtol=2e-2, atol=2e-2)
+
+
+def test_rope_kv_append_reports_bad_position_and_slot():
+    """A position outside the cos/sin table and a write slot outside the pool are not
+    accessed: the token is copied unrotated / not written, and the status word names
+    both errors (the call itself succeeds; the GPU never faults)."""
+    bf = torch.bfloat16
+    hq, hkv, d, ps, P = 8, 2, 128, 16, 4
+    g = torch.Generator().manual_seed(23)
+    cos, sin = rope_table(d, 64, 500000.0)
+    q = torch.randn(4, hq, d, generator=g).to(bf)
+    k = torch.randn(4, hkv, d, generator=g).to(bf)
+    v = torch.randn(4, hkv, d, generator=g).to(bf)
+    pos = torch.tensor([3, 64, 5, 7], dtype=torch.int32)        # 64: one past the table
+    loc = torch.tensor([0, 1, P * ps + 5, 2], dtype=torch.int32)  # token 2: past the pool
+    pk = torch.zeros((P, ps, hkv, d), dtype=bf, device=DEV)
+    pv = torch.zeros_like(pk)
+    q_out = ops.rope_kv_append(q.to(DEV), k.to(DEV), v.to(DEV), pos.to(DEV), cos.to(DEV),
+                               sin.to(DEV), loc.to(DEV), pk, pv)
+    with pytest.raises(RuntimeError) as err:
+        ops.check_device_status(DEV)
+    assert "position outside the RoPE table" in str(err.value)
+    assert "write slot outside the pool" in str(err.value)
+    ok = torch.tensor([0, 2, 3])
+    p64 = pos.long()[ok][None]
+    assert torch.equal(q_out.cpu()[ok], apply_rotary(q[ok][None], cos[p64], sin[p64])[0])
+    assert torch.equal(q_out.cpu()[1], q[1])                    # left unrotated
+    fk = pk.view(-1, hkv, d).cpu()
+    assert torch.equal(fk[[0, 2]], apply_rotary(k[[0, 3]][None], cos[pos.long()[[0, 3]]][None],
+                                                sin[pos.long()[[0, 3]]][None])[0])
+    assert torch.equal(fk[1], k[1])
+    assert int((fk[3:] != 0).sum()) == 0
