@@ -85,11 +85,17 @@ struct PrefillParams {
 };
 
 // ----------------------------------------------------------------- tcgen05 wrappers
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  // start>>4 [0,14) | LBO>>4 [16,30) | SBO>>4 [32,46) | version 1 [46,48) | SWIZZLE_128B (2) [61,64)
-  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) |
-         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+// Shared-memory matrix descriptor (start>>4 [0,14) | LBO>>4 [16,30) | SBO>>4 [32,46) |
+// version 1 [46,48) | SWIZZLE_128B (2) [61,64)) as two 32-bit words. The start field
+// holds addr >> 4 in 14 bits and every shared-memory address here is below 256 KiB, so
+// the descriptor of addr + off (off a multiple of 16) is the low word plus off >> 4:
+// the MMA issuer keeps one low word per buffer and adds compile-time offsets instead of
+// rebuilding the 64-bit value for every instruction.
+__device__ __forceinline__ uint32_t smem_desc_lo(uint32_t addr, uint32_t lbo) {
+  return ((addr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t smem_desc_hi(uint32_t sbo) {
+  return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
 }
 
 // kind::f16 instruction descriptor: f32 accumulate, bf16 A and B, M = 128.
@@ -98,20 +104,23 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n, bool b_mn_major) {
          ((static_cast<uint32_t>(n) >> 3) << 17) | ((128u >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                       uint32_t accumulate) {
+// tcgen05.mma with the shared-memory descriptors passed as (low, high) words
+__device__ __forceinline__ void mma_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                         uint32_t hi, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\tsetp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 da, {%1, %3};\n\tmov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate));
 }
 
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
-                                       uint32_t idesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                         uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\tsetp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -441,6 +450,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdescS = idesc_bf16(kBN, false);
       constexpr uint32_t kIdescO = idesc_bf16(kD, true);
+      constexpr uint32_t kDescHi = smem_desc_hi(1024);
+      // descriptor low words of the first Q slot, K slot and V slot (K-major Q and K:
+      // LBO 16; MN-major V: LBO = the 64-dim half stride)
+      const uint32_t q_lo0 = smem_desc_lo(smem_u32(sq), 16);
+      const uint32_t k_lo0 = smem_desc_lo(smem_u32(sk), 16);
+      const uint32_t v_lo0 = smem_desc_lo(smem_u32(sv), kKVHalf);
       bool ok = true;
       // S_X(u) = Q_X . K(u)^T into S_X[u%2]; the buffer is free once P_X(u-2).V is done.
       // Issued per half, right after that half's P_X(u-1).V: the wait is then on an MMA
@@ -449,17 +464,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_s = [&](int u, int qs, int x) -> bool {
         const int slot = u % kRing, b = u & 1;
         if (x == 0 && !mbar_wait(&k_full[slot], (u / kRing) & 1)) return false;
-        const uint32_t k_base = smem_u32(sk + slot * kTile);
+        const uint32_t k_lo = k_lo0 + slot * (kTile >> 4);
         if (u >= 2 && !mbar_wait(&pv_done[x * 2 + b], ((u - 2) >> 1) & 1)) return false;
         tc_fence_after();
-        const uint32_t q_base = smem_u32(sq + qs * kQSlot + x * kQBytes);
+        const uint32_t q_lo = q_lo0 + (qs * kQSlot + x * kQBytes) / 16;
         const uint32_t dcol = tmem + x * kHalfCols + 64 * b;
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
-          const uint32_t koff = (ks >> 2) * kKVHalf + (ks & 3) * 32;
-          mma_ss(dcol, smem_desc(q_base + off, 16, 1024), smem_desc(k_base + koff, 16, 1024),
-                 kIdescS, ks > 0 ? 1u : 0u);
+          const uint32_t off = ((ks >> 2) * kQHalf + (ks & 3) * 32) >> 4;
+          const uint32_t koff = ((ks >> 2) * kKVHalf + (ks & 3) * 32) >> 4;
+          mma_ss_w(dcol, q_lo + off, k_lo + koff, kDescHi, kIdescS, ks > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[x * 2 + b]);
         if (x == 1) mma_commit(&k_empty[slot]);
@@ -483,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; ok && j < it.ntiles; ++j, ++t) {
           const int slot = t % kRing, b = t & 1;
           if (!(ok = mbar_wait(&v_full[slot], (t / kRing) & 1))) break;
-          const uint32_t v_base = smem_u32(sv + slot * kTile);
+          const uint32_t v_lo = v_lo0 + slot * (kTile >> 4);
           for (int x = 0; x < 2; ++x) {
             if (!(ok = mbar_wait(&p_full[x * 2 + b], (t >> 1) & 1))) break;
             if (j == 0 && n_it > 0 && !(ok = mbar_wait(&o_free[x], (n_it - 1) & 1))) break;
@@ -491,9 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t hb = tmem + x * kHalfCols;
 #pragma unroll
             for (int kt = 0; kt < kBN / 16; ++kt)
-              mma_ts(hb + kColO, hb + 64 * b + kt * 8,
-                     smem_desc(v_base + kt * 2048, kKVHalf, 1024), kIdescO,
-                     (j > 0 || kt > 0) ? 1u : 0u);
+              mma_ts_w(hb + kColO, hb + 64 * b + kt * 8, v_lo + (kt * 2048 >> 4), kDescHi,
+                       kIdescO, (j > 0 || kt > 0) ? 1u : 0u);
             mma_commit(&pv_done[x * 2 + b]);
             if (x == 1) mma_commit(&v_empty[slot]);
             if (t + 1 <= last && !(ok = issue_s(t + 1, qs, x))) break;
