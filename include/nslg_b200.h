@@ -180,6 +180,15 @@ int nslg_rmsnorm_residual(int dtype, int rows, int hidden, const void* x,
 int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gate_up_stride,
                   void* out, int64_t out_stride, void* stream);
 
+/* Greedy sampling: for each of `rows` rows of logits x (cols entries, row stride
+ * x_stride elements), the maximum (out_val[r], fp32; out_val may be NULL) and the index
+ * of its first occurrence plus index_offset (out_idx[r]), ordered as torch.argmax: NaN
+ * above every number, ties to the lowest index. Replaces logits.argmax(-1) of the
+ * greedy decode on the all-gathered LM-head logits (tp_layers.py:89); a vocab-parallel
+ * head calls it on its shard with index_offset = the shard's first vocabulary id. */
+int nslg_argmax_rows(int dtype, int rows, int cols, const void* x, int64_t x_stride,
+                     int64_t index_offset, float* out_val, int64_t* out_idx, void* stream);
+
 /* Device-side plan of a decode step (every sequence adds one token).
  *
  * Replaces the per-forward plan of FlashInferCacheContext.__init__ and

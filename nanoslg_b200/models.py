@@ -1,7 +1,7 @@
 """Llama-architecture models driving the per-layer path (nanoslg/models.py:25-383).
 
 Same module tree and parameter names as the reference's LlamaTP / LlamaPP / LlamaHybrid
-(so its weight loaders and init rules apply unchanged), with three changes on the hot
+(so its weight loaders and init rules apply unchanged), with these changes on the hot
 path:
 
 * ``RMSNorm`` runs the fused residual-add + RMSNorm kernel.  The blocks carry the
@@ -13,6 +13,9 @@ path:
   ``cache_ctx.attend_rope`` when the context has it (the B200 context does): RoPE, the
   KV append and attention become kernels behind the context.  Any other CacheContext
   gets the reference's torch RoPE followed by ``attend``.
+* Greedy decoding reduces the LM-head logits with the ``nslg_argmax_rows`` kernel; a
+  vocab-parallel head reduces its shard and the ranks exchange (max, index) pairs
+  instead of all-gathering the logits.
 * The GEMMs stay cuBLAS through ``F.linear`` (tp_layers), the collectives NCCL.
 """
 import math
@@ -293,12 +296,12 @@ class _LlamaStage(nn.Module):
         tp = getattr(head, "tp_size", 1)
         if (head is None or tp == 1 or not getattr(head, "gather_output", False)
                 or head.out_features >= (1 << 24)):
-            return self.lm_head(h)[:, -1].argmax(-1)
+            return ops.argmax_rows(self.lm_head(h)[:, -1])
         local = F.linear(h[:, -1], head.weight, head.bias)              # [B, V/tp]
-        val, idx = local.max(-1)
         ctx = get_parallel_context()
         offset = ctx.tp_rank * head.out_features_per_partition
-        pair = torch.stack([val.float(), (idx + offset).float()], -1)     # exact below 2^24
+        idx, val = ops.argmax_rows(local, offset, values=True)
+        pair = torch.stack([val, idx.float()], -1)                        # exact below 2^24
         allp = torch.empty((tp,) + tuple(pair.shape), dtype=pair.dtype, device=pair.device)
         dist.all_gather_into_tensor(allp, pair.contiguous(), group=ctx.tp_group)
         best = allp[..., 0].argmax(0)                                      # first max rank

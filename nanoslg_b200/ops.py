@@ -256,3 +256,18 @@ def silu_mul(gate_up, out=None):
     N.call("nslg_silu_mul", dt, rows, inter, _ptr(g2), g2.stride(0), _ptr(o2), o2.stride(0),
            _stream(gate_up))
     return out
+
+
+def argmax_rows(x, index_offset=0, values=False):
+    """Per row of ``x`` [rows, cols] (last dim contiguous): the index of the first
+    maximum plus ``index_offset`` (int64 [rows]), ordered as torch.argmax (NaN above
+    every number, ties to the lowest index); with ``values`` also the maxima (fp32)."""
+    _need_cuda(x)
+    if x.dim() != 2 or x.stride(-1) != 1:
+        raise ValueError("argmax_rows: x must be [rows, cols] with contiguous rows")
+    rows, cols = x.shape
+    idx = torch.empty(rows, dtype=torch.int64, device=x.device)
+    val = torch.empty(rows, dtype=torch.float32, device=x.device) if values else None
+    N.call("nslg_argmax_rows", _dtype_code(x), rows, cols, _ptr(x), x.stride(0),
+           int(index_offset), _ptr(val), _ptr(idx), _stream(x))
+    return (idx, val) if values else idx

@@ -271,3 +271,30 @@ def test_rope_kv_append_reports_bad_position_and_slot():
                                                 sin[pos.long()[[0, 3]]][None])[0])
     assert torch.equal(fk[1], k[1])
     assert int((fk[3:] != 0).sum()) == 0
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_argmax_rows_matches_torch(dt):
+    """nslg_argmax_rows against torch.argmax: first index of the maximum, NaN above every
+    number, all -inf rows to index 0; vector and scalar (odd column count) paths, row
+    strides, the shard offset and the returned maxima."""
+    g = torch.Generator().manual_seed(31)
+    for rows, cols in ((64, 128256), (1, 128256), (5, 1003), (3, 7), (2, 40000)):
+        x = (torch.randn(rows, cols, generator=g) * 4).to(dt)
+        if rows > 2:
+            x[1, cols // 3] = x[1, 2 * cols // 3] = x[1].max() + 1        # tie: first wins
+            x[2] = float("-inf")
+        if rows > 3:
+            x[3, cols - 1] = float("nan")
+            x[3, cols // 2] = float("nan")
+            x[4, :] = x[4, 0]                                               # all equal
+        xd = x.to(DEV)
+        idx = ops.argmax_rows(xd).cpu()
+        assert torch.equal(idx, x.argmax(-1)), (rows, cols)
+        idx2, val = ops.argmax_rows(xd, index_offset=1000, values=True)
+        assert torch.equal(idx2.cpu(), x.argmax(-1) + 1000)
+        ref = x.float().gather(1, x.argmax(-1, keepdim=True))[:, 0]
+        assert torch.equal(val.cpu(), ref) or torch.allclose(val.cpu(), ref, equal_nan=True)
+    # a strided view: the last position of [B, S, V] logits
+    x = torch.randn(4, 3, 1000, generator=g).to(dt)
+    assert torch.equal(ops.argmax_rows(x.to(DEV)[:, -1]).cpu(), x[:, -1].argmax(-1))

@@ -93,6 +93,13 @@ def test_tp_plan_and_ipc_argument_errors_without_gpu(lib):
     # page zeroing: nothing to do is fine, bad sizes are not
     assert lib.nslg_zero_pages(None, 0, None, 1, 1, 16, None, None) == N.OK
     assert lib.nslg_zero_pages(vp(16), 2, vp(16), 1, 64, 24, None, None) == N.ERR_ARG
+    # greedy argmax: shapes, dtype and pointers are checked before any launch
+    assert lib.nslg_argmax_rows(N.DTYPE_BF16, 0, 10, None, 10, 0, None, None, None) == N.OK
+    assert lib.nslg_argmax_rows(7, 1, 10, vp(16), 10, 0, None, vp(16), None) == N.ERR_ARG
+    assert lib.nslg_argmax_rows(N.DTYPE_BF16, -1, 10, vp(16), 10, 0, None, vp(16), None) == N.ERR_ARG
+    assert lib.nslg_argmax_rows(N.DTYPE_BF16, 1, 0, vp(16), 10, 0, None, vp(16), None) == N.ERR_ARG
+    assert lib.nslg_argmax_rows(N.DTYPE_BF16, 1, 10, vp(16), 9, 0, None, vp(16), None) == N.ERR_ARG
+    assert lib.nslg_argmax_rows(N.DTYPE_BF16, 1, 10, vp(16), 10, 0, None, None, None) == N.ERR_ARG
     # the one-call planner from host arrays: same batch limits, its own argument checks
     # (all of them before any CUDA call)
     hbuf = (ctypes.c_int32 * 64)()
