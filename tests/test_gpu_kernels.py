@@ -147,6 +147,24 @@ def test_paged_decode_many_sequences_split_across_ctas():
         torch.testing.assert_close(out[b], ref[0][0], **BF16_TOL)
 
 
+def test_paged_decode_c2_shape_sampled():
+    """The benchmark's decode workload (64 sequences, lengths U[512, 8192], 32/8 heads,
+    pages shuffled over a large pool): all outputs finite, ten sequences against the
+    oracle."""
+    g = torch.Generator().manual_seed(0)
+    lens = torch.randint(512, 8193, (64,), generator=g).tolist()
+    pk = make_paged(lens, 8, 128, sum(-(-n // 16) for n in lens) + 2000, torch.bfloat16, DEV,
+                    seed=41)
+    q = torch.randn(64, 32, 128, generator=g).to(torch.bfloat16)
+    out = ops.paged_decode(q.to(DEV), pk["pool_k"], pk["pool_v"], pk["indptr"], pk["indices"],
+                           pk["lpl"], 1 / math.sqrt(128))
+    assert bool(torch.isfinite(out).all())
+    out = out.cpu()
+    for b in (0, 3, 9, 20, 33, 40, 51, 58, 62, 63):
+        ref = attend_sequences([q[b:b + 1]], [sequence_kv(pk, b, "k")], [sequence_kv(pk, b, "v")])
+        torch.testing.assert_close(out[b], ref[0][0], **BF16_TOL)
+
+
 def test_paged_decode_fp32_and_other_page_sizes():
     for dt, ps, d in [(torch.float32, 16, 64), (torch.float32, 4, 128), (torch.bfloat16, 8, 128)]:
         lens = [1, 7, 64, 301]
@@ -186,6 +204,49 @@ def test_paged_prefill_causal_ragged(dt, hq, hkv, d):
     for b in range(B):
         torch.testing.assert_close(out[b, offsets[b]:], ref[b], **_tol(dt))
         assert bool((out[b, :offsets[b]] == 0).all())     # padded rows stay zero
+
+
+@pytest.mark.parametrize("scale", [1.0, 6.0])
+def test_paged_prefill_long_prompts(scale):
+    """Long prompts through the tcgen05 kernel (many work items and kv tiles per item,
+    prompts that end mid-tile), plain and with query values scaled up so that the row
+    maxima keep growing past the lazy-rescale threshold (2^8) within a row."""
+    hq, hkv, d = 32, 8, 128
+    spec = [(0, 2100), (0, 1500), (300, 700), (0, 129)]
+    lens = [h + n for h, n in spec]
+    pk = make_paged(lens, hkv, d, 2048, torch.bfloat16, DEV, seed=21)
+    g = torch.Generator().manual_seed(22)
+    counts = [n for _, n in spec]
+    T = sum(counts)
+    q = (torch.randn(T, hq, d, generator=g) * scale).to(torch.bfloat16)
+    qo = torch.tensor([0] + list(torch.cumsum(torch.tensor(counts), 0)), dtype=torch.int32)
+    out = ops.paged_prefill(q.to(DEV), qo.to(DEV), max(counts), pk["pool_k"], pk["pool_v"],
+                            pk["indptr"], pk["indices"], pk["lpl"], 1 / math.sqrt(d),
+                            causal=True).cpu()
+    ks = [sequence_kv(pk, b, "k") for b in range(len(spec))]
+    vs = [sequence_kv(pk, b, "v") for b in range(len(spec))]
+    rows = [q[int(qo[b]):int(qo[b + 1])] for b in range(len(spec))]
+    ref = attend_sequences(rows, ks, vs)
+    for b in range(len(spec)):
+        torch.testing.assert_close(out[int(qo[b]):int(qo[b + 1])], ref[b], **BF16_TOL)
+
+
+def test_paged_prefill_c3_shape_sampled():
+    """The benchmark's prefill workload (64 prompts x 512 tokens, 32/8 heads, shuffled
+    pages): every output finite, and eight sequences checked against the oracle."""
+    hq, hkv, d, B, P = 32, 8, 128, 64, 512
+    pk = make_paged([P] * B, hkv, d, B * P // 16 + 1, torch.bfloat16, DEV, seed=31)
+    g = torch.Generator().manual_seed(32)
+    q = torch.randn(B * P, hq, d, generator=g).to(torch.bfloat16)
+    qo = torch.arange(0, B * P + 1, P, dtype=torch.int32)
+    out = ops.paged_prefill(q.to(DEV), qo.to(DEV), P, pk["pool_k"], pk["pool_v"], pk["indptr"],
+                            pk["indices"], pk["lpl"], 1 / math.sqrt(d), causal=True)
+    assert bool(torch.isfinite(out).all())
+    out = out.cpu()
+    for b in (0, 1, 17, 31, 32, 45, 62, 63):
+        ref = attend_sequences([q[b * P:(b + 1) * P]], [sequence_kv(pk, b, "k")],
+                               [sequence_kv(pk, b, "v")])[0]
+        torch.testing.assert_close(out[b * P:(b + 1) * P], ref, **BF16_TOL)
 
 
 def test_bad_page_id_sets_status_without_fault():
