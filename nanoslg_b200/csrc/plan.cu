@@ -148,6 +148,87 @@ __global__ void __launch_bounds__(256) zero_pages_kernel(const int32_t* pages, i
   for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) dst[v] = make_uint4(0u, 0u, 0u, 0u);
 }
 
+// Small batches in one launch: block b < batch plans sequence b alone (its page-list
+// offset is the sum of the page counts of sequences 0..b-1, each block summing them
+// itself; it applies the table updates of its own row, then writes its fields and
+// gathers its page ids); blocks from `batch` on zero the new pages (page i, layer l,
+// pool k or v). Saves the scan launch and the separate zeroing launch of the two-kernel
+// path; each block reads the start positions of the sequences before it, so it is used
+// up to kFusedMaxBatch sequences.
+constexpr int kFusedMaxBatch = 128;
+constexpr int kFusedThreads = 128;
+
+struct ZeroParams {
+  const int32_t* pages;
+  int n, layers;
+  uint8_t *pool0, *pool1;
+  int64_t num_pages, layer_stride, page_bytes;
+};
+
+__global__ void __launch_bounds__(kFusedThreads) plan_decode_fused_kernel(const PlanParams p,
+                                                                         const ZeroParams z) {
+  const int t = threadIdx.x;
+  if (static_cast<int>(blockIdx.x) >= p.batch) {
+    // ---- page zeroing
+    const int zb = blockIdx.x - p.batch;
+    const int pool = zb & 1, rest = zb >> 1;
+    const int l = rest % z.layers, i = rest / z.layers;
+    const int pg = z.pages[i];
+    if (pg < 0 || pg >= z.num_pages) {
+      if (t == 0 && l == 0 && pool == 0) report(p.status, NSLG_DEV_BAD_PLAN);
+      return;
+    }
+    uint4* dst = reinterpret_cast<uint4*>((pool ? z.pool1 : z.pool0) + l * z.layer_stride +
+                                          pg * z.page_bytes);
+    const int64_t nv = z.page_bytes / 16;
+    for (int64_t v = t; v < nv; v += kFusedThreads) dst[v] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  // ---- sequence b
+  __shared__ int32_t warp_sums[kFusedThreads / 32];
+  const int b = blockIdx.x;
+  const int s = p.slots[b];
+  const int pos = p.starts[b];
+  const bool row_ok = s >= 0 && s < p.bt_rows;
+  int part = 0;
+  for (int j = t; j < b; j += kFusedThreads) part += p.starts[j] / p.page_size + 1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((t & 31) == 0) warp_sums[t >> 5] = part;
+  // this row's table changes
+  for (int i = t; i < p.num_updates; i += kFusedThreads) {
+    if (p.updates[3 * i] != s) continue;
+    const int j = p.updates[3 * i + 1], pg = p.updates[3 * i + 2];
+    if (row_ok && j >= 0 && j < p.bt_stride)
+      p.bt[s * p.bt_stride + j] = pg;
+    else
+      report(p.status, NSLG_DEV_BAD_PLAN);
+  }
+  __syncthreads();
+  int run = 0;
+#pragma unroll
+  for (int w = 0; w < kFusedThreads / 32; ++w) run += warp_sums[w];
+  const int n = pos / p.page_size + 1;    // ceil((pos + 1) / page_size)
+  const bool fits = row_ok && n <= p.bt_stride && run + n <= p.max_indices;
+  if (t == 0) {
+    const int pi = pos / p.page_size;
+    p.positions[b] = pos;
+    p.write_loc[b] = fits ? p.bt[s * p.bt_stride + pi] * p.page_size + pos % p.page_size : -1;
+    p.lpl[b] = pos + 1 - (n - 1) * p.page_size;
+    p.qo[b] = b;
+    p.row_start[b] = b;
+    p.indptr[b] = run;
+    if (b == p.batch - 1) {
+      p.indptr[p.batch] = run + n;
+      p.qo[p.batch] = p.batch;
+    }
+    if (!fits) report(p.status, NSLG_DEV_BAD_PLAN);
+  }
+  if (!fits) return;
+  const int32_t* row = p.bt + s * p.bt_stride;
+  for (int j = t; j < n; j += kFusedThreads) p.indices[run + j] = row[j];
+}
+
 int check_plan_args(int batch, int page_size, int64_t bt_stride, int64_t bt_rows,
                     int num_updates, int64_t max_indices) {
   if (batch < 1 || batch > kScanThreads * kMaxItems)
@@ -301,20 +382,28 @@ extern "C" int nslg_plan_decode_host(int batch, int page_size, const int32_t* sl
   err = cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
 
-  if (num_zero) {
-    zero_pages_kernel<<<dim3(num_zero, static_cast<unsigned>(layers), 2), 256, 0, st>>>(
-        d + 2 * batch + 3 * num_updates, num_zero, static_cast<uint8_t*>(pool_k),
-        static_cast<uint8_t*>(pool_v), num_pages, num_pages * page_bytes, page_bytes,
-        dev_status);
-    rc = check_launch("zero_pages");
-  }
-  if (rc == NSLG_OK) {
-    const int64_t B = batch;
-    PlanParams p{batch, page_size, num_updates, d, d + batch,
-                 num_updates ? d + 2 * batch : nullptr, block_tables, bt_stride, bt_rows, plan,
-                 plan + B, plan + 2 * B, plan + 3 * B + 1, plan + 4 * B + 1, plan + 5 * B + 2,
-                 plan + 6 * B + 2, max_indices, dev_status};
-    rc = launch_plan(p, st);
+  const int64_t B = batch;
+  PlanParams p{batch, page_size, num_updates, d, d + batch,
+               num_updates ? d + 2 * batch : nullptr, block_tables, bt_stride, bt_rows, plan,
+               plan + B, plan + 2 * B, plan + 3 * B + 1, plan + 4 * B + 1, plan + 5 * B + 2,
+               plan + 6 * B + 2, max_indices, dev_status};
+  const int64_t zero_blocks = static_cast<int64_t>(num_zero) * layers * 2;
+  if (batch <= kFusedMaxBatch && zero_blocks < (int64_t{1} << 24)) {
+    ZeroParams z{d + 2 * batch + 3 * num_updates, num_zero, static_cast<int>(layers),
+                 static_cast<uint8_t*>(pool_k), static_cast<uint8_t*>(pool_v), num_pages,
+                 num_pages * page_bytes, page_bytes};
+    plan_decode_fused_kernel<<<static_cast<unsigned>(batch + zero_blocks), kFusedThreads, 0,
+                               st>>>(p, z);
+    rc = check_launch("plan_decode_fused");
+  } else {
+    if (num_zero) {
+      zero_pages_kernel<<<dim3(num_zero, static_cast<unsigned>(layers), 2), 256, 0, st>>>(
+          d + 2 * batch + 3 * num_updates, num_zero, static_cast<uint8_t*>(pool_k),
+          static_cast<uint8_t*>(pool_v), num_pages, num_pages * page_bytes, page_bytes,
+          dev_status);
+      rc = check_launch("zero_pages");
+    }
+    if (rc == NSLG_OK) rc = launch_plan(p, st);
   }
   // whatever was launched may still read the slot: it is handed out again only after this
   err = cudaEventRecord(sl.done, st);

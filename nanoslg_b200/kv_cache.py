@@ -167,7 +167,8 @@ class PagePool:
         self.k = torch.zeros(shape, dtype=cfg.dtype, device=cfg.device)
         self.v = torch.zeros(shape, dtype=cfg.dtype, device=cfg.device)
         self.ref_count = [0] * cfg.max_pages
-        self.tokens_used = [0] * cfg.max_pages
+        # numpy, so a decode step updates the pages of a whole batch in one indexed op
+        self.tokens_used = np.zeros(cfg.max_pages, dtype=np.int32)
         self.ref_count[0] = 1
         self.free_set: Set[int] = set(range(1, cfg.max_pages))
         self._lock = threading.Lock()
@@ -514,9 +515,8 @@ class B200CacheContext(CacheContext):
             start = np.asarray(self.start_positions, dtype=np.int64)
             slots = start % ps
             tu = pool.tokens_used
-            for pid, used in zip(pids, (slots + 1).tolist()):
-                if tu[pid] < used:
-                    tu[pid] = used
+            pa = np.asarray(pids, dtype=np.int64)     # distinct: every page is private
+            tu[pa] = np.maximum(tu[pa], slots + 1)
             self._wi_src = (pids, slots.tolist())
             positions = start.astype(np.int32).reshape(B, 1)
             write_loc = (np.asarray(pids, dtype=np.int64) * ps + slots).astype(np.int32).reshape(B, 1)
@@ -840,9 +840,9 @@ class B200PagedKVCache(KVCacheManager):
         """begin_forward for a decode step (one new token per sequence) planned on the
         device, in one pass over the batch: page extension (in batch order, as
         extend_sequence), the write page, tokens_used, the device table row and the table
-        entries to upload. Returns None -- nothing but page extensions and tokens_used
-        updates done, both of which the general path repeats idempotently -- when a
-        target page is shared (copy on write) or missing."""
+        entries to upload. Returns None -- with nothing done but page extensions, which
+        the general path repeats idempotently -- when a target page is shared (copy on
+        write)."""
         ps = self.cfg.page_size
         rc = self.pool.ref_count
         tu = self.pool.tokens_used
@@ -860,9 +860,6 @@ class B200PagedKVCache(KVCacheManager):
             pid = bt[n0 // ps]
             if rc[pid] > 1:
                 return None
-            used = n0 % ps + 1
-            if tu[pid] < used:
-                tu[pid] = used
             if st.slot < 0:
                 if self._slot_free:
                     st.slot = self._slot_free.pop()
@@ -879,10 +876,13 @@ class B200PagedKVCache(KVCacheManager):
             pids.append(pid)
             slots.append(st.slot)
         B = len(sts)
+        pa = np.asarray(pids, dtype=np.int64)         # distinct: every page is private
+        st0 = np.asarray(starts, dtype=np.int64)
+        tu[pa] = np.maximum(tu[pa], st0 % ps + 1)
         nu = self._stage_updates(dirty)
         self._ensure_tables(self._slot_next, longest)
         c = _DecodeBatch()
-        c.ids = tuple(seq_ids)
+        c.ids = list(seq_ids)
         c.mut = self._mut
         c.ver = _PagedSeqState.version
         c.sts = sts
@@ -892,7 +892,7 @@ class B200PagedKVCache(KVCacheManager):
         c.cur_pid = np.asarray(pids, dtype=np.int64)
         c.longest = longest
         self._dc = c
-        ctx = self._decode_context(c, seq_ids, ntoks, starts, c.n0 % ps)
+        ctx = self._decode_context(c, seq_ids, ntoks, c.n0 % ps)
         ctx._wi_src = (pids, ctx._wi_src[1])
         self._launch_device_plan(ctx, c, nu)
         return ctx
@@ -927,29 +927,29 @@ class B200PagedKVCache(KVCacheManager):
                 if bt.dirty_from < nb:
                     dirty.append(st)
         # tokens_used of each sequence's page: positions fill a private page in order
+        # (the pages are private, so the ids are distinct)
         tu = self.pool.tokens_used
-        for pid, used in zip(c.cur_pid.tolist(), (rem + 1).tolist()):
-            if tu[pid] < used:
-                tu[pid] = used
+        tu[c.cur_pid] = np.maximum(tu[c.cur_pid], rem + 1)
         nu = self._stage_updates(dirty) if dirty else 0
         self._ensure_tables(self._slot_next, c.longest)
-        ctx = self._decode_context(c, seq_ids, ntoks, n0.tolist(), rem)
+        ctx = self._decode_context(c, seq_ids, ntoks, rem)
         self._launch_device_plan(ctx, c, nu)
         return ctx
 
-    def _decode_context(self, c, seq_ids, ntoks, starts, rem):
+    def _decode_context(self, c, seq_ids, ntoks, rem):
         """The context of a device-planned decode step of batch ``c`` (start positions
-        ``starts``, in-page slots ``rem``); its plan arrays come from _launch_device_plan."""
-        B = len(starts)
+        ``c.n0``, in-page slots ``rem``); its plan arrays come from _launch_device_plan."""
+        n0 = c.n0
+        B = n0.shape[0]
         ctx = B200CacheContext.__new__(B200CacheContext)
         ctx.cache = self
         ctx.seq_ids = seq_ids
         ctx.new_token_counts = ntoks
         ctx.input_offsets = [0] * B
         ctx.batch_size = B
-        ctx.start_positions = starts
-        ctx.seq_lens = [n + 1 for n in starts]
-        ctx.max_kv_len = max(starts) + 1
+        ctx.start_positions = n0.tolist()
+        ctx.seq_lens = (n0 + 1).tolist()
+        ctx.max_kv_len = int(n0.max()) + 1
         ctx._is_decode = True
         ctx._iw = 1
         ctx._wi = None
@@ -1080,10 +1080,11 @@ class B200PagedKVCache(KVCacheManager):
 
     def begin_forward(self, seq_ids, ntoks, offsets=None):
         if (self.device_plan and 0 < len(seq_ids) <= 4096 and not any(offsets or ())
-                and all(n == 1 for n in ntoks)):
+                and (ntoks.count(1) == len(ntoks) if isinstance(ntoks, list)
+                     else all(n == 1 for n in ntoks))):
             c = self._dc
             if (c is not None and c.mut == self._mut and c.ver == _PagedSeqState.version
-                    and c.ids == tuple(seq_ids)):
+                    and c.ids == list(seq_ids)):
                 ctx = self._begin_decode_cached(c, seq_ids, ntoks)
                 if ctx is not None:
                     return ctx

@@ -226,12 +226,14 @@ def test_runner_cuda_graph_decode_matches_reference_tokens():
     r.release([toks2])
 
 
-def test_device_plan_matches_host_plan():
-    """nslg_plan_decode (device block tables, csrc/plan.cu) builds the same decode plan as
-    the host path (kv_cache.py:547-632 restated) over a run with page-boundary crossings,
-    sequences joining and leaving (table rows reused, tables grown) and radix-shared
-    prefixes (copy on write takes the host path for that step, then the device tables are
-    refreshed)."""
+@pytest.mark.parametrize("n_live", [24, 160])
+def test_device_plan_matches_host_plan(n_live):
+    """nslg_plan_decode_host (device block tables, csrc/plan.cu) builds the same decode
+    plan as the host path (kv_cache.py:547-632 restated) over a run with page-boundary
+    crossings, sequences joining and leaving (table rows reused, tables grown) and
+    radix-shared prefixes (copy on write takes the host path for that step, then the
+    device tables are refreshed). 24 sequences take the one-launch planner, 160 the
+    scan + gather kernels."""
     import random
     from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
     dev = torch.device("cuda:0")
@@ -266,13 +268,15 @@ def test_device_plan_matches_host_plan():
                 m.append_token_ids(sid, [1, 2, 3])
                 m.release_sequence(sid)
 
-    add(24)
+    add(n_live)
     fields = ("_pos_i32", "_write_loc", "kv_indptr", "kv_indices", "kv_last_page_len",
               "qo_indptr", "q_row_start")
     for step in range(60):
         if step in (15, 35):
             drop(8)
             add(12)
+        if n_live > 100 and step > 20:
+            break
         ctxs = [m.begin_forward(list(live), [1] * len(live)) for m in mgrs]
         for f in fields:
             a, b = getattr(ctxs[0], f), getattr(ctxs[1], f)
@@ -280,6 +284,7 @@ def test_device_plan_matches_host_plan():
         assert ctxs[0]._write_info == ctxs[1]._write_info
         assert [list(m.seqs[s].block_table) for s in live for m in mgrs[:1]] == \
                [list(m.seqs[s].block_table) for s in live for m in mgrs[1:]]
+        assert list(mgrs[0].pool.tokens_used) == list(mgrs[1].pool.tokens_used)
         for m, c in zip(mgrs, ctxs):
             m.end_forward(c)
     from nanoslg_b200 import ops
