@@ -17,7 +17,8 @@
 // device, each reused only after the kernels that read it have finished, tracked with
 // one event per slot) and the kernels read the few hundred bytes straight from there;
 // the pages allocated since the last forward are zeroed (K and V pools) in the same
-// call. No device upload buffer, no separate copy: one host call per decode step.
+// call. No device upload buffer, no separate copy: one host call per decode step, and
+// for batches up to kFusedMaxBatch one kernel launch (plan_decode_fused_kernel).
 #include <cstring>
 #include <mutex>
 #include <string>
