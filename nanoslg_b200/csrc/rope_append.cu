@@ -9,9 +9,9 @@
 //   out = x*cos + cat(-x2, x1)*sin
 // with every product and the sum rounded to the activation type.
 //
-// bf16 (rope_kv_append_bf16_kernel): one CTA per token. The token's cos/sin row is
-// rounded to bf16 once, into shared memory, and every q/k head of the token reads it
-// from there; the products and sums run as paired bf16 instructions (mul/add/sub.rn
+// bf16 (rope_kv_append_bf16_kernel): one CTA per token, two 16-byte items per thread,
+// both read before anything else. The token's cos/sin row is rounded to bf16 once, into
+// shared memory, and every q/k head of the token reads it from there; the products and sums run as paired bf16 instructions (mul/add/sub.rn
 // .bf16x2: each rounds the exact result once, as torch does after computing the op in
 // fp32, and explicit .rn keeps them from being contracted into a fused multiply-add).
 // Per 16-byte output: 4 multiplies and 2 adds of bf16 pairs, no conversions.
@@ -158,6 +158,36 @@ __global__ void __launch_bounds__(kBf16MaxThreads) rope_kv_append_bf16_kernel(co
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
+  const int q_items = p.q_out != nullptr ? p.hq * VH : 0;
+  const int k_items = p.hkv * VH;
+  const int per_tok = q_items + k_items + p.hkv * VROW;
+  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) + t * p.q_stride;
+  const __nv_bfloat16* kb = static_cast<const __nv_bfloat16*>(p.k) + t * p.k_stride;
+  const __nv_bfloat16* vb = static_cast<const __nv_bfloat16*>(p.v) + t * p.v_stride;
+  // item w: q/k head idx / VH, 16-byte chunk idx % VH of both halves; or v head
+  // idx / VROW, chunk idx % VROW
+  auto load = [&](int w, uint4& x1, uint4& x2) {
+    if (w < q_items + k_items) {
+      const bool is_q = w < q_items;
+      const int idx = is_q ? w : w - q_items;
+      const __nv_bfloat16* src = (is_q ? qb : kb) + (idx / VH) * D + (idx % VH) * 8;
+      x1 = *reinterpret_cast<const uint4*>(src);
+      x2 = *reinterpret_cast<const uint4*>(src + HALF);
+    } else {
+      const int idx = w - q_items - k_items;
+      x1 = *reinterpret_cast<const uint4*>(vb + (idx / VROW) * D + (idx % VROW) * 8);
+    }
+  };
+  // Each thread owns two items, w = tid and tid + blockDim; both are read before the
+  // table row is staged, so every thread has 32-64 bytes in flight while the position
+  // and the cos/sin row arrive.
+  uint4 f1[2], f2[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    f1[u] = f2[u] = make_uint4(0u, 0u, 0u, 0u);
+    const int w = threadIdx.x + u * blockDim.x;
+    if (w < per_tok) load(w, f1[u], f2[u]);
+  }
   int64_t loc = p.write_loc != nullptr ? p.write_loc[t] : -1;
   if (loc >= p.pool_slots) {
     if (threadIdx.x == 0) report(p.status, NSLG_DEV_BAD_SLOT);
@@ -181,26 +211,18 @@ __global__ void __launch_bounds__(kBf16MaxThreads) rope_kv_append_bf16_kernel(co
     }
   }
   __syncthreads();
-  const int q_items = p.q_out != nullptr ? p.hq * VH : 0;
-  const int k_items = p.hkv * VH;
-  const int per_tok = q_items + k_items + p.hkv * VROW;
-  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) + t * p.q_stride;
-  const __nv_bfloat16* kb = static_cast<const __nv_bfloat16*>(p.k) + t * p.k_stride;
-  for (int w = threadIdx.x; w < per_tok; w += blockDim.x) {
+  auto finish = [&](int w, uint4 x1, uint4 x2) {
     if (w < q_items + k_items) {
       const bool is_q = w < q_items;
       const int idx = is_q ? w : w - q_items;
       const int h = idx / VH, c = idx % VH;
-      const __nv_bfloat16* src = (is_q ? qb : kb) + h * D;
       __nv_bfloat16* dst;
       if (is_q) {
         dst = static_cast<__nv_bfloat16*>(p.q_out) + (static_cast<int64_t>(t) * p.hq + h) * D;
       } else {
-        if (loc < 0) continue;
+        if (loc < 0) return;
         dst = static_cast<__nv_bfloat16*>(p.pool_k) + (loc * p.hkv + h) * D;
       }
-      uint4 x1 = *reinterpret_cast<const uint4*>(src + c * 8);
-      uint4 x2 = *reinterpret_cast<const uint4*>(src + HALF + c * 8);
       if (rot) {
         const uint4 c1 = *reinterpret_cast<const uint4*>(&cs2[c * 4]);
         const uint4 s1 = *reinterpret_cast<const uint4*>(&sn2[c * 4]);
@@ -221,14 +243,23 @@ __global__ void __launch_bounds__(kBf16MaxThreads) rope_kv_append_bf16_kernel(co
       *reinterpret_cast<uint4*>(dst + c * 8) = x1;
       *reinterpret_cast<uint4*>(dst + HALF + c * 8) = x2;
     } else {
-      if (loc < 0) continue;
+      if (loc < 0) return;
       const int idx = w - q_items - k_items;
-      const int h = idx / VROW, c = idx % VROW;
-      const __nv_bfloat16* src =
-          static_cast<const __nv_bfloat16*>(p.v) + t * p.v_stride + h * D + c * 8;
-      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.pool_v) + (loc * p.hkv + h) * D + c * 8;
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.pool_v) +
+                           (loc * p.hkv + idx / VROW) * D + (idx % VROW) * 8;
+      *reinterpret_cast<uint4*>(dst) = x1;
     }
+  };
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int w = threadIdx.x + u * blockDim.x;
+    if (w < per_tok) finish(w, f1[u], f2[u]);
+  }
+  // rows wider than two items per thread (a block has at most kBf16MaxThreads threads)
+  for (int w = threadIdx.x + 2 * blockDim.x; w < per_tok; w += blockDim.x) {
+    uint4 x1 = make_uint4(0u, 0u, 0u, 0u), x2 = x1;
+    load(w, x1, x2);
+    finish(w, x1, x2);
   }
 }
 
@@ -246,7 +277,7 @@ int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, con
   if (dtype == NSLG_DTYPE_BF16 && (d == 128 || d == 64) && num_tokens > 0) {
     const int per_tok = (q_out ? hq * (d / 16) : 0) + hkv * (d / 16) + hkv * (d / 8);
     if (per_tok == 0) return NSLG_OK;
-    int threads = (per_tok + 31) / 32 * 32;
+    int threads = ((per_tok + 1) / 2 + 31) / 32 * 32;   // two items per thread
     if (threads > kBf16MaxThreads) threads = kBf16MaxThreads;
     const dim3 grid(static_cast<unsigned>(num_tokens));
     if (d == 128)
