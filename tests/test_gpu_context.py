@@ -315,3 +315,78 @@ def test_device_plan_zeroes_new_pages():
     untouched = [p for p in range(64) if p not in pages]
     assert bool((mgr.pool.k[:, untouched] == 3.0).all())
     mgr.end_forward(ctx)
+
+
+@pytest.mark.parametrize("batch", [5, 100, 300])
+def test_plan_decode_device_arrays_match_host_arrays(batch):
+    """nslg_plan_decode (inputs in device memory, scan + gather kernels) and
+    nslg_plan_decode_host (inputs from host arrays; one launch up to 128 sequences) give
+    the same plan for the same tables, rows, start positions and table updates."""
+    import ctypes
+    import numpy as np
+    from nanoslg_b200 import _native as N
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(batch)
+    ps, stride, rows = 16, 64, batch + 7
+    slots = rng.permutation(rows)[:batch].astype(np.int32)
+    starts = rng.integers(0, stride * ps - 1, batch).astype(np.int32)
+    tables = rng.integers(1, 50000, (rows, stride)).astype(np.int32)
+    nu = 40
+    upd = np.stack([rng.choice(slots, nu), rng.integers(0, stride, nu),
+                    rng.integers(1, 50000, nu)], 1).astype(np.int32)
+    upd = upd[np.unique(upd[:, :2], axis=0, return_index=True)[1]]   # one value per entry
+    nu = upd.shape[0]
+    total = int((starts // ps + 1).sum())
+    size = 6 * batch + 2 + total
+    outs = []
+    status = ops.status_word(dev)
+    lib = N.lib()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for host in (False, True):
+        bt = torch.from_numpy(tables).to(dev)
+        plan = torch.full((size,), -7, dtype=torch.int32, device=dev)
+        B = batch
+        if host:
+            hs, hst, hu = (np.ascontiguousarray(a) for a in (slots, starts, upd))
+            rc = lib.nslg_plan_decode_host(B, ps, hs.ctypes.data, hst.ctypes.data, nu,
+                                           hu.ctypes.data, 0, None, None, None, 1, 1, 16,
+                                           bt.data_ptr(), stride, rows, plan.data_ptr(), total,
+                                           status.data_ptr(), stream)
+        else:
+            ds, dst, du = (torch.from_numpy(a).to(dev) for a in (slots, starts, upd))
+            p = plan.data_ptr()
+            rc = lib.nslg_plan_decode(B, ps, ds.data_ptr(), dst.data_ptr(), nu, du.data_ptr(),
+                                      bt.data_ptr(), stride, rows, p, p + 4 * B, p + 8 * B,
+                                      p + 4 * (3 * B + 1), p + 4 * (4 * B + 1),
+                                      p + 4 * (5 * B + 2), p + 4 * (6 * B + 2), total,
+                                      status.data_ptr(), stream)
+        assert rc == 0, lib.nslg_last_error()
+        torch.cuda.synchronize(dev)
+        outs.append((plan.cpu(), bt.cpu()))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
+    # and against the plan restated on the host
+    tab = tables.copy()
+    tab[upd[:, 0], upd[:, 1]] = upd[:, 2]
+    n = starts // ps + 1
+    indptr = np.concatenate([[0], np.cumsum(n)])
+    want = np.concatenate([starts, tab[slots, starts // ps] * ps + starts % ps, indptr,
+                           starts + 1 - (n - 1) * ps, np.arange(batch + 1), np.arange(batch),
+                           np.concatenate([tab[s, :k] for s, k in zip(slots, n)])])
+    assert outs[1][0].numpy().tolist() == want.tolist()
+
+
+def test_zero_pages_entry_point():
+    """nslg_zero_pages zeroes exactly the listed pages of every layer of one pool."""
+    from nanoslg_b200 import _native as N
+    dev = torch.device("cuda:0")
+    pool = torch.full((3, 10, 16, 2, 64), 3.0, dtype=torch.bfloat16, device=dev)
+    pages = torch.tensor([2, 5, 9], dtype=torch.int32, device=dev)
+    page_bytes = pool[0, 0].numel() * 2
+    N.call("nslg_zero_pages", pages.data_ptr(), 3, pool.data_ptr(), 3, 10, page_bytes,
+           ops.status_word(dev).data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize(dev)
+    z = [2, 5, 9]
+    assert int(pool[:, z].float().abs().sum()) == 0
+    keep = [p for p in range(10) if p not in z]
+    assert bool((pool[:, keep] == 3.0).all())
