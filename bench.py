@@ -562,9 +562,11 @@ def run_allreduce(device, world, rank, hidden=4096, rows_list=(1, 64, 256), call
 
 
 # ------------------------------------------------------------------------ CPU side
-def cpu_reference(max_seconds, n_calls=None, seed=0):
+def cpu_reference(max_seconds, n_calls=None, seed=0, warmup=1):
     """The reference's contiguous attend (oracle/attention.py restating
-    kv_cache.py:247-325) on the C2 workload, all host threads."""
+    kv_cache.py:247-325) on the C2 workload, all host threads: ``warmup`` untimed calls,
+    then timed calls until ``n_calls`` are done or ``max_seconds`` have passed (whichever
+    comes first; at least one)."""
     from oracle.attention import ContiguousOracle
     torch.set_num_threads(os.cpu_count() or 1)
     lens = c2_lens(seed)
@@ -580,10 +582,12 @@ def cpu_reference(max_seconds, n_calls=None, seed=0):
     k = torch.randn(B, 1, HKV, D, generator=g).to(torch.bfloat16)
     v = torch.randn(B, 1, HKV, D, generator=g).to(torch.bfloat16)
     starts = list(lens)
-    orc.attend(0, q, k, v, starts, [1] * B, [0] * B)       # warm-up
+    for _ in range(max(1, warmup)):
+        orc.attend(0, q, k, v, starts, [1] * B, [0] * B)
     times = []
     t_end = time.perf_counter() + max_seconds
-    while (n_calls is None and time.perf_counter() < t_end) or (n_calls and len(times) < n_calls):
+    while not times or ((n_calls is None or len(times) < n_calls)
+                        and time.perf_counter() < t_end):
         t0 = time.perf_counter()
         orc.attend(0, q, k, v, starts, [1] * B, [0] * B)
         times.append(time.perf_counter() - t0)
@@ -635,12 +639,10 @@ def main():
     if a.impl == "reference":
         if rank != 0:
             return 0
-        per_call = cpu_reference(0, n_calls=1)["s_per_call"]
-        budget = 150.0
-        n = max(1, min(a.steps, int(budget / max(per_call, 1e-3))))
-        r = cpu_reference(0, n_calls=n)
+        # a.warmup untimed calls, then up to a.steps timed ones within 150 s
+        r = cpu_reference(150.0, n_calls=a.steps, warmup=a.warmup)
         line = {"metric": metric, "value": r["value"], "unit": "tok/s", "n_gpus": a.gpus,
-                "steps": r["calls"], "warmup": 1, "ms_per_step": r["s_per_call"] * 1e3,
+                "steps": r["calls"], "warmup": a.warmup, "ms_per_step": r["s_per_call"] * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V, random page table)",
                 "config": config, "impl": "reference",
