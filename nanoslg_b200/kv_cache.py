@@ -529,13 +529,21 @@ class B200CacheContext(CacheContext):
                              "qo_indptr", "q_row_start", "kv_indices"))
 
     def __getattr__(self, name):
-        # a device-planned decode step slices its plan views out of the buffer on first
-        # use (most steps only need the raw pointers)
+        # a device-planned decode step builds its plan views and its per-sequence lists on
+        # first use (most steps only need the raw pointers)
+        d = self.__dict__
         if name in B200CacheContext._PLAN_VIEWS:
-            src = self.__dict__.get("_plan_src")
+            src = d.get("_plan_src")
             if src is not None:
                 self._set_plan_views(*src)
-                return self.__dict__[name]
+                return d[name]
+        elif name in ("start_positions", "seq_lens", "max_kv_len"):
+            n0 = d.get("_n0")
+            if n0 is not None:
+                d["start_positions"] = n0.tolist()
+                d["seq_lens"] = (n0 + 1).tolist()
+                d["max_kv_len"] = int(n0.max()) + 1
+                return d[name]
         raise AttributeError(name)
 
     def _set_plan_views(self, d, B, iw, total):
@@ -947,9 +955,7 @@ class B200PagedKVCache(KVCacheManager):
         ctx.new_token_counts = ntoks
         ctx.input_offsets = [0] * B
         ctx.batch_size = B
-        ctx.start_positions = n0.tolist()
-        ctx.seq_lens = (n0 + 1).tolist()
-        ctx.max_kv_len = int(n0.max()) + 1
+        ctx._n0 = n0.copy()       # start_positions / seq_lens / max_kv_len, built on use
         ctx._is_decode = True
         ctx._iw = 1
         ctx._wi = None
