@@ -10,7 +10,10 @@ or contiguous SDPA (kv_cache.py:312-322), each layer launches the sm_100a kernel
 ``nanoslg_b200/csrc`` through the C ABI -- the KV append (optionally fused with RoPE,
 see ``attend_rope``) and split-KV decode or causal prefill attention reading the pages
 in place.  The per-forward plan (positions, write slots, CSR) is built once per
-``begin_forward`` and shipped to the device in one host-to-device copy.
+``begin_forward``: for decode steps on a CUDA pool it is built on the GPU from block
+tables mirrored in device memory (one ``nslg_plan_decode_host`` call per step, which
+also zeroes the newly allocated pages), otherwise on the host and shipped to the
+device in one host-to-device copy.
 
 ``create_cache_manager`` always returns the B200 backend: there is no second backend
 and no CPU fallback; the bookkeeping itself runs on any device (tests drive it with
@@ -195,7 +198,8 @@ class PagePool:
 
     def take_pending_zero(self) -> List[int]:
         """The pages allocated since the last flush (sorted, unique); the caller zeroes
-        them (nslg_zero_pages)."""
+        them (``nslg_plan_decode_host`` on the device-planned path, ``flush_zero``
+        otherwise)."""
         with self._lock:
             if not self._pending_zero:
                 return []
