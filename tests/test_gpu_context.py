@@ -390,3 +390,29 @@ def test_zero_pages_entry_point():
     assert int(pool[:, z].float().abs().sum()) == 0
     keep = [p for p in range(10) if p not in z]
     assert bool((pool[:, keep] == 3.0).all())
+
+
+def test_plan_decode_host_refuses_graph_capture():
+    """nslg_plan_decode_host reads host staging, so it cannot be baked into a CUDA graph:
+    inside a capture it returns NSLG_ERR_UNSUPPORTED without enqueuing anything, and the
+    capture ends normally."""
+    import numpy as np
+    from nanoslg_b200 import _native as N
+    dev = torch.device("cuda:0")
+    lib = N.lib()
+    slots = np.zeros(1, dtype=np.int32)
+    starts = np.zeros(1, dtype=np.int32)
+    bt = torch.ones((4, 8), dtype=torch.int32, device=dev)
+    plan = torch.zeros(64, dtype=torch.int32, device=dev)
+    side = torch.cuda.Stream(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            rc = lib.nslg_plan_decode_host(1, 16, slots.ctypes.data, starts.ctypes.data, 0, None,
+                                           0, None, None, None, 1, 1, 16, bt.data_ptr(), 8, 4,
+                                           plan.data_ptr(), 8, None, side.cuda_stream)
+            plan.add_(0)                  # the graph holds something to replay
+    assert rc == N.ERR_UNSUPPORTED and b"graph" in lib.nslg_last_error()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    assert int(plan.abs().sum()) == 0
