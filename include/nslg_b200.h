@@ -93,6 +93,13 @@ int64_t nslg_decode_workspace_bytes(int batch, int num_qo_heads, int head_dim);
  *   kv_len(b) = (kv_indptr[b+1]-kv_indptr[b]-1)*page_size + kv_last_page_len[b].
  * GQA: query head h reads kv head h / (num_qo_heads / num_kv_heads).
  * Sequences with no pages produce zeros.
+ * Launched with programmatic dependent launch: it may start while the kernel before it
+ * on the stream runs, if that kernel allows its dependents to launch early (the library's
+ * KV-append, RMSNorm and SwiGLU kernels do). It reads q and the pool only after that
+ * kernel has finished, but the CSR arrays (kv_indptr, kv_indices, kv_last_page_len)
+ * before: they must be written by work that finished before that kernel started (the
+ * planner's kernels never allow an early launch, so a plan followed directly by this
+ * call is always safe).
  */
 int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
                       int head_dim, int page_size, const void* q, int64_t q_stride,

@@ -108,7 +108,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + stages;
   float* comb = reinterpret_cast<float*>(empty + stages);  // [8 warps][G][D] o, then m, l
 
-  pdl_wait();   // q (rotated by the append kernel) and the plan come from earlier work
+  // Programmatic dependent launch: this grid may start while the kernel before it (the
+  // KV append, which also writes the rotated q) is still running. Everything up to the
+  // first page load and the first q read -- staging the CSR, barrier set-up, the first
+  // page ids -- uses only data of kernels that finished before that one started (the
+  // plan), so it runs before the wait; the producer waits before its first TMA load and
+  // the consumers before they read q.
   // The CSR lookups (slice bounds, sequence of a page, segment ends, last-page lengths)
   // are chains of dependent loads; with the arrays in shared memory (one coalesced load
   // by the whole CTA) they no longer delay the first TMA issue or each new segment.
@@ -180,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int np = 0;
     bool have = next_stage(q0, np);
     int my_id = (have && lane < np) ? p.indices[q0 + lane] : 0;
+    pdl_wait();   // the pages hold the keys and values the previous kernel appended
     while (have) {
       int64_t nq0 = 0;
       int nnp = 0;
@@ -238,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // -------------------------------------------------------------- consumers
+  pdl_wait();   // q comes from the previous kernel
   const int h = warp % HKV;
   const int j = warp / HKV;
   const int g = lane >> 2;        // mma row group: query head g (and g + 8)
