@@ -2,11 +2,13 @@
  * nslg_b200.h -- C ABI of the B200 (sm_100a) kernels behind NanoSLG's per-layer
  * attention path.
  *
- * Every entry point takes raw device pointers, element strides and sizes, plus the
- * cudaStream_t to launch on (passed as void*), and returns an int status
- * (NSLG_OK == 0).  On a non-zero status nslg_last_error() returns a message for the
- * calling thread.  No entry point allocates device memory: scratch space is passed in
- * by the caller (see nslg_decode_workspace_bytes).
+ * Every entry point takes raw device pointers (nslg_plan_decode_host: host arrays for
+ * its inputs), element strides and sizes, plus the cudaStream_t to launch on (passed as
+ * void*), and returns an int status (NSLG_OK == 0).  On a non-zero status
+ * nslg_last_error() returns a message for the calling thread.  Apart from
+ * nslg_ipc_alloc, whose job it is, no entry point allocates device memory: scratch
+ * space is passed in by the caller (see nslg_decode_workspace_bytes);
+ * nslg_plan_decode_host keeps pinned host staging of its own.
  *
  * Errors that can only be seen on the device (a page id outside the pool, a write
  * slot outside the pool, a position outside the RoPE table) never trap: the kernel
