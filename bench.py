@@ -396,8 +396,29 @@ def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=N
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
     runner.release()
+    roof = _decode_roofline(runner, batch, prompt + warmup + (steps + 1) / 2)
     return runner, {"batch": batch, "prompt": prompt, "steps": steps, "ms_per_step": ms / steps,
-                    "tok_s": batch * steps / (ms / 1e3), "prefill_ms": prefill_ms}
+                    "tok_s": batch * steps / (ms / 1e3), "prefill_ms": prefill_ms,
+                    "hbm_roofline": dict(roof, frac=roof["ms_per_step"] / (ms / steps))}
+
+
+def _decode_roofline(runner, batch, avg_ctx):
+    """Lower bound of one decode step of this rank from HBM traffic alone: every weight
+    of the rank read once (embedding: only the batch's rows) plus the K/V of every
+    sequence and layer (average context ``avg_ctx`` tokens over the timed steps), at the
+    measured HBM bandwidth."""
+    hidden = runner.hf.hidden_size
+    wbytes = 0
+    for name, prm in runner.model.named_parameters():
+        n = prm.numel() * prm.element_size()
+        if "embed_tokens" in name:
+            n = batch * hidden * prm.element_size()
+        wbytes += n
+    cfg = runner.cache.cfg
+    kv = batch * avg_ctx * cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * 2
+    peak, src = _hbm_peak()
+    return {"weight_bytes": wbytes, "kv_bytes": int(kv), "peak_gbs": peak,
+            "peak_source": src, "ms_per_step": (wbytes + kv) / (peak * 1e9) * 1e3}
 
 
 def run_llama_c4(device, world, rank, runner, batches=(4, 16, 64), prefix_len=1024,
