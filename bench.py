@@ -300,7 +300,9 @@ def run_elementwise_kernels(device, reps=10, batch=64, prompt=512, hidden=4096):
         rows (512 x 128 x 4 B x 2) + positions and write slots (4 B each per row);
       rmsnorm_residual_kernel: x, residual [T, 4096] bf16 with weight; residual <- x +
         residual, out = rmsnorm(residual) * weight. Algorithmic bytes: x, residual read,
-        residual and out written, weight once.
+        residual and out written, weight once;
+      silu_mul_kernel: the stacked gate|up GEMM output [T, 2 x 14336] bf16 read, silu(gate)
+        * up [T, 14336] written.
     CUDA events, median of ``reps`` launches each."""
     from nanoslg_b200 import ops
     from nanoslg_b200.models import precompute_rope_frequencies
@@ -346,6 +348,13 @@ def run_elementwise_kernels(device, reps=10, batch=64, prompt=512, hidden=4096):
     norm_bytes = 4 * T * hidden * 2 + hidden * 2
     del q, k, v, q_out, pool_k, pool_v, x, res, out
     torch.cuda.empty_cache()
+    inter = 14336
+    gu = torch.randn(T, 2 * inter, device=device, generator=g).to(bf)
+    act = torch.empty(T, inter, device=device, dtype=bf)
+    silu_ms = timed(lambda: ops.silu_mul(gu, out=act))
+    silu_bytes = 3 * T * inter * 2
+    del gu, act
+    torch.cuda.empty_cache()
     leg = lambda name, ms, nbytes: {
         "kernel": name, "ms_median": ms, "algorithmic_bytes": nbytes,
         "gbs": nbytes / (ms / 1e3) / 1e9, "frac": nbytes / (ms / 1e3) / 1e9 / peak}
@@ -353,7 +362,8 @@ def run_elementwise_kernels(device, reps=10, batch=64, prompt=512, hidden=4096):
                         f"({T} rows), 32/8 heads, D=128, hidden {hidden}, bf16",
             "peak_gbs": peak, "peak_source": src,
             "rope_kv_append": leg("rope_kv_append_bf16_kernel", rope_ms, rope_bytes),
-            "rmsnorm_residual": leg("rmsnorm_residual_kernel", norm_ms, norm_bytes)}
+            "rmsnorm_residual": leg("rmsnorm_residual_kernel", norm_ms, norm_bytes),
+            "silu_mul": leg("silu_mul_kernel", silu_ms, silu_bytes)}
 
 
 # ------------------------------------------------------------------ model decode

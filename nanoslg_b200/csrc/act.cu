@@ -4,7 +4,9 @@
 // GEMMs and two elementwise kernels. With the gate and up weights stacked, one GEMM
 // writes [rows, 2*I] (gate in columns [0, I), up in [I, 2I)) and this kernel produces
 // silu(gate) * up with the reference's rounding points: silu in fp32 rounded to the
-// activation type, then the product rounded again. 16-byte vector loads and stores.
+// activation type, then the product rounded again (bf16: silu from the hardware
+// exponential and an approximate division, within the bf16 rounding). 16-byte vector
+// loads and stores.
 #include "common.cuh"
 #include "launch.h"
 
@@ -35,7 +37,11 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* gu, int64_t gu_s
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
       const float x = Elem<T>::to_f(g.e[j]);
-      const float s = Elem<T>::round(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
+      // bf16 rounds silu to 8 bits, so the hardware exponential and the approximate
+      // division are enough there (and keep the kernel memory-bound); fp32 keeps the
+      // correctly rounded division and the full-precision exponential
+      const float s = sizeof(T) == 2 ? Elem<T>::round(__fdividef(x, 1.f + __expf(-x)))
+                                     : Elem<T>::round(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
       y.e[j] = Elem<T>::from_f(__fmul_rn(s, Elem<T>::to_f(u.e[j])));
     }
     *reinterpret_cast<uint4*>(out + r * out_stride + c) = y.u;
