@@ -111,6 +111,22 @@ int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
                       float sm_scale, void* workspace, int64_t workspace_bytes,
                       uint32_t* dev_status, void* stream);
 
+/* The decode step of CacheContext.attend in one call: the new token's k and v of each
+ * sequence appended to the pool at write_loc (nslg_rope_kv_append without rotation, q
+ * and k already rotated as attend() receives them), then nslg_paged_decode over the
+ * sequences' pages, the new token included. Arguments as in those two calls; k and v are
+ * [batch, num_kv_heads, head_dim] rows with strides k_stride / v_stride. Replaces the
+ * decode branch of FlashInferCacheContext.attend (kv_cache.py:639-651: _write_kv, then
+ * the decode wrapper's run). */
+int nslg_append_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
+                             int head_dim, int page_size, const void* q, int64_t q_stride,
+                             const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                             const int32_t* write_loc, void* out, int64_t out_stride,
+                             void* pool_k, void* pool_v, int64_t num_pages,
+                             const int32_t* kv_indptr, const int32_t* kv_indices,
+                             const int32_t* kv_last_page_len, float sm_scale, void* workspace,
+                             int64_t workspace_bytes, uint32_t* dev_status, void* stream);
+
 /* Scratch size of nslg_paged_decode_noalloc: a fixed device array inside the library. */
 #define NSLG_NOALLOC_SCRATCH_BYTES (8ll << 20)
 

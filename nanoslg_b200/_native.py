@@ -47,6 +47,9 @@ SIGNATURES = {
     "nslg_plan_decode": (_i32, [_i32, _i32, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _vp, _vp, _vp,
                                 _vp, _vp, _vp, _vp, _i64, _vp, _vp]),
     "nslg_zero_pages": (_i32, [_vp, _i32, _vp, _i64, _i64, _i64, _vp, _vp]),
+    "nslg_append_paged_decode": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64,
+                                        _vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp,
+                                        _vp, _f32, _vp, _i64, _vp, _vp]),
     "nslg_argmax_rows": (_i32, [_i32, _i32, _i32, _vp, _i64, _i64, _vp, _vp, _vp]),
     "nslg_plan_decode_host": (_i32, [_i32, _i32, _vp, _vp, _i32, _vp, _i32, _vp, _vp, _vp, _i64,
                                      _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),

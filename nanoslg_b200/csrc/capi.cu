@@ -139,6 +139,31 @@ int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads, 
                                      kv_last_page_len, sm_scale, 0, dev_status, st);
 }
 
+int nslg_append_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
+                             int head_dim, int page_size, const void* q, int64_t q_stride,
+                             const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                             const int32_t* write_loc, void* out, int64_t out_stride,
+                             void* pool_k, void* pool_v, int64_t num_pages,
+                             const int32_t* kv_indptr, const int32_t* kv_indices,
+                             const int32_t* kv_last_page_len, float sm_scale, void* workspace,
+                             int64_t workspace_bytes, uint32_t* dev_status, void* stream) {
+  g_last_error.clear();
+  if (batch < 0) return set_error(NSLG_ERR_ARG, "append_paged_decode: batch < 0");
+  if (batch == 0) return NSLG_OK;
+  if (!write_loc) return set_error(NSLG_ERR_ARG, "append_paged_decode: null write_loc");
+  if (page_size <= 0 || num_pages <= 0)
+    return set_error(NSLG_ERR_ARG, "append_paged_decode: page_size and num_pages must be positive");
+  int rc = nslg_rope_kv_append(dtype, batch, num_kv_heads, num_kv_heads, head_dim, nullptr, 0, k,
+                               k_stride, v, v_stride, nullptr, nullptr, nullptr, nullptr, 0,
+                               write_loc, pool_k, pool_v, num_pages * page_size, dev_status,
+                               stream);
+  if (rc != NSLG_OK) return rc;
+  return nslg_paged_decode(dtype, batch, num_qo_heads, num_kv_heads, head_dim, page_size, q,
+                           q_stride, out, out_stride, pool_k, pool_v, num_pages, kv_indptr,
+                           kv_indices, kv_last_page_len, sm_scale, workspace, workspace_bytes,
+                           dev_status, stream);
+}
+
 int nslg_paged_prefill(int dtype, int batch, int num_qo_heads, int num_kv_heads, int head_dim,
                        int page_size, const void* q, int64_t q_stride, int64_t q_rows, void* out,
                        int64_t out_stride, const int32_t* qo_indptr, const int32_t* q_row_start,

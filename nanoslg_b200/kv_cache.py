@@ -695,8 +695,9 @@ class B200CacheContext(CacheContext):
         return self._attention(layer_idx, q_rot.view(B, S, hq, d))
 
     def _decode_direct(self, layer_idx, q, k, v):
-        """Decode ``attend`` straight through the C entry points (KV append, then paged
-        decode), skipping the generic wrappers' per-call checks, for the common inputs:
+        """Decode ``attend`` straight through one C call (``nslg_append_paged_decode``: KV
+        append, then paged decode), skipping the generic wrappers' per-call checks, for
+        the common inputs:
         dense CUDA q [B, 1, Hq, D] and k, v [B, 1, Hkv, D] of the pool's dtype and head
         sizes. Returns None for anything else (the caller takes the generic path)."""
         pool = self.cache.pool
@@ -720,17 +721,13 @@ class B200CacheContext(CacheContext):
                                         self.kv_last_page_len.data_ptr())
         stream = ops._stream(q)
         pkp, pvp = pool.layer_ptrs[layer_idx]
-        rc = lib.nslg_rope_kv_append(dtc, B, hkv, hkv, d, None, 0, k.data_ptr(), hkv * d,
-                                     v.data_ptr(), hkv * d, None, None, None, None, 0, ptrs[0],
-                                     pkp, pvp, P * ps, status, stream)
-        if rc:
-            raise N.NativeError("nslg_rope_kv_append", rc, lib.nslg_last_error().decode())
         out = torch.empty((B, 1, hq * d), dtype=dt, device=q.device)
-        rc = lib.nslg_paged_decode(dtc, B, hq, hkv, d, ps, q.data_ptr(), hq * d, out.data_ptr(),
-                                   hq * d, pkp, pvp, P, ptrs[1], ptrs[2], ptrs[3],
-                                   self._sm_scale, ws, wsb, status, stream)
+        rc = lib.nslg_append_paged_decode(dtc, B, hq, hkv, d, ps, q.data_ptr(), hq * d,
+                                          k.data_ptr(), hkv * d, v.data_ptr(), hkv * d, ptrs[0],
+                                          out.data_ptr(), hq * d, pkp, pvp, P, ptrs[1], ptrs[2],
+                                          ptrs[3], self._sm_scale, ws, wsb, status, stream)
         if rc:
-            raise N.NativeError("nslg_paged_decode", rc, lib.nslg_last_error().decode())
+            raise N.NativeError("nslg_append_paged_decode", rc, lib.nslg_last_error().decode())
         return out
 
     def _check_width(self, q):

@@ -93,6 +93,14 @@ def test_tp_plan_and_ipc_argument_errors_without_gpu(lib):
     # page zeroing: nothing to do is fine, bad sizes are not
     assert lib.nslg_zero_pages(None, 0, None, 1, 1, 16, None, None) == N.OK
     assert lib.nslg_zero_pages(vp(16), 2, vp(16), 1, 64, 24, None, None) == N.ERR_ARG
+    # one-call append + decode: batch 0 is a no-op, bad sizes are refused
+    dec = lambda b, ps, wl: lib.nslg_append_paged_decode(
+        N.DTYPE_BF16, b, 32, 8, 128, ps, vp(16), 4096, vp(16), 1024, vp(16), 1024, wl, vp(16),
+        4096, vp(16), vp(16), 64, vp(16), vp(16), vp(16), 0.08, vp(16), 1 << 20, None, None)
+    assert dec(0, 16, None) == N.OK
+    assert dec(-1, 16, vp(16)) == N.ERR_ARG
+    assert dec(4, 16, None) == N.ERR_ARG
+    assert dec(4, 0, vp(16)) == N.ERR_ARG
     # greedy argmax: shapes, dtype and pointers are checked before any launch
     assert lib.nslg_argmax_rows(N.DTYPE_BF16, 0, 10, None, 10, 0, None, None, None) == N.OK
     assert lib.nslg_argmax_rows(7, 1, 10, vp(16), 10, 0, None, vp(16), None) == N.ERR_ARG
