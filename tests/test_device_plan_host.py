@@ -132,3 +132,24 @@ def test_cached_decode_batches_match_host_plan(page_size):
             assert {s: st.num_tokens for s, st in m.seqs.items()} == \
                    {s: st.num_tokens for s, st in mgrs[0].seqs.items()}
     assert hits["cached"] > 40
+
+
+def test_device_planned_context_builds_its_lists_lazily():
+    """A device-planned decode context keeps its start positions as an array and builds
+    start_positions / seq_lens / max_kv_len (and the plan views) on first use; unknown
+    attributes still raise AttributeError."""
+    m = _managers(16, 512)[0]
+    for sid, n in (("a", 40), ("b", 16), ("c", 3)):
+        m.allocate_sequence(sid, None, num_tokens=n)
+        m.seqs[sid].num_tokens = n
+    ctx = m.begin_forward(["a", "b", "c"], [1, 1, 1])
+    assert "start_positions" not in ctx.__dict__
+    assert ctx.get_start_pos(1) == 16
+    assert ctx.start_positions == [40, 16, 3]
+    assert ctx.seq_lens == [41, 17, 4] and ctx.max_kv_len == 41
+    assert not hasattr(ctx, "no_such_attribute")
+    m.end_forward(ctx)
+    ctx2 = m.begin_forward(["a", "b", "c"], [1, 1, 1])       # the cached batch
+    assert ctx2.start_positions == [41, 17, 4]
+    assert ctx.start_positions == [40, 16, 3]                # the old context is unchanged
+    m.end_forward(ctx2)
