@@ -154,9 +154,12 @@ __global__ void __launch_bounds__(256) zero_pages_kernel(const int32_t* pages, i
 // itself; it applies the table updates of its own row, then writes its fields and
 // gathers its page ids); blocks from `batch` on zero the new pages (page i, layer l,
 // pool k or v). Saves the scan launch and the separate zeroing launch of the two-kernel
-// path; each block reads the start positions of the sequences before it, so it is used
-// up to kFusedMaxBatch sequences.
+// path; each block reads the start positions of the sequences before it and the whole
+// update list, so it is used up to kFusedMaxBatch sequences and kFusedMaxUpdates table
+// changes (the steady state of a decode batch: a few new pages per step). The first step
+// of a batch, which uploads whole tables, takes the two-kernel path.
 constexpr int kFusedMaxBatch = 128;
+constexpr int kFusedMaxUpdates = 256;   // every block scans the update list
 constexpr int kFusedThreads = 128;
 
 struct ZeroParams {
@@ -389,7 +392,8 @@ extern "C" int nslg_plan_decode_host(int batch, int page_size, const int32_t* sl
                plan + B, plan + 2 * B, plan + 3 * B + 1, plan + 4 * B + 1, plan + 5 * B + 2,
                plan + 6 * B + 2, max_indices, dev_status};
   const int64_t zero_blocks = static_cast<int64_t>(num_zero) * layers * 2;
-  if (batch <= kFusedMaxBatch && zero_blocks < (int64_t{1} << 24)) {
+  if (batch <= kFusedMaxBatch && num_updates <= kFusedMaxUpdates &&
+      zero_blocks < (int64_t{1} << 24)) {
     ZeroParams z{d + 2 * batch + 3 * num_updates, num_zero, static_cast<int>(layers),
                  static_cast<uint8_t*>(pool_k), static_cast<uint8_t*>(pool_v), num_pages,
                  num_pages * page_bytes, page_bytes};
