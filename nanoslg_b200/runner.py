@@ -127,9 +127,9 @@ class LlamaRunner:
 
     def enable_cuda_graphs(self, batches):
         """Decode steps of these batch sizes run as one captured CUDA graph each: the plan
-        goes into a fixed device buffer (copied from pinned memory before every replay), the
-        token ids into a fixed input tensor, and the whole model forward plus argmax replays
-        without per-kernel launches from Python."""
+        goes into a fixed device buffer (built there by the device planner before every
+        replay), the token ids into a fixed input tensor, and the whole model forward plus
+        argmax replays without per-kernel launches from Python."""
         for b in batches:
             self.cache.use_static_plan(b, 1)
         self.use_graphs = True
