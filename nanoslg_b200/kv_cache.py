@@ -617,7 +617,10 @@ class B200CacheContext(CacheContext):
         npgs = (kv_lens + ps - 1) // ps
         indptr = np.zeros(B + 1, dtype=np.int32)
         indptr[1:] = np.cumsum(npgs)
-        lpl = np.where(npgs > 0, kv_lens - (npgs - 1) * ps, 0).astype(np.int32)
+        # an empty batch still gets one page id and one last-page length of 0, like the
+        # reference's `indices or [0]` / `lpl or [0]` (kv_cache.py:612-615)
+        lpl = (np.where(npgs > 0, kv_lens - (npgs - 1) * ps, 0).astype(np.int32) if B
+               else np.zeros(1, dtype=np.int32))
         total = int(indptr[B])
         indices = (np.concatenate([st.block_table.prefix(n)
                                    for st, n in zip(sts, npgs.tolist())])
@@ -630,7 +633,7 @@ class B200CacheContext(CacheContext):
 
         # one int32 buffer, page ids last so that every other view sits at an offset that
         # depends only on (B, input width): a fixed plan buffer keeps them in place
-        parts = [positions.ravel(), write_loc.ravel(), indptr, lpl[:max(B, 1)], qo, row_start,
+        parts = [positions.ravel(), write_loc.ravel(), indptr, lpl, qo, row_start,
                  indices]
         offs = np.cumsum([0] + [p.size for p in parts])
         size = int(offs[-1])

@@ -195,6 +195,49 @@ def paged_scenarios(kvc):
         scen.append({"name": f"page16_batches_prefix{int(prefix)}",
                      "setup": {"page_size": 16, "max_pages": 64, "prefix": prefix},
                      "ops": ops})
+    # 6. continuous batching (drawn last, so the scenarios above keep their draws):
+    # requests arrive while others decode, are prefilled as a batch of their own
+    # (worker-style clamp and left padding), join the decode batch, and finish at random;
+    # the pool is small enough that the tree evicts cached prefixes.
+    for ps, pages in ((4, 72), (1, 200)):
+        def ri(lo, hi):
+            return int(torch.randint(lo, hi, (1,), generator=g))
+
+        sysp = rt(3 * ps + 5, 1000)
+        ops, running, nxt = [], [], 0
+        for step in range(48):
+            if step == 0 or (len(running) < 6 and ri(0, 4) == 0):
+                new = []
+                for _ in range(ri(1, 4)):
+                    sid = f"r{nxt}"
+                    nxt += 1
+                    kind = ri(0, 3)
+                    if kind == 0:      # the shared system prompt and a question
+                        toks = sysp + rt(ri(1, 3 * ps + 2), 1000)
+                    elif kind == 1:     # a prefix of the system prompt (a whole-prompt hit)
+                        toks = sysp[:ri(1, len(sysp) + 1)]
+                    else:
+                        toks = rt(ri(2, 6 * ps + 3), 1000)
+                    ops.append(["alloc", sid, toks, 0])
+                    new.append(sid)
+                ops += [["prefill_auto", new], ["end"]]
+                running += new
+            if step == 20 and running:
+                ops.append(["extend", running[0], 2])
+            ops += [["begin", list(running), [1] * len(running), None], ["end"]]
+            for s in running:
+                ops.append(["append", s, [ri(0, 1000)]])
+            keep = []
+            for s in running:
+                if ri(0, 8) == 0:
+                    ops.append(["release", s])
+                else:
+                    keep.append(s)
+            running = keep
+        for s in running:
+            ops.append(["release", s])
+        scen.append({"name": f"continuous_batching_page{ps}",
+                     "setup": {"page_size": ps, "max_pages": pages}, "ops": ops})
     return scen
 
 
@@ -377,6 +420,8 @@ def tiny_llama(kvc, M, ParallelContext, ParallelConfig, ParallelMode):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of Guney-olu/nanoslg")
+    ap.add_argument("--only-paged", action="store_true",
+                    help="write paged_scenarios.json only")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import nanoslg.kv_cache as kvc
@@ -390,6 +435,8 @@ def main():
         s["records"] = run_paged_script(kvc, s["setup"], s["ops"])
     with open(os.path.join(HERE, "paged_scenarios.json"), "w") as f:
         json.dump(scen, f)
+    if args.only_paged:
+        return
     torch.save(attention_cases(kvc), os.path.join(HERE, "attention_cases.pt"))
     torch.save(rope_norm_cases(M), os.path.join(HERE, "rope_norm.pt"))
     tl = tiny_llama(kvc, M, ParallelContext, ParallelConfig, ParallelMode)

@@ -153,3 +153,89 @@ def test_device_planned_context_builds_its_lists_lazily():
     assert ctx2.start_positions == [41, 17, 4]
     assert ctx.start_positions == [40, 16, 3]                # the old context is unchanged
     m.end_forward(ctx2)
+
+
+def _golden_scenarios():
+    import json
+    import os
+    from conftest import GOLDEN
+    with open(os.path.join(GOLDEN, "paged_scenarios.json")) as f:
+        return json.load(f)
+
+
+_SCEN = _golden_scenarios()
+
+
+@pytest.mark.parametrize("sc", _SCEN, ids=[s["name"] for s in _SCEN])
+def test_device_planned_manager_replays_reference_scenarios(sc):
+    """Every golden scenario (recorded from the reference's FlashInferPagedKVCache) replayed
+    on a device-planning manager: the state after each op is the reference's, and on the
+    decode steps the device plans, the CSR and write targets that follow from what was
+    sent (the mirrored table rows and the start positions) are the reference's."""
+    from oracle import paged_plan
+    setup = dict(sc["setup"])
+    ps = setup["page_size"]
+    cfg = KVCacheConfig(num_layers=1, num_kv_heads=1, num_qo_heads=1, head_dim=16,
+                        page_size=ps, max_pages=setup["max_pages"], dtype=torch.float32,
+                        device=torch.device("cpu"),
+                        enable_prefix_caching=setup.get("prefix", True))
+    m = B200PagedKVCache(cfg)
+    m.device_plan = True
+    m._mirror = _Mirror(m)
+    m._launch_device_plan = m._mirror
+    ctx, device_steps = None, 0
+    for i, rec in enumerate(sc["records"]):
+        op = rec["op"]
+        kind = op[0]
+        err = None
+        try:
+            if kind == "alloc":
+                assert m.allocate_sequence(op[1], op[2], op[3]) == rec["ret"], i
+            elif kind == "extend":
+                m.extend_sequence(op[1], op[2])
+            elif kind == "begin":
+                ctx = m.begin_forward(op[1], op[2], op[3])
+                assert ctx.start_positions == rec["start_positions"], i
+                assert ctx.seq_lens == rec["seq_lens"], i
+                assert ctx._is_decode == rec["is_decode"], i
+                if getattr(ctx, "_dc", None) is not None:
+                    device_steps += 1
+                    slots, starts = m._mirror.last
+                    assert starts == rec["start_positions"], i
+                    tables = []
+                    for slot, n0 in zip(slots, starts):
+                        row = m._mirror.rows.get(slot, {})
+                        tables.append([row.get(j) for j in range(n0 // ps + 1)])
+                    ind, idx, lpl = paged_plan.csr(tables, rec["seq_lens"], ps)
+                    assert (ind, idx, lpl) == (rec["indptr"], rec["indices"],
+                                               rec["last_page_len"]), i
+                    wi = paged_plan.write_targets(tables, starts, [1] * len(starts), ps)
+                    assert [[list(x) for x in w] for w in wi] == rec["write_info"], i
+                else:
+                    assert [[list(x) for x in w] for w in ctx._write_info] == \
+                        rec["write_info"], i
+                    assert ctx.kv_indptr.tolist() == rec["indptr"], i
+                    assert ctx.kv_indices.tolist() == rec["indices"], i
+                    assert ctx.kv_last_page_len.tolist() == rec["last_page_len"], i
+            elif kind == "end":
+                m.end_forward(ctx)
+            elif kind == "release":
+                m.release_sequence(op[1])
+            elif kind == "append":
+                m.append_token_ids(op[1], op[2])
+            elif kind == "rewind":
+                m.seqs[op[1]].num_tokens = op[2]
+            elif kind == "reset":
+                m.reset()
+        except RuntimeError as e:
+            err = str(e)
+        assert (err is None) == ("error" not in rec), (i, err)
+        st = rec["state"]
+        assert {s: list(x.block_table) for s, x in sorted(m.seqs.items())} == \
+            st["block_tables"], i
+        assert {s: x.num_tokens for s, x in sorted(m.seqs.items())} == st["num_tokens"], i
+        assert m.pool.num_free == st["num_free"], i
+        assert list(m.pool.ref_count) == st["ref_count"], i
+        assert list(m.pool.tokens_used) == st["tokens_used"], i
+    n_dec = sum(1 for r in sc["records"] if r["op"][0] == "begin" and r["is_decode"])
+    assert n_dec == 0 or device_steps > 0
