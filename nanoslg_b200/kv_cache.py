@@ -452,8 +452,10 @@ class _PagedSeqState:
 class _DecodeBatch:
     """A decode batch planned on the device, kept for the next step of the same batch:
     its sequence states, table rows, token counts before the step, the page holding each
-    sequence's next position, and the longest block table."""
-    __slots__ = ("ids", "mut", "ver", "sts", "slots", "n0", "ptrs", "cur_pid", "longest")
+    sequence's next position, and the longest block table; ``open`` is the context of
+    its step begun and not yet ended."""
+    __slots__ = ("ids", "mut", "ver", "sts", "slots", "n0", "ptrs", "cur_pid", "longest",
+                 "open")
 
 
 class B200CacheContext(CacheContext):
@@ -967,6 +969,7 @@ class B200PagedKVCache(KVCacheManager):
         ctx._sm_scale = 1.0 / math.sqrt(self.cfg.head_dim)
         ctx._pos64 = None
         ctx._dc = c
+        c.open = ctx
         return ctx
 
     def _host_scratch(self, n):
@@ -1115,8 +1118,11 @@ class B200PagedKVCache(KVCacheManager):
 
     def end_forward(self, ctx):
         c = getattr(ctx, "_dc", None)
-        if c is not None and c is self._dc:
-            # a step of the cached decode batch: one token each, cache kept in step
+        if c is not None and c is self._dc and c.open is ctx:
+            # the open step of the cached decode batch: one token each, cache kept in
+            # step (any other context, e.g. one ended twice, takes the general path,
+            # which drops the cache)
+            c.open = None
             for st in c.sts:
                 st._n += 1
             c.n0 += 1

@@ -239,3 +239,29 @@ def test_device_planned_manager_replays_reference_scenarios(sc):
         assert list(m.pool.tokens_used) == st["tokens_used"], i
     n_dec = sum(1 for r in sc["records"] if r["op"][0] == "begin" and r["is_decode"])
     assert n_dec == 0 or device_steps > 0
+
+
+def test_context_ended_twice_drops_the_cached_batch():
+    """Ending a decode context a second time (after the next begin ran out of pages)
+    advances the token counts like the reference's end_forward does; the cached batch
+    must not take that step for its own, or the next begin would skip the page the
+    reference allocates (and fails to allocate) there."""
+    mgrs = _managers(4, 3)                 # pages 1 and 2 only
+    outcomes = []
+    for m in mgrs:
+        m.allocate_sequence("a", [1, 2, 3])
+        m.allocate_sequence("b", [4, 5, 6, 7])
+        m.end_forward(m.begin_forward(["a", "b"], [3, 4], [1, 0]))
+        ctx1 = m.begin_forward(["a"], [1])           # position 3: page 1 still has room
+        m.end_forward(ctx1)
+        with pytest.raises(RuntimeError, match="KV OOM"):
+            m.begin_forward(["a"], [1])              # position 4 needs a page: none left
+        m.end_forward(ctx1)                          # the old context once more
+        assert m.seqs["a"].num_tokens == 5
+        try:
+            m.begin_forward(["a"], [1])
+            outcomes.append("ok")
+        except RuntimeError as e:
+            outcomes.append(str(e))
+    assert outcomes[0] == outcomes[2] and outcomes[1] == outcomes[2], outcomes
+    assert outcomes[2].startswith("KV OOM")
