@@ -196,6 +196,19 @@ class PagePool:
             self._pending_zero.extend(out)
             return out
 
+    def alloc_one(self) -> Optional[int]:
+        """The page ``alloc(1)`` would hand out (same free-set pop), or None when the pool
+        is empty."""
+        with self._lock:
+            fs = self.free_set
+            if not fs:
+                return None
+            pid = fs.pop()
+            self.ref_count[pid] = 1
+            self.tokens_used[pid] = 0
+            self._pending_zero.append(pid)
+            return pid
+
     def take_pending_zero(self) -> List[int]:
         """The pages allocated since the last flush (sorted, unique); the caller zeroes
         them (``nslg_plan_decode_host`` on the device-planned path, ``flush_zero``
@@ -404,7 +417,13 @@ class _BlockTable(list):
             self.dirty_from = old
 
     def append(self, page):
-        self.extend([page])
+        old = len(self)
+        if old >= self.arr.size:
+            self._reserve(old + 1, old)
+        super().append(page)
+        self.arr[old] = page
+        if old < self.dirty_from:
+            self.dirty_from = old
 
     def __setitem__(self, i, v):
         super().__setitem__(i, v)
@@ -453,9 +472,12 @@ class _DecodeBatch:
     """A decode batch planned on the device, kept for the next step of the same batch:
     its sequence states, table rows, token counts before the step, the page holding each
     sequence's next position, and the longest block table; ``open`` is the context of
-    its step begun and not yet ended."""
+    its step begun and not yet ended. Every step moves all start positions on by one, so
+    the sequences whose next position opens a page at step ``t`` (counted from when the
+    batch was built) are ``buckets[t % page_size]``, and ``total``, the number of page
+    ids in the step's plan, grows by that bucket's size."""
     __slots__ = ("ids", "mut", "ver", "sts", "slots", "n0", "ptrs", "cur_pid", "longest",
-                 "open")
+                 "open", "t", "buckets", "total")
 
 
 class B200CacheContext(CacheContext):
@@ -905,6 +927,11 @@ class B200PagedKVCache(KVCacheManager):
         c.ptrs = (c.slots.ctypes.data, c.n0.ctypes.data)
         c.cur_pid = np.asarray(pids, dtype=np.int64)
         c.longest = longest
+        c.t = 0
+        c.buckets = [[] for _ in range(ps)]
+        for i, x in enumerate(starts):
+            c.buckets[-x % ps].append(i)
+        c.total = int((st0 // ps).sum()) + B
         self._dc = c
         ctx = self._decode_context(c, seq_ids, ntoks, c.n0 % ps)
         ctx._wi_src = (pids, ctx._wi_src[1])
@@ -920,16 +947,22 @@ class B200PagedKVCache(KVCacheManager):
         n0 = c.n0
         rem = n0 % ps
         dirty = []
-        opening = np.flatnonzero(rem == 0)
-        if opening.size:
+        opening = c.buckets[c.t % ps]
+        if opening:
             rc = self.pool.ref_count
-            for i in opening.tolist():
-                st = c.sts[i]
+            alloc_one = self.pool.alloc_one
+            sts = c.sts
+            for i in opening:
+                st = sts[i]
                 bt = st.block_table
                 pi = int(n0[i]) // ps
                 nb = len(bt)
                 if pi >= nb:
-                    bt.extend(self._alloc(pi + 1 - nb))
+                    pid = alloc_one() if pi == nb else None
+                    if pid is not None:
+                        bt.append(pid)
+                    else:       # several pages, or eviction / the OOM error of _alloc
+                        bt.extend(self._alloc(pi + 1 - nb))
                     nb = len(bt)
                     if nb > c.longest:
                         c.longest = nb
@@ -1028,7 +1061,7 @@ class B200PagedKVCache(KVCacheManager):
         n0 = c.n0
         B = n0.shape[0]
         ps = self.cfg.page_size
-        total = int(((n0 + ps) // ps).sum())           # sum of ceil((start + 1) / ps)
+        total = c.total                                # sum of ceil((start + 1) / ps)
         zero = self.pool.take_pending_zero()           # pages allocated since the last forward
         nz = len(zero)
         if nz:
@@ -1097,7 +1130,7 @@ class B200PagedKVCache(KVCacheManager):
                      else all(n == 1 for n in ntoks))):
             c = self._dc
             if (c is not None and c.mut == self._mut and c.ver == _PagedSeqState.version
-                    and c.ids == list(seq_ids)):
+                    and c.ids == (seq_ids if type(seq_ids) is list else list(seq_ids))):
                 ctx = self._begin_decode_cached(c, seq_ids, ntoks)
                 if ctx is not None:
                     return ctx
@@ -1126,6 +1159,8 @@ class B200PagedKVCache(KVCacheManager):
             for st in c.sts:
                 st._n += 1
             c.n0 += 1
+            c.t += 1
+            c.total += len(c.buckets[c.t % self.cfg.page_size])
             return
         self._mut += 1
         for b in range(ctx.batch_size):

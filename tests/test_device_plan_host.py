@@ -33,6 +33,9 @@ class _Mirror:
             for s, j, pg in self.mgr._hs[:3 * nu].reshape(nu, 3).tolist():
                 self.rows.setdefault(s, {})[j] = pg
         self.mgr.pool.take_pending_zero()
+        ps = self.mgr.cfg.page_size
+        # the page-id count kept by the batch is the one the plan is sized with
+        assert c.total == int(((c.n0.astype(np.int64) + ps) // ps).sum())
         self.last = (c.slots.tolist(), c.n0.tolist())
         ctx.plan_static = False
 
