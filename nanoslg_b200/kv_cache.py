@@ -428,14 +428,57 @@ class _BlockTable(list):
     def __setitem__(self, i, v):
         super().__setitem__(i, v)
         if isinstance(i, slice):
-            self._reserve(len(self), 0)
-            self.arr[:len(self)] = np.asarray(self, dtype=np.int32)
-            self.dirty_from = 0
+            self._resync()
         else:
             j = i if i >= 0 else i + len(self)
             self.arr[j] = v
             if j < self.dirty_from:
                 self.dirty_from = j
+
+    def _resync(self):
+        """Mirror rebuilt from the list, every entry marked for upload (after the list
+        operations the bookkeeping never uses on a block table)."""
+        self._reserve(len(self), 0)
+        self.arr[:len(self)] = np.asarray(self, dtype=np.int32)
+        self.dirty_from = 0
+
+    def __iadd__(self, pages):
+        self.extend(pages)
+        return self
+
+    def __imul__(self, n):
+        super().__imul__(n)
+        self._resync()
+        return self
+
+    def __delitem__(self, i):
+        super().__delitem__(i)
+        self._resync()
+
+    def insert(self, i, page):
+        super().insert(i, page)
+        self._resync()
+
+    def pop(self, i=-1):
+        page = super().pop(i)
+        self._resync()
+        return page
+
+    def remove(self, page):
+        super().remove(page)
+        self._resync()
+
+    def clear(self):
+        super().clear()
+        self._resync()
+
+    def sort(self, *args, **kw):
+        super().sort(*args, **kw)
+        self._resync()
+
+    def reverse(self):
+        super().reverse()
+        self._resync()
 
     def prefix(self, n):
         """int32 array of the first n page ids, 0 (the null page) past the end."""

@@ -268,3 +268,62 @@ def test_context_ended_twice_drops_the_cached_batch():
             outcomes.append(str(e))
     assert outcomes[0] == outcomes[2] and outcomes[1] == outcomes[2], outcomes
     assert outcomes[2].startswith("KV OOM")
+
+
+def test_block_table_mirror_follows_every_list_operation():
+    """The int32 mirror of a block table equals the list after any list operation, and
+    the entries marked for upload cover every entry that changed."""
+    from nanoslg_b200.kv_cache import _BlockTable
+    rng = random.Random(5)
+    bt = _BlockTable([3, 1, 4])
+    shadow = [3, 1, 4]
+    uploaded = list(shadow)          # what the device copy holds
+
+    def upload():
+        nonlocal uploaded
+        d = bt.dirty_from
+        uploaded = uploaded[:d] + list(bt)[d:]
+        bt.dirty_from = len(bt)
+
+    upload()
+    for step in range(400):
+        op = rng.randrange(12)
+        if op == 0:
+            x = [rng.randrange(100) for _ in range(rng.randrange(0, 40))]
+            bt.extend(x); shadow.extend(x)
+        elif op == 1:
+            x = rng.randrange(100)
+            bt.append(x); shadow.append(x)
+        elif op == 2 and shadow:
+            i = rng.randrange(-len(shadow), len(shadow)); x = rng.randrange(100)
+            bt[i] = x; shadow[i] = x
+        elif op == 3 and shadow:
+            i = rng.randrange(len(shadow)); j = rng.randrange(i, len(shadow) + 1)
+            x = [rng.randrange(100) for _ in range(rng.randrange(0, 5))]
+            bt[i:j] = x; shadow[i:j] = x
+        elif op == 4:
+            x = [rng.randrange(100) for _ in range(rng.randrange(0, 5))]
+            bt += x; shadow += x
+        elif op == 5 and shadow:
+            i = rng.randrange(len(shadow))
+            assert bt.pop(i) == shadow.pop(i)
+        elif op == 6:
+            i = rng.randrange(len(shadow) + 1); x = rng.randrange(100)
+            bt.insert(i, x); shadow.insert(i, x)
+        elif op == 7 and shadow:
+            x = rng.choice(shadow)
+            bt.remove(x); shadow.remove(x)
+        elif op == 8 and shadow:
+            i = rng.randrange(len(shadow))
+            del bt[i:]; del shadow[i:]
+        elif op == 9:
+            bt.sort(); shadow.sort()
+        elif op == 10:
+            bt.reverse(); shadow.reverse()
+        elif op == 11 and rng.random() < 0.05:
+            bt.clear(); shadow.clear()
+        assert list(bt) == shadow
+        assert bt.arr[:len(bt)].tolist() == shadow
+        if rng.random() < 0.5:
+            upload()
+            assert uploaded[:len(shadow)] == shadow
