@@ -2,7 +2,6 @@
 outputs (tests/golden): contiguous-SDPA attention cases and the tiny fp32 Llama's greedy
 tokens."""
 import json
-import math
 import os
 from types import SimpleNamespace
 

@@ -5,7 +5,6 @@ rank runs the same bookkeeping on the same token ids, so attention needs no exch
 import os
 import socket
 
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
