@@ -126,3 +126,47 @@ def test_tp_plan_and_ipc_argument_errors_without_gpu(lib):
     ptr = vp()
     assert lib.nslg_ipc_alloc(0, ctypes.byref(ptr), ctypes.create_string_buffer(64)) == N.ERR_ARG
     assert lib.nslg_ipc_open(None, ctypes.byref(ptr)) == N.ERR_ARG
+
+
+C_HOST = r"""
+#include <stdio.h>
+#include <string.h>
+#include "nslg_b200.h"
+
+/* A C99 host bound to the library the way another language's FFI would be: version,
+ * host-side argument checks and the error text, no GPU needed. */
+int main(void) {
+  const char* v = nslg_version();
+  if (v == NULL || strstr(v, "sm_100a") == NULL) return 2;
+  int rc = nslg_rmsnorm_residual(7, 1, 16, NULL, 0, NULL, 0, NULL, NULL, 0, 1e-5f, NULL);
+  if (rc != NSLG_ERR_ARG || strstr(nslg_last_error(), "dtype") == NULL) return 3;
+  rc = nslg_paged_decode(NSLG_DTYPE_BF16, 2, 6, 4, 128, 16, NULL, 0, NULL, 0, NULL, NULL, 1,
+                         NULL, NULL, NULL, 1.0f, NULL, 0, NULL, NULL);
+  if (rc != NSLG_ERR_ARG || strstr(nslg_last_error(), "num_kv_heads") == NULL) return 4;
+  rc = nslg_paged_decode(NSLG_DTYPE_BF16, 0, 32, 8, 128, 16, NULL, 0, NULL, 0, NULL, NULL, 1,
+                         NULL, NULL, NULL, 1.0f, NULL, 0, NULL, NULL);
+  if (rc != NSLG_OK) return 5;
+  printf("c host ok: %s\n", v);
+  return 0;
+}
+"""
+
+
+def test_c_host_compiles_links_and_calls_the_abi(lib, tmp_path):
+    """include/nslg_b200.h is plain C99 and the shared library links into a C program,
+    whose calls behave as through ctypes."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    libdir = os.path.join(ROOT, "nanoslg_b200", "lib")
+    exe = tmp_path / "host"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                    "-I", os.path.join(ROOT, "include"), str(src), "-L", libdir, "-lnslg_b200",
+                    "-Wl,-rpath," + libdir, "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    assert "c host ok" in r.stdout and "sm_100a" in r.stdout
