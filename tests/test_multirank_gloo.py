@@ -1,10 +1,13 @@
-"""N > 1 host logic on CPU with two gloo ranks: the TP linear layers and collectives of
+"""N > 1 host logic on CPU with gloo ranks: the TP linear layers and collectives of
 nanoslg_b200.tp_layers / parallel (Megatron column/row split, SUM all-reduce, LM-head
-all-gather) against one unsplit layer, and identical page tables on every TP rank (each
-rank runs the same bookkeeping on the same token ids, so attention needs no exchange)."""
+all-gather) against one unsplit layer, identical page tables on every TP rank (each
+rank runs the same bookkeeping on the same token ids, so attention needs no exchange),
+and the pipeline micro-batch schedule of LlamaRunner.decode_microbatched over 2 and 3
+stages."""
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -70,3 +73,91 @@ def test_two_rank_tp_layers_and_bookkeeping():
     for rank, (ok_col, ok_row, same, wc, wr) in res.items():
         assert ok_col and ok_row and same, (rank, res[rank])
         assert wc == (4, 16) and wr == (16, 4)
+
+
+def _pp_worker(rank, world, port, num_micro, steps, out):
+    """One pipeline stage per rank (TP 1): LlamaRunner.decode_microbatched's tick schedule
+    and neighbour exchange, with the stage forward replaced by a known function."""
+    import datetime
+    import types
+    from types import SimpleNamespace
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from nanoslg_b200.runner import LlamaRunner
+        P, p, H, B = world, rank, 4, 2 * num_micro
+
+        class _Cache:
+            def __init__(self):
+                self.begun = []
+
+            def begin_forward(self, sids, counts, offsets=None):
+                assert counts == [1] * len(sids)
+                self.begun.append(tuple(sids))
+                return tuple(sids)
+
+            def end_forward(self, ctx):
+                assert self.begun and self.begun[-1] == ctx
+
+        def stage(self, x, ctx, mb):
+            # stage p adds p + 1 to the hidden state; the first embeds the token as a
+            # constant row, the last turns the row back into a token
+            h = x.float().view(mb, 1, 1).expand(mb, 1, H) if p == 0 else x
+            h = h + (p + 1)
+            if p == P - 1:
+                return (h[:, 0, 0].long() * 3 + 1) % 997
+            return h.contiguous()
+
+        r = object.__new__(LlamaRunner)
+        r.pctx = SimpleNamespace(pp_rank=p, tp_rank=0, get_pp_next_rank=lambda: p + 1,
+                                 get_pp_prev_rank=lambda: p - 1)
+        r.pcfg = SimpleNamespace(pp_size=P, tp_size=1)
+        r.seq_ids = [f"s{i}" for i in range(B)]
+        r.hf = SimpleNamespace(hidden_size=H)
+        r.dtype = torch.float32
+        r.device = torch.device("cpu")
+        r.cache = _Cache()
+        r._stage_decode_forward = types.MethodType(stage, r)
+        tokens = torch.arange(B, dtype=torch.long) * 11 + 5
+        got = r.decode_microbatched(tokens, num_micro, steps)
+        out[rank] = (None if got is None else got.tolist(), len(r.cache.begun))
+    finally:
+        dist.destroy_process_group()
+
+
+def _lock_step(tokens, P, steps):
+    shift = P * (P + 1) // 2
+    rows = []
+    for t in tokens:
+        seq = []
+        for _ in range(steps):
+            t = ((t + shift) * 3 + 1) % 997
+            seq.append(t)
+        rows.append(seq)
+    return rows
+
+
+
+@pytest.mark.parametrize("world,num_micro", [(2, 2), (3, 3), (3, 4)])
+def test_pp_microbatch_schedule_matches_lock_step(world, num_micro):
+    """Micro-batches flowing through 2-3 gloo stages give every sequence the tokens of
+    running the stages in lock step, on the first and the last stage; every stage runs
+    steps x num_micro micro-batch forwards."""
+    steps = 3
+    port = _free_port()
+    with mp.get_context("spawn").Manager() as m:
+        out = m.dict()
+        mp.start_processes(_pp_worker, args=(world, port, num_micro, steps, out), nprocs=world,
+                           start_method="spawn", join=True)
+        res = dict(out)
+    B = 2 * num_micro
+    want = _lock_step([i * 11 + 5 for i in range(B)], world, steps)
+    assert set(res) == set(range(world))
+    for rank, (got, nfwd) in res.items():
+        assert nfwd == steps * num_micro, rank
+        if rank in (0, world - 1):
+            assert got == want, rank
+        else:
+            assert got is None
