@@ -60,6 +60,17 @@ def test_ops_refuse_cpu_tensors(lib):
         ops.rmsnorm_residual(x, torch.ones(16), 1e-5)
 
 
+def test_ops_refuse_unsupported_dtypes():
+    """bf16 and fp32 only: fp16 (and anything else) is refused, never converted."""
+    import torch
+    from nanoslg_b200 import ops
+    assert ops._dtype_code(torch.zeros(1, dtype=torch.bfloat16)) == N.DTYPE_BF16
+    assert ops._dtype_code(torch.zeros(1, dtype=torch.float32)) == N.DTYPE_F32
+    for dt in (torch.float16, torch.float64, torch.int32):
+        with pytest.raises(TypeError, match="bfloat16 and float32"):
+            ops._dtype_code(torch.zeros(1, dtype=dt))
+
+
 def test_tp_plan_and_ipc_argument_errors_without_gpu(lib):
     """The tensor-parallel reduction, the decode planner, page zeroing and the IPC helpers
     reject bad arguments on the host, before any CUDA call."""
