@@ -632,48 +632,126 @@ class B200CacheContext(CacheContext):
     def _write_info(self) -> List[List[Tuple[int, int]]]:
         """(page, slot) of every new token of every sequence (kv_cache.py:575-594)."""
         if self._wi is None:
-            pids, slots = self._wi_src
-            self._wi = [[(int(p_), int(s_))] for p_, s_ in zip(pids, slots)]
+            if self._wi_src is not None:           # a decode step: one token each
+                pids, slots = self._wi_src
+                self._wi = [[(int(p_), int(s_))] for p_, s_ in zip(pids, slots)]
+            else:                                  # the general path's array part
+                wi, fast, pids, slots, beg = self._wi_parts
+                pl, sl = pids.tolist(), slots.tolist()
+                for j, b in enumerate(fast):
+                    wi[b] = list(zip(pl[beg[j]:beg[j + 1]], sl[beg[j]:beg[j + 1]]))
+                self._wi = wi
         return self._wi
 
     def _general_write_targets(self, sts, new_token_counts, iw, ps):
-        # write targets with copy-on-write, page by page in the reference's order
-        # (kv_cache.py:575-594: the first token written into a shared page copies it)
+        """Write targets of any forward, with copy-on-write (kv_cache.py:575-594).
+
+        A sequence whose new tokens land in pages shared with another owner goes through
+        the reference's page-by-page order (the first token written into a shared page
+        copies it); all other sequences -- every sequence of a prefill into fresh pages
+        -- are computed together as arrays. Copy-on-write only allocates new private
+        pages and drops references to shared ones, so a sequence found to write private
+        pages only still does after the copies of the sequences before it."""
         B = self.batch_size
         pool = self.cache.pool
+        rc = pool.ref_count
         positions = np.zeros((B, iw), dtype=np.int32)
         write_loc = np.full((B, iw), -1, dtype=np.int32)
-        self._wi = []
+        wi: List = [None] * B
+        fast = []
+        distinct = len(set(self.seq_ids)) == B
         for b in range(B):
             st = sts[b]
             n = new_token_counts[b]
-            o = self.input_offsets[b]
+            if n <= 0:
+                wi[b] = []
+                continue
             start = st.num_tokens
-            info: List[Tuple[int, int]] = []
-            if n > 0:
-                positions[b, o:o + n] = np.arange(start, start + n, dtype=np.int32)
-                ap = start
-                end = start + n
-                while ap < end:
-                    pi = ap // ps
-                    stop = min(end, (pi + 1) * ps)
-                    if pi >= len(st.block_table):
-                        info.extend([(0, 0)] * (stop - ap))
-                    else:
-                        pid = st.block_table[pi]
-                        if pool.is_shared(pid):
-                            np_ = pool.cow(pid)
-                            if np_ is None:
-                                raise RuntimeError("KV OOM during CoW")
-                            st.block_table[pi] = np_
-                            pool.release(pid)
-                            pid = np_
-                        info.extend((pid, sl) for sl in range(ap % ps, stop - pi * ps))
-                        pool.tokens_used[pid] = max(pool.tokens_used[pid], stop - pi * ps)
-                    ap = stop
-                write_loc[b, o:o + n] = [p_ * ps + s_ for p_, s_ in info]
-            self._wi.append(info)
+            p0, p1 = start // ps, (start + n - 1) // ps
+            bt = st.block_table
+            if distinct and p1 < len(bt) and max(map(rc.__getitem__, bt[p0:p1 + 1])) <= 1:
+                fast.append(b)
+                continue
+            try:
+                wi[b] = self._write_targets_in_order(st, n, self.input_offsets[b],
+                                                     positions[b], write_loc[b], ps)
+            except RuntimeError:
+                # out of pages for a copy: the sequences before this one have marked
+                # their pages (tokens_used), as in the reference's token loop
+                if fast:
+                    self._private_targets(fast, sts, new_token_counts, iw, ps, positions,
+                                          write_loc)
+                raise
+        if not fast:
+            self._wi = wi
+            return positions, write_loc
+        pids, slots, beg = self._private_targets(fast, sts, new_token_counts, iw, ps,
+                                                 positions, write_loc)
+        self._wi = None
+        self._wi_parts = (wi, fast, pids, slots, beg)
         return positions, write_loc
+
+    def _private_targets(self, fast, sts, new_token_counts, iw, ps, positions, write_loc):
+        """Write targets of the sequences ``fast``, which write only private pages, in
+        position order, as arrays: fills their cells of positions / write_loc, raises
+        tokens_used of their pages, returns (page ids, slots, per-sequence bounds)."""
+        fb = np.asarray(fast, dtype=np.int64)
+        n = np.asarray([new_token_counts[b] for b in fast], dtype=np.int64)
+        start = np.asarray([sts[b].num_tokens for b in fast], dtype=np.int64)
+        off = np.asarray([self.input_offsets[b] for b in fast], dtype=np.int64)
+        beg = np.zeros(len(fast) + 1, dtype=np.int64)
+        np.cumsum(n, out=beg[1:])
+        seq = np.repeat(np.arange(len(fast)), n)
+        i = np.arange(int(beg[-1]), dtype=np.int64) - beg[seq]
+        pos = start[seq] + i
+        tabs = [sts[b].block_table for b in fast]
+        tbase = np.zeros(len(fast) + 1, dtype=np.int64)
+        np.cumsum([len(t) for t in tabs], out=tbase[1:])
+        flat = np.concatenate([t.arr[:len(t)] for t in tabs])
+        pids = flat[tbase[seq] + pos // ps].astype(np.int64)
+        slots = pos % ps
+        cells = fb[seq] * iw + off[seq] + i
+        positions.reshape(-1)[cells] = pos
+        write_loc.reshape(-1)[cells] = pids * ps + slots
+        # tokens_used: the last token written into each page has its highest slot (a
+        # private page belongs to one sequence, whose tokens arrive in order)
+        last = np.empty(pids.shape[0], dtype=bool)
+        last[:-1] = pids[1:] != pids[:-1]
+        last[-1] = True
+        tu = self.cache.pool.tokens_used
+        lp = pids[last]
+        tu[lp] = np.maximum(tu[lp], slots[last] + 1)
+        return pids, slots, beg
+
+    def _write_targets_in_order(self, st, n, o, pos_row, loc_row, ps):
+        """One sequence's write targets page by page in the reference's order, copying
+        each shared page it writes into; fills its rows of positions / write_loc and
+        returns its (page, slot) list."""
+        pool = self.cache.pool
+        start = st.num_tokens
+        info: List[Tuple[int, int]] = []
+        pos_row[o:o + n] = np.arange(start, start + n, dtype=np.int32)
+        ap = start
+        end = start + n
+        while ap < end:
+            pi = ap // ps
+            stop = min(end, (pi + 1) * ps)
+            if pi >= len(st.block_table):
+                info.extend([(0, 0)] * (stop - ap))
+            else:
+                pid = st.block_table[pi]
+                if pool.is_shared(pid):
+                    np_ = pool.cow(pid)
+                    if np_ is None:
+                        raise RuntimeError("KV OOM during CoW")
+                    st.block_table[pi] = np_
+                    pool.release(pid)
+                    pid = np_
+                info.extend((pid, sl) for sl in range(ap % ps, stop - pi * ps))
+                pool.tokens_used[pid] = max(pool.tokens_used[pid], stop - pi * ps)
+            ap = stop
+        loc_row[o:o + n] = [p_ * ps + s_ for p_, s_ in info]
+        return info
 
     def _finish_plan(self, B, iw, ps, sts, positions, write_loc, new_token_counts, dev):
         cache = self.cache
