@@ -238,6 +238,17 @@ def paged_scenarios(kvc):
             ops.append(["release", s])
         scen.append({"name": f"continuous_batching_page{ps}",
                      "setup": {"page_size": ps, "max_pages": pages}, "ops": ops})
+    # 7. a batch whose second sequence must copy a shared page when no page is free: the
+    # first sequence (a private page) has already marked its page when the copy fails.
+    a_t, b_t, c_t = list(range(200, 208)), list(range(300, 305)), list(range(400, 408))
+    scen.append({"name": "cow_out_of_pages", "setup": {"page_size": 4, "max_pages": 8},
+                 "ops": [["alloc", "x", a_t, 0], ["begin", ["x"], [8], [0]], ["end"],
+                         ["release", "x"],
+                         ["alloc", "y", a_t + [1, 2], 0], ["begin", ["y"], [2], [0]], ["end"],
+                         ["alloc", "z", b_t, 0], ["begin", ["z"], [5], [0]], ["end"],
+                         ["alloc", "w", c_t, 0], ["begin", ["w"], [8], [0]], ["end"],
+                         ["rewind", "y", 6], ["begin", ["z", "y"], [1, 1], None],
+                         ["release", "y"], ["begin", ["z"], [1], None], ["end"]]})
     return scen
 
 
