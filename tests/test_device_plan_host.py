@@ -240,7 +240,7 @@ def test_device_planned_manager_replays_reference_scenarios(sc):
         assert m.pool.num_free == st["num_free"], i
         assert list(m.pool.ref_count) == st["ref_count"], i
         assert list(m.pool.tokens_used) == st["tokens_used"], i
-    n_dec = sum(1 for r in sc["records"] if r["op"][0] == "begin" and r["is_decode"])
+    n_dec = sum(1 for r in sc["records"] if r["op"][0] == "begin" and r.get("is_decode"))
     assert n_dec == 0 or device_steps > 0
 
 
