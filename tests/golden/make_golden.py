@@ -8,7 +8,8 @@ It imports the reference's own Python (``nanoslg/kv_cache.py``, ``nanoslg/models
 on CPU and records what it computes, so that the oracle restatement under ``oracle/``
 and the CUDA path can be pinned to the reference without the reference being present:
 
-* ``paged_scenarios.json``   -- page-pool / radix-tree / CSR-plan bookkeeping of
+* ``paged_scenarios.json``   -- page-pool / radix-tree / CSR-plan bookkeeping (hand-written
+  scenarios and seeded random workloads) of
   ``FlashInferPagedKVCache`` + ``FlashInferCacheContext`` (kv_cache.py:382-777) with the
   two FlashInfer wrappers replaced by recorders (their ``plan`` arguments are the CSR
   arrays ``indptr / indices / last_page_len / qo_indptr``).
@@ -252,6 +253,141 @@ def paged_scenarios(kvc):
     return scen
 
 
+def random_workloads(kvc, seeds=range(12)):
+    """Seeded random workloads over small pools (pages 1, 2, 4 and 16): requests with
+    shared, repeated or fresh prompts arrive in batches, are prefilled (worker-style clamp
+    and left padding), decode in whole or partial batches, sometimes extend by several
+    tokens at once or with mixed counts, have their cursor moved back into shared pages,
+    finish at random, and now and then the manager is reset. Operations that the
+    reference cannot run (a sequence already gone) are dropped while the script is
+    resolved against a shadow reference manager, so every recorded op is a valid call;
+    out-of-pages errors are part of the record. Some scripts also end a context a second
+    time after a begin that failed (the cached decode batch must not mistake that for
+    its own step)."""
+    import random
+    out = []
+    for seed in seeds:
+        rng = random.Random(1000 + seed)
+        ps = [1, 2, 4, 16][seed % 4]
+        pages = rng.choice([10, 16, 24]) if ps > 1 else rng.choice([30, 48])
+        ops, live, nxt, toks_of, finished = [], [], 0, {}, []
+        shared = [rng.randrange(1000) for _ in range(rng.randrange(1, 4 * ps + 3))]
+        for _ in range(rng.randrange(15, 40)):
+            if rng.random() < 0.3 or not live:
+                new = []
+                for _ in range(rng.randrange(1, 4)):
+                    sid = f"r{nxt}"
+                    nxt += 1
+                    k = rng.random()
+                    if k < 0.3:
+                        t = shared + [rng.randrange(1000) for _ in range(rng.randrange(0, 3 * ps))]
+                    elif k < 0.45 and finished:
+                        t = list(rng.choice(finished))
+                        t = t[:rng.randrange(1, len(t) + 1)]
+                    elif k < 0.55:
+                        t = shared[:rng.randrange(1, len(shared) + 1)]
+                    else:
+                        t = [rng.randrange(1000) for _ in range(rng.randrange(1, 6 * ps + 3))]
+                    ops.append(["alloc", sid, t or [1], 0])
+                    new.append(sid)
+                    toks_of[sid] = list(t or [1])
+                ops += [["prefill_auto", new], ["end"]]
+                live += new
+            if rng.random() < 0.1 and live:
+                ops.append(["extend", rng.choice(live), rng.randrange(1, 2 * ps + 2)])
+            if rng.random() < 0.05 and live:
+                ops.append(["rewind_rel", rng.choice(live), rng.randrange(1, 2 * ps + 1)])
+            if rng.random() < 0.15 and live:
+                sub = rng.sample(live, rng.randrange(1, len(live) + 1))
+                cnt = [rng.randrange(1, 3 * ps + 2) for _ in sub]
+                ops += [["begin", sub, cnt, [max(cnt) - c for c in cnt]], ["end"]]
+            batch = list(live) if rng.random() < 0.7 else rng.sample(live, rng.randrange(1, len(live) + 1))
+            ops += [["begin", batch, [1] * len(batch), None], ["end"]]
+            for sid in batch:
+                t = rng.randrange(1000)
+                ops.append(["append", sid, [t]])
+                toks_of[sid].append(t)
+            keep = []
+            for sid in live:
+                if rng.random() < 0.12:
+                    ops.append(["release", sid])
+                    finished.append(toks_of[sid])
+                else:
+                    keep.append(sid)
+            live = keep
+            if rng.random() < 0.02:
+                ops.append(["reset"])
+                live = []
+        ops += [["release", sid] for sid in live]
+        setup = {"page_size": ps, "max_pages": pages}
+        out.append({"name": f"random_{seed}_page{ps}", "setup": setup,
+                    "ops": _resolve_random(kvc, setup, ops, stale_end=seed % 3 == 2)})
+    return out
+
+
+def _resolve_random(kvc, setup, ops, stale_end):
+    """Turns a random script into valid reference calls (see random_workloads)."""
+    mgr = _make_paged(kvc, **setup)
+    out, rets, ctx, begin_ok = [], {}, None, False
+    for op in ops:
+        k = op[0]
+        if k == "prefill_auto":
+            sids = [s for s in op[1] if s in mgr.seqs]
+            if not sids:
+                continue
+            counts = []
+            for s in sids:
+                pl = len(mgr.seqs[s].token_ids)
+                counts.append(pl - (min(rets[s], pl - 1) if pl > 1 else 0))
+            op = ["begin", sids, counts, [max(counts) - c for c in counts]]
+        elif k == "rewind_rel":
+            if op[1] not in mgr.seqs:
+                continue
+            op = ["rewind", op[1], max(mgr.seqs[op[1]].num_tokens - op[2], 0)]
+        elif k == "begin":
+            keep = [(s, c, o) for s, c, o in zip(op[1], op[2], op[3] or [0] * len(op[1]))
+                    if s in mgr.seqs]
+            if not keep:
+                continue
+            if all(c == 1 for _, c, _ in keep):
+                op = ["begin", [s for s, _, _ in keep], [1] * len(keep), None]
+            else:
+                mx = max(c for _, c, _ in keep)
+                op = ["begin", [s for s, _, _ in keep], [c for _, c, _ in keep],
+                      [mx - c for _, c, _ in keep]]
+        elif k in ("extend", "append", "release") and op[1] not in mgr.seqs:
+            continue
+        elif k == "end":
+            if not out or out[-1][0] != "begin" or (not begin_ok and not stale_end):
+                continue
+            if any(s not in mgr.seqs for s in ctx.seq_ids):
+                continue
+        k = op[0]
+        try:
+            if k == "alloc":
+                rets[op[1]] = mgr.allocate_sequence(op[1], op[2], op[3])
+            elif k == "begin":
+                begin_ok = False
+                ctx = mgr.begin_forward(op[1], op[2], op[3])
+                begin_ok = True
+            elif k == "end":
+                mgr.end_forward(ctx)
+            elif k == "release":
+                mgr.release_sequence(op[1])
+            elif k == "append":
+                mgr.append_token_ids(op[1], op[2])
+            elif k == "rewind":
+                mgr.seqs[op[1]].num_tokens = op[2]
+            elif k == "extend":
+                mgr.extend_sequence(op[1], op[2])
+            elif k == "reset":
+                mgr.reset()
+        except RuntimeError:
+            pass
+        out.append(op)
+    return out
+
+
 def expand_prefill_auto(kvc, scen):
     """``prefill_auto`` mirrors worker.py:169-213: per sequence the prefix returned by
     allocate_sequence is clamped to pl-1 and the batch is left-padded.  The generator
@@ -443,6 +579,8 @@ def main():
     scen = paged_scenarios(kvc)
     for s in scen:
         s["ops"] = expand_prefill_auto(kvc, s)
+    scen += random_workloads(kvc)
+    for s in scen:
         s["records"] = run_paged_script(kvc, s["setup"], s["ops"])
     with open(os.path.join(HERE, "paged_scenarios.json"), "w") as f:
         json.dump(scen, f)
