@@ -61,8 +61,14 @@ def test_scenario_bit_exact(sc):
                 got["last_page_len"] = ctx.kv_last_page_len.tolist()
                 if not ctx._is_decode:
                     got["qo_indptr"] = ctx.qo_indptr.tolist()
-                # the position tensor handed to models (kv_cache.py:635-637)
-                assert ctx.get_position_ids(iw).dtype == torch.long
+                # the position tensor handed to models (kv_cache.py:635-637): int64,
+                # zero-padded past the input width
+                pids = ctx.get_position_ids(iw + 2)
+                assert pids.dtype == torch.long and pids.shape == (B, iw + 2)
+                assert pids[:, :iw].tolist() == rec["positions"]
+                assert not bool(pids[:, iw:].any())
+                assert ctx.get_position_ids(max(iw - 1, 0)).tolist() == \
+                    [row[:max(iw - 1, 0)] for row in rec["positions"]]
             elif kind == "end":
                 mgr.end_forward(ctx)
             elif kind == "release":
