@@ -181,3 +181,54 @@ def test_c_host_compiles_links_and_calls_the_abi(lib, tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
     assert "c host ok" in r.stdout and "sm_100a" in r.stdout
+
+
+def _header_prototypes():
+    """name -> (return type, [parameter types]) of every nslg_* prototype in include/*.h,
+    types as written (qualifiers and pointer stars kept, parameter names dropped)."""
+    out = {}
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        text = re.sub(r"^\s*#.*$", "", text, flags=re.M)
+        for m in re.finditer(r"([A-Za-z_][\w\s\*]*?)\b(nslg_\w+)\s*\(([^)]*)\)\s*;", text):
+            ret, name, params = " ".join(m.group(1).split()), m.group(2), m.group(3).strip()
+            types = []
+            if params and params != "void":
+                for prm in params.split(","):
+                    prm = " ".join(prm.split())
+                    # drop the parameter name (the last identifier not followed by '*')
+                    types.append(re.sub(r"\s*\b\w+$", "", prm).replace(" *", "*"))
+            out[name] = (ret.replace(" *", "*"), types)
+    return out
+
+
+def _ctype_of(ctype_str):
+    if ctype_str.endswith("*"):
+        return "pointer"
+    base = ctype_str.replace("const ", "")
+    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "float": ctypes.c_float,
+            "uint32_t": ctypes.c_uint32, "size_t": ctypes.c_size_t}[base]
+
+
+def test_binding_signatures_match_the_header_types():
+    """Every parameter of every prototype has the ctypes type of its C type in
+    nanoslg_b200._native.SIGNATURES (pointers as void*, char* or POINTER), in order, and
+    the return types agree: a mismatch would pass arguments in the wrong registers."""
+    protos = _header_prototypes()
+    assert set(protos) == set(N.SIGNATURES), set(protos) ^ set(N.SIGNATURES)
+    ptr_types = (ctypes.c_void_p, ctypes.c_char_p)
+    for name, (ret, params) in protos.items():
+        res, args = N.SIGNATURES[name]
+        assert len(args) == len(params), (name, len(args), len(params))
+        for i, (c, a) in enumerate(zip(params, args)):
+            want = _ctype_of(c)
+            if want == "pointer":
+                assert a in ptr_types or (isinstance(a, type) and
+                                          issubclass(a, ctypes._Pointer)), (name, i, c, a)
+            else:
+                assert a is want, (name, i, c, a)
+        want_ret = _ctype_of(ret)
+        if want_ret == "pointer":
+            assert res in ptr_types, (name, ret, res)
+        else:
+            assert res is want_ret, (name, ret, res)
