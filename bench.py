@@ -670,11 +670,12 @@ def main():
                     help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
     ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce",
-                                       "elementwise"],
+                                       "elementwise", "e2e"],
                     default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg; elementwise: the RoPE + "
-                         "KV-append and RMSNorm + residual kernels at the C3 prefill shape")
+                         "KV-append and RMSNorm + residual kernels at the C3 prefill shape; "
+                         "e2e: only the two end-to-end legs (one and two steps in flight)")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -719,6 +720,20 @@ def main():
     if not os.path.exists(nbuild.LIB):
         nbuild.build()
 
+    if a.only == "e2e":
+        steps = a.e2e_steps or max(10, a.steps // 2)
+        res = {}
+        for depth in (1, 2):
+            r = run_e2e(device, steps, a.warmup, seed=rank, depth=depth)
+            res[f"depth{depth}"] = {"ms_per_step": r["total_ms"] / steps,
+                                    "tok_s": B * steps / (r["total_ms"] / 1e3),
+                                    "h2d_bytes_per_step": r["h2d"],
+                                    "d2h_bytes_per_step": r["d2h"]}
+        if rank == 0:
+            print(json.dumps({"case": "e2e only", "steps": steps, "e2e": res}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
     if a.only == "prefill":
         if rank == 0:
             print(json.dumps({"case": "prefill only", "prefill_attention":
