@@ -22,6 +22,18 @@ the batch (64 query tokens); the metric is decode tokens/s of that pass.
 N > 1 (torchrun): every rank runs its own independent C2 batch (weak scaling, no
 collective on the data path); ``value`` is the sum over ranks of tokens / the slowest
 rank's time.
+
+Beside the headline, the same line carries, at every N:
+
+* ``parity``          -- the sharded path checked in this run: greedy tokens of a tiny
+                         fp32 Llama (8/8 heads) at TP=N and TP=N/2 x PP=2 (eager and CUDA
+                         graphs, lock step and 2 micro-batches) against tokens recorded from
+                         the reference, and the fused peer reduction bit-exact (N > 1);
+* ``llama8b_decode``  -- the Llama-3.1-8B-shaped model's decode at TP=N, batch 64 and 1,
+                         with a per-category split of a step (GEMM / attention / TP
+                         reduction / other) naming the limiter, and at N > 1 the TP=1 figure
+                         of the same batch measured on rank 0 alone (strong scaling);
+* ``cpu_baseline``    -- rank 0's host cores running the reference's attend.
 """
 import argparse
 import json
@@ -390,10 +402,12 @@ def run_elementwise_kernels(device, reps=10, batch=64, prompt=512, hidden=4096):
 
 # ------------------------------------------------------------------ model decode
 def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=None,
-                     peer_allreduce=True):
+                     peer_allreduce=True, split=False, solo=False):
     """Llama-3.1-8B-architecture decode (BASELINE config C3 at TP=1, TP=world under
     torchrun): prefill of ``prompt`` random token ids per sequence, then ``steps`` timed
-    greedy decode steps of the whole batch through the B200 path."""
+    greedy decode steps of the whole batch through the B200 path. ``split`` adds the
+    per-category split of a step (run_step_split); ``solo`` runs TP=world on this rank
+    alone, with no collective, while other ranks of a process group wait."""
     from nanoslg_b200.runner import LlamaRunner, llama_config
     hf = llama_config("llama-3.1-8b")
     if runner is None:
@@ -413,7 +427,8 @@ def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=N
     prefill_ms = (time.perf_counter() - t0) * 1e3
     for _ in range(warmup):
         tok = runner.decode_step(tok)
-    if torch.distributed.is_initialized():
+    coll = torch.distributed.is_initialized() and not solo
+    if coll:
         torch.distributed.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -423,15 +438,150 @@ def run_llama_decode(device, world, rank, batch, prompt, steps, warmup, runner=N
     e1.record()
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1)
-    if torch.distributed.is_initialized():
+    if coll:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
+    sp = run_step_split(runner, device) if split else None
     runner.release()
     roof = _decode_roofline(runner, batch, prompt + warmup + (steps + 1) / 2)
-    return runner, {"batch": batch, "prompt": prompt, "steps": steps, "ms_per_step": ms / steps,
-                    "tok_s": batch * steps / (ms / 1e3), "prefill_ms": prefill_ms,
-                    "hbm_roofline": dict(roof, frac=roof["ms_per_step"] / (ms / steps))}
+    res = {"batch": batch, "prompt": prompt, "steps": steps, "ms_per_step": ms / steps,
+           "tok_s": batch * steps / (ms / 1e3), "prefill_ms": prefill_ms,
+           "hbm_roofline": dict(roof, frac=roof["ms_per_step"] / (ms / steps))}
+    if sp is not None:
+        res["step_split"] = sp
+    return runner, res
+
+
+def run_step_split(runner, device, reps=10):
+    """Where one decode step of the current batch spends its time, by category: each
+    category's kernels for every layer, with the step's exact shapes, captured alone in a
+    CUDA graph and replayed ``reps`` times (CUDA events, max over ranks):
+
+      gemm       the cuBLAS projections (stacked q|k|v, o, stacked gate|up, down) of every
+                 layer and the LM head on the last position;
+      attention  RoPE + KV append + paged decode attention (CacheContext.attend_rope) of
+                 every layer on the step's own plan;
+      tp_reduce  the two residual-add + RMSNorm calls per layer, fused with the RowParallel
+                 all-reduce over peer memory at TP > 1 (NCCL all-reduce + the norm kernel
+                 when the peer path is off);
+      other      SwiGLU, the embedding gather and the greedy argmax (+ the (max, index)
+                 exchange at TP > 1).
+
+    ``step_ms`` is the whole step replayed the same way; ``limiter`` the largest category.
+    The categories are timed apart, so their sum exceeds the step only by what the step
+    overlaps (programmatic dependent launch) and is below it by launch gaps."""
+    import torch.nn.functional as F
+    from nanoslg_b200 import ops
+    model, mgr = runner.model, runner.cache
+    B = len(runner.seq_ids)
+    hf = runner.hf
+    hid = hf.hidden_size
+    dt = runner.dtype
+    ctx = mgr.begin_forward(runner.seq_ids, [1] * B)
+    if not getattr(ctx, "plan_static", False):
+        mgr.end_forward(ctx)
+        return None
+    layers = list(model.layers)
+    att0 = layers[0].self_attn
+    hq, hkv, hd = att0.n_heads_tp, att0.n_kv_heads_tp, att0.head_dim
+    x = torch.randn(B, 1, hid, device=device).to(dt)
+    qkv = torch.randn(B, 1, (hq + 2 * hkv) * hd, device=device).to(dt)
+    a = torch.randn(B, 1, hq * hd, device=device).to(dt)
+    inter = layers[0].mlp.down_proj.weight.shape[1]
+    gu = torch.randn(B, 1, 2 * inter, device=device).to(dt)
+    act = torch.randn(B, 1, inter, device=device).to(dt)
+    res = torch.randn(B, 1, hid, device=device).to(dt)
+    ids = torch.zeros(B, 1, dtype=torch.long, device=device)
+    peer = runner.peer
+    if peer is not None:
+        peer.active = peer.fits(B)
+    head = getattr(model.lm_head, "lm_head", model.lm_head)
+
+    def gemm():
+        for L in layers:
+            F.linear(x, L.self_attn._qkv)
+            F.linear(a, L.self_attn.o_proj.weight)
+            F.linear(x, L.mlp._gu)
+            F.linear(act, L.mlp.down_proj.weight)
+        F.linear(x[:, -1], head.weight)
+
+    def attention():
+        q = qkv[..., :hq * hd].view(B, 1, hq, hd)
+        k = qkv[..., hq * hd:(hq + hkv) * hd].view(B, 1, hkv, hd)
+        v = qkv[..., (hq + hkv) * hd:].view(B, 1, hkv, hd)
+        for L in layers:
+            ctx.attend_rope(L.self_attn.layer_idx, q, k, v, model.cos, model.sin)
+
+    def tp_reduce():
+        for L in layers:
+            for norm in (L.input_layernorm, L.post_attention_layernorm):
+                if peer is not None and peer.active:
+                    peer.allreduce_add_norm(x, res, norm.weight, norm.eps)
+                else:
+                    y = x
+                    if runner.pcfg.tp_size > 1:
+                        y = x.clone()
+                        torch.distributed.all_reduce(y, group=runner.pctx.tp_group)
+                    ops.rmsnorm_residual(y, norm.weight, norm.eps, residual=res)
+
+    logits = F.linear(x[:, -1], head.weight)
+    tp = runner.pcfg.tp_size
+
+    def other():
+        model.embed_tokens(ids)
+        for _ in layers:
+            ops.silu_mul(gu, out=act)
+        if tp > 1:
+            idx, val = ops.argmax_rows(logits, 0, values=True)
+            pair = torch.stack([val, idx.float()], -1)
+            allp = torch.empty((tp,) + tuple(pair.shape), dtype=pair.dtype, device=device)
+            torch.distributed.all_gather_into_tensor(allp, pair, group=runner.pctx.tp_group)
+        else:
+            ops.argmax_rows(logits)
+
+    def step():
+        model(ids, ctx, last_only=True, greedy=True)
+
+    def timed(fn):
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        if torch.distributed.is_initialized():
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / reps
+        del graph
+        if torch.distributed.is_initialized():
+            t = torch.tensor([ms], device=device, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with torch.inference_mode():
+        cats = {name: timed(fn) for name, fn in (("gemm", gemm), ("attention", attention),
+                                                ("tp_reduce", tp_reduce), ("other", other))}
+        step_ms = timed(step)
+    mgr.end_forward(ctx)
+    ops.check_device_status(device)
+    total = sum(cats.values())
+    return {"step_ms": step_ms, **{f"{k}_ms": v for k, v in cats.items()},
+            "sum_ms": total, "share": {k: v / total for k, v in cats.items()},
+            "limiter": max(cats, key=cats.get),
+            "method": "each category's kernels of every layer captured alone in a CUDA graph, "
+                      f"{reps} replays, CUDA events, max over ranks"}
 
 
 def _decode_roofline(runner, batch, avg_ctx):
@@ -614,6 +764,107 @@ def run_allreduce(device, world, rank, hidden=4096, rows_list=(1, 64, 256), call
     return {"world": world, "hidden": hidden, "dtype": "bf16", **out}
 
 
+# ------------------------------------------------------------------------ parity
+def _tokens_run(runner, prompts, steps, micro=0):
+    """Greedy tokens [B, steps] of a prefill and ``steps - 1`` decode steps (``micro``:
+    the decode steps as pipeline micro-batches). None on ranks that do not hold them."""
+    tok = runner.prefill(prompts)
+    first = tok.clone()
+    if micro:
+        gen = runner.decode_microbatched(tok, micro, steps - 1)
+        if gen is None:
+            return None
+        return torch.cat([first[:, None], gen.to(first.device)], 1).tolist()
+    toks = [first]
+    for _ in range(steps - 1):
+        tok = runner.decode_step(tok)
+        toks.append(tok.clone())
+    return torch.stack(toks, 1).tolist()
+
+
+def run_parity(device, world, rank):
+    """Correctness of the sharded path at this world size, checked inside the benchmark
+    run against fixtures recorded from the reference (tests/golden/tiny_llama_kv8.json:
+    the reference's contiguous-SDPA path on a 2-prompt batch of a tiny fp32 Llama with 8
+    query / 8 KV heads, so TP = 1, 2, 4 and 8 all divide it):
+
+    * ``tp``: TP=world, RowParallel reductions through the fused peer-memory kernel
+      (world > 1), greedy tokens through the vocab-parallel (max, index) exchange; eager
+      and with CUDA-graph decode steps;
+    * ``tp_x_pp2`` (world >= 2): TP=world/2 x PP=2 (PP=2 alone at world 2), lock-step
+      stages and the 2-micro-batch pipeline schedule;
+    * ``allreduce``: nslg_tp_allreduce_rmsnorm's new residual bit-equal to an fp32
+      rank-order sum of the ranks' bf16 partials + residual (hidden 4096; 1 and 64 rows).
+
+    Every rank takes part; ``ok`` is true only if every check held on every rank."""
+    from types import SimpleNamespace
+    from nanoslg_b200.models import reference_random_state_dict
+    from nanoslg_b200.runner import LlamaRunner
+    with open(os.path.join(ROOT, "tests", "golden", "tiny_llama_kv8.json")) as f:
+        g = json.load(f)
+    hf = SimpleNamespace(**g["config"])
+    full = reference_random_state_dict(hf)
+    want = g["tokens"]
+    steps = len(want[0])
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    checks = {}
+    layouts = [("tp", world, 1, False), ("tp_graphs", world, 1, True)]
+    if world >= 2:
+        layouts += [("tp_x_pp2", world // 2, 2, False), ("tp_x_pp2_graphs", world // 2, 2, True)]
+    for name, tp, pp, graphs in layouts:
+        # no prefix caching: the second batch of a runner must not hit the first one's
+        # pages (a full-prompt hit re-feeds the last token one position later, a
+        # reference quirk the fixture does not contain)
+        r = LlamaRunner(hf, device, dtype=torch.float32, tp_size=tp, pp_size=pp, rank=rank,
+                        max_kv_pages=64, prefix_caching=False)
+        r.load_full_state_dict(full)
+        if graphs:
+            r.enable_cuda_graphs([len(want), 1])
+        got = _tokens_run(r, g["prompts"], steps)
+        ok = got == want
+        r.release()
+        if pp > 1:
+            got_mb = _tokens_run(r, g["prompts"], steps, micro=2)
+            ok = ok and (got_mb is None or got_mb == want)
+            r.release()
+        r.close()
+        checks[name] = {"tp": tp, "pp": pp, "cuda_graphs": graphs, "ok": bool(ok)}
+    torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+    if world > 1:
+        checks["allreduce"] = _allreduce_parity(device, world, rank)
+    flags = torch.tensor([int(all(c["ok"] for c in checks.values()))], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(flags, op=torch.distributed.ReduceOp.MIN)
+    return {"ok": bool(flags.item()), "fixture": "tests/golden/tiny_llama_kv8.json "
+            "(reference contiguous SDPA, fp32, batch 2, 16 greedy tokens)", "checks": checks}
+
+
+def _allreduce_parity(device, world, rank, hidden=4096):
+    from nanoslg_b200 import ops
+    from nanoslg_b200.tp_comm import PeerAllReduce
+    bf = torch.bfloat16
+    peer = PeerAllReduce(torch.distributed.group.WORLD, rank, world, device, 64, hidden, bf)
+    ok = True
+    for it, rows in enumerate((64, 1, 64)):
+        parts = [torch.randn(rows, hidden, generator=torch.Generator().manual_seed(1000 * it + r))
+                 .to(bf) for r in range(world)]
+        gs = torch.Generator().manual_seed(99 + it)
+        res = torch.randn(rows, hidden, generator=gs).to(bf)
+        w = (1 + 0.1 * torch.randn(hidden, generator=gs)).to(bf)
+        s = parts[0].float()
+        for p in parts[1:]:
+            s = s + p.float()
+        h_want = (res.float() + s.to(bf).float()).to(bf)
+        r_dev = res.to(device)
+        peer.allreduce_add_norm(parts[rank].to(device), r_dev, w.to(device), 1e-5)
+        ok = ok and torch.equal(r_dev.cpu(), h_want)
+    ops.check_device_status(device)
+    peer.close()
+    return {"world": world, "rows": [64, 1, 64], "ok": bool(ok),
+            "check": "new residual bit-equal to bf16(bf16(fp32 rank-order sum) + residual)"}
+
+
 # ------------------------------------------------------------------------ CPU side
 def cpu_reference(max_seconds, n_calls=None, seed=0, warmup=1):
     """The reference's contiguous attend (oracle/attention.py restating
@@ -670,12 +921,13 @@ def main():
                     help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
     ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce",
-                                       "elementwise", "e2e"],
+                                       "elementwise", "e2e", "parity"],
                     default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg; elementwise: the RoPE + "
                          "KV-append and RMSNorm + residual kernels at the C3 prefill shape; "
-                         "e2e: only the two end-to-end legs (one and two steps in flight)")
+                         "e2e: only the two end-to-end legs (one and two steps in flight); "
+                         "parity: only the sharded-path token / reduction checks")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -714,11 +966,21 @@ def main():
     device = torch.device(f"cuda:{local}")
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+        # rank 0 alone runs the CPU baseline and the TP=1 reference decode while the
+        # other ranks wait in a barrier: the group timeout covers that wait
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=420),
                                              device_id=device)
     from nanoslg_b200 import build as nbuild
     if not os.path.exists(nbuild.LIB):
         nbuild.build()
+    if a.only == "parity":
+        r = run_parity(device, world, rank)
+        if rank == 0:
+            print(json.dumps({"case": "parity only", "n_gpus": world, "parity": r}), flush=True)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return 0 if r["ok"] else 1
 
     if a.only == "e2e":
         steps = a.e2e_steps or max(10, a.steps // 2)
@@ -775,6 +1037,7 @@ def main():
         if world > 1:
             torch.distributed.destroy_process_group()
         return 0
+    parity = run_parity(device, world, rank) if a.only == "all" else None
     kr = run_kernel(device, a.steps, a.warmup, seed=rank, pool_pages=a.pool_pages)
     if a.only == "kernel":
         if rank == 0:
@@ -834,17 +1097,38 @@ def main():
                          "kernel_ms_median": statistics.median(kr["per_ms"])},
             "gpu_launches": 2 * a.steps,
             "clocks": kr["clocks"]}
+    line["parity"] = parity
     line["prefill_attention"] = run_prefill_kernel(device) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
     if not a.no_model:
+        tp1 = None
+        if world > 1:
+            # the same batch-64 decode at TP=1 on rank 0 alone: the denominator of this
+            # line's TP scaling figures
+            if rank == 0:
+                run1, tp1 = run_llama_decode(device, 1, 0, 64, 512, a.model_steps, 4, solo=True)
+                run1.close()
+                del run1
+                torch.cuda.empty_cache()
+            torch.distributed.barrier()
         runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,
-                                       peer_allreduce=a.tp_reduce == "peer")
-        _, r1 = run_llama_decode(device, world, rank, 1, 512, a.model_steps, 4, runner=runner)
+                                       peer_allreduce=a.tp_reduce == "peer", split=True)
+        _, r1 = run_llama_decode(device, world, rank, 1, 512, a.model_steps, 4, runner=runner,
+                                 split=True)
         line["llama8b_decode"] = {
             "model": "Llama-3.1-8B architecture, random init N(0, 0.02), bf16 (BASELINE C3)",
             "parallelism": f"TP={world}", "batch64": r64, "batch1": r1,
             "tp_reduce": a.tp_reduce if world > 1 else None,
             "note": "greedy decode steps through models.LlamaTP + B200PagedKVCache; GEMMs "
                     "cuBLAS, attention/RoPE/append/RMSNorm the nslg kernels"}
+        if tp1 is not None:
+            line["llama8b_decode"]["tp_scaling_batch64"] = {
+                "tp1_tok_s": tp1["tok_s"], "tp1_ms_per_step": tp1["ms_per_step"],
+                "speedup_vs_tp1": r64["tok_s"] / tp1["tok_s"],
+                "efficiency_vs_tp1": r64["tok_s"] / (world * tp1["tok_s"]),
+                "note": "strong scaling (fixed batch 64); TP=1 measured on rank 0 alone in "
+                        "this run"}
         if world > 1:
             line["llama8b_c4_radix"] = {
                 "config": "BASELINE C4: TP=N, shared 1024-token prefix + unique 128-token "
@@ -852,10 +1136,12 @@ def main():
                 **run_llama_c4(device, world, rank, runner)}
         runner.close()
         del runner
-    if rank == 0 and world == 1 and not a.no_cpu:
+    if rank == 0 and not a.no_cpu:
         r = cpu_reference(a.cpu_seconds)
         line["cpu_baseline"] = {"value": r["value"], "unit": "tok/s", "cores": r["cores"],
                                 "kind": "port", "sample": r["sample"]}
+    if world > 1:
+        torch.distributed.barrier()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

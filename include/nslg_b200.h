@@ -7,8 +7,10 @@
  * void*), and returns an int status (NSLG_OK == 0).  On a non-zero status
  * nslg_last_error() returns a message for the calling thread.  Apart from
  * nslg_ipc_alloc, whose job it is, no entry point allocates device memory: scratch
- * space is passed in by the caller (see nslg_decode_workspace_bytes);
- * nslg_plan_decode_host keeps pinned host staging of its own.
+ * space is passed in by the caller (see nslg_decode_workspace_bytes), with one
+ * exception, nslg_paged_decode_noalloc, whose scratch is a fixed
+ * NSLG_NOALLOC_SCRATCH_BYTES __device__ array compiled into the library (held on every
+ * GPU that loads it); nslg_plan_decode_host keeps pinned host staging of its own.
  *
  * Errors that can only be seen on the device (a page id outside the pool, a write
  * slot outside the pool, a position outside the RoPE table) never trap: the kernel
@@ -143,6 +145,9 @@ int nslg_append_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_
  * ((batch + #SMs) * num_qo_heads * (head_dim + 1) * 4 bytes) exceeds it are rejected with
  * NSLG_ERR_WORKSPACE. The first call on a device looks the array's device address up
  * (cudaGetSymbolAddress) with that device current; make it before any stream capture.
+ * The address is kept with the CUDA context it belongs to: the first call in another
+ * context (after cudaDeviceReset, or in a context the caller created) looks it up again
+ * and must also come before any capture.
  * All calls on a device share the array, so calls that overlap on the GPU race: order
  * them. Allocates and frees nothing. */
 int nslg_paged_decode_noalloc(int dtype, int batch, int num_qo_heads, int num_kv_heads,

@@ -20,6 +20,8 @@ int set_error(int code, const std::string& msg) {
   return code;
 }
 
+void clear_error() { g_last_error.clear(); }
+
 int check_launch(const char* what) {
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess)

@@ -17,7 +17,10 @@
 // first call on each device (with that device current) we look its device address up
 // once with cudaGetSymbolAddress and reuse it afterwards; make that first call before
 // any stream capture. The first call on a device also loads this module if it is not
-// loaded yet.
+// loaded yet. The address is kept together with the CUDA context it was looked up in;
+// a call made in another context (after cudaDeviceReset, or in a context the caller
+// created) looks it up again, so make the first call in each new context before any
+// stream capture too.
 //
 // Sharing. Every call on a device uses the same array and it keeps whatever the last
 // call left there. Nothing in it has to start at zero: the merge step reads only
@@ -44,22 +47,53 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NSLG_NOALLOC_SC
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};   // the context each address belongs to
 
-// Device address of g_noalloc_scratch on the current device, looked up once per device.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library does not link
+// libcuda itself); null if the driver does not provide it.
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device
+// and context: the address is cached with the context that was current when it was
+// looked up, and looked up again when the calling thread's current context differs (a
+// new primary context after cudaDeviceReset, or a context the caller created), since
+// the module, and with it the array, is loaded at another address in each context.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(NSLG_ERR_UNSUPPORTED, "paged_decode_noalloc: device index >= 64");
+  CtxGetCurrentFn get = ctx_get_current_fn();
+  if (get == nullptr)
+    return set_error(NSLG_ERR_CUDA, "paged_decode_noalloc: driver has no cuCtxGetCurrent");
+  // null until the runtime has bound a context to this thread; the lookup below does that
+  CUcontext ctx = nullptr;
+  if (get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  if (ctx == nullptr || g_scratch_addr[dev] == nullptr || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
     err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (err != cudaSuccess || p == nullptr)
       return set_error(NSLG_ERR_CUDA, std::string("paged_decode_noalloc: cudaGetSymbolAddress: ") +
                                           cudaGetErrorString(err));
+    if (get(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return set_error(NSLG_ERR_CUDA, "paged_decode_noalloc: no current CUDA context");
     g_scratch_addr[dev] = p;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_addr[dev];
   return NSLG_OK;
@@ -78,6 +112,7 @@ extern "C" int nslg_paged_decode_noalloc(int dtype, int batch, int num_qo_heads,
                                          const int32_t* kv_indptr, const int32_t* kv_indices,
                                          const int32_t* kv_last_page_len, float sm_scale,
                                          uint32_t* dev_status, void* stream) {
+  clear_error();
   if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F32)
     return set_error(NSLG_ERR_ARG, "paged_decode_noalloc: bad dtype");
   if (batch < 0) return set_error(NSLG_ERR_ARG, "paged_decode_noalloc: batch < 0");

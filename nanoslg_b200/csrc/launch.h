@@ -14,6 +14,10 @@ namespace nslg {
 // Records `msg` as this thread's last error and returns `code`.
 int set_error(int code, const std::string& msg);
 
+// Empties this thread's last error (every entry point does this first, so that
+// nslg_last_error() returns "" after a call that succeeded).
+void clear_error();
+
 // Turns a pending launch error into NSLG_ERR_CUDA with the kernel's name.
 int check_launch(const char* what);
 

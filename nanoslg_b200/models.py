@@ -397,6 +397,40 @@ def load_full_state_dict(model, full, tp_size=1, tp_rank=0):
     return model
 
 
+def reference_param_shapes(hf_config):
+    """Names and shapes of an unsharded LlamaTP's parameters, in the order of the
+    reference's ``named_parameters()`` (models.py:108-172, 246-276)."""
+    h, inter, vocab = hf_config.hidden_size, hf_config.intermediate_size, hf_config.vocab_size
+    nq = hf_config.num_attention_heads
+    nkv = getattr(hf_config, "num_key_value_heads", nq)
+    d = h // nq
+    out = [("embed_tokens.weight", (vocab, h))]
+    for i in range(hf_config.num_hidden_layers):
+        p = f"layers.{i}."
+        out += [(p + "self_attn.q_proj.weight", (nq * d, h)),
+                (p + "self_attn.k_proj.weight", (nkv * d, h)),
+                (p + "self_attn.v_proj.weight", (nkv * d, h)),
+                (p + "self_attn.o_proj.weight", (h, nq * d)),
+                (p + "mlp.gate_proj.weight", (inter, h)), (p + "mlp.up_proj.weight", (inter, h)),
+                (p + "mlp.down_proj.weight", (h, inter)),
+                (p + "input_layernorm.weight", (h,)),
+                (p + "post_attention_layernorm.weight", (h,))]
+    return out + [("norm.weight", (h,)), ("lm_head.lm_head.weight", (vocab, h))]
+
+
+def reference_random_state_dict(hf_config, seed=0, std=0.02):
+    """Unsharded fp32 state dict of the BASELINE init rule on the CPU: manual_seed(seed),
+    then normal_(0, std) over the parameters in the reference's order, norm weights 1.
+    Sharded with ``load_full_state_dict``, every TP/PP layout gets the same model."""
+    shapes = reference_param_shapes(hf_config)
+    sd = {n: (torch.ones(s) if "norm" in n else torch.empty(s)) for n, s in shapes}
+    torch.manual_seed(seed)
+    for n, _ in shapes:
+        if "norm" not in n:
+            sd[n].normal_(0.0, std)
+    return sd
+
+
 def init_random_(model, seed=0, std=0.02):
     """Random init of the BASELINE configs: manual_seed(seed), normal_(0, std) over
     named_parameters() in order, norm weights kept at 1 (the golden fixture's rule)."""

@@ -21,6 +21,10 @@ and the CUDA path can be pinned to the reference without the reference being pre
 * ``tiny_llama.json``        -- greedy tokens of the tiny fp32 Llama (2 layers, hidden 256,
   4/2 heads, vocab 1024) driven exactly like ``worker.py`` drives a TP=1 batch, on the
   contiguous-SDPA backend.
+* ``tiny_llama_kv8.json``    -- the same for a batch of two prompts (32 and 19 tokens,
+  left-padded prefill) on the tiny model widened to hidden 512 with 8 query / 8 KV heads,
+  so that tensor-parallel degrees 1, 2, 4 and 8 all divide its heads
+  (``--only-kv8`` writes this file alone).
 
 The shims are the minimum needed to run on CPU: ``ParallelContext.device = cpu``,
 backend ``contiguous`` (or ``flashinfer`` with the wrappers stubbed), and building the
@@ -564,11 +568,80 @@ def tiny_llama(kvc, M, ParallelContext, ParallelConfig, ParallelMode):
             "min_margin": min(margins), "first_logits_head": first_logits[:16].tolist()}
 
 
+# The tiny model widened to 8 query and 8 KV heads, so that every tensor-parallel degree
+# of one 8-GPU node (1, 2, 4, 8) divides its heads; two prompts of different lengths.
+TINY_KV8 = dict(num_hidden_layers=2, hidden_size=512, num_attention_heads=8,
+                num_key_value_heads=8, intermediate_size=1024, vocab_size=1024,
+                rms_norm_eps=1e-5, rope_theta=10000.0, max_position_embeddings=128)
+
+
+def tiny_llama_batch(kvc, M, ParallelContext, ParallelConfig, ParallelMode, cfg=TINY_KV8,
+                     prompt_lens=(32, 19), steps=16):
+    """Greedy tokens of a batch driven like worker.py:365-426 drives one TP batch: one
+    left-padded prefill forward (input_offsets = width - count, worker.py:375-378), then
+    decode steps of the whole batch (worker.py:398-412), on the contiguous-SDPA backend."""
+    pctx = ParallelContext.initialize(ParallelConfig(ParallelMode.TENSOR, 1), 0)
+    pctx.device = torch.device("cpu")
+    hf = SimpleNamespace(**cfg)
+    model = M.create_model(hf, pctx.config).float()
+    torch.manual_seed(0)
+    names = []
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            names.append(n)
+            if "norm" in n:
+                continue
+            p.normal_(0.0, 0.02)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist()
+               for n in prompt_lens]
+    B = len(prompts)
+    nq, nkv = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    kcfg = kvc.KVCacheConfig(num_layers=cfg["num_hidden_layers"], num_kv_heads=nkv,
+                             num_qo_heads=nq, head_dim=cfg["hidden_size"] // nq,
+                             max_batch_size=B, max_seq_len=max(prompt_lens) + steps + 8,
+                             dtype=torch.float32, device=torch.device("cpu"),
+                             backend="contiguous")
+    mgr = kvc.ContiguousKVCache(kcfg)
+    sids = [f"s{i}" for i in range(B)]
+    width = max(prompt_lens)
+    ids = torch.zeros(B, width, dtype=torch.long)
+    for i, p in enumerate(prompts):
+        ids[i, width - len(p):] = torch.tensor(p)
+    toks = [[] for _ in range(B)]
+    margins = []
+    with torch.inference_mode():
+        for sid, p in zip(sids, prompts):
+            mgr.allocate_sequence(sid, p)
+        ctx = mgr.begin_forward(sids, [len(p) for p in prompts],
+                                [width - len(p) for p in prompts])
+        logits = model(ids, ctx, None)
+        mgr.end_forward(ctx)
+        for step in range(steps):
+            last = logits[:, -1]
+            top2 = torch.topk(last, 2, dim=-1).values
+            margins.append(float((top2[:, 0] - top2[:, 1]).min()))
+            t = last.argmax(-1)
+            for i in range(B):
+                toks[i].append(int(t[i]))
+            if step + 1 == steps:
+                break
+            ctx = mgr.begin_forward(sids, [1] * B)
+            logits = model(t[:, None], ctx, None)
+            mgr.end_forward(ctx)
+    return {"config": cfg, "init": "torch.manual_seed(0); normal_(0, 0.02) over "
+            "named_parameters() in order, skipping *norm* weights (kept at 1)",
+            "param_order": names, "prompts": prompts, "tokens": toks,
+            "min_margin": min(margins)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of Guney-olu/nanoslg")
     ap.add_argument("--only-paged", action="store_true",
                     help="write paged_scenarios.json only")
+    ap.add_argument("--only-kv8", action="store_true",
+                    help="write tiny_llama_kv8.json only")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import nanoslg.kv_cache as kvc
@@ -576,6 +649,13 @@ def main():
     from nanoslg.parallel import ParallelContext, ParallelConfig, ParallelMode
 
     torch.set_num_threads(1)
+    if args.only_kv8:
+        tb = tiny_llama_batch(kvc, M, ParallelContext, ParallelConfig, ParallelMode)
+        with open(os.path.join(HERE, "tiny_llama_kv8.json"), "w") as f:
+            json.dump(tb, f, indent=1)
+        print("tiny llama (8 kv heads, batch 2) tokens:", tb["tokens"], "min margin",
+              tb["min_margin"])
+        return
     scen = paged_scenarios(kvc)
     for s in scen:
         s["ops"] = expand_prefill_auto(kvc, s)
@@ -592,6 +672,11 @@ def main():
     with open(os.path.join(HERE, "tiny_llama.json"), "w") as f:
         json.dump(tl, f, indent=1)
     print("tiny llama tokens:", tl["tokens"], "min margin", tl["min_margin"])
+    tb = tiny_llama_batch(kvc, M, ParallelContext, ParallelConfig, ParallelMode)
+    with open(os.path.join(HERE, "tiny_llama_kv8.json"), "w") as f:
+        json.dump(tb, f, indent=1)
+    print("tiny llama (8 kv heads, batch 2) tokens:", tb["tokens"], "min margin",
+          tb["min_margin"])
 
 
 if __name__ == "__main__":

@@ -108,3 +108,32 @@ def test_tiny_llama_oracle_greedy_tokens():
     torch.set_num_threads(1)
     o = TinyLlamaOracle(g["config"], init_params(g["config"]))
     assert o.greedy(g["prompt"], len(g["tokens"])) == g["tokens"]
+
+
+def test_tiny_llama_kv8_oracle_greedy_tokens():
+    """The batch fixture of the widened tiny model (8/8 heads): each prompt alone through
+    the oracle gives the tokens the reference produced for it inside the left-padded
+    batch."""
+    with open(os.path.join(GOLDEN, "tiny_llama_kv8.json")) as f:
+        g = json.load(f)
+    assert g["param_order"] == param_names(g["config"]["num_hidden_layers"])
+    torch.set_num_threads(1)
+    params = init_params(g["config"])
+    for prompt, want in zip(g["prompts"], g["tokens"]):
+        o = TinyLlamaOracle(g["config"], params)
+        assert o.greedy(prompt, len(want)) == want
+
+
+def test_reference_random_state_dict_matches_oracle_init():
+    """models.reference_random_state_dict (the product's copy of the fixtures' init rule)
+    gives the oracle's parameters bit for bit, in the reference's parameter order."""
+    from types import SimpleNamespace
+    from nanoslg_b200.models import reference_random_state_dict
+    for name in ("tiny_llama.json", "tiny_llama_kv8.json"):
+        with open(os.path.join(GOLDEN, name)) as f:
+            g = json.load(f)
+        got = reference_random_state_dict(SimpleNamespace(**g["config"]))
+        want = init_params(g["config"])
+        assert list(got) == g["param_order"]
+        for k in want:
+            assert torch.equal(got[k], want[k]), k
