@@ -203,9 +203,12 @@ def run_e2e(device, steps, warmup, seed, depth=1):
     Each step copies its q/k/v from pinned host memory to the device, plans, appends and
     attends, copies the output to pinned host memory and ends the forward; a step is
     finished when its output is on the host. ``depth`` 1 finishes every step before the
-    next begins; 2 begins step i+1 (host bookkeeping and launches, queued behind step i
-    on the same stream) before waiting for step i's output, so the host work of one step
-    overlaps the device work of the other. The device work itself stays in step order."""
+    next begins (one stream). ``depth`` 2 begins step i+1 before waiting for step i's
+    output, and on a GPU moves the copies to two copy streams with a device input buffer
+    and a host output buffer per step in flight: step i+1's inputs go up while step i's
+    kernels run and step i's output comes down while step i+1's run, so the compute
+    stream only runs the plan, append and attention kernels back to back. The kernels
+    stay in step order on one stream (each step appends to the same sequences)."""
     from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig
     lens = c2_lens(seed)
     cfg = KVCacheConfig(num_layers=1, num_kv_heads=HKV, num_qo_heads=HQ, head_dim=D,
@@ -224,28 +227,49 @@ def run_e2e(device, steps, warmup, seed, depth=1):
     g = torch.Generator().manual_seed(seed + 1)
     nbuf = 4
     # each step's q | k | v packed in one pinned host buffer, copied with one transfer
-    # into one device buffer (stream order puts the copy after the previous step's
-    # kernels, the buffer's last readers)
+    # into the device buffer of its slot (one slot per step in flight)
     qn, kn = B * HQ * D, B * HKV * D
     hin = [torch.randn(qn + 2 * kn, generator=g).to(torch.bfloat16).pin_memory()
            for _ in range(nbuf)]
-    din = torch.empty(qn + 2 * kn, dtype=torch.bfloat16, device=device)
-    q = din[:qn].view(B, 1, HQ, D)
-    k = din[qn:qn + kn].view(B, 1, HKV, D)
-    v = din[qn + kn:].view(B, 1, HKV, D)
-    # one pinned output buffer and one event per step in flight
+    din = [torch.empty(qn + 2 * kn, dtype=torch.bfloat16, device=device) for _ in range(depth)]
+    qkv = [(d[:qn].view(B, 1, HQ, D), d[qn:qn + kn].view(B, 1, HKV, D),
+            d[qn + kn:].view(B, 1, HKV, D)) for d in din]
     hout = [torch.empty(B, 1, HQ * D, dtype=torch.bfloat16).pin_memory() for _ in range(depth)]
     done = [torch.cuda.Event() for _ in range(depth)]
     stream = torch.cuda.current_stream(device)
+    split = depth > 1 and device.type == "cuda"
+    if split:
+        cp_in, cp_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        in_ready = [torch.cuda.Event() for _ in range(depth)]
+        consumed = [torch.cuda.Event() for _ in range(depth)]
+        keep = [None] * depth       # each slot's output, alive until its copy is finished
     stats = {"h2d": 0, "d2h": 0}
 
     def launch(i):
-        # the step's inputs go to the device first, so their copy overlaps the planning
-        din.copy_(hin[i % nbuf], non_blocking=True)
+        s = i % depth
+        q, k, v = qkv[s]
+        if split:
+            # the slot's previous step has finished reading its inputs (and the host has
+            # read its output: ``pipelined`` finishes step i - depth before this launch)
+            cp_in.wait_event(consumed[s])
+            with torch.cuda.stream(cp_in):
+                din[s].copy_(hin[i % nbuf], non_blocking=True)
+            in_ready[s].record(cp_in)
+            stream.wait_event(in_ready[s])
+        else:
+            din[s].copy_(hin[i % nbuf], non_blocking=True)
         ctx = mgr.begin_forward(sids, [1] * B)
         out = ctx.attend(0, q, k, v, HQ, HKV)
-        hout[i % depth].copy_(out, non_blocking=True)
-        done[i % depth].record(stream)
+        if split:
+            consumed[s].record(stream)
+            cp_out.wait_event(consumed[s])
+            with torch.cuda.stream(cp_out):
+                hout[s].copy_(out, non_blocking=True)
+            done[s].record(cp_out)
+            keep[s] = out
+        else:
+            hout[s].copy_(out, non_blocking=True)
+            done[s].record(stream)
         mgr.end_forward(ctx)      # the reference's order: begin, forward, end, read
         stats["h2d"] = q.numel() * 2 + k.numel() * 2 + v.numel() * 2 + ctx._plan_bytes
         stats["d2h"] = hout[0].numel() * 2
@@ -260,7 +284,7 @@ def run_e2e(device, steps, warmup, seed, depth=1):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     pipelined(steps, lambda i: launch(warmup + i), lambda i: finish(warmup + i), depth)
-    e1.record(stream)
+    e1.record(stream)      # every step's output is on the host by now
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1)
     del mgr
@@ -535,7 +559,7 @@ def run_step_split(runner, device, reps=10):
         if tp > 1:
             idx, val = ops.argmax_rows(logits, 0, values=True)
             pair = torch.stack([val, idx.float()], -1)
-            allp = torch.empty((tp,) + tuple(pair.shape), dtype=pair.dtype, device=device)
+            allp = torch.empty((tp * pair.shape[0], 2), dtype=pair.dtype, device=device)
             torch.distributed.all_gather_into_tensor(allp, pair, group=runner.pctx.tp_group)
         else:
             ops.argmax_rows(logits)

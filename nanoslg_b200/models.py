@@ -302,8 +302,11 @@ class _LlamaStage(nn.Module):
         offset = ctx.tp_rank * head.out_features_per_partition
         idx, val = ops.argmax_rows(local, offset, values=True)
         pair = torch.stack([val, idx.float()], -1)                        # exact below 2^24
-        allp = torch.empty((tp,) + tuple(pair.shape), dtype=pair.dtype, device=pair.device)
+        # gathered as the rank-major concatenation [tp * B, 2] (the layout every backend
+        # accepts), viewed as [tp, B, 2]
+        allp = torch.empty((tp * pair.shape[0], 2), dtype=pair.dtype, device=pair.device)
         dist.all_gather_into_tensor(allp, pair.contiguous(), group=ctx.tp_group)
+        allp = allp.view(tp, pair.shape[0], 2)
         best = allp[..., 0].argmax(0)                                      # first max rank
         return allp[..., 1].gather(0, best[None]).squeeze(0).long()
 

@@ -161,3 +161,64 @@ def test_pp_microbatch_schedule_matches_lock_step(world, num_micro):
             assert got == want, rank
         else:
             assert got is None
+
+
+def _greedy_worker(rank, world, port, out):
+    """models._LlamaStage._greedy under TP over gloo: each rank reduces its vocabulary
+    shard and the ranks exchange (max, index) pairs; the argmax kernel is replaced by
+    torch.argmax (CPU), which is what it is GPU-tested against."""
+    import types
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nanoslg_b200 import models, parallel, tp_layers
+        cfg = parallel.ParallelConfig(parallel.ParallelMode.TENSOR, world)
+        ctx = parallel.ParallelContext.initialize(cfg, rank, device="cpu")
+        ctx.setup_groups()
+
+        def argmax_rows(x, index_offset=0, values=False):
+            idx = x.argmax(-1) + index_offset
+            val = x.max(-1).values.float()
+            return (idx, val) if values else idx
+
+        models.ops.argmax_rows = argmax_rows
+        V, H, rows = 24, 6, 7
+        head = tp_layers.ParallelLMHead(H, V, gather_output=True)
+        g = torch.Generator().manual_seed(3)
+        w = torch.randn(V, H, generator=g)
+        # rows 1-3: the maximum ties across shards (equal weight rows in both halves, and
+        # an exact tie between indices 5 and 17 / 2 and 22); row 4: all logits equal
+        w[17] = w[5]
+        w[22] = w[2]
+        h = torch.randn(rows, 1, H, generator=g)
+        h[1, 0] = w[5] * 3
+        h[2, 0] = w[2] * 3
+        h[3, 0] = w[17] * 3
+        h[4, 0] = 0.0
+        with torch.no_grad():
+            head.lm_head.weight.copy_(w.chunk(world, 0)[rank])
+        stage = types.SimpleNamespace(lm_head=head)
+        with torch.inference_mode():                 # as in the runner's decode steps
+            got = models._LlamaStage._greedy(stage, h)
+        want = torch.nn.functional.linear(h[:, -1], w).argmax(-1)
+        out[rank] = (got.tolist(), want.tolist())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_vocab_parallel_greedy_exchange_matches_argmax_of_gathered_logits(world):
+    """The (max, index) exchange of the vocab-parallel LM head picks the token argmax over
+    the all-gathered logits would (the reference's path, tp_layers.py:89 then argmax),
+    including exact ties across shards, which go to the lowest index."""
+    port = _free_port()
+    with mp.get_context("spawn").Manager() as m:
+        out = m.dict()
+        mp.start_processes(_greedy_worker, args=(world, port, out), nprocs=world,
+                           start_method="spawn", join=True)
+        res = dict(out)
+    assert set(res) == set(range(world))
+    for rank, (got, want) in res.items():
+        assert got == want, rank
+    assert res[0][1][1] == 5 and res[0][1][2] == 2 and res[0][1][4] == 0

@@ -66,6 +66,23 @@ def test_rope_tables_match_reference():
         torch.testing.assert_close(sin[g["rows"]], g["sin"], rtol=0, atol=0)
 
 
+def test_product_rope_tables_match_reference():
+    """nanoslg_b200.models.precompute_rope_frequencies (vectorised; the tables every GPU
+    RoPE launch reads) is bit-exact with the reference's tables, Llama-3 scaling included."""
+    from types import SimpleNamespace
+    from nanoslg_b200.models import precompute_rope_frequencies
+    for key in ("t64_1e4", "t128_5e5", "t128_l3"):
+        g = RN[f"table_{key}"]
+        sc = ({"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+               "high_freq_factor": 4.0, "original_max_position_embeddings": 8192}
+              if g["llama3"] else None)
+        cos, sin = precompute_rope_frequencies(g["dim"], g["max"], g["theta"],
+                                               SimpleNamespace(rope_scaling=sc))
+        assert cos.dtype == torch.float32 and cos.shape == (g["max"], g["dim"])
+        torch.testing.assert_close(cos[g["rows"]], g["cos"], rtol=0, atol=0)
+        torch.testing.assert_close(sin[g["rows"]], g["sin"], rtol=0, atol=0)
+
+
 @pytest.mark.parametrize("dt", ["float32", "bfloat16"])
 def test_rope_and_rmsnorm_match_reference(dt):
     cos, sin = rope_table(128, 4096, 500000.0)
