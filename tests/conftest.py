@@ -9,6 +9,12 @@ if ROOT not in sys.path:
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
+# A checkout of the reference (NanoSLG), for the CPU tests that import its own Python:
+# NANOSLG_REFERENCE, else a "reference" checkout beside this repository, else None.
+REFERENCE = os.environ.get("NANOSLG_REFERENCE") or (
+    os.path.join(os.path.dirname(ROOT), "reference")
+    if os.path.isdir(os.path.join(os.path.dirname(ROOT), "reference", "nanoslg")) else None)
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and the built library")
