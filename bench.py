@@ -762,7 +762,14 @@ def run_allreduce(device, world, rank, hidden=4096, rows_list=(1, 64, 256), call
         def fused():
             return peer.allreduce_add_norm(x, r, w, 1e-5)
 
-        for name, fn in (("nccl_allreduce_plus_rmsnorm_us", nccl), ("fused_us", fused)):
+        legs = [("nccl_allreduce_plus_rmsnorm_us", nccl, None), ("fused_us", fused, None)]
+        if world > 2:       # the fused kernel's two modes, forced (decided at capture)
+            legs += [("fused_one_shot_us", fused, "0"), ("fused_two_shot_us", fused, "1")]
+        for name, fn, mode in legs:
+            if mode is None:
+                os.environ.pop("NSLG_TP_TWO_SHOT", None)
+            else:
+                os.environ["NSLG_TP_TWO_SHOT"] = mode
             for _ in range(3):
                 fn()
             torch.cuda.synchronize(device)
@@ -783,6 +790,7 @@ def run_allreduce(device, world, rank, hidden=4096, rows_list=(1, 64, 256), call
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             out.setdefault(f"rows{rows}", {})[name] = round(float(t.item()), 2)
             del g
+    os.environ.pop("NSLG_TP_TWO_SHOT", None)
     ops.check_device_status(device)
     peer.close()
     return {"world": world, "hidden": hidden, "dtype": "bf16", **out}

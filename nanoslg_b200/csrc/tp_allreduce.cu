@@ -27,12 +27,25 @@
 // words of call e + 1, written only after this rank finished call e), and words left
 // from call e - 1 carry another call number.
 //
+// Two-shot mode, for many rows on many ranks: the one-shot push sends world - 1 copies of
+// every row out of each GPU, which at TP=8 and 64 rows is 7 MiB per call (packed). The
+// two-shot mode splits each row into `world` column slices: rank r sends slice j of its
+// partial rows to rank j only (reduce-scatter), rank j sums slice j over the ranks in
+// the same fp32 rank order and rounds it once, then pushes the reduced slice to every
+// rank (all-gather); each rank then has the whole reduced row and does the residual add
+// and RMSNorm as before. Results are identical to the one-shot mode's; each rank sends
+// 2 (world - 1) / world of a row instead of world - 1 rows, for a second NVLink round
+// trip. Both phases use the same in-band call numbers, so the mode may change from call
+// to call.
+//
 // Stage buffer of each rank: [2 slots][world sources][rows][2 x row bytes] (the packed
-// rows are twice the activations). Every wait is bounded by `timeout_ns` of
+// rows are twice the activations); in two-shot mode a slot holds [2 phases][world
+// sources][rows][2 x slice bytes] instead. Every wait is bounded by `timeout_ns` of
 // %globaltimer; a block that gives up records NSLG_DEV_WAIT_TIMEOUT and leaves its rows
 // unwritten, so the context stays usable.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -45,6 +58,16 @@ namespace {
 constexpr int kGrid = 128;          // blocks per call, the same on every rank and call
 constexpr int kThreads = 256;
 constexpr int kVecPerThread = 4;    // 16-byte vectors of a row per thread (hidden <= 8192 bf16)
+// one-shot push volume per rank ((world - 1) x rows x row bytes) from which two-shot is used
+constexpr int64_t kTwoShotBytes = 512 << 10;
+
+// NSLG_TP_TWO_SHOT, read at every call: unset or "auto" -> -1 (choose by size), "0" /
+// "1" -> force one-shot / two-shot (where the shape allows it)
+int two_shot_override() {
+  const char* e = getenv("NSLG_TP_TWO_SHOT");
+  if (e == nullptr || e[0] == '\0' || strcmp(e, "auto") == 0) return -1;
+  return e[0] == '1' ? 1 : 0;
+}
 static_assert(kGrid * 4 <= NSLG_TP_COUNTER_BYTES, "counter buffer too small");
 
 struct ArParams {
@@ -58,7 +81,7 @@ struct ArParams {
   const void* weight;
   void* out;
   int64_t o_stride;
-  int rows, hidden, world, rank;
+  int rows, hidden, world, rank, two_shot;
   float eps;
   uint64_t timeout_ns;
   uint32_t* status;
@@ -98,19 +121,53 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
   __shared__ float red[kThreads / 32];
   if (threadIdx.x == 0) bad = 0;
 
-  // 1. push this rank's partial rows, packed with the call number, to every peer
+  // Polls the packed 32-byte unit at q until both of its 16-byte halves carry this call
+  // number (bounded); returns its 16 data bytes. On a timeout sets `bad` (the block's
+  // other threads stop polling too) and records NSLG_DEV_WAIT_TIMEOUT.
+  auto fetch = [&](const uint4* q, uint4& out) {
+    uint4 a = ld_relaxed_v4(q), b = ld_relaxed_v4(q + 1);
+    if (!(a.y == call && a.w == call && b.y == call && b.w == call)) {
+      const uint64_t t0 = global_ns();
+      while (true) {
+        a = ld_relaxed_v4(q);
+        b = ld_relaxed_v4(q + 1);
+        if (a.y == call && a.w == call && b.y == call && b.w == call) break;
+        if (bad) break;
+        if (global_ns() - t0 > p.timeout_ns) {
+          bad = 1;
+          report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+          break;
+        }
+      }
+    }
+    out = make_uint4(a.x, a.z, b.x, b.z);
+  };
+  auto push = [&](uint4* dst, const uint4 v) {
+    st_relaxed_v4(dst, make_uint4(v.x, call, v.y, call));
+    st_relaxed_v4(dst + 1, make_uint4(v.z, call, v.w, call));
+  };
+  // two-shot layout of a slot, per phase and source rank: [rows][2 * nvs] packed units
+  const int nvs = nv / p.world;                   // 16-byte vectors per column slice
+  const int64_t units_src = 2 * static_cast<int64_t>(p.rows) * nvs;
+
+  // 1. push this rank's partial rows, packed with the call number: one-shot, the whole
+  //    row to every peer; two-shot, column slice j of the row to rank j only
   for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.partial) +
                                                       row * p.p_stride);
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
       const uint4 v = src[i];
-      const uint4 u0 = make_uint4(v.x, call, v.y, call), u1 = make_uint4(v.z, call, v.w, call);
+      if (p.two_shot) {
+        const int j = i / nvs;
+        if (j == p.rank) continue;
+        push(reinterpret_cast<uint4*>(p.stage[j] + slot_off) + p.rank * units_src +
+                 row * 2 * nvs + 2 * (i - j * nvs), v);
+        continue;
+      }
       for (int d = 0; d < p.world; ++d) {
         if (d == p.rank) continue;
-        uint4* dst = reinterpret_cast<uint4*>(p.stage[d] + slot_off + p.rank * p.region_bytes) +
-                     row * units_per_row + 2 * i;
-        st_relaxed_v4(dst, u0);
-        st_relaxed_v4(dst + 1, u1);
+        push(reinterpret_cast<uint4*>(p.stage[d] + slot_off + p.rank * p.region_bytes) +
+                 row * units_per_row + 2 * i, v);
       }
     }
   }
@@ -121,40 +178,63 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
   for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
     const uint4* mine = reinterpret_cast<const uint4*>(static_cast<const T*>(p.partial) +
                                                        row * p.p_stride);
+    const uint4* own = reinterpret_cast<const uint4*>(p.stage[p.rank] + slot_off);
     float acc[kVecPerThread][VEC];
+    if (p.two_shot) {
+      // 2a. reduce this rank's column slice over the ranks (fp32, rank order, one
+      //     rounding) and push the reduced slice to every rank, this one included
+      for (int u = threadIdx.x; u < nvs; u += blockDim.x) {
+        float a[VEC];
 #pragma unroll
-    for (int k = 0; k < kVecPerThread; ++k) {
-      const int i = threadIdx.x + k * kThreads;
+        for (int j = 0; j < VEC; ++j) a[j] = 0.f;
+        for (int s = 0; s < p.world; ++s) {
+          NVec<T, VEC> v;
+          if (s == p.rank) v.u = mine[p.rank * nvs + u];
+          else fetch(own + s * units_src + row * 2 * nvs + 2 * u, v.u);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) acc[k][j] = 0.f;
-      if (i >= nv) continue;
-      for (int s = 0; s < p.world; ++s) {
-        NVec<T, VEC> v;
-        if (s == p.rank) {
-          v.u = mine[i];
-        } else {
-          const uint4* q = reinterpret_cast<const uint4*>(p.stage[p.rank] + slot_off +
-                                                          s * p.region_bytes) +
-                           row * units_per_row + 2 * i;
-          uint4 a = ld_relaxed_v4(q), b = ld_relaxed_v4(q + 1);
-          if (!(a.y == call && a.w == call && b.y == call && b.w == call)) {
-            const uint64_t t0 = global_ns();
-            while (true) {
-              a = ld_relaxed_v4(q);
-              b = ld_relaxed_v4(q + 1);
-              if (a.y == call && a.w == call && b.y == call && b.w == call) break;
-              if (bad) break;
-              if (global_ns() - t0 > p.timeout_ns) {
-                bad = 1;
-                report(p.status, NSLG_DEV_WAIT_TIMEOUT);
-                break;
-              }
-            }
-          }
-          v.u = make_uint4(a.x, a.z, b.x, b.z);
+          for (int j = 0; j < VEC; ++j) a[j] = __fadd_rn(a[j], Elem<T>::to_f(v.e[j]));
         }
+        if (bad) break;   // never push a slice built from words that did not arrive
+        NVec<T, VEC> r;
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) acc[k][j] = __fadd_rn(acc[k][j], Elem<T>::to_f(v.e[j]));
+        for (int j = 0; j < VEC; ++j) r.e[j] = Elem<T>::from_f(a[j]);
+        for (int d = 0; d < p.world; ++d)
+          push(reinterpret_cast<uint4*>(p.stage[d] + slot_off) + (p.world + p.rank) * units_src +
+                   row * 2 * nvs + 2 * u, r.u);
+      }
+      // 2b. gather the reduced slices of every rank
+#pragma unroll
+      for (int k = 0; k < kVecPerThread; ++k) {
+        const int i = threadIdx.x + k * kThreads;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[k][j] = 0.f;
+        if (i >= nv) continue;
+        const int s = i / nvs;
+        NVec<T, VEC> v;
+        fetch(own + (p.world + s) * units_src + row * 2 * nvs + 2 * (i - s * nvs), v.u);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[k][j] = Elem<T>::to_f(v.e[j]);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < kVecPerThread; ++k) {
+        const int i = threadIdx.x + k * kThreads;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[k][j] = 0.f;
+        if (i >= nv) continue;
+        for (int s = 0; s < p.world; ++s) {
+          NVec<T, VEC> v;
+          if (s == p.rank) {
+            v.u = mine[i];
+          } else {
+            const uint4* q = reinterpret_cast<const uint4*>(p.stage[p.rank] + slot_off +
+                                                            s * p.region_bytes) +
+                             row * units_per_row + 2 * i;
+            fetch(q, v.u);
+          }
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) acc[k][j] = __fadd_rn(acc[k][j], Elem<T>::to_f(v.e[j]));
+        }
       }
     }
     __syncthreads();
@@ -304,6 +384,17 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
   p.world = world;
   p.rank = rank;
   p.eps = eps;
+  // Two-shot (reduce-scatter of column slices, then all-gather of the reduced slices)
+  // when the one-shot's (world - 1) full-row pushes per rank are large: it moves
+  // 2 (world - 1) / world of a row per rank instead of (world - 1) rows, at the price of a
+  // second NVLink round trip. Same fp32 rank-order sums, so both give identical results.
+  // NSLG_TP_TWO_SHOT=0/1 forces one mode (where the shape allows two-shot).
+  const int vec = 16 / esz;
+  const bool two_ok = world > 2 && hidden % (world * vec) == 0;
+  const int force = two_shot_override();
+  p.two_shot = two_ok && (force >= 0 ? force == 1
+                                     : static_cast<int64_t>(rows) * row_bytes * (world - 1) >=
+                                           kTwoShotBytes);
   p.timeout_ns = static_cast<uint64_t>(timeout_ns);
   p.status = dev_status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
