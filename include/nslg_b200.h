@@ -33,9 +33,11 @@
 extern "C" {
 #endif
 
-/* element types */
+/* element types (the reference runs float32, bfloat16 and float16 activations,
+ * worker.py:22-26) */
 #define NSLG_DTYPE_F32 0
 #define NSLG_DTYPE_BF16 1
+#define NSLG_DTYPE_F16 2
 
 /* host-side status codes */
 #define NSLG_OK 0

@@ -12,6 +12,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libn
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+DTYPE_F16 = 2
 
 OK = 0
 ERR_ARG = 1

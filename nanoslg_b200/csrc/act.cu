@@ -20,6 +20,11 @@ union AVec {
 };
 
 template <typename T>
+constexpr bool kFastSilu = false;
+template <>
+constexpr bool kFastSilu<__nv_bfloat16> = true;
+
+template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* gu, int64_t gu_stride, T* out,
                                                        int64_t out_stride, int rows, int inter) {
   pdl_wait();
@@ -38,10 +43,10 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* gu, int64_t gu_s
     for (int j = 0; j < VEC; ++j) {
       const float x = Elem<T>::to_f(g.e[j]);
       // bf16 rounds silu to 8 bits, so the hardware exponential and the approximate
-      // division are enough there (and keep the kernel memory-bound); fp32 keeps the
-      // correctly rounded division and the full-precision exponential
-      const float s = sizeof(T) == 2 ? Elem<T>::round(__fdividef(x, 1.f + __expf(-x)))
-                                     : Elem<T>::round(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
+      // division are enough there (and keep the kernel memory-bound); fp32 and fp16
+      // (11 bits) keep the correctly rounded division and the full-precision exponential
+      const float s = kFastSilu<T> ? Elem<T>::round(__fdividef(x, 1.f + __expf(-x)))
+                                   : Elem<T>::round(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
       y.e[j] = Elem<T>::from_f(__fmul_rn(s, Elem<T>::to_f(u.e[j])));
     }
     *reinterpret_cast<uint4*>(out + r * out_stride + c) = y.u;
@@ -53,7 +58,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* gu, int64_t gu_s
 int launch_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gu_stride,
                     void* out, int64_t out_stride, cudaStream_t stream) {
   if (rows == 0) return NSLG_OK;
-  const int vec = dtype == NSLG_DTYPE_BF16 ? 8 : 4;
+  const int vec = 16 / dtype_bytes(dtype);
   const int64_t total = static_cast<int64_t>(rows) * (inter / vec);
   const int threads = 256;
   int64_t blocks = (total + threads - 1) / threads;
@@ -64,6 +69,10 @@ int launch_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t
     return launch_pdl("silu_mul", silu_mul_kernel<__nv_bfloat16>, grid, dim3(threads), 0, stream,
                       static_cast<const __nv_bfloat16*>(gate_up), gu_stride,
                       static_cast<__nv_bfloat16*>(out), out_stride, rows, inter);
+  if (dtype == NSLG_DTYPE_F16)
+    return launch_pdl("silu_mul", silu_mul_kernel<__half>, grid, dim3(threads), 0, stream,
+                      static_cast<const __half*>(gate_up), gu_stride, static_cast<__half*>(out),
+                      out_stride, rows, inter);
   return launch_pdl("silu_mul", silu_mul_kernel<float>, grid, dim3(threads), 0, stream,
                     static_cast<const float*>(gate_up), gu_stride, static_cast<float*>(out),
                     out_stride, rows, inter);

@@ -92,13 +92,13 @@ using namespace nslg;
 extern "C" int nslg_argmax_rows(int dtype, int rows, int cols, const void* x, int64_t x_stride,
                                 int64_t index_offset, float* out_val, int64_t* out_idx,
                                 void* stream) {
-  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F32)
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16 && dtype != NSLG_DTYPE_F32)
     return set_error(NSLG_ERR_ARG, "argmax_rows: bad dtype");
   if (rows < 0 || cols <= 0 || x_stride < cols)
     return set_error(NSLG_ERR_ARG, "argmax_rows: bad shape");
   if (rows == 0) return NSLG_OK;
   if (!x || !out_idx) return set_error(NSLG_ERR_ARG, "argmax_rows: null pointer");
-  const int esz = dtype == NSLG_DTYPE_BF16 ? 2 : 4;
+  const int esz = dtype_bytes(dtype);
   const int vec_ok = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((x_stride * esz) % 16 == 0) &&
                      ((static_cast<int64_t>(cols) * esz) % 16 == 0);
   int threads = kArgmaxThreads;
@@ -109,6 +109,10 @@ extern "C" int nslg_argmax_rows(int dtype, int rows, int cols, const void* x, in
     argmax_rows_kernel<__nv_bfloat16><<<rows, threads, 0, st>>>(
         static_cast<const __nv_bfloat16*>(x), x_stride, cols, index_offset, vec_ok, out_val,
         out_idx);
+  else if (dtype == NSLG_DTYPE_F16)
+    argmax_rows_kernel<__half><<<rows, threads, 0, st>>>(static_cast<const __half*>(x), x_stride,
+                                                         cols, index_offset, vec_ok, out_val,
+                                                         out_idx);
   else
     argmax_rows_kernel<float><<<rows, threads, 0, st>>>(static_cast<const float*>(x), x_stride,
                                                         cols, index_offset, vec_ok, out_val,

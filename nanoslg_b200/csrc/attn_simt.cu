@@ -128,6 +128,7 @@ int launch_paged_attention_simt(int dtype, int batch, int hq, int hkv, int d, in
                batch,     hq,         hkv,        d,                page_size, causal,
                sm_scale,  status};
   if (dtype == NSLG_DTYPE_BF16) return launch_typed<__nv_bfloat16>(p, max_qo_len, stream);
+  if (dtype == NSLG_DTYPE_F16) return launch_typed<__half>(p, max_qo_len, stream);
   return launch_typed<float>(p, max_qo_len, stream);
 }
 

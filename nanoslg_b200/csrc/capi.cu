@@ -45,9 +45,11 @@ namespace {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int esize(int dtype) { return dtype == NSLG_DTYPE_BF16 ? 2 : 4; }
+int esize(int dtype) { return dtype_bytes(dtype); }
 
-bool valid_dtype(int dtype) { return dtype == NSLG_DTYPE_BF16 || dtype == NSLG_DTYPE_F32; }
+bool valid_dtype(int dtype) {
+  return dtype == NSLG_DTYPE_BF16 || dtype == NSLG_DTYPE_F16 || dtype == NSLG_DTYPE_F32;
+}
 
 int check_heads(const char* what, int hq, int hkv, int d) {
   if (hq <= 0 || hkv <= 0 || d <= 0 || hq % hkv != 0)
@@ -129,7 +131,7 @@ int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads, 
   if (decode_tc_supported(dtype, num_qo_heads, num_kv_heads, head_dim, page_size) &&
       aligned16(pool_k) && aligned16(pool_v) && (reinterpret_cast<uintptr_t>(q) & 3u) == 0 &&
       (reinterpret_cast<uintptr_t>(out) & 3u) == 0 && q_stride % 2 == 0 && out_stride % 2 == 0)
-    return launch_paged_decode_tc(batch, num_qo_heads, num_kv_heads, head_dim, q, q_stride, out,
+    return launch_paged_decode_tc(dtype, batch, num_qo_heads, num_kv_heads, head_dim, q, q_stride, out,
                                   out_stride, pool_k, pool_v, num_pages, kv_indptr, kv_indices,
                                   kv_last_page_len, sm_scale, workspace, workspace_bytes,
                                   dev_status, st);
@@ -192,7 +194,7 @@ int nslg_paged_prefill(int dtype, int batch, int num_qo_heads, int num_kv_heads,
   if (prefill_tc_supported(dtype, num_qo_heads, num_kv_heads, head_dim, page_size) &&
       aligned16(q) && aligned16(out) && aligned16(pool_k) && aligned16(pool_v) &&
       (q_stride * 2) % 16 == 0 && (out_stride * 2) % 16 == 0)
-    return launch_paged_prefill_tc(batch, num_qo_heads, num_kv_heads, q, q_stride, q_rows, out,
+    return launch_paged_prefill_tc(dtype, batch, num_qo_heads, num_kv_heads, q, q_stride, q_rows, out,
                                    out_stride, qo_indptr, q_row_start, max_qo_len, pool_k,
                                    pool_v, num_pages, kv_indptr, kv_indices, kv_last_page_len,
                                    sm_scale, causal, dev_status, st);

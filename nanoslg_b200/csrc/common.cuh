@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -33,6 +34,14 @@ struct Elem<__nv_bfloat16> {
   __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
   __device__ __forceinline__ static float round(float x) {
     return __bfloat162float(__float2bfloat16_rn(x));
+  }
+};
+template <>
+struct Elem<__half> {
+  __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
+  __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
+  __device__ __forceinline__ static float round(float x) {
+    return __half2float(__float2half_rn(x));
   }
 };
 
@@ -156,6 +165,49 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// The 16-bit activation types of the tensor-core kernels: the warp-level mma of the
+// type, a pair of fp32 values rounded to it (low half first), and the tcgen05 kind::f16
+// operand format code (0 f16, 1 bf16).
+template <typename T>
+struct Mma16;
+template <>
+struct Mma16<__nv_bfloat16> {
+  static constexpr uint32_t kFormat = 1;
+  __device__ __forceinline__ static void mma(float (&d)[4], const uint32_t (&a)[4],
+                                             uint32_t b0, uint32_t b1) {
+    mma_bf16_16816(d, a, b0, b1);
+  }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    return pack_bf16x2(lo, hi);
+  }
+};
+template <>
+struct Mma16<__half> {
+  static constexpr uint32_t kFormat = 0;
+  __device__ __forceinline__ static void mma(float (&d)[4], const uint32_t (&a)[4],
+                                             uint32_t b0, uint32_t b1) {
+    mma_f16_16816(d, a, b0, b1);
+  }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    return pack_f16x2(lo, hi);
+  }
+};
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

@@ -113,7 +113,7 @@ extern "C" int nslg_paged_decode_noalloc(int dtype, int batch, int num_qo_heads,
                                          const int32_t* kv_last_page_len, float sm_scale,
                                          uint32_t* dev_status, void* stream) {
   clear_error();
-  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F32)
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16 && dtype != NSLG_DTYPE_F32)
     return set_error(NSLG_ERR_ARG, "paged_decode_noalloc: bad dtype");
   if (batch < 0) return set_error(NSLG_ERR_ARG, "paged_decode_noalloc: batch < 0");
   if (batch == 0) return NSLG_OK;
@@ -146,7 +146,7 @@ extern "C" int nslg_paged_decode_noalloc(int dtype, int batch, int num_qo_heads,
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc != NSLG_OK) return rc;
-  return launch_paged_decode_tc(batch, num_qo_heads, num_kv_heads, head_dim, q, q_stride, out,
+  return launch_paged_decode_tc(dtype, batch, num_qo_heads, num_kv_heads, head_dim, q, q_stride, out,
                                 out_stride, pool_k, pool_v, num_pages, kv_indptr, kv_indices,
                                 kv_last_page_len, sm_scale, scratch, NSLG_NOALLOC_SCRATCH_BYTES,
                                 dev_status, st);

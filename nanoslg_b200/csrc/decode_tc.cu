@@ -1,4 +1,4 @@
-// Split-KV GQA decode attention for bf16, page_size 16, head_dim 128 (or 64).
+// Split-KV GQA decode attention for bf16 or fp16, page_size 16, head_dim 128 (or 64).
 //
 // Work split. The pages of all sequences form one flat list (the CSR kv_indices,
 // kv_cache.py:598-615). CTA c of n takes the contiguous slice
@@ -47,8 +47,8 @@ constexpr int kMaxSmem = 232448;         // 227 KiB opt-in per CTA on sm_100
 constexpr int kSmemCsrBatch = 1024;      // batches up to this size keep the CSR in smem
 
 struct DecodeParams {
-  const __nv_bfloat16* q;
-  __nv_bfloat16* out;
+  const void* q;    // [B, hq, D] of the activation type T (bf16 or fp16)
+  void* out;
   const int32_t* indptr;
   const int32_t* indices;
   const int32_t* lpl;
@@ -93,7 +93,7 @@ struct Cfg {
   }
 };
 
-template <int HKV, int D>
+template <typename T, int HKV, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                      const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Q fragments (A operand, 16 rows = query heads h*G + r, r < G).
     uint32_t qa[KS][4];
     {
-      const __nv_bfloat16* qb = p.q + static_cast<int64_t>(b) * p.q_stride +
+      const T* qb = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.q_stride +
                                 static_cast<int64_t>(h) * G * D;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
@@ -305,8 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t addr = sb + C::box(j, 0, half, h) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
             uint32_t b00, b01, b10, b11;
             ldmatrix_x4(addr, b00, b01, b10, b11);
-            mma_bf16_16816(s[0], qa[ks], b00, b01);
-            mma_bf16_16816(s[1], qa[ks], b10, b11);
+            Mma16<T>::mma(s[0], qa[ks], b00, b01);
+            Mma16<T>::mma(s[1], qa[ks], b10, b11);
           }
         }
         // ---- mask the tail of the last page, online softmax
@@ -344,10 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           o[t][2] *= a1; o[t][3] *= a1;
         }
         uint32_t pa[4];
-        pa[0] = pack_bf16x2(ps[0][0], ps[0][1]);
-        pa[1] = pack_bf16x2(ps[0][2], ps[0][3]);
-        pa[2] = pack_bf16x2(ps[1][0], ps[1][1]);
-        pa[3] = pack_bf16x2(ps[1][2], ps[1][3]);
+        pa[0] = Mma16<T>::pack(ps[0][0], ps[0][1]);
+        pa[1] = Mma16<T>::pack(ps[0][2], ps[0][3]);
+        pa[2] = Mma16<T>::pack(ps[1][0], ps[1][1]);
+        pa[3] = Mma16<T>::pack(ps[1][2], ps[1][3]);
         // ---- O += P . V
         {
           const int mi = lane >> 3, r = lane & 7;
@@ -359,8 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t addr = sb + C::box(j, 1, half, h) + tok * 128 + ((ch ^ (tok & 7)) << 4);
             uint32_t v0, v1, v2, v3;
             ldmatrix_x4_trans(addr, v0, v1, v2, v3);
-            mma_bf16_16816(o[2 * qd], pa, v0, v1);
-            mma_bf16_16816(o[2 * qd + 1], pa, v2, v3);
+            Mma16<T>::mma(o[2 * qd], pa, v0, v1);
+            Mma16<T>::mma(o[2 * qd + 1], pa, v2, v3);
           }
         }
       }
@@ -390,12 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int hq = h * G + r;
           const float inv = rr ? inv1 : inv0;
           if (whole) {
-            __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride +
-                                static_cast<int64_t>(hq) * D;
+            T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride +
+                    static_cast<int64_t>(hq) * D;
 #pragma unroll
             for (int t = 0; t < NT; ++t)
               *reinterpret_cast<uint32_t*>(ob + t * 8 + tq * 2) =
-                  pack_bf16x2(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
+                  Mma16<T>::pack(o[t][rr * 2] * inv, o[t][rr * 2 + 1] * inv);
           } else {
             float* po = p.part_o + (slot * p.hq + hq) * D;
 #pragma unroll
@@ -446,8 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
           const int hq = h * G + r;
           if (whole) {
-            p.out[static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D + col] =
-                __float2bfloat16_rn(acc * inv);
+            static_cast<T*>(p.out)[static_cast<int64_t>(b) * p.out_stride +
+                                   static_cast<int64_t>(hq) * D + col] = Elem<T>::from_f(acc * inv);
           } else {
             p.part_o[(slot * p.hq + hq) * D + col] = acc * inv;
             if (j == 0 && e % DS == 0)
@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // partials' log-sum-exps in parallel (lane i: partial i, i + 32, ...) and the weighted
 // partial outputs are loaded four partials at a time, so the merge costs a few load
 // latencies however many CTAs the sequence spans.
-template <int D>
+template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int hq = blockIdx.x * 4 + warp;
@@ -480,10 +480,10 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
   const int64_t beg = p.indptr[b], end = p.indptr[b + 1];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (hq >= p.hq) return;
-  __nv_bfloat16* ob = p.out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
+  T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
   if (beg == end) {
 #pragma unroll
-    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(0.f);
+    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = Elem<T>::from_f(0.f);
     return;
   }
   const int n = num_ctas(total, p.grid);
@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
-    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(acc[e] * inv);
+    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = Elem<T>::from_f(acc[e] * inv);
     return;
   }
   float mx = -INFINITY;
@@ -565,11 +565,11 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
   for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
-  for (int e = 0; e < DV; ++e) ob[lane * DV + e] = __float2bfloat16_rn(acc[e] * inv);
+  for (int e = 0; e < DV; ++e) ob[lane * DV + e] = Elem<T>::from_f(acc[e] * inv);
 }
 
 // ------------------------------------------------------------------ host side
-template <int HKV, int D>
+template <typename T, int HKV, int D>
 int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
                  cudaStream_t stream) {
   using C = Cfg<HKV, D>;
@@ -583,7 +583,7 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
   p.stages = stages;
   const size_t smem =
       1024 + static_cast<size_t>(stages) * C::kStageBytes + 2 * stages * 8 + comb + csr;
-  auto kern = decode_tc_kernel<HKV, D>;
+  auto kern = decode_tc_kernel<T, HKV, D>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
@@ -601,16 +601,38 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  err = cudaLaunchKernelEx(&cfg, decode_merge_kernel<D>, p);
+  err = cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, D>, p);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("decode_merge: ") +
                                                               cudaGetErrorString(err));
   return check_launch("decode_merge");
 }
 
+template <typename T>
+int launch_for_type(int hkv, int d, const CUtensorMap& tk, const CUtensorMap& tv,
+                    DecodeParams p, cudaStream_t stream) {
+  if (d == 128) {
+    switch (hkv) {
+      case 1: return launch_typed<T, 1, 128>(tk, tv, p, stream);
+      case 2: return launch_typed<T, 2, 128>(tk, tv, p, stream);
+      case 4: return launch_typed<T, 4, 128>(tk, tv, p, stream);
+      case 8: return launch_typed<T, 8, 128>(tk, tv, p, stream);
+    }
+  } else if (d == 64) {
+    switch (hkv) {
+      case 1: return launch_typed<T, 1, 64>(tk, tv, p, stream);
+      case 2: return launch_typed<T, 2, 64>(tk, tv, p, stream);
+      case 4: return launch_typed<T, 4, 64>(tk, tv, p, stream);
+      case 8: return launch_typed<T, 8, 64>(tk, tv, p, stream);
+    }
+  }
+  return set_error(NSLG_ERR_UNSUPPORTED, "decode: unsupported head count / head_dim");
+}
+
 }  // namespace
 
 bool decode_tc_supported(int dtype, int hq, int hkv, int d, int page_size) {
-  return dtype == NSLG_DTYPE_BF16 && page_size == kPS && (d == 128 || d == 64) &&
+  return (dtype == NSLG_DTYPE_BF16 || dtype == NSLG_DTYPE_F16) && page_size == kPS &&
+         (d == 128 || d == 64) &&
          (hkv == 1 || hkv == 2 || hkv == 4 || hkv == 8) && hq % hkv == 0 && hq / hkv <= 16;
 }
 
@@ -619,8 +641,8 @@ int64_t decode_tc_workspace_bytes(int batch, int hq, int d) {
   return slots * hq * (static_cast<int64_t>(d) + 1) * 4 + 256;
 }
 
-int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int64_t q_stride,
-                           void* out, int64_t out_stride, const void* pool_k,
+int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const void* q,
+                           int64_t q_stride, void* out, int64_t out_stride, const void* pool_k,
                            const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
                            const int32_t* kv_indices, const int32_t* kv_last_page_len,
                            float sm_scale, void* workspace, int64_t workspace_bytes,
@@ -654,8 +676,8 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
   const int64_t slots = static_cast<int64_t>(batch) + grid;
   uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
   DecodeParams p{};
-  p.q = static_cast<const __nv_bfloat16*>(q);
-  p.out = static_cast<__nv_bfloat16*>(out);
+  p.q = q;
+  p.out = out;
   p.indptr = kv_indptr;
   p.indices = kv_indices;
   p.lpl = kv_last_page_len;
@@ -671,22 +693,9 @@ int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.status = status;
   p.box_all_heads = box_all;
-  if (d == 128) {
-    switch (hkv) {
-      case 1: return launch_typed<1, 128>(tk, tv, p, stream);
-      case 2: return launch_typed<2, 128>(tk, tv, p, stream);
-      case 4: return launch_typed<4, 128>(tk, tv, p, stream);
-      case 8: return launch_typed<8, 128>(tk, tv, p, stream);
-    }
-  } else if (d == 64) {
-    switch (hkv) {
-      case 1: return launch_typed<1, 64>(tk, tv, p, stream);
-      case 2: return launch_typed<2, 64>(tk, tv, p, stream);
-      case 4: return launch_typed<4, 64>(tk, tv, p, stream);
-      case 8: return launch_typed<8, 64>(tk, tv, p, stream);
-    }
-  }
-  return set_error(NSLG_ERR_UNSUPPORTED, "decode: unsupported head count / head_dim");
+  if (dtype == NSLG_DTYPE_F16) return launch_for_type<__half>(hkv, d, tk, tv, p, stream);
+  return launch_for_type<__nv_bfloat16>(hkv, d, tk, tv, p, stream);
 }
+
 
 }  // namespace nslg

@@ -18,6 +18,9 @@ int set_error(int code, const std::string& msg);
 // nslg_last_error() returns "" after a call that succeeded).
 void clear_error();
 
+// Bytes per element of an NSLG_DTYPE_* code (4 for float32, 2 for bfloat16 / float16).
+inline int dtype_bytes(int dtype) { return dtype == NSLG_DTYPE_F32 ? 4 : 2; }
+
 // Turns a pending launch error into NSLG_ERR_CUDA with the kernel's name.
 int check_launch(const char* what);
 
@@ -46,7 +49,9 @@ int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, 
   return check_launch(what);
 }
 
-// 3-D tiled bf16 tensor map with 128-byte swizzle (strides in bytes, dims innermost first).
+// 3-D tiled tensor map of 2-byte elements (bf16 and fp16 alike: TMA moves bytes, and its
+// out-of-bounds fill, 0, is +0.0 in both) with 128-byte swizzle (strides in bytes, dims
+// innermost first).
 int encode_tiled_3d_bf16(CUtensorMap* out, const void* base, uint64_t d0, uint64_t d1,
                          uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                          uint32_t box0, uint32_t box1, uint32_t box2);
@@ -71,7 +76,7 @@ int launch_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int6
 int launch_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t gu_stride,
                     void* out, int64_t out_stride, cudaStream_t stream);
 
-// CUDA-core paged attention (any page size, head_dim <= 256, fp32 or bf16): decode is
+// CUDA-core paged attention (any page size, head_dim <= 256, fp32, bf16 or fp16): decode is
 // the qo_len == 1 case.
 int launch_paged_attention_simt(int dtype, int batch, int hq, int hkv, int d, int page_size,
                                 const void* q, int64_t q_stride, void* out,
@@ -82,19 +87,22 @@ int launch_paged_attention_simt(int dtype, int batch, int hq, int hkv, int d, in
                                 const int32_t* kv_last_page_len, float sm_scale, int causal,
                                 uint32_t* status, cudaStream_t stream);
 
-// TMA-fed split-KV decode for bf16, page_size 16, head_dim 128.
+// TMA-fed split-KV decode for bf16 / fp16, page_size 16, head_dim 128 or 64.
 bool decode_tc_supported(int dtype, int hq, int hkv, int d, int page_size);
 int64_t decode_tc_workspace_bytes(int batch, int hq, int d);
-int launch_paged_decode_tc(int batch, int hq, int hkv, int d, const void* q, int64_t q_stride,
+int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const void* q,
+                           int64_t q_stride,
                            void* out, int64_t out_stride, const void* pool_k,
                            const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
                            const int32_t* kv_indices, const int32_t* kv_last_page_len,
                            float sm_scale, void* workspace, int64_t workspace_bytes,
                            uint32_t* status, cudaStream_t stream);
 
-// tcgen05 causal prefill for bf16, page_size 16, head_dim 128, group <= 16 dividing 128.
+// tcgen05 causal prefill for bf16 / fp16, page_size 16, head_dim 128, group <= 16
+// dividing 128.
 bool prefill_tc_supported(int dtype, int hq, int hkv, int d, int page_size);
-int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q_stride,
+int launch_paged_prefill_tc(int dtype, int batch, int hq, int hkv, const void* q,
+                            int64_t q_stride,
                             int64_t q_rows, void* out, int64_t out_stride,
                             const int32_t* qo_indptr, const int32_t* q_row_start, int max_qo_len,
                             const void* pool_k, const void* pool_v, int64_t num_pages,

@@ -1,5 +1,5 @@
 // Causal paged prefill / extend attention on the 5th-generation tensor cores
-// (tcgen05.mma, accumulators in TMEM), bf16, page_size 16, head_dim 128.
+// (tcgen05.mma, accumulators in TMEM), bf16 or fp16, page_size 16, head_dim 128.
 //
 // Work item. Two adjacent query tiles ("halves" A and B) of one sequence b and one kv
 // head h, each 128 rows: T = 128/G new tokens times the G query heads h*G .. h*G+G-1
@@ -30,11 +30,12 @@
 //                   the other way round).
 //   softmax WG X    (two warpgroups, one per half) thread r owns TMEM lane r = row r:
 //                   loads S_X(t), masks only on tiles that cross the causal or length
-//                   edge, keeps a running max (log2 domain) and sum, writes P as bf16 over
-//                   S, rescales O_X in TMEM only when the max grows by more than 8 (2^8
-//                   headroom for P in bf16).
+//                   edge, keeps a running max (log2 domain) and sum, writes P in the
+//                   activation type (bf16 or fp16) over S, rescales O_X in TMEM only when
+//                   the max grows by more than 8 (2^8 headroom for P, within range for
+//                   both types).
 //   epilogue        softmax WG X reads O_X out of TMEM (then hands O_X back to the MMA
-//                   warp), scales by 1/l and writes bf16 rows into its half of the item's
+//                   warp), scales by 1/l and writes rows of the activation type into its half of the item's
 //                   Q slot (dead once the item's last S is done), in the 128-byte swizzled
 //                   layout of the Q load;
 //   store warp      writes each staged half to `out` with two TMA stores (the Q box
@@ -75,7 +76,7 @@ constexpr int kRing = 3;                        // K ring and V ring depth
 constexpr int kSmemBytes = 1024 + 2 * kQSlot + 2 * kRing * kTile + 512;
 
 struct PrefillParams {
-  __nv_bfloat16* out;
+  void* out;        // rows of the activation type T (bf16 or fp16)
   const int32_t* qo_indptr;
   const int32_t* q_row_start;
   const int32_t* indptr;
@@ -101,9 +102,10 @@ __host__ __device__ constexpr uint32_t smem_desc_hi(uint32_t sbo) {
   return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
 }
 
-// kind::f16 instruction descriptor: f32 accumulate, bf16 A and B, M = 128.
-__host__ __device__ constexpr uint32_t idesc_bf16(int n, bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+// kind::f16 instruction descriptor: f32 accumulate, A and B of operand format `fmt` (0
+// f16, 1 bf16; one type for both operands), M = 128.
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, int n, bool b_mn_major) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          ((static_cast<uint32_t>(n) >> 3) << 17) | ((128u >> 4) << 24);
 }
 
@@ -317,6 +319,7 @@ __device__ __forceinline__ bool load_item(const PrefillParams& p, int item, Item
 // per use of their buffer (parity (t >> 1) & 1); Q-slot barriers (q_full, q_empty,
 // o_staged) once per use of their slot (item n uses slot n & 1, parity (n >> 1) & 1);
 // o_free once per item.
+template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k,
@@ -490,8 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdescS = idesc_bf16(kBN, false);
-      constexpr uint32_t kIdescO = idesc_bf16(kD, true);
+      constexpr uint32_t kIdescS = idesc_f16(Mma16<T>::kFormat, kBN, false);
+      constexpr uint32_t kIdescO = idesc_f16(Mma16<T>::kFormat, kD, true);
       constexpr uint32_t kDescHi = smem_desc_hi(1024);
       // descriptor low words of the first Q slot, K slot and V slot (K-major Q and K:
       // LBO 16; MN-major V: LBO = the 64-dim half stride)
@@ -600,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int r = idx >> 4, c = idx & 15, cc = c & 7;
             const uint4 v = *reinterpret_cast<const uint4*>(stage + (c >> 3) * kQHalf + r * 128 +
                                                             ((cc ^ (r & 7)) << 4));
-            __nv_bfloat16* dst = p.out + static_cast<int64_t>(hx.row0 + r / G) * p.out_stride +
+            T* dst = static_cast<T*>(p.out) + static_cast<int64_t>(hx.row0 + r / G) * p.out_stride +
                                  static_cast<int64_t>(it.h * G + r % G) * kD + c * 8;
             *reinterpret_cast<uint4*>(dst) = v;
           }
@@ -687,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float p0 = fast_exp2(fmaf(s[c], sl, neg));
           const float p1 = fast_exp2(fmaf(s[c + 1], sl, neg));
           rs4[(c >> 1) & 3] += p0 + p1;
-          pk[c / 2] = pack_bf16x2(p0, p1);
+          pk[c / 2] = Mma16<T>::pack(p0, p1);
         }
         const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         // O may only be rescaled once P(t-1).V(t-1) is done (warp-uniform branch: the
@@ -742,10 +745,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 8; ++c) {
           const float* src = c < 4 ? &o0[c * 8] : &o1[(c - 4) * 8];
           uint4 pkt;
-          pkt.x = pack_bf16x2(src[0] * inv, src[1] * inv);
-          pkt.y = pack_bf16x2(src[2] * inv, src[3] * inv);
-          pkt.z = pack_bf16x2(src[4] * inv, src[5] * inv);
-          pkt.w = pack_bf16x2(src[6] * inv, src[7] * inv);
+          pkt.x = Mma16<T>::pack(src[0] * inv, src[1] * inv);
+          pkt.y = Mma16<T>::pack(src[2] * inv, src[3] * inv);
+          pkt.z = Mma16<T>::pack(src[4] * inv, src[5] * inv);
+          pkt.w = Mma16<T>::pack(src[6] * inv, src[7] * inv);
           *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = pkt;
         }
       }
@@ -769,13 +772,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 bool prefill_tc_supported(int dtype, int hq, int hkv, int d, int page_size) {
-  if (dtype != NSLG_DTYPE_BF16 || d != kD || page_size != kPS) return false;
+  if ((dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16) || d != kD || page_size != kPS)
+    return false;
   if (hq % hkv) return false;
   const int g = hq / hkv;
   return g >= 1 && g <= 16 && (kBM % g) == 0;
 }
 
-int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q_stride,
+int launch_paged_prefill_tc(int dtype, int batch, int hq, int hkv, const void* q,
+                            int64_t q_stride,
                             int64_t q_rows, void* out, int64_t out_stride,
                             const int32_t* qo_indptr, const int32_t* q_row_start, int max_qo_len,
                             const void* pool_k, const void* pool_v, int64_t num_pages,
@@ -801,7 +806,7 @@ int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q
                             static_cast<uint64_t>(out_stride) * 2, 64, G, tpt);
   if (rc != NSLG_OK) return rc;
   PrefillParams p{};
-  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out = out;
   p.qo_indptr = qo_indptr;
   p.q_row_start = q_row_start;
   p.indptr = kv_indptr;
@@ -817,8 +822,9 @@ int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q
   p.causal = causal;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.status = status;
-  cudaError_t err = cudaFuncSetAttribute(prefill_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  auto kern = dtype == NSLG_DTYPE_F16 ? prefill_tc_kernel<__half> : prefill_tc_kernel<__nv_bfloat16>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBytes);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
   const int64_t pairs = ((max_qo_len + tpt - 1) / tpt + 1) / 2;
   const int64_t per_group = (pairs + 1) / 2;              // units per (sequence, kv head)
@@ -827,8 +833,7 @@ int launch_paged_prefill_tc(int batch, int hq, int hkv, const void* q, int64_t q
   p.n_items = static_cast<int>(2 * units);
   p.units_per_group = static_cast<int>(per_group);
   const int64_t grid = units < static_cast<int64_t>(sm_count()) ? units : sm_count();
-  prefill_tc_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tq, tk, tv, to,
-                                                                                   p);
+  kern<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, p);
   return check_launch("prefill_tc");
 }
 

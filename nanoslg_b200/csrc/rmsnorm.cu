@@ -92,12 +92,15 @@ int launch_rmsnorm_residual(int dtype, int rows, int hidden, const void* x, int6
                             void* out, int64_t out_stride, float eps, cudaStream_t stream) {
   if (rows == 0) return NSLG_OK;
   NormParams p{x, residual, weight, out, x_stride, residual_stride, out_stride, rows, hidden, eps};
-  const int esz = dtype == NSLG_DTYPE_BF16 ? 2 : 4;
+  const int esz = dtype_bytes(dtype);
   const int nv = hidden * esz / 16;
   int threads = 32;
   while (threads < nv && threads < 256) threads *= 2;
   if (dtype == NSLG_DTYPE_BF16)
     return launch_pdl("rmsnorm_residual", rmsnorm_residual_kernel<__nv_bfloat16>, dim3(rows),
+                      dim3(threads), 0, stream, p);
+  if (dtype == NSLG_DTYPE_F16)
+    return launch_pdl("rmsnorm_residual", rmsnorm_residual_kernel<__half>, dim3(rows),
                       dim3(threads), 0, stream, p);
   return launch_pdl("rmsnorm_residual", rmsnorm_residual_kernel<float>, dim3(rows),
                     dim3(threads), 0, stream, p);

@@ -286,7 +286,7 @@ int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, con
     return launch_pdl("rope_kv_append", rope_kv_append_bf16_kernel<64>, grid, dim3(threads), 0,
                       stream, p);
   }
-  const int esz = dtype == NSLG_DTYPE_BF16 ? 2 : 4;
+  const int esz = dtype_bytes(dtype);
   const int vec = 16 / esz;
   const int per_tok = (q_out ? hq * (d / 2 / vec) : 0) + hkv * (d / 2 / vec) + hkv * (d / vec);
   const int64_t total = static_cast<int64_t>(num_tokens) * per_tok;
@@ -297,6 +297,9 @@ int launch_rope_kv_append(int dtype, int num_tokens, int hq, int hkv, int d, con
   if (dtype == NSLG_DTYPE_BF16)
     return launch_pdl("rope_kv_append", rope_kv_append_kernel<__nv_bfloat16>, grid,
                       dim3(threads), 0, stream, p);
+  if (dtype == NSLG_DTYPE_F16)
+    return launch_pdl("rope_kv_append", rope_kv_append_kernel<__half>, grid, dim3(threads), 0,
+                      stream, p);
   return launch_pdl("rope_kv_append", rope_kv_append_kernel<float>, grid, dim3(threads), 0,
                     stream, p);
 }

@@ -339,12 +339,12 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
                                          const void* weight, void* out, int64_t out_stride,
                                          float eps, int64_t timeout_ns, uint32_t* dev_status,
                                          void* stream) {
-  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F32)
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16 && dtype != NSLG_DTYPE_F32)
     return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad dtype");
   if (world < 2 || world > NSLG_TP_MAX_WORLD || rank < 0 || rank >= world)
     return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: need 2 <= world <= 8 and 0 <= rank < world");
   if (rows < 0 || hidden <= 0) return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad shape");
-  const int esz = dtype == NSLG_DTYPE_BF16 ? 2 : 4;
+  const int esz = dtype_bytes(dtype);
   if ((static_cast<int64_t>(hidden) * esz) % 16)
     return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: hidden * element size must be a multiple of 16 bytes");
   if (static_cast<int64_t>(hidden) * esz > 16ll * kThreads * kVecPerThread)
@@ -400,6 +400,9 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == NSLG_DTYPE_BF16)
     return launch_pdl("tp_allreduce_rmsnorm", tp_allreduce_rmsnorm_kernel<__nv_bfloat16>,
+                      dim3(kGrid), dim3(kThreads), 0, st, p);
+  if (dtype == NSLG_DTYPE_F16)
+    return launch_pdl("tp_allreduce_rmsnorm", tp_allreduce_rmsnorm_kernel<__half>,
                       dim3(kGrid), dim3(kThreads), 0, st, p);
   return launch_pdl("tp_allreduce_rmsnorm", tp_allreduce_rmsnorm_kernel<float>, dim3(kGrid),
                     dim3(kThreads), 0, st, p);

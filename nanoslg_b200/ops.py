@@ -10,14 +10,14 @@ import torch
 
 from . import _native as N
 
-_DTYPES = {torch.bfloat16: N.DTYPE_BF16, torch.float32: N.DTYPE_F32}
+_DTYPES = {torch.bfloat16: N.DTYPE_BF16, torch.float16: N.DTYPE_F16, torch.float32: N.DTYPE_F32}
 
 
 def _dtype_code(t):
     try:
         return _DTYPES[t.dtype]
     except KeyError:
-        raise TypeError(f"nanoslg_b200 kernels support bfloat16 and float32, got {t.dtype}")
+        raise TypeError(f"nanoslg_b200 kernels support bfloat16, float16 and float32, got {t.dtype}")
 
 
 def _need_cuda(*ts):

@@ -30,8 +30,8 @@ class PeerAllReduce:
                  timeout_s=10.0):
         if not 2 <= world <= N.TP_MAX_WORLD:
             raise ValueError(f"PeerAllReduce: world must be in [2, {N.TP_MAX_WORLD}]")
-        if dtype not in (torch.bfloat16, torch.float32):
-            raise TypeError("PeerAllReduce supports bfloat16 and float32 activations")
+        if dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise TypeError("PeerAllReduce supports bfloat16, float16 and float32 activations")
         self.group, self.rank, self.world = group, rank, world
         self.device = torch.device(device)
         self.max_rows, self.hidden, self.dtype = max_rows, hidden, dtype

@@ -518,6 +518,64 @@ def rope_norm_cases(M):
     return out
 
 
+def fp16_cases(kvc, M):
+    """float16 activations (worker.py:22-26 allows them): the contiguous path's attention
+    (its mask fills with -65504 in fp16, kv_cache.py:208), RoPE and RMSNorm, recorded the
+    same way as the bf16 cases."""
+    g = torch.Generator().manual_seed(13)
+    out = {"attention": []}
+    specs = [("f16_gqa4", 8, 2, 128, [1, 12, 29, 40], 2, 0),
+             ("f16_extend", 8, 2, 128, [7, 20], 1, 5),
+             ("f16_gqa4_d64", 8, 2, 64, [3, 17], 2, 0)]
+    dt = torch.float16
+    for name, hq, hkv, d, lens, ndec, ext in specs:
+        B = len(lens)
+        cfg = kvc.KVCacheConfig(num_layers=2, num_kv_heads=hkv, num_qo_heads=hq,
+                                head_dim=d, max_batch_size=B, max_seq_len=128,
+                                dtype=dt, device=torch.device("cpu"), backend="contiguous")
+        mgr = kvc.ContiguousKVCache(cfg)
+        sids = [f"s{i}" for i in range(B)]
+        for s in sids:
+            mgr.allocate_sequence(s)
+        steps = []
+        plan = [("prefill", list(lens))]
+        if ext:
+            plan.append(("prefill", [ext] * B))
+        plan += [("decode", [1] * B)] * ndec
+        for kind, counts in plan:
+            mx = max(counts)
+            offs = [mx - c for c in counts]
+            ctx = mgr.begin_forward(sids, counts, offs)
+            rec = {"kind": kind, "counts": counts, "offsets": offs,
+                   "start_positions": list(ctx.start_positions), "layers": []}
+            for layer in range(2):
+                q = torch.randn(B, mx, hq, d, generator=g).to(dt)
+                k = torch.randn(B, mx, hkv, d, generator=g).to(dt)
+                v = torch.randn(B, mx, hkv, d, generator=g).to(dt)
+                o = ctx.attend(layer, q, k, v, hq, hkv)
+                rec["layers"].append({"q": q, "k": k, "v": v, "out": o})
+            rec["positions"] = ctx.get_position_ids(mx).clone()
+            mgr.end_forward(ctx)
+            steps.append(rec)
+        out["attention"].append({"name": name, "dtype": str(dt), "hq": hq, "hkv": hkv, "d": d,
+                                 "lens": lens, "steps": steps})
+    cos, sin = M.precompute_rope_frequencies(128, 4096, 500000.0, SimpleNamespace())
+    x = torch.randn(3, 5, 4, 128, generator=g).to(dt)
+    pos = torch.randint(0, 4096, (3, 5), generator=g)
+    out["rope"] = {"x": x, "pos": pos, "y": M.apply_rotary_emb(x, cos[pos], sin[pos])}
+    h = 256
+    xs = (torch.randn(7, h, generator=g) * 3).to(dt)
+    w = (1 + 0.1 * torch.randn(h, generator=g)).to(dt)
+    norm = M.RMSNorm(h, eps=1e-5).to(dt)
+    norm.weight.data.copy_(w)
+    with torch.no_grad():
+        out["rmsnorm"] = {"x": xs, "w": w, "eps": 1e-5, "y": norm(xs)}
+        r = torch.randn(7, h, generator=g).to(dt)
+        hsum = xs + r
+        out["addnorm"] = {"x": xs, "r": r, "w": w, "eps": 1e-5, "h": hsum, "y": norm(hsum)}
+    return out
+
+
 # ----------------------------------------------------------------------------------------
 # tiny Llama (config C1)
 # ----------------------------------------------------------------------------------------
@@ -642,6 +700,8 @@ def main():
                     help="write paged_scenarios.json only")
     ap.add_argument("--only-kv8", action="store_true",
                     help="write tiny_llama_kv8.json only")
+    ap.add_argument("--only-fp16", action="store_true",
+                    help="write fp16_cases.pt only")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import nanoslg.kv_cache as kvc
@@ -649,6 +709,9 @@ def main():
     from nanoslg.parallel import ParallelContext, ParallelConfig, ParallelMode
 
     torch.set_num_threads(1)
+    if args.only_fp16:
+        torch.save(fp16_cases(kvc, M), os.path.join(HERE, "fp16_cases.pt"))
+        return
     if args.only_kv8:
         tb = tiny_llama_batch(kvc, M, ParallelContext, ParallelConfig, ParallelMode)
         with open(os.path.join(HERE, "tiny_llama_kv8.json"), "w") as f:
@@ -668,6 +731,7 @@ def main():
         return
     torch.save(attention_cases(kvc), os.path.join(HERE, "attention_cases.pt"))
     torch.save(rope_norm_cases(M), os.path.join(HERE, "rope_norm.pt"))
+    torch.save(fp16_cases(kvc, M), os.path.join(HERE, "fp16_cases.pt"))
     tl = tiny_llama(kvc, M, ParallelContext, ParallelConfig, ParallelMode)
     with open(os.path.join(HERE, "tiny_llama.json"), "w") as f:
         json.dump(tl, f, indent=1)

@@ -1,6 +1,6 @@
 """The B200 CacheContext / model path on the GPU against the reference's recorded
-outputs (tests/golden): contiguous-SDPA attention cases and the tiny fp32 Llama's greedy
-tokens."""
+outputs (tests/golden): contiguous-SDPA attention cases (fp32, bf16 and fp16) and the
+tiny fp32 Llama's greedy tokens."""
 import json
 import os
 from types import SimpleNamespace
@@ -16,7 +16,10 @@ from nanoslg_b200.kv_cache import B200PagedKVCache, KVCacheConfig, create_cache_
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda:0")
-ATT = torch.load(os.path.join(GOLDEN, "attention_cases.pt"))
+ATT = torch.load(os.path.join(GOLDEN, "attention_cases.pt")) + \
+    torch.load(os.path.join(GOLDEN, "fp16_cases.pt"))["attention"]
+DTYPES = {"torch.float32": torch.float32, "torch.bfloat16": torch.bfloat16,
+          "torch.float16": torch.float16}
 
 
 @pytest.fixture(autouse=True)
@@ -28,8 +31,8 @@ def _clean_status():
 
 @pytest.mark.parametrize("case", ATT, ids=[c["name"] for c in ATT])
 def test_context_attend_matches_reference(case):
-    dt = torch.float32 if case["dtype"] == "torch.float32" else torch.bfloat16
-    tol = dict(rtol=1e-2, atol=2e-2) if dt == torch.bfloat16 else dict(rtol=1e-4, atol=1e-5)
+    dt = DTYPES[case["dtype"]]
+    tol = dict(rtol=1e-4, atol=1e-5) if dt == torch.float32 else dict(rtol=1e-2, atol=2e-2)
     B = len(case["lens"])
     cfg = KVCacheConfig(num_layers=2, num_kv_heads=case["hkv"], num_qo_heads=case["hq"],
                         head_dim=case["d"], page_size=16, max_pages=64, dtype=dt, device=DEV)

@@ -61,13 +61,15 @@ def test_ops_refuse_cpu_tensors(lib):
 
 
 def test_ops_refuse_unsupported_dtypes():
-    """bf16 and fp32 only: fp16 (and anything else) is refused, never converted."""
+    """bf16, fp16 and fp32 (the reference's activation types): anything else is refused,
+    never converted."""
     import torch
     from nanoslg_b200 import ops
     assert ops._dtype_code(torch.zeros(1, dtype=torch.bfloat16)) == N.DTYPE_BF16
+    assert ops._dtype_code(torch.zeros(1, dtype=torch.float16)) == N.DTYPE_F16
     assert ops._dtype_code(torch.zeros(1, dtype=torch.float32)) == N.DTYPE_F32
-    for dt in (torch.float16, torch.float64, torch.int32):
-        with pytest.raises(TypeError, match="bfloat16 and float32"):
+    for dt in (torch.float64, torch.int32, torch.float8_e4m3fn):
+        with pytest.raises(TypeError, match="bfloat16, float16 and float32"):
             ops._dtype_code(torch.zeros(1, dtype=dt))
 
 

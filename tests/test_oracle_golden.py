@@ -13,13 +13,17 @@ from oracle.rope_norm import apply_rotary, rmsnorm, rope_table
 
 ATT = torch.load(os.path.join(GOLDEN, "attention_cases.pt"))
 RN = torch.load(os.path.join(GOLDEN, "rope_norm.pt"))
+F16 = torch.load(os.path.join(GOLDEN, "fp16_cases.pt"))
+ALL_ATT = ATT + F16["attention"]
+DTYPES = {"torch.float32": torch.float32, "torch.bfloat16": torch.bfloat16,
+          "torch.float16": torch.float16}
 with open(os.path.join(GOLDEN, "paged_scenarios.json")) as f:
     SCEN = json.load(f)
 
 
-@pytest.mark.parametrize("case", ATT, ids=[c["name"] for c in ATT])
+@pytest.mark.parametrize("case", ALL_ATT, ids=[c["name"] for c in ALL_ATT])
 def test_contiguous_oracle_matches_reference(case):
-    dt = torch.float32 if case["dtype"] == "torch.float32" else torch.bfloat16
+    dt = DTYPES[case["dtype"]]
     B = len(case["lens"])
     orc = ContiguousOracle(2, B, 128, case["hkv"], case["d"], dt)
     for step in case["steps"]:
@@ -33,15 +37,15 @@ def test_contiguous_oracle_matches_reference(case):
             torch.testing.assert_close(out[valid], exp[valid], rtol=0, atol=0)
 
 
-@pytest.mark.parametrize("case", ATT, ids=[c["name"] for c in ATT])
+@pytest.mark.parametrize("case", ALL_ATT, ids=[c["name"] for c in ALL_ATT])
 def test_per_sequence_formulation_matches_reference(case):
     """attend_sequences (used for large GPU parity cases) against the reference's
     outputs, at the north-star tolerance."""
-    dt = torch.float32 if case["dtype"] == "torch.float32" else torch.bfloat16
+    dt = DTYPES[case["dtype"]]
     B = len(case["lens"])
     kh = [[torch.zeros(0, case["hkv"], case["d"], dtype=dt) for _ in range(B)] for _ in range(2)]
     vh = [[torch.zeros(0, case["hkv"], case["d"], dtype=dt) for _ in range(B)] for _ in range(2)]
-    tol = dict(rtol=1e-2, atol=2e-2) if dt == torch.bfloat16 else dict(rtol=1e-4, atol=1e-5)
+    tol = dict(rtol=1e-4, atol=1e-5) if dt == torch.float32 else dict(rtol=1e-2, atol=2e-2)
     for step in case["steps"]:
         for li, lay in enumerate(step["layers"]):
             qs = []
@@ -92,6 +96,19 @@ def test_rope_and_rmsnorm_match_reference(dt):
     g = RN[f"rmsnorm_{dt}"]
     torch.testing.assert_close(rmsnorm(g["x"], g["w"], g["eps"]), g["y"], rtol=0, atol=0)
     g = RN[f"addnorm_{dt}"]
+    h = g["x"] + g["r"]
+    torch.testing.assert_close(h, g["h"], rtol=0, atol=0)
+    torch.testing.assert_close(rmsnorm(h, g["w"], g["eps"]), g["y"], rtol=0, atol=0)
+
+
+def test_fp16_rope_and_rmsnorm_match_reference():
+    cos, sin = rope_table(128, 4096, 500000.0)
+    g = F16["rope"]
+    y = apply_rotary(g["x"], cos[g["pos"]], sin[g["pos"]])
+    torch.testing.assert_close(y, g["y"], rtol=0, atol=0)
+    g = F16["rmsnorm"]
+    torch.testing.assert_close(rmsnorm(g["x"], g["w"], g["eps"]), g["y"], rtol=0, atol=0)
+    g = F16["addnorm"]
     h = g["x"] + g["r"]
     torch.testing.assert_close(h, g["h"], rtol=0, atol=0)
     torch.testing.assert_close(rmsnorm(h, g["w"], g["eps"]), g["y"], rtol=0, atol=0)
