@@ -341,6 +341,69 @@ def run_prefill_kernel(device, reps=10, batch=64, prompt=512):
             "peak_source": src, "algorithmic_flops": flops}
 
 
+def run_decode_model_shapes(device, reps=10, layers=32):
+    """Decode attention at the Llama-3.1-8B model's decode shapes, as the model runs it:
+    ``layers`` layers, each with its own pool (so no layer's K/V is still in L2 from the
+    last), one decode call per layer captured back to back in a CUDA graph, replayed
+    ``reps`` times (CUDA events). Cases: batch 64 with contexts U[512, 640] and batch 1
+    with a 512-token context, at TP=1 (32/8 heads) and at the TP=8 shard (4/1 heads).
+    Algorithmic bytes per layer: every cached K and V byte, q in, out, and the page ids."""
+    from nanoslg_b200 import ops
+    peak, src = _hbm_peak()
+    g = torch.Generator().manual_seed(5)
+    res = {}
+    for name, batch, lo, hi, hq, hkv in (("tp1_batch64", 64, 512, 640, 32, 8),
+                                         ("tp1_batch1", 1, 512, 512, 32, 8),
+                                         ("tp8_batch64", 64, 512, 640, 4, 1),
+                                         ("tp8_batch1", 1, 512, 512, 4, 1)):
+        lens = torch.randint(lo, hi + 1, (batch,), generator=g).tolist()
+        npg = [-(-n // PS) for n in lens]
+        pages = sum(npg) + 1
+        indptr = torch.tensor([0] + torch.cumsum(torch.tensor(npg), 0).tolist(),
+                              dtype=torch.int32, device=device)
+        lpl = torch.tensor([n - (p - 1) * PS for n, p in zip(lens, npg)], dtype=torch.int32,
+                           device=device)
+        pools = []
+        for _ in range(layers):
+            idx = (torch.randperm(pages - 1, generator=g)[:sum(npg)] + 1).to(torch.int32)
+            pk = torch.randn(pages, PS, hkv, D, device=device).to(torch.bfloat16)
+            pv = torch.randn(pages, PS, hkv, D, device=device).to(torch.bfloat16)
+            pools.append((pk, pv, idx.to(device)))
+        q = torch.randn(batch, hq, D, device=device).to(torch.bfloat16)
+        outs = [torch.empty_like(q) for _ in range(layers)]
+        scale = 1.0 / math.sqrt(D)
+
+        def step():
+            for (pk, pv, idx), o in zip(pools, outs):
+                ops.paged_decode(q, pk, pv, indptr, idx, lpl, scale, out=o)
+
+        step()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms_layer = e0.elapsed_time(e1) / reps / layers
+        ops.check_device_status(device)
+        nbytes = (sum(lens) * hkv * D * 2 * 2 + 2 * batch * hq * D * 2 + 4 * sum(npg)
+                  + 4 * (2 * batch + 1))
+        gbs = nbytes / (ms_layer / 1e3) / 1e9
+        res[name] = {"batch": batch, "ctx": f"U[{lo},{hi}]", "heads": f"{hq}/{hkv}",
+                     "us_per_layer": ms_layer * 1e3, "algorithmic_bytes_per_layer": nbytes,
+                     "gbs": gbs, "frac": gbs / peak}
+        del graph, pools, outs
+        torch.cuda.empty_cache()
+    return {"workload": "decode attention at the 8B decode shapes, 32 layers per CUDA graph",
+            "peak_gbs": peak, "peak_source": src, **res}
+
+
 def _hbm_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -953,13 +1016,14 @@ def main():
                     help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
     ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce",
-                                       "elementwise", "e2e", "parity"],
+                                       "elementwise", "e2e", "parity", "decode-shapes"],
                     default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg; elementwise: the RoPE + "
                          "KV-append and RMSNorm + residual kernels at the C3 prefill shape; "
                          "e2e: only the two end-to-end legs (one and two steps in flight); "
-                         "parity: only the sharded-path token / reduction checks")
+                         "parity: only the sharded-path token / reduction checks; "
+                         "decode-shapes: decode attention at the 8B model's decode shapes")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -1032,6 +1096,13 @@ def main():
         if rank == 0:
             print(json.dumps({"case": "prefill only", "prefill_attention":
                               run_prefill_kernel(device)}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
+    if a.only == "decode-shapes":
+        if rank == 0:
+            print(json.dumps({"case": "decode shapes only", "decode_model_shapes":
+                              run_decode_model_shapes(device)}), flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
         return 0
@@ -1131,6 +1202,7 @@ def main():
             "clocks": kr["clocks"]}
     line["parity"] = parity
     line["prefill_attention"] = run_prefill_kernel(device) if rank == 0 else None
+    line["decode_model_shapes"] = run_decode_model_shapes(device) if rank == 0 else None
     if world > 1:
         torch.distributed.barrier()
     if not a.no_model:

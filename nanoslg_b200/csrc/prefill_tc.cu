@@ -7,11 +7,12 @@
 // so every K/V byte brought on chip feeds two 128-row MMAs. Q arrives by TMA as
 // [T tok x G heads x 64 dims] boxes straight out of the caller's [rows, Hq, D] tensor (no
 // packing: sequence b's rows start at q_row_start[b]). A persistent grid (one CTA per
-// SM) walks the items in units of two (a long causal span, then a short one, of the
-// same sequence and kv head: equal work per unit, and the units of one (sequence, kv
-// head) on neighbouring CTAs share its K/V through L2); TMEM, barriers and the TMA
-// pipeline carry across items, and the next item's Q is loaded while the current one
-// runs.
+// SM) walks the items, longest causal spans first (CTA c takes items c, c + grid, ...);
+// TMEM, barriers and the TMA pipeline carry across items, and the next item's Q is
+// loaded while the current one runs. (Dealing the items instead in equal-work units of
+// a long and a short span of one (sequence, kv head) on neighbouring CTAs, so that they
+// share its K/V through L2, measured 0.315 ms against 0.264 ms at the 64 x 512 bench
+// shape, and the K/V re-reads this order causes are not what bounds the kernel.)
 //
 // Pipeline over kv tiles of 64 tokens (4 pages), t counting every tile of the CTA:
 //   producer warp   TMA: Q of the next item (two Q slots), and per page and 64-dim half
@@ -83,7 +84,7 @@ struct PrefillParams {
   const int32_t* indices;
   const int32_t* lpl;
   int64_t out_stride, num_pages;
-  int batch, hq, hkv, group, tokens_per_tile, causal, n_items, units_per_group;
+  int batch, hq, hkv, group, tokens_per_tile, causal, n_items;
   float scale_log2;
   uint32_t* status;
 };
@@ -240,31 +241,20 @@ struct Item {
 // (finish_item), so the loads' latency overlaps the current item instead of delaying
 // the first MMA of the next one.
 struct ItemLoads {
-  int b, h, k, which;
+  int b, h, pk_rev;
   int qo0, qo1, ip0, ip1, lpl, rs;
 };
-
-// Item ids. The query-tile pairs of one (sequence, kv head) are dealt out as units of
-// two: unit k holds pair npairs-1-k (the long causal span, first) and pair k (the short
-// one), so every unit of a sequence costs the same number of kv tiles (npairs + 1 for
-// a prompt without a cached prefix). Item id = 2 * unit + which; units are numbered
-// (sequence, kv head)-major, so the units of one (sequence, kv head) go to neighbouring
-// CTAs, start together, and stream the same K/V tiles at about the same time (each K/V
-// byte then comes from DRAM about once and from L2 for the other units). CTA c takes
-// units c, c + grid, c + 2 * grid, ..., each unit's two items back to back.
-__device__ __forceinline__ int first_item() { return 2 * static_cast<int>(blockIdx.x); }
-__device__ __forceinline__ int next_item_id(int item) {
-  return (item & 1) ? item - 1 + 2 * static_cast<int>(gridDim.x) : item + 1;
-}
+// CTA c takes items c, c + grid, c + 2 grid, ...
+__device__ __forceinline__ int first_item() { return static_cast<int>(blockIdx.x); }
+__device__ __forceinline__ int next_item_id(int item) { return item + static_cast<int>(gridDim.x); }
 
 __device__ __forceinline__ void issue_item(const PrefillParams& p, int item, ItemLoads& L) {
   if (item >= p.n_items) return;
-  const int unit = item >> 1;
-  L.which = item & 1;
-  const int group = unit / p.units_per_group;
-  L.k = unit - group * p.units_per_group;
-  L.b = group / p.hkv;
-  L.h = group - L.b * p.hkv;
+  const int per = p.batch * p.hkv;
+  L.pk_rev = item / per;
+  const int rem = item - L.pk_rev * per;
+  L.b = rem / p.hkv;
+  L.h = rem - L.b * p.hkv;
   L.qo0 = p.qo_indptr[L.b];
   L.qo1 = p.qo_indptr[L.b + 1];
   L.ip0 = p.indptr[L.b];
@@ -281,15 +271,8 @@ __device__ __forceinline__ bool finish_item(const PrefillParams& p, const ItemLo
   it.qo_len = L.qo1 - L.qo0;
   const int ntile_q = (it.qo_len + tpt - 1) / tpt;
   const int npairs = (ntile_q + 1) / 2;
-  // unit k: pair npairs-1-k (which 0) and, if it is another pair, pair k (which 1)
-  int pk;
-  if (L.which == 0) {
-    if (2 * L.k > npairs - 1) return false;
-    pk = npairs - 1 - L.k;
-  } else {
-    if (2 * L.k >= npairs - 1) return false;
-    pk = L.k;
-  }
+  const int pk = npairs - 1 - L.pk_rev;
+  if (pk < 0) return false;
   it.kv_beg = L.ip0;
   it.npages = L.ip1 - L.ip0;
   it.kv_len = it.npages > 0 ? (it.npages - 1) * kPS + L.lpl : 0;
@@ -662,37 +645,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 64; ++c)
             if (kbase + c > lim) s[c] = -INFINITY;
         }
-        // row max as eight independent chains (two softmax warps per scheduler cannot
-        // hide one 63-long chain of dependent fmaxf), then a 3-level tree
-        float m8[8];
+        float mt = s[0];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = s[i];
-#pragma unroll
-        for (int c = 8; c < 64; c += 8)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[c + i]);
-#pragma unroll
-        for (int w = 4; w >= 1; w >>= 1)
-#pragma unroll
-          for (int i = 0; i < w; ++i) m8[i] = fmaxf(m8[i], m8[i + w]);
-        const float mt = m8[0];
+        for (int c = 1; c < 64; ++c) mt = fmaxf(mt, s[c]);
         const float m_new = fmaxf(m_ref, mt * sl);
         const bool rescale = m_new > m_ref + 8.0f;   // also true on the first finite max
         const float alpha = (rescale && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
         if (rescale) m_ref = m_new;
         const float neg = m_ref == -INFINITY ? 0.f : -m_ref;
-        // row sum as four independent chains (the same terms; only the rounding order
-        // of the fp32 sum changes)
-        float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+        float rs = 0.f;
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 64; c += 2) {
           const float p0 = fast_exp2(fmaf(s[c], sl, neg));
           const float p1 = fast_exp2(fmaf(s[c + 1], sl, neg));
-          rs4[(c >> 1) & 3] += p0 + p1;
+          rs += p0 + p1;
           pk[c / 2] = Mma16<T>::pack(p0, p1);
         }
-        const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         // O may only be rescaled once P(t-1).V(t-1) is done (warp-uniform branch: the
         // tcgen05.ld/st are warp-collective; rows with alpha == 1 multiply by 1)
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -827,12 +796,9 @@ int launch_paged_prefill_tc(int dtype, int batch, int hq, int hkv, const void* q
                                          kSmemBytes);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
   const int64_t pairs = ((max_qo_len + tpt - 1) / tpt + 1) / 2;
-  const int64_t per_group = (pairs + 1) / 2;              // units per (sequence, kv head)
-  const int64_t units = per_group * batch * hkv;
-  if (2 * units >= (int64_t{1} << 31)) return set_error(NSLG_ERR_UNSUPPORTED, "prefill: too many tiles");
-  p.n_items = static_cast<int>(2 * units);
-  p.units_per_group = static_cast<int>(per_group);
-  const int64_t grid = units < static_cast<int64_t>(sm_count()) ? units : sm_count();
+  const int64_t items = pairs * batch * hkv;
+  p.n_items = static_cast<int>(items);
+  const int64_t grid = items < static_cast<int64_t>(sm_count()) ? items : sm_count();
   kern<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, p);
   return check_launch("prefill_tc");
 }
