@@ -237,4 +237,33 @@ int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t g
                          static_cast<cudaStream_t>(stream));
 }
 
+int64_t nslg_linear_workspace_bytes(int rows, int out_features, int in_features) {
+  return linear_tc_workspace_bytes(rows, out_features, in_features);
+}
+
+int nslg_linear(int dtype, int rows, int out_features, int in_features, const void* x,
+                int64_t x_stride, const void* weight, int64_t w_stride, void* y,
+                int64_t y_stride, void* workspace, int64_t workspace_bytes, uint32_t* dev_status,
+                void* stream) {
+  g_last_error.clear();
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16)
+    return set_error(NSLG_ERR_ARG, "linear: dtype must be bfloat16 or float16");
+  if (rows < 0 || out_features <= 0 || in_features <= 0)
+    return set_error(NSLG_ERR_ARG, "linear: bad shape");
+  if (rows == 0) return NSLG_OK;
+  if (!linear_tc_supported(dtype, rows, out_features, in_features))
+    return set_error(NSLG_ERR_UNSUPPORTED, "linear: needs 1 <= rows <= " +
+                                               std::to_string(kLinearMaxRows) +
+                                               " and in_features a multiple of 64");
+  if (!x || !weight || !y) return set_error(NSLG_ERR_ARG, "linear: null pointer");
+  if (!aligned16(x) || !aligned16(weight) || (x_stride * 2) % 16 || (w_stride * 2) % 16 ||
+      x_stride < in_features || w_stride < in_features || y_stride < out_features ||
+      (reinterpret_cast<uintptr_t>(y) & 1u))
+    return set_error(NSLG_ERR_ARG,
+                     "linear: x and weight rows must be 16-byte aligned and strides cover the rows");
+  return launch_linear_tc(dtype, rows, out_features, in_features, x, x_stride, weight, w_stride,
+                          y, y_stride, workspace, workspace_bytes, dev_status,
+                          static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

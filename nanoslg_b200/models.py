@@ -16,7 +16,10 @@ path:
 * Greedy decoding reduces the LM-head logits with the ``nslg_argmax_rows`` kernel; a
   vocab-parallel head reduces its shard and the ranks exchange (max, index) pairs
   instead of all-gathering the logits.
-* The GEMMs stay cuBLAS through ``F.linear`` (tp_layers), the collectives NCCL.
+* The projections of decode-sized forwards (at most 256 rows: decode steps, the LM head
+  on the last position) run the tcgen05 linear kernel (``ops.linear``, nslg_linear);
+  larger forwards (prefill) stay cuBLAS GEMMs. The collectives are NCCL or the fused
+  peer-memory reduction.
 """
 import math
 from typing import List
@@ -126,7 +129,7 @@ class TPAttention(nn.Module):
         B, S, _ = x.shape
         hd = self.head_dim
         if _views_intact(self._qkv, [self.q_proj, self.k_proj, self.v_proj]):
-            qkv = F.linear(x, self._qkv)
+            qkv = ops.linear(x, self._qkv)
             nq, nk = self.n_heads_tp * hd, self.n_kv_heads_tp * hd
             q = qkv[..., :nq].view(B, S, self.n_heads_tp, hd)
             k = qkv[..., nq:nq + nk].view(B, S, self.n_kv_heads_tp, hd)
@@ -156,7 +159,7 @@ class TPMLP(nn.Module):
 
     def forward(self, x):
         if _views_intact(self._gu, [self.gate_proj, self.up_proj]):
-            return self.down_proj(ops.silu_mul(F.linear(x, self._gu)))
+            return self.down_proj(ops.silu_mul(ops.linear(x, self._gu)))
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -297,7 +300,7 @@ class _LlamaStage(nn.Module):
         if (head is None or tp == 1 or not getattr(head, "gather_output", False)
                 or head.out_features >= (1 << 24)):
             return ops.argmax_rows(self.lm_head(h)[:, -1])
-        local = F.linear(h[:, -1], head.weight, head.bias)              # [B, V/tp]
+        local = ops.linear(h[:, -1], head.weight, head.bias)            # [B, V/tp]
         ctx = get_parallel_context()
         offset = ctx.tp_rank * head.out_features_per_partition
         idx, val = ops.argmax_rows(local, offset, values=True)

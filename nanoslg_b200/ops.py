@@ -7,6 +7,7 @@ computes on the CPU: the ops need CUDA tensors and the built library.
 import threading
 
 import torch
+import torch.nn.functional as F
 
 from . import _native as N
 
@@ -69,6 +70,8 @@ class _DeviceState:
     def __init__(self):
         self.lock = threading.Lock()
         self.ws = {}
+        self.lin_ws = {}
+        self.lin_ws_all = []
         self.status = {}
 
     def workspace(self, device, nbytes):
@@ -80,6 +83,21 @@ class _DeviceState:
             if buf is None or buf.numel() < nbytes:
                 buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
                 self.ws[device] = buf
+            return buf
+
+    def linear_workspace(self, device, nbytes):
+        """Zero-filled workspace of nslg_linear (its tile counters must start at zero;
+        every call leaves them zero). Grown by replacement; the old buffers stay alive,
+        since CUDA graphs captured earlier still point at them."""
+        buf = self.lin_ws.get(device)
+        if buf is not None and buf.numel() >= nbytes:
+            return buf
+        with self.lock:
+            buf = self.lin_ws.get(device)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 4 << 20), dtype=torch.uint8, device=device)
+                self.lin_ws[device] = buf
+                self.lin_ws_all.append(buf)
             return buf
 
     def status_word(self, device):
@@ -255,6 +273,51 @@ def silu_mul(gate_up, out=None):
     o2 = out.view(rows, inter)
     N.call("nslg_silu_mul", dt, rows, inter, _ptr(g2), g2.stride(0), _ptr(o2), o2.stride(0),
            _stream(gate_up))
+    return out
+
+
+LINEAR_MAX_ROWS = 256
+
+
+def linear_supported(x, weight, bias=None):
+    """Whether ``linear`` runs the tcgen05 kernel for these operands: CUDA bf16 / fp16 x
+    and weight of one type, no bias, at most LINEAR_MAX_ROWS rows of x, in_features a
+    multiple of 64, rows of x and weight contiguous and 16-byte aligned."""
+    if bias is not None or not (x.is_cuda and weight.is_cuda):
+        return False
+    if x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype:
+        return False
+    k = x.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != k or k % 64 or x.stride(-1) != 1:
+        return False
+    if weight.stride(1) != 1 or weight.stride(0) % 8 or weight.data_ptr() % 16:
+        return False
+    rows = x.numel() // k if k else 0
+    return 1 <= rows <= LINEAR_MAX_ROWS
+
+
+def linear(x, weight, bias=None, out=None):
+    """F.linear(x, weight, bias): the tcgen05 kernel (nslg_linear) for decode-sized
+    forwards (``linear_supported``), the cuBLAS GEMM of F.linear for the rest (prefill
+    rows, fp32, biases)."""
+    if not linear_supported(x, weight, bias):
+        return F.linear(x, weight, bias)
+    k, n = x.shape[-1], weight.shape[0]
+    try:
+        rows, xs = _rows(x.unsqueeze(-2), "x")
+    except ValueError:                     # leading dims that do not form one row stride
+        return F.linear(x, weight, bias)
+    if xs % 8 or x.data_ptr() % 16:
+        return F.linear(x, weight, bias)
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (n,), dtype=x.dtype, device=x.device)
+    _, ys = _rows(out.unsqueeze(-2), "out")
+    lib = N.lib()
+    wsb = lib.nslg_linear_workspace_bytes(rows, n, k)
+    ws = _STATE.linear_workspace(x.device, wsb)
+    N.call("nslg_linear", _dtype_code(x), rows, n, k, _ptr(x), xs, _ptr(weight),
+           weight.stride(0), _ptr(out), ys, _ptr(ws), ws.numel(),
+           _ptr(status_word(x.device)), _stream(x))
     return out
 
 

@@ -1,13 +1,16 @@
 """Tensor-parallel linear layers with the reference's surface (nanoslg/tp_layers.py:28-158,
 210-234): Column splits the output features, Row splits the input features and
 all-reduces its output over the TP group (NCCL), the LM head is a gathered Column layer.
-The GEMMs are cuBLAS through ``F.linear``, as in the reference."""
+The products go through ``ops.linear``: the tcgen05 kernel for decode-sized forwards
+(at most 256 rows, bf16 / fp16), the cuBLAS GEMM of ``F.linear`` otherwise (prefill,
+fp32, CPU tensors), as in the reference."""
 import math
 
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import ops
 from .parallel import all_gather_tp, all_reduce_tp, get_parallel_context
 
 
@@ -34,7 +37,7 @@ class ColumnParallelLinear(nn.Module):
             nn.init.uniform_(self.bias, -bound, bound)
 
     def forward(self, x):
-        out = F.linear(x, self.weight, self.bias)
+        out = ops.linear(x, self.weight, self.bias)
         if self.gather_output and self.tp_size > 1:
             out = all_gather_tp(out, dim=-1)
         return out
@@ -65,7 +68,7 @@ class RowParallelLinear(nn.Module):
     peer_reduce = None
 
     def forward(self, x):
-        out = F.linear(x, self.weight)
+        out = ops.linear(x, self.weight)
         if self.tp_size > 1:
             if self.peer_reduce is not None and self.peer_reduce.active and self.bias is None:
                 return out

@@ -1,0 +1,104 @@
+"""The tcgen05 linear layer of decode steps (nslg_linear, ops.linear) against a plain
+torch fp32 reference of the same product, y = x . W^T rounded once to the activation
+type, at the shapes the Llama-3.1-8B decode step runs per layer and rank (TP = 1 and 8),
+the LM head, ragged tiles, and through CUDA-graph replay.
+
+Tolerance: the fp32 sums differ from the reference's only in order, so y is within one
+rounding of the activation type (bf16 2^-8, fp16 2^-11 relative) plus a small absolute
+floor for outputs near zero."""
+import pytest
+import torch
+
+from nanoslg_b200 import _native as N
+from nanoslg_b200 import ops
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+TOL = {torch.bfloat16: dict(rtol=8e-3, atol=8e-3), torch.float16: dict(rtol=2e-3, atol=2e-3)}
+
+
+@pytest.fixture(autouse=True)
+def _clean_status():
+    ops.status_word(DEV).zero_()
+    yield
+    ops.check_device_status(DEV)
+
+
+def _problem(m, n, k, dt, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x = torch.randn(m, k, device=DEV, generator=g).to(dt)
+    w = (torch.randn(n, k, device=DEV, generator=g) / k ** 0.5).to(dt)
+    return x, w
+
+
+def _ref(x, w):
+    return (x.float() @ w.float().t()).to(x.dtype)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [
+    (64, 6144, 4096),      # stacked q|k|v, TP=1
+    (64, 4096, 4096),      # o_proj, TP=1
+    (64, 28672, 4096),     # stacked gate|up, TP=1
+    (64, 4096, 14336),     # down_proj, TP=1
+    (1, 4096, 4096),       # batch 1
+    (64, 768, 4096),       # q|k|v at TP=8
+    (64, 4096, 512),       # o_proj at TP=8
+    (64, 4096, 1792),      # down_proj at TP=8
+    (17, 1000, 512),       # ragged rows and a partial last tile
+    (256, 640, 128),       # the largest row count, few chunks per tile
+])
+def test_linear_matches_fp32_reference(dt, m, n, k):
+    x, w = _problem(m, n, k, dt, seed=m * 7 + n + k)
+    y = ops.linear(x, w)
+    assert ops.linear_supported(x, w)
+    torch.testing.assert_close(y, _ref(x, w), **TOL[dt])
+    # deterministic: the split-K partials are summed in a fixed order
+    assert torch.equal(ops.linear(x, w), y)
+
+
+def test_linear_lm_head_on_a_strided_last_position():
+    """The LM head on the last position of [B, S, hidden] (a strided view) at the TP=8
+    vocabulary shard (128256 / 8 = 16032 rows: a partial last tile)."""
+    dt = torch.bfloat16
+    g = torch.Generator(device=DEV).manual_seed(5)
+    h = torch.randn(8, 3, 4096, device=DEV, generator=g).to(dt)
+    w = (torch.randn(16032, 4096, device=DEV, generator=g) / 64).to(dt)
+    last = h[:, -1]
+    y = ops.linear(last, w)
+    torch.testing.assert_close(y, _ref(last.contiguous(), w), **TOL[dt])
+
+
+def test_linear_counters_left_zero_and_graph_replay():
+    dt = torch.bfloat16
+    x, w = _problem(64, 4096, 4096, dt, seed=11)
+    y = torch.empty(64, 4096, dtype=dt, device=DEV)
+    ops.linear(x, w, out=y)
+    torch.cuda.synchronize(DEV)
+    ws = ops._STATE.lin_ws[DEV]
+    n_tiles = 4096 // 128
+    assert int(ws[:n_tiles * 4].view(torch.int32).abs().sum()) == 0
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.linear(x, w, out=y)
+    for seed in (12, 13):
+        x2, _ = _problem(64, 4096, 4096, dt, seed=seed)
+        x.copy_(x2)
+        graph.replay()
+        torch.cuda.synchronize(DEV)
+        torch.testing.assert_close(y, _ref(x2, w), **TOL[dt])
+    del graph
+
+
+def test_linear_refuses_what_it_does_not_cover():
+    x = torch.zeros(300, 128, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(256, 128, dtype=torch.bfloat16, device=DEV)
+    assert not ops.linear_supported(x, w)                       # too many rows: cuBLAS
+    assert not ops.linear_supported(x[:8, :100], w[:, :100])    # K not a multiple of 64
+    assert not ops.linear_supported(x[:8].float(), w.float())   # fp32: cuBLAS
+    lib = N.lib()
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=DEV)
+    rc = lib.nslg_linear(N.DTYPE_BF16, 300, 256, 128, x.data_ptr(), 128, w.data_ptr(), 128,
+                         x.data_ptr(), 256, ws.data_ptr(), ws.numel(), None,
+                         torch.cuda.current_stream(DEV).cuda_stream)
+    assert rc == N.ERR_UNSUPPORTED and b"rows" in lib.nslg_last_error()
