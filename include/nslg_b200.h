@@ -220,16 +220,11 @@ int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t g
  * and the q|k|v and gate|up projections stacked into one weight each) and the LM head
  * (tp_layers.py:210-234) for forwards of 1 <= rows <= 256 (decode steps); larger
  * forwards stay cuBLAS GEMMs. in_features must be a multiple of 64; x and weight rows
- * 16-byte aligned (strides in elements). The workspace (nslg_linear_workspace_bytes,
- * 256-byte aligned) holds per-tile counters that must be zero before its first use:
- * every call leaves them zero again, except a call that recorded NSLG_DEV_WAIT_TIMEOUT,
- * after which the workspace must be zero-filled again. Calls that share a workspace
- * must not overlap on the GPU (one stream, or ordered). */
-int64_t nslg_linear_workspace_bytes(int rows, int out_features, int in_features);
+ * 16-byte aligned (strides in elements). Needs no workspace: a split of the in_features
+ * sum across CTAs is reduced on chip, within a thread-block cluster. */
 int nslg_linear(int dtype, int rows, int out_features, int in_features, const void* x,
                 int64_t x_stride, const void* weight, int64_t w_stride, void* y,
-                int64_t y_stride, void* workspace, int64_t workspace_bytes, uint32_t* dev_status,
-                void* stream);
+                int64_t y_stride, uint32_t* dev_status, void* stream);
 
 /* Greedy sampling: for each of `rows` rows of logits x (cols entries, row stride
  * x_stride elements), the maximum (out_val[r], fp32; out_val may be NULL) and the index

@@ -237,14 +237,9 @@ int nslg_silu_mul(int dtype, int rows, int inter, const void* gate_up, int64_t g
                          static_cast<cudaStream_t>(stream));
 }
 
-int64_t nslg_linear_workspace_bytes(int rows, int out_features, int in_features) {
-  return linear_tc_workspace_bytes(rows, out_features, in_features);
-}
-
 int nslg_linear(int dtype, int rows, int out_features, int in_features, const void* x,
                 int64_t x_stride, const void* weight, int64_t w_stride, void* y,
-                int64_t y_stride, void* workspace, int64_t workspace_bytes, uint32_t* dev_status,
-                void* stream) {
+                int64_t y_stride, uint32_t* dev_status, void* stream) {
   g_last_error.clear();
   if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16)
     return set_error(NSLG_ERR_ARG, "linear: dtype must be bfloat16 or float16");
@@ -262,8 +257,7 @@ int nslg_linear(int dtype, int rows, int out_features, int in_features, const vo
     return set_error(NSLG_ERR_ARG,
                      "linear: x and weight rows must be 16-byte aligned and strides cover the rows");
   return launch_linear_tc(dtype, rows, out_features, in_features, x, x_stride, weight, w_stride,
-                          y, y_stride, workspace, workspace_bytes, dev_status,
-                          static_cast<cudaStream_t>(stream));
+                          y, y_stride, dev_status, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

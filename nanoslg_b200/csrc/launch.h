@@ -114,10 +114,8 @@ int launch_paged_prefill_tc(int dtype, int batch, int hq, int hkv, const void* q
 // bf16 / fp16, K a multiple of 64 (linear_tc.cu).
 constexpr int kLinearMaxRows = 256;
 bool linear_tc_supported(int dtype, int M, int N, int K);
-int64_t linear_tc_workspace_bytes(int M, int N, int K);
 int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_stride,
                      const void* w, int64_t w_stride, void* y, int64_t y_stride,
-                     void* workspace, int64_t workspace_bytes, uint32_t* status,
-                     cudaStream_t stream);
+                     uint32_t* status, cudaStream_t stream);
 
 }  // namespace nslg

@@ -61,11 +61,12 @@ constexpr int kVecPerThread = 4;    // 16-byte vectors of a row per thread (hidd
 // one-shot push volume per rank ((world - 1) x rows x row bytes) from which two-shot is used
 constexpr int64_t kTwoShotBytes = 512 << 10;
 
-// NSLG_TP_TWO_SHOT, read at every call: unset or "auto" -> -1 (choose by size), "0" /
-// "1" -> force one-shot / two-shot (where the shape allows it)
+// NSLG_TP_TWO_SHOT, read at every call: "auto" -> -1 (choose by size), "1" -> two-shot
+// (where the shape allows it), unset or anything else -> 0 (one-shot)
 int two_shot_override() {
   const char* e = getenv("NSLG_TP_TWO_SHOT");
-  if (e == nullptr || e[0] == '\0' || strcmp(e, "auto") == 0) return -1;
+  if (e == nullptr || e[0] == '\0') return 0;
+  if (strcmp(e, "auto") == 0) return -1;
   return e[0] == '1' ? 1 : 0;
 }
 static_assert(kGrid * 4 <= NSLG_TP_COUNTER_BYTES, "counter buffer too small");
@@ -388,7 +389,7 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
   // when the one-shot's (world - 1) full-row pushes per rank are large: it moves
   // 2 (world - 1) / world of a row per rank instead of (world - 1) rows, at the price of a
   // second NVLink round trip. Same fp32 rank-order sums, so both give identical results.
-  // NSLG_TP_TWO_SHOT=0/1 forces one mode (where the shape allows two-shot).
+  // The mode follows NSLG_TP_TWO_SHOT: one-shot unless it says "1" or "auto" (by size).
   const int vec = 16 / esz;
   const bool two_ok = world > 2 && hidden % (world * vec) == 0;
   const int force = two_shot_override();

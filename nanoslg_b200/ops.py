@@ -70,8 +70,6 @@ class _DeviceState:
     def __init__(self):
         self.lock = threading.Lock()
         self.ws = {}
-        self.lin_ws = {}
-        self.lin_ws_all = []
         self.status = {}
 
     def workspace(self, device, nbytes):
@@ -83,21 +81,6 @@ class _DeviceState:
             if buf is None or buf.numel() < nbytes:
                 buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
                 self.ws[device] = buf
-            return buf
-
-    def linear_workspace(self, device, nbytes):
-        """Zero-filled workspace of nslg_linear (its tile counters must start at zero;
-        every call leaves them zero). Grown by replacement; the old buffers stay alive,
-        since CUDA graphs captured earlier still point at them."""
-        buf = self.lin_ws.get(device)
-        if buf is not None and buf.numel() >= nbytes:
-            return buf
-        with self.lock:
-            buf = self.lin_ws.get(device)
-            if buf is None or buf.numel() < nbytes:
-                buf = torch.zeros(max(nbytes, 4 << 20), dtype=torch.uint8, device=device)
-                self.lin_ws[device] = buf
-                self.lin_ws_all.append(buf)
             return buf
 
     def status_word(self, device):
@@ -276,13 +259,14 @@ def silu_mul(gate_up, out=None):
     return out
 
 
-LINEAR_MAX_ROWS = 256
+LINEAR_MAX_ROWS = 256     # what nslg_linear accepts
+LINEAR_AUTO_ROWS = 16     # what ``linear`` sends it by default
 
 
-def linear_supported(x, weight, bias=None):
-    """Whether ``linear`` runs the tcgen05 kernel for these operands: CUDA bf16 / fp16 x
-    and weight of one type, no bias, at most LINEAR_MAX_ROWS rows of x, in_features a
-    multiple of 64, rows of x and weight contiguous and 16-byte aligned."""
+def linear_supported(x, weight, bias=None, max_rows=LINEAR_MAX_ROWS):
+    """Whether the tcgen05 kernel takes these operands: CUDA bf16 / fp16 x and weight of
+    one type, no bias, at most ``max_rows`` rows of x, in_features a multiple of 64, rows
+    of x and weight contiguous and 16-byte aligned."""
     if bias is not None or not (x.is_cuda and weight.is_cuda):
         return False
     if x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype:
@@ -293,14 +277,17 @@ def linear_supported(x, weight, bias=None):
     if weight.stride(1) != 1 or weight.stride(0) % 8 or weight.data_ptr() % 16:
         return False
     rows = x.numel() // k if k else 0
-    return 1 <= rows <= LINEAR_MAX_ROWS
+    return 1 <= rows <= max_rows
 
 
-def linear(x, weight, bias=None, out=None):
-    """F.linear(x, weight, bias): the tcgen05 kernel (nslg_linear) for decode-sized
-    forwards (``linear_supported``), the cuBLAS GEMM of F.linear for the rest (prefill
-    rows, fp32, biases)."""
-    if not linear_supported(x, weight, bias):
+def linear(x, weight, bias=None, out=None, max_rows=LINEAR_AUTO_ROWS):
+    """F.linear(x, weight, bias): the tcgen05 kernel (nslg_linear) for forwards of at most
+    ``max_rows`` rows (``linear_supported``), the cuBLAS GEMM of F.linear for the rest.
+    The default sends the kernel the small decode batches (up to 16 rows), where it
+    streams the weights faster than cuBLAS on the 8B model's shapes at every TP degree;
+    at 64 rows cuBLAS is still ahead on the narrower products (measured per shape), so
+    larger batches, prefill, fp32 and biased layers stay cuBLAS."""
+    if not linear_supported(x, weight, bias, max_rows):
         return F.linear(x, weight, bias)
     k, n = x.shape[-1], weight.shape[0]
     try:
@@ -312,12 +299,8 @@ def linear(x, weight, bias=None, out=None):
     if out is None:
         out = torch.empty(x.shape[:-1] + (n,), dtype=x.dtype, device=x.device)
     _, ys = _rows(out.unsqueeze(-2), "out")
-    lib = N.lib()
-    wsb = lib.nslg_linear_workspace_bytes(rows, n, k)
-    ws = _STATE.linear_workspace(x.device, wsb)
     N.call("nslg_linear", _dtype_code(x), rows, n, k, _ptr(x), xs, _ptr(weight),
-           weight.stride(0), _ptr(out), ys, _ptr(ws), ws.numel(),
-           _ptr(status_word(x.device)), _stream(x))
+           weight.stride(0), _ptr(out), ys, _ptr(status_word(x.device)), _stream(x))
     return out
 
 

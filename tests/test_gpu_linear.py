@@ -50,11 +50,11 @@ def _ref(x, w):
 ])
 def test_linear_matches_fp32_reference(dt, m, n, k):
     x, w = _problem(m, n, k, dt, seed=m * 7 + n + k)
-    y = ops.linear(x, w)
+    y = ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS)
     assert ops.linear_supported(x, w)
     torch.testing.assert_close(y, _ref(x, w), **TOL[dt])
     # deterministic: the split-K partials are summed in a fixed order
-    assert torch.equal(ops.linear(x, w), y)
+    assert torch.equal(ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS), y)
 
 
 def test_linear_lm_head_on_a_strided_last_position():
@@ -65,22 +65,19 @@ def test_linear_lm_head_on_a_strided_last_position():
     h = torch.randn(8, 3, 4096, device=DEV, generator=g).to(dt)
     w = (torch.randn(16032, 4096, device=DEV, generator=g) / 64).to(dt)
     last = h[:, -1]
-    y = ops.linear(last, w)
+    y = ops.linear(last, w, max_rows=ops.LINEAR_MAX_ROWS)
     torch.testing.assert_close(y, _ref(last.contiguous(), w), **TOL[dt])
 
 
-def test_linear_counters_left_zero_and_graph_replay():
+def test_linear_graph_replay():
     dt = torch.bfloat16
     x, w = _problem(64, 4096, 4096, dt, seed=11)
     y = torch.empty(64, 4096, dtype=dt, device=DEV)
-    ops.linear(x, w, out=y)
+    ops.linear(x, w, out=y, max_rows=ops.LINEAR_MAX_ROWS)
     torch.cuda.synchronize(DEV)
-    ws = ops._STATE.lin_ws[DEV]
-    n_tiles = 4096 // 128
-    assert int(ws[:n_tiles * 4].view(torch.int32).abs().sum()) == 0
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        ops.linear(x, w, out=y)
+        ops.linear(x, w, out=y, max_rows=ops.LINEAR_MAX_ROWS)
     for seed in (12, 13):
         x2, _ = _problem(64, 4096, 4096, dt, seed=seed)
         x.copy_(x2)
@@ -90,6 +87,19 @@ def test_linear_counters_left_zero_and_graph_replay():
     del graph
 
 
+def test_linear_products_of_different_shapes_back_to_back():
+    """Calls of different shapes (whole tiles and cluster-split tiles) back to back,
+    each overlapping the previous one's tail (programmatic dependent launch)."""
+    dt = torch.bfloat16
+    shapes = [(17, 1000, 512), (8, 16032, 4096), (64, 4096, 512), (64, 28672, 4096),
+              (1, 640, 128)]
+    probs = [_problem(m, n, k, dt, seed=i) for i, (m, n, k) in enumerate(shapes)]
+    for _ in range(3):
+        for x, w in probs:
+            torch.testing.assert_close(ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS),
+                                       _ref(x, w), **TOL[dt])
+
+
 def test_linear_refuses_what_it_does_not_cover():
     x = torch.zeros(300, 128, dtype=torch.bfloat16, device=DEV)
     w = torch.zeros(256, 128, dtype=torch.bfloat16, device=DEV)
@@ -97,8 +107,6 @@ def test_linear_refuses_what_it_does_not_cover():
     assert not ops.linear_supported(x[:8, :100], w[:, :100])    # K not a multiple of 64
     assert not ops.linear_supported(x[:8].float(), w.float())   # fp32: cuBLAS
     lib = N.lib()
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=DEV)
     rc = lib.nslg_linear(N.DTYPE_BF16, 300, 256, 128, x.data_ptr(), 128, w.data_ptr(), 128,
-                         x.data_ptr(), 256, ws.data_ptr(), ws.numel(), None,
-                         torch.cuda.current_stream(DEV).cuda_stream)
+                         x.data_ptr(), 256, None, torch.cuda.current_stream(DEV).cuda_stream)
     assert rc == N.ERR_UNSUPPORTED and b"rows" in lib.nslg_last_error()

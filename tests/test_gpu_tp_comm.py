@@ -44,9 +44,10 @@ def _close(a, b):
     return bool(((a.float() - b.float()).abs() <= b.float().abs() * 2 ** -7 + 1e-6).all())
 
 
-def _peer_main(rank, world, port, out):
+def _peer_main(rank, world, port, out, mode="0"):
     import sys
     sys.path.insert(0, ROOT)
+    os.environ["NSLG_TP_TWO_SHOT"] = mode
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -119,13 +120,17 @@ def _peer_main(rank, world, port, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_peer_allreduce_rmsnorm(world):
+@pytest.mark.parametrize("world,mode", [(2, "0"), (4, "0"), (8, "0"), (4, "1"), (8, "1"),
+                                        (8, "auto")])
+def test_peer_allreduce_rmsnorm(world, mode):
+    """One-shot ("0"), two-shot ("1": reduce-scatter of column slices + all-gather) and
+    the size-based choice ("auto", which mixes both over the test's row counts): the
+    same bit-exact residual in every mode."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     with mp.get_context("spawn").Manager() as m:
         out = m.dict()
-        mp.start_processes(_peer_main, args=(world, _free_port(), out), nprocs=world,
+        mp.start_processes(_peer_main, args=(world, _free_port(), out, mode), nprocs=world,
                            start_method="spawn", join=True)
         res = dict(out)
     for rank in range(world):
