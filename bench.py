@@ -406,6 +406,66 @@ def run_decode_model_shapes(device, reps=10, layers=32):
             "peak_gbs": peak, "peak_source": src, **res}
 
 
+LINEAR_SHAPES = [(f"tp{tp}_{m}rows_{name}", m, n // (tp if split == "out" else 1),
+                  k // (tp if split == "in" else 1))
+                 for tp in (1, 2, 8) for m in (1, 64)
+                 for name, n, k, split in (("qkv", 6144, 4096, "out"), ("o", 4096, 4096, "in"),
+                                           ("gate_up", 28672, 4096, "out"),
+                                           ("down", 4096, 14336, "in"))]
+
+
+def run_linear_shapes(device, shapes=None, reps=20, copies=8):
+    """The tcgen05 linear kernel (ops.linear, every row count allowed) against cuBLAS
+    (F.linear) on the 8B model's per-layer projections at TP = 1, 2 and 8 and 1 or 64
+    rows: ``copies`` weight copies rotated between calls (the large ones then come from
+    DRAM; the TP=8 ones still fit in L2 together), ``reps`` calls per CUDA graph, five
+    replays, CUDA events; frac = weight bytes / time / measured HBM bandwidth."""
+    import torch.nn.functional as F
+    from nanoslg_b200 import ops
+    peak, _ = _hbm_peak()
+    out = {}
+
+    def timeit(fn):
+        fn()
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        del g
+        return e0.elapsed_time(e1) * 1e3 / (5 * reps)
+
+    for name, m, n, k in (shapes or LINEAR_SHAPES):
+        ws = [(torch.randn(n, k, device=device) / 64).to(torch.bfloat16) for _ in range(copies)]
+        x = torch.randn(m, k, device=device).to(torch.bfloat16)
+        i = [0]
+
+        def ours():
+            i[0] = (i[0] + 1) % copies
+            ops.linear(x, ws[i[0]], max_rows=ops.LINEAR_MAX_ROWS)
+
+        def cublas():
+            i[0] = (i[0] + 1) % copies
+            F.linear(x, ws[i[0]])
+
+        t_o, t_c = timeit(ours), timeit(cublas)
+        gb = n * k * 2 / 1e9
+        out[name] = {"shape": [m, n, k], "ours_us": t_o, "cublas_us": t_c,
+                     "ours_frac": gb / (t_o * 1e-6) / peak, "cublas_frac": gb / (t_c * 1e-6) / peak}
+        del ws
+        torch.cuda.empty_cache()
+    ops.check_device_status(device)
+    return out
+
+
 def _hbm_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -1031,14 +1091,18 @@ def main():
                     help="TP>1 decode: RowParallel reductions over NVLink peer memory fused "
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
     ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce",
-                                       "elementwise", "e2e", "parity", "decode-shapes"],
+                                       "elementwise", "e2e", "parity", "decode-shapes",
+                                       "linear"],
                     default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg; elementwise: the RoPE + "
                          "KV-append and RMSNorm + residual kernels at the C3 prefill shape; "
                          "e2e: only the two end-to-end legs (one and two steps in flight); "
                          "parity: only the sharded-path token / reduction checks; "
-                         "decode-shapes: decode attention at the 8B model's decode shapes")
+                         "decode-shapes: decode attention at the 8B model's decode shapes; "
+                         "linear: the tcgen05 linear kernel against cuBLAS per 8B shape")
+    ap.add_argument("--linear-shape", default=None,
+                    help="with --only linear: one shape 'rows,out,in' (e.g. 64,6144,4096)")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
@@ -1111,6 +1175,17 @@ def main():
         if rank == 0:
             print(json.dumps({"case": "prefill only", "prefill_attention":
                               run_prefill_kernel(device)}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
+    if a.only == "linear":
+        shapes = None
+        if a.linear_shape:
+            m, n, k = (int(v) for v in a.linear_shape.split(","))
+            shapes = [(f"rows{m}_out{n}_in{k}", m, n, k)]
+        if rank == 0:
+            print(json.dumps({"case": "linear only", "linear_shapes":
+                              run_linear_shapes(device, shapes)}), flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
         return 0
