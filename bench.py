@@ -8,7 +8,8 @@ lengths uniform in [512, 8192] (seed 0), page ids a random draw from a 600k-page
 the batch (64 query tokens); the metric is decode tokens/s of that pass.
 
 * ``value``     -- kernel path, inputs resident in HBM: ops.paged_decode (the C ABI
-                   nslg_paged_decode: split-KV kernel + merge), CUDA events on the
+                   nslg_paged_decode: one split-KV kernel launch, split sequences
+                   merged in-kernel by their last CTA), CUDA events on the
                    launching stream.  The 1.13 GB of KV read per step is 9x the 126 MB L2,
                    so no L2 flush is needed between steps.
 * ``e2e``       -- the same decode step through the reference-facing API:
@@ -349,7 +350,9 @@ def run_decode_model_shapes(device, reps=10, layers=32):
     last), one decode call per layer captured back to back in a CUDA graph, replayed
     ``reps`` times (CUDA events). Cases: batch 64 with contexts U[512, 640] and batch 1
     with a 512-token context, at TP=1 (32/8 heads) and at the TP=8 shard (4/1 heads).
-    Algorithmic bytes per layer: every cached K and V byte, q in, out, and the page ids."""
+    Algorithmic bytes per layer: every cached K and V byte, q in, out, and the page ids.
+    Each case is timed with the library's choice of how split sequences are combined, and
+    with each of the two modes forced (in the decode kernel / by the merge kernel)."""
     from nanoslg_b200 import ops
     peak, src = _hbm_peak()
     g = torch.Generator().manual_seed(5)
@@ -379,28 +382,45 @@ def run_decode_model_shapes(device, reps=10, layers=32):
             for (pk, pv, idx), o in zip(pools, outs):
                 ops.paged_decode(q, pk, pv, indptr, idx, lpl, scale, out=o)
 
-        step()
-        torch.cuda.synchronize(device)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        graph.replay()
-        torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
+        def time_layers(mode):
+            # mode None: the library's own choice of merge; "inline" / "kernel" force one
+            # (the choice is made when the graph is captured)
+            old = os.environ.pop("NSLG_DECODE_MERGE", None)
+            if mode is not None:
+                os.environ["NSLG_DECODE_MERGE"] = mode
+            try:
+                step()
+                torch.cuda.synchronize(device)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    step()
+            finally:
+                os.environ.pop("NSLG_DECODE_MERGE", None)
+                if old is not None:
+                    os.environ["NSLG_DECODE_MERGE"] = old
             graph.replay()
-        e1.record()
-        torch.cuda.synchronize(device)
-        ms_layer = e0.elapsed_time(e1) / reps / layers
-        ops.check_device_status(device)
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            ops.check_device_status(device)
+            del graph
+            return e0.elapsed_time(e1) / reps / layers
+
+        ms_layer = time_layers(None)
+        by_mode = {m: time_layers(m) * 1e3 for m in ("inline", "kernel")}
         nbytes = (sum(lens) * hkv * D * 2 * 2 + 2 * batch * hq * D * 2 + 4 * sum(npg)
                   + 4 * (2 * batch + 1))
         gbs = nbytes / (ms_layer / 1e3) / 1e9
         res[name] = {"batch": batch, "ctx": f"U[{lo},{hi}]", "heads": f"{hq}/{hkv}",
                      "us_per_layer": ms_layer * 1e3, "algorithmic_bytes_per_layer": nbytes,
-                     "gbs": gbs, "frac": gbs / peak}
-        del graph, pools, outs
+                     "gbs": gbs, "frac": gbs / peak,
+                     "us_per_layer_merge_inline": by_mode["inline"],
+                     "us_per_layer_merge_kernel": by_mode["kernel"]}
+        del pools, outs
         torch.cuda.empty_cache()
     return {"workload": "decode attention at the 8B decode shapes, 32 layers per CUDA graph",
             "peak_gbs": peak, "peak_source": src, **res}
@@ -1071,6 +1091,50 @@ def cpu_reference(max_seconds, n_calls=None, seed=0, warmup=1):
                        f"{sum(lens)}, one layer) through the contiguous cache + SDPA, bf16")
 
 
+def run_model_legs(a, device, world, rank):
+    """The Llama-3.1-8B decode legs at TP=world: batch 64 and batch 1 with the per-step
+    split, at world > 1 also the TP=1 batch-64 decode on rank 0 alone (the scaling
+    denominator) and the C4 radix workload."""
+    out = {}
+    tp1 = None
+    if world > 1:
+        # the same batch-64 decode at TP=1 on rank 0 alone: the denominator of this
+        # line's TP scaling figures
+        if rank == 0:
+            run1, tp1 = run_llama_decode(device, 1, 0, 64, 512, a.model_steps, 4, solo=True)
+            run1.close()
+            del run1
+            torch.cuda.empty_cache()
+        torch.distributed.barrier()
+    runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,
+                                   peer_allreduce=a.tp_reduce == "peer", split=True)
+    _, r1 = run_llama_decode(device, world, rank, 1, 512, a.model_steps, 4, runner=runner,
+                             split=True)
+    out["llama8b_decode"] = {
+        "model": "Llama-3.1-8B architecture, random init N(0, 0.02), bf16 (BASELINE C3)",
+        "parallelism": f"TP={world}", "batch64": r64, "batch1": r1,
+        "tp_reduce": a.tp_reduce if world > 1 else None,
+        "note": "greedy decode steps through models.LlamaTP + B200PagedKVCache; projections "
+                "through the tcgen05 linear kernel for batches of up to 16 rows, cuBLAS "
+                "above; attention, RoPE/append, RMSNorm, SwiGLU, argmax and the TP "
+                "reduction the nslg kernels"}
+    if tp1 is not None:
+        out["llama8b_decode"]["tp_scaling_batch64"] = {
+            "tp1_tok_s": tp1["tok_s"], "tp1_ms_per_step": tp1["ms_per_step"],
+            "speedup_vs_tp1": r64["tok_s"] / tp1["tok_s"],
+            "efficiency_vs_tp1": r64["tok_s"] / (world * tp1["tok_s"]),
+            "note": "strong scaling (fixed batch 64); TP=1 measured on rank 0 alone in "
+                    "this run"}
+    if world > 1:
+        out["llama8b_c4_radix"] = {
+            "config": "BASELINE C4: TP=N, shared 1024-token prefix + unique 128-token "
+                      "suffix per request, 128 greedy decode tokens, radix prefix caching",
+            **run_llama_c4(device, world, rank, runner)}
+    runner.close()
+    del runner
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1220,14 +1284,11 @@ def main():
         torch.distributed.destroy_process_group()
         return 0
     if a.only == "model":
-        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,
-                                       peer_allreduce=a.tp_reduce == "peer")
-        c4 = run_llama_c4(device, world, rank, runner) if world > 1 else None
-        runner.close()
+        r = run_model_legs(a, device, world, rank)
         if rank == 0:
-            print(json.dumps({"case": "model only", "llama8b_decode_batch64": r64,
-                              "llama8b_c4_radix": c4}), flush=True)
+            print(json.dumps({"case": "model only", "n_gpus": world, **r}), flush=True)
         if world > 1:
+            torch.distributed.barrier()
             torch.distributed.destroy_process_group()
         return 0
     parity = run_parity(device, world, rank) if a.only == "all" else None
@@ -1296,7 +1357,7 @@ def main():
                          "algorithmic_bytes_per_step": ab,
                          "kernel_ms_mean": mean_ms,
                          "kernel_ms_median": statistics.median(kr["per_ms"])},
-            "gpu_launches": 2 * a.steps,
+            "gpu_launches": a.steps,
             "clocks": kr["clocks"]}
     line["parity"] = parity
     line["prefill_attention"] = run_prefill_kernel(device) if rank == 0 else None
@@ -1304,40 +1365,7 @@ def main():
     if world > 1:
         torch.distributed.barrier()
     if not a.no_model:
-        tp1 = None
-        if world > 1:
-            # the same batch-64 decode at TP=1 on rank 0 alone: the denominator of this
-            # line's TP scaling figures
-            if rank == 0:
-                run1, tp1 = run_llama_decode(device, 1, 0, 64, 512, a.model_steps, 4, solo=True)
-                run1.close()
-                del run1
-                torch.cuda.empty_cache()
-            torch.distributed.barrier()
-        runner, r64 = run_llama_decode(device, world, rank, 64, 512, a.model_steps, 4,
-                                       peer_allreduce=a.tp_reduce == "peer", split=True)
-        _, r1 = run_llama_decode(device, world, rank, 1, 512, a.model_steps, 4, runner=runner,
-                                 split=True)
-        line["llama8b_decode"] = {
-            "model": "Llama-3.1-8B architecture, random init N(0, 0.02), bf16 (BASELINE C3)",
-            "parallelism": f"TP={world}", "batch64": r64, "batch1": r1,
-            "tp_reduce": a.tp_reduce if world > 1 else None,
-            "note": "greedy decode steps through models.LlamaTP + B200PagedKVCache; GEMMs "
-                    "cuBLAS, attention/RoPE/append/RMSNorm the nslg kernels"}
-        if tp1 is not None:
-            line["llama8b_decode"]["tp_scaling_batch64"] = {
-                "tp1_tok_s": tp1["tok_s"], "tp1_ms_per_step": tp1["ms_per_step"],
-                "speedup_vs_tp1": r64["tok_s"] / tp1["tok_s"],
-                "efficiency_vs_tp1": r64["tok_s"] / (world * tp1["tok_s"]),
-                "note": "strong scaling (fixed batch 64); TP=1 measured on rank 0 alone in "
-                        "this run"}
-        if world > 1:
-            line["llama8b_c4_radix"] = {
-                "config": "BASELINE C4: TP=N, shared 1024-token prefix + unique 128-token "
-                          "suffix per request, 128 greedy decode tokens, radix prefix caching",
-                **run_llama_c4(device, world, rank, runner)}
-        runner.close()
-        del runner
+        line.update(run_model_legs(a, device, world, rank))
     if rank == 0 and not a.no_cpu:
         r = cpu_reference(a.cpu_seconds)
         line["cpu_baseline"] = {"value": r["value"], "unit": "tok/s", "cores": r["cores"],

@@ -84,7 +84,11 @@ int nslg_rope_kv_append(int dtype, int num_tokens, int num_qo_heads, int num_kv_
                         int64_t pool_slots, uint32_t* dev_status, void* stream);
 
 /* Bytes of scratch nslg_paged_decode needs for this batch / head count / head_dim on
- * the current device. */
+ * the current device.  The workspace must be zeroed before its first use (cudaMemset);
+ * the kernel keeps per-CTA arrival counts at its head and leaves them zero after every
+ * call, so a workspace kept from call to call (any batch, head count or head_dim that
+ * fits) needs no further zeroing.  Do not share it between calls that may overlap on
+ * the GPU. */
 int64_t nslg_decode_workspace_bytes(int batch, int num_qo_heads, int head_dim);
 
 /* Batched paged decode attention: one query token per sequence.
@@ -99,6 +103,8 @@ int64_t nslg_decode_workspace_bytes(int batch, int num_qo_heads, int head_dim);
  *   kv_len(b) = (kv_indptr[b+1]-kv_indptr[b]-1)*page_size + kv_last_page_len[b].
  * GQA: query head h reads kv head h / (num_qo_heads / num_kv_heads).
  * Sequences with no pages produce zeros.
+ * One kernel launch: sequences split across CTAs are combined by the last CTA to finish
+ * its share (arrival counts in the workspace), with no second kernel.
  * Launched with programmatic dependent launch: it may start while the kernel before it
  * on the stream runs, if that kernel allows its dependents to launch early (the library's
  * KV-append, RMSNorm and SwiGLU kernels do). It reads q and the pool only after that
@@ -143,9 +149,10 @@ int nslg_append_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_
  * synchronisation of cudaMalloc/cudaFree. Same arguments and result as
  * nslg_paged_decode minus the workspace: the split-KV partials go to a fixed
  * NSLG_NOALLOC_SCRATCH_BYTES array compiled into the library, which every GPU that loads
- * the library holds until the process exits. Batches whose scratch
- * ((batch + #SMs) * num_qo_heads * (head_dim + 1) * 4 bytes) exceeds it are rejected with
- * NSLG_ERR_WORKSPACE. The first call on a device looks the array's device address up
+ * the library holds until the process exits (zeroed at load, and the arrival counts at
+ * its head are left zero by every call). Batches whose scratch
+ * ((batch + #SMs) * num_qo_heads * (head_dim + 1) * 4 bytes, plus 1 KiB) exceeds it are
+ * rejected with NSLG_ERR_WORKSPACE. The first call on a device looks the array's device address up
  * (cudaGetSymbolAddress) with that device current; make it before any stream capture.
  * The address is kept with the CUDA context it belongs to: the first call in another
  * context (after cudaDeviceReset, or in a context the caller created) looks it up again

@@ -23,13 +23,17 @@
 // stream capture too.
 //
 // Sharing. Every call on a device uses the same array and it keeps whatever the last
-// call left there. Nothing in it has to start at zero: the merge step reads only
-// partial results that the decode step of the same call has just written. Two calls
-// whose kernels overlap on the GPU (for example on two streams without an ordering
-// between them) race on the array and corrupt each other's results; order them.
+// call left there. The decode kernel needs the array's first words (its per-CTA arrival
+// counts) to be zero before a call and leaves them zero after it; a __device__ array
+// starts zeroed when the module is loaded, so that holds from the first call on. The
+// partial results behind them need no initial value: a call reads only partials that
+// its own CTAs have just written. Two calls whose kernels overlap on the GPU (for
+// example on two streams without an ordering between them) race on the array and
+// corrupt each other's results; order them.
 //
 // Limit. The scratch a call needs is (batch + #SMs) * num_qo_heads * (head_dim + 1) * 4
-// bytes (plus 256 for alignment); calls needing more than 8 MiB are rejected with
+// bytes, plus the arrival counts (#SMs words rounded up to 256 bytes) and 256 bytes for
+// alignment; calls needing more than 8 MiB are rejected with
 // NSLG_ERR_WORKSPACE and a message. Shapes the tensor-core kernel does not cover run the
 // CUDA-core kernel, which needs no scratch. No call allocates or frees device memory.
 #include <cuda_runtime.h>

@@ -9,8 +9,20 @@
 // boundaries; segment (b, c) writes its softmax partial (o, lse) to slot b + c of the
 // workspace (unique: along the flat list either b or c grows by one at each new
 // segment). A sequence lying inside one CTA's slice is finished in place and written
-// straight to `out`; the others are combined by decode_merge_kernel with a
-// log-sum-exp merge.
+// straight to `out`.
+//
+// Combining split sequences, two modes chosen per call by the host (merge_inline).
+// In-kernel, with no second launch: a sequence spread over CTAs cf..cl is combined by
+// the last of those CTAs to finish its segment: each writes its partial, fences, and adds
+// one to the arrival count of slot cf (at most one sequence that continues past its
+// slice starts in any CTA's slice, so the counts are indexed by CTA, [#SMs] words at
+// the head of the workspace whatever the batch); the CTA that brings the count to
+// cl - cf + 1 merges the partials (log-sum-exp weights in fp32, partials summed in slot
+// order, so the result does not depend on which CTA merges) and puts the count back to
+// zero. The counts are zero between calls: a new workspace must start zeroed. No CTA
+// waits for another. Merge kernel: decode_merge_kernel, launched behind the decode grid
+// with programmatic dependent launch, combines them on (hq / 4) x batch CTAs. In both
+// modes sequences without pages are written as zeros by decode CTA b % grid.
 //
 // Data movement. One producer warp issues TMA tile loads (no multicast) of each page:
 // per kv head and per 64-dim half, a [16 tokens x 64 dims] box with 128-byte swizzle,
@@ -30,6 +42,8 @@
 #include <cuda.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
@@ -54,9 +68,11 @@ struct DecodeParams {
   const int32_t* lpl;
   float* part_o;    // [slots, hq, D]
   float* part_lse;  // [slots, hq]
+  uint32_t* arrive; // [grid] arrival counts of the split sequences, by first CTA
   int64_t q_stride, out_stride, num_pages;
   int batch, hq, group, stages, grid;
   int smem_csr;       // kv_indptr and kv_last_page_len are staged in shared memory
+  int inline_merge;   // 1: split sequences merged by their last CTA; 0: by the merge kernel
   int box_all_heads;  // tensor maps with a [64 dim x 16 tok x HKV head] box (token-major)
   float scale_log2;
   uint32_t* status;
@@ -82,6 +98,158 @@ __device__ __forceinline__ int seq_of(const int32_t* indptr, int batch, int64_t 
   return lo - 1;
 }
 
+constexpr int kMaxHq = 128;        // 8 kv heads x 16 query heads per group
+constexpr int kMergeThreads = kConsumerWarps * 32;
+constexpr int kStaticSmem = 2 * kMaxHq * 4 + 16;   // s_stat + s_merge, rounded up
+
+// Sequences without pages (no CTA streams them) are zeros; CTA c writes sequences
+// c, c + grid, ... Run after the PDL wait: the kernel before may still read `out`.
+template <typename T, int D>
+__device__ void zero_empty_sequences(const DecodeParams& p, const int32_t* indptr, int c,
+                                     int tid, int nthreads) {
+  const int words = p.hq * D / 2;
+  for (int b = c; b < p.batch; b += p.grid) {
+    if (indptr[b] != indptr[b + 1]) continue;
+    uint32_t* ob = reinterpret_cast<uint32_t*>(static_cast<T*>(p.out) +
+                                               static_cast<int64_t>(b) * p.out_stride);
+    for (int e = tid; e < words; e += nthreads) ob[e] = 0u;
+  }
+}
+
+// Combines the `cnt` partials of sequence b (slots b + cf .. b + cf + cnt - 1) into
+// out[b]; run by the kConsumerWarps warps of the CTA that arrived last. The partials
+// were written by other CTAs and fenced before their arrival; they are read through L2
+// (ld.global.cg), never from this SM's L1.
+//   pass 1: per query head, m = max_i lse_i and 1 / sum_i 2^(lse_i - m); 8 lanes per
+//           head split the partials (32 heads per pass of the CTA);
+//   pass 2: per (head, 4 dims), sum_i 2^(lse_i - m) o_i, times 1 / sum; with many
+//           outputs each thread takes 4 at once (8 independent loads per step of its
+//           loop over the partials, two steps unrolled), with few (hq x D / 4 <= 128)
+//           2 to 8 lanes share one output's partials and add up by shuffles. The order
+//           of the sums depends only on the shapes, not on which CTA merges.
+template <typename T, int D>
+__device__ void merge_sequence(const DecodeParams& p, int b, int cf, int cnt, float* stat,
+                               int tid) {
+  const int warp = tid / 32, lane = tid % 32;
+  const int64_t slot0 = static_cast<int64_t>(b) + cf;
+  const float* lse0 = p.part_lse + slot0 * p.hq;
+  for (int h0 = warp * 4; h0 < p.hq; h0 += kConsumerWarps * 4) {
+    const int hq = h0 + lane / 8, sub = lane % 8;
+    float m = -INFINITY, s = 0.f;
+    if (hq < p.hq) {
+#pragma unroll 4
+      for (int i = sub; i < cnt; i += 8) {
+        const float l = __ldcg(lse0 + static_cast<int64_t>(i) * p.hq + hq);
+        const float nm = fmaxf(m, l);
+        if (nm != -INFINITY) s = s * fast_exp2(m - nm) + fast_exp2(l - nm);
+        m = nm;
+      }
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o);
+      const float os = __shfl_xor_sync(0xffffffffu, s, o);
+      const float nm = fmaxf(m, om);
+      s = nm == -INFINITY ? 0.f : s * fast_exp2(m - nm) + os * fast_exp2(om - nm);
+      m = nm;
+    }
+    if (sub == 0 && hq < p.hq) {
+      stat[2 * hq] = m;
+      stat[2 * hq + 1] = s > 0.f ? 1.f / s : 0.f;
+    }
+  }
+  named_barrier_sync(1, kMergeThreads);
+  constexpr int DQ = D / 4;
+  constexpr int kE = 4;                                   // outputs per thread per round
+  const int n_out = p.hq * DQ;
+  const int64_t step = static_cast<int64_t>(p.hq) * D;   // from one partial to the next
+  int tpo = 1;   // threads per output: 2..8 neighbouring lanes when the outputs are few
+  while (tpo < 8 && n_out * tpo * 2 <= kMergeThreads) tpo *= 2;
+  if (tpo > 1) {
+    // lanes e*tpo .. e*tpo + tpo - 1 (one aligned group inside a warp) split the
+    // partials of output e (i = sub, sub + tpo, ...) and add their sums by shuffles
+    const int e = tid / tpo, sub = tid % tpo;
+    const bool live = e < n_out;
+    const int ec = live ? e : n_out - 1;   // idle lanes load a valid address, store nothing
+    const int hq = ec / DQ;
+    const float m = stat[2 * hq];
+    const float* po = p.part_o + (slot0 * p.hq + hq) * D + (ec % DQ) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int i = sub; i < cnt; i += tpo) {
+      const float l = __ldcg(lse0 + static_cast<int64_t>(i) * p.hq + hq);
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(po + i * step));
+      const float w = l == -INFINITY ? 0.f : fast_exp2(l - m);
+      acc.x = fmaf(w, v.x, acc.x);
+      acc.y = fmaf(w, v.y, acc.y);
+      acc.z = fmaf(w, v.z, acc.z);
+      acc.w = fmaf(w, v.w, acc.w);
+    }
+    for (int o = tpo / 2; o > 0; o >>= 1) {
+      acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+      acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+      acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+      acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+    }
+    if (live && sub == 0) {
+      const float inv = stat[2 * hq + 1];
+      T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride +
+              static_cast<int64_t>(hq) * D + (ec % DQ) * 4;
+      reinterpret_cast<uint32_t*>(ob)[0] = Mma16<T>::pack(acc.x * inv, acc.y * inv);
+      reinterpret_cast<uint32_t*>(ob)[1] = Mma16<T>::pack(acc.z * inv, acc.w * inv);
+    }
+    return;
+  }
+  for (int e0 = tid; e0 < n_out; e0 += kE * kMergeThreads) {
+    int hq[kE];
+    float m[kE];
+    const float* po[kE];
+    float4 acc[kE];
+#pragma unroll
+    for (int k = 0; k < kE; ++k) {
+      const int e = min(e0 + k * kMergeThreads, n_out - 1);   // clamped: loads stay in range
+      hq[k] = e / DQ;
+      m[k] = stat[2 * hq[k]];
+      po[k] = p.part_o + (slot0 * p.hq + hq[k]) * D + (e % DQ) * 4;
+      acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll 2
+    for (int i = 0; i < cnt; ++i) {
+      float l[kE];
+      float4 v[kE];
+#pragma unroll
+      for (int k = 0; k < kE; ++k) {
+        if (e0 + k * kMergeThreads < n_out) {
+          l[k] = __ldcg(lse0 + static_cast<int64_t>(i) * p.hq + hq[k]);
+          v[k] = __ldcg(reinterpret_cast<const float4*>(po[k] + i * step));
+        } else {
+          l[k] = -INFINITY;
+          v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kE; ++k) {
+        const float w = l[k] == -INFINITY ? 0.f : fast_exp2(l[k] - m[k]);
+        acc[k].x = fmaf(w, v[k].x, acc[k].x);
+        acc[k].y = fmaf(w, v[k].y, acc[k].y);
+        acc[k].z = fmaf(w, v[k].z, acc[k].z);
+        acc[k].w = fmaf(w, v[k].w, acc[k].w);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kE; ++k) {
+      const int e = e0 + k * kMergeThreads;
+      if (e >= n_out) continue;
+      const float inv = stat[2 * hq[k] + 1];
+      T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride +
+              static_cast<int64_t>(hq[k]) * D + (e % DQ) * 4;
+      // 4-byte stores: `out` and its row stride are only required to be 4-byte aligned
+      reinterpret_cast<uint32_t*>(ob)[0] = Mma16<T>::pack(acc[k].x * inv, acc[k].y * inv);
+      reinterpret_cast<uint32_t*>(ob)[1] = Mma16<T>::pack(acc[k].z * inv, acc[k].w * inv);
+    }
+  }
+}
+
 template <int HKV, int D>
 struct Cfg {
   static constexpr int kPPS = kConsumerWarps / HKV;  // pages per stage
@@ -101,6 +269,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NT = D / 8;   // 8-wide n tiles of the output
   constexpr int KS = D / 16;  // 16-deep k steps of Q.K^T
   extern __shared__ uint8_t smem_raw[];
+  __shared__ float s_stat[2 * kMaxHq];   // merge: per query head, max lse and 1 / sum
+  __shared__ int s_merge;                // this CTA merges the segment's sequence
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int stages = p.stages;
@@ -134,13 +304,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t total = indptr[p.batch];
   const int n = num_ctas(total, p.grid);
   const int c = blockIdx.x;
-  if (c >= n) return;
+  if (c >= n) {
+    pdl_wait();
+    zero_empty_sequences<T, D>(p, indptr, c, threadIdx.x, blockDim.x);
+    return;
+  }
   const int64_t p0 = total * c / n;
   const int64_t p1 = total * (c + 1) / n;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // let the merge kernel (launched with programmatic stream serialisation) be scheduled
-  // as SMs free up; it waits for this grid's completion before reading any partial
+  // let the next kernel (if launched with programmatic stream serialisation) be
+  // scheduled as SMs free up; it waits for this grid's completion before reading `out`
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -245,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // -------------------------------------------------------------- consumers
   pdl_wait();   // q comes from the previous kernel
+  zero_empty_sequences<T, D>(p, indptr, c, threadIdx.x, kMergeThreads);
   const int h = warp % HKV;
   const int j = warp / HKV;
   const int g = lane >> 2;        // mma row group: query head g (and g + 8)
@@ -457,17 +632,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if constexpr (C::kPPS > 1) named_barrier_sync(1, kConsumerWarps * 32);
+    if (!whole && p.inline_merge) {
+      // Publish this segment's partial and count it in; the last CTA of the sequence
+      // merges. Every CTA of the sequence arrives exactly once, also after a timed-out
+      // wait (its partial is then garbage, and the status word says so), so the counts
+      // always return to zero.
+      __threadfence();
+      named_barrier_sync(1, kMergeThreads);
+      const int cf = cta_of(seq_beg, total, n);
+      const int cnt = cta_of(seq_end - 1, total, n) - cf + 1;
+      if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(&p.arrive[cf], 1u);
+        const bool last = prev + 1u == static_cast<uint32_t>(cnt);
+        if (last) {
+          __threadfence();   // the others' partials, fenced before their arrivals
+          atomicExch(&p.arrive[cf], 0u);
+        }
+        s_merge = last ? 1 : 0;
+      }
+      named_barrier_sync(1, kMergeThreads);
+      if (s_merge) merge_sequence<T, D>(p, b, cf, cnt, s_stat, threadIdx.x);
+    }
     ++b;
     while (b < p.batch && indptr[b + 1] <= pp) ++b;
   }
 }
 
-// Combines the partials of sequences that span several CTAs; one warp per
-// (sequence, query head). Sequences finished in place by the decode kernel, and
-// sequences without pages (written as zeros here), need no merge. The lanes read the
-// partials' log-sum-exps in parallel (lane i: partial i, i + 32, ...) and the weighted
-// partial outputs are loaded four partials at a time, so the merge costs a few load
-// latencies however many CTAs the sequence spans.
+// The merge-kernel mode (DecodeParams::inline_merge == 0): the partials of sequences
+// that span several CTAs are combined by this second kernel, launched with programmatic
+// dependent launch right behind the decode grid; one warp per (sequence, query head).
+// Sequences finished in place by the decode kernel, and sequences without pages (written
+// as zeros there), need no merge. The lanes read the partials' log-sum-exps in parallel
+// (lane i: partial i, i + 32, ...) and the weighted partial outputs are loaded four
+// partials at a time, so the merge costs a few load latencies however many CTAs the
+// sequence spans, spread over (hq / 4) x batch CTAs.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -481,11 +679,7 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (hq >= p.hq) return;
   T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
-  if (beg == end) {
-#pragma unroll
-    for (int e = 0; e < DV; ++e) ob[lane * DV + e] = Elem<T>::from_f(0.f);
-    return;
-  }
+  if (beg == end) return;
   const int n = num_ctas(total, p.grid);
   const int cf = cta_of(beg, total, n), cl = cta_of(end - 1, total, n);
   if (cf == cl) return;
@@ -576,7 +770,8 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
   const size_t comb = C::kPPS > 1 ? static_cast<size_t>(kConsumerWarps) * p.group * (D + 2) * 4 : 0;
   p.smem_csr = p.batch <= kSmemCsrBatch ? 1 : 0;
   const size_t csr = p.smem_csr ? static_cast<size_t>(2 * p.batch + 1) * 4 : 0;
-  const size_t fixed = 1024 + comb + csr + 2 * 8 * 8;
+  // the static __shared__ merge state counts against the same per-CTA limit
+  const size_t fixed = 1024 + comb + csr + 2 * 8 * 8 + kStaticSmem;
   int stages = static_cast<int>((kMaxSmem - fixed) / C::kStageBytes);
   if (stages > 4) stages = 4;
   if (stages < 2) return set_error(NSLG_ERR_UNSUPPORTED, "decode: group too large for smem");
@@ -587,10 +782,11 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
-  int rc = launch_pdl("decode_tc", kern, dim3(p.grid), dim3(kThreads), smem, stream, tk, tv, p);
-  if (rc != NSLG_OK) return rc;
-  // programmatic dependent launch: the merge grid is launched while the decode grid
-  // drains and starts its work once the decode grid has completed
+  const int rc = launch_pdl("decode_tc", kern, dim3(p.grid), dim3(kThreads), smem, stream, tk,
+                            tv, p);
+  if (rc != NSLG_OK || p.inline_merge) return rc;
+  // merge-kernel mode: launched with programmatic dependent launch while the decode grid
+  // drains; it starts its work once the decode grid has completed
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.hq + 3) / 4, p.batch);
   cfg.blockDim = dim3(128);
@@ -602,8 +798,8 @@ int launch_typed(const CUtensorMap& tk, const CUtensorMap& tv, DecodeParams p,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   err = cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, D>, p);
-  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("decode_merge: ") +
-                                                              cudaGetErrorString(err));
+  if (err != cudaSuccess)
+    return set_error(NSLG_ERR_CUDA, std::string("decode_merge: ") + cudaGetErrorString(err));
   return check_launch("decode_merge");
 }
 
@@ -636,9 +832,38 @@ bool decode_tc_supported(int dtype, int hq, int hkv, int d, int page_size) {
          (hkv == 1 || hkv == 2 || hkv == 4 || hkv == 8) && hq % hkv == 0 && hq / hkv <= 16;
 }
 
+namespace {
+// The arrival counts: one 32-bit word per CTA at the head of the workspace, padded to
+// 256 bytes so that the partials behind them keep their alignment.
+int64_t arrive_bytes(int grid) { return (static_cast<int64_t>(grid) * 4 + 255) / 256 * 256; }
+
+// Which CTA combines a split sequence. In-kernel (the last CTA of the sequence to finish)
+// saves the second launch and its wait for the whole decode grid (about 1 us per call on
+// B200), but one SM then reads all the sequence's partials; the merge kernel spreads the
+// same reads over ceil(hq / 4) CTAs per sequence. The host cannot see the lengths (they
+// are on the device), so it estimates the partials per split sequence from the batch
+// alone, as for sequences of equal length: about #SMs / batch + 1 CTAs, each hq x
+// head_dim fp32 values. In-kernel when that is at most 64 KiB, or when the merge kernel
+// would get no more than 2 CTAs per sequence anyway (hq <= 8). Measured at the 8B decode
+// shapes (32 layers per graph): hq 32, batch 64: 30.7 us per layer in-kernel against
+// 31.9; hq 32, batch 1: 11.0 against 8.6; hq 4, batch 64: 14.0 against 14.8; hq 4,
+// batch 1: 7.2 against 8.1. NSLG_DECODE_MERGE=inline or =kernel forces a mode.
+constexpr int64_t kInlineMergeBytes = 64 << 10;
+int merge_inline(int batch, int hq, int d, int grid) {
+  const char* e = std::getenv("NSLG_DECODE_MERGE");
+  if (e != nullptr && std::strcmp(e, "inline") == 0) return 1;
+  if (e != nullptr && std::strcmp(e, "kernel") == 0) return 0;
+  if (hq <= 8) return 1;
+  const int64_t per_merge =
+      static_cast<int64_t>((grid + batch - 1) / batch + 1) * hq * static_cast<int64_t>(d) * 4;
+  return per_merge <= kInlineMergeBytes ? 1 : 0;
+}
+}  // namespace
+
 int64_t decode_tc_workspace_bytes(int batch, int hq, int d) {
-  const int64_t slots = static_cast<int64_t>(batch) + sm_count();
-  return slots * hq * (static_cast<int64_t>(d) + 1) * 4 + 256;
+  const int grid = sm_count();
+  const int64_t slots = static_cast<int64_t>(batch) + grid;
+  return arrive_bytes(grid) + slots * hq * (static_cast<int64_t>(d) + 1) * 4 + 256;
 }
 
 int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const void* q,
@@ -681,7 +906,8 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
   p.indptr = kv_indptr;
   p.indices = kv_indices;
   p.lpl = kv_last_page_len;
-  p.part_o = reinterpret_cast<float*>(ws);
+  p.arrive = reinterpret_cast<uint32_t*>(ws);
+  p.part_o = reinterpret_cast<float*>(ws + arrive_bytes(grid));
   p.part_lse = p.part_o + slots * hq * d;
   p.q_stride = q_stride;
   p.out_stride = out_stride;
@@ -693,6 +919,7 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.status = status;
   p.box_all_heads = box_all;
+  p.inline_merge = merge_inline(batch, hq, d, grid);
   if (dtype == NSLG_DTYPE_F16) return launch_for_type<__half>(hkv, d, tk, tv, p, stream);
   return launch_for_type<__nv_bfloat16>(hkv, d, tk, tv, p, stream);
 }

@@ -73,13 +73,15 @@ class _DeviceState:
         self.status = {}
 
     def workspace(self, device, nbytes):
+        """The decode workspace: zeroed when allocated (the kernel's arrival counts at its
+        head must start at zero; every call leaves them zero)."""
         buf = self.ws.get(device)
         if buf is not None and buf.numel() >= nbytes:
             return buf
         with self.lock:
             buf = self.ws.get(device)
             if buf is None or buf.numel() < nbytes:
-                buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
                 self.ws[device] = buf
             return buf
 

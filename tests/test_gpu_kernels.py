@@ -120,8 +120,11 @@ DECODE_CASES = [
 ]
 
 
+@pytest.mark.parametrize("mode", ["auto", "inline", "kernel"])
 @pytest.mark.parametrize("hq,hkv,d,lens", DECODE_CASES)
-def test_paged_decode_bf16(hq, hkv, d, lens):
+def test_paged_decode_bf16(hq, hkv, d, lens, mode, monkeypatch):
+    if mode != "auto":
+        monkeypatch.setenv("NSLG_DECODE_MERGE", mode)
     pk = make_paged(lens, hkv, d, 4096, torch.bfloat16, DEV, seed=len(lens) + hq)
     g = torch.Generator().manual_seed(5)
     q = torch.randn(len(lens), hq, d, generator=g).to(torch.bfloat16)
@@ -145,6 +148,38 @@ def test_paged_decode_many_sequences_split_across_ctas():
     for b in range(len(lens)):
         ref = attend_sequences([q[b:b + 1]], [sequence_kv(pk, b, "k")], [sequence_kv(pk, b, "v")])
         torch.testing.assert_close(out[b], ref[0][0], **BF16_TOL)
+
+
+@pytest.mark.parametrize("mode", ["inline", "kernel"])
+def test_paged_decode_merge_modes_and_arrival_counts(mode, monkeypatch):
+    """Both ways of combining sequences split across CTAs: inside the one decode launch by
+    the last CTA of each sequence to finish ("inline"), or by the merge kernel behind it
+    ("kernel"). After every call the per-CTA arrival counts at the workspace's head are
+    zero again, whatever the batch; the same call twice gives bit-identical outputs (the
+    inline merge does not depend on which CTA runs it). Spans from 2 to all CTAs per
+    sequence (a 40000-token sequence over every SM), empty sequences among them."""
+    monkeypatch.setenv("NSLG_DECODE_MERGE", mode)
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    g = torch.Generator().manual_seed(12)
+    for i, lens in enumerate([[5000], [1, 0, 40000, 17], [700] * 40, [3000, 0, 2]]):
+        pk = make_paged(lens, 8, 128, sum(-(-n // 16) for n in lens) + 64, torch.bfloat16,
+                        DEV, seed=70 + i)
+        q = torch.randn(len(lens), 32, 128, generator=g).to(torch.bfloat16)
+        args = (q.to(DEV), pk["pool_k"], pk["pool_v"], pk["indptr"], pk["indices"], pk["lpl"],
+                1 / math.sqrt(128))
+        out = ops.paged_decode(*args)
+        torch.cuda.synchronize(DEV)
+        ws = ops._STATE.ws[DEV]
+        assert int(ws[:sms * 4].count_nonzero()) == 0
+        assert torch.equal(ops.paged_decode(*args), out)
+        out = out.cpu()
+        for b, n in enumerate(lens):
+            if n == 0:
+                assert not bool(out[b].any())
+                continue
+            ref = attend_sequences([q[b:b + 1]], [sequence_kv(pk, b, "k")],
+                                   [sequence_kv(pk, b, "v")])
+            torch.testing.assert_close(out[b], ref[0][0], **BF16_TOL)
 
 
 def test_paged_decode_c2_shape_sampled():
