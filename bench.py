@@ -434,12 +434,14 @@ LINEAR_SHAPES = [(f"tp{tp}_{m}rows_{name}", m, n // (tp if split == "out" else 1
                                            ("down", 4096, 14336, "in"))]
 
 
-def run_linear_shapes(device, shapes=None, reps=20, copies=8):
+def run_linear_shapes(device, shapes=None, reps=20, copies=8, policies=None):
     """The tcgen05 linear kernel (ops.linear, every row count allowed) against cuBLAS
     (F.linear) on the 8B model's per-layer projections at TP = 1, 2 and 8 and 1 or 64
     rows: ``copies`` weight copies rotated between calls (the large ones then come from
     DRAM; the TP=8 ones still fit in L2 together), ``reps`` calls per CUDA graph, five
-    replays, CUDA events; frac = weight bytes / time / measured HBM bandwidth."""
+    replays, CUDA events; frac = weight bytes / time / measured HBM bandwidth.
+    ``policies``: (CTAs per SM, fewest K chunks per split) pairs of the kernel's split
+    rule to time as well (through its NSLG_LINEAR_* overrides)."""
     import torch.nn.functional as F
     from nanoslg_b200 import ops
     peak, _ = _hbm_peak()
@@ -480,6 +482,15 @@ def run_linear_shapes(device, shapes=None, reps=20, copies=8):
         gb = n * k * 2 / 1e9
         out[name] = {"shape": [m, n, k], "ours_us": t_o, "cublas_us": t_c,
                      "ours_frac": gb / (t_o * 1e-6) / peak, "cublas_frac": gb / (t_c * 1e-6) / peak}
+        for cps, minc in policies or ():
+            os.environ["NSLG_LINEAR_CTAS_PER_SM"] = str(cps)
+            os.environ["NSLG_LINEAR_MIN_CHUNKS"] = str(minc)
+            try:
+                out[name].setdefault("ours_us_by_policy", {})[f"cps{cps}_min{minc}"] = \
+                    timeit(ours)
+            finally:
+                os.environ.pop("NSLG_LINEAR_CTAS_PER_SM", None)
+                os.environ.pop("NSLG_LINEAR_MIN_CHUNKS", None)
         del ws
         torch.cuda.empty_cache()
     ops.check_device_status(device)
@@ -938,8 +949,59 @@ def run_allreduce(device, world, rank, hidden=4096, rows_list=(1, 64, 256), call
             del g
     os.environ.pop("NSLG_TP_TWO_SHOT", None)
     ops.check_device_status(device)
+    out["gemm_then_reduce"] = _gemm_reduce_timing(device, world, rank, peer, hidden, calls,
+                                                  replays)
     peer.close()
     return {"world": world, "hidden": hidden, "dtype": "bf16", **out}
+
+
+def _gemm_reduce_timing(device, world, rank, peer, hidden, calls, replays):
+    """A RowParallel product (o_proj of the 8B model at TP=world: [rows, 4096/world] x
+    [4096, 4096/world]^T) followed by the fused reduction + residual + RMSNorm, as the
+    decode step runs it: with the push in the reduction kernel (``separate_us``) and with
+    the GEMM pushing its own rows (nslg_linear_tp_push, ``fused_push_us``). Pairs of calls
+    captured back to back in a CUDA graph; CUDA events, max over ranks, us per pair."""
+    from nanoslg_b200 import ops
+    bf = torch.bfloat16
+    k = 4096 // world
+    res = {}
+    for rows in (1, 16):
+        x = torch.randn(rows, k, device=device).to(bf)
+        wt = (torch.randn(hidden, k, device=device) / k ** 0.5).to(bf)
+        r = torch.randn(rows, hidden, device=device).to(bf)
+        nw = torch.ones(hidden, dtype=bf, device=device)
+        for name, fuse in (("separate_us", False), ("fused_push_us", True)):
+            peer.fuse_push = fuse
+
+            def pair():
+                y = peer.linear_push(x, wt) if fuse else None
+                if y is None:
+                    y = ops.linear(x, wt)
+                return peer.allreduce_add_norm(y, r, nw, 1e-5)
+
+            for _ in range(3):
+                pair()
+            torch.cuda.synchronize(device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(calls):
+                    pair()
+            g.replay()
+            torch.cuda.synchronize(device)
+            torch.distributed.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(replays):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (calls * replays)], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            res.setdefault(f"rows{rows}", {})[name] = round(float(t.item()), 2)
+            del g
+    peer.fuse_push = True
+    ops.check_device_status(device)
+    return {"shape": f"[rows, {k}] x [{hidden}, {k}]^T", **res}
 
 
 # ------------------------------------------------------------------------ parity
@@ -1050,6 +1112,34 @@ def _allreduce_parity(device, world, rank, hidden=4096):
             ok = False
         res_ok[name] = bool(ok)
     os.environ.pop("NSLG_TP_TWO_SHOT", None)
+    # the RowParallel GEMM pushing its own rows (nslg_linear_tp_push), then the reduction
+    ok = True
+    k = 4096 // world
+    for it, rows in enumerate((1, 16, 5)):
+        g = torch.Generator().manual_seed(500 + 10 * it + rank)
+        x = torch.randn(rows, k, generator=g).to(bf).to(device)
+        wt = (torch.randn(hidden, k, generator=g) / k ** 0.5).to(bf).to(device)
+        gs = torch.Generator().manual_seed(77 + it)
+        res = torch.randn(rows, hidden, generator=gs).to(bf)
+        w = (1 + 0.1 * torch.randn(hidden, generator=gs)).to(bf)
+        part = peer.linear_push(x, wt)
+        if part is None:
+            ok = False
+            break
+        r_dev = res.to(device)
+        peer.allreduce_add_norm(part, r_dev, w.to(device), 1e-5)
+        parts = [torch.empty_like(part) for _ in range(world)]
+        torch.distributed.all_gather(parts, part)
+        s = parts[0].float()
+        for p in parts[1:]:
+            s = s + p.float()
+        h_want = (res.to(device).float() + s.to(bf).float()).to(bf)
+        ok = ok and torch.equal(r_dev, h_want)
+    try:
+        ops.check_device_status(device)
+    except RuntimeError:
+        ok = False
+    res_ok["fused_gemm_push"] = bool(ok)
     peer.close()
     return {"world": world, "rows": [64, 1, 64], "ok": all(res_ok.values()), "modes": res_ok,
             "check": "new residual bit-equal to bf16(bf16(fp32 rank-order sum) + residual)"}
@@ -1165,6 +1255,8 @@ def main():
                          "parity: only the sharded-path token / reduction checks; "
                          "decode-shapes: decode attention at the 8B model's decode shapes; "
                          "linear: the tcgen05 linear kernel against cuBLAS per 8B shape")
+    ap.add_argument("--linear-sweep", action="store_true",
+                    help="--only linear: also time the kernel under other split policies")
     ap.add_argument("--linear-shape", default=None,
                     help="with --only linear: one shape 'rows,out,in' (e.g. 64,6144,4096)")
     a = ap.parse_args()
@@ -1247,9 +1339,11 @@ def main():
         if a.linear_shape:
             m, n, k = (int(v) for v in a.linear_shape.split(","))
             shapes = [(f"rows{m}_out{n}_in{k}", m, n, k)]
+        policies = [(1, 8), (2, 8), (1, 2), (2, 2), (2, 4)] if a.linear_sweep else None
         if rank == 0:
             print(json.dumps({"case": "linear only", "linear_shapes":
-                              run_linear_shapes(device, shapes)}), flush=True)
+                              run_linear_shapes(device, shapes, policies=policies)}),
+                  flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
         return 0

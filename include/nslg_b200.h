@@ -342,6 +342,32 @@ int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int world, int ra
                               void* out, int64_t out_stride, float eps, int64_t timeout_ns,
                               uint32_t* dev_status, void* stream);
 
+/* The RowParallel product and its collective in one kernel: nslg_linear (y = x . W^T,
+ * `rows` <= 256 rows, y the caller's [rows, out_features] with 16-byte aligned rows) that
+ * also stores y's rows, packed with the reduction's call numbers, into every peer's stage
+ * buffer over NVLink as soon as each tile is final -- the one-shot push that
+ * nslg_tp_allreduce_rmsnorm would otherwise do after the product.  y stays this rank's
+ * partial (the reduction reads it).  Arguments after y_stride as in
+ * nslg_tp_allreduce_rmsnorm (out_features is its `hidden`); counters are only read.  Must
+ * be followed on the same stream, before any other reduction call of the group, by
+ * nslg_tp_reduce_pushed_rmsnorm on the same y, rows and buffers.  Replaces
+ * RowParallelLinear.forward's F.linear + all-reduce (tp_layers.py:148-158,
+ * parallel.py:167-172) for decode steps. */
+int nslg_linear_tp_push(int dtype, int rows, int out_features, int in_features, const void* x,
+                        int64_t x_stride, const void* weight, int64_t w_stride, void* y,
+                        int64_t y_stride, int world, int rank, void* const* stage_bufs,
+                        int64_t stage_bytes, const void* counters, uint32_t* dev_status,
+                        void* stream);
+
+/* nslg_tp_allreduce_rmsnorm without its push: the partial rows were already pushed by
+ * nslg_linear_tp_push (always the one-shot layout). Same arguments and results. */
+int nslg_tp_reduce_pushed_rmsnorm(int dtype, int rows, int hidden, int world, int rank,
+                                  const void* partial, int64_t partial_stride,
+                                  void* const* stage_bufs, int64_t stage_bytes,
+                                  void* counters, void* residual, int64_t residual_stride,
+                                  const void* weight, void* out, int64_t out_stride, float eps,
+                                  int64_t timeout_ns, uint32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,11 @@ SIGNATURES = {
     "nslg_ipc_free": (_i32, [_vp]),
     "nslg_tp_allreduce_rmsnorm": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp,
                                          _vp, _i64, _vp, _vp, _i64, _f32, _i64, _vp, _vp]),
+    "nslg_tp_reduce_pushed_rmsnorm": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64,
+                                             _vp, _vp, _i64, _vp, _vp, _i64, _f32, _i64, _vp,
+                                             _vp]),
+    "nslg_linear_tp_push": (_i32, [_i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _i32,
+                                   _i32, _vp, _i64, _vp, _vp, _vp]),
 }
 
 IPC_HANDLE_BYTES = 64

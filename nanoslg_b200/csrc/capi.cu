@@ -257,7 +257,54 @@ int nslg_linear(int dtype, int rows, int out_features, int in_features, const vo
     return set_error(NSLG_ERR_ARG,
                      "linear: x and weight rows must be 16-byte aligned and strides cover the rows");
   return launch_linear_tc(dtype, rows, out_features, in_features, x, x_stride, weight, w_stride,
-                          y, y_stride, dev_status, static_cast<cudaStream_t>(stream));
+                          y, y_stride, nullptr, dev_status, static_cast<cudaStream_t>(stream));
+}
+
+int nslg_linear_tp_push(int dtype, int rows, int out_features, int in_features, const void* x,
+                        int64_t x_stride, const void* weight, int64_t w_stride, void* y,
+                        int64_t y_stride, int world, int rank, void* const* stage_bufs,
+                        int64_t stage_bytes, const void* counters, uint32_t* dev_status,
+                        void* stream) {
+  g_last_error.clear();
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16)
+    return set_error(NSLG_ERR_ARG, "linear_tp_push: dtype must be bfloat16 or float16");
+  if (rows < 0 || out_features <= 0 || in_features <= 0)
+    return set_error(NSLG_ERR_ARG, "linear_tp_push: bad shape");
+  if (world < 2 || world > NSLG_TP_MAX_WORLD || rank < 0 || rank >= world)
+    return set_error(NSLG_ERR_ARG, "linear_tp_push: need 2 <= world <= 8 and 0 <= rank < world");
+  if (rows == 0) return NSLG_OK;
+  if (!linear_tc_supported(dtype, rows, out_features, in_features))
+    return set_error(NSLG_ERR_UNSUPPORTED, "linear_tp_push: needs 1 <= rows <= " +
+                                               std::to_string(kLinearMaxRows) +
+                                               " and in_features a multiple of 64");
+  if (out_features % 8)
+    return set_error(NSLG_ERR_ARG, "linear_tp_push: out_features must be a multiple of 8");
+  if (!x || !weight || !y || !stage_bufs || !counters)
+    return set_error(NSLG_ERR_ARG, "linear_tp_push: null pointer");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(y) || !aligned16(counters) ||
+      (x_stride * 2) % 16 || (w_stride * 2) % 16 || (y_stride * 2) % 16 ||
+      x_stride < in_features || w_stride < in_features || y_stride < out_features)
+    return set_error(NSLG_ERR_ARG,
+                     "linear_tp_push: x, weight and y rows must be 16-byte aligned and strides "
+                     "cover the rows");
+  TpPush push{};
+  int64_t region = 0, slot = 0;
+  tp_stage_geometry(stage_bytes, world, &region, &slot);
+  if (2 * static_cast<int64_t>(out_features) * 2 * rows > region)
+    return set_error(NSLG_ERR_WORKSPACE, "linear_tp_push: " + std::to_string(rows) +
+                                             " rows do not fit the stage buffers");
+  for (int i = 0; i < world; ++i) {
+    if (!stage_bufs[i] || !aligned16(stage_bufs[i]))
+      return set_error(NSLG_ERR_ARG, "linear_tp_push: bad stage buffer");
+    push.stage[i] = static_cast<uint8_t*>(stage_bufs[i]);
+  }
+  push.counters = static_cast<const uint32_t*>(counters);
+  push.slot_bytes = slot;
+  push.region_bytes = region;
+  push.world = world;
+  push.rank = rank;
+  return launch_linear_tc(dtype, rows, out_features, in_features, x, x_stride, weight, w_stride,
+                          y, y_stride, &push, dev_status, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -114,8 +114,33 @@ int launch_paged_prefill_tc(int dtype, int batch, int hq, int hkv, const void* q
 // bf16 / fp16, K a multiple of 64 (linear_tc.cu).
 constexpr int kLinearMaxRows = 256;
 bool linear_tc_supported(int dtype, int M, int N, int K);
+
+// Blocks of every tensor-parallel reduction call (tp_allreduce.cu). Block b numbers its
+// calls with counter word b and handles rows b, b + kTpReduceGrid, ...; a producer that
+// pushes row m into the peers' stage buffers tags it with counter word m % kTpReduceGrid.
+constexpr int kTpReduceGrid = 128;
+
+// Where a linear layer pushes its output rows as this rank's partial of a one-shot
+// tensor-parallel reduction: the stage buffers of every rank (this one's included, not
+// written), this rank's call counters, and the slot / source-region geometry the
+// reduction kernel uses for `world` ranks (tp_stage_geometry).
+struct TpPush {
+  uint8_t* stage[NSLG_TP_MAX_WORLD];
+  const uint32_t* counters;
+  int64_t slot_bytes, region_bytes;
+  int world, rank;
+};
+// [2 slots][world sources][rows][2 x row bytes]: region (one source's rows of one slot)
+// and slot sizes of a stage buffer of stage_bytes.
+inline void tp_stage_geometry(int64_t stage_bytes, int world, int64_t* region, int64_t* slot) {
+  *region = (stage_bytes / 2 / world) & ~static_cast<int64_t>(15);
+  *slot = *region * world;
+}
+
+// push == nullptr: y only. Otherwise also every row of y, packed with this rank's call
+// numbers, into every peer's stage buffer (out_features is then the reduced row length).
 int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_stride,
                      const void* w, int64_t w_stride, void* y, int64_t y_stride,
-                     uint32_t* status, cudaStream_t stream);
+                     const TpPush* push, uint32_t* status, cudaStream_t stream);
 
 }  // namespace nslg

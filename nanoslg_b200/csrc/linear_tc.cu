@@ -23,10 +23,20 @@
 // TP shards). The s CTAs of a tile form one thread-block cluster, and the split-K sum
 // never leaves the chip: each CTA stages its fp32 partial tile in its own shared memory
 // (the stage ring, idle once the MMAs are done), the cluster synchronises, and CTA j
-// sums rows [128 j / s, 128 (j + 1) / s) of the tile over the s partials, read through
-// distributed shared memory in rank order (the same order on every call), rounds once
-// and writes them to y; a second cluster barrier keeps every partial in place until all
-// readers are done.
+// sums rows [8 floor(16 j / s), 8 floor(16 (j + 1) / s)) of the tile over the s
+// partials, read through distributed shared memory in rank order (the same order on
+// every call), rounds once and writes them to y; a second cluster barrier keeps every
+// partial in place until all readers are done.
+//
+// Fused tensor-parallel push (nslg_linear_tp_push). For a RowParallel product (o_proj,
+// down_proj) of a TP decode step, y is this rank's partial of the all-reduce that
+// follows. With the push on, each CTA, once its rows of y are final, also stores them
+// packed with the reduction's call numbers straight into every peer's stage buffer over
+// NVLink (the layout nslg_tp_allreduce_rmsnorm's one-shot mode reads), so the transfer
+// runs while other tiles are still on the tensor cores and the reduction kernel that
+// follows only waits for, sums and normalises the rows (nslg_tp_reduce_pushed_rmsnorm).
+// The compute and the collective's data movement are one kernel; no load ever reads a
+// peer's memory.
 //
 // Pipeline (up to two CTAs per SM, 256 threads each):
 //   warp 0     TMA producer: the first ring's worth of weight boxes before waiting for
@@ -44,6 +54,7 @@
 #include <cooperative_groups.h>
 #include <cuda.h>
 
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
@@ -72,8 +83,54 @@ struct LinParams {
   void* y;
   int64_t y_stride;
   int M, N, Mp, kc, splits, stages, tmem_cols;
+  int do_push;      // also push y's rows to the peers (push)
+  TpPush push;
   uint32_t* status;
 };
+
+// First row of the tile that CTA j of s sums in the split-K reduction: a multiple of 8
+// (whole 16-byte vectors of a y row for the push), every CTA at least 16 rows.
+__device__ __forceinline__ int split_row_lo(int j, int s) { return 8 * ((16 * j) / s); }
+
+__device__ __forceinline__ void st_sys_v4(void* ptr, uint32_t a, uint32_t b, uint32_t c,
+                                          uint32_t d) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(a),
+               "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// The push of a fused RowParallel product: the rows [r_lo, r_hi) of tile t of y that
+// this CTA wrote, for every activation row m, go to every peer's stage buffer as this
+// rank's partial of the one-shot reduction that tp_allreduce.cu runs next (source
+// region `rank` of slot call & 1, row m, 16-byte vector n / 8), packed as that kernel
+// reads them: {d0, call, d1, call} per 16-byte store, call = this rank's counter word of
+// the reduction block that owns row m, plus one. Plain stores over NVLink (no multicast,
+// no loads from peer memory); nothing waits here: the reduction kernel polls for the
+// words.
+template <typename T>
+__device__ void push_rows(const LinParams& p, int t, int r_lo, int r_hi) {
+  const int nvec = (r_hi - r_lo) / 8;
+  const int64_t units_per_row = 2 * static_cast<int64_t>(p.N / 8);
+  const T* y = static_cast<const T*>(p.y);
+  for (int u = threadIdx.x; u < p.M * nvec; u += kThreads) {
+    const int m = u / nvec;
+    const int n = t * kTileN + r_lo + 8 * (u % nvec);
+    if (n >= p.N) continue;
+    const uint4 v =
+        __ldcg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(m) * p.y_stride + n));
+    const uint32_t call =
+        *reinterpret_cast<const volatile uint32_t*>(p.push.counters + m % kTpReduceGrid) + 1u;
+    const int64_t off = static_cast<int64_t>(call & 1u) * p.push.slot_bytes +
+                        p.push.rank * p.push.region_bytes +
+                        (static_cast<int64_t>(m) * units_per_row + 2 * (n / 8)) * 16;
+    for (int d = 0; d < p.push.world; ++d) {
+      if (d == p.push.rank) continue;
+      uint8_t* dst = p.push.stage[d] + off;
+      st_sys_v4(dst, v.x, call, v.y, call);
+      st_sys_v4(dst + 16, v.z, call, v.w, call);
+    }
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -231,8 +288,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     cluster.sync();                                 // every partial is staged
     if (!*abort_flag) {
       T* y = static_cast<T*>(p.y);
-      const int r_lo = kTileN * j / p.splits;
-      const int rows_s = kTileN * (j + 1) / p.splits - r_lo;
+      const int r_lo = split_row_lo(j, p.splits);
+      const int rows_s = split_row_lo(j + 1, p.splits) - r_lo;
       const int E = rows_s * p.M;                   // (row, m) elements of this CTA's rows
       const float* src[kMaxSplits];
 #pragma unroll
@@ -253,6 +310,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     cluster.sync();                                 // no partial is read any more
   }
+  if (p.do_push) {
+    __syncthreads();      // y's rows of this CTA are written (read back through L2)
+    if (!*abort_flag)
+      push_rows<T>(p, t, p.splits == 1 ? 0 : split_row_lo(j, p.splits),
+                   p.splits == 1 ? kTileN : split_row_lo(j + 1, p.splits));
+  }
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -265,14 +328,24 @@ struct Plan {
   int Mp, n_tiles, kc, splits, grid, stages, tmem_cols;
 };
 
+// Split policy overrides, for measurements: NSLG_LINEAR_CTAS_PER_SM (1 or 2: the grid
+// may fill the SMs once or twice over with K splits) and NSLG_LINEAR_MIN_CHUNKS (the
+// fewest 64-element K chunks a split may have, 1 to 64).
+int env_int(const char* name, int dflt, int lo, int hi) {
+  const char* e = std::getenv(name);
+  if (e == nullptr || e[0] == '\0') return dflt;
+  const int v = std::atoi(e);
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
 Plan plan_for(int M, int N, int K) {
   Plan pl{};
   pl.Mp = (M + 15) / 16 * 16;
   pl.n_tiles = (N + kTileN - 1) / kTileN;
   pl.kc = K / kChunk;
-  const int sms = sm_count();
+  const int sms = sm_count() * env_int("NSLG_LINEAR_CTAS_PER_SM", 1, 1, 2);
   int s = sms / pl.n_tiles;                    // tiles x splits <= #SMs
-  int s_max = pl.kc / kMinChunksPerSplit;
+  int s_max = pl.kc / env_int("NSLG_LINEAR_MIN_CHUNKS", kMinChunksPerSplit, 1, 64);
   if (s_max > kMaxSplits) s_max = kMaxSplits;
   if (s > s_max) s = s_max;
   if (s < 1) s = 1;
@@ -297,7 +370,7 @@ bool linear_tc_supported(int dtype, int M, int N, int K) {
 
 int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_stride,
                      const void* w, int64_t w_stride, void* y, int64_t y_stride,
-                     uint32_t* status, cudaStream_t stream) {
+                     const TpPush* push, uint32_t* status, cudaStream_t stream) {
   const Plan pl = plan_for(M, N, K);
   CUtensorMap tw, tx;
   // W [N, K] and x [M, K], K innermost; boxes [64 x 128] and [64 x Mp] with 128-byte swizzle
@@ -317,6 +390,8 @@ int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_st
   p.splits = pl.splits;
   p.stages = pl.stages;
   p.tmem_cols = pl.tmem_cols;
+  p.do_push = push != nullptr ? 1 : 0;
+  if (push != nullptr) p.push = *push;
   p.status = status;
   const size_t smem = 1024 + static_cast<size_t>(pl.stages) * (kWBytes + pl.Mp * 128) + 256;
   auto kern = dtype == NSLG_DTYPE_F16 ? linear_tc_kernel<__half> : linear_tc_kernel<__nv_bfloat16>;

@@ -55,7 +55,7 @@
 namespace nslg {
 namespace {
 
-constexpr int kGrid = 128;          // blocks per call, the same on every rank and call
+constexpr int kGrid = kTpReduceGrid;   // blocks per call, the same on every rank and call
 constexpr int kThreads = 256;
 constexpr int kVecPerThread = 4;    // 16-byte vectors of a row per thread (hidden <= 8192 bf16)
 // one-shot push volume per rank ((world - 1) x rows x row bytes) from which two-shot is used
@@ -83,6 +83,7 @@ struct ArParams {
   void* out;
   int64_t o_stride;
   int rows, hidden, world, rank, two_shot;
+  int pushed;       // phase 1 already done by the producer (nslg_linear_tp_push)
   float eps;
   uint64_t timeout_ns;
   uint32_t* status;
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
 
   // 1. push this rank's partial rows, packed with the call number: one-shot, the whole
   //    row to every peer; two-shot, column slice j of the row to rank j only
-  for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+  for (int row = p.pushed ? p.rows : blockIdx.x; row < p.rows; row += gridDim.x) {
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.partial) +
                                                       row * p.p_stride);
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
@@ -333,13 +334,12 @@ extern "C" int nslg_ipc_free(void* dev_ptr) {
   return NSLG_OK;
 }
 
-extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int world, int rank,
-                                         const void* partial, int64_t partial_stride,
-                                         void* const* stage_bufs, int64_t stage_bytes,
-                                         void* counters, void* residual, int64_t residual_stride,
-                                         const void* weight, void* out, int64_t out_stride,
-                                         float eps, int64_t timeout_ns, uint32_t* dev_status,
-                                         void* stream) {
+namespace {
+int tp_reduce(int dtype, int rows, int hidden, int world, int rank, const void* partial,
+              int64_t partial_stride, void* const* stage_bufs, int64_t stage_bytes,
+              void* counters, void* residual, int64_t residual_stride, const void* weight,
+              void* out, int64_t out_stride, float eps, int64_t timeout_ns,
+              uint32_t* dev_status, void* stream, int pushed) {
   if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16 && dtype != NSLG_DTYPE_F32)
     return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad dtype");
   if (world < 2 || world > NSLG_TP_MAX_WORLD || rank < 0 || rank >= world)
@@ -354,7 +354,8 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
     return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: null pointer");
   // [2 slots][world][rows][2 * row bytes]
   const int64_t row_bytes = static_cast<int64_t>(hidden) * esz;
-  const int64_t region = (stage_bytes / 2 / world) & ~static_cast<int64_t>(15);
+  int64_t region = 0, slot = 0;
+  tp_stage_geometry(stage_bytes, world, &region, &slot);
   if (2 * row_bytes * rows > region)
     return set_error(NSLG_ERR_WORKSPACE, "tp_allreduce_rmsnorm: " + std::to_string(rows) +
                                              " rows need " + std::to_string(4 * row_bytes * rows * world) +
@@ -373,7 +374,7 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
   p.partial = partial;
   p.p_stride = partial_stride;
   p.region_bytes = region;
-  p.slot_bytes = region * world;
+  p.slot_bytes = slot;
   p.counters = static_cast<uint32_t*>(counters);
   p.residual = residual;
   p.r_stride = residual_stride;
@@ -393,9 +394,10 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
   const int vec = 16 / esz;
   const bool two_ok = world > 2 && hidden % (world * vec) == 0;
   const int force = two_shot_override();
-  p.two_shot = two_ok && (force >= 0 ? force == 1
-                                     : static_cast<int64_t>(rows) * row_bytes * (world - 1) >=
-                                           kTwoShotBytes);
+  p.two_shot = !pushed && two_ok &&
+               (force >= 0 ? force == 1
+                           : static_cast<int64_t>(rows) * row_bytes * (world - 1) >= kTwoShotBytes);
+  p.pushed = pushed;
   p.timeout_ns = static_cast<uint64_t>(timeout_ns);
   p.status = dev_status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -407,4 +409,31 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
                       dim3(kGrid), dim3(kThreads), 0, st, p);
   return launch_pdl("tp_allreduce_rmsnorm", tp_allreduce_rmsnorm_kernel<float>, dim3(kGrid),
                     dim3(kThreads), 0, st, p);
+}
+}  // namespace
+
+extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int world, int rank,
+                                         const void* partial, int64_t partial_stride,
+                                         void* const* stage_bufs, int64_t stage_bytes,
+                                         void* counters, void* residual, int64_t residual_stride,
+                                         const void* weight, void* out, int64_t out_stride,
+                                         float eps, int64_t timeout_ns, uint32_t* dev_status,
+                                         void* stream) {
+  return tp_reduce(dtype, rows, hidden, world, rank, partial, partial_stride, stage_bufs,
+                   stage_bytes, counters, residual, residual_stride, weight, out, out_stride,
+                   eps, timeout_ns, dev_status, stream, 0);
+}
+
+extern "C" int nslg_tp_reduce_pushed_rmsnorm(int dtype, int rows, int hidden, int world,
+                                             int rank, const void* partial,
+                                             int64_t partial_stride, void* const* stage_bufs,
+                                             int64_t stage_bytes, void* counters,
+                                             void* residual, int64_t residual_stride,
+                                             const void* weight, void* out,
+                                             int64_t out_stride, float eps,
+                                             int64_t timeout_ns, uint32_t* dev_status,
+                                             void* stream) {
+  return tp_reduce(dtype, rows, hidden, world, rank, partial, partial_stride, stage_bufs,
+                   stage_bytes, counters, residual, residual_stride, weight, out, out_stride,
+                   eps, timeout_ns, dev_status, stream, 1);
 }

@@ -19,7 +19,8 @@ path:
 * The projections of decode-sized forwards (at most 256 rows: decode steps, the LM head
   on the last position) run the tcgen05 linear kernel (``ops.linear``, nslg_linear);
   larger forwards (prefill) stay cuBLAS GEMMs. The collectives are NCCL or the fused
-  peer-memory reduction.
+  peer-memory reduction; with the latter, a RowParallel product the tcgen05 kernel
+  takes also pushes its partial rows to the peers from inside the GEMM.
 """
 import math
 from typing import List
@@ -270,12 +271,15 @@ class _LlamaStage(nn.Module):
             h, residual = layer(h, self.cos, self.sin, cache_ctx, residual)
         if residual is not None:
             # the stage's output is the residual stream after its last block (with an
-            # active peer reduction, h is still this rank's partial down_proj output;
-            # slicing the last position commutes with the sum)
+            # active peer reduction, h is still this rank's partial down_proj output)
             if self.is_last:
-                if last_only:
+                if last_only and peer is None:
                     h, residual = h[:, -1:].contiguous(), residual[:, -1:].contiguous()
+                # with an active peer reduction every row is reduced (the GEMM may already
+                # have pushed them all to the peers) and the last position taken after
                 h, _ = self.norm.add_forward(h, residual, peer)
+                if last_only and peer is not None:
+                    h = h[:, -1:].contiguous()
                 if greedy and last_only:
                     return self._greedy(h)
                 return self.lm_head(h)

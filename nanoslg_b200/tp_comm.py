@@ -6,13 +6,17 @@ the residual and applies the next RMSNorm (models.py:169-172).  ``PeerAllReduce`
 the three in one kernel (``nslg_tp_allreduce_rmsnorm``) over buffers that every rank of
 the TP group maps from every other rank with CUDA IPC (plain NVLink peer stores, no
 multicast objects).  The model marks forwards whose rows fit the buffers
-(decode steps) ``active``; larger forwards (prefill) keep the NCCL all-reduce.
+(decode steps) ``active``; larger forwards (prefill) keep the NCCL all-reduce.  For
+decode batches the tcgen05 linear kernel takes, the RowParallel GEMM itself pushes its
+output rows to the peers (``linear_push``, one kernel for the product and the
+collective's transfer) and the reduction kernel only gathers, sums and normalises.
 
 Every rank of the group has to run the same sequence of calls with the same row
 counts, as the TP ranks of the reference already do (they run the same forward on the
 same broadcast token ids).
 """
 import ctypes
+import os
 
 import torch
 import torch.distributed as dist
@@ -39,6 +43,11 @@ class PeerAllReduce:
         esz = torch.tensor([], dtype=dtype).element_size()
         self.stage_bytes = 4 * world * max_rows * hidden * esz
         self.active = False
+        # RowParallel products of decode batches the tcgen05 linear kernel takes push their
+        # partial rows to the peers from inside the GEMM (nslg_linear_tp_push);
+        # NSLG_TP_FUSED_PUSH=0 keeps the push in the reduction kernel instead
+        self.fuse_push = os.environ.get("NSLG_TP_FUSED_PUSH", "1") != "0"
+        self._pushed_ptr = None        # the partial whose rows were pushed by the GEMM
         self._own, self._opened = [], []
         with torch.cuda.device(self.device):
             stage, h_stage = self._alloc(self.stage_bytes)
@@ -68,6 +77,31 @@ class PeerAllReduce:
     def fits(self, rows):
         return rows <= self.max_rows
 
+    def linear_push(self, x, weight):
+        """This rank's RowParallel product y = x . weight^T with its rows pushed into every
+        peer's stage buffer by the same kernel (nslg_linear_tp_push: the GEMM and the
+        collective's data movement in one launch). Returns y, the partial that the next
+        ``allreduce_add_norm`` reduces (it then skips its own push), or None when the
+        fused kernel does not take these operands (the caller runs the plain product)."""
+        if not self.fuse_push or not ops.linear_supported(x, weight):
+            return None
+        k, n = x.shape[-1], weight.shape[0]
+        if n != self.hidden or x.dtype != self.dtype:
+            return None
+        try:
+            rows, xs = ops._rows(x.unsqueeze(-2), "x")
+        except ValueError:
+            return None
+        if rows > self.max_rows or xs % 8 or x.data_ptr() % 16:
+            return None
+        out = torch.empty(x.shape[:-1] + (n,), dtype=x.dtype, device=x.device)
+        N.call("nslg_linear_tp_push", ops._dtype_code(x), rows, n, k, ops._ptr(x), xs,
+               ops._ptr(weight), weight.stride(0), ops._ptr(out), n, self.world, self.rank,
+               ctypes.cast(self._stage_arr, ctypes.c_void_p), self.stage_bytes,
+               ops._ptr(self.counters), ops._ptr(self.status), ops._stream(x))
+        self._pushed_ptr = out.data_ptr()
+        return out
+
     def allreduce_add_norm(self, partial, residual, weight, eps, out=None):
         """residual <- residual + sum over the group of ``partial`` (in place); returns
         rmsnorm(residual) * weight, or ``residual`` itself when ``weight`` is None."""
@@ -86,7 +120,11 @@ class PeerAllReduce:
             if out is None:
                 out = torch.empty_like(p2)
             o2 = out.view(rows, hidden)
-        N.call("nslg_tp_allreduce_rmsnorm", ops._dtype_code(partial), rows, hidden,
+        # the GEMM that produced ``partial`` already pushed its rows: reduce only
+        pushed = self._pushed_ptr is not None and partial.data_ptr() == self._pushed_ptr
+        self._pushed_ptr = None
+        fn = "nslg_tp_reduce_pushed_rmsnorm" if pushed else "nslg_tp_allreduce_rmsnorm"
+        N.call(fn, ops._dtype_code(partial), rows, hidden,
                self.world, self.rank, ops._ptr(p2), p2.stride(0),
                ctypes.cast(self._stage_arr, ctypes.c_void_p), self.stage_bytes,
                ops._ptr(self.counters), ops._ptr(r2), r2.stride(0),

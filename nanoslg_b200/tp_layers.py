@@ -68,10 +68,13 @@ class RowParallelLinear(nn.Module):
     peer_reduce = None
 
     def forward(self, x):
+        if (self.tp_size > 1 and self.peer_reduce is not None and self.peer_reduce.active
+                and self.bias is None):
+            # the partial product; the GEMM pushes it to the peers itself when it can
+            out = self.peer_reduce.linear_push(x, self.weight)
+            return out if out is not None else ops.linear(x, self.weight)
         out = ops.linear(x, self.weight)
         if self.tp_size > 1:
-            if self.peer_reduce is not None and self.peer_reduce.active and self.bias is None:
-                return out
             out = all_reduce_tp(out)
         if self.bias is not None:
             out = out + self.bias

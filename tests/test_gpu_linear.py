@@ -110,3 +110,18 @@ def test_linear_refuses_what_it_does_not_cover():
     rc = lib.nslg_linear(N.DTYPE_BF16, 300, 256, 128, x.data_ptr(), 128, w.data_ptr(), 128,
                          x.data_ptr(), 256, None, torch.cuda.current_stream(DEV).cuda_stream)
     assert rc == N.ERR_UNSUPPORTED and b"rows" in lib.nslg_last_error()
+
+
+@pytest.mark.parametrize("cps,minc", [(2, 8), (1, 2), (2, 2), (2, 1)])
+@pytest.mark.parametrize("m,n,k", [(64, 6144, 4096), (1, 4096, 512), (16, 4096, 1792),
+                                   (64, 768, 4096), (5, 1000, 192)])
+def test_linear_split_policies(cps, minc, m, n, k, monkeypatch):
+    """Other split rules (two CTAs per SM's worth of K splits, splits of 1 to 8 chunks,
+    clusters up to 8): the same products within the same tolerance, still deterministic."""
+    monkeypatch.setenv("NSLG_LINEAR_CTAS_PER_SM", str(cps))
+    monkeypatch.setenv("NSLG_LINEAR_MIN_CHUNKS", str(minc))
+    dt = torch.bfloat16
+    x, w = _problem(m, n, k, dt, seed=m + n + k + cps + minc)
+    y = ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS)
+    torch.testing.assert_close(y, _ref(x, w), **TOL[dt])
+    assert torch.equal(ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS), y)
