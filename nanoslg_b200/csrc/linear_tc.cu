@@ -16,11 +16,12 @@
 // lives in TMEM. Four tcgen05.mma (K = 16 each) per 64-element chunk of K.
 //
 // Work split. CTA c computes tile c / s over the K-chunk range of split c % s, where
-// the host picks s (splits per tile, at most 8) so that n_tiles * s fills the SMs
-// without cutting K into pieces of fewer than kMinChunksPerSplit chunks: s = 1 for wide
-// products (each CTA one whole tile, written straight to y; two CTAs fit on an SM, so a
-// 224-tile product runs at once on 148 SMs), s > 1 for narrow ones (o_proj, down_proj,
-// TP shards). The s CTAs of a tile form one thread-block cluster, and the split-K sum
+// the host picks s (splits per tile, at most 8) so that n_tiles * s fills the SMs twice
+// over (two CTAs fit on an SM) without cutting K into pieces of fewer than
+// kMinChunksPerSplit chunks, as a power of two when the grid exceeds the SM count (so
+// the clusters pack into the GPCs in one wave): s = 1 for wide products (each CTA one whole tile, written straight to y; a 224-tile
+// product runs at once on 148 SMs), s > 1 for narrow ones (o_proj, down_proj, TP
+// shards). The s CTAs of a tile form one thread-block cluster, and the split-K sum
 // never leaves the chip: each CTA stages its fp32 partial tile in its own shared memory
 // (the stage ring, idle once the MMAs are done), the cluster synchronises, and CTA j
 // sums rows [8 floor(16 j / s), 8 floor(16 (j + 1) / s)) of the tile over the s
@@ -69,7 +70,8 @@ constexpr int kChunk = 64;        // K elements per stage: one 128-byte swizzle 
 constexpr int kThreads = 256;     // warp 0 TMA, warp 1 MMA, warps 4-7 epilogue
 constexpr int kMaxStages = 8;
 constexpr int kMinStages = 3;
-constexpr int kMinChunksPerSplit = 8;   // 128 KiB of weights per CTA at least
+constexpr int kMinChunksPerSplit = 2;   // 32 KiB of weights per CTA at least
+constexpr int kCtasPerSm = 2;           // K splits may fill the SMs twice over
 constexpr int kMaxSplits = 8;           // portable cluster size
 constexpr int kWBytes = kTileN * 128;   // 16 KiB W box per stage
 // Stage ring of about 112 KiB, so that two CTAs fit on an SM: a wide product's whole
@@ -338,23 +340,36 @@ int env_int(const char* name, int dflt, int lo, int hi) {
   return v < lo ? lo : (v > hi ? hi : v);
 }
 
+size_t smem_bytes(int stages, int Mp) {
+  return 1024 + static_cast<size_t>(stages) * (kWBytes + Mp * 128) + 256;
+}
+
+int stages_for(int Mp) {
+  const int st = kLinearSmemBudget / (kWBytes + Mp * 128);
+  return st < kMinStages ? kMinStages : (st > kMaxStages ? kMaxStages : st);
+}
+
+// Splits per tile: as many as fill the SMs `cps` times over (two CTAs fit on an SM),
+// at most kMaxSplits and at least kMinChunksPerSplit chunks each. When the grid takes
+// more than one CTA per SM the cluster size is rounded down to a power of two, so that
+// the clusters pack into the GPCs' CTA slots in one wave (measured on the 8B q|k|v
+// product at one row: 48 clusters of 6, 288 CTAs, 15.7 us; of 3, 144 CTAs, 12.3 us).
 Plan plan_for(int M, int N, int K) {
   Plan pl{};
   pl.Mp = (M + 15) / 16 * 16;
   pl.n_tiles = (N + kTileN - 1) / kTileN;
   pl.kc = K / kChunk;
-  const int sms = sm_count() * env_int("NSLG_LINEAR_CTAS_PER_SM", 1, 1, 2);
-  int s = sms / pl.n_tiles;                    // tiles x splits <= #SMs
+  const int cps = env_int("NSLG_LINEAR_CTAS_PER_SM", kCtasPerSm, 1, 2);
+  int s = sm_count() * cps / pl.n_tiles;
   int s_max = pl.kc / env_int("NSLG_LINEAR_MIN_CHUNKS", kMinChunksPerSplit, 1, 64);
   if (s_max > kMaxSplits) s_max = kMaxSplits;
   if (s > s_max) s = s_max;
   if (s < 1) s = 1;
+  if (pl.n_tiles * s > sm_count())
+    while (s & (s - 1)) --s;                   // a power of two
   pl.splits = s;
   pl.grid = pl.n_tiles * s;
-  const int sbytes = kWBytes + pl.Mp * 128;
-  int st = kLinearSmemBudget / sbytes;
-  if (st < kMinStages) st = kMinStages;
-  pl.stages = st > kMaxStages ? kMaxStages : st;
+  pl.stages = stages_for(pl.Mp);
   int cols = 32;
   while (cols < pl.Mp) cols *= 2;
   pl.tmem_cols = cols;
@@ -393,7 +408,7 @@ int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_st
   p.do_push = push != nullptr ? 1 : 0;
   if (push != nullptr) p.push = *push;
   p.status = status;
-  const size_t smem = 1024 + static_cast<size_t>(pl.stages) * (kWBytes + pl.Mp * 128) + 256;
+  const size_t smem = smem_bytes(pl.stages, pl.Mp);
   auto kern = dtype == NSLG_DTYPE_F16 ? linear_tc_kernel<__half> : linear_tc_kernel<__nv_bfloat16>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
