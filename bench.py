@@ -441,7 +441,8 @@ def run_linear_shapes(device, shapes=None, reps=20, copies=8, policies=None):
     DRAM; the TP=8 ones still fit in L2 together), ``reps`` calls per CUDA graph, five
     replays, CUDA events; frac = weight bytes / time / measured HBM bandwidth.
     ``policies``: (CTAs per SM, fewest K chunks per split) pairs of the kernel's split
-    rule to time as well (through its NSLG_LINEAR_* overrides)."""
+    rule, or ("splits", s) for a fixed split count, to time as well (through its
+    NSLG_LINEAR_* overrides)."""
     import torch.nn.functional as F
     from nanoslg_b200 import ops
     peak, _ = _hbm_peak()
@@ -482,15 +483,16 @@ def run_linear_shapes(device, shapes=None, reps=20, copies=8, policies=None):
         gb = n * k * 2 / 1e9
         out[name] = {"shape": [m, n, k], "ours_us": t_o, "cublas_us": t_c,
                      "ours_frac": gb / (t_o * 1e-6) / peak, "cublas_frac": gb / (t_c * 1e-6) / peak}
-        for cps, minc in policies or ():
-            os.environ["NSLG_LINEAR_CTAS_PER_SM"] = str(cps)
-            os.environ["NSLG_LINEAR_MIN_CHUNKS"] = str(minc)
+        for pol in policies or ():
+            env = ({"NSLG_LINEAR_SPLITS": str(pol[1])} if pol[0] == "splits" else
+                   {"NSLG_LINEAR_CTAS_PER_SM": str(pol[0]), "NSLG_LINEAR_MIN_CHUNKS": str(pol[1])})
+            key = (f"splits{pol[1]}" if pol[0] == "splits" else f"cps{pol[0]}_min{pol[1]}")
+            os.environ.update(env)
             try:
-                out[name].setdefault("ours_us_by_policy", {})[f"cps{cps}_min{minc}"] = \
-                    timeit(ours)
+                out[name].setdefault("ours_us_by_policy", {})[key] = timeit(ours)
             finally:
-                os.environ.pop("NSLG_LINEAR_CTAS_PER_SM", None)
-                os.environ.pop("NSLG_LINEAR_MIN_CHUNKS", None)
+                for e in env:
+                    os.environ.pop(e, None)
         del ws
         torch.cuda.empty_cache()
     ops.check_device_status(device)
@@ -1339,7 +1341,8 @@ def main():
         if a.linear_shape:
             m, n, k = (int(v) for v in a.linear_shape.split(","))
             shapes = [(f"rows{m}_out{n}_in{k}", m, n, k)]
-        policies = [(1, 8), (2, 8), (1, 2), (2, 2), (2, 4)] if a.linear_sweep else None
+        policies = ([(1, 8), (2, 8), (1, 2)] + [("splits", n) for n in (1, 2, 3, 4, 6, 8)]
+                    if a.linear_sweep else None)
         if rank == 0:
             print(json.dumps({"case": "linear only", "linear_shapes":
                               run_linear_shapes(device, shapes, policies=policies)}),

@@ -331,8 +331,9 @@ struct Plan {
 };
 
 // Split policy overrides, for measurements: NSLG_LINEAR_CTAS_PER_SM (1 or 2: the grid
-// may fill the SMs once or twice over with K splits) and NSLG_LINEAR_MIN_CHUNKS (the
-// fewest 64-element K chunks a split may have, 1 to 64).
+// may fill the SMs once or twice over with K splits), NSLG_LINEAR_MIN_CHUNKS (the
+// fewest 64-element K chunks a split may have, 1 to 64) and NSLG_LINEAR_SPLITS (1 to 8
+// splits per tile, at most one per chunk, instead of the rule).
 int env_int(const char* name, int dflt, int lo, int hi) {
   const char* e = std::getenv(name);
   if (e == nullptr || e[0] == '\0') return dflt;
@@ -367,6 +368,8 @@ Plan plan_for(int M, int N, int K) {
   if (s < 1) s = 1;
   if (pl.n_tiles * s > sm_count())
     while (s & (s - 1)) --s;                   // a power of two
+  const int forced = env_int("NSLG_LINEAR_SPLITS", 0, 0, kMaxSplits);
+  if (forced > 0) s = forced <= pl.kc ? forced : pl.kc;
   pl.splits = s;
   pl.grid = pl.n_tiles * s;
   pl.stages = stages_for(pl.Mp);
