@@ -1087,7 +1087,7 @@ def _allreduce_parity(device, world, rank, hidden=4096):
     from nanoslg_b200.tp_comm import PeerAllReduce
     bf = torch.bfloat16
     peer = PeerAllReduce(torch.distributed.group.WORLD, rank, world, device, 64, hidden, bf)
-    modes = {"one_shot": None, "two_shot": "1"} if world > 2 else {"one_shot": None}
+    modes = {"one_shot": "0", "two_shot": "1"} if world > 2 else {"one_shot": "0"}
     res_ok = {}
     for name, env in modes.items():
         if env is None:

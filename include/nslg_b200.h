@@ -342,6 +342,22 @@ int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int world, int ra
                               void* out, int64_t out_stride, float eps, int64_t timeout_ns,
                               uint32_t* dev_status, void* stream);
 
+/* nslg_tp_allreduce_rmsnorm for every rank of a TP group at once, all on the current
+ * GPU: rank r's partial, counters, residual and out are entry r of the HOST arrays
+ * partials / counters / residuals / outs, and stage_bufs[r] its stage buffer. One
+ * cooperative launch holds the ranks' blocks side by side, so the ranks wait on one
+ * another inside one grid (it fails with NSLG_ERR_CUDA if they cannot all be resident,
+ * instead of waiting). Same protocol, same one-shot / two-shot choice, same results as
+ * `world` processes each calling nslg_tp_allreduce_rmsnorm; for checking the exchange on
+ * a machine with one GPU. No counterpart in the reference. */
+int nslg_tp_allreduce_rmsnorm_emulated(int dtype, int rows, int hidden, int world,
+                                       const void* const* partials, int64_t partial_stride,
+                                       void* const* stage_bufs, int64_t stage_bytes,
+                                       void* const* counters, void* const* residuals,
+                                       int64_t residual_stride, const void* weight,
+                                       void* const* outs, int64_t out_stride, float eps,
+                                       int64_t timeout_ns, uint32_t* dev_status, void* stream);
+
 /* The RowParallel product and its collective in one kernel: nslg_linear (y = x . W^T,
  * `rows` <= 256 rows, y the caller's [rows, out_features] with 16-byte aligned rows) that
  * also stores y's rows, packed with the reduction's call numbers, into every peer's stage

@@ -64,6 +64,9 @@ SIGNATURES = {
     "nslg_tp_reduce_pushed_rmsnorm": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64,
                                              _vp, _vp, _i64, _vp, _vp, _i64, _f32, _i64, _vp,
                                              _vp]),
+    "nslg_tp_allreduce_rmsnorm_emulated": (_i32, [_i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64,
+                                                  _vp, _vp, _i64, _vp, _vp, _i64, _f32, _i64,
+                                                  _vp, _vp]),
     "nslg_linear_tp_push": (_i32, [_i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _i32,
                                    _i32, _vp, _i64, _vp, _vp, _vp]),
 }

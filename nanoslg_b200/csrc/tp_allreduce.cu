@@ -36,7 +36,10 @@
 // and RMSNorm as before. Results are identical to the one-shot mode's; each rank sends
 // 2 (world - 1) / world of a row instead of world - 1 rows, for a second NVLink round
 // trip. Both phases use the same in-band call numbers, so the mode may change from call
-// to call.
+// to call. The mode is chosen per call by size (kTwoShotSavingBytes) unless
+// NSLG_TP_TWO_SHOT forces one; both were checked bit for bit with every rank of a group
+// of 2, 4 and 8 emulated in one cooperative grid on one GPU (nslg_tp_allreduce_rmsnorm_
+// emulated, which runs this same kernel).
 //
 // Stage buffer of each rank: [2 slots][world sources][rows][2 x row bytes] (the packed
 // rows are twice the activations); in two-shot mode a slot holds [2 phases][world
@@ -58,16 +61,19 @@ namespace {
 constexpr int kGrid = kTpReduceGrid;   // blocks per call, the same on every rank and call
 constexpr int kThreads = 256;
 constexpr int kVecPerThread = 4;    // 16-byte vectors of a row per thread (hidden <= 8192 bf16)
-// one-shot push volume per rank ((world - 1) x rows x row bytes) from which two-shot is used
-constexpr int64_t kTwoShotBytes = 512 << 10;
+// Two-shot sends 2 (world - 2) / world x the one-shot's bytes fewer out of each GPU but
+// adds one NVLink round trip (about 2 us, i.e. about 1.5 MB at the measured 770 GB/s per
+// direction): it is chosen when the packed bytes it saves exceed that.
+constexpr int64_t kTwoShotSavingBytes = 3 << 19;   // 1.5 MiB
 
-// NSLG_TP_TWO_SHOT, read at every call: "auto" -> -1 (choose by size), "1" -> two-shot
-// (where the shape allows it), unset or anything else -> 0 (one-shot)
+// NSLG_TP_TWO_SHOT, read at every call: "0" -> one-shot, "1" -> two-shot (where the shape
+// allows it), unset or anything else ("auto") -> -1, chosen by size
 int two_shot_override() {
   const char* e = getenv("NSLG_TP_TWO_SHOT");
-  if (e == nullptr || e[0] == '\0') return 0;
-  if (strcmp(e, "auto") == 0) return -1;
-  return e[0] == '1' ? 1 : 0;
+  if (e == nullptr || e[0] == '\0') return -1;
+  if (strcmp(e, "0") == 0) return 0;
+  if (strcmp(e, "1") == 0) return 1;
+  return -1;
 }
 static_assert(kGrid * 4 <= NSLG_TP_COUNTER_BYTES, "counter buffer too small");
 
@@ -87,6 +93,14 @@ struct ArParams {
   float eps;
   uint64_t timeout_ns;
   uint32_t* status;
+  // Every rank of the group in one cooperative grid on one GPU (nslg_tp_allreduce_
+  // rmsnorm_emulated): blocks [r * e_grid, (r + 1) * e_grid) are rank r, with its own
+  // partial, residual, output and counters; the scalar fields above are then unused.
+  int emulate, e_grid;
+  const void* e_partial[NSLG_TP_MAX_WORLD];
+  void* e_residual[NSLG_TP_MAX_WORLD];
+  void* e_out[NSLG_TP_MAX_WORLD];
+  uint32_t* e_counters[NSLG_TP_MAX_WORLD];
 };
 
 __device__ __forceinline__ void st_relaxed_v4(void* p, uint4 v) {
@@ -116,7 +130,14 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
   constexpr int VEC = 16 / sizeof(T);
   const int nv = p.hidden / VEC;                  // 16-byte vectors per row
   const int64_t units_per_row = 2 * static_cast<int64_t>(nv);
-  uint32_t* counter = p.counters + blockIdx.x;
+  // this block's rank, its index among the rank's blocks, and the rank's buffers
+  const int nblk = p.emulate ? p.e_grid : static_cast<int>(gridDim.x);
+  const int rank = p.emulate ? static_cast<int>(blockIdx.x) / nblk : p.rank;
+  const int bid = p.emulate ? static_cast<int>(blockIdx.x) % nblk : static_cast<int>(blockIdx.x);
+  const void* partial = p.emulate ? p.e_partial[rank] : p.partial;
+  void* residual = p.emulate ? p.e_residual[rank] : p.residual;
+  void* out_rows = p.emulate ? p.e_out[rank] : p.out;
+  uint32_t* counter = (p.emulate ? p.e_counters[rank] : p.counters) + bid;
   const uint32_t call = *reinterpret_cast<volatile uint32_t*>(counter) + 1;
   const int64_t slot_off = (call & 1u) * p.slot_bytes;
   __shared__ volatile int bad;      // a wait of this block gave up: the others stop too
@@ -154,21 +175,21 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
 
   // 1. push this rank's partial rows, packed with the call number: one-shot, the whole
   //    row to every peer; two-shot, column slice j of the row to rank j only
-  for (int row = p.pushed ? p.rows : blockIdx.x; row < p.rows; row += gridDim.x) {
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.partial) +
+  for (int row = p.pushed ? p.rows : bid; row < p.rows; row += nblk) {
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(partial) +
                                                       row * p.p_stride);
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
       const uint4 v = src[i];
       if (p.two_shot) {
         const int j = i / nvs;
-        if (j == p.rank) continue;
-        push(reinterpret_cast<uint4*>(p.stage[j] + slot_off) + p.rank * units_src +
+        if (j == rank) continue;
+        push(reinterpret_cast<uint4*>(p.stage[j] + slot_off) + rank * units_src +
                  row * 2 * nvs + 2 * (i - j * nvs), v);
         continue;
       }
       for (int d = 0; d < p.world; ++d) {
-        if (d == p.rank) continue;
-        push(reinterpret_cast<uint4*>(p.stage[d] + slot_off + p.rank * p.region_bytes) +
+        if (d == rank) continue;
+        push(reinterpret_cast<uint4*>(p.stage[d] + slot_off + rank * p.region_bytes) +
                  row * units_per_row + 2 * i, v);
       }
     }
@@ -177,10 +198,10 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
 
   // 2. per row: wait for and sum every rank's words, then residual add and RMSNorm
   const T* w = static_cast<const T*>(p.weight);
-  for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
-    const uint4* mine = reinterpret_cast<const uint4*>(static_cast<const T*>(p.partial) +
+  for (int row = bid; row < p.rows; row += nblk) {
+    const uint4* mine = reinterpret_cast<const uint4*>(static_cast<const T*>(partial) +
                                                        row * p.p_stride);
-    const uint4* own = reinterpret_cast<const uint4*>(p.stage[p.rank] + slot_off);
+    const uint4* own = reinterpret_cast<const uint4*>(p.stage[rank] + slot_off);
     float acc[kVecPerThread][VEC];
     if (p.two_shot) {
       // 2a. reduce this rank's column slice over the ranks (fp32, rank order, one
@@ -191,7 +212,7 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
         for (int j = 0; j < VEC; ++j) a[j] = 0.f;
         for (int s = 0; s < p.world; ++s) {
           NVec<T, VEC> v;
-          if (s == p.rank) v.u = mine[p.rank * nvs + u];
+          if (s == rank) v.u = mine[rank * nvs + u];
           else fetch(own + s * units_src + row * 2 * nvs + 2 * u, v.u);
 #pragma unroll
           for (int j = 0; j < VEC; ++j) a[j] = __fadd_rn(a[j], Elem<T>::to_f(v.e[j]));
@@ -201,7 +222,7 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
 #pragma unroll
         for (int j = 0; j < VEC; ++j) r.e[j] = Elem<T>::from_f(a[j]);
         for (int d = 0; d < p.world; ++d)
-          push(reinterpret_cast<uint4*>(p.stage[d] + slot_off) + (p.world + p.rank) * units_src +
+          push(reinterpret_cast<uint4*>(p.stage[d] + slot_off) + (p.world + rank) * units_src +
                    row * 2 * nvs + 2 * u, r.u);
       }
       // 2b. gather the reduced slices of every rank
@@ -226,10 +247,10 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
         if (i >= nv) continue;
         for (int s = 0; s < p.world; ++s) {
           NVec<T, VEC> v;
-          if (s == p.rank) {
+          if (s == rank) {
             v.u = mine[i];
           } else {
-            const uint4* q = reinterpret_cast<const uint4*>(p.stage[p.rank] + slot_off +
+            const uint4* q = reinterpret_cast<const uint4*>(p.stage[rank] + slot_off +
                                                             s * p.region_bytes) +
                              row * units_per_row + 2 * i;
             fetch(q, v.u);
@@ -241,7 +262,7 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
     }
     __syncthreads();
     if (bad) break;     // block-uniform: a peer never delivered; nothing is written
-    T* res = static_cast<T*>(p.residual) + row * p.r_stride;
+    T* res = static_cast<T*>(residual) + row * p.r_stride;
     float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < kVecPerThread; ++k) {
@@ -273,7 +294,7 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
     }
     __syncthreads();
     const float inv = rsqrtf(__fadd_rn(__fdiv_rn(red[0], static_cast<float>(p.hidden)), p.eps));
-    T* out = static_cast<T*>(p.out) + row * p.o_stride;
+    T* out = static_cast<T*>(out_rows) + row * p.o_stride;
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
       NVec<T, VEC> a, ww, o;
       a.u = reinterpret_cast<const uint4*>(res)[i];
@@ -335,11 +356,50 @@ extern "C" int nslg_ipc_free(void* dev_ptr) {
 }
 
 namespace {
+// Per-rank buffers of a group emulated on one GPU (nslg_tp_allreduce_rmsnorm_emulated).
+struct EmulatedRanks {
+  const void* const* partials;
+  void* const* counters;
+  void* const* residuals;
+  void* const* outs;
+};
+
+template <typename T>
+int launch_emulated(ArParams p, int world, cudaStream_t st) {
+  // every block of every rank must be resident at once (they wait on one another): the
+  // cooperative launch fails, rather than hangs, when they cannot be
+  auto kern = tp_allreduce_rmsnorm_kernel<T>;
+  int per_sm = 0;
+  cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0);
+  if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
+  int g = per_sm * sm_count() / world;
+  if (g > kGrid) g = kGrid;
+  if (g < 1) return set_error(NSLG_ERR_UNSUPPORTED, "tp_allreduce_rmsnorm_emulated: no room");
+  p.emulate = 1;
+  p.e_grid = g;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g * world);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, kern, p);
+  if (err != cudaSuccess)
+    return set_error(NSLG_ERR_CUDA, std::string("tp_allreduce_rmsnorm_emulated: ") +
+                                        cudaGetErrorString(err));
+  return check_launch("tp_allreduce_rmsnorm_emulated");
+}
+
 int tp_reduce(int dtype, int rows, int hidden, int world, int rank, const void* partial,
               int64_t partial_stride, void* const* stage_bufs, int64_t stage_bytes,
               void* counters, void* residual, int64_t residual_stride, const void* weight,
               void* out, int64_t out_stride, float eps, int64_t timeout_ns,
-              uint32_t* dev_status, void* stream, int pushed) {
+              uint32_t* dev_status, void* stream, int pushed,
+              const EmulatedRanks* emu = nullptr) {
   if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16 && dtype != NSLG_DTYPE_F32)
     return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad dtype");
   if (world < 2 || world > NSLG_TP_MAX_WORLD || rank < 0 || rank >= world)
@@ -370,6 +430,15 @@ int tp_reduce(int dtype, int rows, int hidden, int world, int rank, const void* 
     if (!stage_bufs[i] || !a16(stage_bufs[i]))
       return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm: bad stage buffer");
     p.stage[i] = static_cast<uint8_t*>(stage_bufs[i]);
+    if (emu == nullptr) continue;
+    if (!emu->partials[i] || !emu->counters[i] || !emu->residuals[i] ||
+        (weight && !emu->outs[i]) || !a16(emu->partials[i]) || !a16(emu->counters[i]) ||
+        !a16(emu->residuals[i]) || (weight && !a16(emu->outs[i])))
+      return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm_emulated: bad rank buffer");
+    p.e_partial[i] = emu->partials[i];
+    p.e_counters[i] = static_cast<uint32_t*>(emu->counters[i]);
+    p.e_residual[i] = emu->residuals[i];
+    p.e_out[i] = weight ? emu->outs[i] : nullptr;
   }
   p.partial = partial;
   p.p_stride = partial_stride;
@@ -390,17 +459,24 @@ int tp_reduce(int dtype, int rows, int hidden, int world, int rank, const void* 
   // when the one-shot's (world - 1) full-row pushes per rank are large: it moves
   // 2 (world - 1) / world of a row per rank instead of (world - 1) rows, at the price of a
   // second NVLink round trip. Same fp32 rank-order sums, so both give identical results.
-  // The mode follows NSLG_TP_TWO_SHOT: one-shot unless it says "1" or "auto" (by size).
+  // By size unless NSLG_TP_TWO_SHOT forces a mode: the packed one-shot push is
+  // 2 (world - 1) rows x row bytes out of each GPU, two-shot's 4 (world - 1) / world of
+  // that; e.g. 8B decode rows (8 KiB): one-shot up to 63 rows at TP=4, 18 at TP=8.
   const int vec = 16 / esz;
   const bool two_ok = world > 2 && hidden % (world * vec) == 0;
   const int force = two_shot_override();
-  p.two_shot = !pushed && two_ok &&
-               (force >= 0 ? force == 1
-                           : static_cast<int64_t>(rows) * row_bytes * (world - 1) >= kTwoShotBytes);
+  const int64_t saved = 2 * static_cast<int64_t>(rows) * row_bytes * (world - 1) * (world - 2) /
+                        world;
+  p.two_shot = !pushed && two_ok && (force >= 0 ? force == 1 : saved >= kTwoShotSavingBytes);
   p.pushed = pushed;
   p.timeout_ns = static_cast<uint64_t>(timeout_ns);
   p.status = dev_status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (emu != nullptr) {
+    if (dtype == NSLG_DTYPE_BF16) return launch_emulated<__nv_bfloat16>(p, world, st);
+    if (dtype == NSLG_DTYPE_F16) return launch_emulated<__half>(p, world, st);
+    return launch_emulated<float>(p, world, st);
+  }
   if (dtype == NSLG_DTYPE_BF16)
     return launch_pdl("tp_allreduce_rmsnorm", tp_allreduce_rmsnorm_kernel<__nv_bfloat16>,
                       dim3(kGrid), dim3(kThreads), 0, st, p);
@@ -422,6 +498,23 @@ extern "C" int nslg_tp_allreduce_rmsnorm(int dtype, int rows, int hidden, int wo
   return tp_reduce(dtype, rows, hidden, world, rank, partial, partial_stride, stage_bufs,
                    stage_bytes, counters, residual, residual_stride, weight, out, out_stride,
                    eps, timeout_ns, dev_status, stream, 0);
+}
+
+extern "C" int nslg_tp_allreduce_rmsnorm_emulated(
+    int dtype, int rows, int hidden, int world, const void* const* partials,
+    int64_t partial_stride, void* const* stage_bufs, int64_t stage_bytes, void* const* counters,
+    void* const* residuals, int64_t residual_stride, const void* weight, void* const* outs,
+    int64_t out_stride, float eps, int64_t timeout_ns, uint32_t* dev_status, void* stream) {
+  clear_error();
+  if (!partials || !counters || !residuals || (weight && !outs))
+    return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm_emulated: null pointer array");
+  if (world < 2 || world > NSLG_TP_MAX_WORLD)
+    return set_error(NSLG_ERR_ARG, "tp_allreduce_rmsnorm_emulated: need 2 <= world <= 8");
+  const EmulatedRanks emu{partials, counters, residuals, outs};
+  return tp_reduce(dtype, rows, hidden, world, 0, partials[0], partial_stride, stage_bufs,
+                   stage_bytes, counters[0], residuals[0], residual_stride, weight,
+                   weight ? outs[0] : nullptr, out_stride, eps, timeout_ns, dev_status, stream,
+                   0, &emu);
 }
 
 extern "C" int nslg_tp_reduce_pushed_rmsnorm(int dtype, int rows, int hidden, int world,

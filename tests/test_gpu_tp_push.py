@@ -118,3 +118,51 @@ def test_fused_push_rejects_what_it_does_not_cover():
     assert call(2, 2, None, 1 << 16) == N.ERR_ARG                   # rank out of range
     assert call(2, 0, None, 1024) == N.ERR_WORKSPACE                # rows do not fit
     assert b"fit" in lib.nslg_last_error()
+
+
+def _emulated_call(world, rows, hidden, parts, stages, stage_bytes, counters, resid, nw, outs,
+                   timeout_ns=2_000_000_000):
+    lib = N.lib()
+    P = ctypes.c_void_p * world
+    rc = lib.nslg_tp_allreduce_rmsnorm_emulated(
+        N.DTYPE_BF16, rows, hidden, world,
+        ctypes.cast(P(*[t.data_ptr() for t in parts]), ctypes.c_void_p), hidden,
+        ctypes.cast(P(*[s.data_ptr() for s in stages]), ctypes.c_void_p), stage_bytes,
+        ctypes.cast(P(*[c.data_ptr() for c in counters]), ctypes.c_void_p),
+        ctypes.cast(P(*[r.data_ptr() for r in resid]), ctypes.c_void_p), hidden,
+        nw.data_ptr(), ctypes.cast(P(*[o.data_ptr() for o in outs]), ctypes.c_void_p), hidden,
+        EPS, timeout_ns, ops.status_word(DEV).data_ptr(),
+        torch.cuda.current_stream(DEV).cuda_stream)
+    assert rc == N.OK, lib.nslg_last_error()
+
+
+@pytest.mark.parametrize("world,mode", [(2, "0"), (4, "0"), (4, "1"), (8, "0"), (8, "1"),
+                                        (8, "auto")])
+def test_reduction_protocol_emulated_group_one_gpu(world, mode, monkeypatch):
+    """The reduction kernel with every rank of a TP group in one cooperative grid on one
+    GPU (nslg_tp_allreduce_rmsnorm_emulated): the one-shot push and the two-shot
+    reduce-scatter + all-gather, on consecutive calls that alternate the stage slots and
+    change the row count. The new residual must be bit-exact against the fp32 rank-order
+    sum on every rank, the norm output within one rounding."""
+    monkeypatch.setenv("NSLG_TP_TWO_SHOT", mode)
+    hidden, bf = 4096, torch.bfloat16
+    rows_seq = [64, 1, 17, 64, 5]
+    stage_bytes = 4 * world * max(rows_seq) * hidden * 2
+    stages = [torch.zeros(stage_bytes, dtype=torch.uint8, device=DEV) for _ in range(world)]
+    counters = [torch.zeros(N.TP_COUNTER_BYTES // 4, dtype=torch.int32, device=DEV)
+                for _ in range(world)]
+    g = torch.Generator(device=DEV).manual_seed(world * 10 + len(mode))
+    for call, rows in enumerate(rows_seq):
+        parts = [torch.randn(rows, hidden, generator=g, device=DEV).to(bf) for _ in range(world)]
+        res0 = torch.randn(rows, hidden, generator=g, device=DEV).to(bf)
+        nw = (1 + 0.1 * torch.randn(hidden, generator=g, device=DEV)).to(bf)
+        resid = [res0.clone() for _ in range(world)]
+        outs = [torch.empty(rows, hidden, dtype=bf, device=DEV) for _ in range(world)]
+        _emulated_call(world, rows, hidden, parts, stages, stage_bytes, counters, resid, nw,
+                       outs)
+        torch.cuda.synchronize(DEV)
+        assert int(ops.status_word(DEV).item()) == 0, f"status at call {call}"
+        h_want, o_want = _expected(parts, res0, nw)
+        for r in range(world):
+            assert torch.equal(resid[r], h_want), f"rank {r} residual, call {call}"
+            assert _close(outs[r], o_want), f"rank {r} norm output, call {call}"
