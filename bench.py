@@ -1036,7 +1036,11 @@ def run_parity(device, world, rank):
     * ``tp_x_pp2`` (world >= 2): TP=world/2 x PP=2 (PP=2 alone at world 2), lock-step
       stages and the 2-micro-batch pipeline schedule;
     * ``allreduce``: nslg_tp_allreduce_rmsnorm's new residual bit-equal to an fp32
-      rank-order sum of the ranks' bf16 partials + residual (hidden 4096; 1 and 64 rows).
+      rank-order sum of the ranks' bf16 partials + residual (hidden 4096; 1 and 64 rows);
+    * ``tp_exchange_one_gpu`` (rank 0, every world size): the same check with all ranks of
+      a TP=8 group on this GPU -- the reduction's one-shot, two-shot and size-chosen
+      modes in one cooperative grid, and the RowParallel GEMM's own push followed by the
+      push-less reduction.
 
     Every rank takes part; ``ok`` is true only if every check held on every rank."""
     from types import SimpleNamespace
@@ -1075,11 +1079,98 @@ def run_parity(device, world, rank):
     torch.backends.cuda.matmul.allow_tf32 = prev_tf32
     if world > 1:
         checks["allreduce"] = _allreduce_parity(device, world, rank)
+    if rank == 0:
+        checks["tp_exchange_one_gpu"] = _emulated_exchange_parity(device)
     flags = torch.tensor([int(all(c["ok"] for c in checks.values()))], device=device)
     if world > 1:
         torch.distributed.all_reduce(flags, op=torch.distributed.ReduceOp.MIN)
     return {"ok": bool(flags.item()), "fixture": "tests/golden/tiny_llama_kv8.json "
             "(reference contiguous SDPA, fp32, batch 2, 16 greedy tokens)", "checks": checks}
+
+
+def _emulated_exchange_parity(device, world=8, hidden=4096):
+    """All ranks of a TP group emulated on this GPU (see run_parity): residual bit-equal
+    to bf16(bf16(fp32 rank-order sum of the partials) + residual) on every rank."""
+    import ctypes
+    from nanoslg_b200 import _native as N
+    from nanoslg_b200 import ops
+    lib = N.lib()
+    bf = torch.bfloat16
+    stream = torch.cuda.current_stream(device).cuda_stream
+    status = ops.status_word(device)
+    P = ctypes.c_void_p * world
+    arr = lambda ts: ctypes.cast(P(*[t.data_ptr() for t in ts]), ctypes.c_void_p)
+    stage_bytes = 4 * world * 64 * hidden * 2
+    g = torch.Generator(device=device).manual_seed(123)
+
+    def want(parts, res):
+        s = parts[0].float()
+        for p in parts[1:]:
+            s = s + p.float()
+        return (res.float() + s.to(bf).float()).to(bf)
+
+    out = {}
+    for name, mode in (("one_shot", "0"), ("two_shot", "1"), ("by_size", None)):
+        old = os.environ.pop("NSLG_TP_TWO_SHOT", None)
+        if mode is not None:
+            os.environ["NSLG_TP_TWO_SHOT"] = mode
+        try:
+            stages = [torch.zeros(stage_bytes, dtype=torch.uint8, device=device)
+                      for _ in range(world)]
+            cnt = [torch.zeros(N.TP_COUNTER_BYTES // 4, dtype=torch.int32, device=device)
+                   for _ in range(world)]
+            ok = True
+            for rows in (64, 1, 17):
+                parts = [torch.randn(rows, hidden, generator=g, device=device).to(bf)
+                         for _ in range(world)]
+                res = torch.randn(rows, hidden, generator=g, device=device).to(bf)
+                resid = [res.clone() for _ in range(world)]
+                rc = lib.nslg_tp_allreduce_rmsnorm_emulated(
+                    N.DTYPE_BF16, rows, hidden, world, arr(parts), hidden, arr(stages),
+                    stage_bytes, arr(cnt), arr(resid), hidden, None, None, 0, 1e-5,
+                    2_000_000_000, status.data_ptr(), stream)
+                torch.cuda.synchronize(device)
+                h = want(parts, res)
+                ok = ok and rc == 0 and all(torch.equal(r, h) for r in resid)
+            out[name] = bool(ok)
+        finally:
+            os.environ.pop("NSLG_TP_TWO_SHOT", None)
+            if old is not None:
+                os.environ["NSLG_TP_TWO_SHOT"] = old
+    # the RowParallel GEMM pushing its own rows, then the reductions without a push
+    stages = [torch.zeros(stage_bytes, dtype=torch.uint8, device=device) for _ in range(world)]
+    cnt = [torch.zeros(N.TP_COUNTER_BYTES // 4, dtype=torch.int32, device=device)
+           for _ in range(world)]
+    k = hidden // world
+    ok = True
+    for rows in (1, 16):
+        xs = [torch.randn(rows, k, generator=g, device=device).to(bf) for _ in range(world)]
+        ws = [(torch.randn(hidden, k, generator=g, device=device) / k ** 0.5).to(bf)
+              for _ in range(world)]
+        parts = [torch.empty(rows, hidden, dtype=bf, device=device) for _ in range(world)]
+        res = torch.randn(rows, hidden, generator=g, device=device).to(bf)
+        resid = [res.clone() for _ in range(world)]
+        for r in range(world):
+            ok = ok and lib.nslg_linear_tp_push(
+                N.DTYPE_BF16, rows, hidden, k, xs[r].data_ptr(), k, ws[r].data_ptr(), k,
+                parts[r].data_ptr(), hidden, world, r, arr(stages), stage_bytes,
+                cnt[r].data_ptr(), status.data_ptr(), stream) == 0
+        for r in range(world):
+            ok = ok and lib.nslg_tp_reduce_pushed_rmsnorm(
+                N.DTYPE_BF16, rows, hidden, world, r, parts[r].data_ptr(), hidden,
+                arr(stages), stage_bytes, cnt[r].data_ptr(), resid[r].data_ptr(), hidden,
+                None, None, 0, 1e-5, 2_000_000_000, status.data_ptr(), stream) == 0
+        torch.cuda.synchronize(device)
+        h = want(parts, res)
+        ok = ok and all(torch.equal(r, h) for r in resid)
+    out["gemm_push"] = bool(ok)
+    try:
+        ops.check_device_status(device)
+    except RuntimeError:
+        out = {n: False for n in out}
+    return {"world": world, "ok": all(out.values()), "modes": out,
+            "check": "every emulated rank's new residual bit-equal to bf16(bf16(fp32 "
+                     "rank-order sum) + residual)"}
 
 
 def _allreduce_parity(device, world, rank, hidden=4096):
