@@ -62,9 +62,12 @@ constexpr int kGrid = kTpReduceGrid;   // blocks per call, the same on every ran
 constexpr int kThreads = 256;
 constexpr int kVecPerThread = 4;    // 16-byte vectors of a row per thread (hidden <= 8192 bf16)
 // Two-shot sends 2 (world - 2) / world x the one-shot's bytes fewer out of each GPU but
-// adds one NVLink round trip (about 2 us, i.e. about 1.5 MB at the measured 770 GB/s per
-// direction): it is chosen when the packed bytes it saves exceed that.
-constexpr int64_t kTwoShotSavingBytes = 3 << 19;   // 1.5 MiB
+// adds a second NVLink round trip: it is chosen when the packed bytes it saves exceed
+// kTwoShotSavingBytes. Measured at TP=4 on B200 (8 KiB rows, CUDA-graph loops, max over
+// ranks): one-shot 7.5 / 14.1 / 40.3 us, two-shot 7.9 / 9.5 / 20.5 us at 1 / 64 / 256
+// rows, i.e. the second round trip costs about 0.4 us and two-shot wins from about 5
+// rows (~120 KB saved).
+constexpr int64_t kTwoShotSavingBytes = 128 << 10;
 
 // NSLG_TP_TWO_SHOT, read at every call: "0" -> one-shot, "1" -> two-shot (where the shape
 // allows it), unset or anything else ("auto") -> -1, chosen by size
@@ -461,7 +464,7 @@ int tp_reduce(int dtype, int rows, int hidden, int world, int rank, const void* 
   // second NVLink round trip. Same fp32 rank-order sums, so both give identical results.
   // By size unless NSLG_TP_TWO_SHOT forces a mode: the packed one-shot push is
   // 2 (world - 1) rows x row bytes out of each GPU, two-shot's 4 (world - 1) / world of
-  // that; e.g. 8B decode rows (8 KiB): one-shot up to 63 rows at TP=4, 18 at TP=8.
+  // that; e.g. 8B decode rows (8 KiB): one-shot up to 5 rows at TP=4, 1 at TP=8.
   const int vec = 16 / esz;
   const bool two_ok = world > 2 && hidden % (world * vec) == 0;
   const int force = two_shot_override();
