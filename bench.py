@@ -967,7 +967,7 @@ def _gemm_reduce_timing(device, world, rank, peer, hidden, calls, replays):
     bf = torch.bfloat16
     k = 4096 // world
     res = {}
-    for rows in (1, 16):
+    for rows in (1, 4):
         x = torch.randn(rows, k, device=device).to(bf)
         wt = (torch.randn(hidden, k, device=device) / k ** 0.5).to(bf)
         r = torch.randn(rows, hidden, device=device).to(bf)
@@ -1206,9 +1206,11 @@ def _allreduce_parity(device, world, rank, hidden=4096):
         res_ok[name] = bool(ok)
     os.environ.pop("NSLG_TP_TWO_SHOT", None)
     # the RowParallel GEMM pushing its own rows (nslg_linear_tp_push), then the reduction
+    # (decode batches of up to tp_comm.FUSED_PUSH_MAX_ROWS rows take this path)
+    from nanoslg_b200.tp_comm import FUSED_PUSH_MAX_ROWS
     ok = True
     k = 4096 // world
-    for it, rows in enumerate((1, 16, 5)):
+    for it, rows in enumerate(sorted({1, FUSED_PUSH_MAX_ROWS, max(1, FUSED_PUSH_MAX_ROWS - 1)})):
         g = torch.Generator().manual_seed(500 + 10 * it + rank)
         x = torch.randn(rows, k, generator=g).to(bf).to(device)
         wt = (torch.randn(hidden, k, generator=g) / k ** 0.5).to(bf).to(device)

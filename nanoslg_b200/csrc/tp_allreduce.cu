@@ -150,8 +150,10 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
   // Polls the packed 32-byte unit at q until both of its 16-byte halves carry this call
   // number (bounded); returns its 16 data bytes. On a timeout sets `bad` (the block's
   // other threads stop polling too) and records NSLG_DEV_WAIT_TIMEOUT.
-  auto fetch = [&](const uint4* q, uint4& out) {
-    uint4 a = ld_relaxed_v4(q), b = ld_relaxed_v4(q + 1);
+  // Second half of a fetch: (a, b) were loaded from q already (the caller issues the
+  // loads of a whole set of units first, so they cost one memory latency together rather
+  // than one each); polls q again only if they did not carry this call's number yet.
+  auto settle = [&](const uint4* q, uint4& a, uint4& b) {
     if (!(a.y == call && a.w == call && b.y == call && b.w == call)) {
       const uint64_t t0 = global_ns();
       while (true) {
@@ -166,7 +168,6 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
         }
       }
     }
-    out = make_uint4(a.x, a.z, b.x, b.z);
   };
   auto push = [&](uint4* dst, const uint4 v) {
     st_relaxed_v4(dst, make_uint4(v.x, call, v.y, call));
@@ -213,10 +214,24 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
         float a[VEC];
 #pragma unroll
         for (int j = 0; j < VEC; ++j) a[j] = 0.f;
-        for (int s = 0; s < p.world; ++s) {
+        uint4 ua[NSLG_TP_MAX_WORLD], ub[NSLG_TP_MAX_WORLD];
+#pragma unroll
+        for (int s = 0; s < NSLG_TP_MAX_WORLD; ++s) {
+          if (s >= p.world || s == rank) continue;
+          const uint4* q = own + s * units_src + row * 2 * nvs + 2 * u;
+          ua[s] = ld_relaxed_v4(q);
+          ub[s] = ld_relaxed_v4(q + 1);
+        }
+#pragma unroll
+        for (int s = 0; s < NSLG_TP_MAX_WORLD; ++s) {
+          if (s >= p.world) continue;
           NVec<T, VEC> v;
-          if (s == rank) v.u = mine[rank * nvs + u];
-          else fetch(own + s * units_src + row * 2 * nvs + 2 * u, v.u);
+          if (s == rank) {
+            v.u = mine[rank * nvs + u];
+          } else {
+            settle(own + s * units_src + row * 2 * nvs + 2 * u, ua[s], ub[s]);
+            v.u = make_uint4(ua[s].x, ua[s].z, ub[s].x, ub[s].z);
+          }
 #pragma unroll
           for (int j = 0; j < VEC; ++j) a[j] = __fadd_rn(a[j], Elem<T>::to_f(v.e[j]));
         }
@@ -228,7 +243,17 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
           push(reinterpret_cast<uint4*>(p.stage[d] + slot_off) + (p.world + rank) * units_src +
                    row * 2 * nvs + 2 * u, r.u);
       }
-      // 2b. gather the reduced slices of every rank
+      // 2b. gather the reduced slices of every rank (all loads of the thread first)
+      uint4 ua[kVecPerThread], ub[kVecPerThread];
+#pragma unroll
+      for (int k = 0; k < kVecPerThread; ++k) {
+        const int i = threadIdx.x + k * kThreads;
+        if (i >= nv) continue;
+        const int s = i / nvs;
+        const uint4* q = own + (p.world + s) * units_src + row * 2 * nvs + 2 * (i - s * nvs);
+        ua[k] = ld_relaxed_v4(q);
+        ub[k] = ld_relaxed_v4(q + 1);
+      }
 #pragma unroll
       for (int k = 0; k < kVecPerThread; ++k) {
         const int i = threadIdx.x + k * kThreads;
@@ -236,8 +261,9 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
         for (int j = 0; j < VEC; ++j) acc[k][j] = 0.f;
         if (i >= nv) continue;
         const int s = i / nvs;
+        settle(own + (p.world + s) * units_src + row * 2 * nvs + 2 * (i - s * nvs), ua[k], ub[k]);
         NVec<T, VEC> v;
-        fetch(own + (p.world + s) * units_src + row * 2 * nvs + 2 * (i - s * nvs), v.u);
+        v.u = make_uint4(ua[k].x, ua[k].z, ub[k].x, ub[k].z);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) acc[k][j] = Elem<T>::to_f(v.e[j]);
       }
@@ -248,7 +274,21 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
 #pragma unroll
         for (int j = 0; j < VEC; ++j) acc[k][j] = 0.f;
         if (i >= nv) continue;
-        for (int s = 0; s < p.world; ++s) {
+        // every peer's unit of this vector loaded at once, then settled and summed in
+        // rank order
+        uint4 ua[NSLG_TP_MAX_WORLD], ub[NSLG_TP_MAX_WORLD];
+#pragma unroll
+        for (int s = 0; s < NSLG_TP_MAX_WORLD; ++s) {
+          if (s >= p.world || s == rank) continue;
+          const uint4* q = reinterpret_cast<const uint4*>(p.stage[rank] + slot_off +
+                                                          s * p.region_bytes) +
+                           row * units_per_row + 2 * i;
+          ua[s] = ld_relaxed_v4(q);
+          ub[s] = ld_relaxed_v4(q + 1);
+        }
+#pragma unroll
+        for (int s = 0; s < NSLG_TP_MAX_WORLD; ++s) {
+          if (s >= p.world) continue;
           NVec<T, VEC> v;
           if (s == rank) {
             v.u = mine[i];
@@ -256,7 +296,8 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_rmsnorm_kernel(const Ar
             const uint4* q = reinterpret_cast<const uint4*>(p.stage[rank] + slot_off +
                                                             s * p.region_bytes) +
                              row * units_per_row + 2 * i;
-            fetch(q, v.u);
+            settle(q, ua[s], ub[s]);
+            v.u = make_uint4(ua[s].x, ua[s].z, ub[s].x, ub[s].z);
           }
 #pragma unroll
           for (int j = 0; j < VEC; ++j) acc[k][j] = __fadd_rn(acc[k][j], Elem<T>::to_f(v.e[j]));

@@ -4,6 +4,7 @@ Each op checks devices, dtypes and layouts, passes raw pointers and the current 
 stream to the native library, and raises on any non-zero status.  Nothing here
 computes on the CPU: the ops need CUDA tensors and the built library.
 """
+import os
 import threading
 
 import torch
@@ -262,7 +263,9 @@ def silu_mul(gate_up, out=None):
 
 
 LINEAR_MAX_ROWS = 256     # what nslg_linear accepts
-LINEAR_AUTO_ROWS = 16     # what ``linear`` sends it by default
+# what ``linear`` sends it by default; NSLG_LINEAR_ROWS (read at import) changes it, for
+# measurements (1 to LINEAR_MAX_ROWS)
+LINEAR_AUTO_ROWS = max(1, min(int(os.environ.get("NSLG_LINEAR_ROWS", "16")), 256))
 
 
 def linear_supported(x, weight, bias=None, max_rows=LINEAR_MAX_ROWS):
