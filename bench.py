@@ -1207,7 +1207,9 @@ def _allreduce_parity(device, world, rank, hidden=4096):
     os.environ.pop("NSLG_TP_TWO_SHOT", None)
     # the RowParallel GEMM pushing its own rows (nslg_linear_tp_push), then the reduction
     # (decode batches of up to tp_comm.FUSED_PUSH_MAX_ROWS rows take this path)
-    from nanoslg_b200.tp_comm import FUSED_PUSH_MAX_ROWS
+    from nanoslg_b200.tp_comm import FUSED_PUSH_MAX_ROWS, FUSED_PUSH_MIN_WORLD
+    min_world = FUSED_PUSH_MIN_WORLD
+    peer_world_ok = world >= min_world
     ok = True
     k = 4096 // world
     for it, rows in enumerate(sorted({1, FUSED_PUSH_MAX_ROWS, max(1, FUSED_PUSH_MAX_ROWS - 1)})):
@@ -1217,9 +1219,10 @@ def _allreduce_parity(device, world, rank, hidden=4096):
         gs = torch.Generator().manual_seed(77 + it)
         res = torch.randn(rows, hidden, generator=gs).to(bf)
         w = (1 + 0.1 * torch.randn(hidden, generator=gs)).to(bf)
-        part = peer.linear_push(x, wt)
+        part = peer.linear_push(x, wt) if peer_world_ok else None
         if part is None:
-            ok = False
+            if peer_world_ok:
+                ok = False
             break
         r_dev = res.to(device)
         peer.allreduce_add_norm(part, r_dev, w.to(device), 1e-5)
@@ -1234,7 +1237,8 @@ def _allreduce_parity(device, world, rank, hidden=4096):
         ops.check_device_status(device)
     except RuntimeError:
         ok = False
-    res_ok["fused_gemm_push"] = bool(ok)
+    if peer_world_ok:                     # below FUSED_PUSH_MIN_WORLD the path is unused
+        res_ok["fused_gemm_push"] = bool(ok)
     peer.close()
     return {"world": world, "rows": [64, 1, 64], "ok": all(res_ok.values()), "modes": res_ok,
             "check": "new residual bit-equal to bf16(bf16(fp32 rank-order sum) + residual)"}

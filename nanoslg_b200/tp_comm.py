@@ -25,10 +25,12 @@ from . import _native as N
 from . import ops
 
 
-# Rows up to which the RowParallel GEMM pushes its own rows. Measured at TP=4 on B200
-# (o_proj shard, [rows, 1024] x [4096, 1024]^T, then the reduction + RMSNorm, graph
-# loops): 1 row 11.0 us fused against 11.6 separate, 16 rows 14.8 against 14.2.
+# Rows up to which, and group sizes from which, the RowParallel GEMM pushes its own rows.
+# Measured on B200s (o_proj shard, then the reduction + RMSNorm, CUDA-graph loops, max
+# over ranks): TP=4, 1 row 11.0 us fused against 11.6 separate, 16 rows 14.8 against
+# 14.2; TP=2, 1 row 10.4 against 10.0, 4 rows 10.9 against 10.4.
 FUSED_PUSH_MAX_ROWS = 4
+FUSED_PUSH_MIN_WORLD = 4
 
 
 class PeerAllReduce:
@@ -89,7 +91,8 @@ class PeerAllReduce:
         collective's data movement in one launch). Returns y, the partial that the next
         ``allreduce_add_norm`` reduces (it then skips its own push), or None when the
         fused kernel does not take these operands (the caller runs the plain product)."""
-        if not self.fuse_push or not ops.linear_supported(x, weight):
+        if (not self.fuse_push or self.world < FUSED_PUSH_MIN_WORLD
+                or not ops.linear_supported(x, weight)):
             return None
         k, n = x.shape[-1], weight.shape[0]
         if n != self.hidden or x.dtype != self.dtype:
