@@ -47,9 +47,10 @@
 //   warp 1     MMA issuer: 4 MMAs per stage, commits each stage back to the producer and
 //              the accumulator to the epilogue;
 //   warps 4-7  epilogue: thread r owns TMEM lane r = weight row n0 + r; reads D in
-//              16-column pieces and writes y[m][n0 + r] (each store instruction of a warp
-//              covers 32 consecutive n of one row m), or the fp32 partial to shared
-//              memory; then all 256 threads of the CTA do its share of the cluster's sum.
+//              32-column pieces into shared memory (the idle stage ring): the rounded y
+//              tile, or the fp32 partial tile; then all 256 threads of the CTA write the
+//              tile's rows of y with 16-byte stores, or do its share of the cluster's
+//              sum (16-byte loads of the partials, 8-byte stores of y).
 // Every wait is bounded (2 s); on a timeout the kernel records NSLG_DEV_WAIT_TIMEOUT,
 // stops, drains what it issued (bounded), frees TMEM and returns.
 #include <cooperative_groups.h>
@@ -74,6 +75,10 @@ constexpr int kMinChunksPerSplit = 2;   // 32 KiB of weights per CTA at least
 constexpr int kCtasPerSm = 2;           // K splits may fill the SMs twice over
 constexpr int kMaxSplits = 8;           // portable cluster size
 constexpr int kWBytes = kTileN * 128;   // 16 KiB W box per stage
+// Row stride (floats) of a staged fp32 partial tile: 128 + 16, so that rows m and m + 1
+// sit 16 banks apart. Mp * 576 bytes fit in the stage ring for every Mp <= 256 (at
+// least three stages of 16 KiB + Mp * 128 bytes).
+constexpr int kPartStride = kTileN + 16;
 // Stage ring of about 112 KiB, so that two CTAs fit on an SM: a wide product's whole
 // grid runs at once, and the next launch's CTA can set up and start its weight loads
 // while this one drains (a 200 KiB ring of 8 stages, one CTA per SM, measured slower on
@@ -86,9 +91,39 @@ struct LinParams {
   int64_t y_stride;
   int M, N, Mp, kc, splits, stages, tmem_cols;
   int do_push;      // also push y's rows to the peers (push)
+  int y_vec;        // y's rows start on 16-byte boundaries (base and stride)
   TpPush push;
   uint32_t* status;
 };
+
+// y[m][n0 .. n0 + 8) = the eight values packed in v: one 16-byte store where the row is
+// aligned and the eight columns exist, else element by element up to out_features.
+template <typename T>
+__device__ __forceinline__ void store_y8(const LinParams& p, int m, int n0, uint4 v) {
+  T* dst = static_cast<T*>(p.y) + static_cast<int64_t>(m) * p.y_stride + n0;
+  if (p.y_vec && n0 + 8 <= p.N) {
+    *reinterpret_cast<uint4*>(dst) = v;
+  } else {
+    const T* e = reinterpret_cast<const T*>(&v);
+    for (int i = 0; i < 8 && n0 + i < p.N; ++i) dst[i] = e[i];
+  }
+}
+
+// y[m][n0 .. n0 + 4) = v rounded to T: one 8-byte store where the row is aligned and
+// the four columns exist, else element by element up to out_features.
+template <typename T>
+__device__ __forceinline__ void store_y4(const LinParams& p, int m, int n0, const float (&v)[4]) {
+  T* dst = static_cast<T*>(p.y) + static_cast<int64_t>(m) * p.y_stride + n0;
+  if (p.y_vec && n0 + 4 <= p.N) {
+    uint2 out;
+    T* e = reinterpret_cast<T*>(&out);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = Elem<T>::from_f(v[i]);
+    *reinterpret_cast<uint2*>(dst) = out;
+  } else {
+    for (int i = 0; i < 4 && n0 + i < p.N; ++i) dst[i] = Elem<T>::from_f(v[i]);
+  }
+}
 
 // First row of the tile that CTA j of s sums in the split-K reduction: a multiple of 8
 // (whole 16-byte vectors of a y row for the push), every CTA at least 16 rows.
@@ -148,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* mma_drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* partial = reinterpret_cast<float*>(smem);   // [Mp][kTileN], over the stage ring
+  float* partial = reinterpret_cast<float*>(smem);   // [Mp][kPartStride], over the stage ring
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int t = blockIdx.x / p.splits;            // tile
@@ -252,9 +287,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     // -------------------------------------------------------------- epilogue
     const int r = (warp & 3) * 32 + lane;          // TMEM lane = row of the tile
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const int et = threadIdx.x - 128;              // 0..127
-    const int n = t * kTileN + r;
-    T* y = static_cast<T*>(p.y);
     const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0));
     if (!ok) {
       if (lane == 0) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
@@ -262,19 +294,23 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     if (ok) {
       tc_fence_after();
-      for (int c0 = 0; c0 < p.Mp; c0 += 16) {
-        float v[16];
-        tmem_ld16(lane_base + c0, v);
+      // this thread's row of D, 32 columns (activation rows) per wait, into shared
+      // memory: the rounded y tile [Mp][128] (splits == 1) or the fp32 partial tile
+      // [Mp][128]; each store instruction of a warp covers 32 consecutive tile rows
+      T* tile_y = reinterpret_cast<T*>(smem);
+      for (int c0 = 0; c0 < p.Mp; c0 += 32) {
+        float v[32];
+        tmem_ld16(lane_base + c0, *reinterpret_cast<float(*)[16]>(v));
+        if (c0 + 16 < p.Mp) tmem_ld16(lane_base + c0 + 16, *reinterpret_cast<float(*)[16]>(v + 16));
         tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
+        for (int q = 0; q < 32; ++q) {
           const int m = c0 + q;
           if (m >= p.M) break;
-          if (p.splits == 1) {
-            if (n < p.N) y[static_cast<int64_t>(m) * p.y_stride + n] = Elem<T>::from_f(v[q]);
-          } else {
-            partial[m * kTileN + r] = v[q];
-          }
+          if (p.splits == 1)
+            tile_y[m * kTileN + r] = Elem<T>::from_f(v[q]);
+          else
+            partial[m * kPartStride + r] = v[q];
         }
       }
     }
@@ -282,32 +318,46 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   tc_fence_before();
   __syncthreads();
-  if (p.splits > 1) {
+  if (p.splits == 1) {
+    // the staged tile to y, 8 consecutive outputs (16 bytes) of one row per store
+    if (!*abort_flag) {
+      const T* tile_y = reinterpret_cast<const T*>(smem);
+      for (int u = threadIdx.x; u < p.M * (kTileN / 8); u += kThreads) {
+        const int m = u / (kTileN / 8), c = 8 * (u % (kTileN / 8));
+        store_y8<T>(p, m, t * kTileN + c, *reinterpret_cast<const uint4*>(tile_y + m * kTileN + c));
+      }
+    }
+  } else {
     // split-K sum across the cluster (the s CTAs of this tile) through distributed
-    // shared memory; rank order = split order
+    // shared memory; rank order = split order. Unit = 4 consecutive rows of the tile for
+    // one activation row m: one 16-byte load from each of the s partials, all issued
+    // before the sum, one 8-byte store of y. With 32 or 16 rows per CTA (s = 4, 8) the
+    // eight threads of a quarter warp read 128 bytes of one row m, or 64 of each of
+    // two rows m 16 banks apart (the padded row stride): one wavefront per quarter warp.
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();                                 // every partial is staged
     if (!*abort_flag) {
-      T* y = static_cast<T*>(p.y);
       const int r_lo = split_row_lo(j, p.splits);
-      const int rows_s = split_row_lo(j + 1, p.splits) - r_lo;
-      const int E = rows_s * p.M;                   // (row, m) elements of this CTA's rows
+      const int quads = (split_row_lo(j + 1, p.splits) - r_lo) / 4;
       const float* src[kMaxSplits];
 #pragma unroll
       for (int sp = 0; sp < kMaxSplits; ++sp)
         src[sp] = cluster.map_shared_rank(partial, sp < p.splits ? sp : 0);
-      for (int e = threadIdx.x; e < E; e += kThreads) {
-        const int m = e / rows_s, row = r_lo + e % rows_s;
-        float v[kMaxSplits];
+      for (int e = threadIdx.x; e < p.M * quads; e += kThreads) {
+        const int m = e / quads, row = r_lo + 4 * (e % quads);
+        float4 a[kMaxSplits];
 #pragma unroll
         for (int sp = 0; sp < kMaxSplits; ++sp)
-          v[sp] = sp < p.splits ? src[sp][m * kTileN + row] : 0.f;
-        float acc = 0.f;
+          a[sp] = sp < p.splits
+                      ? *reinterpret_cast<const float4*>(src[sp] + m * kPartStride + row)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int sp = 0; sp < kMaxSplits; ++sp) acc += v[sp];
-        const int nn = t * kTileN + row;
-        if (nn < p.N) y[static_cast<int64_t>(m) * p.y_stride + nn] = Elem<T>::from_f(acc);
+        for (int sp = 0; sp < kMaxSplits; ++sp) {
+          acc[0] += a[sp].x; acc[1] += a[sp].y; acc[2] += a[sp].z; acc[3] += a[sp].w;
+        }
+        store_y4<T>(p, m, t * kTileN + row, acc);
       }
     }
     cluster.sync();                                 // no partial is read any more
@@ -409,6 +459,7 @@ int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_st
   p.stages = pl.stages;
   p.tmem_cols = pl.tmem_cols;
   p.do_push = push != nullptr ? 1 : 0;
+  p.y_vec = (reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_stride % 8 == 0) ? 1 : 0;
   if (push != nullptr) p.push = *push;
   p.status = status;
   const size_t smem = smem_bytes(pl.stages, pl.Mp);

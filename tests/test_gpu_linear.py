@@ -69,6 +69,23 @@ def test_linear_lm_head_on_a_strided_last_position():
     torch.testing.assert_close(y, _ref(last.contiguous(), w), **TOL[dt])
 
 
+@pytest.mark.parametrize("m,n,k", [(17, 1001, 512), (5, 4093, 1792), (64, 3000, 4096)])
+@pytest.mark.parametrize("pad", [0, 3])
+def test_linear_output_rows_unaligned_or_ragged(m, n, k, pad):
+    """y written into rows of stride n + pad (pad 3: no row starts on a 16-byte
+    boundary, so every store is element-wise) with out_features not a multiple of 4 or
+    8 (the last vector of a row is cut at out_features), for whole tiles (n = 1001,
+    3000) and cluster-split tiles (4093 x 1792); nothing past out_features is written."""
+    dt = torch.bfloat16
+    x, w = _problem(m, n, k, dt, seed=m + n + pad)
+    buf = torch.full((m, n + pad), 7.0, dtype=dt, device=DEV)
+    y = buf[:, :n]
+    ops.linear(x, w, out=y, max_rows=ops.LINEAR_MAX_ROWS)
+    torch.testing.assert_close(y, _ref(x, w), **TOL[dt])
+    assert bool((buf[:, n:] == 7.0).all())
+    assert torch.equal(y, ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS))
+
+
 def test_linear_graph_replay():
     dt = torch.bfloat16
     x, w = _problem(64, 4096, 4096, dt, seed=11)
