@@ -155,6 +155,7 @@ def build_c2_device(device, seed, pool_pages=POOL_PAGES):
 
 
 def run_kernel(device, steps, warmup, seed, pool_pages=POOL_PAGES):
+    """The headline: C2 decode steps on resident inputs."""
     from nanoslg_b200 import ops
     c = build_c2_device(device, seed, pool_pages)
     out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=device)
@@ -296,10 +297,10 @@ def run_e2e(device, steps, warmup, seed, depth=1):
 
 
 # ------------------------------------------------------------------ prefill kernel
-def run_prefill_kernel(device, reps=10, batch=64, prompt=512):
-    """Causal prefill attention of the C3 batch-64 prompts (32/8 heads, D=128) on the
-    tcgen05 kernel: algorithmic FLOPs = sum_b sum_i 4*Hq*D*(i+1) over the causal rows."""
-    from nanoslg_b200 import ops
+def c3_prefill_inputs(device, batch=64, prompt=512):
+    """The C3 prefill prompts as one ragged batch: q [batch * prompt, 32, 128] and its
+    qo_indptr, a pool holding every prompt's K/V (pages drawn from a permutation), the
+    CSR page table and last-page lengths; seeded N(0, 1) bf16."""
     npg = -(-prompt // PS)
     pages = batch * npg + 1
     g = torch.Generator(device=device).manual_seed(7)
@@ -310,6 +311,106 @@ def run_prefill_kernel(device, reps=10, batch=64, prompt=512):
     lpl = torch.full((batch,), prompt - (npg - 1) * PS, device=device, dtype=torch.int32)
     qo = torch.arange(0, batch * prompt + 1, prompt, device=device, dtype=torch.int32)
     q = torch.randn(batch * prompt, HQ, D, device=device, generator=g).to(torch.bfloat16)
+    return q, qo, pool_k, pool_v, indptr, indices, lpl
+
+
+def _median_ms(fn, reps, warm=3):
+    """Median CUDA-event time of ``fn`` over ``reps`` back-to-back calls, after ``warm``."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    ev[0].record()
+    for i in range(reps):
+        fn()
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    return statistics.median(ev[i].elapsed_time(ev[i + 1]) for i in range(reps))
+
+
+def run_reference_backend(device, reps=20):
+    """The reference's GPU attention backend, FlashInfer (kv_cache.py:704-705: one
+    BatchDecodeWithPagedKVCacheWrapper and one BatchPrefillWithPagedKVCacheWrapper, NHD;
+    planned as kv_cache.py:617-633 does, with the same CSR page table; run as
+    kv_cache.py:650-654), on the C2 decode batch and the C3 prefill prompts, timed beside
+    this repo's kernels on the same inputs. FlashInfer is the build installed in the image
+    (library code, not part of this repository); its first call JIT-compiles or loads its
+    kernels, outside the timing. Prefill is timed on the backend the reference gets
+    (the wrapper's default) and on FlashInfer's TensorRT-LLM Blackwell kernels
+    (backend "trtllm-gen", prebuilt), the fastest library prefill on this GPU."""
+    try:
+        import flashinfer
+    except Exception as e:                 # not in this environment
+        return {"unavailable": f"flashinfer not importable: {type(e).__name__}: {e}"}
+    from nanoslg_b200 import ops
+    hbm, _ = peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        tpk = 1590.0
+    scale = 1.0 / math.sqrt(D)
+    res = {"library": f"flashinfer {flashinfer.__version__}",
+           "timing": f"median of {reps} back-to-back calls, CUDA events, eager launches"}
+    ws = torch.empty(128 << 20, dtype=torch.uint8, device=device)
+    c2 = None
+    try:
+        c2 = build_c2_device(device, 0)
+        dec = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD")
+        dec.plan(c2["indptr"], c2["indices"], c2["lpl"], HQ, HKV, D, PS,
+                 q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16)
+        o_fi = dec.run(c2["q"], (c2["pool_k"], c2["pool_v"]))
+        o_us = torch.empty_like(c2["q"])
+        ops.paged_decode(c2["q"], c2["pool_k"], c2["pool_v"], c2["indptr"], c2["indices"],
+                         c2["lpl"], scale, out=o_us)
+        torch.cuda.synchronize()
+        ab = alg_bytes(c2["lens"])
+        fi_ms = _median_ms(lambda: dec.run(c2["q"], (c2["pool_k"], c2["pool_v"]), out=o_fi), reps)
+        us_ms = _median_ms(lambda: ops.paged_decode(
+            c2["q"], c2["pool_k"], c2["pool_v"], c2["indptr"], c2["indices"], c2["lpl"], scale,
+            out=o_us), reps)
+        res["c2_decode"] = {
+            "flashinfer_ms": fi_ms, "ours_ms": us_ms, "speedup": fi_ms / us_ms,
+            "flashinfer_hbm_frac": ab / (fi_ms / 1e3) / 1e9 / hbm,
+            "ours_hbm_frac": ab / (us_ms / 1e3) / 1e9 / hbm,
+            "max_abs_diff": float((o_fi.float() - o_us.float()).abs().max())}
+        del o_fi, o_us, dec
+    except Exception as e:
+        res["c2_decode"] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+    del c2
+    torch.cuda.empty_cache()
+    q, qo, pool_k, pool_v, indptr, indices, lpl = c3_prefill_inputs(device)
+    flops = 64 * 4 * HQ * D * (512 * 513 // 2)
+    o_us = torch.empty_like(q)
+    run_us = lambda: ops.paged_prefill(q, qo, 512, pool_k, pool_v, indptr, indices, lpl, scale,
+                                       causal=True, out=o_us)
+    us_ms = _median_ms(run_us, reps)
+    for backend in ("auto", "trtllm-gen"):
+        try:
+            pf = flashinfer.BatchPrefillWithPagedKVCacheWrapper(ws, "NHD", backend=backend)
+            pf.plan(qo, indptr, indices, lpl, HQ, HKV, D, PS, causal=True,
+                    q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16)
+            o_fi = pf.run(q, (pool_k, pool_v))
+            torch.cuda.synchronize()
+            fi_ms = _median_ms(lambda: pf.run(q, (pool_k, pool_v), out=o_fi), reps)
+            res[f"c3_prefill_{backend}"] = {
+                "flashinfer_ms": fi_ms, "ours_ms": us_ms, "speedup": fi_ms / us_ms,
+                "flashinfer_tensor_frac": flops / (fi_ms / 1e3) / 1e12 / tpk,
+                "ours_tensor_frac": flops / (us_ms / 1e3) / 1e12 / tpk,
+                "max_abs_diff": float((o_fi.float() - o_us.float()).abs().max())}
+            del o_fi, pf
+        except Exception as e:
+            res[f"c3_prefill_{backend}"] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+    del q, pool_k, pool_v, o_us, ws
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_prefill_kernel(device, reps=10, batch=64, prompt=512):
+    """Causal prefill attention of the C3 batch-64 prompts (32/8 heads, D=128) on the
+    tcgen05 kernel: algorithmic FLOPs = sum_b sum_i 4*Hq*D*(i+1) over the causal rows."""
+    from nanoslg_b200 import ops
+    q, qo, pool_k, pool_v, indptr, indices, lpl = c3_prefill_inputs(device, batch, prompt)
     out = torch.empty_like(q)
     scale = 1.0 / math.sqrt(D)
 
@@ -1345,7 +1446,7 @@ def main():
                          "with residual add + RMSNorm (peer), or NCCL all-reduce (nccl)")
     ap.add_argument("--only", choices=["all", "kernel", "model", "prefill", "allreduce",
                                        "elementwise", "e2e", "parity", "decode-shapes",
-                                       "linear"],
+                                       "linear", "refbackend"],
                     default="all",
                     help="kernel: only the resident-input kernel timing (profiling case); "
                          "model: only the Llama-3.1-8B decode leg; elementwise: the RoPE + "
@@ -1353,7 +1454,11 @@ def main():
                          "e2e: only the two end-to-end legs (one and two steps in flight); "
                          "parity: only the sharded-path token / reduction checks; "
                          "decode-shapes: decode attention at the 8B model's decode shapes; "
-                         "linear: the tcgen05 linear kernel against cuBLAS per 8B shape")
+                         "linear: the tcgen05 linear kernel against cuBLAS per 8B shape; "
+                         "refbackend: the reference's FlashInfer backend against these "
+                         "kernels on C2 decode and C3 prefill")
+    ap.add_argument("--no-ref-backend", action="store_true",
+                    help="skip the FlashInfer (reference GPU backend) leg of the default run")
     ap.add_argument("--linear-sweep", action="store_true",
                     help="--only linear: also time the kernel under other split policies")
     ap.add_argument("--linear-shape", default=None,
@@ -1444,6 +1549,13 @@ def main():
             print(json.dumps({"case": "linear only", "linear_shapes":
                               run_linear_shapes(device, shapes, policies=policies)}),
                   flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
+    if a.only == "refbackend":
+        if rank == 0:
+            print(json.dumps({"case": "reference GPU backend only", "reference_gpu_backend":
+                              run_reference_backend(device)}), flush=True)
         if world > 1:
             torch.distributed.destroy_process_group()
         return 0
@@ -1560,6 +1672,9 @@ def main():
         torch.distributed.barrier()
     if not a.no_model:
         line.update(run_model_legs(a, device, world, rank))
+    if a.only == "all" and world == 1 and not a.no_ref_backend:
+        # last of the GPU legs: the library's kernels run after every leg of this repo
+        line["reference_gpu_backend"] = run_reference_backend(device)
     if rank == 0 and not a.no_cpu:
         r = cpu_reference(a.cpu_seconds)
         line["cpu_baseline"] = {"value": r["value"], "unit": "tok/s", "cores": r["cores"],
