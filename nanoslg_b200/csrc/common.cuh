@@ -65,6 +65,18 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
   return v;
 }
 
+// Atomic add with acquire-release semantics at GPU scope; returns the old value. After a
+// CTA barrier, one thread's release publishes every write the CTA made before the
+// barrier (release is cumulative over what the barrier ordered before it), and its
+// acquire orders the CTA's later reads (after the next barrier) behind every write
+// published by the increments that preceded it.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_u32(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

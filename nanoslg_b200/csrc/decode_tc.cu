@@ -118,8 +118,9 @@ __device__ void zero_empty_sequences(const DecodeParams& p, const int32_t* indpt
 
 // Combines the `cnt` partials of sequence b (slots b + cf .. b + cf + cnt - 1) into
 // out[b]; run by the kConsumerWarps warps of the CTA that arrived last. The partials
-// were written by other CTAs and fenced before their arrival; they are read through L2
-// (ld.global.cg), never from this SM's L1.
+// were written by other CTAs and published by their arrivals; they are read through L2
+// (ld.global.cg), never from this SM's L1. Up to kFastMerge partials: one pass (below).
+// More:
 //   pass 1: per query head, m = max_i lse_i and 1 / sum_i 2^(lse_i - m); 8 lanes per
 //           head split the partials (32 heads per pass of the CTA);
 //   pass 2: per (head, 4 dims), sum_i 2^(lse_i - m) o_i, times 1 / sum; with many
@@ -127,12 +128,71 @@ __device__ void zero_empty_sequences(const DecodeParams& p, const int32_t* indpt
 //           loop over the partials, two steps unrolled), with few (hq x D / 4 <= 128)
 //           2 to 8 lanes share one output's partials and add up by shuffles. The order
 //           of the sums depends only on the shapes, not on which CTA merges.
+constexpr int kFastMerge = 4;   // partials merged in one pass of loads
+
 template <typename T, int D>
 __device__ void merge_sequence(const DecodeParams& p, int b, int cf, int cnt, float* stat,
                                int tid) {
   const int warp = tid / 32, lane = tid % 32;
   const int64_t slot0 = static_cast<int64_t>(b) + cf;
   const float* lse0 = p.part_lse + slot0 * p.hq;
+  if (cnt <= kFastMerge) {
+    // Few partials (a sequence over at most 4 CTAs): each thread takes (head, 4 dims)
+    // outputs e, e + 256, ... and issues every load it needs -- the log-sum-exp and the
+    // 4 partial values of each of its outputs' partials -- before any arithmetic, so the
+    // merge costs one L2 round trip. Per output: m = max_i lse_i, w_i = 2^(lse_i - m),
+    // out = (sum_i w_i o_i) / (sum_i w_i), sums in partial order.
+    constexpr int DQ = D / 4;
+    constexpr int kE = 4;
+    const int n_out = p.hq * DQ;
+    const int64_t step = static_cast<int64_t>(p.hq) * D;
+    for (int e0 = tid; e0 < n_out; e0 += kE * kMergeThreads) {
+      float l[kE][kFastMerge];
+      float4 v[kE][kFastMerge];
+#pragma unroll
+      for (int k = 0; k < kE; ++k) {
+        const int e = e0 + k * kMergeThreads;
+        const int ec = e < n_out ? e : n_out - 1;     // clamped: loads stay in range
+        const int hq = ec / DQ;
+        const float* po = p.part_o + (slot0 * p.hq + hq) * D + (ec % DQ) * 4;
+#pragma unroll
+        for (int i = 0; i < kFastMerge; ++i) {
+          if (i < cnt && e < n_out) {
+            l[k][i] = __ldcg(lse0 + static_cast<int64_t>(i) * p.hq + hq);
+            v[k][i] = __ldcg(reinterpret_cast<const float4*>(po + i * step));
+          } else {
+            l[k][i] = -INFINITY;
+            v[k][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kE; ++k) {
+        const int e = e0 + k * kMergeThreads;
+        if (e >= n_out) continue;
+        float m = l[k][0];
+#pragma unroll
+        for (int i = 1; i < kFastMerge; ++i) m = fmaxf(m, l[k][i]);
+        float s = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < kFastMerge; ++i) {
+          const float w = l[k][i] == -INFINITY ? 0.f : fast_exp2(l[k][i] - m);
+          s += w;
+          acc.x = fmaf(w, v[k][i].x, acc.x);
+          acc.y = fmaf(w, v[k][i].y, acc.y);
+          acc.z = fmaf(w, v[k][i].z, acc.z);
+          acc.w = fmaf(w, v[k][i].w, acc.w);
+        }
+        const float inv = s > 0.f ? 1.f / s : 0.f;
+        T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride +
+                static_cast<int64_t>(e / DQ) * D + (e % DQ) * 4;
+        reinterpret_cast<uint32_t*>(ob)[0] = Mma16<T>::pack(acc.x * inv, acc.y * inv);
+        reinterpret_cast<uint32_t*>(ob)[1] = Mma16<T>::pack(acc.z * inv, acc.w * inv);
+      }
+    }
+    return;
+  }
   for (int h0 = warp * 4; h0 < p.hq; h0 += kConsumerWarps * 4) {
     const int hq = h0 + lane / 8, sub = lane % 8;
     float m = -INFINITY, s = 0.f;
@@ -637,17 +697,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // merges. Every CTA of the sequence arrives exactly once, also after a timed-out
       // wait (its partial is then garbage, and the status word says so), so the counts
       // always return to zero.
-      __threadfence();
+      // One barrier, then one acquire-release increment by thread 0: its release
+      // publishes the partial all warps stored before the barrier, its acquire makes the
+      // partials of the CTAs that arrived earlier visible to the merge (one round trip
+      // instead of a fence per thread followed by the increment).
       named_barrier_sync(1, kMergeThreads);
       const int cf = cta_of(seq_beg, total, n);
       const int cnt = cta_of(seq_end - 1, total, n) - cf + 1;
       if (threadIdx.x == 0) {
-        const uint32_t prev = atomicAdd(&p.arrive[cf], 1u);
+        const uint32_t prev = atom_add_acq_rel_u32(&p.arrive[cf], 1u);
         const bool last = prev + 1u == static_cast<uint32_t>(cnt);
-        if (last) {
-          __threadfence();   // the others' partials, fenced before their arrivals
-          atomicExch(&p.arrive[cf], 0u);
-        }
+        if (last) atomicExch(&p.arrive[cf], 0u);
         s_merge = last ? 1 : 0;
       }
       named_barrier_sync(1, kMergeThreads);
