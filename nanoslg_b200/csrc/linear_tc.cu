@@ -22,12 +22,17 @@
 // the clusters pack into the GPCs in one wave): s = 1 for wide products (each CTA one whole tile, written straight to y; a 224-tile
 // product runs at once on 148 SMs), s > 1 for narrow ones (o_proj, down_proj, TP
 // shards). The s CTAs of a tile form one thread-block cluster, and the split-K sum
-// never leaves the chip: each CTA stages its fp32 partial tile in its own shared memory
-// (the stage ring, idle once the MMAs are done), the cluster synchronises, and CTA j
-// sums rows [8 floor(16 j / s), 8 floor(16 (j + 1) / s)) of the tile over the s
-// partials, read through distributed shared memory in rank order (the same order on
-// every call), rounds once and writes them to y; a second cluster barrier keeps every
-// partial in place until all readers are done.
+// never leaves the chip: CTA j owns rows [8 floor(16 j / s), 8 floor(16 (j + 1) / s))
+// of the tile, sums them over the s fp32 partials in rank order (the same order on
+// every call), rounds once and writes them to y. Decode batches (up to 32 rows): every
+// CTA stores its partial of each owner's rows straight into that owner's shared memory
+// (st.async, 4 bytes per store, each counted on the owner's mbarrier), and the owner
+// waits for its mbarrier alone -- one cluster arrive at the start, no cluster barrier
+// at the end (about 1 us less per call than the pulled sum). Larger batches: each CTA
+// stages its partial tile in its own shared memory (the stage ring, idle once the MMAs
+// are done), the cluster synchronises, the owners read the partials through
+// distributed shared memory, and a second cluster barrier keeps every partial in place
+// until all readers are done.
 //
 // Fused tensor-parallel push (nslg_linear_tp_push). For a RowParallel product (o_proj,
 // down_proj) of a TP decode step, y is this rank's partial of the all-reduce that
@@ -85,6 +90,12 @@ constexpr int kPartStride = kTileN + 16;
 // the 8B shapes: 19.5 against 12.3 us for q|k|v at one row).
 constexpr int kLinearSmemBudget = 112 * 1024;
 constexpr int kMaxTiles = 1 << 16;      // out_features <= 8,388,608
+// Split-K sums of batches up to this many (padded) rows are pushed: each CTA stores its
+// partial rows straight into the shared memory of the CTA that owns them (st.async,
+// completing on the owner's mbarrier), instead of staging them and pulling them through
+// distributed shared memory between two cluster barriers. The receive buffer,
+// s * Mp * (largest row share) floats <= 168 * Mp * 4 bytes, comes out of the ring.
+constexpr int kPushMaxMp = 32;
 
 struct LinParams {
   void* y;
@@ -92,6 +103,7 @@ struct LinParams {
   int M, N, Mp, kc, splits, stages, tmem_cols;
   int do_push;      // also push y's rows to the peers (push)
   int y_vec;        // y's rows start on 16-byte boundaries (base and stride)
+  int push_sum;     // split-K partials pushed to their owners (splits > 1, Mp <= 32)
   TpPush push;
   uint32_t* status;
 };
@@ -128,6 +140,56 @@ __device__ __forceinline__ void store_y4(const LinParams& p, int m, int n0, cons
 // First row of the tile that CTA j of s sums in the split-K reduction: a multiple of 8
 // (whole 16-byte vectors of a y row for the push), every CTA at least 16 rows.
 __device__ __forceinline__ int split_row_lo(int j, int s) { return 8 * ((16 * j) / s); }
+
+// The CTA of the cluster whose share of the tile's rows holds row r.
+__device__ __forceinline__ int split_owner(int r, int s) {
+  int o = 0;
+  for (int j = 1; j < s; ++j)
+    if (split_row_lo(j, s) <= r) o = j;
+  return o;
+}
+
+// Address of this CTA's shared-memory word `local` in the shared memory of cluster CTA
+// `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+// 4-byte store into another cluster CTA's shared memory that counts 4 bytes of
+// transaction on that CTA's mbarrier `bar` when it lands (both cluster addresses).
+__device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                   addr),
+               "r"(__float_as_uint(v)), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Bounded wait (the same limit as mbar_wait) for a phase completed by other CTAs'
+// st.async transactions: acquire at cluster scope, so their stores are visible.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
 
 __device__ __forceinline__ void st_sys_v4(void* ptr, uint32_t a, uint32_t b, uint32_t c,
                                           uint32_t d) {
@@ -181,9 +243,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* empty = full + kMaxStages;
   uint64_t* acc_full = empty + kMaxStages;
   uint64_t* mma_drain = acc_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
+  uint64_t* recv_full = mma_drain + 1;            // push_sum: every partial row has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* partial = reinterpret_cast<float*>(smem);   // [Mp][kPartStride], over the stage ring
+  // push_sum: [s][M][rows of this CTA's share] received partials, after the barriers
+  float* recv = reinterpret_cast<float*>(smem + p.stages * sbytes + 256);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int t = blockIdx.x / p.splits;            // tile
@@ -197,8 +262,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     mbar_init(acc_full, 1);
     mbar_init(mma_drain, 1);
+    mbar_init(recv_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
+    if (p.push_sum)   // every CTA of the cluster sends its partial of this CTA's rows
+      mbar_arrive_expect_tx(recv_full, static_cast<uint32_t>(p.splits * p.M * 4 *
+                                                             (split_row_lo(j + 1, p.splits) -
+                                                              split_row_lo(j, p.splits))));
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -211,6 +281,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // push_sum: the receive barriers of the cluster are armed once every CTA has passed
+  // this arrive; senders wait for it before their first remote store
+  if (p.push_sum) cluster_arrive_release();
   pdl_trigger();     // the next kernel may start its prologue; it waits for our completion
 
   if (warp == 0) {
@@ -285,7 +358,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else if (warp >= 4) {
     // -------------------------------------------------------------- epilogue
+    if (p.push_sum) cluster_wait_acquire();
     const int r = (warp & 3) * 32 + lane;          // TMEM lane = row of the tile
+    // push_sum: the owner of row r, and where this CTA's values of row r go there
+    const int own = p.push_sum ? split_owner(r, p.splits) : 0;
+    const int own_lo = split_row_lo(own, p.splits);
+    const int own_rows = split_row_lo(own + 1, p.splits) - own_lo;
+    const uint32_t dst0 =
+        p.push_sum ? cluster_addr(smem_u32(recv) + 4u * static_cast<uint32_t>(
+                                                           j * p.M * own_rows + (r - own_lo)),
+                                  own)
+                   : 0u;
+    const uint32_t dst_bar = p.push_sum ? cluster_addr(smem_u32(recv_full), own) : 0u;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0));
     if (!ok) {
@@ -309,6 +393,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (m >= p.M) break;
           if (p.splits == 1)
             tile_y[m * kTileN + r] = Elem<T>::from_f(v[q]);
+          else if (p.push_sum)
+            st_async_f32(dst0 + 4u * static_cast<uint32_t>(m * own_rows), v[q], dst_bar);
           else
             partial[m * kPartStride + r] = v[q];
         }
@@ -316,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
+  if (p.push_sum && warp < 4) cluster_wait_acquire();
   tc_fence_before();
   __syncthreads();
   if (p.splits == 1) {
@@ -325,6 +412,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int u = threadIdx.x; u < p.M * (kTileN / 8); u += kThreads) {
         const int m = u / (kTileN / 8), c = 8 * (u % (kTileN / 8));
         store_y8<T>(p, m, t * kTileN + c, *reinterpret_cast<const uint4*>(tile_y + m * kTileN + c));
+      }
+    }
+  } else if (p.push_sum) {
+    // this CTA's rows of the tile: wait (bounded) for the s partials to land, sum them
+    // in split order (the order of the pulled sum below), round once, store
+    const bool landed = mbar_wait_cluster(recv_full, 0);
+    if (!landed) {
+      if (threadIdx.x == 0) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+    } else if (!*abort_flag) {
+      const int r_lo = split_row_lo(j, p.splits);
+      const int rows_s = split_row_lo(j + 1, p.splits) - r_lo;
+      const int quads = rows_s / 4;
+      for (int e = threadIdx.x; e < p.M * quads; e += kThreads) {
+        const int m = e / quads, q4 = 4 * (e % quads);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp) {
+          const float4 a = sp < p.splits ? *reinterpret_cast<const float4*>(
+                                               recv + (sp * p.M + m) * rows_s + q4)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+          acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+        }
+        store_y4<T>(p, m, t * kTileN + r_lo + q4, acc);
       }
     }
   } else {
@@ -377,13 +487,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 struct Plan {
-  int Mp, n_tiles, kc, splits, grid, stages, tmem_cols;
+  int Mp, n_tiles, kc, splits, grid, stages, tmem_cols, push_sum, recv_bytes;
 };
 
 // Split policy overrides, for measurements: NSLG_LINEAR_CTAS_PER_SM (1 or 2: the grid
 // may fill the SMs once or twice over with K splits), NSLG_LINEAR_MIN_CHUNKS (the
-// fewest 64-element K chunks a split may have, 1 to 64) and NSLG_LINEAR_SPLITS (1 to 8
-// splits per tile, at most one per chunk, instead of the rule).
+// fewest 64-element K chunks a split may have, 1 to 64), NSLG_LINEAR_SPLITS (1 to 8
+// splits per tile, at most one per chunk, instead of the rule) and NSLG_LINEAR_PUSH_SUM
+// (0: the pulled split-K sum at every batch size).
 int env_int(const char* name, int dflt, int lo, int hi) {
   const char* e = std::getenv(name);
   if (e == nullptr || e[0] == '\0') return dflt;
@@ -391,13 +502,23 @@ int env_int(const char* name, int dflt, int lo, int hi) {
   return v < lo ? lo : (v > hi ? hi : v);
 }
 
-size_t smem_bytes(int stages, int Mp) {
-  return 1024 + static_cast<size_t>(stages) * (kWBytes + Mp * 128) + 256;
+size_t smem_bytes(int stages, int Mp, int recv_bytes) {
+  return 1024 + static_cast<size_t>(stages) * (kWBytes + Mp * 128) + 256 + recv_bytes;
 }
 
-int stages_for(int Mp) {
-  const int st = kLinearSmemBudget / (kWBytes + Mp * 128);
+int stages_for(int Mp, int recv_bytes) {
+  const int st = (kLinearSmemBudget - recv_bytes) / (kWBytes + Mp * 128);
   return st < kMinStages ? kMinStages : (st > kMaxStages ? kMaxStages : st);
+}
+
+// Receive buffer of a pushed split-K sum: s partials of the largest row share.
+int recv_bytes_for(int splits, int Mp) {
+  int rows = 0;
+  for (int j = 0; j < splits; ++j) {
+    const int r = 8 * ((16 * (j + 1)) / splits) - 8 * ((16 * j) / splits);
+    rows = r > rows ? r : rows;
+  }
+  return splits * Mp * rows * 4;
 }
 
 // Splits per tile: as many as fill the SMs `cps` times over (two CTAs fit on an SM),
@@ -422,7 +543,9 @@ Plan plan_for(int M, int N, int K) {
   if (forced > 0) s = forced <= pl.kc ? forced : pl.kc;
   pl.splits = s;
   pl.grid = pl.n_tiles * s;
-  pl.stages = stages_for(pl.Mp);
+  pl.push_sum = (s > 1 && pl.Mp <= kPushMaxMp && env_int("NSLG_LINEAR_PUSH_SUM", 1, 0, 1)) ? 1 : 0;
+  pl.recv_bytes = pl.push_sum ? recv_bytes_for(s, pl.Mp) : 0;
+  pl.stages = stages_for(pl.Mp, pl.recv_bytes);
   int cols = 32;
   while (cols < pl.Mp) cols *= 2;
   pl.tmem_cols = cols;
@@ -460,9 +583,10 @@ int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_st
   p.tmem_cols = pl.tmem_cols;
   p.do_push = push != nullptr ? 1 : 0;
   p.y_vec = (reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_stride % 8 == 0) ? 1 : 0;
+  p.push_sum = pl.push_sum;
   if (push != nullptr) p.push = *push;
   p.status = status;
-  const size_t smem = smem_bytes(pl.stages, pl.Mp);
+  const size_t smem = smem_bytes(pl.stages, pl.Mp, pl.recv_bytes);
   auto kern = dtype == NSLG_DTYPE_F16 ? linear_tc_kernel<__half> : linear_tc_kernel<__nv_bfloat16>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
