@@ -24,7 +24,7 @@
 // shards). The s CTAs of a tile form one thread-block cluster, and the split-K sum
 // never leaves the chip: CTA j owns rows [8 floor(16 j / s), 8 floor(16 (j + 1) / s))
 // of the tile, sums them over the s fp32 partials in rank order (the same order on
-// every call), rounds once and writes them to y. Decode batches (up to 32 rows): every
+// every call), rounds once and writes them to y. Decode batches (up to 64 rows): every
 // CTA stores its partial of each owner's rows straight into that owner's shared memory
 // (st.async, 4 bytes per store, each counted on the owner's mbarrier), and the owner
 // waits for its mbarrier alone -- one cluster arrive at the start, no cluster barrier
@@ -94,8 +94,10 @@ constexpr int kMaxTiles = 1 << 16;      // out_features <= 8,388,608
 // partial rows straight into the shared memory of the CTA that owns them (st.async,
 // completing on the owner's mbarrier), instead of staging them and pulling them through
 // distributed shared memory between two cluster barriers. The receive buffer,
-// s * Mp * (largest row share) floats <= 168 * Mp * 4 bytes, comes out of the ring.
-constexpr int kPushMaxMp = 32;
+// s * Mp * (largest row share) floats <= 168 * Mp * 4 bytes, comes out of the ring; the
+// push is used where it leaves at least kMinStages stages (at 64 rows: every s but 7).
+// Measured on the 8B shapes: 0.7-1.2 us faster per call at 1-16 rows, 2.5-4 us at 64.
+constexpr int kPushMaxMp = 64;
 
 struct LinParams {
   void* y;
@@ -103,7 +105,7 @@ struct LinParams {
   int M, N, Mp, kc, splits, stages, tmem_cols;
   int do_push;      // also push y's rows to the peers (push)
   int y_vec;        // y's rows start on 16-byte boundaries (base and stride)
-  int push_sum;     // split-K partials pushed to their owners (splits > 1, Mp <= 32)
+  int push_sum;     // split-K partials pushed to their owners (splits > 1, Mp <= 64)
   TpPush push;
   uint32_t* status;
 };
@@ -543,7 +545,11 @@ Plan plan_for(int M, int N, int K) {
   if (forced > 0) s = forced <= pl.kc ? forced : pl.kc;
   pl.splits = s;
   pl.grid = pl.n_tiles * s;
-  pl.push_sum = (s > 1 && pl.Mp <= kPushMaxMp && env_int("NSLG_LINEAR_PUSH_SUM", 1, 0, 1)) ? 1 : 0;
+  pl.push_sum = (s > 1 && pl.Mp <= kPushMaxMp && env_int("NSLG_LINEAR_PUSH_SUM", 1, 0, 1) &&
+                 recv_bytes_for(s, pl.Mp) + kMinStages * (kWBytes + pl.Mp * 128) <=
+                     kLinearSmemBudget)
+                    ? 1
+                    : 0;
   pl.recv_bytes = pl.push_sum ? recv_bytes_for(s, pl.Mp) : 0;
   pl.stages = stages_for(pl.Mp, pl.recv_bytes);
   int cols = 32;
