@@ -86,6 +86,25 @@ def test_linear_output_rows_unaligned_or_ragged(m, n, k, pad):
     assert torch.equal(y, ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS))
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("splits", [2, 3, 5, 6, 7, 8])
+@pytest.mark.parametrize("m", [1, 17, 64, 100])
+def test_linear_pushed_and_pulled_split_sums_agree(dt, splits, m, monkeypatch):
+    """The two ways of summing a tile's K splits inside its cluster -- partials pushed
+    into the owning CTA's shared memory (st.async on its mbarrier; up to 64 rows where
+    the receive buffer fits) and partials staged and pulled through distributed shared
+    memory between cluster barriers (NSLG_LINEAR_PUSH_SUM=0, and past 64 rows) -- add
+    the same fp32 values in the same order: bit-identical outputs, at every split count
+    (uneven row shares at 3, 5, 6, 7) and a ragged last tile."""
+    x, w = _problem(m, 1000, 1024, dt, seed=splits * 100 + m)
+    monkeypatch.setenv("NSLG_LINEAR_SPLITS", str(splits))
+    pushed = ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS)
+    monkeypatch.setenv("NSLG_LINEAR_PUSH_SUM", "0")
+    pulled = ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS)
+    assert torch.equal(pushed, pulled)
+    torch.testing.assert_close(pushed, _ref(x, w), **TOL[dt])
+
+
 def test_linear_graph_replay():
     dt = torch.bfloat16
     x, w = _problem(64, 4096, 4096, dt, seed=11)
