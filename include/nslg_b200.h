@@ -233,6 +233,21 @@ int nslg_linear(int dtype, int rows, int out_features, int in_features, const vo
                 int64_t x_stride, const void* weight, int64_t w_stride, void* y,
                 int64_t y_stride, uint32_t* dev_status, void* stream);
 
+/* The MLP's gate|up product and its SwiGLU in one kernel (nslg_linear's tcgen05 path):
+ *   out[rows, inter] = silu(x . gate^T) * (x . up^T)
+ * with gate_up = [gate; up], 2 * inter rows of w_stride elements (gate rows first),
+ * rounded as the reference does (models.py:156-157: each product rounded to the
+ * activation type, silu rounded, the product rounded) -- the same values as
+ * nslg_linear followed by nslg_silu_mul, without the [rows, 2 * inter] intermediate or
+ * the second kernel. Replaces F.silu(gate_proj(x)) * up_proj(x) (models.py:156-157,
+ * gate_proj / up_proj being ColumnParallelLinear, tp_layers.py:28-91) for decode
+ * batches. Same operand rules as nslg_linear; returns NSLG_ERR_UNSUPPORTED where the
+ * shape's split of the in_features sum would not fit the kernel's on-chip reduction
+ * (then call the two kernels). */
+int nslg_linear_swiglu(int dtype, int rows, int inter, int in_features, const void* x,
+                       int64_t x_stride, const void* gate_up, int64_t w_stride, void* out,
+                       int64_t out_stride, uint32_t* dev_status, void* stream);
+
 /* Greedy sampling: for each of `rows` rows of logits x (cols entries, row stride
  * x_stride elements), the maximum (out_val[r], fp32; out_val may be NULL) and the index
  * of its first occurrence plus index_offset (out_idx[r]), ordered as torch.argmax: NaN

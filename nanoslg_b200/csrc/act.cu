@@ -20,11 +20,6 @@ union AVec {
 };
 
 template <typename T>
-constexpr bool kFastSilu = false;
-template <>
-constexpr bool kFastSilu<__nv_bfloat16> = true;
-
-template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* gu, int64_t gu_stride, T* out,
                                                        int64_t out_stride, int rows, int inter) {
   pdl_wait();
@@ -40,15 +35,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* gu, int64_t gu_s
     g.u = *reinterpret_cast<const uint4*>(gu + r * gu_stride + c);
     u.u = *reinterpret_cast<const uint4*>(gu + r * gu_stride + inter + c);
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      const float x = Elem<T>::to_f(g.e[j]);
-      // bf16 rounds silu to 8 bits, so the hardware exponential and the approximate
-      // division are enough there (and keep the kernel memory-bound); fp32 and fp16
-      // (11 bits) keep the correctly rounded division and the full-precision exponential
-      const float s = kFastSilu<T> ? Elem<T>::round(__fdividef(x, 1.f + __expf(-x)))
-                                   : Elem<T>::round(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
-      y.e[j] = Elem<T>::from_f(__fmul_rn(s, Elem<T>::to_f(u.e[j])));
-    }
+    for (int j = 0; j < VEC; ++j) y.e[j] = swiglu<T>(g.e[j], u.e[j]);
     *reinterpret_cast<uint4*>(out + r * out_stride + c) = y.u;
   }
 }

@@ -260,6 +260,30 @@ int nslg_linear(int dtype, int rows, int out_features, int in_features, const vo
                           y, y_stride, nullptr, dev_status, static_cast<cudaStream_t>(stream));
 }
 
+int nslg_linear_swiglu(int dtype, int rows, int inter, int in_features, const void* x,
+                       int64_t x_stride, const void* gate_up, int64_t w_stride, void* out,
+                       int64_t out_stride, uint32_t* dev_status, void* stream) {
+  g_last_error.clear();
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16)
+    return set_error(NSLG_ERR_ARG, "linear_swiglu: dtype must be bfloat16 or float16");
+  if (rows < 0 || inter <= 0 || in_features <= 0)
+    return set_error(NSLG_ERR_ARG, "linear_swiglu: bad shape");
+  if (rows == 0) return NSLG_OK;
+  if (!linear_tc_supported(dtype, rows, inter, in_features) || inter > (1 << 22))
+    return set_error(NSLG_ERR_UNSUPPORTED, "linear_swiglu: needs 1 <= rows <= " +
+                                               std::to_string(kLinearMaxRows) +
+                                               ", inter <= 4194304 and in_features a multiple of 64");
+  if (!x || !gate_up || !out) return set_error(NSLG_ERR_ARG, "linear_swiglu: null pointer");
+  if (!aligned16(x) || !aligned16(gate_up) || (x_stride * 2) % 16 || (w_stride * 2) % 16 ||
+      x_stride < in_features || w_stride < in_features || out_stride < inter ||
+      (reinterpret_cast<uintptr_t>(out) & 1u))
+    return set_error(NSLG_ERR_ARG, "linear_swiglu: x and weight rows must be 16-byte aligned "
+                                   "and strides cover the rows");
+  return launch_linear_tc(dtype, rows, inter, in_features, x, x_stride, gate_up, w_stride, out,
+                          out_stride, nullptr, dev_status, static_cast<cudaStream_t>(stream),
+                          true);
+}
+
 int nslg_linear_tp_push(int dtype, int rows, int out_features, int in_features, const void* x,
                         int64_t x_stride, const void* weight, int64_t w_stride, void* y,
                         int64_t y_stride, int world, int rank, void* const* stage_bufs,

@@ -45,6 +45,28 @@ struct Elem<__half> {
   }
 };
 
+// ---------------------------------------------------------------- SwiGLU
+// silu(g) * u of one gate / up pair of the activation type, with the reference's rounding
+// points (models.py:156-157: F.silu on the rounded gate, rounded, times the rounded up,
+// rounded). bf16 rounds silu to 8 bits, so the hardware exponential and the approximate
+// division are enough there; fp32 and fp16 (11 bits) keep the correctly rounded division
+// and the full-precision exponential.
+template <typename T>
+struct FastSilu {
+  static constexpr bool value = false;
+};
+template <>
+struct FastSilu<__nv_bfloat16> {
+  static constexpr bool value = true;
+};
+template <typename T>
+__device__ __forceinline__ T swiglu(T g, T u) {
+  const float x = Elem<T>::to_f(g);
+  const float s = FastSilu<T>::value ? Elem<T>::round(__fdividef(x, 1.f + __expf(-x)))
+                                     : Elem<T>::round(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
+  return Elem<T>::from_f(__fmul_rn(s, Elem<T>::to_f(u)));
+}
+
 // ---------------------------------------------------------------- shared memory
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -139,8 +139,12 @@ inline void tp_stage_geometry(int64_t stage_bytes, int world, int64_t* region, i
 
 // push == nullptr: y only. Otherwise also every row of y, packed with this rank's call
 // numbers, into every peer's stage buffer (out_features is then the reduced row length).
+// swiglu: w is a stacked [2N, K] gate|up weight and y[m][c] = silu(x.gate_c) * (x.up_c)
+// with the reference's rounding points (no push; NSLG_ERR_UNSUPPORTED where the split-K
+// sum of the shape would not be pushed).
 int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_stride,
                      const void* w, int64_t w_stride, void* y, int64_t y_stride,
-                     const TpPush* push, uint32_t* status, cudaStream_t stream);
+                     const TpPush* push, uint32_t* status, cudaStream_t stream,
+                     bool swiglu = false);
 
 }  // namespace nslg

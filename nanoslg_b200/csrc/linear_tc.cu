@@ -106,6 +106,8 @@ struct LinParams {
   int do_push;      // also push y's rows to the peers (push)
   int y_vec;        // y's rows start on 16-byte boundaries (base and stride)
   int push_sum;     // split-K partials pushed to their owners (splits > 1, Mp <= 64)
+  int swiglu;       // tile t = gate rows [64t, 64t + 64) and up rows [I + 64t, ...) of a
+                    // stacked gate|up weight; y[m][c] = silu(gate) * up, N = I
   TpPush push;
   uint32_t* status;
 };
@@ -143,11 +145,27 @@ __device__ __forceinline__ void store_y4(const LinParams& p, int m, int n0, cons
 // (whole 16-byte vectors of a y row for the push), every CTA at least 16 rows.
 __device__ __forceinline__ int split_row_lo(int j, int s) { return 8 * ((16 * j) / s); }
 
+// SwiGLU mode: CTA j of s owns the output columns [half_lo(j), half_lo(j + 1)) of its
+// tile's 64, i.e. gate rows [lo, hi) and up rows [64 + lo, 64 + hi) of the tile.
+__device__ __forceinline__ int half_lo(int j, int s) { return 8 * ((8 * j) / s); }
+
+// Rows of the tile (of D, 128) that CTA j sums, and the position of row r among them.
+__device__ __forceinline__ int owned_rows(const LinParams& p, int j) {
+  return p.swiglu ? 2 * (half_lo(j + 1, p.splits) - half_lo(j, p.splits))
+                  : split_row_lo(j + 1, p.splits) - split_row_lo(j, p.splits);
+}
+
 // The CTA of the cluster whose share of the tile's rows holds row r.
 __device__ __forceinline__ int split_owner(int r, int s) {
   int o = 0;
   for (int j = 1; j < s; ++j)
     if (split_row_lo(j, s) <= r) o = j;
+  return o;
+}
+__device__ __forceinline__ int half_owner(int c, int s) {
+  int o = 0;
+  for (int j = 1; j < s; ++j)
+    if (half_lo(j, s) <= c) o = j;
   return o;
 }
 
@@ -236,6 +254,7 @@ __device__ void push_rows(const LinParams& p, int t, int r_lo, int r_hi) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                     const __grid_constant__ CUtensorMap tmap_w2,
                      const __grid_constant__ CUtensorMap tmap_x, const LinParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -268,9 +287,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     *abort_flag = 0;
     fence_barrier_init();
     if (p.push_sum)   // every CTA of the cluster sends its partial of this CTA's rows
-      mbar_arrive_expect_tx(recv_full, static_cast<uint32_t>(p.splits * p.M * 4 *
-                                                             (split_row_lo(j + 1, p.splits) -
-                                                              split_row_lo(j, p.splits))));
+      mbar_arrive_expect_tx(recv_full,
+                            static_cast<uint32_t>(p.splits * p.M * 4 * owned_rows(p, j)));
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -292,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // -------------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&tmap_w);
+      if (p.swiglu) prefetch_tmap(&tmap_w2);
       prefetch_tmap(&tmap_x);
       const uint64_t stream_w = l2_policy_evict_first();   // every weight byte used once
       const uint64_t keep_x = l2_policy_evict_last();      // x is re-read by every CTA
@@ -299,8 +318,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int pre = n < p.stages ? n : p.stages;
       for (int i = 0; i < pre; ++i) {                 // first use of stages 0 .. pre-1
         mbar_arrive_expect_tx(&full[i], sbytes);
-        tma_load_3d(smem + i * sbytes, &tmap_w, &full[i], (k_lo + i) * kChunk, t * kTileN, 0,
-                    stream_w);
+        if (p.swiglu) {   // gate rows into the A tile's first 64 rows, up rows below
+          tma_load_3d(smem + i * sbytes, &tmap_w, &full[i], (k_lo + i) * kChunk, t * 64, 0,
+                      stream_w);
+          tma_load_3d(smem + i * sbytes + kWBytes / 2, &tmap_w2, &full[i], (k_lo + i) * kChunk,
+                      t * 64, 0, stream_w);
+        } else {
+          tma_load_3d(smem + i * sbytes, &tmap_w, &full[i], (k_lo + i) * kChunk, t * kTileN, 0,
+                      stream_w);
+        }
       }
       pdl_wait();      // x is the previous kernel's output
       for (int i = 0; i < pre; ++i)
@@ -314,7 +340,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
         uint8_t* sb = smem + stage * sbytes;
         mbar_arrive_expect_tx(&full[stage], sbytes);
-        tma_load_3d(sb, &tmap_w, &full[stage], k * kChunk, t * kTileN, 0, stream_w);
+        if (p.swiglu) {
+          tma_load_3d(sb, &tmap_w, &full[stage], k * kChunk, t * 64, 0, stream_w);
+          tma_load_3d(sb + kWBytes / 2, &tmap_w2, &full[stage], k * kChunk, t * 64, 0, stream_w);
+        } else {
+          tma_load_3d(sb, &tmap_w, &full[stage], k * kChunk, t * kTileN, 0, stream_w);
+        }
         tma_load_3d(sb + kWBytes, &tmap_x, &full[stage], k * kChunk, 0, 0, keep_x);
         ++issued;
         if (++stage == p.stages) { stage = 0; phase ^= 1; }
@@ -363,12 +394,22 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (p.push_sum) cluster_wait_acquire();
     const int r = (warp & 3) * 32 + lane;          // TMEM lane = row of the tile
     // push_sum: the owner of row r, and where this CTA's values of row r go there
-    const int own = p.push_sum ? split_owner(r, p.splits) : 0;
-    const int own_lo = split_row_lo(own, p.splits);
-    const int own_rows = split_row_lo(own + 1, p.splits) - own_lo;
+    // (SwiGLU: the owner of output column r % 64 takes gate row r and up row r + 64;
+    // its rows are [its gate rows, its up rows])
+    const int own = !p.push_sum ? 0
+                    : p.swiglu  ? half_owner(r & 63, p.splits)
+                                : split_owner(r, p.splits);
+    const int own_rows = owned_rows(p, own);
+    int own_pos;
+    if (p.swiglu) {
+      const int lo = half_lo(own, p.splits);
+      own_pos = (r < 64 ? 0 : own_rows / 2) + (r & 63) - lo;
+    } else {
+      own_pos = r - split_row_lo(own, p.splits);
+    }
     const uint32_t dst0 =
         p.push_sum ? cluster_addr(smem_u32(recv) + 4u * static_cast<uint32_t>(
-                                                           j * p.M * own_rows + (r - own_lo)),
+                                                           j * p.M * own_rows + own_pos),
                                   own)
                    : 0u;
     const uint32_t dst_bar = p.push_sum ? cluster_addr(smem_u32(recv_full), own) : 0u;
@@ -409,7 +450,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (p.splits == 1) {
     // the staged tile to y, 8 consecutive outputs (16 bytes) of one row per store
-    if (!*abort_flag) {
+    if (!*abort_flag && p.swiglu) {
+      // y[m][64t + c] = silu(gate) * up from rows c and 64 + c of the staged tile
+      const T* tile_y = reinterpret_cast<const T*>(smem);
+      for (int u = threadIdx.x; u < p.M * 8; u += kThreads) {
+        const int m = u / 8, c = 8 * (u % 8);
+        const uint4 g = *reinterpret_cast<const uint4*>(tile_y + m * kTileN + c);
+        const uint4 up = *reinterpret_cast<const uint4*>(tile_y + m * kTileN + 64 + c);
+        uint4 o;
+        const T* ge = reinterpret_cast<const T*>(&g);
+        const T* ue = reinterpret_cast<const T*>(&up);
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) oe[i] = swiglu<T>(ge[i], ue[i]);
+        store_y8<T>(p, m, t * 64 + c, o);
+      }
+    } else if (!*abort_flag) {
       const T* tile_y = reinterpret_cast<const T*>(smem);
       for (int u = threadIdx.x; u < p.M * (kTileN / 8); u += kThreads) {
         const int m = u / (kTileN / 8), c = 8 * (u % (kTileN / 8));
@@ -422,6 +478,30 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool landed = mbar_wait_cluster(recv_full, 0);
     if (!landed) {
       if (threadIdx.x == 0) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
+    } else if (!*abort_flag && p.swiglu) {
+      // gate and up sums of this CTA's columns [lo, hi) of the tile, rounded, activated
+      const int lo = half_lo(j, p.splits);
+      const int h = half_lo(j + 1, p.splits) - lo;
+      const int quads = h / 4;
+      for (int e = threadIdx.x; e < p.M * quads; e += kThreads) {
+        const int m = e / quads, q4 = 4 * (e % quads);
+        float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplits; ++sp) {
+          const float* row = recv + (sp * p.M + m) * 2 * h;
+          const float4 a = sp < p.splits ? *reinterpret_cast<const float4*>(row + q4)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 b = sp < p.splits ? *reinterpret_cast<const float4*>(row + h + q4)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+          g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
+          u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
+        }
+        float o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o[i] = Elem<T>::to_f(swiglu<T>(Elem<T>::from_f(g[i]), Elem<T>::from_f(u[i])));
+        store_y4<T>(p, m, t * 64 + lo + q4, o);
+      }
     } else if (!*abort_flag) {
       const int r_lo = split_row_lo(j, p.splits);
       const int rows_s = split_row_lo(j + 1, p.splits) - r_lo;
@@ -513,11 +593,13 @@ int stages_for(int Mp, int recv_bytes) {
   return st < kMinStages ? kMinStages : (st > kMaxStages ? kMaxStages : st);
 }
 
-// Receive buffer of a pushed split-K sum: s partials of the largest row share.
-int recv_bytes_for(int splits, int Mp) {
+// Receive buffer of a pushed split-K sum: s partials of the largest row share (SwiGLU
+// mode: twice the largest share of the tile's 64 output columns).
+int recv_bytes_for(int splits, int Mp, bool swiglu) {
   int rows = 0;
   for (int j = 0; j < splits; ++j) {
-    const int r = 8 * ((16 * (j + 1)) / splits) - 8 * ((16 * j) / splits);
+    const int r = swiglu ? 2 * (8 * ((8 * (j + 1)) / splits) - 8 * ((8 * j) / splits))
+                         : 8 * ((16 * (j + 1)) / splits) - 8 * ((16 * j) / splits);
     rows = r > rows ? r : rows;
   }
   return splits * Mp * rows * 4;
@@ -528,10 +610,11 @@ int recv_bytes_for(int splits, int Mp) {
 // more than one CTA per SM the cluster size is rounded down to a power of two, so that
 // the clusters pack into the GPCs' CTA slots in one wave (measured on the 8B q|k|v
 // product at one row: 48 clusters of 6, 288 CTAs, 15.7 us; of 3, 144 CTAs, 12.3 us).
-Plan plan_for(int M, int N, int K) {
+Plan plan_for(int M, int N, int K, bool swiglu) {
   Plan pl{};
   pl.Mp = (M + 15) / 16 * 16;
-  pl.n_tiles = (N + kTileN - 1) / kTileN;
+  // a tile is 128 weight rows: 128 outputs, or 64 gate|up pairs (SwiGLU)
+  pl.n_tiles = swiglu ? (N + 63) / 64 : (N + kTileN - 1) / kTileN;
   pl.kc = K / kChunk;
   const int cps = env_int("NSLG_LINEAR_CTAS_PER_SM", kCtasPerSm, 1, 2);
   int s = sm_count() * cps / pl.n_tiles;
@@ -546,11 +629,11 @@ Plan plan_for(int M, int N, int K) {
   pl.splits = s;
   pl.grid = pl.n_tiles * s;
   pl.push_sum = (s > 1 && pl.Mp <= kPushMaxMp && env_int("NSLG_LINEAR_PUSH_SUM", 1, 0, 1) &&
-                 recv_bytes_for(s, pl.Mp) + kMinStages * (kWBytes + pl.Mp * 128) <=
+                 recv_bytes_for(s, pl.Mp, swiglu) + kMinStages * (kWBytes + pl.Mp * 128) <=
                      kLinearSmemBudget)
                     ? 1
                     : 0;
-  pl.recv_bytes = pl.push_sum ? recv_bytes_for(s, pl.Mp) : 0;
+  pl.recv_bytes = pl.push_sum ? recv_bytes_for(s, pl.Mp, swiglu) : 0;
   pl.stages = stages_for(pl.Mp, pl.recv_bytes);
   int cols = 32;
   while (cols < pl.Mp) cols *= 2;
@@ -567,12 +650,27 @@ bool linear_tc_supported(int dtype, int M, int N, int K) {
 
 int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_stride,
                      const void* w, int64_t w_stride, void* y, int64_t y_stride,
-                     const TpPush* push, uint32_t* status, cudaStream_t stream) {
-  const Plan pl = plan_for(M, N, K);
-  CUtensorMap tw, tx;
-  // W [N, K] and x [M, K], K innermost; boxes [64 x 128] and [64 x Mp] with 128-byte swizzle
-  int rc = encode_tiled_3d_bf16(&tw, w, K, N, 1, static_cast<uint64_t>(w_stride) * 2,
-                                static_cast<uint64_t>(w_stride) * 2 * N, kChunk, kTileN, 1);
+                     const TpPush* push, uint32_t* status, cudaStream_t stream, bool swiglu) {
+  const Plan pl = plan_for(M, N, K, swiglu);
+  if (swiglu && (push != nullptr || (pl.splits > 1 && !pl.push_sum)))
+    return set_error(NSLG_ERR_UNSUPPORTED,
+                     "linear_swiglu: the split-K sum of this shape does not fit the push");
+  CUtensorMap tw, tw2, tx;
+  // W [N, K] and x [M, K], K innermost; boxes [64 x 128] and [64 x Mp] with 128-byte
+  // swizzle. SwiGLU: W is [2N, K] (gate rows, then up rows), one map per half, each with
+  // N rows (so a ragged last tile reads zeros, not the other half) and [64 x 64] boxes.
+  int rc;
+  if (swiglu) {
+    const uint64_t sb = static_cast<uint64_t>(w_stride) * 2;
+    rc = encode_tiled_3d_bf16(&tw, w, K, N, 1, sb, sb * N, kChunk, 64, 1);
+    if (rc != NSLG_OK) return rc;
+    rc = encode_tiled_3d_bf16(&tw2, static_cast<const uint8_t*>(w) + sb * N, K, N, 1, sb, sb * N,
+                              kChunk, 64, 1);
+  } else {
+    rc = encode_tiled_3d_bf16(&tw, w, K, N, 1, static_cast<uint64_t>(w_stride) * 2,
+                              static_cast<uint64_t>(w_stride) * 2 * N, kChunk, kTileN, 1);
+    tw2 = tw;
+  }
   if (rc != NSLG_OK) return rc;
   rc = encode_tiled_3d_bf16(&tx, x, K, M, 1, static_cast<uint64_t>(x_stride) * 2,
                             static_cast<uint64_t>(x_stride) * 2 * M, kChunk, pl.Mp, 1);
@@ -590,6 +688,7 @@ int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_st
   p.do_push = push != nullptr ? 1 : 0;
   p.y_vec = (reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_stride % 8 == 0) ? 1 : 0;
   p.push_sum = pl.push_sum;
+  p.swiglu = swiglu ? 1 : 0;
   if (push != nullptr) p.push = *push;
   p.status = status;
   const size_t smem = smem_bytes(pl.stages, pl.Mp, pl.recv_bytes);
@@ -612,7 +711,7 @@ int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_st
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  err = cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
+  err = cudaLaunchKernelEx(&cfg, kern, tw, tw2, tx, p);
   if (err != cudaSuccess) return set_error(NSLG_ERR_CUDA, std::string("linear_tc: ") + cudaGetErrorString(err));
   return check_launch("linear_tc");
 }

@@ -154,13 +154,15 @@ class TPMLP(nn.Module):
         self._gu = None
 
     def fuse_projections(self):
-        """Stacks gate and up weights (views, as in TPAttention.fuse_projections): one GEMM
-        and one silu*mul kernel instead of two GEMMs and two elementwise kernels."""
+        """Stacks gate and up weights (views, as in TPAttention.fuse_projections): for
+        decode batches one kernel (the gate|up product with SwiGLU in its epilogue), for
+        larger ones one GEMM and one silu*mul kernel, instead of two GEMMs and two
+        elementwise kernels."""
         self._gu = _stack_as_views([self.gate_proj, self.up_proj])
 
     def forward(self, x):
         if _views_intact(self._gu, [self.gate_proj, self.up_proj]):
-            return self.down_proj(ops.silu_mul(ops.linear(x, self._gu)))
+            return self.down_proj(ops.linear_swiglu(x, self._gu))
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 

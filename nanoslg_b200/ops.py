@@ -309,6 +309,36 @@ def linear(x, weight, bias=None, out=None, max_rows=LINEAR_AUTO_ROWS):
     return out
 
 
+def linear_swiglu(x, gate_up, max_rows=LINEAR_AUTO_ROWS):
+    """silu(x . gate^T) * (x . up^T) for a stacked [gate; up] weight ([2 I, in]): the
+    tcgen05 linear kernel with the activation in its epilogue (nslg_linear_swiglu) where
+    ``linear_supported(x, gate_up)`` holds; ``silu_mul(linear(x, gate_up))`` otherwise,
+    and where the kernel reports that the shape's split-K sum would not be pushed. Both
+    give the same values: each product rounded to the activation type, silu rounded, the
+    product rounded."""
+    two_i = gate_up.shape[0]
+    if two_i % 2 or not linear_supported(x, gate_up, None, max_rows):
+        return silu_mul(linear(x, gate_up, max_rows=max_rows))
+    k, inter = x.shape[-1], two_i // 2
+    try:
+        rows, xs = _rows(x.unsqueeze(-2), "x")
+    except ValueError:
+        return silu_mul(linear(x, gate_up, max_rows=max_rows))
+    if xs % 8 or x.data_ptr() % 16:
+        return silu_mul(linear(x, gate_up, max_rows=max_rows))
+    out = torch.empty(x.shape[:-1] + (inter,), dtype=x.dtype, device=x.device)
+    lib = N.lib()
+    rc = lib.nslg_linear_swiglu(_dtype_code(x), rows, inter, k, _ptr(x), xs, _ptr(gate_up),
+                                gate_up.stride(0), _ptr(out), inter,
+                                _ptr(status_word(x.device)), _stream(x))
+    if rc == N.ERR_UNSUPPORTED:
+        return silu_mul(linear(x, gate_up, max_rows=max_rows), out=out)
+    if rc != N.OK:
+        raise N.NativeError("nslg_linear_swiglu", rc,
+                            lib.nslg_last_error().decode(errors="replace"))
+    return out
+
+
 def argmax_rows(x, index_offset=0, values=False):
     """Per row of ``x`` [rows, cols] (last dim contiguous): the index of the first
     maximum plus ``index_offset`` (int64 [rows]), ordered as torch.argmax (NaN above

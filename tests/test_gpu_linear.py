@@ -105,6 +105,42 @@ def test_linear_pushed_and_pulled_split_sums_agree(dt, splits, m, monkeypatch):
     torch.testing.assert_close(pushed, _ref(x, w), **TOL[dt])
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,inter,k", [
+    (1, 14336, 4096),      # TP=1: whole tiles
+    (16, 7168, 4096),      # TP=2: 2-way K split
+    (5, 3584, 4096),       # TP=4
+    (64, 1792, 4096),      # TP=8: 8-way split, 64 rows
+    (3, 1000, 512),        # ragged: the last tile has 40 gate|up pairs
+    (100, 512, 1024),      # past 64 rows with a K split: the kernel declines, two kernels run
+])
+def test_linear_swiglu_matches_linear_then_silu_mul(dt, m, inter, k):
+    """The gate|up product with SwiGLU in the kernel's epilogue gives exactly the values of
+    the product (rounded) followed by the silu*mul kernel, and is within one rounding of
+    the torch fp32 reference of silu(x.gate) * (x.up)."""
+    x, w = _problem(m, 2 * inter, k, dt, seed=m + inter + k)
+    fused = ops.linear_swiglu(x, w, max_rows=ops.LINEAR_MAX_ROWS)
+    two = ops.silu_mul(ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS))
+    assert fused.shape == (m, inter)
+    assert torch.equal(fused, two)
+    g = (x.float() @ w[:inter].float().t()).to(dt).float()
+    u = (x.float() @ w[inter:].float().t()).to(dt).float()
+    ref = (torch.nn.functional.silu(g).to(dt).float() * u).to(dt)
+    torch.testing.assert_close(fused, ref, **TOL[dt])
+
+
+@pytest.mark.parametrize("splits", [3, 5, 6, 7])
+@pytest.mark.parametrize("m", [1, 64])
+def test_linear_swiglu_uneven_split_shares(splits, m, monkeypatch):
+    """Forced K splits whose shares of a tile's 64 gate|up pairs are uneven: each owner
+    sums its gate rows and the matching up rows; equal to the two-kernel path (which
+    splits the same way), or the two-kernel path itself where the push does not fit."""
+    monkeypatch.setenv("NSLG_LINEAR_SPLITS", str(splits))
+    x, w = _problem(m, 2 * 1000, 1024, torch.bfloat16, seed=splits + m)
+    fused = ops.linear_swiglu(x, w, max_rows=ops.LINEAR_MAX_ROWS)
+    assert torch.equal(fused, ops.silu_mul(ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS)))
+
+
 def test_linear_graph_replay():
     dt = torch.bfloat16
     x, w = _problem(64, 4096, 4096, dt, seed=11)
