@@ -248,6 +248,27 @@ int nslg_linear_swiglu(int dtype, int rows, int inter, int in_features, const vo
                        int64_t x_stride, const void* gate_up, int64_t w_stride, void* out,
                        int64_t out_stride, uint32_t* dev_status, void* stream);
 
+/* The attention's q|k|v product followed by nslg_rope_kv_append, in one kernel
+ * (nslg_linear's tcgen05 path; head_dim 128, where one 128-row tile of the stacked
+ * weight is one head): w_qkv = [q; k; v] weight, (num_qo_heads + 2 * num_kv_heads) * 128
+ * rows of w_stride elements; the products are rounded to the activation type and then
+ * rotated (q into q_out, contiguous [rows, num_qo_heads, 128]; k into the pool slot
+ * write_loc[m]) or copied (v into the pool slot), exactly as nslg_rope_kv_append does
+ * with the same positions, tables, write_loc and pool arguments (their meaning and
+ * device-status reports are that function's). Replaces the q/k/v projections
+ * (models.py:136-138, ColumnParallelLinear, tp_layers.py:28-91) and the RoPE + KV write
+ * that follow them (models.py:99-103, kv_cache.py:661-674) for decode batches. Returns
+ * NSLG_ERR_UNSUPPORTED for another head_dim, or where the shape's split of the
+ * in_features sum would not fit the kernel's on-chip reduction (then call nslg_linear
+ * and nslg_rope_kv_append). */
+int nslg_linear_rope_append(int dtype, int rows, int num_qo_heads, int num_kv_heads,
+                            int head_dim, int in_features, const void* x, int64_t x_stride,
+                            const void* w_qkv, int64_t w_stride, void* q_out,
+                            const int32_t* positions, const float* cos_table,
+                            const float* sin_table, int64_t table_rows,
+                            const int32_t* write_loc, void* pool_k, void* pool_v,
+                            int64_t pool_slots, uint32_t* dev_status, void* stream);
+
 /* Greedy sampling: for each of `rows` rows of logits x (cols entries, row stride
  * x_stride elements), the maximum (out_val[r], fp32; out_val may be NULL) and the index
  * of its first occurrence plus index_offset (out_idx[r]), ordered as torch.argmax: NaN

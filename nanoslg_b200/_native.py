@@ -46,6 +46,8 @@ SIGNATURES = {
     "nslg_linear": (_i32, [_i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp]),
     "nslg_linear_swiglu": (_i32, [_i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp,
                                   _vp]),
+    "nslg_linear_rope_append": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64,
+                                       _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
     "nslg_rmsnorm_residual": (_i32, [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i64,
                                      _f32, _vp]),
     "nslg_plan_decode": (_i32, [_i32, _i32, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _vp, _vp, _vp,

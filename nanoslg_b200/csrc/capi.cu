@@ -284,6 +284,48 @@ int nslg_linear_swiglu(int dtype, int rows, int inter, int in_features, const vo
                           true);
 }
 
+int nslg_linear_rope_append(int dtype, int rows, int num_qo_heads, int num_kv_heads,
+                            int head_dim, int in_features, const void* x, int64_t x_stride,
+                            const void* w_qkv, int64_t w_stride, void* q_out,
+                            const int32_t* positions, const float* cos_table,
+                            const float* sin_table, int64_t table_rows,
+                            const int32_t* write_loc, void* pool_k, void* pool_v,
+                            int64_t pool_slots, uint32_t* dev_status, void* stream) {
+  g_last_error.clear();
+  if (dtype != NSLG_DTYPE_BF16 && dtype != NSLG_DTYPE_F16)
+    return set_error(NSLG_ERR_ARG, "linear_rope_append: dtype must be bfloat16 or float16");
+  if (rows < 0 || num_qo_heads <= 0 || num_kv_heads <= 0 || in_features <= 0 ||
+      num_qo_heads > 4096 || num_kv_heads > 4096)
+    return set_error(NSLG_ERR_ARG, "linear_rope_append: bad shape");
+  if (rows == 0) return NSLG_OK;
+  const int n = (num_qo_heads + 2 * num_kv_heads) * 128;
+  if (head_dim != 128 || !linear_tc_supported(dtype, rows, n, in_features))
+    return set_error(NSLG_ERR_UNSUPPORTED, "linear_rope_append: needs head_dim 128, 1 <= rows <= " +
+                                               std::to_string(kLinearMaxRows) +
+                                               " and in_features a multiple of 64");
+  if (!x || !w_qkv || !q_out || !pool_k || !pool_v || (positions && (!cos_table || !sin_table)))
+    return set_error(NSLG_ERR_ARG, "linear_rope_append: null pointer");
+  if (!aligned16(x) || !aligned16(w_qkv) || !aligned16(q_out) || !aligned16(pool_k) ||
+      !aligned16(pool_v) || (x_stride * 2) % 16 || (w_stride * 2) % 16 ||
+      x_stride < in_features || w_stride < in_features)
+    return set_error(NSLG_ERR_ARG, "linear_rope_append: x, weight, q_out and pool rows must be "
+                                   "16-byte aligned and strides cover the rows");
+  LinearRope r{};
+  r.hq = num_qo_heads;
+  r.hkv = num_kv_heads;
+  r.q_out = q_out;
+  r.positions = positions;
+  r.cos_t = cos_table;
+  r.sin_t = sin_table;
+  r.table_rows = table_rows;
+  r.write_loc = write_loc;
+  r.pool_k = pool_k;
+  r.pool_v = pool_v;
+  r.pool_slots = pool_slots;
+  return launch_linear_tc(dtype, rows, n, in_features, x, x_stride, w_qkv, w_stride, nullptr, n,
+                          nullptr, dev_status, static_cast<cudaStream_t>(stream), false, &r);
+}
+
 int nslg_linear_tp_push(int dtype, int rows, int out_features, int in_features, const void* x,
                         int64_t x_stride, const void* weight, int64_t w_stride, void* y,
                         int64_t y_stride, int world, int rank, void* const* stage_bufs,

@@ -142,9 +142,24 @@ inline void tp_stage_geometry(int64_t stage_bytes, int world, int64_t* region, i
 // swiglu: w is a stacked [2N, K] gate|up weight and y[m][c] = silu(x.gate_c) * (x.up_c)
 // with the reference's rounding points (no push; NSLG_ERR_UNSUPPORTED where the split-K
 // sum of the shape would not be pushed).
+// rope: N = (hq + 2 hkv) * 128 rows of a stacked q|k|v weight, y unused; the epilogue
+// rotates q into q_out and appends rotated k and v to the pool (nslg_rope_kv_append's
+// operation), NSLG_ERR_UNSUPPORTED like swiglu.
+struct LinearRope {
+  int hq, hkv;
+  void* q_out;
+  const int32_t* positions;
+  const float* cos_t;
+  const float* sin_t;
+  int64_t table_rows;
+  const int32_t* write_loc;
+  void* pool_k;
+  void* pool_v;
+  int64_t pool_slots;
+};
 int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_stride,
                      const void* w, int64_t w_stride, void* y, int64_t y_stride,
                      const TpPush* push, uint32_t* status, cudaStream_t stream,
-                     bool swiglu = false);
+                     bool swiglu = false, const LinearRope* rope = nullptr);
 
 }  // namespace nslg

@@ -99,6 +99,23 @@ constexpr int kMaxTiles = 1 << 16;      // out_features <= 8,388,608
 // Measured on the 8B shapes: 0.7-1.2 us faster per call at 1-16 rows, 2.5-4 us at 64.
 constexpr int kPushMaxMp = 64;
 
+// RoPE + paged KV append in the epilogue of a stacked q|k|v product with head_dim 128
+// (one tile = one head: q heads 0..hq-1, k heads, v heads), the operation and the
+// rounding of nslg_rope_kv_append: q rotated into q_out [rows, hq, 128], k rotated and
+// v copied into the pool slot write_loc[m] (< 0: not written).
+struct RopeAppend {
+  int on, hq, hkv;
+  void* q_out;
+  const int32_t* positions;   // NULL: no rotation
+  const float* cos_t;
+  const float* sin_t;
+  int64_t table_rows;
+  const int32_t* write_loc;
+  void* pool_k;
+  void* pool_v;
+  int64_t pool_slots;
+};
+
 struct LinParams {
   void* y;
   int64_t y_stride;
@@ -108,6 +125,8 @@ struct LinParams {
   int push_sum;     // split-K partials pushed to their owners (splits > 1, Mp <= 64)
   int swiglu;       // tile t = gate rows [64t, 64t + 64) and up rows [I + 64t, ...) of a
                     // stacked gate|up weight; y[m][c] = silu(gate) * up, N = I
+  int paired;       // epilogue pairs row r < 64 of a tile with row r + 64 (SwiGLU, RoPE)
+  RopeAppend rope;  // rope.on: tile t is q / k / v head t of a stacked q|k|v product
   TpPush push;
   uint32_t* status;
 };
@@ -145,13 +164,73 @@ __device__ __forceinline__ void store_y4(const LinParams& p, int m, int n0, cons
 // (whole 16-byte vectors of a y row for the push), every CTA at least 16 rows.
 __device__ __forceinline__ int split_row_lo(int j, int s) { return 8 * ((16 * j) / s); }
 
+// The RoPE epilogue's output for activation row m (a token), tile t (a head) and the
+// head dims [c, c + n) and [64 + c, 64 + c + n): a holds the product's values (rounded)
+// of the first dims, b of the second. q and k heads are rotated as
+// rope_kv_append_kernel does (rotate-half, cos/sin rounded to T, every product and sum
+// rounded to T); v heads are copied. q goes to q_out, k and v to the pool slot.
+template <typename T, int n>
+__device__ void rope_store(const LinParams& p, int m, int t, int c, const T (&a)[n],
+                           const T (&b)[n]) {
+  const RopeAppend& r = p.rope;
+  const bool is_q = t < r.hq, is_v = t >= r.hq + r.hkv;
+  T* dst;
+  if (is_q) {
+    dst = static_cast<T*>(r.q_out) + (static_cast<int64_t>(m) * r.hq + t) * 128;
+  } else {
+    int64_t loc = r.write_loc != nullptr ? r.write_loc[m] : -1;
+    if (loc >= r.pool_slots) {
+      report(p.status, NSLG_DEV_BAD_SLOT);
+      loc = -1;
+    }
+    if (loc < 0) return;
+    const int h = is_v ? t - r.hq - r.hkv : t - r.hq;
+    dst = static_cast<T*>(is_v ? r.pool_v : r.pool_k) + (loc * r.hkv + h) * 128;
+  }
+  alignas(16) T o1[n];
+  alignas(16) T o2[n];
+  int64_t pos = -1;
+  if (!is_v && r.positions != nullptr) {
+    pos = r.positions[m];
+    if (pos < 0 || pos >= r.table_rows) {   // reported, row left unrotated
+      report(p.status, NSLG_DEV_BAD_POSITION);
+      pos = -1;
+    }
+  }
+  if (pos < 0) {
+#pragma unroll
+    for (int i = 0; i < n; ++i) { o1[i] = a[i]; o2[i] = b[i]; }
+  } else {
+    const float* cs = r.cos_t + pos * 128 + c;
+    const float* sn = r.sin_t + pos * 128 + c;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float x1 = Elem<T>::to_f(a[i]), x2 = Elem<T>::to_f(b[i]);
+      const float c1 = Elem<T>::round(cs[i]), s1 = Elem<T>::round(sn[i]);
+      const float c2 = Elem<T>::round(cs[64 + i]), s2 = Elem<T>::round(sn[64 + i]);
+      o1[i] = Elem<T>::from_f(__fadd_rn(Elem<T>::round(__fmul_rn(x1, c1)),
+                                        Elem<T>::round(__fmul_rn(-x2, s1))));
+      o2[i] = Elem<T>::from_f(__fadd_rn(Elem<T>::round(__fmul_rn(x2, c2)),
+                                        Elem<T>::round(__fmul_rn(x1, s2))));
+    }
+  }
+  if constexpr (n == 8) {
+    *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(o1);
+    *reinterpret_cast<uint4*>(dst + 64 + c) = *reinterpret_cast<const uint4*>(o2);
+  } else {
+    static_assert(n == 4, "4 or 8 dims");
+    *reinterpret_cast<uint2*>(dst + c) = *reinterpret_cast<const uint2*>(o1);
+    *reinterpret_cast<uint2*>(dst + 64 + c) = *reinterpret_cast<const uint2*>(o2);
+  }
+}
+
 // SwiGLU mode: CTA j of s owns the output columns [half_lo(j), half_lo(j + 1)) of its
 // tile's 64, i.e. gate rows [lo, hi) and up rows [64 + lo, 64 + hi) of the tile.
 __device__ __forceinline__ int half_lo(int j, int s) { return 8 * ((8 * j) / s); }
 
 // Rows of the tile (of D, 128) that CTA j sums, and the position of row r among them.
 __device__ __forceinline__ int owned_rows(const LinParams& p, int j) {
-  return p.swiglu ? 2 * (half_lo(j + 1, p.splits) - half_lo(j, p.splits))
+  return p.paired ? 2 * (half_lo(j + 1, p.splits) - half_lo(j, p.splits))
                   : split_row_lo(j + 1, p.splits) - split_row_lo(j, p.splits);
 }
 
@@ -397,11 +476,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     // (SwiGLU: the owner of output column r % 64 takes gate row r and up row r + 64;
     // its rows are [its gate rows, its up rows])
     const int own = !p.push_sum ? 0
-                    : p.swiglu  ? half_owner(r & 63, p.splits)
+                    : p.paired  ? half_owner(r & 63, p.splits)
                                 : split_owner(r, p.splits);
     const int own_rows = owned_rows(p, own);
     int own_pos;
-    if (p.swiglu) {
+    if (p.paired) {
       const int lo = half_lo(own, p.splits);
       own_pos = (r < 64 ? 0 : own_rows / 2) + (r & 63) - lo;
     } else {
@@ -450,7 +529,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (p.splits == 1) {
     // the staged tile to y, 8 consecutive outputs (16 bytes) of one row per store
-    if (!*abort_flag && p.swiglu) {
+    if (!*abort_flag && p.rope.on) {
+      // head t of token m: dims c.. and 64 + c.. of the staged tile, rotated, stored
+      const T* tile_y = reinterpret_cast<const T*>(smem);
+      for (int u = threadIdx.x; u < p.M * 8; u += kThreads) {
+        const int m = u / 8, c = 8 * (u % 8);
+        alignas(16) T a[8];
+        alignas(16) T b[8];
+        *reinterpret_cast<uint4*>(a) = *reinterpret_cast<const uint4*>(tile_y + m * kTileN + c);
+        *reinterpret_cast<uint4*>(b) =
+            *reinterpret_cast<const uint4*>(tile_y + m * kTileN + 64 + c);
+        rope_store<T, 8>(p, m, t, c, a, b);
+      }
+    } else if (!*abort_flag && p.swiglu) {
       // y[m][64t + c] = silu(gate) * up from rows c and 64 + c of the staged tile
       const T* tile_y = reinterpret_cast<const T*>(smem);
       for (int u = threadIdx.x; u < p.M * 8; u += kThreads) {
@@ -478,8 +569,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool landed = mbar_wait_cluster(recv_full, 0);
     if (!landed) {
       if (threadIdx.x == 0) report(p.status, NSLG_DEV_WAIT_TIMEOUT);
-    } else if (!*abort_flag && p.swiglu) {
-      // gate and up sums of this CTA's columns [lo, hi) of the tile, rounded, activated
+    } else if (!*abort_flag && p.paired) {
+      // sums of this CTA's rows [lo, hi) and [64 + lo, 64 + hi) of the tile (gate and
+      // up, or the two halves of a head), rounded, then activated or rotated
       const int lo = half_lo(j, p.splits);
       const int h = half_lo(j + 1, p.splits) - lo;
       const int quads = h / 4;
@@ -496,11 +588,22 @@ __global__ void __launch_bounds__(kThreads, 2)
           g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
           u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
         }
-        float o[4];
+        if (p.rope.on) {
+          alignas(16) T a[4];
+          alignas(16) T b[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[i] = Elem<T>::to_f(swiglu<T>(Elem<T>::from_f(g[i]), Elem<T>::from_f(u[i])));
-        store_y4<T>(p, m, t * 64 + lo + q4, o);
+          for (int i = 0; i < 4; ++i) {
+            a[i] = Elem<T>::from_f(g[i]);
+            b[i] = Elem<T>::from_f(u[i]);
+          }
+          rope_store<T, 4>(p, m, t, lo + q4, a, b);
+        } else {
+          float o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[i] = Elem<T>::to_f(swiglu<T>(Elem<T>::from_f(g[i]), Elem<T>::from_f(u[i])));
+          store_y4<T>(p, m, t * 64 + lo + q4, o);
+        }
       }
     } else if (!*abort_flag) {
       const int r_lo = split_row_lo(j, p.splits);
@@ -595,10 +698,10 @@ int stages_for(int Mp, int recv_bytes) {
 
 // Receive buffer of a pushed split-K sum: s partials of the largest row share (SwiGLU
 // mode: twice the largest share of the tile's 64 output columns).
-int recv_bytes_for(int splits, int Mp, bool swiglu) {
+int recv_bytes_for(int splits, int Mp, bool paired) {
   int rows = 0;
   for (int j = 0; j < splits; ++j) {
-    const int r = swiglu ? 2 * (8 * ((8 * (j + 1)) / splits) - 8 * ((8 * j) / splits))
+    const int r = paired ? 2 * (8 * ((8 * (j + 1)) / splits) - 8 * ((8 * j) / splits))
                          : 8 * ((16 * (j + 1)) / splits) - 8 * ((16 * j) / splits);
     rows = r > rows ? r : rows;
   }
@@ -610,7 +713,7 @@ int recv_bytes_for(int splits, int Mp, bool swiglu) {
 // more than one CTA per SM the cluster size is rounded down to a power of two, so that
 // the clusters pack into the GPCs' CTA slots in one wave (measured on the 8B q|k|v
 // product at one row: 48 clusters of 6, 288 CTAs, 15.7 us; of 3, 144 CTAs, 12.3 us).
-Plan plan_for(int M, int N, int K, bool swiglu) {
+Plan plan_for(int M, int N, int K, bool swiglu, bool paired) {
   Plan pl{};
   pl.Mp = (M + 15) / 16 * 16;
   // a tile is 128 weight rows: 128 outputs, or 64 gate|up pairs (SwiGLU)
@@ -629,11 +732,11 @@ Plan plan_for(int M, int N, int K, bool swiglu) {
   pl.splits = s;
   pl.grid = pl.n_tiles * s;
   pl.push_sum = (s > 1 && pl.Mp <= kPushMaxMp && env_int("NSLG_LINEAR_PUSH_SUM", 1, 0, 1) &&
-                 recv_bytes_for(s, pl.Mp, swiglu) + kMinStages * (kWBytes + pl.Mp * 128) <=
+                 recv_bytes_for(s, pl.Mp, paired) + kMinStages * (kWBytes + pl.Mp * 128) <=
                      kLinearSmemBudget)
                     ? 1
                     : 0;
-  pl.recv_bytes = pl.push_sum ? recv_bytes_for(s, pl.Mp, swiglu) : 0;
+  pl.recv_bytes = pl.push_sum ? recv_bytes_for(s, pl.Mp, paired) : 0;
   pl.stages = stages_for(pl.Mp, pl.recv_bytes);
   int cols = 32;
   while (cols < pl.Mp) cols *= 2;
@@ -650,11 +753,14 @@ bool linear_tc_supported(int dtype, int M, int N, int K) {
 
 int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_stride,
                      const void* w, int64_t w_stride, void* y, int64_t y_stride,
-                     const TpPush* push, uint32_t* status, cudaStream_t stream, bool swiglu) {
-  const Plan pl = plan_for(M, N, K, swiglu);
-  if (swiglu && (push != nullptr || (pl.splits > 1 && !pl.push_sum)))
+                     const TpPush* push, uint32_t* status, cudaStream_t stream, bool swiglu,
+                     const LinearRope* rope) {
+  const bool paired = swiglu || rope != nullptr;
+  const Plan pl = plan_for(M, N, K, swiglu, paired);
+  if (paired && (push != nullptr || (pl.splits > 1 && !pl.push_sum)))
     return set_error(NSLG_ERR_UNSUPPORTED,
-                     "linear_swiglu: the split-K sum of this shape does not fit the push");
+                     std::string(swiglu ? "linear_swiglu" : "linear_rope_append") +
+                         ": the split-K sum of this shape does not fit the push");
   CUtensorMap tw, tw2, tx;
   // W [N, K] and x [M, K], K innermost; boxes [64 x 128] and [64 x Mp] with 128-byte
   // swizzle. SwiGLU: W is [2N, K] (gate rows, then up rows), one map per half, each with
@@ -689,6 +795,21 @@ int launch_linear_tc(int dtype, int M, int N, int K, const void* x, int64_t x_st
   p.y_vec = (reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_stride % 8 == 0) ? 1 : 0;
   p.push_sum = pl.push_sum;
   p.swiglu = swiglu ? 1 : 0;
+  p.paired = paired ? 1 : 0;
+  if (rope != nullptr) {
+    p.rope.on = 1;
+    p.rope.hq = rope->hq;
+    p.rope.hkv = rope->hkv;
+    p.rope.q_out = rope->q_out;
+    p.rope.positions = rope->positions;
+    p.rope.cos_t = rope->cos_t;
+    p.rope.sin_t = rope->sin_t;
+    p.rope.table_rows = rope->table_rows;
+    p.rope.write_loc = rope->write_loc;
+    p.rope.pool_k = rope->pool_k;
+    p.rope.pool_v = rope->pool_v;
+    p.rope.pool_slots = rope->pool_slots;
+  }
   if (push != nullptr) p.push = *push;
   p.status = status;
   const size_t smem = smem_bytes(pl.stages, pl.Mp, pl.recv_bytes);

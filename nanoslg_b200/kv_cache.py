@@ -842,6 +842,25 @@ class B200CacheContext(CacheContext):
                                    pool.k_layers[layer_idx], pool.v_layers[layer_idx])
         return self._attention(layer_idx, q_rot.view(B, S, hq, d))
 
+    def attend_qkv(self, layer_idx, x, w_qkv, n_heads, n_kv_heads, cos, sin):
+        """Decode steps: the layer's q|k|v product, RoPE and KV append in one kernel
+        (``ops.linear_rope_append``, x [B, 1, hidden] against the stacked [q; k; v]
+        weight), then attention -- what the projections followed by ``attend_rope`` do.
+        Returns None (nothing launched) where that kernel does not take the operands;
+        the caller then projects and calls ``attend_rope``."""
+        if not self._is_decode or x.dim() != 3:
+            return None
+        B, S, _ = x.shape
+        if B != self.batch_size or S != self._iw:
+            return None
+        pool = self.cache.pool
+        q_rot = ops.linear_rope_append(x, w_qkv, n_heads, n_kv_heads, self._pos_i32, cos, sin,
+                                       self._write_loc, pool.k_layers[layer_idx],
+                                       pool.v_layers[layer_idx])
+        if q_rot is None:
+            return None
+        return self._attention(layer_idx, q_rot.view(B, S, n_heads, -1))
+
     def _decode_direct(self, layer_idx, q, k, v):
         """Decode ``attend`` straight through one C call (``nslg_append_paged_decode``: KV
         append, then paged decode), skipping the generic wrappers' per-call checks, for

@@ -130,6 +130,14 @@ class TPAttention(nn.Module):
         B, S, _ = x.shape
         hd = self.head_dim
         if _views_intact(self._qkv, [self.q_proj, self.k_proj, self.v_proj]):
+            # decode batches: projections, RoPE and KV append in one kernel when the
+            # context offers it (B200CacheContext.attend_qkv)
+            attend_qkv = getattr(cache_ctx, "attend_qkv", None)
+            if attend_qkv is not None:
+                a = attend_qkv(self.layer_idx, x, self._qkv, self.n_heads_tp,
+                               self.n_kv_heads_tp, cos, sin)
+                if a is not None:
+                    return self.o_proj(a)
             qkv = ops.linear(x, self._qkv)
             nq, nk = self.n_heads_tp * hd, self.n_kv_heads_tp * hd
             q = qkv[..., :nq].view(B, S, self.n_heads_tp, hd)

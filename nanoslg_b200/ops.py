@@ -339,6 +339,46 @@ def linear_swiglu(x, gate_up, max_rows=LINEAR_AUTO_ROWS):
     return out
 
 
+def linear_rope_append(x, w_qkv, hq, hkv, positions, cos, sin, write_loc, pool_k, pool_v,
+                       max_rows=LINEAR_AUTO_ROWS):
+    """The q|k|v product of x with a stacked [q; k; v] weight, then rope_kv_append's
+    RoPE and KV append, in one kernel (nslg_linear_rope_append): returns the rotated q
+    ([rows, hq, 128]) after k and v went to the pool slots ``write_loc``. Returns None
+    where that kernel does not take the operands (head_dim other than 128, more than
+    ``max_rows`` rows, a split-K sum it would not push, ...); the caller then runs
+    ``linear`` and ``rope_kv_append``, which give the same values."""
+    d = pool_k.shape[-1]
+    if (d != 128 or w_qkv.shape[0] != (hq + 2 * hkv) * d
+            or not linear_supported(x, w_qkv, None, max_rows)):
+        return None
+    if (pool_k.dtype != x.dtype or pool_v.dtype != x.dtype or not pool_k.is_contiguous()
+            or not pool_v.is_contiguous() or pool_k.shape[-2] != hkv):
+        return None
+    try:
+        rows, xs = _rows(x.unsqueeze(-2), "x")
+    except ValueError:
+        return None
+    if xs % 8 or x.data_ptr() % 16:
+        return None
+    if (positions is None or positions.dtype != torch.int32 or positions.numel() != rows
+            or write_loc is None or write_loc.dtype != torch.int32 or write_loc.numel() != rows
+            or cos.dtype != torch.float32 or not cos.is_contiguous() or not sin.is_contiguous()):
+        return None
+    q_out = torch.empty((rows, hq, d), dtype=x.dtype, device=x.device)
+    lib = N.lib()
+    rc = lib.nslg_linear_rope_append(
+        _dtype_code(x), rows, hq, hkv, d, x.shape[-1], _ptr(x), xs, _ptr(w_qkv),
+        w_qkv.stride(0), _ptr(q_out), _ptr(positions), _ptr(cos), _ptr(sin), cos.shape[0],
+        _ptr(write_loc), _ptr(pool_k), _ptr(pool_v), pool_k.shape[0] * pool_k.shape[1],
+        _ptr(status_word(x.device)), _stream(x))
+    if rc == N.ERR_UNSUPPORTED:
+        return None
+    if rc != N.OK:
+        raise N.NativeError("nslg_linear_rope_append", rc,
+                            lib.nslg_last_error().decode(errors="replace"))
+    return q_out
+
+
 def argmax_rows(x, index_offset=0, values=False):
     """Per row of ``x`` [rows, cols] (last dim contiguous): the index of the first
     maximum plus ``index_offset`` (int64 [rows]), ordered as torch.argmax (NaN above

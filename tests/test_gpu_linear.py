@@ -197,3 +197,77 @@ def test_linear_split_policies(cps, minc, m, n, k, monkeypatch):
     y = ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS)
     torch.testing.assert_close(y, _ref(x, w), **TOL[dt])
     assert torch.equal(ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS), y)
+
+
+def _rope_case(m, hq, hkv, k, dt, seed, pages=64):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x = torch.randn(m, 1, k, device=DEV, generator=g).to(dt)
+    w = (torch.randn((hq + 2 * hkv) * 128, k, device=DEV, generator=g) / k ** 0.5).to(dt)
+    pool_k = torch.randn(pages, 16, hkv, 128, device=DEV, generator=g).to(dt)
+    pool_v = torch.randn(pages, 16, hkv, 128, device=DEV, generator=g).to(dt)
+    pos = torch.randint(0, 4000, (m,), device=DEV, generator=g).to(torch.int32)
+    loc = torch.randperm(pages * 16, device=DEV, generator=g)[:m].to(torch.int32)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 64, device=DEV).float() / 64))
+    ang = torch.outer(torch.arange(4096, device=DEV).float(), inv)
+    cos = torch.cat([ang.cos(), ang.cos()], -1).contiguous()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).contiguous()
+    return x, w, pool_k, pool_v, pos, loc, cos, sin
+
+
+def _rope_two_kernels(x, w, hq, hkv, pos, loc, cos, sin, pool_k, pool_v):
+    qkv = ops.linear(x, w, max_rows=ops.LINEAR_MAX_ROWS)
+    q = qkv[..., :hq * 128].view(-1, hq, 128)
+    kk = qkv[..., hq * 128:(hq + hkv) * 128].view(-1, hkv, 128)
+    v = qkv[..., (hq + hkv) * 128:].view(-1, hkv, 128)
+    return ops.rope_kv_append(q, kk, v, pos, cos, sin, loc, pool_k, pool_v)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,hq,hkv,k", [
+    (1, 32, 8, 4096),      # TP=1: 48 heads, 4-way K split
+    (16, 16, 4, 4096),     # TP=2
+    (5, 4, 1, 4096),       # TP=8 shard: 6 heads, 8-way split
+    (64, 8, 2, 1024),      # 64 rows
+    (3, 2, 2, 128),        # 2 chunks: whole tiles
+])
+def test_linear_rope_append_matches_linear_then_rope_kv_append(dt, m, hq, hkv, k):
+    """The q|k|v product with RoPE and the paged KV append in its epilogue writes exactly
+    what the product (rounded) followed by rope_kv_append writes: the rotated q, and the
+    rotated k and plain v in the pool slots."""
+    x, w, pk, pv, pos, loc, cos, sin = _rope_case(m, hq, hkv, k, dt, seed=m + hq + k)
+    pk2, pv2 = pk.clone(), pv.clone()
+    q_fused = ops.linear_rope_append(x, w, hq, hkv, pos, cos, sin, loc, pk, pv,
+                                     max_rows=ops.LINEAR_MAX_ROWS)
+    assert q_fused is not None
+    q_two = _rope_two_kernels(x, w, hq, hkv, pos, loc, cos, sin, pk2, pv2)
+    assert torch.equal(q_fused, q_two)
+    assert torch.equal(pk, pk2) and torch.equal(pv, pv2)
+
+
+def test_linear_rope_append_out_of_range_positions_and_slots():
+    """A position outside the cos/sin table leaves that token unrotated and sets the
+    position bit of the status word; a write slot < 0 is skipped, one past the pool sets
+    the slot bit and is skipped -- as rope_kv_append does."""
+    x, w, pk, pv, pos, loc, cos, sin = _rope_case(4, 8, 2, 512, torch.bfloat16, seed=3)
+    pos[1] = 5000                        # the table has 4096 rows
+    loc[2] = -1
+    loc[3] = pk.shape[0] * 16            # one past the last slot
+    pk2, pv2 = pk.clone(), pv.clone()
+    q_fused = ops.linear_rope_append(x, w, 8, 2, pos, cos, sin, loc, pk, pv,
+                                     max_rows=ops.LINEAR_MAX_ROWS)
+    st = int(ops.status_word(DEV).item())
+    assert st & N.DEV_BAD_POSITION and st & N.DEV_BAD_SLOT
+    ops.status_word(DEV).zero_()
+    q_two = _rope_two_kernels(x, w, 8, 2, pos, loc, cos, sin, pk2, pv2)
+    ops.status_word(DEV).zero_()
+    assert torch.equal(q_fused, q_two)
+    assert torch.equal(pk, pk2) and torch.equal(pv, pv2)
+
+
+def test_linear_rope_append_declines_what_it_does_not_cover():
+    """head_dim 64 and more rows than allowed: None, nothing launched (the caller runs the
+    two kernels)."""
+    x, w, pk, pv, pos, loc, cos, sin = _rope_case(2, 4, 2, 256, torch.bfloat16, seed=4)
+    pk64 = torch.zeros(8, 16, 2, 64, dtype=torch.bfloat16, device=DEV)
+    assert ops.linear_rope_append(x, w, 4, 2, pos, cos, sin, loc, pk64, pk64) is None
+    assert ops.linear_rope_append(x, w, 4, 2, pos, cos, sin, loc, pk, pv, max_rows=1) is None
