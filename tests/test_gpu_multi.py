@@ -139,3 +139,59 @@ def test_pipeline_microbatched_decode_matches_lock_step():
     for rank in range(world):
         assert res[rank].get("done"), res[rank]
         assert all(v for k, v in res[rank].items() if k != "done"), res[rank]
+
+
+def _fused_main(rank, world, port, fused, out):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from nanoslg_b200 import ops
+        import nanoslg_b200.kv_cache as kvc
+        from nanoslg_b200.runner import LlamaRunner
+        if not fused:   # the two-kernel paths: projections, then RoPE/append and silu*mul
+            kvc.B200CacheContext.attend_qkv = lambda self, *a, **k: None
+            ops.linear_swiglu = lambda x, w, max_rows=ops.LINEAR_AUTO_ROWS: ops.silu_mul(
+                ops.linear(x, w, max_rows=max_rows))
+        cfg = SimpleNamespace(num_hidden_layers=2, hidden_size=1024, num_attention_heads=8,
+                              num_key_value_heads=2, intermediate_size=2048, vocab_size=1000,
+                              rms_norm_eps=1e-5, rope_theta=10000.0,
+                              max_position_embeddings=512)
+        r = LlamaRunner(cfg, dev, dtype=torch.bfloat16, tp_size=world, rank=rank,
+                        max_kv_pages=64, seed=7)
+        g = torch.Generator().manual_seed(3)
+        prompts = torch.randint(0, 1000, (3, 40), generator=g).tolist()
+        tok = r.prefill(prompts)
+        toks = [tok.tolist()]
+        for _ in range(12):
+            tok = r.decode_step(tok)
+            toks.append(tok.tolist())
+        out[(rank, fused)] = toks
+        r.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_fused_epilogues_keep_the_tokens_at_tp(tp):
+    """bf16, head_dim 128, TP=1 and 2: decode steps with the q|k|v product + RoPE + KV
+    append and the gate|up product + SwiGLU each in one kernel (decode batches) give the
+    same greedy tokens on every rank as with the separate kernels (each fused op is bit
+    for bit its two-kernel path; this checks the wiring on sharded heads and weights)."""
+    if torch.cuda.device_count() < tp:
+        pytest.skip(f"needs {tp} GPUs")
+    with mp.get_context("spawn").Manager() as m:
+        out = m.dict()
+        for fused in (True, False):
+            mp.start_processes(_fused_main, args=(tp, _free_port(), fused, out), nprocs=tp,
+                               start_method="spawn", join=True)
+        res = dict(out)
+    for rank in range(tp):
+        assert res[(rank, True)] == res[(rank, False)], f"rank {rank}"
+    assert all(res[(r, True)] == res[(0, True)] for r in range(tp))
