@@ -3,8 +3,9 @@
 // Work split. The pages of all sequences form one flat list (the CSR kv_indices,
 // kv_cache.py:598-615). CTA c of n takes the contiguous slice
 // [floor(T*c/n), floor(T*(c+1)/n)) of it, T = kv_indptr[B], so every CTA streams the
-// same number of pages whatever the sequence lengths are. n = min(#SMs, ceil(T/2)) and
-// is computed on the device from kv_indptr, so the launch needs no host-side plan and
+// same number of pages whatever the sequence lengths are. n = min(#SMs, ceil(T/m)), m =
+// the pages of at least 2 and 32 KiB of K/V, and n is computed on the device from
+// kv_indptr, so the launch needs no host-side plan and
 // can be replayed inside a CUDA graph. A CTA's slice is cut into segments at sequence
 // boundaries; segment (b, c) writes its softmax partial (o, lse) to slot b + c of the
 // workspace (unique: along the flat list either b or c grows by one at each new
@@ -56,6 +57,13 @@ constexpr int kPS = 16;             // tokens per page
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMinPagesPerCta = 2;
+// ... and at least this many K/V bytes per CTA (a page holds 64 * hkv * head_dim bytes:
+// 64 KiB at 8 kv heads, 8 KiB at 1): every extra CTA of a sequence is one more partial
+// to merge, every missing one a slower stream. Measured at the TP=8 shard (1 kv head),
+// batch 1, 512 tokens, 32 layers per graph: 16 / 32 / 64 / 128 KiB per CTA (16, 8, 4,
+// 2 CTAs) gave 6.67 / 6.48 / 6.72 / 8.02 us per layer; the 8 kv head shapes keep 2
+// pages (64 KiB each) per CTA.
+constexpr int kMinCtaBytes = 32 << 10;
 constexpr int kBoxBytes = kPS * 64 * 2;  // one [16 x 64] bf16 box: 2 KiB
 constexpr int kMaxSmem = 232448;         // 227 KiB opt-in per CTA on sm_100
 constexpr int kSmemCsrBatch = 1024;      // batches up to this size keep the CSR in smem
@@ -73,13 +81,14 @@ struct DecodeParams {
   int batch, hq, group, stages, grid;
   int smem_csr;       // kv_indptr and kv_last_page_len are staged in shared memory
   int inline_merge;   // 1: split sequences merged by their last CTA; 0: by the merge kernel
+  int min_pages;      // fewest pages a CTA streams (kMinPagesPerCta, kMinCtaBytes)
   int box_all_heads;  // tensor maps with a [64 dim x 16 tok x HKV head] box (token-major)
   float scale_log2;
   uint32_t* status;
 };
 
-__device__ __forceinline__ int num_ctas(int64_t total_pages, int grid) {
-  const int64_t want = (total_pages + kMinPagesPerCta - 1) / kMinPagesPerCta;
+__device__ __forceinline__ int num_ctas(int64_t total_pages, int grid, int min_pages) {
+  const int64_t want = (total_pages + min_pages - 1) / min_pages;
   return static_cast<int>(want < grid ? want : grid);
 }
 
@@ -362,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   const int64_t total = indptr[p.batch];
-  const int n = num_ctas(total, p.grid);
+  const int n = num_ctas(total, p.grid, p.min_pages);
   const int c = blockIdx.x;
   if (c >= n) {
     pdl_wait();
@@ -740,7 +749,7 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeParams p)
   if (hq >= p.hq) return;
   T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
   if (beg == end) return;
-  const int n = num_ctas(total, p.grid);
+  const int n = num_ctas(total, p.grid, p.min_pages);
   const int cf = cta_of(beg, total, n), cl = cta_of(end - 1, total, n);
   if (cf == cl) return;
   const int cnt = cl - cf + 1;
@@ -980,6 +989,17 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
   p.status = status;
   p.box_all_heads = box_all;
   p.inline_merge = merge_inline(batch, hq, d, grid);
+  {
+    // NSLG_DECODE_MIN_CTA_KB overrides kMinCtaBytes (1 to 4096 KiB), for measurements
+    int min_bytes = kMinCtaBytes;
+    if (const char* e = std::getenv("NSLG_DECODE_MIN_CTA_KB")) {
+      const int kb = std::atoi(e);
+      if (kb >= 1 && kb <= 4096) min_bytes = kb << 10;
+    }
+    const int page_bytes = 64 * hkv * d;
+    const int by_bytes = (min_bytes + page_bytes - 1) / page_bytes;
+    p.min_pages = by_bytes > kMinPagesPerCta ? by_bytes : kMinPagesPerCta;
+  }
   if (dtype == NSLG_DTYPE_F16) return launch_for_type<__half>(hkv, d, tk, tv, p, stream);
   return launch_for_type<__nv_bfloat16>(hkv, d, tk, tv, p, stream);
 }
