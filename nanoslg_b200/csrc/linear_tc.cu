@@ -44,6 +44,16 @@
 // The compute and the collective's data movement are one kernel; no load ever reads a
 // peer's memory.
 //
+// Paired epilogues. Two modes keep row r < 64 of a tile together with row r + 64 (in the
+// staged tile, and in each split owner's share: columns [lo, hi) of 64 mean rows
+// [lo, hi) and [64 + lo, 64 + hi)). SwiGLU (nslg_linear_swiglu): tile t is loaded as
+// gate rows [64t, 64t + 64) and up rows [I + 64t, ...) of a stacked gate|up weight (two
+// 64-row boxes into the one swizzled A tile), and the epilogue writes silu(gate) * up.
+// RoPE + KV append (nslg_linear_rope_append): with head_dim 128 a tile of the stacked
+// q|k|v product is one head, whose rotate-half pairs are rows r and r + 64; the epilogue
+// rotates q into q_out and k into the paged pool and copies v there. Both round as the
+// separate kernels do, so their results are bit for bit the two-kernel results.
+//
 // Pipeline (up to two CTAs per SM, 256 threads each):
 //   warp 0     TMA producer: the first ring's worth of weight boxes before waiting for
 //              the previous kernel (programmatic dependent launch: the weights do not
