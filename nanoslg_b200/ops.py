@@ -263,9 +263,22 @@ def silu_mul(gate_up, out=None):
 
 
 LINEAR_MAX_ROWS = 256     # what nslg_linear accepts
-# what ``linear`` sends it by default; NSLG_LINEAR_ROWS (read at import) changes it, for
-# measurements (1 to LINEAR_MAX_ROWS)
-LINEAR_AUTO_ROWS = max(1, min(int(os.environ.get("NSLG_LINEAR_ROWS", "16")), 256))
+# What ``linear`` sends the kernel by default: batches of up to LINEAR_AUTO_ROWS rows, and
+# of up to LINEAR_WIDE_ROWS rows for products of at least LINEAR_WIDE_BYTES of weights
+# (at 64 rows the kernel is level with or ahead of cuBLAS on the 8B model's TP=1 gate|up
+# and down products, 235 and 117 MB, and behind on the narrower ones). NSLG_LINEAR_ROWS
+# (read at import, 1 to LINEAR_MAX_ROWS) replaces both limits, for measurements.
+_ROWS_ENV = os.environ.get("NSLG_LINEAR_ROWS")
+LINEAR_AUTO_ROWS = max(1, min(int(_ROWS_ENV or "16"), 256))
+LINEAR_WIDE_ROWS = LINEAR_AUTO_ROWS if _ROWS_ENV else 64
+LINEAR_WIDE_BYTES = 96 << 20
+
+
+def auto_rows(weight):
+    """The default row limit of ``linear`` / ``linear_swiglu`` / ``linear_rope_append``
+    for this weight."""
+    big = weight.numel() * weight.element_size() >= LINEAR_WIDE_BYTES
+    return LINEAR_WIDE_ROWS if big else LINEAR_AUTO_ROWS
 
 
 def linear_supported(x, weight, bias=None, max_rows=LINEAR_MAX_ROWS):
@@ -285,13 +298,15 @@ def linear_supported(x, weight, bias=None, max_rows=LINEAR_MAX_ROWS):
     return 1 <= rows <= max_rows
 
 
-def linear(x, weight, bias=None, out=None, max_rows=LINEAR_AUTO_ROWS):
+def linear(x, weight, bias=None, out=None, max_rows=None):
     """F.linear(x, weight, bias): the tcgen05 kernel (nslg_linear) for forwards of at most
     ``max_rows`` rows (``linear_supported``), the cuBLAS GEMM of F.linear for the rest.
-    The default sends the kernel the small decode batches (up to 16 rows), where it
-    streams the weights faster than cuBLAS on the 8B model's shapes at every TP degree;
-    at 64 rows cuBLAS is still ahead on the narrower products (measured per shape), so
-    larger batches, prefill, fp32 and biased layers stay cuBLAS."""
+    The default (``auto_rows``) sends the kernel the small decode batches (up to 16 rows),
+    where it streams the weights faster than cuBLAS on the 8B model's shapes at every TP
+    degree, and batches of up to 64 rows on the largest products; prefill, fp32 and
+    biased layers stay cuBLAS."""
+    if max_rows is None:
+        max_rows = auto_rows(weight)
     if not linear_supported(x, weight, bias, max_rows):
         return F.linear(x, weight, bias)
     k, n = x.shape[-1], weight.shape[0]
@@ -309,13 +324,15 @@ def linear(x, weight, bias=None, out=None, max_rows=LINEAR_AUTO_ROWS):
     return out
 
 
-def linear_swiglu(x, gate_up, max_rows=LINEAR_AUTO_ROWS):
+def linear_swiglu(x, gate_up, max_rows=None):
     """silu(x . gate^T) * (x . up^T) for a stacked [gate; up] weight ([2 I, in]): the
     tcgen05 linear kernel with the activation in its epilogue (nslg_linear_swiglu) where
     ``linear_supported(x, gate_up)`` holds; ``silu_mul(linear(x, gate_up))`` otherwise,
     and where the kernel reports that the shape's split-K sum would not be pushed. Both
     give the same values: each product rounded to the activation type, silu rounded, the
     product rounded."""
+    if max_rows is None:
+        max_rows = auto_rows(gate_up)
     two_i = gate_up.shape[0]
     if two_i % 2 or not linear_supported(x, gate_up, None, max_rows):
         return silu_mul(linear(x, gate_up, max_rows=max_rows))
@@ -340,13 +357,15 @@ def linear_swiglu(x, gate_up, max_rows=LINEAR_AUTO_ROWS):
 
 
 def linear_rope_append(x, w_qkv, hq, hkv, positions, cos, sin, write_loc, pool_k, pool_v,
-                       max_rows=LINEAR_AUTO_ROWS):
+                       max_rows=None):
     """The q|k|v product of x with a stacked [q; k; v] weight, then rope_kv_append's
     RoPE and KV append, in one kernel (nslg_linear_rope_append): returns the rotated q
     ([rows, hq, 128]) after k and v went to the pool slots ``write_loc``. Returns None
     where that kernel does not take the operands (head_dim other than 128, more than
     ``max_rows`` rows, a split-K sum it would not push, ...); the caller then runs
     ``linear`` and ``rope_kv_append``, which give the same values."""
+    if max_rows is None:
+        max_rows = auto_rows(w_qkv)
     d = pool_k.shape[-1]
     if (d != 128 or w_qkv.shape[0] != (hq + 2 * hkv) * d
             or not linear_supported(x, w_qkv, None, max_rows)):

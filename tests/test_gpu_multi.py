@@ -157,7 +157,7 @@ def _fused_main(rank, world, port, fused, out):
         from nanoslg_b200.runner import LlamaRunner
         if not fused:   # the two-kernel paths: projections, then RoPE/append and silu*mul
             kvc.B200CacheContext.attend_qkv = lambda self, *a, **k: None
-            ops.linear_swiglu = lambda x, w, max_rows=ops.LINEAR_AUTO_ROWS: ops.silu_mul(
+            ops.linear_swiglu = lambda x, w, max_rows=None: ops.silu_mul(
                 ops.linear(x, w, max_rows=max_rows))
         cfg = SimpleNamespace(num_hidden_layers=2, hidden_size=1024, num_attention_heads=8,
                               num_key_value_heads=2, intermediate_size=2048, vocab_size=1000,
