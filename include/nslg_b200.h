@@ -311,9 +311,11 @@ int nslg_zero_pages(const int32_t* pages, int num_pages_to_zero, void* pool, int
 
 /* One decode step's planning from HOST arrays in a single call: nslg_zero_pages of
  * zero_pages[0 .. num_zero) on both pools (pool_k, pool_v; skipped when num_zero == 0),
- * then nslg_plan_decode. slots, starts, updates and zero_pages are host memory, copied
- * into pinned, device-mapped staging owned by the library before the call returns (the
- * caller may reuse them at once); the kernels read them from there. The plan goes to one
+ * then nslg_plan_decode. slots, starts, updates and zero_pages are host memory, read
+ * before the call returns (the caller may reuse them at once): up to 128 sequences, 192
+ * updates and 96 pages to zero they travel in the kernel launch's parameters, larger
+ * steps are copied into pinned, device-mapped staging owned by the library, which the
+ * kernels read. The plan goes to one
  * device array `plan` laid out as
  *   positions[B] | write_loc[B] | kv_indptr[B+1] | kv_last_page_len[B] | qo_indptr[B+1] |
  *   q_row_start[B] | kv_indices[max_indices]
