@@ -121,6 +121,38 @@ int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
                       float sm_scale, void* workspace, int64_t workspace_bytes,
                       uint32_t* dev_status, void* stream);
 
+/* Decode attention of a small batch split by kv head as well as by pages: sequence
+ * b * num_kv_heads + h is kv head h of sequence b with its group of num_qo_heads /
+ * num_kv_heads query heads, so batch 1 spreads over many more CTAs without more partials
+ * per query head. The page list comes from nslg_split_heads_plan (v_indptr, v_indices,
+ * v_last_page_len, built once per step from the plan's CSR). q and out are contiguous
+ * [batch, num_qo_heads, head_dim]; the pool, scale, workspace and status as in
+ * nslg_paged_decode (the workspace sized for batch * num_kv_heads sequences of the group
+ * size: nslg_decode_workspace_bytes(batch * num_kv_heads, group, head_dim)). The same
+ * attention as nslg_paged_decode with the plain CSR, within fp32 rounding of the merge
+ * order. No counterpart in the reference (it is a work split of the decode of
+ * kv_cache.py:639-651); NSLG_ERR_UNSUPPORTED off the tensor-core path or for one kv
+ * head. */
+int nslg_paged_decode_split_heads(int dtype, int batch, int num_qo_heads, int num_kv_heads,
+                                  int head_dim, int page_size, const void* q, void* out,
+                                  const void* pool_k, const void* pool_v, int64_t num_pages,
+                                  const int32_t* v_indptr, const int32_t* v_indices,
+                                  const int32_t* v_last_page_len, float sm_scale,
+                                  void* workspace, int64_t workspace_bytes,
+                                  uint32_t* dev_status, void* stream);
+
+/* The page list of nslg_paged_decode_split_heads from a decode plan's CSR (kv_indptr
+ * [batch + 1], kv_indices, kv_last_page_len [batch], device arrays): v_indptr
+ * [batch * num_kv_heads + 1], v_indices [num_kv_heads * kv_indptr[batch] <=
+ * max_v_indices] (page * num_kv_heads + h), v_last_page_len [batch * num_kv_heads]. One
+ * launch, graph-capturable; a page list longer than max_v_indices sets NSLG_DEV_BAD_PLAN.
+ * No counterpart in the reference. */
+int nslg_split_heads_plan(int batch, int num_kv_heads, const int32_t* kv_indptr,
+                          const int32_t* kv_indices, const int32_t* kv_last_page_len,
+                          int32_t* v_indptr, int32_t* v_indices, int32_t* v_last_page_len,
+                          int64_t max_v_indices, int64_t num_pages, uint32_t* dev_status,
+                          void* stream);
+
 /* The decode step of CacheContext.attend in one call: the new token's k and v of each
  * sequence appended to the pool at write_loc (nslg_rope_kv_append without rotation, q
  * and k already rotated as attend() receives them), then nslg_paged_decode over the

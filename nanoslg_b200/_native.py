@@ -35,6 +35,11 @@ SIGNATURES = {
     "nslg_rope_kv_append": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64,
                                    _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
     "nslg_decode_workspace_bytes": (_i64, [_i32, _i32, _i32]),
+    "nslg_paged_decode_split_heads": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+                                             _vp, _i64, _vp, _vp, _vp, _f32, _vp, _i64, _vp,
+                                             _vp]),
+    "nslg_split_heads_plan": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp,
+                                     _vp]),
     "nslg_paged_decode": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp,
                                  _vp, _i64, _vp, _vp, _vp, _f32, _vp, _i64, _vp, _vp]),
     "nslg_paged_decode_noalloc": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp,

@@ -143,6 +143,42 @@ int nslg_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads, 
                                      kv_last_page_len, sm_scale, 0, dev_status, st);
 }
 
+int nslg_paged_decode_split_heads(int dtype, int batch, int num_qo_heads, int num_kv_heads,
+                                  int head_dim, int page_size, const void* q, void* out,
+                                  const void* pool_k, const void* pool_v, int64_t num_pages,
+                                  const int32_t* v_indptr, const int32_t* v_indices,
+                                  const int32_t* v_last_page_len, float sm_scale,
+                                  void* workspace, int64_t workspace_bytes,
+                                  uint32_t* dev_status, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return set_error(NSLG_ERR_ARG, "paged_decode_split_heads: bad dtype");
+  if (batch < 0) return set_error(NSLG_ERR_ARG, "paged_decode_split_heads: batch < 0");
+  if (batch == 0) return NSLG_OK;
+  int rc = check_heads("paged_decode_split_heads", num_qo_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (page_size <= 0 || num_pages <= 0)
+    return set_error(NSLG_ERR_ARG, "paged_decode_split_heads: page_size and num_pages must be positive");
+  if (!q || !out || !pool_k || !pool_v || !v_indptr || !v_indices || !v_last_page_len)
+    return set_error(NSLG_ERR_ARG, "paged_decode_split_heads: null pointer");
+  if (!(sm_scale > 0.f)) return set_error(NSLG_ERR_ARG, "paged_decode_split_heads: sm_scale must be > 0");
+  const int group = num_qo_heads / num_kv_heads;
+  if (num_kv_heads < 2 || static_cast<int64_t>(batch) * num_kv_heads > (int64_t{1} << 20) ||
+      num_pages * num_kv_heads >= (int64_t{1} << 31) ||
+      !decode_tc_supported(dtype, group, 1, head_dim, page_size) || !aligned16(pool_k) ||
+      !aligned16(pool_v) || (reinterpret_cast<uintptr_t>(q) & 3u) ||
+      (reinterpret_cast<uintptr_t>(out) & 3u))
+    return set_error(NSLG_ERR_UNSUPPORTED,
+                     "paged_decode_split_heads: needs the tensor-core decode path, 2 or more "
+                     "kv heads and 4-byte aligned q / out");
+  // sequence b * hkv + h: the group of query heads of kv head h of sequence b, rows of
+  // group * head_dim elements in the contiguous [batch, num_qo_heads, head_dim] q / out
+  const int64_t row = static_cast<int64_t>(group) * head_dim;
+  return launch_paged_decode_tc(dtype, batch * num_kv_heads, group, 1, head_dim, q, row, out,
+                                row, pool_k, pool_v, num_pages, v_indptr, v_indices,
+                                v_last_page_len, sm_scale, workspace, workspace_bytes,
+                                dev_status, static_cast<cudaStream_t>(stream), num_kv_heads);
+}
+
 int nslg_append_paged_decode(int dtype, int batch, int num_qo_heads, int num_kv_heads,
                              int head_dim, int page_size, const void* q, int64_t q_stride,
                              const void* k, int64_t k_stride, const void* v, int64_t v_stride,

@@ -82,6 +82,7 @@ struct DecodeParams {
   int smem_csr;       // kv_indptr and kv_last_page_len are staged in shared memory
   int inline_merge;   // 1: split sequences merged by their last CTA; 0: by the merge kernel
   int min_pages;      // fewest pages a CTA streams (kMinPagesPerCta, kMinCtaBytes)
+  int vheads;         // > 1: split-heads call, page id = pool page * vheads + kv head
   int box_all_heads;  // tensor maps with a [64 dim x 16 tok x HKV head] box (token-major)
   float scale_log2;
   uint32_t* status;
@@ -449,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++armed[stage];
       }
       __syncwarp();
-      if (lane < np && (my_id < 0 || my_id >= p.num_pages)) {
+      if (lane < np && (my_id < 0 || my_id >= p.num_pages * (p.vheads > 1 ? p.vheads : 1))) {
         report(p.status, NSLG_DEV_BAD_PAGE);
         my_id = 0;  // keep the transaction count; page 0 is the pool's null page
       }
@@ -473,8 +474,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                       policy);
         } else {
           const int half = r % C::kHalves, h = r / C::kHalves;
-          tma_load_3d(sb + C::box(jj, kv, half, h), map, &full[stage], half * 64, h, pid * kPS,
-                      policy);
+          // split-heads calls: the page id carries the kv head (the map's head coordinate)
+          const int vh = p.vheads > 1 ? pid % p.vheads : 0;
+          const int pg = p.vheads > 1 ? pid / p.vheads : pid;
+          tma_load_3d(sb + C::box(jj, kv, half, h), map, &full[stage], half * 64, h + vh,
+                      pg * kPS, policy);
         }
       }
       if (++stage == stages) { stage = 0; phase ^= 1; }
@@ -940,7 +944,7 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
                            const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
                            const int32_t* kv_indices, const int32_t* kv_last_page_len,
                            float sm_scale, void* workspace, int64_t workspace_bytes,
-                           uint32_t* status, cudaStream_t stream) {
+                           uint32_t* status, cudaStream_t stream, int vheads) {
   if (batch == 0) return NSLG_OK;
   const int64_t need = decode_tc_workspace_bytes(batch, hq, d);
   if (workspace == nullptr || workspace_bytes < need)
@@ -950,7 +954,9 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
   CUtensorMap tk, tv;
   // -1 unknown, 1 the driver takes the token-major all-heads map, 0 it does not
   static std::atomic<int> all_heads_ok{-1};
-  int box_all = all_heads_ok.load(std::memory_order_relaxed) != 0 ? 1 : 0;
+  // split-heads calls (vheads > 1, hkv == 1) read one head per box from the real pool
+  int box_all = vheads <= 1 && all_heads_ok.load(std::memory_order_relaxed) != 0 ? 1 : 0;
+  const int map_heads = vheads > 1 ? vheads : hkv;
   int rc = NSLG_ERR_UNSUPPORTED;
   if (box_all) {
     rc = pool_tensor_map_all_heads(pool_k, num_pages, hkv, d, &tk);
@@ -961,9 +967,9 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
   if (rc != NSLG_OK) {
     // the driver did not take the token-major strides: one box per kv head instead
     box_all = 0;
-    rc = pool_tensor_map(pool_k, num_pages, hkv, d, &tk);
+    rc = pool_tensor_map(pool_k, num_pages, map_heads, d, &tk);
     if (rc != NSLG_OK) return rc;
-    rc = pool_tensor_map(pool_v, num_pages, hkv, d, &tv);
+    rc = pool_tensor_map(pool_v, num_pages, map_heads, d, &tv);
     if (rc != NSLG_OK) return rc;
   }
   const int grid = sm_count();
@@ -988,6 +994,7 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.status = status;
   p.box_all_heads = box_all;
+  p.vheads = vheads > 1 ? vheads : 1;
   p.inline_merge = merge_inline(batch, hq, d, grid);
   {
     // NSLG_DECODE_MIN_CTA_KB overrides kMinCtaBytes (1 to 4096 KiB), for measurements

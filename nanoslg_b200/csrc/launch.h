@@ -96,7 +96,7 @@ int launch_paged_decode_tc(int dtype, int batch, int hq, int hkv, int d, const v
                            const void* pool_v, int64_t num_pages, const int32_t* kv_indptr,
                            const int32_t* kv_indices, const int32_t* kv_last_page_len,
                            float sm_scale, void* workspace, int64_t workspace_bytes,
-                           uint32_t* status, cudaStream_t stream);
+                           uint32_t* status, cudaStream_t stream, int vheads = 1);
 
 // tcgen05 causal prefill for bf16 / fp16, page_size 16, head_dim 128, group <= 16
 // dividing 128.

@@ -260,6 +260,32 @@ __global__ void __launch_bounds__(kFusedThreads) plan_decode_fused_kernel(
   for (int j = t; j < n; j += kFusedThreads) p.indices[run + j] = row[j];
 }
 
+// Split-heads plan: sequence b' = b * hkv + h of the split-heads decode is kv head h of
+// sequence b, with b's pages, its last-page length, and page ids page * hkv + h (the
+// decode kernel takes the head from the id). Block b' writes its pages; the CSR offsets
+// follow from kv_indptr alone: v_indptr[b * hkv + h] = hkv * kv_indptr[b] + h * n_b.
+__global__ void __launch_bounds__(128) split_heads_plan_kernel(
+    int batch, int hkv, const int32_t* kv_indptr, const int32_t* kv_indices,
+    const int32_t* kv_lpl, int32_t* v_indptr, int32_t* v_indices, int32_t* v_lpl,
+    int64_t max_v, uint32_t* status) {
+  pdl_wait();
+  pdl_trigger();
+  const int bv = blockIdx.x, b = bv / hkv, h = bv % hkv;
+  const int beg = kv_indptr[b], n = kv_indptr[b + 1] - beg;
+  const int64_t vbeg = static_cast<int64_t>(hkv) * beg + static_cast<int64_t>(h) * n;
+  if (threadIdx.x == 0) {
+    v_indptr[bv] = static_cast<int32_t>(vbeg);
+    v_lpl[bv] = kv_lpl[b];
+    if (bv == batch * hkv - 1) v_indptr[batch * hkv] = hkv * kv_indptr[batch];
+  }
+  if (n < 0 || vbeg + n > max_v) {
+    if (threadIdx.x == 0) report(status, NSLG_DEV_BAD_PLAN);
+    return;
+  }
+  for (int j = threadIdx.x; j < n; j += blockDim.x)
+    v_indices[vbeg + j] = kv_indices[beg + j] * hkv + h;
+}
+
 int check_plan_args(int batch, int page_size, int64_t bt_stride, int64_t bt_rows,
                     int num_updates, int64_t max_indices) {
   if (batch < 1 || batch > kScanThreads * kMaxItems)
@@ -467,4 +493,26 @@ extern "C" int nslg_plan_decode_host(int batch, int page_size, const int32_t* sl
     rc = set_error(NSLG_ERR_CUDA, cudaGetErrorString(err));
   }
   return rc;
+}
+
+extern "C" int nslg_split_heads_plan(int batch, int num_kv_heads, const int32_t* kv_indptr,
+                                     const int32_t* kv_indices,
+                                     const int32_t* kv_last_page_len, int32_t* v_indptr,
+                                     int32_t* v_indices, int32_t* v_last_page_len,
+                                     int64_t max_v_indices, int64_t num_pages,
+                                     uint32_t* dev_status, void* stream) {
+  if (batch < 0 || num_kv_heads < 1 || max_v_indices < 1 || num_pages < 1)
+    return set_error(NSLG_ERR_ARG, "split_heads_plan: bad sizes");
+  if (batch == 0) return NSLG_OK;
+  if (static_cast<int64_t>(batch) * num_kv_heads > (int64_t{1} << 20) ||
+      num_pages * num_kv_heads >= (int64_t{1} << 31))
+    return set_error(NSLG_ERR_UNSUPPORTED, "split_heads_plan: too many sequences or pages");
+  if (!kv_indptr || !kv_indices || !kv_last_page_len || !v_indptr || !v_indices ||
+      !v_last_page_len)
+    return set_error(NSLG_ERR_ARG, "split_heads_plan: null pointer");
+  return launch_pdl("split_heads_plan", split_heads_plan_kernel,
+                    dim3(static_cast<unsigned>(batch * num_kv_heads)), dim3(128), 0,
+                    static_cast<cudaStream_t>(stream), batch, num_kv_heads, kv_indptr,
+                    kv_indices, kv_last_page_len, v_indptr, v_indices, v_last_page_len,
+                    max_v_indices, dev_status);
 }

@@ -561,6 +561,7 @@ class B200CacheContext(CacheContext):
         self.seq_lens = [self.start_positions[i] + new_token_counts[i] for i in range(B)]
         self.max_kv_len = max(self.seq_lens) if self.seq_lens else 0
         self._is_decode = all(n == 1 for n in new_token_counts)
+        self._split_plan = None      # split-heads page list, built by the first decode call
         self._iw = (max(o + n for o, n in zip(self.input_offsets, new_token_counts))
                     if B else 1)
         iw = self._iw
@@ -907,6 +908,18 @@ class B200CacheContext(CacheContext):
         pool = self.cache.pool
         pk, pv = pool.k_layers[layer_idx], pool.v_layers[layer_idx]
         if self._is_decode:
+            hkv = pk.shape[2]
+            if (2 <= hkv and B * hkv <= ops.DECODE_SPLIT_HEADS_PAIRS and q.dtype != torch.float32
+                    and d in (64, 128) and pk.shape[1] == 16 and hq // hkv <= 16):
+                # small batches: the decode split by kv head as well as by pages (the split
+                # page list built once per step, at the first layer)
+                if self._split_plan is None:
+                    self._split_plan = ops.split_heads_plan(self.kv_indptr, self.kv_indices,
+                                                            self.kv_last_page_len, hkv,
+                                                            pk.shape[0])
+                out = ops.paged_decode_split_heads(q[:, 0].contiguous(), pk, pv,
+                                                   self._split_plan, self._sm_scale)
+                return out.view(B, 1, hq * d)
             out = ops.paged_decode(q[:, 0], pk, pv, self.kv_indptr, self.kv_indices,
                                    self.kv_last_page_len, self._sm_scale)
             return out.view(B, 1, hq * d)
@@ -1136,6 +1149,7 @@ class B200PagedKVCache(KVCacheManager):
         ctx.batch_size = B
         ctx._n0 = n0.copy()       # start_positions / seq_lens / max_kv_len, built on use
         ctx._is_decode = True
+        ctx._split_plan = None
         ctx._iw = 1
         ctx._wi = None
         ctx._wi_src = (c.cur_pid.copy(), rem)

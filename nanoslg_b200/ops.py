@@ -197,6 +197,56 @@ def paged_decode(q, pool_k, pool_v, kv_indptr, kv_indices, kv_last_page_len, sm_
     return out
 
 
+# Decode batches of at most this many (sequence, kv head) pairs take the split-heads path
+# in the paged context (the work split by kv head as well as by pages). Off by default:
+# alone it is faster (one B200, 32 decode calls per CUDA graph, us per layer, plain ->
+# split: TP=1 batch 1, 512 tokens, 8.9 -> 7.3; TP=4 batch 1 10.0 -> 6.8; TP=1 batch 8
+# 15.4 -> 13.6; TP=2 batch 16 20.4 -> 16.7; slower from 128 pairs: TP=1 batch 16 20.8 ->
+# 23.8), but inside the 8B decode step, between the q|k|v and o_proj products, it was
+# slower (same-box A/B: batch 1 3.17-3.20 -> 3.27 ms per step, batch 4 3.27-3.30 ->
+# 3.31-3.35). NSLG_DECODE_SPLIT_HEADS=1 (read at import) enables it up to 64 pairs.
+_SPLIT_ENV = os.environ.get("NSLG_DECODE_SPLIT_HEADS")
+DECODE_SPLIT_HEADS_PAIRS = 64 if _SPLIT_ENV == "1" else 0
+
+
+def split_heads_plan(kv_indptr, kv_indices, kv_last_page_len, hkv, num_pages):
+    """The page list of ``paged_decode_split_heads`` from a decode plan's CSR (int32 device
+    arrays): returns (v_indptr, v_indices, v_last_page_len) for batch * hkv sequences, one
+    per (sequence, kv head), page ids page * hkv + head (nslg_split_heads_plan)."""
+    _need_cuda(kv_indptr, kv_indices, kv_last_page_len)
+    batch = kv_indptr.numel() - 1
+    dev = kv_indptr.device
+    v_indptr = torch.empty(batch * hkv + 1, dtype=torch.int32, device=dev)
+    v_indices = torch.empty(max(hkv * kv_indices.numel(), 1), dtype=torch.int32, device=dev)
+    v_lpl = torch.empty(batch * hkv, dtype=torch.int32, device=dev)
+    N.call("nslg_split_heads_plan", batch, hkv, _ptr(kv_indptr), _ptr(kv_indices),
+           _ptr(kv_last_page_len), _ptr(v_indptr), _ptr(v_indices), _ptr(v_lpl),
+           v_indices.numel(), int(num_pages), _ptr(status_word(dev)), _stream(kv_indptr))
+    return v_indptr, v_indices, v_lpl
+
+
+def paged_decode_split_heads(q, pool_k, pool_v, split_plan, sm_scale, out=None):
+    """``paged_decode`` with the work split by kv head as well as by pages
+    (nslg_paged_decode_split_heads): q contiguous [B, Hq, D] -> out [B, Hq, D];
+    ``split_plan`` from ``split_heads_plan``. The same attention within fp32 rounding
+    of the merge order."""
+    _need_cuda(q, pool_k, pool_v)
+    dt = _dtype_code(q)
+    if q.dim() != 3 or not q.is_contiguous():
+        raise ValueError("paged_decode_split_heads: q must be contiguous [B, Hq, D]")
+    b, hq, d = q.shape
+    num_pages, ps, hkv = pool_k.shape[0], pool_k.shape[1], pool_k.shape[2]
+    if out is None:
+        out = torch.empty_like(q)
+    v_indptr, v_indices, v_lpl = split_plan
+    wsb = N.lib().nslg_decode_workspace_bytes(b * hkv, hq // hkv, d)
+    ws = _STATE.workspace(q.device, wsb)
+    N.call("nslg_paged_decode_split_heads", dt, b, hq, hkv, d, ps, _ptr(q), _ptr(out),
+           _ptr(pool_k), _ptr(pool_v), num_pages, _ptr(v_indptr), _ptr(v_indices), _ptr(v_lpl),
+           float(sm_scale), _ptr(ws), ws.numel(), _ptr(status_word(q.device)), _stream(q))
+    return out
+
+
 def paged_prefill(q, qo_indptr, max_qo_len, pool_k, pool_v, kv_indptr, kv_indices,
                   kv_last_page_len, sm_scale, causal=True, q_row_start=None, out=None):
     """Causal prefill/extend attention over the paged KV.

@@ -51,8 +51,11 @@ def test_context_attend_matches_reference(case):
         mgr.end_forward(ctx)
 
 
-def test_attend_rope_equals_unfused_path():
-    """attend_rope (fused kernel) == torch RoPE (the reference's ops) + attend."""
+def test_attend_rope_equals_unfused_path(monkeypatch):
+    """attend_rope (fused kernel) == torch RoPE (the reference's ops) + attend, both on
+    the plain decode split (the split-heads decode of small batches merges in another
+    order; it is compared with the plain one in test_gpu_kernels)."""
+    monkeypatch.setattr(ops, "DECODE_SPLIT_HEADS_PAIRS", 0)
     hq, hkv, d = 32, 8, 128
     cos, sin = rope_table(d, 8192, 500000.0)
     cos_d, sin_d = cos.to(DEV), sin.to(DEV)
@@ -418,3 +421,35 @@ def test_plan_decode_host_refuses_graph_capture():
     g.replay()
     torch.cuda.synchronize(dev)
     assert int(plan.abs().sum()) == 0
+
+
+def test_small_batch_decode_takes_the_split_heads_path(monkeypatch):
+    """Decode steps of a small batch through the context split the work by kv head as
+    well as by pages (its page list built once per step) and agree with the plain split
+    within fp32 rounding of the merge order, step after step."""
+    hq, hkv, d = 32, 8, 128
+    cos, sin = rope_table(d, 8192, 500000.0)
+    cos_d, sin_d = cos.to(DEV), sin.to(DEV)
+    outs = {}
+    for pairs in (64, 0):
+        monkeypatch.setattr(ops, "DECODE_SPLIT_HEADS_PAIRS", pairs)
+        cfg = KVCacheConfig(num_layers=1, num_kv_heads=hkv, num_qo_heads=hq, head_dim=d,
+                            page_size=16, max_pages=256, dtype=torch.bfloat16, device=DEV)
+        mgr = B200PagedKVCache(cfg)
+        g = torch.Generator().manual_seed(5)
+        sids = ["a", "b"]
+        for s, n in zip(sids, (700, 33)):
+            mgr.allocate_sequence(s, None, num_tokens=n)
+            mgr.seqs[s].num_tokens = n          # history already cached
+        res = []
+        for _ in range(3):
+            ctx = mgr.begin_forward(sids, [1, 1])
+            q = torch.randn(2, 1, hq, d, generator=g).to(torch.bfloat16).to(DEV)
+            k = torch.randn(2, 1, hkv, d, generator=g).to(torch.bfloat16).to(DEV)
+            v = torch.randn(2, 1, hkv, d, generator=g).to(torch.bfloat16).to(DEV)
+            res.append(ctx.attend_rope(0, q, k, v, cos_d, sin_d).cpu())
+            assert (ctx._split_plan is not None) == (pairs > 0)
+            mgr.end_forward(ctx)
+        outs[pairs] = res
+    for a, b in zip(outs[64], outs[0]):
+        torch.testing.assert_close(a, b, rtol=1e-2, atol=1e-2)

@@ -138,6 +138,41 @@ def test_paged_decode_bf16(hq, hkv, d, lens, mode, monkeypatch):
         torch.testing.assert_close(out[b], exp, **BF16_TOL)
 
 
+@pytest.mark.parametrize("hq,hkv,d,lens", [
+    (32, 8, 128, [512]),                                 # 8B TP=1, batch 1
+    (32, 8, 128, [1, 17, 300, 2049]),
+    (16, 4, 128, [0, 700, 33]),                          # a sequence without pages
+    (16, 2, 128, [5000]),
+    (8, 2, 64, [9, 300, 1024]),
+])
+def test_paged_decode_split_heads(hq, hkv, d, lens):
+    """The decode split by kv head as well as by pages (each (sequence, kv head) a
+    sequence of the group's query heads, page ids page * hkv + head from
+    split_heads_plan): the oracle's attention within the bf16 tolerance, and the plain
+    decode's within fp32 rounding of the merge order."""
+    pk = make_paged(lens, hkv, d, 4096, torch.bfloat16, DEV, seed=len(lens) + 3 * hq)
+    g = torch.Generator().manual_seed(11)
+    q = torch.randn(len(lens), hq, d, generator=g).to(torch.bfloat16)
+    qd = q.to(DEV)
+    plan = ops.split_heads_plan(pk["indptr"], pk["indices"], pk["lpl"], hkv,
+                                pk["pool_k"].shape[0])
+    out = ops.paged_decode_split_heads(qd, pk["pool_k"], pk["pool_v"], plan,
+                                       1 / math.sqrt(d))
+    plain = ops.paged_decode(qd, pk["pool_k"], pk["pool_v"], pk["indptr"], pk["indices"],
+                             pk["lpl"], 1 / math.sqrt(d))
+    torch.testing.assert_close(out, plain, rtol=1e-2, atol=1e-2)
+    out = out.cpu()
+    ks = [sequence_kv(pk, b, "k") for b in range(len(lens))]
+    vs = [sequence_kv(pk, b, "v") for b in range(len(lens))]
+    ref = attend_sequences([q[b:b + 1] for b in range(len(lens))], ks, vs)
+    for b, n in enumerate(lens):
+        exp = ref[b][0] if n > 0 else torch.zeros(hq, d, dtype=torch.bfloat16)
+        torch.testing.assert_close(out[b], exp, **BF16_TOL)
+    # deterministic
+    again = ops.paged_decode_split_heads(qd, pk["pool_k"], pk["pool_v"], plan, 1 / math.sqrt(d))
+    assert torch.equal(again.cpu(), out)
+
+
 def test_paged_decode_many_sequences_split_across_ctas():
     g = torch.Generator().manual_seed(6)
     lens = torch.randint(1, 3000, (97,), generator=g).tolist()
